@@ -1,0 +1,363 @@
+"""Benchmark of the GPU-resident rollout hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl mine|reference]
+
+Under torchrun (N > 1) every rank runs its own shard (weak scaling: a fixed
+per-GPU share) with no data-path collective; the step time is the maximum
+over ranks.  Rank 0 prints one JSON line.
+
+Workloads (synthetic, seeded):
+  attention  config 2: paged GQA decode attention, B=64 ragged sequences
+             L ~ U[128,4096], 32 q / 8 kv heads, d=128, bf16 16-token pages
+             scattered in the arena, Q/K/V ~ N(0,1).  One step = one decode
+             attention call over the batch.  Two arena copies (>1 GB in
+             total, larger than the 126 MB L2) alternate between steps.
+
+--impl reference times the reference path's CPU implementation (the CPU
+oracle port of the same computation; the reference has no CPU
+implementation of paged attention) on this host's cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+import __graft_entry__ as ge  # noqa: E402
+
+HBM_FALLBACK_GBS = 6650.0
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f), "measured"
+    except OSError:
+        return {"hbm_gbs": HBM_FALLBACK_GBS, "bf16_tflops": 1590.0}, "fallback"
+
+
+def ncu_traffic(kernel: str):
+    """Per-launch DRAM bytes recorded from an ncu capture in profiles/ncu_traffic.txt
+    (lines: <kernel> <workload> <bytes_per_launch>)."""
+    path = os.path.join(ROOT, "profiles", "ncu_traffic.txt")
+    try:
+        with open(path) as f:
+            for line in f:
+                parts = line.split()
+                if len(parts) >= 3 and not line.startswith("#") and parts[0] == kernel:
+                    return float(parts[2])
+    except OSError:
+        pass
+    return None
+
+
+# ----------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples SM clock and clock-event reasons via NVML while running."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+        0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+        0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+        0x100: "display_clock_setting",
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.05):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self.period = period_s
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            import torch
+            props = torch.cuda.get_device_properties(device_index)
+            bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+            self.h = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+            self.nvml = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # noqa: BLE001 - clocks are reported as unavailable
+            self.nvml = None
+            self.err = repr(e)
+
+    def _sample(self):
+        n = self.nvml
+        self.samples.append(n.nvmlDeviceGetClockInfo(self.h, n.NVML_CLOCK_SM))
+        try:
+            mask = n.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+        except AttributeError:
+            mask = n.nvmlDeviceGetCurrentClocksThrottleReasons(self.h)
+        for bit, name in self.REASONS.items():
+            if mask & bit and name != "gpu_idle":
+                self.reasons.add(name)
+
+    def _run(self):
+        while not self._stop.is_set():
+            self._sample()
+            time.sleep(self.period)
+
+    def start(self):
+        if self.nvml:
+            self._sample()
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+
+    def stop(self):
+        if self.nvml:
+            self._stop.set()
+            self._thread.join()
+            self._sample()
+
+    def report(self):
+        if not self.nvml:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": self.err}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------- workloads
+class AttentionWorkload:
+    """BASELINE config 2 (paged GQA decode attention)."""
+
+    name = "paged_gqa_decode_attention_c2"
+    kernel = "paged_gqa_decode_kernel"
+
+    def __init__(self, args, rank, world, dev):
+        import torch
+        self.torch = torch
+        self.pkg = ge.load_package()
+        self.dev = dev
+        self.B, self.Hq, self.Hkv = 64, 32, 8
+        # each rank owns its own batch (seeded by rank): weak scaling
+        self.lens = np.random.default_rng(2 + 1000 * rank).integers(128, 4097, size=self.B).astype(np.int32)
+        rng = np.random.default_rng(20 + rank)
+        n_pages = (self.lens + 15) // 16
+        self.P = int(n_pages.max())
+        total = int(n_pages.sum())
+        self.arena_pages = int(total * 1.25) + 1
+        pt = np.full((self.B, self.P), -1, dtype=np.int32)
+        perm = rng.permutation(self.arena_pages).astype(np.int32)
+        k = 0
+        for b, n in enumerate(n_pages):
+            pt[b, :n] = perm[k:k + n]
+            k += n
+        self.pt_host = pt
+        self.page_table = torch.from_numpy(pt).to(dev)
+        self.seq_lens = torch.from_numpy(self.lens).to(dev)
+        elems = self.arena_pages * self.Hkv * 2 * 16 * 128
+        self.arenas = []
+        for c in range(2):
+            a = torch.empty(elems, dtype=torch.bfloat16, device=dev)
+            self.pkg.fill_normal_bf16(a, seed=2 + rank, stream_id=1)   # same contents, two copies
+            self.arenas.append(a)
+        self.q = torch.empty(self.B, self.Hq, 128, dtype=torch.bfloat16, device=dev)
+        self.pkg.fill_normal_bf16(self.q, seed=2 + rank, stream_id=2)
+        self.out = torch.empty(self.B, self.Hq, 128, dtype=torch.float32, device=dev)
+        self.attn = self.pkg.PagedDecodeAttention(self.B, self.Hq, self.Hkv, self.P,
+                                                  int(self.lens.max()), self.arena_pages,
+                                                  chunk_pages=args.chunk_pages)
+        self.i = 0
+        # algorithmic bytes per launch: KV once + q + out + page-table entries
+        self.kv_bytes = int(self.lens.sum()) * self.Hkv * 128 * 2 * 2
+        self.bytes = (self.kv_bytes + self.B * self.Hq * 128 * (2 + 4) + int(n_pages.sum()) * 4)
+        self.flops = 4 * self.Hq * 128 * int(self.lens.sum())
+        torch.cuda.synchronize()
+
+    def step(self):
+        self.attn(self.q, self.arenas[self.i & 1], self.page_table, self.seq_lens, out=self.out)
+        self.i += 1
+
+    launches_per_step = 1
+
+    def units_per_step(self):
+        return self.bytes / 1e9  # GB
+
+    metric = "decode-attn HBM GB/s (paged GQA, config 2)"
+    unit = "GB/s"
+
+    def e2e(self, steps, warmup):
+        """Same metric through the C ABI with host buffers: the step's query is
+        copied from pinned host memory and the output read back each step (the
+        KV arena is the resident cache)."""
+        torch = self.torch
+        q_h = self.q.cpu().pin_memory()
+        out_h = torch.empty(self.out.shape, dtype=torch.float32).pin_memory()
+        s = torch.cuda.current_stream()
+
+        def one():
+            self.q.copy_(q_h, non_blocking=True)
+            self.step()
+            out_h.copy_(self.out, non_blocking=True)
+
+        for _ in range(warmup):
+            one()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(steps):
+            one()
+        e1.record(s)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        return {"value": self.units_per_step() / (ms / 1e3), "unit": self.unit,
+                "ms_per_step": ms, "h2d_bytes_per_step": int(q_h.numel() * 2),
+                "d2h_bytes_per_step": int(out_h.numel() * 4)}
+
+    def check_errors(self):
+        return self.attn.error_code()
+
+    def cpu_sample(self, threads):
+        """CPU oracle port on a bounded sample: the first n sequences."""
+        orc = ge.load_oracle()
+        torch = self.torch
+        n = 8
+        q = self.q[:n].view(torch.int16).cpu().numpy().view(np.uint16)
+        arena = self.arenas[0].view(torch.int16).cpu().numpy().view(np.uint16)
+        t0 = time.perf_counter()
+        orc.paged_gqa_attention(q, arena, self.pt_host[:n], self.lens[:n], self.Hq, self.Hkv,
+                                128 ** -0.5, n_threads=threads)
+        dt = time.perf_counter() - t0
+        sample_bytes = int(self.lens[:n].sum()) * self.Hkv * 128 * 4 + n * self.Hq * 128 * 6
+        return {"value": sample_bytes / 1e9 / dt, "unit": self.unit, "cores": threads,
+                "kind": "port", "seconds": dt,
+                "sample": f"first {n} of 64 sequences of config 2 ({int(self.lens[:n].sum())} tokens), "
+                          f"oracle/oracle.c fp64-accumulate restatement, OpenMP"}
+
+    def config(self):
+        return {"workload": self.name, "batch": self.B, "seq_len": "U[128,4096] seed 2",
+                "q_heads": self.Hq, "kv_heads": self.Hkv, "head_dim": 128, "page_tokens": 16,
+                "kv_dtype": "bf16", "l2": "two arena copies alternate (2 x %.0f MB > 126 MB L2)"
+                % (self.kv_bytes / 1e6), "chunk_pages": self.attn.plan()[0]}
+
+
+WORKLOADS = {"attention": AttentionWorkload}
+
+
+# -------------------------------------------------------------------- main
+def run_mine(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    wl = WORKLOADS[args.workload](args, rank, world, dev)
+    for _ in range(args.warmup):
+        wl.step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(s)
+    for _ in range(args.steps):
+        wl.step()
+    e1.record(s)
+    torch.cuda.synchronize()
+    clocks.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    err = wl.check_errors()
+    e2e = wl.e2e(args.steps, args.warmup)
+    if world > 1:
+        t = torch.tensor([e2e["ms_per_step"]], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e["value"] = wl.units_per_step() / (float(t.item()) / 1e3) * world
+        e2e["ms_per_step"] = float(t.item())
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = wl.cpu_sample(os.cpu_count() or 1)
+
+    if rank == 0:
+        peaks, src = measured_peaks()
+        achieved = wl.bytes / (ms / 1e3) / 1e9
+        traffic = ncu_traffic(wl.kernel)
+        line = {
+            "metric": wl.metric, "value": wl.units_per_step() / (ms / 1e3) * world,
+            "unit": wl.unit, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (Philox N(0,1), seeded)",
+            "config": wl.config() | {"parallelism": f"replicas{world}" if world > 1 else "single"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
+                         "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
+                         "peak_source": f"{src} copy bandwidth (MEASURED_PEAKS.json hbm_gbs)"
+                         if src == "measured" else "fallback 6.65 TB/s",
+                         "frac_of_nominal_8tbs": achieved / 8000.0,
+                         "traffic": traffic, "kernel": wl.kernel},
+            "cpu_baseline": cpu,
+            "e2e": {k: e2e[k] for k in ("value", "unit", "h2d_bytes_per_step", "d2h_bytes_per_step")},
+            "gpu_launches": wl.launches_per_step * args.steps,
+            "clocks": clocks.report(),
+            "device_error_code": err,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import torch
+    dev = torch.device("cuda", 0) if torch.cuda.is_available() else None
+    if dev is None:
+        print(json.dumps({"impl": "reference", "unavailable": "needs a GPU box to build inputs"}))
+        return
+    wl = WORKLOADS[args.workload](args, 0, 1, dev)
+    threads = os.cpu_count() or 1
+    samples = [wl.cpu_sample(threads) for _ in range(max(1, min(args.steps, 3)))]
+    v = statistics.median(s["value"] for s in samples)
+    cpu = samples[0] | {"value": v}
+    cpu.pop("seconds", None)
+    print(json.dumps({
+        "impl": "reference", "metric": wl.metric, "value": v, "unit": wl.unit, "n_gpus": world,
+        "steps": len(samples), "warmup": 0, "higher_is_better": True,
+        "config": wl.config(), "cpu_baseline": cpu,
+        "e2e": {"value": v, "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--workload", default="attention", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
+    ap.add_argument("--chunk-pages", type=int, default=0)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_mine(args)
+
+
+if __name__ == "__main__":
+    main()
