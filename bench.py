@@ -214,21 +214,23 @@ class AttentionWorkload:
     def check_errors(self):
         return self.attn.error_code()
 
-    def cpu_sample(self, threads):
-        """CPU oracle port on a bounded sample: the first n sequences."""
+    def cpu_sample(self, threads, budget_s=10.0):
+        """CPU oracle port on a bounded sample: whole config-2 batches repeated
+        until the time budget is spent (at least one)."""
         orc = ge.load_oracle()
         torch = self.torch
-        n = 8
-        q = self.q[:n].view(torch.int16).cpu().numpy().view(np.uint16)
+        q = self.q.view(torch.int16).cpu().numpy().view(np.uint16)
         arena = self.arenas[0].view(torch.int16).cpu().numpy().view(np.uint16)
         t0 = time.perf_counter()
-        orc.paged_gqa_attention(q, arena, self.pt_host[:n], self.lens[:n], self.Hq, self.Hkv,
-                                128 ** -0.5, n_threads=threads)
+        reps = 0
+        while reps == 0 or time.perf_counter() - t0 < budget_s:
+            orc.paged_gqa_attention(q, arena, self.pt_host, self.lens, self.Hq, self.Hkv,
+                                    128 ** -0.5, n_threads=threads)
+            reps += 1
         dt = time.perf_counter() - t0
-        sample_bytes = int(self.lens[:n].sum()) * self.Hkv * 128 * 4 + n * self.Hq * 128 * 6
-        return {"value": sample_bytes / 1e9 / dt, "unit": self.unit, "cores": threads,
+        return {"value": reps * self.bytes / 1e9 / dt, "unit": self.unit, "cores": threads,
                 "kind": "port", "seconds": dt,
-                "sample": f"first {n} of 64 sequences of config 2 ({int(self.lens[:n].sum())} tokens), "
+                "sample": f"{reps} full config-2 batch(es) (64 sequences, {int(self.lens.sum())} tokens), "
                           f"oracle/oracle.c fp64-accumulate restatement, OpenMP"}
 
     def config(self):
@@ -238,7 +240,92 @@ class AttentionWorkload:
                 % (self.kv_bytes / 1e6), "chunk_pages": self.attn.plan()[0]}
 
 
-WORKLOADS = {"attention": AttentionWorkload}
+class SamplingWorkload:
+    """256 rows x 32,000 fp32 logits ~ N(0, 2), T=0.8,
+    top-k 50, top-p 0.9, Philox seed 1234, counter = (rollout_id = row, step).
+    Eight logits buffers (262 MB > 126 MB L2) rotate between steps."""
+
+    name = "fused_sampling_c3"
+    kernel = "sample_rows_kernel"
+    metric = "sampling logits HBM GB/s (config 3)"
+    unit = "GB/s"
+    launches_per_step = 1
+
+    def __init__(self, args, rank, world, dev):
+        import torch
+        self.torch = torch
+        self.pkg = ge.load_package()
+        self.R, self.V, self.nbuf = 256, 32000, 8
+        self.bufs = []
+        for i in range(self.nbuf):
+            t = torch.empty(self.R, self.V, dtype=torch.float32, device=dev)
+            self.pkg.fill_normal_f32(t, seed=3 + rank, stream_id=100 + i, std=2.0)
+            self.bufs.append(t)
+        rows = self.pkg.sample_row_table(0.8, 50, 0.9, np.arange(self.R, dtype=np.uint32), 0)
+        self.rows_np = rows
+        self.rows = torch.from_numpy(rows.view(np.uint8)).to(dev)
+        self.out = torch.empty(self.R, dtype=torch.int32, device=dev)
+        self.bytes = self.R * self.V * 4 + self.R * (24 + 4)
+        self.i = 0
+        torch.cuda.synchronize()
+
+    def step(self):
+        self.pkg.sample_rows(self.bufs[self.i % self.nbuf], self.rows, self.V, 1234, out=self.out)
+        self.i += 1
+
+    def units_per_step(self):
+        return self.bytes / 1e9
+
+    def e2e(self, steps, warmup):
+        """Logits rows copied from pinned host memory each step, tokens read back."""
+        torch = self.torch
+        host = self.bufs[0].cpu().pin_memory()
+        tok_h = torch.empty(self.R, dtype=torch.int32).pin_memory()
+        s = torch.cuda.current_stream()
+
+        def one():
+            self.bufs[0].copy_(host, non_blocking=True)
+            self.pkg.sample_rows(self.bufs[0], self.rows, self.V, 1234, out=self.out)
+            tok_h.copy_(self.out, non_blocking=True)
+
+        for _ in range(warmup):
+            one()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(steps):
+            one()
+        e1.record(s)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        return {"value": self.units_per_step() / (ms / 1e3), "unit": self.unit, "ms_per_step": ms,
+                "h2d_bytes_per_step": int(host.numel() * 4), "d2h_bytes_per_step": self.R * 4}
+
+    def check_errors(self):
+        return 0
+
+    def cpu_sample(self, threads, budget_s=10.0):
+        """The reference algorithm (cu/sample.cu:40-123 restated in
+        oracle/oracle.c, insertion top-k) on host rows, one core, until the
+        time budget is spent."""
+        orc = ge.load_oracle()
+        host = self.bufs[0].cpu().numpy()
+        t0 = time.perf_counter()
+        n = 0
+        while time.perf_counter() - t0 < budget_s and n < self.R:
+            orc.sample_row(host[n], 0.8, 50, 0.9, orc.sample_u24(1234, n, 0))
+            n += 1
+        dt = time.perf_counter() - t0
+        return {"value": n * self.V * 4 / 1e9 / dt, "unit": self.unit, "cores": 1, "kind": "port",
+                "seconds": dt, "sample": f"{n} of 256 rows of config 3, serial reference algorithm"}
+
+    def config(self):
+        return {"workload": self.name, "rows": self.R, "vocab": self.V, "temperature": 0.8,
+                "top_k": 50, "top_p": 0.9, "seed": 1234,
+                "l2": "8 logits buffers rotate (262 MB > 126 MB L2)"}
+
+
+WORKLOADS = {"attention": AttentionWorkload, "sampling": SamplingWorkload}
 
 
 # -------------------------------------------------------------------- main

@@ -89,6 +89,18 @@ class rt_attn_params_t(ctypes.Structure):
                 ("chunk_pages", ctypes.c_uint32)]
 
 
+class rt_sample_row_t(ctypes.Structure):
+    _fields_ = [("temperature", ctypes.c_float), ("top_k", ctypes.c_uint32),
+                ("top_p", ctypes.c_float), ("rollout_id", ctypes.c_uint32),
+                ("step", ctypes.c_uint64)]
+
+
+class rt_sample_params_t(ctypes.Structure):
+    _fields_ = [("num_rows", ctypes.c_uint32), ("vocab", ctypes.c_uint32),
+                ("row_stride", ctypes.c_uint64), ("seed", ctypes.c_uint64),
+                ("fused_cum", ctypes.c_uint32)]
+
+
 # ------------------------------------------------------------------ loader
 _lib = None
 
@@ -105,6 +117,8 @@ _SIGS = {
     "rt_paged_decode_attention": (ctypes.c_int, [ctypes.POINTER(rt_attn_params_t), _P, _P, _P,
                                                  _P, _P, _P, ctypes.c_size_t, _P]),
     "rt_attn_workspace_error": (ctypes.c_int, [_P, _P, ctypes.POINTER(ctypes.c_int32)]),
+    "rt_sample_rows": (ctypes.c_int, [ctypes.POINTER(rt_sample_params_t), _P, _P, _P, _P]),
+    "rt_sample_uniform24": (ctypes.c_uint32, [ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint64]),
     "rt_fill_normal_bf16": (ctypes.c_int, [_P, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint32,
                                            ctypes.c_float, ctypes.c_float, _P]),
     "rt_fill_normal_f32": (ctypes.c_int, [_P, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint32,
@@ -202,3 +216,38 @@ def fill_normal_f32(t, seed, stream_id=0, mean=0.0, std=1.0, stream=None):
     check(lib().rt_fill_normal_f32(_ptr(t), t.numel(), seed, stream_id, mean, std,
                                    _stream_ptr(stream)), "rt_fill_normal_f32")
     return t
+
+
+# ----------------------------------------------------------------- sampler
+SAMPLE_ROW_BYTES = 24
+
+
+def sample_row_table(temperature, top_k, top_p, rollout_id, step):
+    """Pack per-row sampling parameters (rt_sample_row_t) into a numpy record
+    array; scalars broadcast."""
+    import numpy as np
+    dt = np.dtype([("temperature", "<f4"), ("top_k", "<u4"), ("top_p", "<f4"),
+                   ("rollout_id", "<u4"), ("step", "<u8")])
+    assert dt.itemsize == SAMPLE_ROW_BYTES
+    n = max(np.size(x) for x in (temperature, top_k, top_p, rollout_id, step))
+    t = np.zeros(n, dtype=dt)
+    t["temperature"], t["top_k"], t["top_p"] = temperature, top_k, top_p
+    t["rollout_id"], t["step"] = rollout_id, step
+    return t
+
+
+def sample_rows(logits, rows, vocab, seed, fused_cum=True, out=None, stream=None):
+    """rt_sample_rows: logits fp32 [R, stride] (device), rows = device uint8
+    tensor holding R rt_sample_row_t records; returns int32 tokens [R]."""
+    import torch
+    R = logits.shape[0]
+    if out is None:
+        out = torch.empty(R, dtype=torch.int32, device=logits.device)
+    p = rt_sample_params_t(R, vocab, logits.stride(0), seed, 1 if fused_cum else 0)
+    check(lib().rt_sample_rows(ctypes.byref(p), _ptr(logits), _ptr(rows), _ptr(out),
+                               _stream_ptr(stream)), "rt_sample_rows")
+    return out
+
+
+def sample_uniform24(seed, rollout_id, step) -> int:
+    return int(lib().rt_sample_uniform24(seed, rollout_id, step))

@@ -84,6 +84,51 @@ int rt_attn_plan(const rt_attn_params_t *p, uint32_t *chunk_pages,
                  uint32_t *max_chunks, uint64_t *ctas);
 
 /* ------------------------------------------------------------------------
+ * Fused sampler (replaces reference cu/sample.cu:40-123 sample_token).
+ *
+ * One call samples one token per row of fp32 logits with the reference's
+ * selection semantics, exactly:
+ *   1. temperature > 0: logits *= 1.0f / temperature (fp32);
+ *   2. 0 < top_k < vocab: keep entries >= the min(top_k,256)-th largest
+ *      value counted with multiplicity among values > -FLT_MAX (ties at the
+ *      cutoff survive); the rest become -FLT_MAX;
+ *   3. 0 < top_p < 1: m = max, sum = sequential fp32 sum of __expf(l - m) in
+ *      index order, inv = 1.0f / sum, walk cum += __expf(l - m) * inv and
+ *      return the first index with cum >= r (top_p only selects this walk;
+ *      there is no nucleus truncation, as in the reference); otherwise
+ *      walk cum += __expf(l - m) / sum; vocab - 1 if the walk never reaches r.
+ * The uniform r = (u & 0xFFFFFF) / 2^24 comes from Philox4x32-10 with
+ * key = seed and counter = {step lo, step hi, rollout_id, 0}, u = word 0
+ * (the reference draws it from per-trajectory xoshiro256** state instead).
+ * Logits are read once and not modified (the reference filters in place).
+ * ---------------------------------------------------------------------- */
+typedef struct {
+    float    temperature;
+    uint32_t top_k;          /* reference SampleState.top_k is uint16 */
+    float    top_p;
+    uint32_t rollout_id;     /* Philox counter word 2 */
+    uint64_t step;           /* Philox counter words 0..1 */
+} rt_sample_row_t;
+
+typedef struct {
+    uint32_t num_rows;
+    uint32_t vocab;          /* 1 .. 32768 */
+    uint64_t row_stride;     /* floats between consecutive rows (>= vocab) */
+    uint64_t seed;           /* Philox key */
+    uint32_t fused_cum;      /* 1: top-p walk accumulates with one fma
+                                (matches nvcc's default contraction of the
+                                reference), 0: separate multiply and add */
+} rt_sample_params_t;
+
+/* logits fp32 [num_rows][row_stride] (device), rows [num_rows] (device),
+ * tokens_out uint32 [num_rows] (device). */
+int rt_sample_rows(const rt_sample_params_t *p, const float *logits,
+                   const rt_sample_row_t *rows, uint32_t *tokens_out, void *stream);
+
+/* The 24-bit uniform rt_sample_rows uses for (seed, rollout_id, step). */
+uint32_t rt_sample_uniform24(uint64_t seed, uint32_t rollout_id, uint64_t step);
+
+/* ------------------------------------------------------------------------
  * Synthetic data (seeded, counter-based, reproducible on any GPU).
  * ---------------------------------------------------------------------- */
 /* n bf16 values ~ N(mean, std) from Philox4x32-10(key = seed,

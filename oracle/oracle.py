@@ -230,3 +230,52 @@ class Harness:
         fn = getattr(self.lib, name)
         n = fn(_ptr(log), *[_ptr(e) if isinstance(e, np.ndarray) else e for e in extra])
         return log[:n]
+
+
+# ------------------------------------------------------- reference on GPU
+_M64 = 1 << 64
+_INV5 = pow(5, -1, _M64)
+_INV9 = pow(9, -1, _M64)
+
+
+def xoshiro_s1_for_first_output(value: int) -> int:
+    """State word s1 that makes the reference's first xoshiro256** draw
+    (rotl(s1 * 5, 7) * 9, reference cu/sample.cu:13-14) equal `value`."""
+    x = (value * _INV9) % _M64
+    x = ((x >> 7) | (x << 57)) % _M64          # rotr 7
+    return (x * _INV5) % _M64
+
+
+class RefCuda:
+    """The reference's own cu/sample.cu compiled for sm_100a into
+    oracle/_ref/libref_cuda.so, driven by harness/ref_sample.cu."""
+
+    def __init__(self):
+        path = os.path.join(REF, "libref_cuda.so")
+        if not os.path.exists(path):
+            raise OSError(f"{path} missing: build oracle/_ref where the reference tree exists")
+        l = ctypes.CDLL(path)
+        l.hx_ref_sample_rows.restype = _int
+        l.hx_ref_sample_rows.argtypes = [_P, _u32, _u64, _P, _P, _P, _P, _P, _u32]
+        self.lib = l
+
+    def sample_rows(self, logits, vocab, temperature, top_k, top_p, u24):
+        """logits: torch fp32 [R, stride] on the GPU (copied; the reference
+        filters in place).  Per-row arrays are numpy.  Returns numpy uint32."""
+        import torch
+        R = logits.shape[0]
+        dev = logits.device
+        work = logits.clone()
+        bc = lambda x, dt: torch.from_numpy(np.ascontiguousarray(np.broadcast_to(x, R), dtype=dt)).to(dev)
+        t = bc(temperature, np.float32)
+        k = bc(top_k, np.int16)  # uint16 bits
+        p = bc(top_p, np.float32)
+        s1 = np.array([xoshiro_s1_for_first_output(int(u)) for u in np.broadcast_to(u24, R)],
+                      dtype=np.uint64)
+        s1t = torch.from_numpy(s1.view(np.int64)).to(dev)
+        out = torch.zeros(R, dtype=torch.int32, device=dev)
+        rc = self.lib.hx_ref_sample_rows(work.data_ptr(), vocab, work.stride(0), t.data_ptr(),
+                                         k.data_ptr(), p.data_ptr(), s1t.data_ptr(),
+                                         out.data_ptr(), R)
+        assert rc == 0, f"reference sampler failed: {rc}"
+        return out.cpu().numpy().view(np.uint32)

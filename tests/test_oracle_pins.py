@@ -130,3 +130,18 @@ def test_sample_oracle_semantics(orc):
     assert orc.sample_row(logits, 1.0, 1, 0.9, 0xFFFFFF) == 2
     # no top-p gate: division walk
     assert orc.sample_row(logits, 1.0, 0, 1.0, 0x800000) in (1, 2)
+
+
+def test_sampler_uniform_matches_oracle_philox(pkg, orc):
+    """rt_sample_uniform24 (product, host side) == oracle Philox stream."""
+    for seed, r, s in [(1234, 0, 0), (1234, 255, 0), (5, 77, 2**40 + 3), (2**63 + 1, 2**32 - 1, 7)]:
+        assert pkg.sample_uniform24(seed, r, s) == orc.sample_u24(seed, r, s)
+
+
+def test_xoshiro_inversion(orc):
+    """The reference's first xoshiro256** draw reproduces any injected value."""
+    M = 1 << 64
+    rotl = lambda x, k: ((x << k) | (x >> (64 - k))) % M
+    for v in [0, 1, 0xFFFFFF, 0x123456, 12345678]:
+        s1 = orc.xoshiro_s1_for_first_output(v)
+        assert (rotl((s1 * 5) % M, 7) * 9) % M == v

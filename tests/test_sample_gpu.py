@@ -1,0 +1,131 @@
+"""Fused sampler (rt_sample_rows) against the reference's own sample_token
+(reference cu/sample.cu, compiled unmodified for sm_100a into oracle/_ref)
+on identical logits and identical 24-bit uniforms: token ids bit-exact.
+The CPU oracle (expf instead of __expf) is checked with a tolerance."""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+SEED = 1234
+
+
+@pytest.fixture(scope="module")
+def refcuda(orc):
+    try:
+        return orc.RefCuda()
+    except OSError as e:
+        pytest.skip(str(e))
+
+
+def u24s(pkg, rollouts, steps, seed=SEED):
+    return np.array([pkg.sample_uniform24(seed, int(r), int(s)) for r, s in
+                     zip(np.broadcast_to(rollouts, np.broadcast(rollouts, steps).shape),
+                         np.broadcast_to(steps, np.broadcast(rollouts, steps).shape))],
+                    dtype=np.uint32)
+
+
+def run_mine(pkg, logits, vocab, T, k, p, rollouts, steps, fused=True, seed=SEED):
+    rows = pkg.sample_row_table(T, k, p, rollouts, steps)
+    rows_d = torch.from_numpy(rows.view(np.uint8)).to(logits.device)
+    out = pkg.sample_rows(logits, rows_d, vocab, seed, fused_cum=fused)
+    return out.cpu().numpy().view(np.uint32)
+
+
+def normal_logits(pkg, cuda, R, V, seed, std=2.0, stride=None):
+    t = torch.empty(R, stride or V, dtype=torch.float32, device=cuda)
+    pkg.fill_normal_f32(t, seed=seed, stream_id=3, std=std)
+    return t
+
+
+def test_c3_bit_exact_against_reference_kernel(pkg, orc, cuda, refcuda):
+    """256 rows x 32,000 logits ~ N(0, 2), T=0.8, k=50,
+    p=0.9, Philox seed 1234, counter = (rollout_id = row, step = 0)."""
+    R, V = 256, 32000
+    logits = normal_logits(pkg, cuda, R, V, seed=3)
+    rid = np.arange(R, dtype=np.uint32)
+    u = u24s(pkg, rid, 0)
+    ref = refcuda.sample_rows(logits, V, 0.8, 50, 0.9, u)
+    mine = run_mine(pkg, logits, V, 0.8, 50, 0.9, rid, 0, fused=True)
+    mine_nf = run_mine(pkg, logits, V, 0.8, 50, 0.9, rid, 0, fused=False)
+    n_eq = int((mine == ref).sum())
+    n_eq_nf = int((mine_nf == ref).sum())
+    assert n_eq == R, f"fused walk: {n_eq}/{R} equal (unfused: {n_eq_nf}/{R})"
+    # CPU oracle with expf: agrees except where r sits within rounding of a CDF step
+    host = logits.cpu().numpy()
+    cpu = np.array([orc.sample_row(host[i], 0.8, 50, 0.9, int(u[i])) for i in range(R)])
+    assert (cpu == ref).sum() >= R - 2
+
+
+@pytest.mark.parametrize("case", ["topk_off", "topk_ge_vocab", "topk_over_256", "no_topp",
+                                  "no_temperature", "k1", "small_vocab", "vocab_32768",
+                                  "ties_at_cutoff", "all_equal", "neg_inf", "nan_row",
+                                  "pos_inf_row", "huge_negative"])
+def test_edge_cases_bit_exact(pkg, cuda, refcuda, case):
+    R, V, T, k, p = 64, 4096, 0.8, 50, 0.9
+    stride = None
+    if case == "small_vocab":
+        V = 7
+    if case == "vocab_32768":
+        V, R = 32768, 32
+    logits = normal_logits(pkg, cuda, R, V, seed=hash(case) & 0xFFFF, stride=stride)
+    if case == "topk_off":
+        k = 0
+    elif case == "topk_ge_vocab":
+        k = V
+    elif case == "topk_over_256":
+        k = 1000
+    elif case == "no_topp":
+        p = 1.0
+    elif case == "no_temperature":
+        T = 0.0
+    elif case == "k1":
+        k = 1
+    elif case == "ties_at_cutoff":
+        logits = torch.round(logits)          # many exact ties
+    elif case == "all_equal":
+        logits.fill_(0.25)
+    elif case == "neg_inf":
+        logits[:, ::3] = -float("inf")
+    elif case == "nan_row":
+        logits[::2, 5] = float("nan")
+    elif case == "pos_inf_row":
+        logits[1::2, 17] = float("inf")
+    elif case == "huge_negative":
+        logits.fill_(-3.0e38)
+        logits[:, 3] = -3.3e38
+    rid = np.arange(R, dtype=np.uint32) + 77
+    step = np.arange(R, dtype=np.uint64) * 3 + 5
+    u = u24s(pkg, rid, step)
+    ref = refcuda.sample_rows(logits, V, T, k, p, u)
+    mine = run_mine(pkg, logits, V, T, k, p, rid, step)
+    assert np.array_equal(mine, ref), f"{(mine != ref).sum()} rows differ"
+
+
+def test_row_stride_and_determinism(pkg, cuda, refcuda):
+    R, V = 16, 1000
+    logits = normal_logits(pkg, cuda, R, V, seed=8, stride=1024)
+    rid = np.arange(R, dtype=np.uint32)
+    a = run_mine(pkg, logits, V, 1.0, 40, 0.5, rid, 9)
+    b = run_mine(pkg, logits, V, 1.0, 40, 0.5, rid, 9)
+    ref = refcuda.sample_rows(logits, V, 1.0, 40, 0.5, u24s(pkg, rid, 9))
+    assert np.array_equal(a, b) and np.array_equal(a, ref)
+
+
+def test_token_distribution_follows_softmax(pkg, cuda):
+    """Many draws of one row: empirical frequencies match the top-k softmax."""
+    V, k, T, N = 64, 8, 1.0, 8192
+    base = torch.linspace(-2, 2, V, device=cuda)
+    logits = base.repeat(N, 1).contiguous()
+    rid = np.zeros(N, dtype=np.uint32)
+    step = np.arange(N, dtype=np.uint64)
+    tok = run_mine(pkg, logits, V, T, k, 0.9, rid, step)
+    x = base.cpu().numpy().astype(np.float64)
+    keep = np.argsort(-x)[:k]
+    pr = np.zeros(V)
+    pr[keep] = np.exp(x[keep] - x[keep].max())
+    pr /= pr.sum()
+    freq = np.bincount(tok, minlength=V) / N
+    assert set(np.unique(tok)) <= set(keep)
+    assert np.abs(freq - pr).max() < 0.02
