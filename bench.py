@@ -261,7 +261,7 @@ class SamplingWorkload:
             t = torch.empty(self.R, self.V, dtype=torch.float32, device=dev)
             self.pkg.fill_normal_f32(t, seed=3 + rank, stream_id=100 + i, std=2.0)
             self.bufs.append(t)
-        rows = self.pkg.sample_row_table(0.8, 50, 0.9, np.arange(self.R, dtype=np.uint32), 0)
+        rows = self.pkg.sample_row_table(0.8, 50, 0.9, np.arange(self.R, dtype=np.uint32), 0, 1234)
         self.rows_np = rows
         self.rows = torch.from_numpy(rows.view(np.uint8)).to(dev)
         self.out = torch.empty(self.R, dtype=torch.int32, device=dev)
@@ -270,7 +270,7 @@ class SamplingWorkload:
         torch.cuda.synchronize()
 
     def step(self):
-        self.pkg.sample_rows(self.bufs[self.i % self.nbuf], self.rows, self.V, 1234, out=self.out)
+        self.pkg.sample_rows(self.bufs[self.i % self.nbuf], self.rows, self.V, out=self.out)
         self.i += 1
 
     def units_per_step(self):
@@ -285,7 +285,7 @@ class SamplingWorkload:
 
         def one():
             self.bufs[0].copy_(host, non_blocking=True)
-            self.pkg.sample_rows(self.bufs[0], self.rows, self.V, 1234, out=self.out)
+            self.pkg.sample_rows(self.bufs[0], self.rows, self.V, out=self.out)
             tok_h.copy_(self.out, non_blocking=True)
 
         for _ in range(warmup):

@@ -92,13 +92,47 @@ class rt_attn_params_t(ctypes.Structure):
 class rt_sample_row_t(ctypes.Structure):
     _fields_ = [("temperature", ctypes.c_float), ("top_k", ctypes.c_uint32),
                 ("top_p", ctypes.c_float), ("rollout_id", ctypes.c_uint32),
-                ("step", ctypes.c_uint64)]
+                ("step", ctypes.c_uint64), ("seed", ctypes.c_uint64)]
 
 
 class rt_sample_params_t(ctypes.Structure):
     _fields_ = [("num_rows", ctypes.c_uint32), ("vocab", ctypes.c_uint32),
-                ("row_stride", ctypes.c_uint64), ("seed", ctypes.c_uint64),
-                ("fused_cum", ctypes.c_uint32)]
+                ("row_stride", ctypes.c_uint64), ("fused_cum", ctypes.c_uint32),
+                ("row_enable", ctypes.c_void_p)]
+
+
+class KVArena(ctypes.Structure):
+    _fields_ = [("base", ctypes.c_void_p), ("capacity", ctypes.c_size_t),
+                ("block_size", ctypes.c_size_t), ("bitmap", ctypes.c_uint64 * 16384)]
+
+
+class rt_rollout_config_t(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_uint32) for n in (
+        "num_q_heads", "num_kv_heads", "vocab", "max_slots", "max_context", "max_new_tokens",
+        "max_admit", "drop_when_full", "decode_mode", "reward_mode")] + [
+        ("reward_seed", ctypes.c_uint64), ("logit_std", ctypes.c_float),
+        ("max_prefixes", ctypes.c_uint32), ("max_prefix_pages", ctypes.c_uint32),
+        ("max_passes", ctypes.c_uint64), ("idle_timeout_ms", ctypes.c_uint32),
+        ("chunk_pages", ctypes.c_uint32)]
+
+
+class rt_rollout_io_t(ctypes.Structure):
+    _fields_ = [("ring", ctypes.c_void_p), ("requests", ctypes.c_void_p),
+                ("n_requests", ctypes.c_uint32), ("done_ring", ctypes.c_void_p),
+                ("dones", ctypes.c_void_p), ("state", ctypes.c_void_p),
+                ("step_count", ctypes.c_void_p), ("trajectories", ctypes.c_void_p),
+                ("rewards", ctypes.c_void_p), ("n_rows", ctypes.c_uint32)]
+
+
+class rt_rollout_stats_t(ctypes.Structure):
+    _fields_ = [("passes", ctypes.c_uint64), ("tokens", ctypes.c_uint64),
+                ("consumed", ctypes.c_uint32), ("admitted", ctypes.c_uint32),
+                ("dropped", ctypes.c_uint32), ("done", ctypes.c_uint32),
+                ("max_active", ctypes.c_uint32), ("stopped_by_sentinel", ctypes.c_uint32),
+                ("error", ctypes.c_int32), ("attn_error", ctypes.c_int32)]
+
+    def as_dict(self):
+        return {n: getattr(self, n) for n, _ in self._fields_}
 
 
 # ------------------------------------------------------------------ loader
@@ -119,6 +153,24 @@ _SIGS = {
     "rt_attn_workspace_error": (ctypes.c_int, [_P, _P, ctypes.POINTER(ctypes.c_int32)]),
     "rt_sample_rows": (ctypes.c_int, [ctypes.POINTER(rt_sample_params_t), _P, _P, _P, _P]),
     "rt_sample_uniform24": (ctypes.c_uint32, [ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint64]),
+    "rt_rollout_create": (ctypes.c_int, [ctypes.POINTER(rt_rollout_config_t),
+                                         ctypes.POINTER(KVArena), ctypes.POINTER(_P)]),
+    "rt_rollout_destroy": (ctypes.c_int, [_P]),
+    "rt_rollout_set_prefix": (ctypes.c_int, [_P, ctypes.c_uint32, _P, ctypes.c_uint32,
+                                             ctypes.c_uint32]),
+    "rt_rollout_launch": (ctypes.c_int, [_P, ctypes.POINTER(rt_rollout_io_t), _P]),
+    "rt_rollout_wait": (ctypes.c_int, [_P, _P, ctypes.POINTER(rt_rollout_stats_t)]),
+    "rt_logits_synth": (ctypes.c_int, [_P, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_uint32,
+                                       ctypes.c_uint64, ctypes.c_float, _P]),
+    "rt_launch_rollout_worker": (ctypes.c_int, [_P, _P, _P, _P, ctypes.c_uint32, _P]),
+    "rt_host_pump": (ctypes.c_int64, [_P, _P, ctypes.c_uint32, _P, _P, ctypes.c_uint32,
+                                      ctypes.c_int, ctypes.c_uint32]),
+    "req_ring_create": (_P, []), "req_ring_destroy": (None, [_P]),
+    "done_ring_create": (_P, []), "done_ring_destroy": (None, [_P]),
+    "arena_init": (None, [ctypes.POINTER(KVArena), ctypes.c_size_t, ctypes.c_size_t]),
+    "arena_acquire": (ctypes.c_int64, [ctypes.POINTER(KVArena)]),
+    "arena_release": (None, [ctypes.POINTER(KVArena), ctypes.c_int64]),
+    "arena_destroy": (None, [ctypes.POINTER(KVArena)]),
     "rt_fill_normal_bf16": (ctypes.c_int, [_P, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint32,
                                            ctypes.c_float, ctypes.c_float, _P]),
     "rt_fill_normal_f32": (ctypes.c_int, [_P, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint32,
@@ -219,31 +271,32 @@ def fill_normal_f32(t, seed, stream_id=0, mean=0.0, std=1.0, stream=None):
 
 
 # ----------------------------------------------------------------- sampler
-SAMPLE_ROW_BYTES = 24
+SAMPLE_ROW_BYTES = 32
 
 
-def sample_row_table(temperature, top_k, top_p, rollout_id, step):
+def sample_row_table(temperature, top_k, top_p, rollout_id, step, seed):
     """Pack per-row sampling parameters (rt_sample_row_t) into a numpy record
     array; scalars broadcast."""
     import numpy as np
     dt = np.dtype([("temperature", "<f4"), ("top_k", "<u4"), ("top_p", "<f4"),
-                   ("rollout_id", "<u4"), ("step", "<u8")])
+                   ("rollout_id", "<u4"), ("step", "<u8"), ("seed", "<u8")])
     assert dt.itemsize == SAMPLE_ROW_BYTES
-    n = max(np.size(x) for x in (temperature, top_k, top_p, rollout_id, step))
+    n = max(np.size(x) for x in (temperature, top_k, top_p, rollout_id, step, seed))
     t = np.zeros(n, dtype=dt)
     t["temperature"], t["top_k"], t["top_p"] = temperature, top_k, top_p
-    t["rollout_id"], t["step"] = rollout_id, step
+    t["rollout_id"], t["step"], t["seed"] = rollout_id, step, seed
     return t
 
 
-def sample_rows(logits, rows, vocab, seed, fused_cum=True, out=None, stream=None):
+def sample_rows(logits, rows, vocab, fused_cum=True, out=None, row_enable=None, stream=None):
     """rt_sample_rows: logits fp32 [R, stride] (device), rows = device uint8
     tensor holding R rt_sample_row_t records; returns int32 tokens [R]."""
     import torch
     R = logits.shape[0]
     if out is None:
         out = torch.empty(R, dtype=torch.int32, device=logits.device)
-    p = rt_sample_params_t(R, vocab, logits.stride(0), seed, 1 if fused_cum else 0)
+    p = rt_sample_params_t(R, vocab, logits.stride(0), 1 if fused_cum else 0,
+                           None if row_enable is None else row_enable.data_ptr())
     check(lib().rt_sample_rows(ctypes.byref(p), _ptr(logits), _ptr(rows), _ptr(out),
                                _stream_ptr(stream)), "rt_sample_rows")
     return out
@@ -251,3 +304,136 @@ def sample_rows(logits, rows, vocab, seed, fused_cum=True, out=None, stream=None
 
 def sample_uniform24(seed, rollout_id, step) -> int:
     return int(lib().rt_sample_uniform24(seed, rollout_id, step))
+
+
+# ------------------------------------------------------------ rollout loop
+RT_ROLLOUT_DECODE_NONE, RT_ROLLOUT_DECODE_FULL = 0, 1
+RT_REWARD_MOCK, RT_REWARD_PHILOX = 0, 1
+PAGE_TOKENS = 16
+
+
+def page_bytes(num_kv_heads: int) -> int:
+    return num_kv_heads * 2 * 16 * 128 * 2
+
+
+class DeviceArena:
+    """A KVArena (arena.h) whose blocks live in a torch-allocated HBM buffer.
+    arena_acquire / arena_release from the C library manage the bitmap."""
+
+    def __init__(self, n_pages, num_kv_heads=8, device="cuda"):
+        import torch
+        self.block = page_bytes(num_kv_heads)
+        self.n_pages = n_pages
+        self.buf = torch.zeros(n_pages * self.block, dtype=torch.uint8, device=device)
+        self.c = KVArena()
+        self.c.base = self.buf.data_ptr()
+        self.c.capacity = n_pages * self.block
+        self.c.block_size = self.block
+
+    def acquire(self, n):
+        out = []
+        for _ in range(n):
+            b = lib().arena_acquire(ctypes.byref(self.c))
+            if b < 0:
+                raise RuntimeErrorRT("arena exhausted")
+            out.append(b)
+        return out
+
+    def bf16(self):
+        import torch
+        return self.buf.view(torch.bfloat16)
+
+    def fill_pages(self, pages, seed, stream_id=0):
+        """Fill whole pages with N(0,1) bf16 (synthetic prefill; contiguous runs)."""
+        import numpy as np
+        pages = np.sort(np.asarray(pages, dtype=np.int64))
+        if len(pages) == 0:
+            return
+        starts = np.concatenate([[0], np.nonzero(np.diff(pages) != 1)[0] + 1])
+        ends = np.concatenate([starts[1:], [len(pages)]])
+        v = self.bf16()
+        per = self.block // 2
+        for a, b in zip(starts, ends):
+            lo = int(pages[a]) * per
+            hi = (int(pages[b - 1]) + 1) * per
+            fill_normal_bf16(v[lo:hi], seed=seed, stream_id=stream_id + int(pages[a]))
+
+
+class RolloutEngine:
+    """rt_rollout_* (GPU-resident rollout loop).  cfg: dict of
+    rt_rollout_config_t fields (missing ones default to 0)."""
+
+    def __init__(self, cfg: dict, arena: DeviceArena | None = None):
+        self.cfg = rt_rollout_config_t(**cfg)
+        self.arena = arena
+        h = ctypes.c_void_p()
+        check(lib().rt_rollout_create(ctypes.byref(self.cfg),
+                                      ctypes.byref(arena.c) if arena else None,
+                                      ctypes.byref(h)), "rt_rollout_create")
+        self.h = h
+
+    def set_prefix(self, prefix_id, pages, token_len):
+        import numpy as np
+        arr = np.ascontiguousarray(pages, dtype=np.int32)
+        check(lib().rt_rollout_set_prefix(self.h, prefix_id, arr.ctypes.data_as(ctypes.c_void_p),
+                                          len(arr), token_len), "rt_rollout_set_prefix")
+
+    def launch(self, *, requests=None, n_requests=0, ring=None, done_ring=None, dones=None,
+               state=None, step_count=None, trajectories=None, rewards=None, n_rows=0,
+               stream=None):
+        ptr = lambda t: None if t is None else (t if isinstance(t, int) else t.data_ptr())
+        io = rt_rollout_io_t(ptr(ring), ptr(requests), n_requests, ptr(done_ring), ptr(dones),
+                             ptr(state), ptr(step_count), ptr(trajectories), ptr(rewards), n_rows)
+        check(lib().rt_rollout_launch(self.h, ctypes.byref(io), _stream_ptr(stream)),
+              "rt_rollout_launch")
+
+    def wait(self, stream=None, check_errors=True):
+        st = rt_rollout_stats_t()
+        rc = lib().rt_rollout_wait(self.h, _stream_ptr(stream), ctypes.byref(st))
+        if check_errors:
+            check(rc, "rt_rollout_wait")
+        return st.as_dict()
+
+    def close(self):
+        if self.h:
+            lib().rt_rollout_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 - interpreter shutdown
+            pass
+
+
+def logits_synth(out, vocab, seed, request_lo, token_index, logit_std, stream=None):
+    check(lib().rt_logits_synth(_ptr(out), vocab, seed, request_lo, token_index, logit_std,
+                                _stream_ptr(stream)), "rt_logits_synth")
+    return out
+
+
+class HostRings:
+    """A RequestRing and a DoneRing in pinned, device-mapped host memory."""
+
+    def __init__(self):
+        self.req = lib().req_ring_create()
+        self.done = lib().done_ring_create()
+        if not self.req or not self.done:
+            raise RuntimeErrorRT("ring allocation failed")
+
+    def pump(self, requests, n_expected, send_sentinel=True, timeout_ms=60000):
+        """rt_host_pump: requests is a numpy array of 34-byte RolloutRequest
+        records; returns the drained RolloutDone records (numpy bytes)."""
+        import numpy as np
+        reqs = np.ascontiguousarray(requests)
+        out = np.zeros(max(n_expected, 1) * 24, dtype=np.uint8)
+        n = lib().rt_host_pump(self.req, reqs.ctypes.data_as(ctypes.c_void_p), len(reqs),
+                               self.done, out.ctypes.data_as(ctypes.c_void_p), n_expected,
+                               1 if send_sentinel else 0, timeout_ms)
+        return n, out
+
+    def close(self):
+        if self.req:
+            lib().req_ring_destroy(self.req)
+            lib().done_ring_destroy(self.done)
+            self.req = self.done = None

@@ -31,6 +31,7 @@
 #include "kv_layout.h"
 #include "rlrt.h"
 #include "rt_common.cuh"
+#include "rt_internal.h"
 
 namespace {
 
@@ -430,23 +431,57 @@ int get_kv_map(const void *base, uint64_t rows, CUtensorMap *out)
     return RT_OK;
 }
 
+// Opt-in to > 48 KiB dynamic shared memory, once per device and group size.
+template <int G>
+int prepare_g()
+{
+    static std::mutex mu;
+    static bool done[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess)
+        return rt::cuda_fail(e, "attention: cudaGetDevice");
+    std::lock_guard<std::mutex> lk(mu);
+    if (dev < 64 && done[dev])
+        return RT_OK;
+    e = cudaFuncSetAttribute(paged_gqa_decode_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kSmemBytes);
+    if (e != cudaSuccess)
+        return rt::cuda_fail(e, "attention: cudaFuncSetAttribute");
+    if (dev < 64)
+        done[dev] = true;
+    return RT_OK;
+}
+
+int prepare_group(uint32_t g)
+{
+    switch (g) {
+    case 1: return prepare_g<1>();
+    case 2: return prepare_g<2>();
+    case 4: return prepare_g<4>();
+    default: return prepare_g<8>();
+    }
+}
+
 template <int G>
 int launch_g(const CUtensorMap &map, const AttnArgs &args, dim3 grid, cudaStream_t s)
 {
-    static std::once_flag once;
-    static cudaError_t attr_err = cudaSuccess;
-    std::call_once(once, [] {
-        attr_err = cudaFuncSetAttribute(paged_gqa_decode_kernel<G>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    });
-    if (attr_err != cudaSuccess)
-        return rt::cuda_fail(attr_err, "attention: cudaFuncSetAttribute");
+    int rc = prepare_g<G>();
+    if (rc != RT_OK)
+        return rc;
     paged_gqa_decode_kernel<G><<<grid, kWarps * 32, kSmemBytes, s>>>(map, args);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? RT_OK : rt::cuda_fail(e, "attention: launch");
 }
 
 }  // namespace
+
+int rt::attn_prepare(const rt_attn_params_t *p)
+{
+    Plan pl;
+    int rc = make_plan(p, &pl);
+    return rc == RT_OK ? prepare_group(pl.group) : rc;
+}
 
 extern "C" size_t rt_attn_workspace_bytes(const rt_attn_params_t *p)
 {

@@ -1,0 +1,59 @@
+/* pump.c - host producer/consumer for a ring-fed GPU rollout run. */
+#define _POSIX_C_SOURCE 200112L
+#include <string.h>
+#include <time.h>
+
+#include "rlrt.h"
+
+static uint64_t
+pump_now_ms(void)
+{
+    struct timespec ts;
+    clock_gettime(CLOCK_MONOTONIC, &ts);
+    return (uint64_t)ts.tv_sec * 1000u + (uint64_t)ts.tv_nsec / 1000000u;
+}
+
+int64_t
+rt_host_pump(RequestRing *rq, const RolloutRequest *reqs, uint32_t n, DoneRing *dn,
+             RolloutDone *dones, uint32_t n_expected, int send_sentinel, uint32_t timeout_ms)
+{
+    uint32_t pushed = 0, drained = 0;
+    int sentinel_sent = !send_sentinel;
+    const uint64_t t0 = pump_now_ms();
+
+    if (!rq || !dn || (n && !reqs) || (n_expected && !dones))
+        return -1;
+    while (drained < n_expected || pushed < n || !sentinel_sent) {
+        int progress = 0;
+        while (pushed < n) {
+            uint32_t pos = req_ring_acquire(rq);
+            if (pos == UINT32_MAX)
+                break;
+            rq->slots[pos] = reqs[pushed++];
+            req_ring_commit(rq);
+            progress = 1;
+        }
+        if (pushed == n && !sentinel_sent && drained >= n_expected) {
+            uint32_t pos = req_ring_acquire(rq);
+            if (pos != UINT32_MAX) {
+                RolloutRequest s;
+                memset(&s, 0, sizeof(s));
+                s.request_id = RT_REQUEST_SENTINEL;
+                rq->slots[pos] = s;
+                req_ring_commit(rq);
+                sentinel_sent = 1;
+                progress = 1;
+            }
+        }
+        while (drained < n_expected && done_ring_pop(dn, &dones[drained]))
+            drained++, progress = 1;
+        if (!progress) {
+            if (timeout_ms && pump_now_ms() - t0 > timeout_ms)
+                return -1;
+#if defined(__x86_64__)
+            __asm__ volatile("pause" ::: "memory");
+#endif
+        }
+    }
+    return (int64_t)drained;
+}

@@ -1,0 +1,958 @@
+// rollout.cu - the GPU-resident rollout loop (scheduler + decode step).
+//
+// Reference: cu/gpu_scheduler.cu:4-83 (rollout_worker, find_free_slot,
+// release_slot).  The reference runs one persistent thread that, per pass,
+// admits at most one request and then walks the 256 slots, finishing or
+// "decoding" (tokens_generated++) each active one.  Here a pass is a chain of
+// kernels captured once into a CUDA graph whose body repeats under a device
+// controlled WHILE conditional node, so the loop runs without the host:
+//
+//   schedule_kernel  1 CTA x 256 threads (thread s <-> slot s): commit the
+//                    previous pass's sampled tokens, admit requests, retire
+//                    finished slots in slot order (RolloutDone), plan this
+//                    pass (sequence lengths, sampling rows), decide whether
+//                    the loop continues (cudaGraphSetConditional).
+//   prepare_kernel   1 CTA per active slot: copy-on-write of a shared
+//                    prefix's partial last page on the first write, q and
+//                    the new token's K/V from Philox N(0,1) into the arena.
+//   attention        rt_paged_decode_attention over all slots (idle slots
+//                    have length 0 and cost one early-exit CTA each).
+//   logits_kernel    synthetic logits ~ N(0, logit_std), Philox.
+//   sampler          rt_sample_rows with the per-slot enable mask.
+//
+// Counter-only decode (the reference's mock) uses the same schedule pass
+// with tokens_generated++ in place of the decode chain; the drop-in launcher
+// rt_launch_rollout_worker runs that pass in a persistent single-CTA kernel.
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+#include <new>
+
+#include "kv_layout.h"
+#include "reward.h"
+#include "rlrt.h"
+#include "rt_common.cuh"
+#include "rt_internal.h"
+
+namespace {
+
+constexpr int kSched = 256;  // schedule CTA: one thread per slot (GPU_MAX_ROLLOUTS)
+constexpr uint64_t kDonePushLimitNs = 10000000000ull;  // 10 s bounded wait on a full done ring
+
+struct RtIo {
+    RequestRing *ring;
+    const RolloutRequest *reqs;
+    uint32_t n_reqs;
+    DoneRing *done_ring;
+    RolloutDone *dones;
+    GpuRolloutState *state;
+    unsigned long long *step_count;
+    uint32_t *traj;
+    float *rewards;
+    uint32_t n_rows;
+};
+
+struct RtCtl {
+    unsigned long long passes, tokens, idle_since;
+    uint32_t consumed, admitted, dropped, done, max_active, sentinel;
+    int32_t error;
+    uint32_t stop;
+};
+
+struct SlotExt {
+    uint32_t row, request_lo, pos, ctx_len, last_token, decoding, cow_rows;
+    int32_t cow_src;
+    uint64_t seed;
+};
+
+struct Dev {
+    // configuration
+    uint32_t max_slots, max_admit, drop, decode, reward_mode, vocab, maxp, ppriv, max_new;
+    uint32_t hq, hkv, max_prefixes;
+    uint64_t reward_seed, max_passes, idle_ns;
+    float logit_std;
+    // device state
+    RtIo *io;
+    RtCtl *ctl;
+    SlotExt *ext;
+    int32_t *page_table;  // [max_slots][maxp]
+    int32_t *priv;        // [max_slots][ppriv]
+    int32_t *seq_lens;    // [max_slots]
+    uint32_t *enable;     // [max_slots]
+    rt_sample_row_t *srows;
+    uint32_t *tokens;     // [max_slots]
+    __nv_bfloat16 *q;     // [max_slots][hq][128]
+    float *attn_out;      // [max_slots][hq][128]
+    __nv_bfloat16 *arena;
+    float *logits;        // [max_slots][vocab]
+    uint32_t *pf_len, *pf_np, *pf_off;
+    int32_t *pf_pages;
+};
+
+__device__ __forceinline__ float reward_for(const Dev &d, uint32_t request_lo, uint32_t tokens)
+{
+    if (d.reward_mode == RT_REWARD_PHILOX) {
+        uint32_t x[4];
+        rt::philox4x32_10(request_lo, 0u, 0x52455744u, 0u, (uint32_t)d.reward_seed,
+                          (uint32_t)(d.reward_seed >> 32), x);
+        return (float)(x[0] >> 8) * (1.0f / 16777216.0f);
+    }
+    return reward_score_mock_inline(tokens);
+}
+
+// ---- request source / done sink (thread 0 only) ----
+__device__ bool src_peek(const RtIo &io, const RtCtl *ctl, RolloutRequest *out)
+{
+    if (io.ring) {
+        const uint32_t head = rt_load_relaxed_u32(&io.ring->cons.head);
+        const uint32_t tail = rt_load_acquire_u32(&io.ring->prod.tail);
+        if (head == tail)
+            return false;
+        rt_copy_bytes(out, &io.ring->slots[head & (REQUEST_RING_SIZE - 1)], sizeof(RolloutRequest));
+        return true;
+    }
+    if (ctl->consumed + ctl->sentinel >= io.n_reqs)
+        return false;
+    rt_copy_bytes(out, &io.reqs[ctl->consumed + ctl->sentinel], sizeof(RolloutRequest));
+    return true;
+}
+
+__device__ void src_pop(const RtIo &io)
+{
+    if (io.ring) {
+        const uint32_t head = rt_load_relaxed_u32(&io.ring->cons.head);
+        rt_store_release_u32(&io.ring->cons.head, head + 1u);
+    }
+}
+
+__device__ bool src_empty(const RtIo &io, const RtCtl *ctl)
+{
+    if (io.ring)
+        return rt_load_relaxed_u32(&io.ring->cons.head) == rt_load_acquire_u32(&io.ring->prod.tail);
+    return ctl->consumed + ctl->sentinel >= io.n_reqs;
+}
+
+// Reference done_ring_push semantics per attempt (overflow++ on a full
+// ring); the spin is bounded so an absent consumer cannot hang the GPU.
+__device__ bool sink_push(const RtIo &io, RtCtl *ctl, const RolloutDone &rec)
+{
+    if (!io.done_ring) {
+        if (io.dones && ctl->done < io.n_rows)
+            io.dones[ctl->done] = rec;
+        return true;
+    }
+    if (done_ring_push(io.done_ring, &rec) == 0)
+        return true;
+    const uint64_t t0 = rt::globaltimer_ns();
+    while (done_ring_push(io.done_ring, &rec) != 0) {
+        __nanosleep(200);
+        if (rt::globaltimer_ns() - t0 > kDonePushLimitNs)
+            return false;
+    }
+    return true;
+}
+
+// Lowest free slot below max_slots (reference find_free_slot order).
+__device__ int take_lowest_free(GpuRolloutState *st, uint32_t max_slots)
+{
+    for (uint32_t w = 0; w < (GPU_MAX_ROLLOUTS + 63) / 64; w++) {
+        uint64_t free_bits = ~st->bitmap[w];
+        const uint32_t lo = w * 64u;
+        if (lo >= max_slots)
+            break;
+        if (max_slots - lo < 64u)
+            free_bits &= (1ull << (max_slots - lo)) - 1ull;
+        if (free_bits) {
+            const int b = __ffsll((long long)free_bits) - 1;
+            st->bitmap[w] |= 1ull << b;
+            return (int)(lo + (uint32_t)b);
+        }
+    }
+    return -1;
+}
+
+struct SchedShared {
+    uint32_t fin[kSched];
+    uint32_t fin_tokens[kSched];
+    uint32_t fin_req[kSched];
+    uint32_t stop, n_fin;
+};
+
+// One pass of the reference rollout_worker loop (see file comment).
+// Returns true when the loop must stop.  All 256 threads call it.
+__device__ bool schedule_pass(const Dev &d, SchedShared &sh)
+{
+    const uint32_t s = threadIdx.x;
+    const RtIo io = *d.io;
+    RtCtl *ctl = d.ctl;
+    GpuRolloutState *st = io.state;
+    const bool full = d.decode == RT_ROLLOUT_DECODE_FULL;
+
+    // 1. commit the tokens sampled in the previous pass
+    const bool committing = full && s < d.max_slots && d.ext[s].decoding;
+    if (committing) {
+        SlotExt &e = d.ext[s];
+        GpuRolloutSlot &rs = st->slots[s];
+        const uint32_t tok = d.tokens[s];
+        const uint32_t g = rs.tokens_generated;
+        if (io.traj && e.row < io.n_rows && g < d.max_new)
+            io.traj[(size_t)e.row * d.max_new + g] = tok;
+        rs.tokens_generated = g + 1u;
+        e.pos += 1u;
+        e.last_token = tok;
+        e.decoding = 0u;
+    }
+    if (s == 0)
+        sh.stop = 0u;
+    const uint32_t n_commit = __syncthreads_count(committing);
+    if (s == 0)
+        ctl->tokens += n_commit;
+
+    // 2. admission, in source order, lowest free slot first
+    if (s == 0) {
+        for (uint32_t a = 0; a < d.max_admit; a++) {
+            RolloutRequest rq;
+            if (!src_peek(io, ctl, &rq))
+                break;
+            if (rq.request_id == RT_REQUEST_SENTINEL) {
+                src_pop(io);
+                ctl->sentinel = 1u;
+                sh.stop = 1u;
+                break;
+            }
+            const int slot = take_lowest_free(st, d.max_slots);
+            if (slot < 0) {
+                if (!d.drop)
+                    break;              // backpressure: leave it queued
+                src_pop(io);            // reference: consumed and lost
+                ctl->consumed++;
+                ctl->dropped++;
+                continue;
+            }
+            src_pop(io);
+            const uint32_t row = ctl->consumed++;
+            ctl->admitted++;
+            GpuRolloutSlot &rs = st->slots[slot];
+            rs.active = 1u;
+            rs.request_id = (uint32_t)(rq.request_id & 0xFFFFFFFFull);
+            rs.tokens_generated = 0u;
+            rs.max_tokens = rq.max_tokens;
+            rs.kv_blocks = rq.kv_blocks;
+            rs.rng_state[0] = rq.rng_seed;
+            rs.rng_state[1] = rq.rng_seed ^ 0x9e3779b97f4a7c15ULL;
+            rs.rng_state[2] = (rq.rng_seed << 17) ^ 0x3c6ef372fe94f82aULL;
+            rs.rng_state[3] = ~rq.rng_seed;
+            rs.temperature = rq.temperature;
+            rs.top_k = rq.top_k;
+            rs.top_p = rq.top_p;
+            if (full) {
+                SlotExt &e = d.ext[slot];
+                const uint32_t pfx = RT_REQUEST_PREFIX(rq.request_id);
+                uint32_t ctx = 0, np = 0, off = 0;
+                if (pfx != 0u && pfx - 1u < d.max_prefixes) {
+                    ctx = d.pf_len[pfx - 1u];
+                    np = d.pf_np[pfx - 1u];
+                    off = d.pf_off[pfx - 1u];
+                }
+                // keep the context inside the page table / private pages
+                const uint32_t cap = d.maxp * 16u;
+                if (ctx > cap)
+                    ctx = cap;
+                e.row = row;
+                e.request_lo = rs.request_id;
+                e.ctx_len = ctx;
+                e.pos = ctx;
+                e.last_token = 0u;
+                e.decoding = 0u;
+                e.seed = rq.rng_seed;
+                int32_t *pt = d.page_table + (size_t)slot * d.maxp;
+                const int32_t *priv = d.priv + (size_t)slot * d.ppriv;
+                const uint32_t full_pages = ctx / 16u;
+                for (uint32_t i = 0; i < full_pages && i < np; i++)
+                    pt[i] = d.pf_pages[off + i];
+                uint32_t next = 0;
+                if ((ctx & 15u) && full_pages < np) {
+                    e.cow_src = d.pf_pages[off + full_pages];
+                    e.cow_rows = ctx & 15u;
+                } else {
+                    e.cow_src = -1;
+                    e.cow_rows = 0u;
+                }
+                for (uint32_t i = full_pages; i < d.maxp && next < d.ppriv; i++)
+                    pt[i] = priv[next++];
+            }
+        }
+    }
+    __syncthreads();
+    if (sh.stop)
+        return true;  // reference: the sentinel ends the worker before the scan
+
+    // 3. retire finished slots, in slot order
+    uint32_t fin = 0;
+    if (s < d.max_slots) {
+        const GpuRolloutSlot &rs = st->slots[s];
+        if (rs.active && rs.tokens_generated >= rs.max_tokens) {
+            fin = 1u;
+            sh.fin_tokens[s] = rs.tokens_generated;
+            sh.fin_req[s] = rs.request_id;
+        }
+    }
+    sh.fin[s] = fin;
+    const uint32_t n_fin = __syncthreads_count(fin);
+    if (n_fin && s == 0) {
+        for (uint32_t k = 0; k < d.max_slots; k++) {
+            if (!sh.fin[k])
+                continue;
+            RolloutDone rec;
+            rec.request_id = sh.fin_req[k];
+            rec.rollout_id = k;
+            rec.tokens_generated = sh.fin_tokens[k];
+            rec.reward = reward_for(d, sh.fin_req[k], sh.fin_tokens[k]);
+            rec.status = 0u;
+            if (!sink_push(io, ctl, rec)) {
+                ctl->error = RT_ETIMEOUT;
+                sh.stop = 1u;
+                break;
+            }
+            ctl->done++;
+        }
+        if (io.step_count)
+            atomicAdd(io.step_count, (unsigned long long)n_fin);
+    }
+    __syncthreads();
+    if (fin) {
+        GpuRolloutSlot &rs = st->slots[s];
+        rs.active = 0u;
+        atomicAnd((unsigned long long *)&st->bitmap[s / 64u], ~(1ull << (s % 64u)));
+        if (io.rewards && full && d.ext[s].row < io.n_rows)
+            io.rewards[d.ext[s].row] = reward_for(d, sh.fin_req[s], sh.fin_tokens[s]);
+    }
+    if (sh.stop)
+        return true;
+
+    // 4. this pass's decode: every slot still active generates one token
+    uint32_t act = 0;
+    if (s < d.max_slots) {
+        GpuRolloutSlot &rs = st->slots[s];
+        act = rs.active && !fin;
+        if (full) {
+            SlotExt &e = d.ext[s];
+            const bool room = e.pos < d.maxp * 16u;
+            if (act && !room) {
+                act = 0u;  // context full: counts as an error, slot is left idle
+                atomicCAS(&ctl->error, 0, RT_EDEVICE);
+            }
+            d.enable[s] = act;
+            d.seq_lens[s] = act ? (int32_t)(e.pos + 1u) : 0;
+            if (act) {
+                e.decoding = 1u;
+                rt_sample_row_t r;
+                r.temperature = rs.temperature;
+                r.top_k = rs.top_k;
+                r.top_p = rs.top_p;
+                r.rollout_id = e.request_lo;
+                r.step = rs.tokens_generated;
+                r.seed = e.seed;
+                d.srows[s] = r;
+            }
+        } else if (act) {
+            rs.tokens_generated++;  // the reference's counter-only decode
+        }
+    }
+    const uint32_t n_act = __syncthreads_count(act);
+
+    // 5. loop control
+    if (s == 0) {
+        ctl->passes++;
+        if (!full)
+            ctl->tokens += n_act;  // full decode counts tokens when they are committed
+        if (n_act > ctl->max_active)
+            ctl->max_active = n_act;
+        bool stop = ctl->error != 0;
+        if (n_act == 0u && !io.ring && src_empty(io, ctl))
+            stop = true;
+        if (n_act == 0u && io.ring && src_empty(io, ctl)) {
+            const uint64_t now = rt::globaltimer_ns();
+            if (ctl->idle_since == 0ull)
+                ctl->idle_since = now;
+            else if (now - ctl->idle_since > d.idle_ns) {
+                ctl->error = RT_ETIMEOUT;
+                stop = true;
+            }
+        } else {
+            ctl->idle_since = 0ull;
+        }
+        if (ctl->passes >= d.max_passes) {
+            ctl->error = RT_ETIMEOUT;
+            stop = true;
+        }
+        sh.stop = stop ? 1u : 0u;
+    }
+    __syncthreads();
+    return sh.stop != 0u;
+}
+
+__global__ void __launch_bounds__(kSched, 1)
+schedule_kernel(const Dev d, cudaGraphConditionalHandle handle)
+{
+    __shared__ SchedShared sh;
+    const bool stop = schedule_pass(d, sh);
+    if (threadIdx.x == 0) {
+        if (stop) {
+            d.ctl->stop = 1u;
+            for (uint32_t s = 0; s < d.max_slots; s++)
+                d.enable[s] = 0u;
+        }
+        cudaGraphSetConditional(handle, stop ? 0u : 1u);
+    }
+}
+
+__global__ void __launch_bounds__(256) prepare_kernel(const Dev d)
+{
+    const uint32_t s = blockIdx.x;
+    if (!d.enable[s])
+        return;
+    SlotExt &e = d.ext[s];
+    const int32_t *pt = d.page_table + (size_t)s * d.maxp;
+    const int32_t cow = e.cow_src;
+    if (cow >= 0) {
+        // first write into a shared prefix's partial page: private copy
+        const uint64_t page_elems = rt_page_bytes(d.hkv) / 2u;
+        const uint4 *src = reinterpret_cast<const uint4 *>(d.arena + (uint64_t)cow * page_elems);
+        uint4 *dst = reinterpret_cast<uint4 *>(d.arena + (uint64_t)pt[e.ctx_len >> 4] * page_elems);
+        const uint32_t n16 = (uint32_t)(rt_page_bytes(d.hkv) / 16u);
+        for (uint32_t i = threadIdx.x; i < n16; i += blockDim.x)
+            dst[i] = src[i];
+        __syncthreads();
+        if (threadIdx.x == 0)
+            e.cow_src = -1;
+    }
+    const uint32_t pos = e.pos, lt = e.last_token, rq = e.request_lo;
+    const uint64_t seed = e.seed;
+    const uint64_t page = (uint64_t)pt[pos >> 4];
+    const uint32_t row = pos & 15u;
+    // new token's K and V: hkv heads x 2 planes x 128 dims, 4 per Philox block
+    for (uint32_t g = threadIdx.x; g < d.hkv * 2u * 32u; g += blockDim.x) {
+        const uint32_t h = g >> 6, plane = (g >> 5) & 1u, d4 = g & 31u;
+        float z[4];
+        rt::philox_normal4(seed, pos, rq, 0x6B000000u | (plane << 8) | h, z, (lt << 5) | d4);
+        __nv_bfloat16 *dst = d.arena + rt_page_elem_offset(page, h, plane, row, d.hkv) + d4 * 4u;
+        reinterpret_cast<uint2 *>(dst)[0] =
+            make_uint2(rt::pack_bf16x2(z[0], z[1]), rt::pack_bf16x2(z[2], z[3]));
+    }
+    // query: hq heads x 128 dims
+    for (uint32_t g = threadIdx.x; g < d.hq * 32u; g += blockDim.x) {
+        const uint32_t h = g >> 5, d4 = g & 31u;
+        float z[4];
+        rt::philox_normal4(seed, pos, rq, 0x71000000u | h, z, (lt << 5) | d4);
+        __nv_bfloat16 *dst = d.q + ((size_t)s * d.hq + h) * 128u + d4 * 4u;
+        reinterpret_cast<uint2 *>(dst)[0] =
+            make_uint2(rt::pack_bf16x2(z[0], z[1]), rt::pack_bf16x2(z[2], z[3]));
+    }
+}
+
+// logits[v] = std * N(0,1), Philox key = seed, counter = (token index lo,
+// request low 32, tag | token index hi, v / 4).
+__device__ __forceinline__ void logits_row(float *out, uint32_t vocab, uint64_t seed,
+                                           uint32_t request_lo, uint64_t tix, float stdv,
+                                           uint32_t start, uint32_t stride)
+{
+    const uint32_t groups = (vocab + 3u) / 4u;
+    for (uint32_t g = start; g < groups; g += stride) {
+        float z[4];
+        rt::philox_normal4(seed, (uint32_t)tix, request_lo,
+                           0x4C000000u | (uint32_t)((tix >> 32) & 0xFFFFu), z, g);
+        const uint32_t v = g * 4u;
+        if (v + 3u < vocab && ((reinterpret_cast<uintptr_t>(out + v) & 15u) == 0u)) {
+            reinterpret_cast<float4 *>(out + v)[0] =
+                make_float4(stdv * z[0], stdv * z[1], stdv * z[2], stdv * z[3]);
+        } else {
+            for (uint32_t k = 0; k < 4u && v + k < vocab; k++)
+                out[v + k] = stdv * z[k];
+        }
+    }
+}
+
+__global__ void __launch_bounds__(256) logits_kernel(const Dev d)
+{
+    const uint32_t s = blockIdx.y;
+    if (!d.enable[s])
+        return;
+    const rt_sample_row_t r = d.srows[s];
+    logits_row(d.logits + (size_t)s * d.vocab, d.vocab, r.seed, r.rollout_id, r.step, d.logit_std,
+               blockIdx.x * blockDim.x + threadIdx.x, gridDim.x * blockDim.x);
+}
+
+__global__ void logits_synth_kernel(float *out, uint32_t vocab, uint64_t seed, uint32_t rq,
+                                    uint64_t tix, float stdv)
+{
+    logits_row(out, vocab, seed, rq, tix, stdv, blockIdx.x * blockDim.x + threadIdx.x,
+               gridDim.x * blockDim.x);
+}
+
+// Persistent single-CTA worker: the reference's pass loop, counter-only.
+__global__ void __launch_bounds__(kSched, 1) persistent_worker_kernel(const Dev d)
+{
+    __shared__ SchedShared sh;
+    for (;;) {
+        if (schedule_pass(d, sh))
+            break;
+        if (threadIdx.x == 0 && d.ctl->idle_since != 0ull)
+            __nanosleep(1000);
+        __syncthreads();
+    }
+    if (threadIdx.x == 0)
+        d.ctl->stop = 1u;
+}
+
+template <typename T>
+cudaError_t dalloc(T **p, size_t count)
+{
+    return cudaMalloc(reinterpret_cast<void **>(p), count * sizeof(T) + 16);
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------- engine
+struct rt_rollout {
+    rt_rollout_config_t cfg;
+    Dev d;
+    KVArena *arena;
+    int64_t *priv_blocks;  // host list of reserved arena blocks (released on destroy)
+    uint32_t n_priv;
+    rt_attn_params_t ap;
+    void *attn_ws;
+    size_t attn_ws_bytes;
+    uint32_t pf_used;
+    int device;
+    cudaStream_t cap;
+    cudaGraph_t graph;
+    cudaGraphExec_t exec;
+    RtIo *io_stage;  // pinned host staging of the io block
+};
+
+namespace {
+
+int engine_build_graph(rt_rollout *e)
+{
+    cudaError_t err;
+    cudaGraphConditionalHandle h;
+    if ((err = cudaGraphCreate(&e->graph, 0)) != cudaSuccess)
+        return rt::cuda_fail(err, "rollout: cudaGraphCreate");
+    if ((err = cudaGraphConditionalHandleCreate(&h, e->graph, 1, cudaGraphCondAssignDefault)) !=
+        cudaSuccess)
+        return rt::cuda_fail(err, "rollout: cudaGraphConditionalHandleCreate");
+    // cudaGraphNodeParams has no default constructor in C++: zeroed storage
+    alignas(cudaGraphNodeParams) unsigned char storage[sizeof(cudaGraphNodeParams)];
+    memset(storage, 0, sizeof(storage));
+    cudaGraphNodeParams &cp = *reinterpret_cast<cudaGraphNodeParams *>(storage);
+    cp.type = cudaGraphNodeTypeConditional;
+    cp.conditional.handle = h;
+    cp.conditional.type = cudaGraphCondTypeWhile;
+    cp.conditional.size = 1;
+    cudaGraphNode_t node;
+    if ((err = cudaGraphAddNode(&node, e->graph, nullptr, 0, &cp)) != cudaSuccess)
+        return rt::cuda_fail(err, "rollout: cudaGraphAddNode(conditional)");
+    cudaGraph_t body = cp.conditional.phGraph_out[0];
+
+    if ((err = cudaStreamBeginCaptureToGraph(e->cap, body, nullptr, nullptr, 0,
+                                             cudaStreamCaptureModeThreadLocal)) != cudaSuccess)
+        return rt::cuda_fail(err, "rollout: cudaStreamBeginCaptureToGraph");
+    int rc = RT_OK;
+    const Dev &d = e->d;
+    schedule_kernel<<<1, kSched, 0, e->cap>>>(d, h);
+    if (e->cfg.decode_mode == RT_ROLLOUT_DECODE_FULL) {
+        prepare_kernel<<<d.max_slots, 256, 0, e->cap>>>(d);
+        rc = rt_paged_decode_attention(&e->ap, d.q, d.arena, d.page_table, d.seq_lens, d.attn_out,
+                                       e->attn_ws, e->attn_ws_bytes, e->cap);
+        if (rc == RT_OK) {
+            const dim3 lg((d.vocab / 4u + 1023u) / 1024u, d.max_slots);
+            logits_kernel<<<lg, 256, 0, e->cap>>>(d);
+            rt_sample_params_t sp;
+            sp.num_rows = d.max_slots;
+            sp.vocab = d.vocab;
+            sp.row_stride = d.vocab;
+            sp.fused_cum = 1u;
+            sp.row_enable = d.enable;
+            rc = rt_sample_rows(&sp, d.logits, d.srows, d.tokens, e->cap);
+        }
+    }
+    cudaGraph_t captured = nullptr;
+    err = cudaStreamEndCapture(e->cap, &captured);
+    if (rc != RT_OK)
+        return rc;
+    if (err != cudaSuccess)
+        return rt::cuda_fail(err, "rollout: cudaStreamEndCapture");
+    if ((err = cudaGraphInstantiate(&e->exec, e->graph, 0)) != cudaSuccess)
+        return rt::cuda_fail(err, "rollout: cudaGraphInstantiate");
+    return RT_OK;
+}
+
+void engine_free(rt_rollout *e)
+{
+    if (!e)
+        return;
+    if (e->exec)
+        cudaGraphExecDestroy(e->exec);
+    if (e->graph)
+        cudaGraphDestroy(e->graph);
+    if (e->cap)
+        cudaStreamDestroy(e->cap);
+    void *bufs[] = {e->d.io, e->d.ctl, e->d.ext, e->d.page_table, e->d.priv, e->d.seq_lens,
+                    e->d.enable, e->d.srows, e->d.tokens, e->d.q, e->d.attn_out, e->d.logits,
+                    e->d.pf_len, e->d.pf_np, e->d.pf_off, e->d.pf_pages, e->attn_ws};
+    for (void *p : bufs)
+        if (p)
+            cudaFree(p);
+    if (e->io_stage)
+        cudaFreeHost(e->io_stage);
+    if (e->arena && e->priv_blocks)
+        for (uint32_t i = 0; i < e->n_priv; i++)
+            arena_release(e->arena, e->priv_blocks[i]);
+    free(e->priv_blocks);
+    delete e;
+}
+
+}  // namespace
+
+extern "C" int rt_rollout_create(const rt_rollout_config_t *cfg, KVArena *arena, rt_rollout_t **out)
+{
+    if (!cfg || !out) {
+        rt::set_error("rollout: null argument");
+        return RT_EINVAL;
+    }
+    *out = nullptr;
+    const bool full = cfg->decode_mode == RT_ROLLOUT_DECODE_FULL;
+    if (cfg->max_slots == 0 || cfg->max_slots > GPU_MAX_ROLLOUTS || cfg->max_admit == 0 ||
+        (cfg->decode_mode != RT_ROLLOUT_DECODE_FULL && cfg->decode_mode != RT_ROLLOUT_DECODE_NONE)) {
+        rt::set_error("rollout: max_slots 1..%d, max_admit >= 1, decode_mode 0/1", GPU_MAX_ROLLOUTS);
+        return RT_EINVAL;
+    }
+    if (full) {
+        if (!arena || !arena->base || cfg->num_kv_heads == 0 || cfg->num_q_heads == 0 ||
+            cfg->num_q_heads % cfg->num_kv_heads || cfg->vocab == 0 || cfg->vocab > 32768u ||
+            cfg->max_context < 16u || cfg->max_new_tokens == 0) {
+            rt::set_error("rollout: full decode needs an arena, heads (q multiple of kv), "
+                          "vocab 1..32768, max_context >= 16, max_new_tokens >= 1");
+            return RT_EINVAL;
+        }
+        if (arena->block_size != rt_page_bytes(cfg->num_kv_heads)) {
+            rt::set_error("rollout: arena block_size %zu != page size %llu", arena->block_size,
+                          (unsigned long long)rt_page_bytes(cfg->num_kv_heads));
+            return RT_EINVAL;
+        }
+    }
+    rt_rollout *e = new (std::nothrow) rt_rollout();
+    if (!e) {
+        rt::set_error("rollout: out of host memory");
+        return RT_ENOMEM;
+    }
+    e->cfg = *cfg;
+    e->arena = arena;
+    cudaGetDevice(&e->device);
+    Dev &d = e->d;
+    d.max_slots = cfg->max_slots;
+    d.max_admit = cfg->max_admit;
+    d.drop = cfg->drop_when_full ? 1u : 0u;
+    d.decode = cfg->decode_mode;
+    d.reward_mode = cfg->reward_mode;
+    d.reward_seed = cfg->reward_seed;
+    d.vocab = cfg->vocab;
+    d.hq = cfg->num_q_heads;
+    d.hkv = cfg->num_kv_heads;
+    d.max_new = cfg->max_new_tokens;
+    d.max_prefixes = cfg->max_prefixes;
+    d.maxp = full ? (cfg->max_context + 15u) / 16u : 1u;
+    d.ppriv = full ? (cfg->max_new_tokens + 16u + 15u) / 16u : 1u;
+    d.max_passes = cfg->max_passes ? cfg->max_passes : (1ull << 40);
+    d.idle_ns = (uint64_t)(cfg->idle_timeout_ms ? cfg->idle_timeout_ms : 10000u) * 1000000ull;
+    d.logit_std = cfg->logit_std;
+
+    cudaError_t err = cudaSuccess;
+    auto ok = [&](cudaError_t x) { if (err == cudaSuccess) err = x; };
+    const uint32_t S = d.max_slots;
+    ok(dalloc(&d.io, 1));
+    ok(dalloc(&d.ctl, 1));
+    ok(dalloc(&d.ext, S));
+    ok(dalloc(&d.seq_lens, S));
+    ok(dalloc(&d.enable, S));
+    ok(dalloc(&d.srows, S));
+    ok(dalloc(&d.tokens, S));
+    ok(cudaMallocHost(reinterpret_cast<void **>(&e->io_stage), sizeof(RtIo)));
+    if (full) {
+        ok(dalloc(&d.page_table, (size_t)S * d.maxp));
+        ok(dalloc(&d.priv, (size_t)S * d.ppriv));
+        ok(dalloc(&d.q, (size_t)S * d.hq * 128u));
+        ok(dalloc(&d.attn_out, (size_t)S * d.hq * 128u));
+        ok(dalloc(&d.logits, (size_t)S * d.vocab));
+        const uint32_t npf = cfg->max_prefixes ? cfg->max_prefixes : 1u;
+        ok(dalloc(&d.pf_len, npf));
+        ok(dalloc(&d.pf_np, npf));
+        ok(dalloc(&d.pf_off, npf));
+        ok(dalloc(&d.pf_pages, cfg->max_prefix_pages ? cfg->max_prefix_pages : 1u));
+    }
+    if (err != cudaSuccess) {
+        engine_free(e);
+        return rt::cuda_fail(err, "rollout: device allocation");
+    }
+    if (full) {
+        ok(cudaMemset(d.pf_len, 0, sizeof(uint32_t) * (cfg->max_prefixes ? cfg->max_prefixes : 1u)));
+        ok(cudaMemset(d.pf_np, 0, sizeof(uint32_t) * (cfg->max_prefixes ? cfg->max_prefixes : 1u)));
+        d.arena = reinterpret_cast<__nv_bfloat16 *>(arena->base);
+        // reserve the private pages from the arena (lowest free blocks first)
+        e->n_priv = S * d.ppriv;
+        e->priv_blocks = static_cast<int64_t *>(malloc(sizeof(int64_t) * e->n_priv));
+        int32_t *h = static_cast<int32_t *>(malloc(sizeof(int32_t) * e->n_priv));
+        uint32_t got = 0;
+        for (; got < e->n_priv; got++) {
+            const int64_t b = arena_acquire(arena);
+            if (b < 0 || b > INT32_MAX)
+                break;
+            e->priv_blocks[got] = b;
+            h[got] = (int32_t)b;
+        }
+        if (got < e->n_priv) {
+            e->n_priv = got;
+            free(h);
+            engine_free(e);
+            rt::set_error("rollout: arena has fewer than %u free pages", S * d.ppriv);
+            return RT_ENOMEM;
+        }
+        ok(cudaMemcpy(d.priv, h, sizeof(int32_t) * e->n_priv, cudaMemcpyHostToDevice));
+        free(h);
+        const uint64_t arena_pages = arena->capacity / arena->block_size;
+        e->ap.num_seqs = S;
+        e->ap.num_q_heads = d.hq;
+        e->ap.num_kv_heads = d.hkv;
+        e->ap.head_dim = 128u;
+        e->ap.max_pages_per_seq = d.maxp;
+        e->ap.max_seq_len = d.maxp * 16u;
+        e->ap.arena_pages = arena_pages;
+        e->ap.scale = 0.08838834764831845f;  // 1/sqrt(128)
+        e->ap.chunk_pages = cfg->chunk_pages;
+        e->attn_ws_bytes = rt_attn_workspace_bytes(&e->ap);
+        if (e->attn_ws_bytes == 0) {
+            engine_free(e);
+            return RT_EINVAL;
+        }
+        ok(cudaMalloc(&e->attn_ws, e->attn_ws_bytes));
+        ok(cudaMemset(e->attn_ws, 0, e->attn_ws_bytes));
+        if (err == cudaSuccess) {
+            int rc = rt::attn_prepare(&e->ap);
+            if (rc != RT_OK) {
+                engine_free(e);
+                return rc;
+            }
+        }
+    }
+    ok(cudaStreamCreateWithFlags(&e->cap, cudaStreamNonBlocking));
+    if (err != cudaSuccess) {
+        engine_free(e);
+        return rt::cuda_fail(err, "rollout: setup");
+    }
+    int rc = engine_build_graph(e);
+    if (rc != RT_OK) {
+        engine_free(e);
+        return rc;
+    }
+    *out = e;
+    return RT_OK;
+}
+
+extern "C" int rt_rollout_destroy(rt_rollout_t *e)
+{
+    if (e) {
+        cudaDeviceSynchronize();
+        engine_free(e);
+    }
+    return RT_OK;
+}
+
+extern "C" int rt_rollout_set_prefix(rt_rollout_t *e, uint32_t prefix_id, const int32_t *pages,
+                                     uint32_t n_pages, uint32_t token_len)
+{
+    if (!e || (!pages && n_pages) || e->cfg.decode_mode != RT_ROLLOUT_DECODE_FULL) {
+        rt::set_error("rollout_set_prefix: needs a full-decode engine and a page list");
+        return RT_EINVAL;
+    }
+    if (prefix_id >= e->cfg.max_prefixes || (token_len + 15u) / 16u > n_pages ||
+        token_len > e->d.maxp * 16u) {
+        rt::set_error("rollout_set_prefix: prefix %u (max %u) with %u tokens needs %u pages, got %u",
+                      prefix_id, e->cfg.max_prefixes, token_len, (token_len + 15u) / 16u, n_pages);
+        return RT_EINVAL;
+    }
+    if (e->pf_used + n_pages > e->cfg.max_prefix_pages) {
+        rt::set_error("rollout_set_prefix: prefix page pool full (%u of %u)", e->pf_used,
+                      e->cfg.max_prefix_pages);
+        return RT_ENOMEM;
+    }
+    const uint64_t arena_pages = e->arena->capacity / e->arena->block_size;
+    for (uint32_t i = 0; i < n_pages; i++)
+        if (pages[i] < 0 || (uint64_t)pages[i] >= arena_pages) {
+            rt::set_error("rollout_set_prefix: page %d outside the arena", pages[i]);
+            return RT_EINVAL;
+        }
+    cudaError_t err = cudaMemcpy(e->d.pf_pages + e->pf_used, pages, sizeof(int32_t) * n_pages,
+                                 cudaMemcpyHostToDevice);
+    const uint32_t off = e->pf_used;
+    if (err == cudaSuccess)
+        err = cudaMemcpy(e->d.pf_len + prefix_id, &token_len, 4, cudaMemcpyHostToDevice);
+    if (err == cudaSuccess)
+        err = cudaMemcpy(e->d.pf_np + prefix_id, &n_pages, 4, cudaMemcpyHostToDevice);
+    if (err == cudaSuccess)
+        err = cudaMemcpy(e->d.pf_off + prefix_id, &off, 4, cudaMemcpyHostToDevice);
+    if (err != cudaSuccess)
+        return rt::cuda_fail(err, "rollout_set_prefix: copy");
+    e->pf_used += n_pages;
+    return RT_OK;
+}
+
+extern "C" int rt_rollout_launch(rt_rollout_t *e, const rt_rollout_io_t *io, void *stream)
+{
+    if (!e || !io || !io->state || (!io->ring && !io->requests && io->n_requests)) {
+        rt::set_error("rollout_launch: needs an engine, a state table and a request source");
+        return RT_EINVAL;
+    }
+    if (io->ring && io->requests) {
+        rt::set_error("rollout_launch: give either a request ring or a request array");
+        return RT_EINVAL;
+    }
+    RtIo *x = e->io_stage;
+    x->ring = io->ring;
+    x->reqs = io->requests;
+    x->n_reqs = io->ring ? 0u : io->n_requests;
+    x->done_ring = io->done_ring;
+    x->dones = io->dones;
+    x->state = io->state;
+    x->step_count = reinterpret_cast<unsigned long long *>(io->step_count);
+    x->traj = io->trajectories;
+    x->rewards = io->rewards;
+    x->n_rows = io->n_rows;
+    cudaStream_t s = (cudaStream_t)stream;
+    cudaError_t err = cudaMemcpyAsync(e->d.io, x, sizeof(RtIo), cudaMemcpyHostToDevice, s);
+    if (err == cudaSuccess)
+        err = cudaMemsetAsync(e->d.ctl, 0, sizeof(RtCtl), s);
+    if (err == cudaSuccess)
+        err = cudaMemsetAsync(e->d.ext, 0, sizeof(SlotExt) * e->d.max_slots, s);
+    if (err == cudaSuccess)
+        err = cudaMemsetAsync(e->d.enable, 0, sizeof(uint32_t) * e->d.max_slots, s);
+    if (err == cudaSuccess)
+        err = cudaMemsetAsync(io->state, 0, sizeof(GpuRolloutState), s);
+    if (err == cudaSuccess)
+        err = cudaGraphLaunch(e->exec, s);
+    if (err != cudaSuccess)
+        return rt::cuda_fail(err, "rollout_launch");
+    return RT_OK;
+}
+
+extern "C" int rt_rollout_wait(rt_rollout_t *e, void *stream, rt_rollout_stats_t *st)
+{
+    if (!e) {
+        rt::set_error("rollout_wait: null engine");
+        return RT_EINVAL;
+    }
+    cudaStream_t s = (cudaStream_t)stream;
+    RtCtl c;
+    cudaError_t err = cudaStreamSynchronize(s);
+    if (err == cudaSuccess)
+        err = cudaMemcpy(&c, e->d.ctl, sizeof(c), cudaMemcpyDeviceToHost);
+    if (err != cudaSuccess)
+        return rt::cuda_fail(err, "rollout_wait");
+    int32_t attn_err = 0;
+    if (e->attn_ws && rt_attn_workspace_error(e->attn_ws, stream, &attn_err) != RT_OK)
+        return RT_ECUDA;
+    if (st) {
+        st->passes = c.passes;
+        st->tokens = c.tokens;
+        st->consumed = c.consumed;
+        st->admitted = c.admitted;
+        st->dropped = c.dropped;
+        st->done = c.done;
+        st->max_active = c.max_active;
+        st->stopped_by_sentinel = c.sentinel;
+        st->error = c.error;
+        st->attn_error = attn_err;
+    }
+    if (c.error) {
+        rt::set_error("rollout: loop stopped with error %d after %llu passes", c.error,
+                      (unsigned long long)c.passes);
+        return c.error;
+    }
+    if (attn_err) {
+        rt::set_error("rollout: attention reported device error %d", attn_err);
+        return RT_EDEVICE;
+    }
+    return RT_OK;
+}
+
+extern "C" int rt_logits_synth(float *out, uint32_t vocab, uint64_t seed, uint32_t request_lo,
+                               uint64_t token_index, float logit_std, void *stream)
+{
+    if (!out || vocab == 0) {
+        rt::set_error("logits_synth: bad argument");
+        return RT_EINVAL;
+    }
+    const uint32_t groups = (vocab + 3u) / 4u;
+    logits_synth_kernel<<<(groups + 255u) / 256u, 256, 0, (cudaStream_t)stream>>>(
+        out, vocab, seed, request_lo, token_index, logit_std);
+    cudaError_t err = cudaGetLastError();
+    return err == cudaSuccess ? RT_OK : rt::cuda_fail(err, "logits_synth: launch");
+}
+
+// Drop-in for the reference's rollout_worker launch: a per-device control
+// block (allocated on the first call) and a persistent single-CTA kernel.
+extern "C" int rt_launch_rollout_worker(RequestRing *req_ring, DoneRing *done_ring,
+                                        GpuRolloutState *state, uint64_t *step_count,
+                                        uint32_t idle_timeout_ms, void *stream)
+{
+    static std::mutex mu;
+    static RtIo *io_dev[64] = {};
+    static RtCtl *ctl_dev[64] = {};
+    if (!req_ring || !done_ring || !state) {
+        rt::set_error("rollout_worker: null ring or state");
+        return RT_EINVAL;
+    }
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) {
+        rt::set_error("rollout_worker: device index %d out of range", dev);
+        return RT_EINVAL;
+    }
+    cudaStream_t s = (cudaStream_t)stream;
+    cudaError_t err = cudaSuccess;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (!io_dev[dev]) {
+            err = cudaMalloc(&io_dev[dev], sizeof(RtIo));
+            if (err == cudaSuccess)
+                err = cudaMalloc(&ctl_dev[dev], sizeof(RtCtl));
+            if (err != cudaSuccess)
+                return rt::cuda_fail(err, "rollout_worker: control block");
+        }
+    }
+    RtIo x;
+    memset(&x, 0, sizeof(x));
+    x.ring = req_ring;
+    x.done_ring = done_ring;
+    x.state = state;
+    x.step_count = reinterpret_cast<unsigned long long *>(step_count);
+    Dev d;
+    memset(&d, 0, sizeof(d));
+    d.max_slots = GPU_MAX_ROLLOUTS;
+    d.max_admit = 1u;
+    d.drop = 1u;
+    d.decode = RT_ROLLOUT_DECODE_NONE;
+    d.reward_mode = RT_REWARD_MOCK;
+    d.max_passes = 1ull << 62;
+    d.idle_ns = (uint64_t)(idle_timeout_ms ? idle_timeout_ms : 10000u) * 1000000ull;
+    d.io = io_dev[dev];
+    d.ctl = ctl_dev[dev];
+    err = cudaMemcpyAsync(d.io, &x, sizeof(x), cudaMemcpyHostToDevice, s);
+    if (err == cudaSuccess)
+        err = cudaMemsetAsync(d.ctl, 0, sizeof(RtCtl), s);
+    if (err != cudaSuccess)
+        return rt::cuda_fail(err, "rollout_worker: setup");
+    persistent_worker_kernel<<<1, kSched, 0, s>>>(d);
+    err = cudaGetLastError();
+    return err == cudaSuccess ? RT_OK : rt::cuda_fail(err, "rollout_worker: launch");
+}

@@ -172,10 +172,10 @@ __host__ __device__ __forceinline__ void philox4x32_10(uint32_t c0, uint32_t c1,
 
 // Four N(0,1) samples from one Philox block by the Box-Muller transform.
 __device__ __forceinline__ void philox_normal4(uint64_t seed, uint32_t c0, uint32_t c1,
-                                               uint32_t c2, float (&z)[4])
+                                               uint32_t c2, float (&z)[4], uint32_t c3 = 0u)
 {
     uint32_t x[4];
-    philox4x32_10(c0, c1, c2, 0u, (uint32_t)seed, (uint32_t)(seed >> 32), x);
+    philox4x32_10(c0, c1, c2, c3, (uint32_t)seed, (uint32_t)(seed >> 32), x);
 #pragma unroll
     for (int k = 0; k < 2; k++) {
         const float u1 = ((float)((x[2 * k] >> 8) + 1u)) * (1.0f / 16777216.0f);

@@ -39,9 +39,9 @@ constexpr int kCap = 2048;          // survivors handled by the fast path
 struct SampleArgs {
     const float *logits;
     const rt_sample_row_t *rows;
+    const uint32_t *enable;
     uint32_t *out;
     uint64_t stride;
-    uint64_t seed;
     uint32_t vocab;
     uint32_t fused;
 };
@@ -190,6 +190,8 @@ __global__ void __launch_bounds__(kThreads, 1) sample_rows_kernel(const SampleAr
     __shared__ Smem s;
     const int tid = threadIdx.x;
     const uint32_t V = a.vocab;
+    if (a.enable && a.enable[blockIdx.x] == 0u)
+        return;
     const rt_sample_row_t P = a.rows[blockIdx.x];
     const float *lr = a.logits + (size_t)blockIdx.x * a.stride;
 
@@ -216,7 +218,7 @@ __global__ void __launch_bounds__(kThreads, 1) sample_rows_kernel(const SampleAr
     if (tid == 0) {
         uint32_t ph[4];
         rt::philox4x32_10((uint32_t)P.step, (uint32_t)(P.step >> 32), P.rollout_id, 0u,
-                          (uint32_t)a.seed, (uint32_t)(a.seed >> 32), ph);
+                          (uint32_t)P.seed, (uint32_t)(P.seed >> 32), ph);
         s.token = ph[0] & 0x00FFFFFFu;  // u24 (reused below)
         s.count = 0u;
         s.done = 0u;
@@ -395,7 +397,8 @@ extern "C" int rt_sample_rows(const rt_sample_params_t *p, const float *logits,
                       kThreads * kItems, (unsigned long long)p->row_stride);
         return RT_EINVAL;
     }
-    if (((uintptr_t)logits & 3u) || ((uintptr_t)rows & 7u) || ((uintptr_t)tokens_out & 3u)) {
+    if (((uintptr_t)logits & 3u) || ((uintptr_t)rows & 7u) || ((uintptr_t)tokens_out & 3u) ||
+        ((uintptr_t)p->row_enable & 3u)) {
         rt::set_error("sample: misaligned pointer");
         return RT_EINVAL;
     }
@@ -409,8 +412,8 @@ extern "C" int rt_sample_rows(const rt_sample_params_t *p, const float *logits,
     a.logits = logits;
     a.rows = rows;
     a.out = tokens_out;
+    a.enable = p->row_enable;
     a.stride = p->row_stride;
-    a.seed = p->seed;
     a.vocab = p->vocab;
     a.fused = p->fused_cum ? 1u : 0u;
     sample_rows_kernel<<<p->num_rows, kThreads, 0, (cudaStream_t)stream>>>(a);

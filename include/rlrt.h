@@ -16,6 +16,7 @@
 #include "request.h"
 #include "ring.h"
 #include "kv_prefix.h"
+#include "arena.h"
 
 #ifdef __cplusplus
 extern "C" {
@@ -108,16 +109,20 @@ typedef struct {
     float    top_p;
     uint32_t rollout_id;     /* Philox counter word 2 */
     uint64_t step;           /* Philox counter words 0..1 */
+    uint64_t seed;           /* Philox key */
 } rt_sample_row_t;
 
 typedef struct {
     uint32_t num_rows;
     uint32_t vocab;          /* 1 .. 32768 */
     uint64_t row_stride;     /* floats between consecutive rows (>= vocab) */
-    uint64_t seed;           /* Philox key */
     uint32_t fused_cum;      /* 1: top-p walk accumulates with one fma
                                 (matches nvcc's default contraction of the
-                                reference), 0: separate multiply and add */
+                                reference; verified bit-exact on B200),
+                                0: separate multiply and add */
+    const uint32_t *row_enable; /* device [num_rows] or NULL; rows whose flag
+                                   is 0 are skipped and their token is left
+                                   untouched */
 } rt_sample_params_t;
 
 /* logits fp32 [num_rows][row_stride] (device), rows [num_rows] (device),
@@ -127,6 +132,135 @@ int rt_sample_rows(const rt_sample_params_t *p, const float *logits,
 
 /* The 24-bit uniform rt_sample_rows uses for (seed, rollout_id, step). */
 uint32_t rt_sample_uniform24(uint64_t seed, uint32_t rollout_id, uint64_t step);
+
+/* ------------------------------------------------------------------------
+ * GPU-resident rollout loop.
+ *
+ * Replaces reference cu/gpu_scheduler.cu:26-83 (rollout_worker, whose
+ * per-pass "decode" is a token counter).  Each pass, on the GPU and without
+ * host involvement:
+ *   1. commit the tokens sampled in the previous pass
+ *      (tokens_generated++ per decoding slot);
+ *   2. admit up to max_admit requests, in ring order, each into the lowest
+ *      free slot, initialising the reference's GpuRolloutSlot fields
+ *      exactly as cu/gpu_scheduler.cu:40-55 (request_id low 32 bits,
+ *      rng_state {s, s^0x9e37.., (s<<17)^0x3c6e.., ~s}); request_id ==
+ *      UINT64_MAX stops the loop at once; with drop_when_full a request that
+ *      finds no free slot is consumed and lost (reference), otherwise it
+ *      stays queued (backpressure);
+ *   3. in slot order, finish every active slot whose tokens_generated has
+ *      reached max_tokens: push RolloutDone{request_id low 32, slot,
+ *      tokens, reward, 0} (reward (tokens & 0xFF)/255 in RT_REWARD_MOCK),
+ *      free the slot, bump *step_count;
+ *   4. decode one token for every remaining active slot:
+ *      RT_ROLLOUT_DECODE_FULL: synthesize q and the new token's K/V
+ *      (Philox N(0,1)), copy-on-write the partial last page of a shared
+ *      prefix on the first write, paged GQA attention over the slot's
+ *      context, synthetic logits ~ N(0, logit_std) (Philox key = request
+ *      rng_seed, counter = (token index, request low 32)), fused sampling
+ *      with the slot's temperature/top_k/top_p;
+ *      RT_ROLLOUT_DECODE_NONE: no math (the reference's counter).
+ * A request routes to a shared prefix through request_id bits 32..63
+ * (prefix id + 1, see request.h); the prefix's pages are registered with
+ * rt_rollout_set_prefix.  Token ids land in `trajectories` row r =
+ * the request's consume index (0, 1, 2, ... in ring/array order).
+ * ---------------------------------------------------------------------- */
+#define RT_ROLLOUT_DECODE_NONE  0u
+#define RT_ROLLOUT_DECODE_FULL  1u
+#define RT_REWARD_MOCK          0u   /* (tokens & 0xFF) / 255 (reference) */
+#define RT_REWARD_PHILOX        1u   /* U(0,1): Philox(key = reward_seed, ctr = {request low 32}) */
+
+typedef struct {
+    uint32_t num_q_heads;       /* 32 */
+    uint32_t num_kv_heads;      /* 8 (page bytes = num_kv_heads * 8 KiB) */
+    uint32_t vocab;             /* <= 32768 */
+    uint32_t max_slots;         /* concurrent rollouts, <= GPU_MAX_ROLLOUTS */
+    uint32_t max_context;       /* tokens per rollout incl. prefix */
+    uint32_t max_new_tokens;    /* per rollout (trajectory row length) */
+    uint32_t max_admit;         /* requests admitted per pass (1 = reference) */
+    uint32_t drop_when_full;    /* 1 = reference, 0 = backpressure */
+    uint32_t decode_mode;       /* RT_ROLLOUT_DECODE_* */
+    uint32_t reward_mode;       /* RT_REWARD_* */
+    uint64_t reward_seed;
+    float    logit_std;         /* synthetic logits ~ N(0, logit_std) */
+    uint32_t max_prefixes;      /* prefix ids 0 .. max_prefixes-1 */
+    uint32_t max_prefix_pages;  /* total pages over all registered prefixes */
+    uint64_t max_passes;        /* stop with RT_ETIMEOUT after this many passes */
+    uint32_t idle_timeout_ms;   /* ring source: stop with RT_ETIMEOUT when idle this long */
+    uint32_t chunk_pages;       /* attention split-K chunk (0 = auto) */
+} rt_rollout_config_t;
+
+typedef struct {
+    RequestRing *ring;                 /* request source: a ring ... */
+    const RolloutRequest *requests;    /* ... or a device array (ring == NULL) */
+    uint32_t n_requests;
+    DoneRing *done_ring;               /* done sink: a ring ... */
+    RolloutDone *dones;                /* ... or a device array (capacity n_rows) */
+    GpuRolloutState *state;            /* device, reference layout; zeroed at launch */
+    uint64_t *step_count;              /* device, may be NULL */
+    uint32_t *trajectories;            /* device [n_rows][max_new_tokens], may be NULL */
+    float *rewards;                    /* device [n_rows], may be NULL */
+    uint32_t n_rows;
+} rt_rollout_io_t;
+
+typedef struct {
+    uint64_t passes;
+    uint64_t tokens;          /* tokens generated (committed) */
+    uint32_t consumed;        /* requests taken from the source (incl. dropped) */
+    uint32_t admitted;
+    uint32_t dropped;
+    uint32_t done;
+    uint32_t max_active;
+    uint32_t stopped_by_sentinel;
+    int32_t  error;           /* 0, or RT_ETIMEOUT / RT_EDEVICE */
+    int32_t  attn_error;      /* attention workspace error word */
+} rt_rollout_stats_t;
+
+typedef struct rt_rollout rt_rollout_t;
+
+/* Allocate the engine's device state and reserve its private KV pages
+ * (max_slots x ceil((max_new_tokens + 16) / 16) blocks) from `arena`,
+ * whose block_size must be the page size (num_kv_heads * 8 KiB). */
+int rt_rollout_create(const rt_rollout_config_t *cfg, KVArena *arena, rt_rollout_t **out);
+int rt_rollout_destroy(rt_rollout_t *eng);
+
+/* Register the pages (arena block indices, host array) of shared prefix
+ * `prefix_id` holding `token_len` tokens (the prefix_id of
+ * kv_prefix_register).  A partial last page is copied on first write. */
+int rt_rollout_set_prefix(rt_rollout_t *eng, uint32_t prefix_id, const int32_t *pages,
+                          uint32_t n_pages, uint32_t token_len);
+
+/* Launch the loop asynchronously on `stream`.  It ends at the sentinel,
+ * when an array source is exhausted and no rollout is active, or on error. */
+int rt_rollout_launch(rt_rollout_t *eng, const rt_rollout_io_t *io, void *stream);
+
+/* Wait for the loop (stream sync) and read its counters. */
+int rt_rollout_wait(rt_rollout_t *eng, void *stream, rt_rollout_stats_t *stats);
+
+/* Synthetic logits of the loop for (seed, request low 32, token index):
+ * out[v] = logit_std * N(0,1), v < vocab (device); used to replay a run. */
+int rt_logits_synth(float *out, uint32_t vocab, uint64_t seed, uint32_t request_lo,
+                    uint64_t token_index, float logit_std, void *stream);
+
+/* Host side of a ring-fed run, in C (the producer/consumer loop of the
+ * reference's bench driver, bench/bench_gpu_scheduler.cu:57-83): push the
+ * n requests into `rq` as space allows (then the stop sentinel when
+ * send_sentinel), while draining `dn` into `dones` until n_expected records
+ * arrived.  Returns the number drained, or -1 when timeout_ms passed first
+ * (the records drained so far are in `dones`). */
+int64_t rt_host_pump(RequestRing *rq, const RolloutRequest *reqs, uint32_t n, DoneRing *dn,
+                     RolloutDone *dones, uint32_t n_expected, int send_sentinel,
+                     uint32_t timeout_ms);
+
+/* Drop-in for the reference launch
+ *     rollout_worker<<<1, 32>>>(req_ring, done_ring, state, step_count)
+ * (reference bench/bench_gpu_scheduler.cu:55): a persistent single-CTA
+ * kernel with the reference's pass semantics and counter-only decode,
+ * returning immediately; it exits at the request_id == UINT64_MAX sentinel
+ * (or after idle_timeout_ms without work, flagging RT_ETIMEOUT). */
+int rt_launch_rollout_worker(RequestRing *req_ring, DoneRing *done_ring,
+                             GpuRolloutState *state, uint64_t *step_count,
+                             uint32_t idle_timeout_ms, void *stream);
 
 /* ------------------------------------------------------------------------
  * Synthetic data (seeded, counter-based, reproducible on any GPU).

@@ -1,0 +1,199 @@
+"""GPU-resident rollout loop (rt_rollout_*, rt_launch_rollout_worker) against
+the oracle's restatement of the reference pass loop (cu/gpu_scheduler.cu:26-83)
+and, for full decode, against a token-by-token replay of the loop's logits
+through the standalone sampler."""
+import threading
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+STATE_BYTES = 72 * 256 + 32
+
+
+def make_requests(orc, n, max_tokens, seed=42, prefix_plus_one=None, temperature=0.8,
+                  top_k=50, top_p=0.9):
+    r = np.zeros(n, dtype=orc.REQUEST_DTYPE)
+    ids = np.arange(1, n + 1, dtype=np.uint64)
+    if prefix_plus_one is not None:
+        ids = ids | (np.asarray(prefix_plus_one, dtype=np.uint64) << np.uint64(32))
+    r["request_id"] = ids
+    r["max_tokens"] = max_tokens
+    r["kv_blocks"] = 4
+    r["temperature"] = temperature
+    r["top_k"] = top_k
+    r["top_p"] = top_p
+    r["rng_seed"] = seed
+    return r
+
+
+def run_array(pkg, cuda, eng, reqs, max_new=1, traj=False):
+    n = len(reqs)
+    req_d = torch.from_numpy(reqs.view(np.uint8).copy()).to(cuda)
+    dones = torch.zeros(n * 24, dtype=torch.uint8, device=cuda)
+    state = torch.zeros(STATE_BYTES, dtype=torch.uint8, device=cuda)
+    steps = torch.zeros(1, dtype=torch.int64, device=cuda)
+    tr = torch.full((n, max_new), -1, dtype=torch.int32, device=cuda) if traj else None
+    rw = torch.zeros(n, dtype=torch.float32, device=cuda) if traj else None
+    eng.launch(requests=req_d, n_requests=n, dones=dones, state=state, step_count=steps,
+               trajectories=tr, rewards=rw, n_rows=n)
+    st = eng.wait()
+    return st, dones.cpu().numpy(), state.cpu().numpy(), int(steps.item()), tr, rw
+
+
+def mock_cfg(max_admit=1, drop=1, max_slots=256):
+    return dict(max_slots=max_slots, max_admit=max_admit, drop_when_full=drop,
+                decode_mode=0, reward_mode=0, max_passes=1 << 30, idle_timeout_ms=2000)
+
+
+@pytest.mark.parametrize("max_admit,drop,n,tok_hi", [(1, 1, 200, 40), (256, 0, 300, 60),
+                                                      (256, 1, 300, 60), (7, 0, 600, 9)])
+def test_counter_decode_matches_reference_pass_loop(pkg, orc, cuda, max_admit, drop, n, tok_hi):
+    rng = np.random.default_rng(n + max_admit)
+    reqs = make_requests(orc, n, rng.integers(0, tok_hi + 1, size=n))
+    eng = pkg.RolloutEngine(mock_cfg(max_admit, drop))
+    st, dones, state, steps, _, _ = run_array(pkg, cuda, eng, reqs)
+    od, _, ostate, opasses = orc.scheduler_run(reqs, max_admit=max_admit, drop_when_full=bool(drop))
+    got = dones[: st["done"] * 24].view(orc.DONE_DTYPE)
+    assert st["done"] == len(od) == steps
+    assert got.tobytes() == od.tobytes()
+    assert state.tobytes() == ostate.tobytes()
+    assert st["passes"] == opasses
+    assert st["dropped"] == (n - len(od) if drop else 0)
+    eng.close()
+
+
+def test_dropin_rollout_worker_over_mapped_rings(pkg, orc, cuda):
+    """The reference bench's flow (bench/bench_gpu_scheduler.cu:41-112): mapped
+    rings, the worker launched once, requests pushed by the host, dones
+    drained, sentinel, sync."""
+    n, tokens = 3000, 128
+    reqs = make_requests(orc, n, tokens)
+    rings = pkg.HostRings()
+    state = torch.zeros(STATE_BYTES, dtype=torch.uint8, device=cuda)
+    steps = torch.zeros(1, dtype=torch.int64, device=cuda)
+    s = torch.cuda.Stream()
+    pkg.check(pkg.lib().rt_launch_rollout_worker(rings.req, rings.done, state.data_ptr(),
+                                                  steps.data_ptr(), 5000,
+                                                  pkg._stream_ptr(s)), "rt_launch_rollout_worker")
+    got_n, raw = rings.pump(reqs.view(np.uint8), n, send_sentinel=True, timeout_ms=60000)
+    s.synchronize()
+    assert got_n == n
+    d = raw[: n * 24].view(orc.DONE_DTYPE)
+    assert sorted(d["request_id"].tolist()) == list(range(1, n + 1))
+    assert np.all(d["tokens_generated"] == tokens)
+    assert np.allclose(d["reward"], (tokens & 0xFF) / 255.0)
+    assert int(steps.item()) == n
+    rings.close()
+
+
+def full_cfg(max_slots=64, max_admit=256, vocab=2048, max_new=24, max_context=512,
+             n_prefix=4, prefix_pages=64):
+    return dict(num_q_heads=32, num_kv_heads=8, vocab=vocab, max_slots=max_slots,
+                max_context=max_context, max_new_tokens=max_new, max_admit=max_admit,
+                drop_when_full=0, decode_mode=1, reward_mode=0, logit_std=2.0,
+                max_prefixes=n_prefix, max_prefix_pages=prefix_pages, max_passes=1 << 20,
+                idle_timeout_ms=2000)
+
+
+def setup_prefixes(pkg, arena, eng, lens, seed=9):
+    ids = []
+    for pid, L in enumerate(lens):
+        pages = arena.acquire((L + 15) // 16)
+        arena.fill_pages(pages, seed=seed, stream_id=1000 * pid)
+        eng.set_prefix(pid, pages, L)
+        ids.append(pid)
+    return ids
+
+
+def replay_tokens(pkg, cuda, reqs, dones, traj, vocab, logit_std=2.0):
+    """Expected token stream of every finished request: the loop's logits for
+    (seed, request low 32, token index) regenerated with rt_logits_synth and
+    sampled with rt_sample_rows using the request's parameters."""
+    rows, meta = [], []
+    by_id = {int(r["request_id"]) & 0xFFFFFFFF: (i, r) for i, r in enumerate(reqs)}
+    for d in dones:
+        i, r = by_id[int(d["request_id"])]
+        for t in range(int(d["tokens_generated"])):
+            meta.append((i, t))
+            rows.append((float(r["temperature"]), int(r["top_k"]), float(r["top_p"]),
+                         int(r["request_id"]) & 0xFFFFFFFF, t, int(r["rng_seed"])))
+    R = len(rows)
+    logits = torch.empty(R, vocab, dtype=torch.float32, device=cuda)
+    for k, row in enumerate(rows):
+        pkg.logits_synth(logits[k], vocab, row[5], row[3], row[4], logit_std)
+    tab = pkg.sample_row_table(*[np.array([row[j] for row in rows]) for j in range(6)])
+    tok = pkg.sample_rows(logits, torch.from_numpy(tab.view(np.uint8)).to(cuda), vocab)
+    tok = tok.cpu().numpy()
+    tr = traj.cpu().numpy()
+    return [(i, t, int(tok[k]), int(tr[i, t])) for k, (i, t) in enumerate(meta)]
+
+
+def test_full_decode_tokens_and_schedule(pkg, orc, cuda):
+    """Full decode: 2 GRPO groups x 16 rollouts sharing 40- and 64-token
+    prefixes (the 40-token one has a partial last page: copy-on-write),
+    plus 8 rollouts without a prefix; max_admit 256, backpressure."""
+    arena = pkg.DeviceArena(2048)
+    eng = pkg.RolloutEngine(full_cfg(), arena)
+    setup_prefixes(pkg, arena, eng, [40, 64])
+    rng = np.random.default_rng(5)
+    n = 40
+    pfx = np.array([1] * 16 + [2] * 16 + [0] * 8)
+    reqs = make_requests(orc, n, rng.integers(1, 25, size=n), seed=1234, prefix_plus_one=pfx)
+    st, dones, state, steps, traj, rew = run_array(pkg, cuda, eng, reqs, max_new=24, traj=True)
+    assert st["error"] == 0 and st["attn_error"] == 0
+    od, _, ostate, opasses = orc.scheduler_run(reqs, max_admit=256, drop_when_full=False)
+    got = dones[: st["done"] * 24].view(orc.DONE_DTYPE)
+    assert got.tobytes() == od.tobytes()
+    assert state.tobytes() == ostate.tobytes()
+    assert st["tokens"] == int(reqs["max_tokens"].sum())
+    checks = replay_tokens(pkg, cuda, reqs, got, traj, 2048)
+    bad = [c for c in checks if c[2] != c[3]]
+    assert not bad, f"{len(bad)}/{len(checks)} tokens differ, first {bad[:3]}"
+    eng.close()
+
+
+def test_full_decode_ring_fed_matches_array(pkg, orc, cuda):
+    """The same requests through mapped rings with the C host pump give the
+    same token streams (by request) as the device-array source."""
+    cfg = full_cfg(max_slots=32)
+    arena = pkg.DeviceArena(2048)
+    eng = pkg.RolloutEngine(cfg, arena)
+    setup_prefixes(pkg, arena, eng, [33])
+    n = 48
+    reqs = make_requests(orc, n, np.random.default_rng(8).integers(1, 20, size=n), seed=77,
+                         prefix_plus_one=np.array([1] * 32 + [0] * 16))
+    _, adones, _, _, atraj, _ = run_array(pkg, cuda, eng, reqs, max_new=24, traj=True)
+    rings = pkg.HostRings()
+    state = torch.zeros(STATE_BYTES, dtype=torch.uint8, device=cuda)
+    tr = torch.full((n, 24), -1, dtype=torch.int32, device=cuda)
+    s = torch.cuda.Stream()
+    eng.launch(ring=rings.req, done_ring=rings.done, state=state, trajectories=tr, n_rows=n,
+               stream=s)
+    got_n, raw = rings.pump(reqs.view(np.uint8), n, send_sentinel=True, timeout_ms=60000)
+    st = eng.wait(stream=s)
+    assert got_n == n and st["stopped_by_sentinel"] == 1
+    # rows are consume order == push order in both runs
+    a = atraj.cpu().numpy()
+    b = tr.cpu().numpy()
+    assert np.array_equal(a, b)
+    rings.close()
+    eng.close()
+
+
+def test_loop_reports_context_overflow(pkg, orc, cuda):
+    """A prefix + max_tokens longer than max_context is reported (RT_EDEVICE),
+    not written out of bounds."""
+    arena = pkg.DeviceArena(1024)
+    eng = pkg.RolloutEngine(full_cfg(max_context=64, max_new=40, max_slots=4), arena)
+    setup_prefixes(pkg, arena, eng, [48])
+    reqs = make_requests(orc, 2, 30, prefix_plus_one=np.array([1, 1]))
+    n = len(reqs)
+    req_d = torch.from_numpy(reqs.view(np.uint8).copy()).to(cuda)
+    state = torch.zeros(STATE_BYTES, dtype=torch.uint8, device=cuda)
+    eng.launch(requests=req_d, n_requests=n, state=state)
+    st = eng.wait(check_errors=False)
+    assert st["error"] == pkg.RT_EDEVICE
+    eng.close()

@@ -27,9 +27,9 @@ def u24s(pkg, rollouts, steps, seed=SEED):
 
 
 def run_mine(pkg, logits, vocab, T, k, p, rollouts, steps, fused=True, seed=SEED):
-    rows = pkg.sample_row_table(T, k, p, rollouts, steps)
+    rows = pkg.sample_row_table(T, k, p, rollouts, steps, seed)
     rows_d = torch.from_numpy(rows.view(np.uint8)).to(logits.device)
-    out = pkg.sample_rows(logits, rows_d, vocab, seed, fused_cum=fused)
+    out = pkg.sample_rows(logits, rows_d, vocab, fused_cum=fused)
     return out.cpu().numpy().view(np.uint32)
 
 
@@ -129,3 +129,17 @@ def test_token_distribution_follows_softmax(pkg, cuda):
     freq = np.bincount(tok, minlength=V) / N
     assert set(np.unique(tok)) <= set(keep)
     assert np.abs(freq - pr).max() < 0.02
+
+
+def test_row_enable_skips_rows(pkg, cuda):
+    R, V = 8, 500
+    logits = normal_logits(pkg, cuda, R, V, seed=12)
+    rows = pkg.sample_row_table(1.0, 10, 0.9, np.arange(R, dtype=np.uint32), 0, 7)
+    rows_d = torch.from_numpy(rows.view(np.uint8)).to(cuda)
+    full = pkg.sample_rows(logits, rows_d, V).cpu().numpy()
+    en = torch.tensor([1, 0, 1, 0, 0, 1, 1, 0], dtype=torch.int32, device=cuda)
+    out = torch.full((R,), -5, dtype=torch.int32, device=cuda)
+    pkg.sample_rows(logits, rows_d, V, out=out, row_enable=en)
+    got = out.cpu().numpy()
+    m = en.cpu().numpy().astype(bool)
+    assert np.array_equal(got[m], full[m]) and np.all(got[~m] == -5)
