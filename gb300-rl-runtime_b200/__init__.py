@@ -163,6 +163,7 @@ _SIGS = {
     "rt_logits_synth": (ctypes.c_int, [_P, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_uint32,
                                        ctypes.c_uint64, ctypes.c_float, _P]),
     "rt_launch_rollout_worker": (ctypes.c_int, [_P, _P, _P, _P, ctypes.c_uint32, _P]),
+    "rt_rollout_worker_stats": (ctypes.c_int, [_P, ctypes.POINTER(rt_rollout_stats_t)]),
     "rt_host_pump": (ctypes.c_int64, [_P, _P, ctypes.c_uint32, _P, _P, ctypes.c_uint32,
                                       ctypes.c_int, ctypes.c_uint32]),
     "req_ring_create": (_P, []), "req_ring_destroy": (None, [_P]),

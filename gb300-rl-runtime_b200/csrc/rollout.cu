@@ -901,13 +901,45 @@ extern "C" int rt_logits_synth(float *out, uint32_t vocab, uint64_t seed, uint32
 
 // Drop-in for the reference's rollout_worker launch: a per-device control
 // block (allocated on the first call) and a persistent single-CTA kernel.
+static std::mutex g_worker_mu;
+static RtIo *g_worker_io[64] = {};
+static RtCtl *g_worker_ctl[64] = {};
+
+extern "C" int rt_rollout_worker_stats(void *stream, rt_rollout_stats_t *st)
+{
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !g_worker_ctl[dev] || !st) {
+        rt::set_error("rollout_worker_stats: no worker was launched on this device");
+        return RT_EINVAL;
+    }
+    RtCtl c;
+    cudaError_t err = cudaMemcpyAsync(&c, g_worker_ctl[dev], sizeof(c), cudaMemcpyDeviceToHost,
+                                      (cudaStream_t)stream);
+    if (err == cudaSuccess)
+        err = cudaStreamSynchronize((cudaStream_t)stream);
+    if (err != cudaSuccess)
+        return rt::cuda_fail(err, "rollout_worker_stats");
+    memset(st, 0, sizeof(*st));
+    st->passes = c.passes;
+    st->tokens = c.tokens;
+    st->consumed = c.consumed;
+    st->admitted = c.admitted;
+    st->dropped = c.dropped;
+    st->done = c.done;
+    st->max_active = c.max_active;
+    st->stopped_by_sentinel = c.sentinel;
+    st->error = c.error;
+    return RT_OK;
+}
+
 extern "C" int rt_launch_rollout_worker(RequestRing *req_ring, DoneRing *done_ring,
                                         GpuRolloutState *state, uint64_t *step_count,
                                         uint32_t idle_timeout_ms, void *stream)
 {
-    static std::mutex mu;
-    static RtIo *io_dev[64] = {};
-    static RtCtl *ctl_dev[64] = {};
+    std::mutex &mu = g_worker_mu;
+    RtIo **io_dev = g_worker_io;
+    RtCtl **ctl_dev = g_worker_ctl;
     if (!req_ring || !done_ring || !state) {
         rt::set_error("rollout_worker: null ring or state");
         return RT_EINVAL;

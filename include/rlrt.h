@@ -262,6 +262,10 @@ int rt_launch_rollout_worker(RequestRing *req_ring, DoneRing *done_ring,
                              GpuRolloutState *state, uint64_t *step_count,
                              uint32_t idle_timeout_ms, void *stream);
 
+/* Counters of the last rt_launch_rollout_worker on the current device
+ * (reads device memory on `stream`; safe while the worker runs). */
+int rt_rollout_worker_stats(void *stream, rt_rollout_stats_t *stats);
+
 /* ------------------------------------------------------------------------
  * Synthetic data (seeded, counter-based, reproducible on any GPU).
  * ---------------------------------------------------------------------- */
