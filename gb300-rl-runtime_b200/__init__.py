@@ -423,12 +423,15 @@ class HostRings:
             raise RuntimeErrorRT("ring allocation failed")
 
     def pump(self, requests, n_expected, send_sentinel=True, timeout_ms=60000):
-        """rt_host_pump: requests is a numpy array of 34-byte RolloutRequest
-        records; returns the drained RolloutDone records (numpy bytes)."""
+        """rt_host_pump: requests holds 34-byte RolloutRequest records (a
+        structured array, or raw bytes); returns (n drained, RolloutDone bytes)."""
         import numpy as np
         reqs = np.ascontiguousarray(requests)
+        if reqs.nbytes % 34:
+            raise ValueError("requests must be whole 34-byte RolloutRequest records")
+        n_req = reqs.nbytes // 34
         out = np.zeros(max(n_expected, 1) * 24, dtype=np.uint8)
-        n = lib().rt_host_pump(self.req, reqs.ctypes.data_as(ctypes.c_void_p), len(reqs),
+        n = lib().rt_host_pump(self.req, reqs.ctypes.data_as(ctypes.c_void_p), n_req,
                                self.done, out.ctypes.data_as(ctypes.c_void_p), n_expected,
                                1 if send_sentinel else 0, timeout_ms)
         return n, out
