@@ -325,7 +325,196 @@ class SamplingWorkload:
                 "l2": "8 logits buffers rotate (262 MB > 126 MB L2)"}
 
 
-WORKLOADS = {"attention": AttentionWorkload, "sampling": SamplingWorkload}
+class RolloutWorkload:
+    """BASELINE config 5 (config 4's attention shape and config-3 sampling):
+    8,192 rollouts = 512 GRPO groups x 16, split by group across the N GPUs
+    (strong scaling: the same 8,192 rollouts whatever N).  Each group's 16
+    rollouts share a 512-token prompt held once in the KV arena
+    (copy-on-write prefix); each rollout generates 256 tokens.  One step =
+    one RL step: every local rollout generated to completion by the
+    GPU-resident loop (requests from a device array), rewards ~ U(0,1)
+    (Philox seed 5) allgathered over NCCL, group-normalised advantages."""
+
+    name = "grpo_rollouts_c5"
+    kernel = "paged_gqa_decode_kernel"
+    metric = "rollout tokens/s (config 5; value = all GPUs, per GPU = value / n_gpus)"
+    unit = "tokens/s"
+
+    GROUPS, G, PROMPT, GEN, VOCAB = 512, 16, 512, 256, 32000
+
+    def __init__(self, args, rank, world, dev):
+        import torch
+        self.torch = torch
+        self.pkg = pkg = ge.load_package()
+        self.rank, self.world, self.dev = rank, world, dev
+        if self.GROUPS % world:
+            raise SystemExit(f"{self.GROUPS} groups do not split over {world} GPUs")
+        self.ng = self.GROUPS // world
+        self.g0 = rank * self.ng
+        self.n = self.ng * self.G
+        pages_prompt = self.PROMPT // 16
+        priv = 256 * ((self.GEN + 16 + 15) // 16)
+        self.arena = pkg.DeviceArena(self.ng * pages_prompt + priv + 64, device=dev)
+        cfg = dict(num_q_heads=32, num_kv_heads=8, vocab=self.VOCAB, max_slots=256,
+                   max_context=self.PROMPT + self.GEN, max_new_tokens=self.GEN, max_admit=256,
+                   drop_when_full=0, decode_mode=1, reward_mode=1, reward_seed=5, logit_std=2.0,
+                   max_prefixes=self.ng, max_prefix_pages=self.ng * pages_prompt,
+                   max_passes=1 << 24, idle_timeout_ms=20000, chunk_pages=args.chunk_pages)
+        self.eng = pkg.RolloutEngine(cfg, self.arena)
+        prompt_pages = self.arena.acquire(self.ng * pages_prompt)
+        self.arena.fill_pages(prompt_pages, seed=4 + rank, stream_id=0)  # synthetic prefill (untimed)
+        for g in range(self.ng):
+            self.eng.set_prefix(g, prompt_pages[g * pages_prompt:(g + 1) * pages_prompt], self.PROMPT)
+        orc_dtype = np.dtype([("request_id", "<u8"), ("max_tokens", "<u4"), ("kv_blocks", "<u4"),
+                              ("temperature", "<f4"), ("top_k", "<u2"), ("top_p", "<f4"),
+                              ("rng_seed", "<u8")])
+        r = np.zeros(self.n, dtype=orc_dtype)
+        gid = np.arange(self.n) // self.G                       # local group
+        r["request_id"] = (np.arange(self.n, dtype=np.uint64) + np.uint64(self.g0 * self.G + 1)) | \
+            ((gid.astype(np.uint64) + np.uint64(1)) << np.uint64(32))
+        r["max_tokens"] = self.GEN
+        r["kv_blocks"] = pages_prompt
+        r["temperature"], r["top_k"], r["top_p"], r["rng_seed"] = 0.8, 50, 0.9, 1234
+        self.reqs_host = r
+        self.req_d = torch.from_numpy(r.view(np.uint8).copy()).to(dev)
+        self.dones = torch.zeros(self.n * 24, dtype=torch.uint8, device=dev)
+        self.state = torch.zeros(72 * 256 + 32, dtype=torch.uint8, device=dev)
+        self.traj = torch.zeros(self.n, self.GEN, dtype=torch.int32, device=dev)
+        self.rewards = torch.zeros(self.n, dtype=torch.float32, device=dev)
+        self.all_rewards = torch.zeros(self.GROUPS * self.G, dtype=torch.float32, device=dev)
+        self.adv = torch.zeros_like(self.all_rewards)
+        self.nccl = None
+        if world > 1:
+            import torch.distributed as dist
+
+            def exchange(b):
+                obj = [b]
+                dist.broadcast_object_list(obj, src=0)
+                return obj[0]
+            self.nccl = pkg.NcclRewards(rank, world, exchange)
+        self.tokens_per_step = self.n * self.GEN
+        torch.cuda.synchronize()
+
+    launches_per_step = None  # counted from the loop's pass counter
+
+    def _post(self, stream=None):
+        if self.nccl:
+            self.nccl.allgather(self.rewards, self.all_rewards, stream=stream)
+        else:
+            self.all_rewards.copy_(self.rewards)
+        self.pkg.grpo_advantages(self.all_rewards, self.G, out=self.adv, stream=stream)
+
+    def step(self):
+        self.eng.launch(requests=self.req_d, n_requests=self.n, dones=self.dones, state=self.state,
+                        trajectories=self.traj, rewards=self.rewards, n_rows=self.n)
+        self._post()
+
+    def units_per_step(self):
+        return float(self.tokens_per_step)
+
+    def check_errors(self):
+        st = self.eng.wait()
+        self.last_stats = st
+        return st["error"] or st["attn_error"]
+
+    def gpu_launches(self, steps):
+        # per pass: schedule, prepare, attention, logits, sampler; per step:
+        # one allgather (when N > 1) and one advantage kernel
+        return int(self.last_stats["passes"]) * 5 * steps + 2 * steps
+
+    def e2e(self, steps, warmup):
+        """Through the C ABI with host buffers: requests pushed into a mapped
+        RequestRing and dones drained from a mapped DoneRing by the host C
+        pump (rt_host_pump), then the trajectories and advantages copied to
+        pinned host memory; all inside the timed region."""
+        torch = self.torch
+        rings = self.pkg.HostRings()
+        traj_h = torch.empty(self.traj.shape, dtype=torch.int32).pin_memory()
+        adv_h = torch.empty(self.adv.shape, dtype=torch.float32).pin_memory()
+        s = torch.cuda.current_stream()
+
+        def one():
+            self.eng.launch(ring=rings.req, done_ring=rings.done, state=self.state,
+                            trajectories=self.traj, rewards=self.rewards, n_rows=self.n)
+            got, _ = rings.pump(self.reqs_host, self.n, send_sentinel=True, timeout_ms=120000)
+            if got != self.n:
+                raise RuntimeError(f"e2e pump drained {got} of {self.n}")
+            self._post()
+            traj_h.copy_(self.traj, non_blocking=True)
+            adv_h.copy_(self.adv, non_blocking=True)
+
+        for _ in range(min(warmup, 1)):
+            one()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(steps):
+            one()
+        e1.record(s)
+        torch.cuda.synchronize()
+        self.eng.wait()
+        rings.close()
+        ms = e0.elapsed_time(e1) / steps
+        return {"value": self.units_per_step() / (ms / 1e3), "unit": self.unit, "ms_per_step": ms,
+                "h2d_bytes_per_step": self.n * 34,
+                "d2h_bytes_per_step": self.n * 24 + traj_h.numel() * 4 + adv_h.numel() * 4}
+
+    def kernel_profile(self, n_rollouts=512):
+        """Per-kernel device time from a host-stepped replay (rt_rollout_profile)
+        of the first n_rollouts of the step."""
+        n = min(n_rollouts, self.n)
+        prof = self.eng.profile(requests=self.req_d, n_requests=n, dones=self.dones,
+                                state=self.state, trajectories=self.traj, rewards=self.rewards,
+                                n_rows=self.n)
+        return prof
+
+    def cpu_sample(self, threads, budget_s=10.0):
+        """The same decode step on the host: one GRPO group (16 rollouts, shared
+        512-token prompt) generating tokens with the CPU oracle - paged GQA
+        attention (oracle/oracle.c, OpenMP) + N(0,2) logits + the reference
+        sampling algorithm (cu/sample.cu:40-123, insertion top-k) - until the
+        time budget is spent."""
+        from concurrent.futures import ThreadPoolExecutor
+        orc = ge.load_oracle()
+        torch = self.torch
+        B, Hq, Hkv = self.G, 32, 8
+        ctx = self.PROMPT
+        n_pages = (ctx + self.GEN + 15) // 16
+        rng = np.random.default_rng(11)
+        arena = rng.standard_normal(B * n_pages * Hkv * 2 * 16 * 128, dtype=np.float32)
+        arena_b = (arena.view(np.uint32) >> 16).astype(np.uint16)
+        pt = np.arange(B * n_pages, dtype=np.int32).reshape(B, n_pages)
+        pool = ThreadPoolExecutor(max_workers=threads)
+        t0 = time.perf_counter()
+        steps = 0
+        while steps == 0 or time.perf_counter() - t0 < budget_s:
+            q = (rng.standard_normal((B, Hq, 128), dtype=np.float32).view(np.uint32) >> 16).astype(np.uint16)
+            lens = np.full(B, ctx + steps + 1, dtype=np.int32)
+            orc.paged_gqa_attention(q, arena_b, pt, lens, Hq, Hkv, 128 ** -0.5, n_threads=threads)
+            logits = rng.standard_normal((B, self.VOCAB), dtype=np.float32) * 2.0
+            list(pool.map(lambda b: orc.sample_row(logits[b], 0.8, 50, 0.9,
+                                                   orc.sample_u24(1234, b, steps)), range(B)))
+            steps += 1
+            if steps >= self.GEN:
+                break
+        dt = time.perf_counter() - t0
+        pool.shutdown()
+        return {"value": B * steps / dt, "unit": self.unit, "cores": threads, "kind": "port",
+                "seconds": dt,
+                "sample": f"1 group x 16 rollouts, {steps} decode steps from a 512-token prompt "
+                          f"(attention + logits + reference sampling per token)"}
+
+    def config(self):
+        return {"workload": self.name, "rollouts": self.GROUPS * self.G, "groups": self.GROUPS,
+                "group_size": self.G, "prompt_tokens": self.PROMPT, "new_tokens": self.GEN,
+                "rollouts_per_gpu": self.n, "q_heads": 32, "kv_heads": 8, "head_dim": 128,
+                "page_tokens": 16, "vocab": self.VOCAB, "sampling": "T=0.8 top-k 50 top-p 0.9",
+                "slots": 256, "reward": "U(0,1) Philox seed 5, NCCL allgather, GRPO advantages",
+                "l2": f"KV arena {self.arena.buf.numel() / 1e9:.2f} GB > 126 MB L2"}
+
+
+WORKLOADS = {"rollout": RolloutWorkload, "attention": AttentionWorkload,
+             "sampling": SamplingWorkload}
 
 
 # -------------------------------------------------------------------- main
@@ -366,6 +555,9 @@ def run_mine(args):
         ms = float(t.item())
         dist.barrier()
     err = wl.check_errors()
+    n_launch = wl.gpu_launches(args.steps) if wl.launches_per_step is None else \
+        wl.launches_per_step * args.steps
+    prof = wl.kernel_profile() if hasattr(wl, "kernel_profile") else None
     e2e = wl.e2e(args.steps, args.warmup)
     if world > 1:
         t = torch.tensor([e2e["ms_per_step"]], device=dev)
@@ -378,12 +570,33 @@ def run_mine(args):
 
     if rank == 0:
         peaks, src = measured_peaks()
-        achieved = wl.bytes / (ms / 1e3) / 1e9
-        traffic = ncu_traffic(wl.kernel)
+        if prof is not None:
+            # dominant kernel of the loop: paged attention, per-launch average
+            # from the host-stepped replay's CUDA events
+            attn_s = prof["ms_attention"] / 1e3
+            achieved = prof["attn_bytes_unique"] / attn_s / 1e9
+            tot = sum(prof[k] for k in ("ms_schedule", "ms_prepare", "ms_attention", "ms_logits",
+                                        "ms_sample"))
+            prof_report = {
+                "source": "rt_rollout_profile host-stepped replay, CUDA events per kernel",
+                "passes": prof["passes"],
+                "avg_us": {k[3:]: 1e3 * prof[k] / max(prof["passes"], 1)
+                           for k in ("ms_schedule", "ms_prepare", "ms_attention", "ms_logits",
+                                     "ms_sample")},
+                "share": {k[3:]: prof[k] / tot for k in ("ms_schedule", "ms_prepare",
+                                                         "ms_attention", "ms_logits", "ms_sample")},
+                "attn_logical_GBps": prof["attn_bytes_logical"] / attn_s / 1e9,
+                "attn_unique_bytes_per_launch": prof["attn_bytes_unique"] / max(prof["attn_launches"], 1),
+            }
+        else:
+            achieved = wl.bytes / (ms / 1e3) / 1e9
+            prof_report = None
+        traffic = ncu_traffic(wl.kernel + ":" + wl.name) or ncu_traffic(wl.kernel)
         line = {
             "metric": wl.metric, "value": wl.units_per_step() / (ms / 1e3) * world,
             "unit": wl.unit, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong" if wl.name == "grpo_rollouts_c5" else "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (Philox N(0,1), seeded)",
             "config": wl.config() | {"parallelism": f"replicas{world}" if world > 1 else "single"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
@@ -394,7 +607,8 @@ def run_mine(args):
                          "traffic": traffic, "kernel": wl.kernel},
             "cpu_baseline": cpu,
             "e2e": {k: e2e[k] for k in ("value", "unit", "h2d_bytes_per_step", "d2h_bytes_per_step")},
-            "gpu_launches": wl.launches_per_step * args.steps,
+            "gpu_launches": n_launch,
+            "kernels": prof_report,
             "clocks": clocks.report(),
             "device_error_code": err,
         }
@@ -431,13 +645,18 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--workload", default="attention", choices=sorted(WORKLOADS))
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=None)
+    ap.add_argument("--workload", default="rollout", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
     ap.add_argument("--chunk-pages", type=int, default=0)
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
+    quick = args.workload != "rollout"   # rollout steps are whole RL steps (~seconds)
+    if args.steps is None:
+        args.steps = 200 if quick else 3
+    if args.warmup is None:
+        args.warmup = 10 if quick else 3
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

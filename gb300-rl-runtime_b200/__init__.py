@@ -135,6 +135,16 @@ class rt_rollout_stats_t(ctypes.Structure):
         return {n: getattr(self, n) for n, _ in self._fields_}
 
 
+class rt_rollout_profile_t(ctypes.Structure):
+    _fields_ = [("passes", ctypes.c_uint64), ("attn_launches", ctypes.c_uint64),
+                ("sample_rows", ctypes.c_uint64)] + [
+        (n, ctypes.c_double) for n in ("ms_schedule", "ms_prepare", "ms_attention", "ms_logits",
+                                       "ms_sample", "attn_bytes_logical", "attn_bytes_unique")]
+
+    def as_dict(self):
+        return {n: getattr(self, n) for n, _ in self._fields_}
+
+
 # ------------------------------------------------------------------ loader
 _lib = None
 
@@ -159,6 +169,16 @@ _SIGS = {
     "rt_rollout_set_prefix": (ctypes.c_int, [_P, ctypes.c_uint32, _P, ctypes.c_uint32,
                                              ctypes.c_uint32]),
     "rt_rollout_launch": (ctypes.c_int, [_P, ctypes.POINTER(rt_rollout_io_t), _P]),
+    "rt_rollout_profile": (ctypes.c_int, [_P, ctypes.POINTER(rt_rollout_io_t), _P,
+                                          ctypes.POINTER(rt_rollout_profile_t)]),
+    "rt_reward_score": (ctypes.c_int, [_P, ctypes.c_uint32, _P, _P]),
+    "rt_grpo_advantages": (ctypes.c_int, [_P, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_float,
+                                          _P, _P]),
+    "rt_nccl_unique_id": (ctypes.c_int, [_P]),
+    "rt_nccl_init": (ctypes.c_int, [ctypes.POINTER(_P), ctypes.c_int, _P, ctypes.c_int]),
+    "rt_nccl_destroy": (ctypes.c_int, [_P]),
+    "rt_reward_allgather": (ctypes.c_int, [_P, _P, _P, ctypes.c_uint64, _P]),
+    "rt_nccl_wait": (ctypes.c_int, [_P, _P, ctypes.c_uint32]),
     "rt_rollout_wait": (ctypes.c_int, [_P, _P, ctypes.POINTER(rt_rollout_stats_t)]),
     "rt_logits_synth": (ctypes.c_int, [_P, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_uint32,
                                        ctypes.c_uint64, ctypes.c_float, _P]),
@@ -379,14 +399,31 @@ class RolloutEngine:
         check(lib().rt_rollout_set_prefix(self.h, prefix_id, arr.ctypes.data_as(ctypes.c_void_p),
                                           len(arr), token_len), "rt_rollout_set_prefix")
 
+    @staticmethod
+    def _io(ring, requests, n_requests, done_ring, dones, state, step_count, trajectories,
+            rewards, n_rows):
+        ptr = lambda t: None if t is None else (t if isinstance(t, int) else t.data_ptr())
+        return rt_rollout_io_t(ptr(ring), ptr(requests), n_requests, ptr(done_ring), ptr(dones),
+                               ptr(state), ptr(step_count), ptr(trajectories), ptr(rewards),
+                               n_rows)
+
     def launch(self, *, requests=None, n_requests=0, ring=None, done_ring=None, dones=None,
                state=None, step_count=None, trajectories=None, rewards=None, n_rows=0,
                stream=None):
-        ptr = lambda t: None if t is None else (t if isinstance(t, int) else t.data_ptr())
-        io = rt_rollout_io_t(ptr(ring), ptr(requests), n_requests, ptr(done_ring), ptr(dones),
-                             ptr(state), ptr(step_count), ptr(trajectories), ptr(rewards), n_rows)
+        io = self._io(ring, requests, n_requests, done_ring, dones, state, step_count,
+                      trajectories, rewards, n_rows)
         check(lib().rt_rollout_launch(self.h, ctypes.byref(io), _stream_ptr(stream)),
               "rt_rollout_launch")
+
+    def profile(self, *, requests=None, n_requests=0, dones=None, state=None, trajectories=None,
+                rewards=None, n_rows=0, stream=None):
+        """rt_rollout_profile: host-stepped replay with per-kernel CUDA events."""
+        io = self._io(None, requests, n_requests, None, dones, state, None, trajectories,
+                      rewards, n_rows)
+        out = rt_rollout_profile_t()
+        check(lib().rt_rollout_profile(self.h, ctypes.byref(io), _stream_ptr(stream),
+                                       ctypes.byref(out)), "rt_rollout_profile")
+        return out.as_dict()
 
     def wait(self, stream=None, check_errors=True):
         st = rt_rollout_stats_t()
@@ -441,3 +478,42 @@ class HostRings:
             lib().req_ring_destroy(self.req)
             lib().done_ring_destroy(self.done)
             self.req = self.done = None
+
+
+# ----------------------------------------------------------- rewards / NCCL
+def grpo_advantages(rewards, group, eps=1e-6, out=None, stream=None):
+    import torch
+    if out is None:
+        out = torch.empty_like(rewards)
+    check(lib().rt_grpo_advantages(_ptr(rewards), rewards.numel(), group, eps, _ptr(out),
+                                   _stream_ptr(stream)), "rt_grpo_advantages")
+    return out
+
+
+class NcclRewards:
+    """rt_nccl_* communicator for the reward allgather.  `exchange_id(id_bytes)`
+    distributes rank 0's 128-byte unique id (e.g. through torch.distributed)."""
+
+    def __init__(self, rank, world, exchange_id):
+        buf = ctypes.create_string_buffer(128)
+        if rank == 0:
+            check(lib().rt_nccl_unique_id(buf), "rt_nccl_unique_id")
+        uid = exchange_id(bytes(buf.raw))
+        buf = ctypes.create_string_buffer(uid, 128)
+        comm = ctypes.c_void_p()
+        check(lib().rt_nccl_init(ctypes.byref(comm), world, buf, rank), "rt_nccl_init")
+        self.comm = comm
+        self.world = world
+
+    def allgather(self, send, recv, stream=None):
+        check(lib().rt_reward_allgather(self.comm, _ptr(send), _ptr(recv), send.numel(),
+                                        _stream_ptr(stream)), "rt_reward_allgather")
+        return recv
+
+    def wait(self, stream=None, timeout_ms=60000):
+        check(lib().rt_nccl_wait(self.comm, _stream_ptr(stream), timeout_ms), "rt_nccl_wait")
+
+    def close(self):
+        if self.comm:
+            lib().rt_nccl_destroy(self.comm)
+            self.comm = None

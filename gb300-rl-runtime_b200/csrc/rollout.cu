@@ -63,6 +63,8 @@ struct SlotExt {
     uint32_t row, request_lo, pos, ctx_len, last_token, decoding, cow_rows;
     int32_t cow_src;
     uint64_t seed;
+    uint32_t prefix;  // shared-prefix id + 1, 0 = none
+    uint32_t pad;
 };
 
 struct Dev {
@@ -259,6 +261,7 @@ __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
                 if (ctx > cap)
                     ctx = cap;
                 e.row = row;
+                e.prefix = (pfx != 0u && pfx - 1u < d.max_prefixes) ? pfx : 0u;
                 e.request_lo = rs.request_id;
                 e.ctx_len = ctx;
                 e.pos = ctx;
@@ -393,7 +396,7 @@ __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
 }
 
 __global__ void __launch_bounds__(kSched, 1)
-schedule_kernel(const Dev d, cudaGraphConditionalHandle handle)
+schedule_kernel(const Dev d, cudaGraphConditionalHandle handle, int in_graph)
 {
     __shared__ SchedShared sh;
     const bool stop = schedule_pass(d, sh);
@@ -403,7 +406,8 @@ schedule_kernel(const Dev d, cudaGraphConditionalHandle handle)
             for (uint32_t s = 0; s < d.max_slots; s++)
                 d.enable[s] = 0u;
         }
-        cudaGraphSetConditional(handle, stop ? 0u : 1u);
+        if (in_graph)
+            cudaGraphSetConditional(handle, stop ? 0u : 1u);
     }
 }
 
@@ -533,6 +537,38 @@ struct rt_rollout {
 
 namespace {
 
+// The decode chain of one pass (after the schedule kernel).  When `ev` is
+// given, events are recorded around each of the four launches.
+int launch_decode(rt_rollout *e, cudaStream_t st, cudaEvent_t *ev)
+{
+    const Dev &d = e->d;
+    if (ev)
+        cudaEventRecord(ev[0], st);
+    prepare_kernel<<<d.max_slots, 256, 0, st>>>(d);
+    if (ev)
+        cudaEventRecord(ev[1], st);
+    int rc = rt_paged_decode_attention(&e->ap, d.q, d.arena, d.page_table, d.seq_lens, d.attn_out,
+                                       e->attn_ws, e->attn_ws_bytes, st);
+    if (rc != RT_OK)
+        return rc;
+    if (ev)
+        cudaEventRecord(ev[2], st);
+    const dim3 lg((d.vocab / 4u + 1023u) / 1024u, d.max_slots);
+    logits_kernel<<<lg, 256, 0, st>>>(d);
+    if (ev)
+        cudaEventRecord(ev[3], st);
+    rt_sample_params_t sp;
+    sp.num_rows = d.max_slots;
+    sp.vocab = d.vocab;
+    sp.row_stride = d.vocab;
+    sp.fused_cum = 1u;
+    sp.row_enable = d.enable;
+    rc = rt_sample_rows(&sp, d.logits, d.srows, d.tokens, st);
+    if (ev)
+        cudaEventRecord(ev[4], st);
+    return rc;
+}
+
 int engine_build_graph(rt_rollout *e)
 {
     cudaError_t err;
@@ -560,23 +596,9 @@ int engine_build_graph(rt_rollout *e)
         return rt::cuda_fail(err, "rollout: cudaStreamBeginCaptureToGraph");
     int rc = RT_OK;
     const Dev &d = e->d;
-    schedule_kernel<<<1, kSched, 0, e->cap>>>(d, h);
-    if (e->cfg.decode_mode == RT_ROLLOUT_DECODE_FULL) {
-        prepare_kernel<<<d.max_slots, 256, 0, e->cap>>>(d);
-        rc = rt_paged_decode_attention(&e->ap, d.q, d.arena, d.page_table, d.seq_lens, d.attn_out,
-                                       e->attn_ws, e->attn_ws_bytes, e->cap);
-        if (rc == RT_OK) {
-            const dim3 lg((d.vocab / 4u + 1023u) / 1024u, d.max_slots);
-            logits_kernel<<<lg, 256, 0, e->cap>>>(d);
-            rt_sample_params_t sp;
-            sp.num_rows = d.max_slots;
-            sp.vocab = d.vocab;
-            sp.row_stride = d.vocab;
-            sp.fused_cum = 1u;
-            sp.row_enable = d.enable;
-            rc = rt_sample_rows(&sp, d.logits, d.srows, d.tokens, e->cap);
-        }
-    }
+    schedule_kernel<<<1, kSched, 0, e->cap>>>(d, h, 1);
+    if (e->cfg.decode_mode == RT_ROLLOUT_DECODE_FULL)
+        rc = launch_decode(e, e->cap, nullptr);
     cudaGraph_t captured = nullptr;
     err = cudaStreamEndCapture(e->cap, &captured);
     if (rc != RT_OK)
@@ -807,7 +829,21 @@ extern "C" int rt_rollout_set_prefix(rt_rollout_t *e, uint32_t prefix_id, const 
     return RT_OK;
 }
 
+static int rollout_setup(rt_rollout_t *e, const rt_rollout_io_t *io, cudaStream_t s);
+
 extern "C" int rt_rollout_launch(rt_rollout_t *e, const rt_rollout_io_t *io, void *stream)
+{
+    cudaStream_t s = (cudaStream_t)stream;
+    int rc = rollout_setup(e, io, s);
+    if (rc != RT_OK)
+        return rc;
+    cudaError_t err = cudaGraphLaunch(e->exec, s);
+    if (err != cudaSuccess)
+        return rt::cuda_fail(err, "rollout_launch");
+    return RT_OK;
+}
+
+static int rollout_setup(rt_rollout_t *e, const rt_rollout_io_t *io, cudaStream_t s)
 {
     if (!e || !io || !io->state || (!io->ring && !io->requests && io->n_requests)) {
         rt::set_error("rollout_launch: needs an engine, a state table and a request source");
@@ -817,7 +853,10 @@ extern "C" int rt_rollout_launch(rt_rollout_t *e, const rt_rollout_io_t *io, voi
         rt::set_error("rollout_launch: give either a request ring or a request array");
         return RT_EINVAL;
     }
-    RtIo *x = e->io_stage;
+    // Pageable staging: cudaMemcpyAsync copies it before returning, so a
+    // later launch cannot overwrite the block of an earlier one in flight.
+    RtIo stage;
+    RtIo *x = &stage;
     x->ring = io->ring;
     x->reqs = io->requests;
     x->n_reqs = io->ring ? 0u : io->n_requests;
@@ -828,7 +867,6 @@ extern "C" int rt_rollout_launch(rt_rollout_t *e, const rt_rollout_io_t *io, voi
     x->traj = io->trajectories;
     x->rewards = io->rewards;
     x->n_rows = io->n_rows;
-    cudaStream_t s = (cudaStream_t)stream;
     cudaError_t err = cudaMemcpyAsync(e->d.io, x, sizeof(RtIo), cudaMemcpyHostToDevice, s);
     if (err == cudaSuccess)
         err = cudaMemsetAsync(e->d.ctl, 0, sizeof(RtCtl), s);
@@ -838,11 +876,95 @@ extern "C" int rt_rollout_launch(rt_rollout_t *e, const rt_rollout_io_t *io, voi
         err = cudaMemsetAsync(e->d.enable, 0, sizeof(uint32_t) * e->d.max_slots, s);
     if (err == cudaSuccess)
         err = cudaMemsetAsync(io->state, 0, sizeof(GpuRolloutState), s);
-    if (err == cudaSuccess)
-        err = cudaGraphLaunch(e->exec, s);
     if (err != cudaSuccess)
-        return rt::cuda_fail(err, "rollout_launch");
+        return rt::cuda_fail(err, "rollout_launch: setup");
     return RT_OK;
+}
+
+// Host-stepped replay of the loop with CUDA events around every kernel of
+// every pass (per-kernel durations for roofline reporting).  Same kernels,
+// same data as rt_rollout_launch; the host synchronises once per pass.
+extern "C" int rt_rollout_profile(rt_rollout_t *e, const rt_rollout_io_t *io, void *stream,
+                                  rt_rollout_profile_t *out)
+{
+    if (!e || !out || e->cfg.decode_mode != RT_ROLLOUT_DECODE_FULL) {
+        rt::set_error("rollout_profile: needs a full-decode engine and an output struct");
+        return RT_EINVAL;
+    }
+    cudaStream_t s = (cudaStream_t)stream;
+    int rc = rollout_setup(e, io, s);
+    if (rc != RT_OK)
+        return rc;
+    memset(out, 0, sizeof(*out));
+    cudaEvent_t ev[6];
+    for (auto &x : ev)
+        cudaEventCreate(&x);
+    const uint32_t S = e->d.max_slots;
+    int32_t *lens = new int32_t[S];
+    SlotExt *ext = new SlotExt[S];
+    const double tok_bytes = (double)e->d.hkv * 128.0 * 2.0 * 2.0;  // K+V bf16 per token
+    cudaError_t err = cudaSuccess;
+    for (uint64_t pass = 0; pass < e->d.max_passes; pass++) {
+        cudaEventRecord(ev[5], s);
+        schedule_kernel<<<1, kSched, 0, s>>>(e->d, 0, 0);
+        rc = launch_decode(e, s, ev);
+        if (rc != RT_OK)
+            break;
+        RtCtl c;
+        err = cudaMemcpyAsync(lens, e->d.seq_lens, sizeof(int32_t) * S, cudaMemcpyDeviceToHost, s);
+        if (err == cudaSuccess)
+            err = cudaMemcpyAsync(ext, e->d.ext, sizeof(SlotExt) * S, cudaMemcpyDeviceToHost, s);
+        if (err == cudaSuccess)
+            err = cudaMemcpyAsync(&c, e->d.ctl, sizeof(c), cudaMemcpyDeviceToHost, s);
+        if (err == cudaSuccess)
+            err = cudaStreamSynchronize(s);
+        if (err != cudaSuccess)
+            break;
+        float ms[5];
+        cudaEventElapsedTime(&ms[0], ev[5], ev[0]);
+        for (int k = 0; k < 4; k++)
+            cudaEventElapsedTime(&ms[k + 1], ev[k], ev[k + 1]);
+        out->ms_schedule += ms[0];
+        out->ms_prepare += ms[1];
+        out->ms_attention += ms[2];
+        out->ms_logits += ms[3];
+        out->ms_sample += ms[4];
+        out->passes++;
+        uint32_t active = 0;
+        double uniq = 0.0;
+        uint32_t seen[64];
+        uint32_t n_seen = 0;
+        for (uint32_t k = 0; k < S; k++) {
+            if (lens[k] <= 0)
+                continue;
+            active++;
+            out->attn_bytes_logical += (double)lens[k] * tok_bytes;
+            const uint32_t pf = ext[k].prefix;
+            uniq += (double)(lens[k] - (int32_t)ext[k].ctx_len) * tok_bytes;
+            bool dup = false;
+            for (uint32_t j = 0; j < n_seen; j++)
+                dup |= seen[j] == pf;
+            if (pf && !dup) {
+                if (n_seen < 64)
+                    seen[n_seen++] = pf;
+                uniq += (double)ext[k].ctx_len * tok_bytes;
+            } else if (!pf) {
+                uniq += (double)ext[k].ctx_len * tok_bytes;
+            }
+        }
+        out->attn_bytes_unique += uniq;
+        out->sample_rows += active;
+        out->attn_launches += active ? 1u : 0u;
+        if (c.stop || c.error)
+            break;
+    }
+    for (auto &x : ev)
+        cudaEventDestroy(x);
+    delete[] lens;
+    delete[] ext;
+    if (err != cudaSuccess)
+        return rt::cuda_fail(err, "rollout_profile");
+    return rc;
 }
 
 extern "C" int rt_rollout_wait(rt_rollout_t *e, void *stream, rt_rollout_stats_t *st)

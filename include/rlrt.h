@@ -17,6 +17,7 @@
 #include "ring.h"
 #include "kv_prefix.h"
 #include "arena.h"
+#include "reward.h"
 
 #ifdef __cplusplus
 extern "C" {
@@ -234,6 +235,21 @@ int rt_rollout_set_prefix(rt_rollout_t *eng, uint32_t prefix_id, const int32_t *
  * when an array source is exhausted and no rollout is active, or on error. */
 int rt_rollout_launch(rt_rollout_t *eng, const rt_rollout_io_t *io, void *stream);
 
+/* Per-kernel device time of a host-stepped replay of the loop. */
+typedef struct {
+    uint64_t passes;
+    uint64_t attn_launches;       /* passes with at least one active slot */
+    uint64_t sample_rows;         /* active slot-passes (rows sampled) */
+    double ms_schedule, ms_prepare, ms_attention, ms_logits, ms_sample;
+    double attn_bytes_logical;    /* sum over slots of context x K/V bytes per token */
+    double attn_bytes_unique;     /* same with each shared prefix counted once per pass */
+} rt_rollout_profile_t;
+
+/* Run the loop pass by pass from the host, with CUDA events around each
+ * kernel (same kernels and data as rt_rollout_launch); synchronous. */
+int rt_rollout_profile(rt_rollout_t *eng, const rt_rollout_io_t *io, void *stream,
+                       rt_rollout_profile_t *out);
+
 /* Wait for the loop (stream sync) and read its counters. */
 int rt_rollout_wait(rt_rollout_t *eng, void *stream, rt_rollout_stats_t *stats);
 
@@ -265,6 +281,34 @@ int rt_launch_rollout_worker(RequestRing *req_ring, DoneRing *done_ring,
 /* Counters of the last rt_launch_rollout_worker on the current device
  * (reads device memory on `stream`; safe while the worker runs). */
 int rt_rollout_worker_stats(void *stream, rt_rollout_stats_t *stats);
+
+/* ------------------------------------------------------------------------
+ * Rewards and group-normalised advantages (new; the reference has only the
+ * mock scorer, cu/reward.cu:4-15, never launched).
+ * ---------------------------------------------------------------------- */
+/* Drop-in for reward_score_kernel: descs[i].reward = scores[i] =
+ * (descs[i].token_count & 0xFF) / 255 for i < n (device pointers; scores
+ * may be NULL). */
+int rt_reward_score(RewardDesc *descs, uint32_t n, float *scores, void *stream);
+
+/* A_i = (r_i - mean_g) / (std_g + eps) over consecutive groups of G,
+ * population std; per group: fp32 sum in index order, mean = sum / G,
+ * var = sum of (r - mean)^2 in index order, std = sqrt(var / G) (all
+ * correctly rounded, no fused multiply-add).  n must be a multiple of G. */
+int rt_grpo_advantages(const float *rewards, uint32_t n, uint32_t G, float eps, float *adv,
+                       void *stream);
+
+/* NCCL plumbing for the one cross-GPU exchange of the path: every rank
+ * contributes its rollouts' rewards, every rank receives all of them in
+ * rank order.  `comm` is an ncclComm_t passed as void*. */
+int rt_nccl_unique_id(void *id128);
+int rt_nccl_init(void **comm, int nranks, const void *id128, int rank);
+int rt_nccl_destroy(void *comm);
+int rt_reward_allgather(void *comm, const float *send, float *recv, uint64_t n_per_rank,
+                        void *stream);
+/* Wait for the stream's work with a deadline; on expiry (e.g. a peer rank
+ * died) abort the communicator and return RT_ETIMEOUT instead of hanging. */
+int rt_nccl_wait(void *comm, void *stream, uint32_t timeout_ms);
 
 /* ------------------------------------------------------------------------
  * Synthetic data (seeded, counter-based, reproducible on any GPU).

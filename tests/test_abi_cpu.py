@@ -20,11 +20,16 @@ def declared_functions():
         if not fn.endswith(".h"):
             continue
         src = open(os.path.join(INCLUDE, fn)).read()
+        src = re.sub(r"/\*.*?\*/", " ", src, flags=re.S)      # drop comments
+        src = re.sub(r"//[^\n]*", " ", src)
         # only prototypes inside extern "C" blocks are exported functions
-        for block in re.findall(r'extern "C" \{\n#endif\n(.*?)#ifdef __cplusplus\n\}', src, re.S):
-            for line in block.split(";"):
-                line = " ".join(l for l in line.split("\n") if not l.strip().startswith(("/*", "*")))
-                m = pat.search(line.strip())
+        for block in re.findall(r'extern "C" \{\s*#endif(.*?)#ifdef __cplusplus\s*\}', src, re.S):
+            block = "\n".join(l for l in block.split("\n") if not l.strip().startswith("#"))
+            for decl in block.split(";"):
+                decl = " ".join(decl.split())
+                if decl.startswith(("typedef", "#")) or "{" in decl or "}" in decl:
+                    continue
+                m = pat.search(decl)
                 if m:
                     names.add(m.group(1))
     return sorted(names)
