@@ -347,10 +347,7 @@ class RolloutWorkload:
         self.torch = torch
         self.pkg = pkg = ge.load_package()
         self.rank, self.world, self.dev = rank, world, dev
-        if self.GROUPS % world:
-            raise SystemExit(f"{self.GROUPS} groups do not split over {world} GPUs")
-        self.ng = self.GROUPS // world
-        self.g0 = rank * self.ng
+        self.g0, self.ng = pkg.shard_groups(self.GROUPS, world, rank)
         self.n = self.ng * self.G
         pages_prompt = self.PROMPT // 16
         priv = 256 * ((self.GEN + 16 + 15) // 16)

@@ -517,3 +517,33 @@ class NcclRewards:
         if self.comm:
             lib().rt_nccl_destroy(self.comm)
             self.comm = None
+
+
+# ------------------------------------------------------- GRPO host helpers
+REQUEST_RECORD = [("request_id", "<u8"), ("max_tokens", "<u4"), ("kv_blocks", "<u4"),
+                  ("temperature", "<f4"), ("top_k", "<u2"), ("top_p", "<f4"), ("rng_seed", "<u8")]
+
+
+def shard_groups(total_groups, world, rank):
+    """Contiguous split of GRPO groups over ranks: (first group, count).
+    A group never straddles two GPUs, so its shared prefix lives on one."""
+    base, rem = divmod(total_groups, world)
+    g0 = rank * base + min(rank, rem)
+    return g0, base + (1 if rank < rem else 0)
+
+
+def grpo_requests(g0, ng, group_size, max_tokens, prompt_pages, temperature=0.8, top_k=50,
+                  top_p=0.9, seed=1234):
+    """RolloutRequest records for local groups g0 .. g0+ng-1: request ids
+    1 + global rollout index (low 32 bits), shared prefix = local group
+    (request_id bits 32..63 = local group + 1)."""
+    import numpy as np
+    n = ng * group_size
+    r = np.zeros(n, dtype=np.dtype(REQUEST_RECORD))
+    local_group = np.arange(n) // group_size
+    r["request_id"] = (np.arange(n, dtype=np.uint64) + np.uint64(g0 * group_size + 1)) | \
+        ((local_group.astype(np.uint64) + np.uint64(1)) << np.uint64(32))
+    r["max_tokens"] = max_tokens
+    r["kv_blocks"] = prompt_pages
+    r["temperature"], r["top_k"], r["top_p"], r["rng_seed"] = temperature, top_k, top_p, seed
+    return r

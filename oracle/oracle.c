@@ -430,6 +430,19 @@ orc_scheduler_run(const RolloutRequest *reqs, uint32_t n_reqs,
     return nd;
 }
 
+/* Reward of a finished rollout in the Philox reward mode:
+ * U(0,1) = (word0 >> 8) / 2^24, key = seed, counter = {request low 32, 0,
+ * 0x52455744, 0}. */
+float
+orc_reward_u01(uint64_t seed, uint32_t request_lo)
+{
+    uint32_t ctr[4] = {request_lo, 0u, 0x52455744u, 0u};
+    uint32_t key[2] = {(uint32_t)seed, (uint32_t)(seed >> 32)};
+    uint32_t out[4];
+    orc_philox4x32_10(ctr, key, out);
+    return (float)(out[0] >> 8) * (1.0f / 16777216.0f);
+}
+
 /* ----------------------------------------------------------- advantages */
 void
 orc_grpo_advantages(const float *r, uint32_t n, uint32_t G, float eps, float *adv)

@@ -88,6 +88,9 @@ uint32_t orc_scheduler_run(const RolloutRequest *reqs, uint32_t n_reqs,
                            RolloutDone *dones, uint32_t *done_pass,
                            GpuRolloutState *state, uint32_t *passes_run);
 
+/* Philox U(0,1) reward of the rollout loop's RT_REWARD_PHILOX mode. */
+float orc_reward_u01(uint64_t seed, uint32_t request_lo);
+
 /* Group-normalised advantages, group size G (n % G == 0):
  * A_i = (r_i - mean_g) / (std_g + eps), population std, every sum in fp32
  * in index order, no fused multiply-add. */

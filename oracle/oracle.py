@@ -77,6 +77,7 @@ def oracle_lib() -> ctypes.CDLL:
             "orc_sample_u24": (_u32, [_u64, _u32, _u64]),
             "orc_scheduler_run": (_u32, [_P, _u32, _P, _u32, _int, _u32, _P, _P, _P, _P]),
             "orc_grpo_advantages": (None, [_P, _u32, _u32, _f32, _P]),
+            "orc_reward_u01": (_f32, [_u64, _u32]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(l, name)
@@ -150,6 +151,10 @@ def scheduler_run(reqs: np.ndarray, arrival_pass=None, max_admit=1, drop_when_fu
         _ptr(reqs), n, None if arr is None else _ptr(arr), max_admit, int(drop_when_full),
         max_passes, _ptr(dones), _ptr(done_pass), _ptr(state), _ptr(passes))
     return dones[:nd], done_pass[:nd], state, int(passes[0])
+
+
+def reward_u01(seed, request_lo) -> float:
+    return float(np.float32(oracle_lib().orc_reward_u01(seed, request_lo)))
 
 
 def grpo_advantages(rewards, group, eps=1e-6):
