@@ -161,9 +161,10 @@ class AttentionWorkload:
         self.q = torch.empty(self.B, self.Hq, 128, dtype=torch.bfloat16, device=dev)
         self.pkg.fill_normal_bf16(self.q, seed=2 + rank, stream_id=2)
         self.out = torch.empty(self.B, self.Hq, 128, dtype=torch.float32, device=dev)
+        # pure streaming (no page is shared): evict-first keeps L2 clean
         self.attn = self.pkg.PagedDecodeAttention(self.B, self.Hq, self.Hkv, self.P,
                                                   int(self.lens.max()), self.arena_pages,
-                                                  chunk_pages=args.chunk_pages)
+                                                  chunk_pages=args.chunk_pages, evict_first=True)
         self.i = 0
         # algorithmic bytes per launch: KV once + q + out + page-table entries
         self.kv_bytes = int(self.lens.sum()) * self.Hkv * 128 * 2 * 2
@@ -648,7 +649,17 @@ def main():
     ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
     ap.add_argument("--chunk-pages", type=int, default=0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--ncu-replay", type=int, default=0,
+                    help="rollout only: run the host-stepped replay of this many rollouts and "
+                         "exit (plain kernel launches, for ncu captures)")
     args = ap.parse_args()
+    if args.ncu_replay:
+        import torch
+        torch.cuda.set_device(0)
+        wl = WORKLOADS["rollout"](args, 0, 1, torch.device("cuda", 0))
+        prof = wl.kernel_profile(args.ncu_replay)
+        print(json.dumps({"ncu_replay": args.ncu_replay, "profile": prof}), flush=True)
+        return
     quick = args.workload != "rollout"   # rollout steps are whole RL steps (~seconds)
     if args.steps is None:
         args.steps = 200 if quick else 3

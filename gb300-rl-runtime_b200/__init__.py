@@ -86,7 +86,7 @@ class rt_attn_params_t(ctypes.Structure):
                 ("num_kv_heads", ctypes.c_uint32), ("head_dim", ctypes.c_uint32),
                 ("max_pages_per_seq", ctypes.c_uint32), ("max_seq_len", ctypes.c_uint32),
                 ("arena_pages", ctypes.c_uint64), ("scale", ctypes.c_float),
-                ("chunk_pages", ctypes.c_uint32)]
+                ("chunk_pages", ctypes.c_uint32), ("kv_evict_first", ctypes.c_uint32)]
 
 
 class rt_sample_row_t(ctypes.Structure):
@@ -245,11 +245,12 @@ class PagedDecodeAttention:
     """
 
     def __init__(self, num_seqs, num_q_heads, num_kv_heads, max_pages_per_seq, max_seq_len,
-                 arena_pages, scale=None, chunk_pages=0, device="cuda"):
+                 arena_pages, scale=None, chunk_pages=0, evict_first=False, device="cuda"):
         import torch
         self.params = rt_attn_params_t(
             num_seqs, num_q_heads, num_kv_heads, 128, max_pages_per_seq, max_seq_len,
-            arena_pages, scale if scale is not None else 128 ** -0.5, chunk_pages)
+            arena_pages, scale if scale is not None else 128 ** -0.5, chunk_pages,
+            1 if evict_first else 0)
         n = lib().rt_attn_workspace_bytes(ctypes.byref(self.params))
         if n == 0:
             raise RuntimeErrorRT("bad attention params: " + lib().rt_last_error().decode())

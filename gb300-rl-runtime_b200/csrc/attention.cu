@@ -55,6 +55,7 @@ struct AttnArgs {
     uint32_t num_q_heads, num_kv_heads, max_pages, max_chunks, chunk_pages, max_seq_len;
     uint64_t arena_pages;
     float scale_log2;
+    uint32_t evict_first;
 };
 
 __device__ __forceinline__ void flag_error(int32_t *err, int32_t code)
@@ -70,8 +71,11 @@ paged_gqa_decode_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnAr
     __shared__ __align__(8) uint64_t bars[kWarps][kStages];
     __shared__ int s_last;
 
+    // Grid: x = sequence (fastest), y = KV head, z = chunk.  Sequences that
+    // share prefix pages (a GRPO group) are adjacent, so their CTAs for one
+    // (head, chunk) run together and the shared pages come from L2.
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int chunk = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int b = blockIdx.x, h = blockIdx.y, chunk = blockIdx.z;
     const int L = a.seq_lens[b];
     const uint32_t Hq = a.num_q_heads, Hkv = a.num_kv_heads;
 
@@ -122,7 +126,7 @@ paged_gqa_decode_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnAr
     }
     __syncwarp();
 
-    const uint64_t policy = rt::l2_policy_evict_first();
+    const uint64_t policy = a.evict_first ? rt::l2_policy_evict_first() : rt::l2_policy_evict_normal();
     auto issue = [&](int i, int s) {
         const int pg = __shfl_sync(0xffffffffu, my_pg, i);
         if (lane == 0) {
@@ -366,7 +370,7 @@ int make_plan(const rt_attn_params_t *p, Plan *pl)
         rt::set_error("attention: group size %u unsupported (1, 2, 4 or 8)", g);
         return RT_EINVAL;
     }
-    if (p->num_seqs == 0 || p->num_seqs > 65535u || p->num_kv_heads > 65535u) {
+    if (p->num_seqs == 0 || p->num_kv_heads > 65535u) {
         rt::set_error("attention: num_seqs %u / num_kv_heads %u out of range", p->num_seqs,
                       p->num_kv_heads);
         return RT_EINVAL;
@@ -563,8 +567,12 @@ extern "C" int rt_paged_decode_attention(const rt_attn_params_t *p, const void *
     args.max_seq_len = p->max_seq_len;
     args.arena_pages = p->arena_pages;
     args.scale_log2 = p->scale * 1.4426950408889634f;
-
-    const dim3 grid(pl.max_chunks, p->num_kv_heads, p->num_seqs);
+    args.evict_first = p->kv_evict_first ? 1u : 0u;
+    if (pl.max_chunks > 65535u) {
+        rt::set_error("attention: %u chunks exceed the grid's z limit", pl.max_chunks);
+        return RT_EINVAL;
+    }
+    const dim3 grid(p->num_seqs, p->num_kv_heads, pl.max_chunks);
     cudaStream_t s = (cudaStream_t)stream;
     switch (pl.group) {
     case 1: return launch_g<1>(map, args, grid, s);

@@ -752,6 +752,7 @@ extern "C" int rt_rollout_create(const rt_rollout_config_t *cfg, KVArena *arena,
         e->ap.arena_pages = arena_pages;
         e->ap.scale = 0.08838834764831845f;  // 1/sqrt(128)
         e->ap.chunk_pages = cfg->chunk_pages;
+        e->ap.kv_evict_first = 0u;  // group members re-read shared prefix pages
         e->attn_ws_bytes = rt_attn_workspace_bytes(&e->ap);
         if (e->attn_ws_bytes == 0) {
             engine_free(e);

@@ -93,6 +93,13 @@ __device__ __forceinline__ uint64_t l2_policy_evict_first()
     return p;
 }
 
+__device__ __forceinline__ uint64_t l2_policy_evict_normal()
+{
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *map)
 {
     asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
@@ -170,7 +177,9 @@ __host__ __device__ __forceinline__ void philox4x32_10(uint32_t c0, uint32_t c1,
     out[3] = c3;
 }
 
-// Four N(0,1) samples from one Philox block by the Box-Muller transform.
+// Four N(0,1) samples from one Philox block by the Box-Muller transform
+// (synthetic data only: the SFU approximations of log / sin / cos are used
+// for speed; every consumer regenerates values with this same function).
 __device__ __forceinline__ void philox_normal4(uint64_t seed, uint32_t c0, uint32_t c1,
                                                uint32_t c2, float (&z)[4], uint32_t c3 = 0u)
 {
@@ -180,9 +189,9 @@ __device__ __forceinline__ void philox_normal4(uint64_t seed, uint32_t c0, uint3
     for (int k = 0; k < 2; k++) {
         const float u1 = ((float)((x[2 * k] >> 8) + 1u)) * (1.0f / 16777216.0f);
         const float u2 = ((float)(x[2 * k + 1] >> 8)) * (1.0f / 16777216.0f);
-        const float rad = sqrtf(-2.0f * logf(u1));
+        const float rad = __fsqrt_rn(-2.0f * __logf(u1));
         float s, c;
-        sincospif(2.0f * u2, &s, &c);
+        __sincosf(6.283185307179586f * u2, &s, &c);
         z[2 * k] = rad * c;
         z[2 * k + 1] = rad * s;
     }

@@ -59,6 +59,10 @@ typedef struct {
     uint64_t arena_pages;        /* pages addressable in kv_arena */
     float    scale;              /* softmax scale, usually 1/sqrt(128) */
     uint32_t chunk_pages;        /* pages per split-K work unit; 0 = auto */
+    uint32_t kv_evict_first;     /* 1: KV loads carry an L2 evict-first hint
+                                    (pure streaming); 0: normal caching, so
+                                    pages shared by several sequences (a
+                                    copy-on-write prefix) are reused from L2 */
 } rt_attn_params_t;
 
 /* Device scratch the attention call needs (split-K partials, per-(seq,head)

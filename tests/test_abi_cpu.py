@@ -78,7 +78,7 @@ def test_fixed128_config(pkg):
 
 
 def test_attention_params_validation_on_cpu(pkg):
-    p = pkg.rt_attn_params_t(64, 32, 8, 128, 256, 4096, 100000, 128 ** -0.5, 0)
+    p = pkg.rt_attn_params_t(64, 32, 8, 128, 256, 4096, 100000, 128 ** -0.5, 0, 0)
     assert pkg.lib().rt_attn_workspace_bytes(ctypes.byref(p)) > 0
     bad = pkg.rt_attn_params_t(64, 32, 8, 64, 256, 4096, 100000, 1.0, 0)
     assert pkg.lib().rt_attn_workspace_bytes(ctypes.byref(bad)) == 0
