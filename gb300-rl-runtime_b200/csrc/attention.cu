@@ -5,22 +5,24 @@
 // softmax over 16-token tiles, .V) to paged grouped-query attention over the
 // KV arena, built for B200's memory system:
 //
-//  * Work unit (CTA): one sequence b, one KV head h, one chunk of
-//    `chunk_pages` 16-token pages.  4 warps split the chunk's pages
-//    round-robin; each warp runs its own 3-stage pipeline.
-//  * Staging: for every page a warp's elected lane issues four 2-D TMA
-//    tensor loads (K and V, two 64-column halves each, 128-byte swizzle)
-//    into one 8 KiB stage, completion tracked by a shared-memory mbarrier
-//    with transaction bytes.  The KV stream is read exactly once and
-//    carries an L2 evict-first hint.
+//  * Work unit: one WARP owns one item = (sequence b, KV head h, chunk of
+//    `chunk_pages` 16-token pages).  Warps never synchronise with each other,
+//    so a warp in its prologue (page ids, Q fragment, first TMA round trip)
+//    overlaps the steady state of the other warps on the SM.  Items are
+//    numbered sequence-fastest: sequences that share prefix pages (a GRPO
+//    group) run side by side and the shared pages come from L2.
+//  * Staging: per page the warp's elected lane issues four 2-D TMA tensor
+//    loads (K and V, two 64-column halves each, 128-byte swizzle) into one
+//    8 KiB stage of the warp's 3-stage ring, completion tracked by a
+//    shared-memory mbarrier with transaction bytes (no multicast).
 //  * Math: the G query heads of the KV group form the rows of one
-//    m16n8k16 bf16 tensor-core tile (rows >= G are zero), so
-//    S = Q.K^T and O += P.V are each 16 mma per page; the S accumulator
-//    layout is reused directly as the A operand of P.V.  Softmax runs in
-//    registers in the log2 domain with quad shuffles for the row max.
-//  * Split-K: chunks of one (b, h) write unnormalised partials; the last CTA
-//    to arrive (per-(b,h) counter) merges them with the log-sum-exp rule and
-//    resets the counter, so no second kernel launch is needed.
+//    m16n8k16 bf16 tensor-core tile (rows >= G are zero), so S = Q.K^T and
+//    O += P.V are each 16 mma per page; the S accumulator layout is reused
+//    directly as the A operand of P.V.  Softmax runs in registers in the log2
+//    domain with quad shuffles for the row max.
+//  * Split-K: the chunks of one (b, h) write unnormalised partials; the last
+//    warp to arrive (per-(b,h) counter) merges them with the log-sum-exp rule
+//    and resets the counter, so no second kernel launch is needed.
 //
 // HBM roofline: the kernel must move sum_b L_b * Hkv * 128 * 2 * 2 bytes of
 // KV plus q/out; at ~4 flop/byte it sits far below the tensor ridge.
@@ -35,9 +37,10 @@
 
 namespace {
 
-constexpr int kWarps = 4;
-constexpr int kStages = 3;
-constexpr int kStageBytes = 8192;     // K (2 x 2 KiB halves) + V (2 x 2 KiB)
+constexpr int kWarps = 4;            // warps (independent items) per CTA
+constexpr int kStages = 3;           // pipeline depth per warp
+constexpr int kStageBytes = 8192;    // K (2 x 2 KiB halves) + V (2 x 2 KiB)
+constexpr int kMaxChunkPages = 64;   // page ids live in two registers per lane
 constexpr int kSmemBytes = kWarps * kStages * kStageBytes + 1024;  // + 1 KiB alignment slack
 constexpr uint64_t kWaitLimitNs = 2000000000ull;                    // 2 s per pipeline wait
 
@@ -52,8 +55,9 @@ struct AttnArgs {
     float *part_ml;     // [B][Hkv][max_chunks][G][2]  (max, sum) in log2 domain
     int32_t *counters;  // [B][Hkv]
     int32_t *error;
-    uint32_t num_q_heads, num_kv_heads, max_pages, max_chunks, chunk_pages, max_seq_len;
+    uint32_t num_seqs, num_q_heads, num_kv_heads, max_pages, max_chunks, chunk_pages, max_seq_len;
     uint64_t arena_pages;
+    uint64_t n_items;
     float scale_log2;
     uint32_t evict_first;
 };
@@ -69,24 +73,26 @@ paged_gqa_decode_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnAr
 {
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t bars[kWarps][kStages];
-    __shared__ int s_last;
 
-    // Grid: x = sequence (fastest), y = KV head, z = chunk.  Sequences that
-    // share prefix pages (a GRPO group) are adjacent, so their CTAs for one
-    // (head, chunk) run together and the shared pages come from L2.
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int b = blockIdx.x, h = blockIdx.y, chunk = blockIdx.z;
+    const uint64_t item = (uint64_t)blockIdx.x * kWarps + (uint64_t)warp;
+    if (item >= a.n_items)
+        return;
+    const uint32_t B = a.num_seqs, Hq = a.num_q_heads, Hkv = a.num_kv_heads;
+    const uint32_t b = (uint32_t)(item % B);
+    const uint64_t rest = item / B;
+    const uint32_t h = (uint32_t)(rest % Hkv);
+    const int chunk = (int)(rest / Hkv);
     const int L = a.seq_lens[b];
-    const uint32_t Hq = a.num_q_heads, Hkv = a.num_kv_heads;
 
     if (L < 0 || (uint32_t)L > a.max_seq_len || (uint32_t)L > a.max_pages * 16u) {
-        if (threadIdx.x == 0 && chunk == 0)
+        if (lane == 0 && chunk == 0)
             flag_error(a.error, kErrSeqLen);
         return;
     }
     if (L == 0) {
         if (chunk == 0)
-            for (int i = threadIdx.x; i < G * 128; i += kWarps * 32)
+            for (int i = lane; i < G * 128; i += 32)
                 a.out[((size_t)b * Hq + (size_t)h * G) * 128 + i] = 0.0f;
         return;
     }
@@ -95,26 +101,30 @@ paged_gqa_decode_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnAr
     const int n_chunks = (n_pages + cp - 1) / cp;
     if (chunk >= n_chunks)
         return;
+    const int p_begin = chunk * cp;
+    const int n_mine = min(n_pages, p_begin + cp) - p_begin;
 
-    // 1 KiB-aligned stage area (128-byte swizzle repeats every 1 KiB).
+    // 1 KiB-aligned stage ring of this warp (128-byte swizzle repeats every 1 KiB).
     const uint32_t raw_u32 = rt::smem_u32(smem_raw);
     const uint32_t base_u32 = (raw_u32 + 1023u) & ~1023u;
     uint8_t *base_ptr = smem_raw + (base_u32 - raw_u32);
     const uint32_t stage0 = base_u32 + (uint32_t)(warp * kStages * kStageBytes);
 
-    const int p_begin = chunk * cp;
-    const int p_end = min(n_pages, p_begin + cp);
-    const int span = p_end - p_begin;
-    const int n_mine = span > warp ? (span - warp + kWarps - 1) / kWarps : 0;
-
-    // Page ids of this warp's pages: lane i holds its i-th page (cp <= 128).
-    int my_pg = 0;
-    if (lane < n_mine) {
-        my_pg = a.page_table[(size_t)b * a.max_pages + (size_t)(p_begin + warp + lane * kWarps)];
-        if (my_pg < 0 || (uint64_t)my_pg >= a.arena_pages) {
-            flag_error(a.error, kErrPage);
-            my_pg = 0;
-        }
+    // Page ids of this item: lane i holds pages i and 32 + i.
+    const int32_t *ptab = a.page_table + (size_t)b * a.max_pages + p_begin;
+    int pg_lo = 0, pg_hi = 0;
+    if (lane < n_mine)
+        pg_lo = ptab[lane];
+    if (lane + 32 < n_mine)
+        pg_hi = ptab[lane + 32];
+    const bool bad = (lane < n_mine && (pg_lo < 0 || (uint64_t)pg_lo >= a.arena_pages)) ||
+                     (lane + 32 < n_mine && (pg_hi < 0 || (uint64_t)pg_hi >= a.arena_pages));
+    if (bad) {
+        flag_error(a.error, kErrPage);
+        if (pg_lo < 0 || (uint64_t)pg_lo >= a.arena_pages)
+            pg_lo = 0;
+        if (pg_hi < 0 || (uint64_t)pg_hi >= a.arena_pages)
+            pg_hi = 0;
     }
 
     if (lane == 0) {
@@ -128,7 +138,7 @@ paged_gqa_decode_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnAr
 
     const uint64_t policy = a.evict_first ? rt::l2_policy_evict_first() : rt::l2_policy_evict_normal();
     auto issue = [&](int i, int s) {
-        const int pg = __shfl_sync(0xffffffffu, my_pg, i);
+        const int pg = __shfl_sync(0xffffffffu, i < 32 ? pg_lo : pg_hi, i & 31);
         if (lane == 0) {
             const uint32_t bar = rt::smem_u32(&bars[warp][s]);
             const uint32_t dst = stage0 + (uint32_t)(s * kStageBytes);
@@ -140,6 +150,8 @@ paged_gqa_decode_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnAr
             rt::tma_load_2d(dst + 6144u, &kv_map, 64, row_k + 16, bar, policy);
         }
     };
+    for (int i = 0; i < n_mine && i < kStages; i++)
+        issue(i, i);
 
     // Q fragment: row r = lane/4 is query head h*G + r (rows >= G are zero);
     // k-step j covers dims 16j..16j+15.
@@ -168,9 +180,6 @@ paged_gqa_decode_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnAr
     const uint32_t k_row = (uint32_t)((((mi >> 1) << 3) + rr) * 128);
     const uint32_t v_row = (uint32_t)((((mi & 1) << 3) + rr) * 128);
 
-    for (int i = 0; i < n_mine && i < kStages; i++)
-        issue(i, i);
-
     uint32_t phases = 0;
     bool failed = false;
     for (int i = 0; i < n_mine; i++) {
@@ -183,8 +192,7 @@ paged_gqa_decode_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnAr
         }
         phases ^= 1u << s;
         const uint32_t st = stage0 + (uint32_t)(s * kStageBytes);
-        const int page = p_begin + warp + i * kWarps;
-        const int valid = min(16, L - page * 16);
+        const int valid = min(16, L - (p_begin + i) * 16);
         if (valid < 16) {
             // Tail page: zero the V rows past the sequence end so that
             // P = 0 never meets non-finite stale data.
@@ -255,92 +263,68 @@ paged_gqa_decode_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnAr
         if (lane == 0)
             flag_error(a.error, kErrTimeout);
         // Give copies still in flight a bounded chance to land before the
-        // shared memory is reused.
+        // warp (and then the CTA) releases its shared memory.
         for (int s = 0; s < kStages; s++)
             (void)rt::mbar_wait_bounded(rt::smem_u32(&bars[warp][s]), (phases >> s) & 1u,
                                         kWaitLimitNs / 4);
-        m_run = -INFINITY;
-        l_run = 0.0f;
-#pragma unroll
-        for (int n = 0; n < 16; n++)
-            o[n][0] = o[n][1] = 0.0f;
+        return;
     }
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
 
-    // ---- merge the warps of this CTA (stage memory is free now) ----
-    __syncthreads();
-    float *co = reinterpret_cast<float *>(base_ptr);  // [kWarps][G][128]
-    float *cm = co + kWarps * G * 128;                // [kWarps][G]
-    float *cl = cm + kWarps * G;
-    if (r < G) {
-        if (q4 == 0) {
-            cm[warp * G + r] = m_run;
-            cl[warp * G + r] = l_run;
-        }
-#pragma unroll
-        for (int n = 0; n < 16; n++) {
-            float *dst = co + (warp * G + r) * 128 + n * 8 + 2 * q4;
-            dst[0] = o[n][0];
-            dst[1] = o[n][1];
-        }
-    }
-    __syncthreads();
-
     const size_t bh = (size_t)b * Hkv + h;
-    for (int idx = threadIdx.x; idx < G * 128; idx += kWarps * 32) {
-        const int row = idx >> 7, d = idx & 127;
-        float M = -INFINITY;
+    if (n_chunks == 1) {
+        if (r < G) {
+            const float inv = 1.0f / l_run;
+            float *dst = a.out + ((size_t)b * Hq + (size_t)h * G + r) * 128 + 2 * q4;
 #pragma unroll
-        for (int w = 0; w < kWarps; w++)
-            M = fmaxf(M, cm[w * G + row]);
-        float Ls = 0.0f, O = 0.0f;
-#pragma unroll
-        for (int w = 0; w < kWarps; w++) {
-            const float wt = rt::fast_exp2(cm[w * G + row] - M);
-            Ls += cl[w * G + row] * wt;
-            O += co[(w * G + row) * 128 + d] * wt;
+            for (int n = 0; n < 16; n++)
+                *reinterpret_cast<float2 *>(dst + n * 8) = make_float2(o[n][0] * inv, o[n][1] * inv);
         }
-        if (n_chunks == 1) {
-            a.out[((size_t)b * Hq + (size_t)h * G + row) * 128 + d] = O / Ls;
-        } else {
-            const size_t pi = (bh * a.max_chunks + chunk) * G + row;
-            a.part_o[pi * 128 + d] = O;
-            if (d == 0) {
-                a.part_ml[pi * 2] = M;
-                a.part_ml[pi * 2 + 1] = Ls;
-            }
-        }
-    }
-    if (n_chunks == 1)
         return;
+    }
 
-    // ---- split-K: the last chunk CTA of (b, h) merges all partials ----
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        const int prev = atomicAdd(&a.counters[bh], 1);
-        s_last = (prev == n_chunks - 1);
+    // ---- split-K: write this chunk's partial; the last warp merges ----
+    if (r < G) {
+        const size_t pi = (bh * a.max_chunks + chunk) * G + r;
+        float *dst = a.part_o + pi * 128 + 2 * q4;
+#pragma unroll
+        for (int n = 0; n < 16; n++)
+            *reinterpret_cast<float2 *>(dst + n * 8) = make_float2(o[n][0], o[n][1]);
+        if (q4 == 0)
+            *reinterpret_cast<float2 *>(a.part_ml + pi * 2) = make_float2(m_run, l_run);
     }
-    __syncthreads();
-    if (!s_last)
+    __threadfence();
+    __syncwarp();
+    int prev = 0;
+    if (lane == 0)
+        prev = atomicAdd(&a.counters[bh], 1);
+    prev = __shfl_sync(0xffffffffu, prev, 0);
+    if (prev != n_chunks - 1)
         return;
     __threadfence();
-    for (int idx = threadIdx.x; idx < G * 128; idx += kWarps * 32) {
-        const int row = idx >> 7, d = idx & 127;
+    for (int row = 0; row < G; row++) {
         float M = -INFINITY;
         for (int c = 0; c < n_chunks; c++)
             M = fmaxf(M, __ldcg(&a.part_ml[((bh * a.max_chunks + c) * G + row) * 2]));
-        float Ls = 0.0f, O = 0.0f;
+        float Ls = 0.0f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int c = 0; c < n_chunks; c++) {
             const size_t pi = (bh * a.max_chunks + c) * G + row;
-            const float wt = rt::fast_exp2(__ldcg(&a.part_ml[pi * 2]) - M);
-            Ls += __ldcg(&a.part_ml[pi * 2 + 1]) * wt;
-            O += __ldcg(&a.part_o[pi * 128 + d]) * wt;
+            const float2 ml = __ldcg(reinterpret_cast<const float2 *>(&a.part_ml[pi * 2]));
+            const float wt = rt::fast_exp2(ml.x - M);
+            Ls += ml.y * wt;
+            const float4 v = __ldcg(reinterpret_cast<const float4 *>(&a.part_o[pi * 128 + lane * 4]));
+            acc.x += v.x * wt;
+            acc.y += v.y * wt;
+            acc.z += v.z * wt;
+            acc.w += v.w * wt;
         }
-        a.out[((size_t)b * Hq + (size_t)h * G + row) * 128 + d] = O / Ls;
+        const float inv = 1.0f / Ls;
+        *reinterpret_cast<float4 *>(a.out + ((size_t)b * Hq + (size_t)h * G + row) * 128 + lane * 4) =
+            make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
     }
-    if (threadIdx.x == 0)
+    if (lane == 0)
         a.counters[bh] = 0;
 }
 
@@ -383,14 +367,16 @@ int make_plan(const rt_attn_params_t *p, Plan *pl)
     const uint32_t pages_max = (p->max_seq_len + 15u) / 16u;
     uint32_t cp = p->chunk_pages;
     if (cp == 0) {
-        cp = 32;
-        const uint64_t slots = (uint64_t)rt::num_sms() * 2u;
-        while (cp > 8 && (uint64_t)p->num_seqs * p->num_kv_heads * ((pages_max + cp - 1) / cp) <
-                             4u * slots)
+        // 16 pages (256 tokens) per warp item; smaller when there are too few
+        // items to give every warp slot of the GPU several of them.
+        cp = 16;
+        const uint64_t warp_slots = (uint64_t)rt::num_sms() * 2u * kWarps;
+        while (cp > 4 && (uint64_t)p->num_seqs * p->num_kv_heads * ((pages_max + cp - 1) / cp) <
+                             2u * warp_slots)
             cp /= 2;
     }
-    if (cp < 1 || cp > 128) {
-        rt::set_error("attention: chunk_pages %u outside 1..128", cp);
+    if (cp < 1 || cp > (uint32_t)kMaxChunkPages) {
+        rt::set_error("attention: chunk_pages %u outside 1..%d", cp, kMaxChunkPages);
         return RT_EINVAL;
     }
     pl->group = g;
@@ -512,7 +498,8 @@ extern "C" int rt_attn_plan(const rt_attn_params_t *p, uint32_t *chunk_pages, ui
         return rc;
     if (chunk_pages) *chunk_pages = pl.chunk_pages;
     if (max_chunks) *max_chunks = pl.max_chunks;
-    if (ctas) *ctas = (uint64_t)pl.max_chunks * p->num_kv_heads * p->num_seqs;
+    if (ctas)
+        *ctas = ((uint64_t)pl.max_chunks * p->num_kv_heads * p->num_seqs + kWarps - 1) / kWarps;
     return RT_OK;
 }
 
@@ -568,11 +555,14 @@ extern "C" int rt_paged_decode_attention(const rt_attn_params_t *p, const void *
     args.arena_pages = p->arena_pages;
     args.scale_log2 = p->scale * 1.4426950408889634f;
     args.evict_first = p->kv_evict_first ? 1u : 0u;
-    if (pl.max_chunks > 65535u) {
-        rt::set_error("attention: %u chunks exceed the grid's z limit", pl.max_chunks);
+    args.num_seqs = p->num_seqs;
+    args.n_items = (uint64_t)p->num_seqs * p->num_kv_heads * pl.max_chunks;
+    const uint64_t ctas = (args.n_items + kWarps - 1) / kWarps;
+    if (ctas > 0x7FFFFFFFull) {
+        rt::set_error("attention: %llu CTAs exceed the grid limit", (unsigned long long)ctas);
         return RT_EINVAL;
     }
-    const dim3 grid(p->num_seqs, p->num_kv_heads, pl.max_chunks);
+    const dim3 grid((unsigned)ctas);
     cudaStream_t s = (cudaStream_t)stream;
     switch (pl.group) {
     case 1: return launch_g<1>(map, args, grid, s);

@@ -61,7 +61,7 @@ def test_group_sizes(pkg, orc, cuda, G):
     check(orc, *case[:4], Hq, Hkv, got)
 
 
-@pytest.mark.parametrize("chunk_pages", [1, 2, 3, 8, 32, 128])
+@pytest.mark.parametrize("chunk_pages", [1, 2, 3, 8, 32, 64])
 def test_chunk_sizes_agree(pkg, orc, cuda, chunk_pages):
     lens = [16 * 128, 16 * 37 + 5, 33, 2049]
     case = make_case(pkg, cuda, lens, 32, 8, seed=11)
