@@ -590,3 +590,72 @@ extern "C" int rt_attn_workspace_error(void *workspace, void *stream, int32_t *c
     *code = v;
     return RT_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant.  Some callers cannot create device memory at the
+// point where they run decode attention: code that follows a no-allocation
+// hot-path rule (the reference's own HotpathGuard counts every allocation
+// made after activation as a violation), hosts whose device memory is owned
+// by another allocator that must not be bypassed, and loops where a
+// cudaMalloc/cudaFree would synchronise the device.  For them the split-K
+// scratch is a fixed array in the library's own device memory instead of a
+// caller-provided workspace.
+namespace {
+
+constexpr size_t kStaticScratchBytes = (size_t)32 << 20;  // 32 MiB per device
+__device__ __align__(256) uint8_t g_attn_static_scratch[kStaticScratchBytes];
+
+// Device address of g_attn_static_scratch, resolved once per device.
+int static_scratch_ptr(void **out)
+{
+    static std::mutex mu;
+    static void *ptrs[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess)
+        return rt::cuda_fail(e, "attention_noalloc: cudaGetDevice");
+    if (dev < 0 || dev >= 64) {
+        rt::set_error("attention_noalloc: device index %d out of range", dev);
+        return RT_EINVAL;
+    }
+    std::lock_guard<std::mutex> lk(mu);
+    if (!ptrs[dev]) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_attn_static_scratch);
+        if (e != cudaSuccess)
+            return rt::cuda_fail(e, "attention_noalloc: cudaGetSymbolAddress");
+        ptrs[dev] = p;
+    }
+    *out = ptrs[dev];
+    return RT_OK;
+}
+
+}  // namespace
+
+extern "C" int rt_paged_decode_attention_noalloc(const rt_attn_params_t *p, const void *q,
+                                                 const void *kv_arena, const int32_t *page_table,
+                                                 const int32_t *seq_lens, float *out,
+                                                 void *stream)
+{
+    Plan pl;
+    int rc = make_plan(p, &pl);
+    if (rc != RT_OK)
+        return rc;
+    if (pl.total > kStaticScratchBytes) {
+        rt::set_error("attention_noalloc: these shapes need %zu B of scratch, the built-in "
+                      "array holds %zu B; use rt_paged_decode_attention with a workspace",
+                      pl.total, kStaticScratchBytes);
+        return RT_ENOMEM;
+    }
+    void *scratch = nullptr;
+    rc = static_scratch_ptr(&scratch);
+    if (rc != RT_OK)
+        return rc;
+    // The error word and the split-K arrival counters must start at zero;
+    // the array keeps whatever the previous call left in it.
+    cudaError_t e = cudaMemsetAsync(scratch, 0, pl.off_ml, (cudaStream_t)stream);
+    if (e != cudaSuccess)
+        return rt::cuda_fail(e, "attention_noalloc: clear counters");
+    return rt_paged_decode_attention(p, q, kv_arena, page_table, seq_lens, out, scratch,
+                                     kStaticScratchBytes, stream);
+}

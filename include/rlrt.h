@@ -78,6 +78,27 @@ int rt_paged_decode_attention(const rt_attn_params_t *p,
                               float *out, void *workspace, size_t workspace_bytes,
                               void *stream);
 
+/* Same computation as rt_paged_decode_attention, for callers that cannot
+ * allocate device memory where they run it: code under a no-allocation
+ * hot-path rule (the reference's HotpathGuard treats any allocation after
+ * activation as a violation), hosts whose device memory belongs to an
+ * allocator that must not be bypassed, and loops where cudaMalloc/cudaFree
+ * would synchronise the device.  No counterpart in the reference.
+ *
+ * The split-K scratch is a 32 MiB array in the library's own device memory
+ * (every GPU that loads the library holds it until exit); shapes needing
+ * more (rt_attn_workspace_bytes > 32 MiB) are rejected with RT_ENOMEM.  It
+ * calls no allocator.  The first call on a device looks up the array's
+ * address with that device current; make that first call before any stream
+ * capture.  All calls share the one array and each call clears its counters,
+ * so calls that overlap on the GPU (any streams) race and must be
+ * serialised by the caller.  Index errors are still caught on the device but
+ * are not reported by this variant. */
+int rt_paged_decode_attention_noalloc(const rt_attn_params_t *p,
+                                      const void *q, const void *kv_arena,
+                                      const int32_t *page_table, const int32_t *seq_lens,
+                                      float *out, void *stream);
+
 /* Read back (and clear) the device error word of a workspace.  0 = no
  * error; otherwise RT_EDEVICE-class codes: 1 = seq_len above
  * max_seq_len / page capacity, 2 = page index outside the arena,
