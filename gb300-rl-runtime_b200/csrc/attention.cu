@@ -67,17 +67,15 @@ __device__ __forceinline__ void flag_error(int32_t *err, int32_t code)
     atomicCAS(err, 0, code);
 }
 
+// One warp processes one item; see the file comment.  Returns false when a
+// pipeline wait expired (the warp then stops taking items).
 template <int G>
-__global__ void __launch_bounds__(kWarps * 32, 2)
-paged_gqa_decode_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnArgs a)
+__device__ __forceinline__ bool process_item(const CUtensorMap &kv_map, const AttnArgs &a,
+                                             uint64_t item, uint32_t stage0, uint8_t *base_ptr,
+                                             uint32_t base_u32, uint64_t (&bars)[kStages],
+                                             uint32_t &phases, uint64_t policy)
 {
-    extern __shared__ uint8_t smem_raw[];
-    __shared__ __align__(8) uint64_t bars[kWarps][kStages];
-
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint64_t item = (uint64_t)blockIdx.x * kWarps + (uint64_t)warp;
-    if (item >= a.n_items)
-        return;
+    const int lane = threadIdx.x & 31;
     const uint32_t B = a.num_seqs, Hq = a.num_q_heads, Hkv = a.num_kv_heads;
     const uint32_t b = (uint32_t)(item % B);
     const uint64_t rest = item / B;
@@ -88,27 +86,21 @@ paged_gqa_decode_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnAr
     if (L < 0 || (uint32_t)L > a.max_seq_len || (uint32_t)L > a.max_pages * 16u) {
         if (lane == 0 && chunk == 0)
             flag_error(a.error, kErrSeqLen);
-        return;
+        return true;
     }
     if (L == 0) {
         if (chunk == 0)
             for (int i = lane; i < G * 128; i += 32)
                 a.out[((size_t)b * Hq + (size_t)h * G) * 128 + i] = 0.0f;
-        return;
+        return true;
     }
     const int n_pages = (L + 15) >> 4;
     const int cp = (int)a.chunk_pages;
     const int n_chunks = (n_pages + cp - 1) / cp;
     if (chunk >= n_chunks)
-        return;
+        return true;
     const int p_begin = chunk * cp;
     const int n_mine = min(n_pages, p_begin + cp) - p_begin;
-
-    // 1 KiB-aligned stage ring of this warp (128-byte swizzle repeats every 1 KiB).
-    const uint32_t raw_u32 = rt::smem_u32(smem_raw);
-    const uint32_t base_u32 = (raw_u32 + 1023u) & ~1023u;
-    uint8_t *base_ptr = smem_raw + (base_u32 - raw_u32);
-    const uint32_t stage0 = base_u32 + (uint32_t)(warp * kStages * kStageBytes);
 
     // Page ids of this item: lane i holds pages i and 32 + i.
     const int32_t *ptab = a.page_table + (size_t)b * a.max_pages + p_begin;
@@ -127,20 +119,10 @@ paged_gqa_decode_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnAr
             pg_hi = 0;
     }
 
-    if (lane == 0) {
-        rt::prefetch_tensormap(&kv_map);
-        for (int s = 0; s < kStages; s++)
-            rt::mbar_init(rt::smem_u32(&bars[warp][s]), 1u);
-        rt::mbar_fence_init();
-        rt::fence_proxy_async_smem();
-    }
-    __syncwarp();
-
-    const uint64_t policy = a.evict_first ? rt::l2_policy_evict_first() : rt::l2_policy_evict_normal();
     auto issue = [&](int i, int s) {
         const int pg = __shfl_sync(0xffffffffu, i < 32 ? pg_lo : pg_hi, i & 31);
         if (lane == 0) {
-            const uint32_t bar = rt::smem_u32(&bars[warp][s]);
+            const uint32_t bar = rt::smem_u32(&bars[s]);
             const uint32_t dst = stage0 + (uint32_t)(s * kStageBytes);
             const int32_t row_k = (int32_t)(((int64_t)pg * Hkv + h) * 32);
             rt::mbar_arrive_expect_tx(bar, (uint32_t)kStageBytes);
@@ -150,6 +132,9 @@ paged_gqa_decode_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnAr
             rt::tma_load_2d(dst + 6144u, &kv_map, 64, row_k + 16, bar, policy);
         }
     };
+    // The stage ring was left idle by the previous item: order this warp's
+    // earlier generic accesses of it before the new TMA writes.
+    rt::fence_proxy_async_smem();
     for (int i = 0; i < n_mine && i < kStages; i++)
         issue(i, i);
 
@@ -180,15 +165,19 @@ paged_gqa_decode_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnAr
     const uint32_t k_row = (uint32_t)((((mi >> 1) << 3) + rr) * 128);
     const uint32_t v_row = (uint32_t)((((mi & 1) << 3) + rr) * 128);
 
-    uint32_t phases = 0;
-    bool failed = false;
     for (int i = 0; i < n_mine; i++) {
         const int s = i % kStages;
-        const bool ok = rt::mbar_wait_bounded(rt::smem_u32(&bars[warp][s]), (phases >> s) & 1u,
+        const bool ok = rt::mbar_wait_bounded(rt::smem_u32(&bars[s]), (phases >> s) & 1u,
                                               kWaitLimitNs);
         if (!__all_sync(0xffffffffu, ok)) {
-            failed = true;
-            break;
+            if (lane == 0)
+                flag_error(a.error, kErrTimeout);
+            // Give copies still in flight a bounded chance to land before the
+            // shared memory is released.
+            for (int s2 = 0; s2 < kStages; s2++)
+                (void)rt::mbar_wait_bounded(rt::smem_u32(&bars[s2]), (phases >> s2) & 1u,
+                                            kWaitLimitNs / 4);
+            return false;
         }
         phases ^= 1u << s;
         const uint32_t st = stage0 + (uint32_t)(s * kStageBytes);
@@ -259,16 +248,6 @@ paged_gqa_decode_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnAr
             issue(i + kStages, s);
         }
     }
-    if (failed) {
-        if (lane == 0)
-            flag_error(a.error, kErrTimeout);
-        // Give copies still in flight a bounded chance to land before the
-        // warp (and then the CTA) releases its shared memory.
-        for (int s = 0; s < kStages; s++)
-            (void)rt::mbar_wait_bounded(rt::smem_u32(&bars[warp][s]), (phases >> s) & 1u,
-                                        kWaitLimitNs / 4);
-        return;
-    }
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
 
@@ -281,7 +260,7 @@ paged_gqa_decode_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnAr
             for (int n = 0; n < 16; n++)
                 *reinterpret_cast<float2 *>(dst + n * 8) = make_float2(o[n][0] * inv, o[n][1] * inv);
         }
-        return;
+        return true;
     }
 
     // ---- split-K: write this chunk's partial; the last warp merges ----
@@ -301,7 +280,7 @@ paged_gqa_decode_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnAr
         prev = atomicAdd(&a.counters[bh], 1);
     prev = __shfl_sync(0xffffffffu, prev, 0);
     if (prev != n_chunks - 1)
-        return;
+        return true;
     __threadfence();
     for (int row = 0; row < G; row++) {
         float M = -INFINITY;
@@ -326,6 +305,42 @@ paged_gqa_decode_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnAr
     }
     if (lane == 0)
         a.counters[bh] = 0;
+    return true;
+}
+
+// Persistent warps: warp w of the grid takes items w, w + W, w + 2W, ...
+// (W = all warps of the grid), so a warp whose item is empty moves on at once
+// and the items of a GRPO group's sequences run side by side.
+template <int G>
+__global__ void __launch_bounds__(kWarps * 32, 2)
+paged_gqa_decode_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnArgs a)
+{
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t bars[kWarps][kStages];
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // 1 KiB-aligned stage ring of this warp (128-byte swizzle repeats every 1 KiB).
+    const uint32_t raw_u32 = rt::smem_u32(smem_raw);
+    const uint32_t base_u32 = (raw_u32 + 1023u) & ~1023u;
+    uint8_t *base_ptr = smem_raw + (base_u32 - raw_u32);
+    const uint32_t stage0 = base_u32 + (uint32_t)(warp * kStages * kStageBytes);
+
+    if (lane == 0) {
+        rt::prefetch_tensormap(&kv_map);
+        for (int s = 0; s < kStages; s++)
+            rt::mbar_init(rt::smem_u32(&bars[warp][s]), 1u);
+        rt::mbar_fence_init();
+        rt::fence_proxy_async_smem();
+    }
+    __syncwarp();
+    const uint64_t policy = a.evict_first ? rt::l2_policy_evict_first() : rt::l2_policy_evict_normal();
+    uint32_t phases = 0;
+    const uint64_t stride = (uint64_t)gridDim.x * kWarps;
+    for (uint64_t item = (uint64_t)blockIdx.x * kWarps + (uint64_t)warp; item < a.n_items;
+         item += stride) {
+        if (!process_item<G>(kv_map, a, item, stage0, base_ptr, base_u32, bars[warp], phases, policy))
+            break;
+    }
 }
 
 // ------------------------------------------------------------------ host
@@ -498,8 +513,11 @@ extern "C" int rt_attn_plan(const rt_attn_params_t *p, uint32_t *chunk_pages, ui
         return rc;
     if (chunk_pages) *chunk_pages = pl.chunk_pages;
     if (max_chunks) *max_chunks = pl.max_chunks;
-    if (ctas)
-        *ctas = ((uint64_t)pl.max_chunks * p->num_kv_heads * p->num_seqs + kWarps - 1) / kWarps;
+    if (ctas) {
+        const uint64_t need = ((uint64_t)pl.max_chunks * p->num_kv_heads * p->num_seqs + kWarps - 1) / kWarps;
+        const uint64_t resident = (uint64_t)rt::num_sms() * 2u;
+        *ctas = need < resident ? need : resident;
+    }
     return RT_OK;
 }
 
@@ -557,11 +575,12 @@ extern "C" int rt_paged_decode_attention(const rt_attn_params_t *p, const void *
     args.evict_first = p->kv_evict_first ? 1u : 0u;
     args.num_seqs = p->num_seqs;
     args.n_items = (uint64_t)p->num_seqs * p->num_kv_heads * pl.max_chunks;
-    const uint64_t ctas = (args.n_items + kWarps - 1) / kWarps;
-    if (ctas > 0x7FFFFFFFull) {
-        rt::set_error("attention: %llu CTAs exceed the grid limit", (unsigned long long)ctas);
-        return RT_EINVAL;
-    }
+    // Persistent grid: two CTAs per SM (the shared-memory limit), never
+    // more CTAs than there are items to hand out.
+    uint64_t ctas = (args.n_items + kWarps - 1) / kWarps;
+    const uint64_t resident = (uint64_t)rt::num_sms() * 2u;
+    if (ctas > resident)
+        ctas = resident;
     const dim3 grid((unsigned)ctas);
     cudaStream_t s = (cudaStream_t)stream;
     switch (pl.group) {

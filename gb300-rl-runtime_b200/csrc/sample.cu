@@ -142,15 +142,17 @@ __device__ __forceinline__ uint32_t block_inclusive_scan(uint32_t v, Smem &s, ui
 // One radix digit: histogram the keys of candidates that match `prefix` on
 // `mask`, then find the digit d holding the need-th largest key.  Updates
 // prefix/mask/need for the next digit.
-__device__ __forceinline__ void radix_pass(const float (&x)[kItems], int shift, int bits, uint32_t &prefix, uint32_t &mask,
-                                           uint32_t &need, Smem &s)
+template <int N>
+__device__ __forceinline__ void radix_pass(const float (&x)[N], int shift, int bits,
+                                           uint32_t &prefix, uint32_t &mask, uint32_t &need,
+                                           Smem &s)
 {
     const int nb = 1 << bits;
     for (int b = threadIdx.x; b < nb; b += kThreads)
         s.u.hist[b] = 0u;
     __syncthreads();
 #pragma unroll
-    for (int i = 0; i < kItems; i++) {
+    for (int i = 0; i < N; i++) {
         if (x[i] > -FLT_MAX) {  // entries past the vocabulary hold -inf
             const uint32_t k = float_key(x[i]);
             if ((k & mask) == prefix)
@@ -239,30 +241,95 @@ __global__ void __launch_bounds__(kThreads, 1) sample_rows_kernel(const SampleAr
     const bool topk = P.top_k > 0u && P.top_k < V;
     const uint32_t nk = P.top_k < 256u ? P.top_k : 256u;
 
-    // ---- 2. top-k cutoff ----
+    // ---- 2. top-k cutoff and survivors ----
+    // A value survives iff it is >= the nk-th largest value (counted with
+    // multiplicity) among values > -FLT_MAX, i.e. iff fewer than nk values
+    // are strictly greater than it.
     float cutoff = -FLT_MAX;
     bool fast = topk;
+    uint32_t ns = 0;
+    bool sorted_ready = false;
     if (topk) {
         uint32_t ncand = 0;
 #pragma unroll
         for (int i = 0; i < kItems; i++)
             ncand += x[i] > -FLT_MAX ? 1u : 0u;
         ncand = block_sum_u32(ncand, s);
-        if (ncand >= nk) {
+        if (ncand < nk)
+            fast = false;  // cutoff stays -FLT_MAX; almost everything survives
+    }
+    if (fast) {
+        // Quick path: tau0 = the nk-th largest of the 1024 per-thread maxima.
+        // Those maxima are nk distinct entries >= tau0, so tau0 <= cutoff and
+        // every survivor is among the few entries >= tau0.
+        float tm[1] = {-INFINITY};
+#pragma unroll
+        for (int i = 0; i < kItems; i++)
+            if (x[i] > -FLT_MAX)
+                tm[0] = fmaxf(tm[0], x[i]);
+        const uint32_t nvalid = (uint32_t)__syncthreads_count(tm[0] > -FLT_MAX);
+        if (nvalid >= nk) {
+            uint32_t prefix = 0, mask = 0, need = nk;
+            radix_pass(tm, 20, 12, prefix, mask, need, s);
+            radix_pass(tm, 8, 12, prefix, mask, need, s);
+            radix_pass(tm, 0, 8, prefix, mask, need, s);
+            const float tau0 = key_float(prefix);
+            if (tid == 0)
+                s.count = 0u;
+            __syncthreads();
+#pragma unroll
+            for (int i = 0; i < kItems; i++) {
+                if (x[i] >= tau0 && x[i] > -FLT_MAX) {
+                    const uint32_t pos = atomicAdd(&s.count, 1u);
+                    if (pos < (uint32_t)kCap) {
+                        s.surv_idx[pos] = (uint32_t)tid + (uint32_t)i * kThreads;
+                        s.surv_val[pos] = x[i];
+                    }
+                }
+            }
+            __syncthreads();
+            const uint32_t nc = s.count;
+            if (nc <= (uint32_t)kCap) {
+                uint32_t *keep = reinterpret_cast<uint32_t *>(s.e);  // reused before the walk
+                uint32_t mine = 0;
+                for (uint32_t j = tid; j < nc; j += kThreads) {
+                    const float v = s.surv_val[j];
+                    uint32_t gt = 0;
+                    for (uint32_t i2 = 0; i2 < nc; i2++)
+                        gt += s.surv_val[i2] > v ? 1u : 0u;
+                    keep[j] = gt < nk ? 1u : 0u;
+                    mine += keep[j];
+                }
+                ns = block_sum_u32(mine, s);  // includes a barrier: keep[] is complete
+                for (uint32_t j = tid; j < nc; j += kThreads) {
+                    if (!keep[j])
+                        continue;
+                    const uint32_t id = s.surv_idx[j];
+                    uint32_t rank = 0;
+                    for (uint32_t i2 = 0; i2 < nc; i2++)
+                        rank += (keep[i2] && s.surv_idx[i2] < id) ? 1u : 0u;
+                    s.u.sorted.idx[rank] = id;
+                    s.u.sorted.val[rank] = s.surv_val[j];
+                }
+                sorted_ready = true;
+            }
+        }
+        if (!sorted_ready) {
+            // Tie-heavy or degenerate rows: exact cutoff by a full-row radix select.
             uint32_t prefix = 0, mask = 0, need = nk;
             radix_pass(x, 20, 12, prefix, mask, need, s);
             radix_pass(x, 8, 12, prefix, mask, need, s);
             radix_pass(x, 0, 8, prefix, mask, need, s);
             cutoff = key_float(prefix);
-        } else {
-            fast = false;  // cutoff stays -FLT_MAX; almost everything survives
         }
     }
 
     // ---- 3. survivors, sorted by index ----
     float mx = -FLT_MAX;
-    uint32_t ns = 0;
-    if (fast) {
+    if (fast && !sorted_ready) {
+        if (tid == 0)
+            s.count = 0u;
+        __syncthreads();
 #pragma unroll
         for (int i = 0; i < kItems; i++) {
             if (x[i] >= cutoff) {
@@ -277,18 +344,22 @@ __global__ void __launch_bounds__(kThreads, 1) sample_rows_kernel(const SampleAr
         ns = s.count;
         if (ns > (uint32_t)kCap)
             fast = false;
+        if (fast) {
+            for (uint32_t j = tid; j < ns; j += kThreads) {
+                const uint32_t id = s.surv_idx[j];
+                uint32_t rank = 0;
+                for (uint32_t q = 0; q < ns; q++)
+                    rank += s.surv_idx[q] < id ? 1u : 0u;
+                s.u.sorted.idx[rank] = id;
+                s.u.sorted.val[rank] = s.surv_val[j];
+            }
+        }
     }
     if (fast) {
+        __syncthreads();  // sorted survivors complete
         float m = -FLT_MAX;
-        for (uint32_t j = tid; j < ns; j += kThreads) {
-            const uint32_t id = s.surv_idx[j];
-            uint32_t rank = 0;
-            for (uint32_t q = 0; q < ns; q++)
-                rank += s.surv_idx[q] < id ? 1u : 0u;
-            s.u.sorted.idx[rank] = id;
-            s.u.sorted.val[rank] = s.surv_val[j];
-            m = fmaxf(m, s.surv_val[j]);
-        }
+        for (uint32_t j = tid; j < ns; j += kThreads)
+            m = fmaxf(m, s.u.sorted.val[j]);
         mx = block_max_f32(m, s);
         // masked entries hold -FLT_MAX; their terms must be exactly zero
         if (__expf(__fsub_rn(-FLT_MAX, mx)) != 0.0f)
