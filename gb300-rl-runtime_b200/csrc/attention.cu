@@ -55,6 +55,8 @@ struct AttnArgs {
     float *part_ml;     // [B][Hkv][max_chunks][G][2]  (max, sum) in log2 domain
     int32_t *counters;  // [B][Hkv]
     int32_t *error;
+    unsigned long long *work_next;  // item dispenser (dynamic scheduling)
+    unsigned int *work_done;        // warps that left the loop
     uint32_t num_seqs, num_q_heads, num_kv_heads, max_pages, max_chunks, chunk_pages, max_seq_len;
     uint64_t arena_pages;
     uint64_t n_items;
@@ -244,7 +246,11 @@ __device__ __forceinline__ bool process_item(const CUtensorMap &kv_map, const At
         }
         __syncwarp();
         if (i + kStages < n_mine) {
-            rt::fence_proxy_async_smem();
+            // The stage's shared memory was only read (ldmatrix, consumed by
+            // the mma above) unless this was a tail page whose V rows were
+            // zeroed: only generic writes need ordering before the TMA write.
+            if (valid < 16)
+                rt::fence_proxy_async_smem();
             issue(i + kStages, s);
         }
     }
@@ -308,9 +314,11 @@ __device__ __forceinline__ bool process_item(const CUtensorMap &kv_map, const At
     return true;
 }
 
-// Persistent warps: warp w of the grid takes items w, w + W, w + 2W, ...
-// (W = all warps of the grid), so a warp whose item is empty moves on at once
-// and the items of a GRPO group's sequences run side by side.
+// Persistent warps take items in increasing order from a global dispenser
+// (one atomic per item, fetched one item ahead), so a warp whose item is
+// empty moves on at once, long and short items balance dynamically, and the
+// items of a GRPO group's sequences run side by side.  The last warp to
+// leave resets the dispenser for the next launch.
 template <int G>
 __global__ void __launch_bounds__(kWarps * 32, 2)
 paged_gqa_decode_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnArgs a)
@@ -335,11 +343,25 @@ paged_gqa_decode_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnAr
     __syncwarp();
     const uint64_t policy = a.evict_first ? rt::l2_policy_evict_first() : rt::l2_policy_evict_normal();
     uint32_t phases = 0;
-    const uint64_t stride = (uint64_t)gridDim.x * kWarps;
-    for (uint64_t item = (uint64_t)blockIdx.x * kWarps + (uint64_t)warp; item < a.n_items;
-         item += stride) {
+    unsigned long long grab = 0;
+    if (lane == 0)
+        grab = atomicAdd(a.work_next, 1ull);
+    uint64_t item = __shfl_sync(0xffffffffu, grab, 0);
+    while (item < a.n_items) {
+        if (lane == 0)
+            grab = atomicAdd(a.work_next, 1ull);  // next item, in flight meanwhile
         if (!process_item<G>(kv_map, a, item, stage0, base_ptr, base_u32, bars[warp], phases, policy))
             break;
+        item = __shfl_sync(0xffffffffu, grab, 0);
+    }
+    if (lane == 0) {
+        __threadfence();
+        const unsigned int total = gridDim.x * kWarps;
+        if (atomicAdd(a.work_done, 1u) == total - 1u) {
+            *a.work_next = 0ull;
+            *a.work_done = 0u;
+            __threadfence();
+        }
     }
 }
 
@@ -382,9 +404,10 @@ int make_plan(const rt_attn_params_t *p, Plan *pl)
     const uint32_t pages_max = (p->max_seq_len + 15u) / 16u;
     uint32_t cp = p->chunk_pages;
     if (cp == 0) {
-        // 16 pages (256 tokens) per warp item; smaller when there are too few
-        // items to give every warp slot of the GPU several of them.
-        cp = 16;
+        // 48 pages (768 tokens) per warp item (measured best on B200 for both
+        // the ragged config-2 batch and the rollout loop); smaller when there
+        // are too few items to give every warp slot of the GPU several.
+        cp = 48;
         const uint64_t warp_slots = (uint64_t)rt::num_sms() * 2u * kWarps;
         while (cp > 4 && (uint64_t)p->num_seqs * p->num_kv_heads * ((pages_max + cp - 1) / cp) <
                              2u * warp_slots)
@@ -564,6 +587,8 @@ extern "C" int rt_paged_decode_attention(const rt_attn_params_t *p, const void *
     args.part_ml = reinterpret_cast<float *>(ws + pl.off_ml);
     args.counters = reinterpret_cast<int32_t *>(ws + pl.off_counters);
     args.error = reinterpret_cast<int32_t *>(ws);
+    args.work_next = reinterpret_cast<unsigned long long *>(ws + 8);
+    args.work_done = reinterpret_cast<unsigned int *>(ws + 16);
     args.num_q_heads = p->num_q_heads;
     args.num_kv_heads = p->num_kv_heads;
     args.max_pages = p->max_pages_per_seq;

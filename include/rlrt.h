@@ -66,8 +66,9 @@ typedef struct {
 } rt_attn_params_t;
 
 /* Device scratch the attention call needs (split-K partials, per-(seq,head)
- * arrival counters, one error word).  Zero it once (rt_attn_workspace_init)
- * before the first call; every call leaves the counters at zero again.
+ * arrival counters, the work dispenser, one error word).  Zero it once
+ * (rt_attn_workspace_init) before the first call; every call leaves the
+ * counters and the dispenser at zero again.
  * Calls sharing one workspace must not overlap on the GPU. */
 size_t rt_attn_workspace_bytes(const rt_attn_params_t *p);
 int rt_attn_workspace_init(void *workspace, size_t bytes, void *stream);

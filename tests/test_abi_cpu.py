@@ -88,4 +88,4 @@ def test_attention_params_validation_on_cpu(pkg):
     bad = pkg.rt_attn_params_t(64, 32, 8, 128, 16, 4096, 100000, 1.0, 0)   # 16 pages < 4096 tok
     assert pkg.lib().rt_attn_workspace_bytes(ctypes.byref(bad)) == 0
     cp, mc, ctas = pkg.PagedDecodeAttention.plan(type("X", (), {"params": p})())
-    assert cp == 16 and mc == 16 and ctas == min(16 * 8 * 64 // 4, 148 * 2)
+    assert cp == 48 and mc == 6 and ctas == min(6 * 8 * 64 // 4, 148 * 2)
