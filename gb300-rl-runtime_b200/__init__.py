@@ -89,6 +89,16 @@ class rt_attn_params_t(ctypes.Structure):
                 ("chunk_pages", ctypes.c_uint32), ("kv_evict_first", ctypes.c_uint32)]
 
 
+class rt_attn_group_t(ctypes.Structure):
+    _fields_ = [("n_members", ctypes.c_uint32), ("shared_pages", ctypes.c_uint32),
+                ("members", ctypes.c_uint32 * 16)]
+
+
+class rt_attn_group_params_t(ctypes.Structure):
+    _fields_ = [("max_groups", ctypes.c_uint32), ("max_shared_pages", ctypes.c_uint32),
+                ("chunk_pages", ctypes.c_uint32), ("reserved", ctypes.c_uint32)]
+
+
 class rt_sample_row_t(ctypes.Structure):
     _fields_ = [("temperature", ctypes.c_float), ("top_k", ctypes.c_uint32),
                 ("top_p", ctypes.c_float), ("rollout_id", ctypes.c_uint32),
@@ -113,7 +123,7 @@ class rt_rollout_config_t(ctypes.Structure):
         ("reward_seed", ctypes.c_uint64), ("logit_std", ctypes.c_float),
         ("max_prefixes", ctypes.c_uint32), ("max_prefix_pages", ctypes.c_uint32),
         ("max_passes", ctypes.c_uint64), ("idle_timeout_ms", ctypes.c_uint32),
-        ("chunk_pages", ctypes.c_uint32)]
+        ("chunk_pages", ctypes.c_uint32), ("prefix_attention", ctypes.c_uint32)]
 
 
 class rt_rollout_io_t(ctypes.Structure):
@@ -133,6 +143,15 @@ class rt_rollout_stats_t(ctypes.Structure):
 
     def as_dict(self):
         return {n: getattr(self, n) for n, _ in self._fields_}
+
+
+class rt_rollout_buffers_t(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n in ("q", "attn_out", "page_table", "seq_lens",
+                                               "groups", "n_groups", "skip_pages")] + [
+        ("max_pages", ctypes.c_uint32), ("max_groups", ctypes.c_uint32)]
+
+
+PASS_HOOK = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_uint64)
 
 
 class rt_rollout_profile_t(ctypes.Structure):
@@ -160,6 +179,11 @@ _SIGS = {
                                     ctypes.POINTER(ctypes.c_uint64)]),
     "rt_paged_decode_attention": (ctypes.c_int, [ctypes.POINTER(rt_attn_params_t), _P, _P, _P,
                                                  _P, _P, _P, ctypes.c_size_t, _P]),
+    "rt_attn_grouped_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(rt_attn_params_t),
+                                                          ctypes.POINTER(rt_attn_group_params_t)]),
+    "rt_paged_decode_attention_grouped": (ctypes.c_int, [ctypes.POINTER(rt_attn_params_t),
+                                                         ctypes.POINTER(rt_attn_group_params_t)]
+                                          + [_P] * 9 + [ctypes.c_size_t, _P]),
     "rt_attn_workspace_error": (ctypes.c_int, [_P, _P, ctypes.POINTER(ctypes.c_int32)]),
     "rt_sample_rows": (ctypes.c_int, [ctypes.POINTER(rt_sample_params_t), _P, _P, _P, _P]),
     "rt_sample_uniform24": (ctypes.c_uint32, [ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint64]),
@@ -171,6 +195,9 @@ _SIGS = {
     "rt_rollout_launch": (ctypes.c_int, [_P, ctypes.POINTER(rt_rollout_io_t), _P]),
     "rt_rollout_profile": (ctypes.c_int, [_P, ctypes.POINTER(rt_rollout_io_t), _P,
                                           ctypes.POINTER(rt_rollout_profile_t)]),
+    "rt_rollout_profile_hook": (ctypes.c_int, [_P, ctypes.POINTER(rt_rollout_io_t), _P,
+                                               ctypes.POINTER(rt_rollout_profile_t), _P, _P]),
+    "rt_rollout_buffers": (ctypes.c_int, [_P, ctypes.POINTER(rt_rollout_buffers_t)]),
     "rt_reward_score": (ctypes.c_int, [_P, ctypes.c_uint32, _P, _P]),
     "rt_grpo_advantages": (ctypes.c_int, [_P, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_float,
                                           _P, _P]),
@@ -280,6 +307,57 @@ class PagedDecodeAttention:
         return code.value
 
 
+GROUP_RECORD_WORDS = 18  # rt_attn_group_t as uint32 words
+
+
+def group_table(groups, max_groups=None):
+    """Pack [(shared_pages, [members...]), ...] into an int32 array of
+    rt_attn_group_t records (n_members, shared_pages, members[16])."""
+    import numpy as np
+    n = max_groups or max(1, len(groups))
+    t = np.zeros((n, GROUP_RECORD_WORDS), dtype=np.uint32)
+    for i, (shared, members) in enumerate(groups):
+        t[i, 0] = len(members)
+        t[i, 1] = shared
+        t[i, 2:2 + len(members)] = members
+    return t
+
+
+class GroupedDecodeAttention(PagedDecodeAttention):
+    """Shared-prefix decode attention (rlrt.h rt_paged_decode_attention_grouped).
+
+    groups: device uint32 [max_groups, 18] (group_table), n_groups: device
+    uint32 [1], skip_pages: device uint32 [B]."""
+
+    def __init__(self, num_seqs, num_q_heads, num_kv_heads, max_pages_per_seq, max_seq_len,
+                 arena_pages, max_groups, max_shared_pages, group_chunk_pages=0, scale=None,
+                 chunk_pages=0, evict_first=False, device="cuda"):
+        import torch
+        self.params = rt_attn_params_t(
+            num_seqs, num_q_heads, num_kv_heads, 128, max_pages_per_seq, max_seq_len,
+            arena_pages, scale if scale is not None else 128 ** -0.5, chunk_pages,
+            1 if evict_first else 0)
+        self.gparams = rt_attn_group_params_t(max_groups, max_shared_pages, group_chunk_pages, 0)
+        n = lib().rt_attn_grouped_workspace_bytes(ctypes.byref(self.params),
+                                                  ctypes.byref(self.gparams))
+        if n == 0:
+            raise RuntimeErrorRT("bad attention params: " + lib().rt_last_error().decode())
+        self.workspace = torch.zeros(n, dtype=torch.uint8, device=device)
+        self.device = device
+
+    def __call__(self, q, arena, page_table, seq_lens, groups, n_groups, skip_pages, out=None,
+                 stream=None):
+        import torch
+        if out is None:
+            out = torch.empty(q.shape, dtype=torch.float32, device=q.device)
+        check(lib().rt_paged_decode_attention_grouped(
+            ctypes.byref(self.params), ctypes.byref(self.gparams), _ptr(q), _ptr(arena),
+            _ptr(page_table), _ptr(seq_lens), _ptr(groups), _ptr(n_groups), _ptr(skip_pages),
+            _ptr(out), _ptr(self.workspace), self.workspace.numel(), _stream_ptr(stream)),
+            "rt_paged_decode_attention_grouped")
+        return out
+
+
 def fill_normal_bf16(t, seed, stream_id=0, mean=0.0, std=1.0, stream=None):
     check(lib().rt_fill_normal_bf16(_ptr(t), t.numel(), seed, stream_id, mean, std,
                                     _stream_ptr(stream)), "rt_fill_normal_bf16")
@@ -331,6 +409,8 @@ def sample_uniform24(seed, rollout_id, step) -> int:
 # ------------------------------------------------------------ rollout loop
 RT_ROLLOUT_DECODE_NONE, RT_ROLLOUT_DECODE_FULL = 0, 1
 RT_REWARD_MOCK, RT_REWARD_PHILOX = 0, 1
+RT_PREFIX_ATTN_GROUPED = 0
+RT_PREFIX_ATTN_PER_SEQUENCE = 1
 PAGE_TOKENS = 16
 
 
@@ -425,6 +505,36 @@ class RolloutEngine:
         check(lib().rt_rollout_profile(self.h, ctypes.byref(io), _stream_ptr(stream),
                                        ctypes.byref(out)), "rt_rollout_profile")
         return out.as_dict()
+
+    def step(self, hook, *, requests=None, n_requests=0, dones=None, state=None,
+             trajectories=None, rewards=None, n_rows=0, stream=None):
+        """rt_rollout_profile_hook: host-stepped replay calling hook(pass) after
+        every pass; a truthy return stops it."""
+        io = self._io(None, requests, n_requests, None, dones, state, None, trajectories,
+                      rewards, n_rows)
+        out = rt_rollout_profile_t()
+        err = []
+
+        def tramp(_user, p):
+            try:
+                return 1 if hook(int(p)) else 0
+            except BaseException as exc:  # surface after the C call returns
+                err.append(exc)
+                return 1
+
+        cb = PASS_HOOK(tramp)
+        rc = lib().rt_rollout_profile_hook(self.h, ctypes.byref(io), _stream_ptr(stream),
+                                           ctypes.byref(out), ctypes.cast(cb, ctypes.c_void_p),
+                                           None)
+        if err:
+            raise err[0]
+        check(rc, "rt_rollout_profile_hook")
+        return out.as_dict()
+
+    def buffers(self):
+        b = rt_rollout_buffers_t()
+        check(lib().rt_rollout_buffers(self.h, ctypes.byref(b)), "rt_rollout_buffers")
+        return b
 
     def wait(self, stream=None, check_errors=True):
         st = rt_rollout_stats_t()

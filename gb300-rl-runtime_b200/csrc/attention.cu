@@ -44,7 +44,7 @@ constexpr int kMaxChunkPages = 64;   // page ids live in two registers per lane
 constexpr int kSmemBytes = kWarps * kStages * kStageBytes + 1024;  // + 1 KiB alignment slack
 constexpr uint64_t kWaitLimitNs = 2000000000ull;                    // 2 s per pipeline wait
 
-enum : int32_t { kErrSeqLen = 1, kErrPage = 2, kErrTimeout = 3 };
+enum : int32_t { kErrSeqLen = 1, kErrPage = 2, kErrTimeout = 3, kErrGroup = 4 };
 
 struct AttnArgs {
     const __nv_bfloat16 *q;
@@ -62,11 +62,110 @@ struct AttnArgs {
     uint64_t n_items;
     float scale_log2;
     uint32_t evict_first;
+    // shared-prefix groups (cascade); groups == nullptr disables them
+    const rt_attn_group_t *groups;
+    const uint32_t *n_groups;          // device count of valid group records
+    const uint32_t *skip_pages;        // [B] pages covered by the sequence's group, or nullptr
+    unsigned long long *group_next;    // CTA-level dispenser of group items
+    unsigned int *group_done;          // CTAs that left the group phase
+    uint32_t max_groups, gchunk_pages, max_gchunks;
+    uint32_t slots;                    // partial slots per (b, h): max_gchunks + max_chunks
 };
+
+constexpr int kGroupStages = kWarps * kStages;  // the CTA's whole ring, shared by its warps
+constexpr uint32_t kMaxGroupMembers = 16;
 
 __device__ __forceinline__ void flag_error(int32_t *err, int32_t code)
 {
     atomicCAS(err, 0, code);
+}
+
+// Partial slots of (b, h): group-prefix chunks use slots [0, max_gchunks),
+// the sequence's own chunks use [max_gchunks, max_gchunks + max_chunks).
+
+// Log-sum-exp merge of all partials of (b, h) into out; called by one warp.
+// Latency-bound (L2 round trips), so the loads are issued wide: first the
+// (max, sum) pairs of all parts x rows across the lanes, reduced per row with
+// shuffles (row = lane % G is kept by xor offsets >= G), then per row the
+// partial outputs four parts at a time, each lane owning 4 of the 128 dims.
+template <int G>
+__device__ __forceinline__ void merge_parts(const AttnArgs &a, size_t bh, uint32_t b, uint32_t h,
+                                            uint32_t n_g, uint32_t n_s)
+{
+    const int lane = threadIdx.x & 31;
+    const uint32_t n = n_g + n_s, pairs = n * G;
+    auto slot_of = [&](uint32_t k) { return k < n_g ? k : a.max_gchunks + (k - n_g); };
+    auto ml_at = [&](uint32_t k, uint32_t row) {
+        return __ldcg(reinterpret_cast<const float2 *>(
+            &a.part_ml[((bh * a.slots + slot_of(k)) * G + row) * 2]));
+    };
+    float m_lane = -INFINITY;
+    for (uint32_t j = lane; j < pairs; j += 32)
+        m_lane = fmaxf(m_lane, ml_at(j / G, j % G).x);
+#pragma unroll
+    for (int off = 16; off >= G; off >>= 1)
+        m_lane = fmaxf(m_lane, __shfl_xor_sync(0xffffffffu, m_lane, off));
+    float l_lane = 0.0f;
+    for (uint32_t j = lane; j < pairs; j += 32) {
+        const float2 ml = ml_at(j / G, j % G);
+        l_lane += ml.y * rt::fast_exp2(ml.x - m_lane);
+    }
+#pragma unroll
+    for (int off = 16; off >= G; off >>= 1)
+        l_lane += __shfl_xor_sync(0xffffffffu, l_lane, off);
+
+#pragma unroll
+    for (int row = 0; row < G; row++) {
+        const float M = __shfl_sync(0xffffffffu, m_lane, row);
+        const float inv = 1.0f / __shfl_sync(0xffffffffu, l_lane, row);
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        uint32_t k = 0;
+        for (; k + 4u <= n; k += 4u) {
+            float2 ml[4];
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const size_t pi = (bh * a.slots + slot_of(k + u)) * G + row;
+                ml[u] = __ldcg(reinterpret_cast<const float2 *>(&a.part_ml[pi * 2]));
+                v[u] = __ldcg(reinterpret_cast<const float4 *>(&a.part_o[pi * 128 + lane * 4]));
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const float wt = rt::fast_exp2(ml[u].x - M);
+                acc.x += v[u].x * wt;
+                acc.y += v[u].y * wt;
+                acc.z += v[u].z * wt;
+                acc.w += v[u].w * wt;
+            }
+        }
+        for (; k < n; k++) {
+            const size_t pi = (bh * a.slots + slot_of(k)) * G + row;
+            const float wt = rt::fast_exp2(__ldcg(&a.part_ml[pi * 2]) - M);
+            const float4 v = __ldcg(reinterpret_cast<const float4 *>(&a.part_o[pi * 128 + lane * 4]));
+            acc.x += v.x * wt;
+            acc.y += v.y * wt;
+            acc.z += v.z * wt;
+            acc.w += v.w * wt;
+        }
+        *reinterpret_cast<float4 *>(a.out + ((size_t)b * a.num_q_heads + (size_t)h * G + row) * 128 +
+                                    lane * 4) =
+            make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+    }
+}
+
+// Pages of sequence b that its group covers, as the sequence's own items see
+// it: skip_pages[b] when it fits the sequence and the planned group chunks,
+// else 0 (flagged).  The group items apply the same rule to every member.
+__device__ __forceinline__ uint32_t seq_skip(const AttnArgs &a, uint32_t b, int n_pages)
+{
+    if (!a.skip_pages)
+        return 0u;
+    const uint32_t skip = a.skip_pages[b];
+    if (skip > (uint32_t)n_pages || skip > a.max_gchunks * a.gchunk_pages) {
+        flag_error(a.error, kErrGroup);
+        return 0u;
+    }
+    return skip;
 }
 
 // One warp processes one item; see the file comment.  Returns false when a
@@ -97,12 +196,16 @@ __device__ __forceinline__ bool process_item(const CUtensorMap &kv_map, const At
         return true;
     }
     const int n_pages = (L + 15) >> 4;
+    const int skip = (int)seq_skip(a, b, n_pages);
     const int cp = (int)a.chunk_pages;
-    const int n_chunks = (n_pages + cp - 1) / cp;
+    const uint32_t n_g = (uint32_t)((skip + (int)a.gchunk_pages - 1) / (int)a.gchunk_pages);
+    // This sequence's own chunks; a fully covered sequence still has chunk 0,
+    // which folds the group's partials into the output.
+    const int n_chunks = max((n_pages - skip + cp - 1) / cp, n_g ? 1 : 0);
     if (chunk >= n_chunks)
         return true;
-    const int p_begin = chunk * cp;
-    const int n_mine = min(n_pages, p_begin + cp) - p_begin;
+    const int p_begin = skip + chunk * cp;
+    const int n_mine = max(0, min(n_pages, p_begin + cp) - p_begin);
 
     // Page ids of this item: lane i holds pages i and 32 + i.
     const int32_t *ptab = a.page_table + (size_t)b * a.max_pages + p_begin;
@@ -161,6 +264,31 @@ __device__ __forceinline__ bool process_item(const CUtensorMap &kv_map, const At
     for (int n = 0; n < 16; n++)
         o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
     float m_run = -INFINITY, l_run = 0.0f;
+    const size_t bh = (size_t)b * Hkv + h;
+    if (chunk == 0 && n_g && r < G) {
+        // Start from the group's prefix partials (written by the group
+        // kernel): o = sum_k o_k 2^(m_k - M), l = sum_k l_k 2^(m_k - M).
+        const size_t pi0 = (bh * a.slots) * G + r;
+        for (uint32_t k = 0; k < n_g; k++)
+            m_run = fmaxf(m_run, a.part_ml[(pi0 + (size_t)k * G) * 2]);
+        for (uint32_t k = 0; k < n_g; k++) {
+            const size_t pi = pi0 + (size_t)k * G;
+            const float2 ml = *reinterpret_cast<const float2 *>(&a.part_ml[pi * 2]);
+            const float wt = rt::fast_exp2(ml.x - m_run);
+            l_run += ml.y * wt;
+            const float *src = a.part_o + pi * 128 + 2 * q4;
+            float2 v[16];
+#pragma unroll
+            for (int n = 0; n < 16; n++)
+                v[n] = *reinterpret_cast<const float2 *>(src + n * 8);
+#pragma unroll
+            for (int n = 0; n < 16; n++) {
+                o[n][0] += v[n].x * wt;
+                o[n][1] += v[n].y * wt;
+            }
+        }
+        l_run *= 0.25f;  // every lane of the quad adds the full sum; the quad reduction below sums 4x
+    }
 
     // Per-lane ldmatrix row offsets (swizzled chunk index = chunk ^ row%8).
     const int mi = lane >> 3, rr = lane & 7;
@@ -231,7 +359,13 @@ __device__ __forceinline__ bool process_item(const CUtensorMap &kv_map, const At
             o[n][0] *= corr;
             o[n][1] *= corr;
         }
-        const uint32_t pa[4] = {rt::pack_bf16x2(p0, p1), 0u, rt::pack_bf16x2(p2, p3), 0u};
+        // P in two bf16 terms (hi + lo): P.V then carries ~16 mantissa bits
+        // of the probabilities, not bf16's 8.
+        uint32_t h01, l01, h23, l23;
+        rt::split_bf16x2(p0, p1, h01, l01);
+        rt::split_bf16x2(p2, p3, h23, l23);
+        const uint32_t pa[4] = {h01, 0u, h23, 0u};
+        const uint32_t pl[4] = {l01, 0u, l23, 0u};
 
         // O += P V over 128 dims (16 n-tiles of 8, two per ldmatrix.x4).
 #pragma unroll
@@ -243,6 +377,8 @@ __device__ __forceinline__ bool process_item(const CUtensorMap &kv_map, const At
             rt::ldsm_x4_trans(addr, v0, v1, v2, v3);
             rt::mma_bf16_16816(o[2 * dd], pa, v0, v1);
             rt::mma_bf16_16816(o[2 * dd + 1], pa, v2, v3);
+            rt::mma_bf16_16816(o[2 * dd], pl, v0, v1);
+            rt::mma_bf16_16816(o[2 * dd + 1], pl, v2, v3);
         }
         __syncwarp();
         if (i + kStages < n_mine) {
@@ -257,7 +393,6 @@ __device__ __forceinline__ bool process_item(const CUtensorMap &kv_map, const At
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
 
-    const size_t bh = (size_t)b * Hkv + h;
     if (n_chunks == 1) {
         if (r < G) {
             const float inv = 1.0f / l_run;
@@ -269,9 +404,9 @@ __device__ __forceinline__ bool process_item(const CUtensorMap &kv_map, const At
         return true;
     }
 
-    // ---- split-K: write this chunk's partial; the last warp merges ----
+    // ---- split-K: write this chunk's partial; the last part to arrive merges ----
     if (r < G) {
-        const size_t pi = (bh * a.max_chunks + chunk) * G + r;
+        const size_t pi = (bh * a.slots + a.max_gchunks + chunk) * G + r;
         float *dst = a.part_o + pi * 128 + 2 * q4;
 #pragma unroll
         for (int n = 0; n < 16; n++)
@@ -288,30 +423,292 @@ __device__ __forceinline__ bool process_item(const CUtensorMap &kv_map, const At
     if (prev != n_chunks - 1)
         return true;
     __threadfence();
-    for (int row = 0; row < G; row++) {
-        float M = -INFINITY;
-        for (int c = 0; c < n_chunks; c++)
-            M = fmaxf(M, __ldcg(&a.part_ml[((bh * a.max_chunks + c) * G + row) * 2]));
-        float Ls = 0.0f;
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int c = 0; c < n_chunks; c++) {
-            const size_t pi = (bh * a.max_chunks + c) * G + row;
-            const float2 ml = __ldcg(reinterpret_cast<const float2 *>(&a.part_ml[pi * 2]));
-            const float wt = rt::fast_exp2(ml.x - M);
-            Ls += ml.y * wt;
-            const float4 v = __ldcg(reinterpret_cast<const float4 *>(&a.part_o[pi * 128 + lane * 4]));
-            acc.x += v.x * wt;
-            acc.y += v.y * wt;
-            acc.z += v.z * wt;
-            acc.w += v.w * wt;
-        }
-        const float inv = 1.0f / Ls;
-        *reinterpret_cast<float4 *>(a.out + ((size_t)b * Hq + (size_t)h * G + row) * 128 + lane * 4) =
-            make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
-    }
+    merge_parts<G>(a, bh, b, h, 0u, (uint32_t)n_chunks);
     if (lane == 0)
         a.counters[bh] = 0;
     return true;
+}
+
+// One (group, row block, KV head, prefix chunk) item, processed by the whole
+// CTA: the group's shared prefix pages stream once through the CTA's 12-stage
+// ring (warp 0 loads the page ids, lane 0 issues the TMA copies), and each
+// warp attends 16 query rows to every page - 16/G member sequences x G
+// heads, so for G = 4 every row of the m16n8k16 tile is a real query (4
+// sequences x 4 heads per warp, 16 sequences per CTA).  G = 8 needs two row
+// blocks for 16 members; G = 1, 2 leave warps idle.  Each member's result is
+// an unnormalised partial (o, max, sum) in slot `chunk` of its (b, h); the
+// sequence kernel that runs next folds these into its own online softmax.
+template <int G>
+__device__ __forceinline__ bool process_group_item(const CUtensorMap &kv_map, const AttnArgs &a,
+                                                   uint64_t gi, uint32_t n_live, uint32_t ring0,
+                                                   uint64_t *gbars, uint32_t &gphases,
+                                                   uint64_t policy)
+{
+    constexpr int MPW = 16 / G;                        // member sequences per warp
+    constexpr int RB = (16 * G + 16 * kWarps - 1) / (16 * kWarps);  // row blocks per group
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t Hkv = a.num_kv_heads, Hq = a.num_q_heads;
+    const uint32_t g = (uint32_t)(gi % n_live);
+    uint64_t rest = gi / n_live;
+    const int rb = (int)(rest % RB);
+    rest /= RB;
+    const uint32_t h = (uint32_t)(rest % Hkv);
+    const int chunk = (int)(rest / Hkv);
+    const rt_attn_group_t &grp = a.groups[g];
+    const uint32_t n_mem = min(grp.n_members, kMaxGroupMembers);
+    const int P = (int)grp.shared_pages;
+    const int cpg = (int)a.gchunk_pages;
+    const int p0 = chunk * cpg;
+    if (n_mem == 0 || P == 0 || p0 >= P)
+        return true;
+    const uint32_t src = grp.members[0];
+    if (src >= a.num_seqs || (uint32_t)P > a.max_gchunks * (uint32_t)cpg ||
+        (uint32_t)P > a.max_pages) {
+        if (threadIdx.x == 0)
+            flag_error(a.error, kErrGroup);
+        return true;
+    }
+    const int np = min(P, p0 + cpg) - p0;
+
+    // Page ids (warp 0): lane i holds pages i and 32 + i of this chunk.
+    int pg_lo = 0, pg_hi = 0;
+    if (warp == 0) {
+        const int32_t *ptab = a.page_table + (size_t)src * a.max_pages + p0;
+        if (lane < np)
+            pg_lo = ptab[lane];
+        if (lane + 32 < np)
+            pg_hi = ptab[lane + 32];
+        const bool bad = (lane < np && (pg_lo < 0 || (uint64_t)pg_lo >= a.arena_pages)) ||
+                         (lane + 32 < np && (pg_hi < 0 || (uint64_t)pg_hi >= a.arena_pages));
+        if (bad) {
+            flag_error(a.error, kErrPage);
+            if (pg_lo < 0 || (uint64_t)pg_lo >= a.arena_pages)
+                pg_lo = 0;
+            if (pg_hi < 0 || (uint64_t)pg_hi >= a.arena_pages)
+                pg_hi = 0;
+        }
+    }
+    auto issue = [&](int i) {  // warp 0 only
+        const int pg = __shfl_sync(0xffffffffu, i < 32 ? pg_lo : pg_hi, i & 31);
+        if (lane == 0) {
+            const int s = i % kGroupStages;
+            const uint32_t bar = rt::smem_u32(&gbars[s]);
+            const uint32_t dst = ring0 + (uint32_t)(s * kStageBytes);
+            const int32_t row_k = (int32_t)(((int64_t)pg * Hkv + h) * 32);
+            rt::mbar_arrive_expect_tx(bar, (uint32_t)kStageBytes);
+            rt::tma_load_2d(dst, &kv_map, 0, row_k, bar, policy);
+            rt::tma_load_2d(dst + 2048u, &kv_map, 64, row_k, bar, policy);
+            rt::tma_load_2d(dst + 4096u, &kv_map, 0, row_k + 16, bar, policy);
+            rt::tma_load_2d(dst + 6144u, &kv_map, 64, row_k + 16, bar, policy);
+        }
+    };
+    if (warp == 0)
+        for (int i = 0; i < np && i < kGroupStages; i++)
+            issue(i);
+
+    // A member takes part when the group covers exactly its skipped pages.
+    auto member_ok = [&](int m) -> bool {
+        if (m >= (int)n_mem)
+            return false;
+        const uint32_t b = grp.members[m];
+        if (b >= a.num_seqs)
+            return false;
+        const int L = a.seq_lens[b];
+        if (L < 0 || (uint32_t)L > a.max_seq_len || (uint32_t)L > a.max_pages * 16u)
+            return false;
+        return a.skip_pages[b] == (uint32_t)P && P <= ((L + 15) >> 4);
+    };
+
+    // Rows of this warp: row r -> member (rb*kWarps + warp)*MPW + r/G, head r%G.
+    const int wm0 = (rb * kWarps + warp) * MPW;
+    const int rA = lane >> 2, rB = rA + 8, q4 = lane & 3;
+    const int mA = wm0 + rA / G, mB = wm0 + rB / G;
+    const bool vA = member_ok(mA), vB = member_ok(mB);
+    if (lane == 0 && chunk == 0 && h == 0)
+        for (int m = wm0; m < wm0 + MPW && m < (int)n_mem; m++)
+            if (!member_ok(m))
+                flag_error(a.error, kErrGroup);
+    const bool active = __any_sync(0xffffffffu, vA || vB);
+    const uint32_t bA = vA ? grp.members[mA] : 0u, bB = vB ? grp.members[mB] : 0u;
+    uint32_t qf[8][4];
+    {
+        const uint32_t *qa = reinterpret_cast<const uint32_t *>(
+            a.q + ((size_t)bA * Hq + (size_t)h * G + rA % G) * 128);
+        const uint32_t *qb = reinterpret_cast<const uint32_t *>(
+            a.q + ((size_t)bB * Hq + (size_t)h * G + rB % G) * 128);
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            qf[j][0] = vA ? qa[8 * j + q4] : 0u;
+            qf[j][1] = vB ? qb[8 * j + q4] : 0u;
+            qf[j][2] = vA ? qa[8 * j + 4 + q4] : 0u;
+            qf[j][3] = vB ? qb[8 * j + 4 + q4] : 0u;
+        }
+    }
+
+    float o[16][4];
+#pragma unroll
+    for (int n = 0; n < 16; n++)
+        o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+    float mA_run = -INFINITY, lA = 0.0f, mB_run = -INFINITY, lB = 0.0f;
+    const int mi = lane >> 3, rr = lane & 7;
+    const uint32_t k_row = (uint32_t)((((mi >> 1) << 3) + rr) * 128);
+    const uint32_t v_row = (uint32_t)((((mi & 1) << 3) + rr) * 128);
+    for (int i = 0; i < np; i++) {
+        const int s = i % kGroupStages;
+        const bool ok = rt::mbar_wait_bounded(rt::smem_u32(&gbars[s]), (gphases >> s) & 1u,
+                                              kWaitLimitNs);
+        if (!__syncthreads_and(ok)) {
+            if (threadIdx.x == 0) {
+                flag_error(a.error, kErrTimeout);
+                // Give the copies still in flight (pages i .. i+11) a bounded
+                // chance to land before the shared memory is released.
+                for (int j = i; j < np && j < i + kGroupStages; j++) {
+                    const int s2 = j % kGroupStages;
+                    (void)rt::mbar_wait_bounded(rt::smem_u32(&gbars[s2]), (gphases >> s2) & 1u,
+                                                kWaitLimitNs / 4);
+                }
+            }
+            return false;
+        }
+        gphases ^= 1u << s;
+        if (active) {
+            const uint32_t st = ring0 + (uint32_t)(s * kStageBytes);
+            float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const int c = ((j & 3) << 1) + (mi & 1);
+                const uint32_t addr =
+                    st + (uint32_t)((j >> 2) * 2048) + k_row + (uint32_t)((c ^ rr) << 4);
+                uint32_t k0, k1, k2, k3;
+                rt::ldsm_x4(addr, k0, k1, k2, k3);
+                rt::mma_bf16_16816(sc[0], qf[j], k0, k1);
+                rt::mma_bf16_16816(sc[1], qf[j], k2, k3);
+            }
+            // rows rA (c0, c1) and rB (c2, c3); every token of a shared page is valid
+            const float a0 = sc[0][0] * a.scale_log2, a1 = sc[0][1] * a.scale_log2;
+            const float a2 = sc[1][0] * a.scale_log2, a3 = sc[1][1] * a.scale_log2;
+            const float b0 = sc[0][2] * a.scale_log2, b1 = sc[0][3] * a.scale_log2;
+            const float b2 = sc[1][2] * a.scale_log2, b3 = sc[1][3] * a.scale_log2;
+            float xa = fmaxf(fmaxf(a0, a1), fmaxf(a2, a3));
+            float xb = fmaxf(fmaxf(b0, b1), fmaxf(b2, b3));
+            xa = fmaxf(xa, __shfl_xor_sync(0xffffffffu, xa, 1));
+            xa = fmaxf(xa, __shfl_xor_sync(0xffffffffu, xa, 2));
+            xb = fmaxf(xb, __shfl_xor_sync(0xffffffffu, xb, 1));
+            xb = fmaxf(xb, __shfl_xor_sync(0xffffffffu, xb, 2));
+            const float nA = fmaxf(mA_run, xa), nB = fmaxf(mB_run, xb);
+            const float cA = rt::fast_exp2(mA_run - nA), cB = rt::fast_exp2(mB_run - nB);
+            const float pa0 = rt::fast_exp2(a0 - nA), pa1 = rt::fast_exp2(a1 - nA);
+            const float pa2 = rt::fast_exp2(a2 - nA), pa3 = rt::fast_exp2(a3 - nA);
+            const float pb0 = rt::fast_exp2(b0 - nB), pb1 = rt::fast_exp2(b1 - nB);
+            const float pb2 = rt::fast_exp2(b2 - nB), pb3 = rt::fast_exp2(b3 - nB);
+            lA = lA * cA + ((pa0 + pa1) + (pa2 + pa3));
+            lB = lB * cB + ((pb0 + pb1) + (pb2 + pb3));
+            mA_run = nA;
+            mB_run = nB;
+#pragma unroll
+            for (int n = 0; n < 16; n++) {
+                o[n][0] *= cA;
+                o[n][1] *= cA;
+                o[n][2] *= cB;
+                o[n][3] *= cB;
+            }
+            uint32_t pf[4], pl[4];  // P = hi + lo in bf16 (see process_item)
+            rt::split_bf16x2(pa0, pa1, pf[0], pl[0]);
+            rt::split_bf16x2(pb0, pb1, pf[1], pl[1]);
+            rt::split_bf16x2(pa2, pa3, pf[2], pl[2]);
+            rt::split_bf16x2(pb2, pb3, pf[3], pl[3]);
+#pragma unroll
+            for (int dd = 0; dd < 8; dd++) {
+                const int c = ((dd & 3) << 1) + (mi >> 1);
+                const uint32_t addr =
+                    st + 4096u + (uint32_t)((dd >> 2) * 2048) + v_row + (uint32_t)((c ^ rr) << 4);
+                uint32_t v0, v1, v2, v3;
+                rt::ldsm_x4_trans(addr, v0, v1, v2, v3);
+                rt::mma_bf16_16816(o[2 * dd], pf, v0, v1);
+                rt::mma_bf16_16816(o[2 * dd + 1], pf, v2, v3);
+                rt::mma_bf16_16816(o[2 * dd], pl, v0, v1);
+                rt::mma_bf16_16816(o[2 * dd + 1], pl, v2, v3);
+            }
+        }
+        // Every warp has read stage s (shared-memory reads only, so the TMA
+        // rewrite needs no proxy fence).
+        __syncthreads();
+        if (warp == 0 && i + kGroupStages < np)
+            issue(i + kGroupStages);
+    }
+    if (!active)
+        return true;
+    lA += __shfl_xor_sync(0xffffffffu, lA, 1);
+    lA += __shfl_xor_sync(0xffffffffu, lA, 2);
+    lB += __shfl_xor_sync(0xffffffffu, lB, 1);
+    lB += __shfl_xor_sync(0xffffffffu, lB, 2);
+
+    // Partials of both rows of this lane; the kernel boundary publishes them.
+    if (vA) {
+        const size_t pi = (((size_t)bA * Hkv + h) * a.slots + chunk) * G + rA % G;
+        float *dst = a.part_o + pi * 128 + 2 * q4;
+#pragma unroll
+        for (int n = 0; n < 16; n++)
+            *reinterpret_cast<float2 *>(dst + n * 8) = make_float2(o[n][0], o[n][1]);
+        if (q4 == 0)
+            *reinterpret_cast<float2 *>(a.part_ml + pi * 2) = make_float2(mA_run, lA);
+    }
+    if (vB) {
+        const size_t pi = (((size_t)bB * Hkv + h) * a.slots + chunk) * G + rB % G;
+        float *dst = a.part_o + pi * 128 + 2 * q4;
+#pragma unroll
+        for (int n = 0; n < 16; n++)
+            *reinterpret_cast<float2 *>(dst + n * 8) = make_float2(o[n][2], o[n][3]);
+        if (q4 == 0)
+            *reinterpret_cast<float2 *>(a.part_ml + pi * 2) = make_float2(mB_run, lB);
+    }
+    return true;
+}
+
+// Shared-prefix kernel of the grouped entry point: persistent CTAs take
+// (group, row block, head, chunk) items from a dispenser; the last CTA out
+// resets it for the next launch.
+template <int G>
+__global__ void __launch_bounds__(kWarps * 32, 2)
+paged_gqa_group_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnArgs a)
+{
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t gbars[kGroupStages];
+    __shared__ unsigned long long s_gitem;
+    const uint32_t raw_u32 = rt::smem_u32(smem_raw);
+    const uint32_t base_u32 = (raw_u32 + 1023u) & ~1023u;  // 128-byte swizzle: 1 KiB aligned
+    if (threadIdx.x == 0) {
+        rt::prefetch_tensormap(&kv_map);
+        for (int s = 0; s < kGroupStages; s++)
+            rt::mbar_init(rt::smem_u32(&gbars[s]), 1u);
+        rt::mbar_fence_init();
+    }
+    __syncthreads();
+    const uint64_t policy = a.evict_first ? rt::l2_policy_evict_first() : rt::l2_policy_evict_normal();
+    constexpr int RB = (16 * G + 16 * kWarps - 1) / (16 * kWarps);
+    const uint32_t n_live = min(*a.n_groups, a.max_groups);
+    const uint64_t n_gi = (uint64_t)n_live * RB * a.num_kv_heads * a.max_gchunks;
+    uint32_t gphases = 0;
+    while (n_gi) {
+        if (threadIdx.x == 0)
+            s_gitem = atomicAdd(a.group_next, 1ull);
+        __syncthreads();
+        const uint64_t gi = s_gitem;
+        __syncthreads();
+        if (gi >= n_gi)
+            break;
+        // A false return means a wait expired (flagged): stop taking items.
+        if (!process_group_item<G>(kv_map, a, gi, n_live, base_u32, gbars, gphases, policy))
+            break;
+    }
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(a.group_done, 1u) == gridDim.x - 1u) {
+            *a.group_next = 0ull;
+            *a.group_done = 0u;
+            __threadfence();
+        }
+    }
 }
 
 // Persistent warps take items in increasing order from a global dispenser
@@ -368,10 +765,15 @@ paged_gqa_decode_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnAr
 // ------------------------------------------------------------------ host
 struct Plan {
     uint32_t group, chunk_pages, max_chunks;
+    uint32_t gchunk_pages, max_gchunks, slots;  // group phase (0 when ungrouped)
     size_t off_counters, off_ml, off_o, total;
 };
 
-int make_plan(const rt_attn_params_t *p, Plan *pl)
+constexpr uint32_t kDefaultGroupChunkPages = 8;
+
+// Workspace header: error word at 0, per-warp item dispenser at 8/16, group
+// item dispenser at 24/32; arrival counters from 256.
+int make_plan(const rt_attn_params_t *p, Plan *pl, const rt_attn_group_params_t *gp = nullptr)
 {
     if (!p) {
         rt::set_error("attention: null params");
@@ -420,12 +822,27 @@ int make_plan(const rt_attn_params_t *p, Plan *pl)
     pl->group = g;
     pl->chunk_pages = cp;
     pl->max_chunks = pages_max ? (pages_max + cp - 1) / cp : 1u;
+    pl->gchunk_pages = 0;
+    pl->max_gchunks = 0;
+    if (gp) {
+        uint32_t cpg = gp->chunk_pages ? gp->chunk_pages : kDefaultGroupChunkPages;
+        if (gp->max_groups == 0 || gp->max_groups > (1u << 24) || cpg > (uint32_t)kMaxChunkPages ||
+            gp->max_shared_pages > pages_max) {
+            rt::set_error("attention: group params out of range (max_groups %u, "
+                          "max_shared_pages %u of %u pages, chunk_pages %u)",
+                          gp->max_groups, gp->max_shared_pages, pages_max, cpg);
+            return RT_EINVAL;
+        }
+        pl->gchunk_pages = cpg;
+        pl->max_gchunks = (gp->max_shared_pages + cpg - 1) / cpg;
+    }
+    pl->slots = pl->max_gchunks + pl->max_chunks;
     const size_t bh = (size_t)p->num_seqs * p->num_kv_heads;
     auto up = [](size_t x) { return (x + 255u) & ~(size_t)255u; };
     pl->off_counters = 256;
     pl->off_ml = pl->off_counters + up(bh * 4u);
-    pl->off_o = pl->off_ml + up(bh * pl->max_chunks * g * 2u * 4u);
-    pl->total = pl->off_o + up(bh * pl->max_chunks * g * 128u * 4u);
+    pl->off_o = pl->off_ml + up(bh * pl->slots * g * 2u * 4u);
+    pl->total = pl->off_o + up(bh * pl->slots * g * 128u * 4u);
     return RT_OK;
 }
 
@@ -474,6 +891,9 @@ int prepare_g()
         return RT_OK;
     e = cudaFuncSetAttribute(paged_gqa_decode_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kSmemBytes);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(paged_gqa_group_kernel<G>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess)
         return rt::cuda_fail(e, "attention: cudaFuncSetAttribute");
     if (dev < 64)
@@ -497,6 +917,12 @@ int launch_g(const CUtensorMap &map, const AttnArgs &args, dim3 grid, cudaStream
     int rc = prepare_g<G>();
     if (rc != RT_OK)
         return rc;
+    if (args.groups) {
+        // Group prefixes first; the stream orders their partials before the
+        // sequence kernel that folds them in.
+        const dim3 ggrid((unsigned)rt::num_sms() * 2u);
+        paged_gqa_group_kernel<G><<<ggrid, kWarps * 32, kSmemBytes, s>>>(map, args);
+    }
     paged_gqa_decode_kernel<G><<<grid, kWarps * 32, kSmemBytes, s>>>(map, args);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? RT_OK : rt::cuda_fail(e, "attention: launch");
@@ -544,22 +970,30 @@ extern "C" int rt_attn_plan(const rt_attn_params_t *p, uint32_t *chunk_pages, ui
     return RT_OK;
 }
 
-extern "C" int rt_paged_decode_attention(const rt_attn_params_t *p, const void *q,
-                                         const void *kv_arena, const int32_t *page_table,
-                                         const int32_t *seq_lens, float *out, void *workspace,
-                                         size_t workspace_bytes, void *stream)
+namespace {
+
+int launch_attention(const rt_attn_params_t *p, const rt_attn_group_params_t *gp, const void *q,
+                     const void *kv_arena, const int32_t *page_table, const int32_t *seq_lens,
+                     const rt_attn_group_t *groups, const uint32_t *n_groups,
+                     const uint32_t *skip_pages, float *out, void *workspace,
+                     size_t workspace_bytes, void *stream)
 {
     Plan pl;
-    int rc = make_plan(p, &pl);
+    int rc = make_plan(p, &pl, gp);
     if (rc != RT_OK)
         return rc;
     if (!q || !kv_arena || !page_table || !seq_lens || !out || !workspace) {
         rt::set_error("attention: null pointer argument");
         return RT_EINVAL;
     }
+    if (gp && (!groups || !n_groups || !skip_pages)) {
+        rt::set_error("attention: grouped call needs groups, n_groups and skip_pages");
+        return RT_EINVAL;
+    }
     if (((uintptr_t)q & 3u) || ((uintptr_t)out & 3u) || ((uintptr_t)workspace & 255u) ||
         ((uintptr_t)kv_arena & 15u) || ((uintptr_t)page_table & 3u) ||
-        ((uintptr_t)seq_lens & 3u)) {
+        ((uintptr_t)seq_lens & 3u) || ((uintptr_t)groups & 3u) || ((uintptr_t)n_groups & 3u) ||
+        ((uintptr_t)skip_pages & 3u)) {
         rt::set_error("attention: misaligned pointer (q/out/tables 4 B, arena 16 B, workspace 256 B)");
         return RT_EINVAL;
     }
@@ -600,6 +1034,15 @@ extern "C" int rt_paged_decode_attention(const rt_attn_params_t *p, const void *
     args.evict_first = p->kv_evict_first ? 1u : 0u;
     args.num_seqs = p->num_seqs;
     args.n_items = (uint64_t)p->num_seqs * p->num_kv_heads * pl.max_chunks;
+    args.groups = gp ? groups : nullptr;
+    args.n_groups = gp ? n_groups : nullptr;
+    args.skip_pages = gp ? skip_pages : nullptr;
+    args.group_next = reinterpret_cast<unsigned long long *>(ws + 24);
+    args.group_done = reinterpret_cast<unsigned int *>(ws + 32);
+    args.max_groups = gp ? gp->max_groups : 0u;
+    args.gchunk_pages = gp ? pl.gchunk_pages : 1u;
+    args.max_gchunks = pl.max_gchunks;
+    args.slots = pl.slots;
     // Persistent grid: two CTAs per SM (the shared-memory limit), never
     // more CTAs than there are items to hand out.
     uint64_t ctas = (args.n_items + kWarps - 1) / kWarps;
@@ -614,6 +1057,40 @@ extern "C" int rt_paged_decode_attention(const rt_attn_params_t *p, const void *
     case 4: return launch_g<4>(map, args, grid, s);
     default: return launch_g<8>(map, args, grid, s);
     }
+}
+
+}  // namespace
+
+extern "C" int rt_paged_decode_attention(const rt_attn_params_t *p, const void *q,
+                                         const void *kv_arena, const int32_t *page_table,
+                                         const int32_t *seq_lens, float *out, void *workspace,
+                                         size_t workspace_bytes, void *stream)
+{
+    return launch_attention(p, nullptr, q, kv_arena, page_table, seq_lens, nullptr, nullptr,
+                            nullptr, out, workspace, workspace_bytes, stream);
+}
+
+extern "C" size_t rt_attn_grouped_workspace_bytes(const rt_attn_params_t *p,
+                                                  const rt_attn_group_params_t *gp)
+{
+    Plan pl;
+    if (!gp)
+        return rt_attn_workspace_bytes(p);
+    return make_plan(p, &pl, gp) == RT_OK ? pl.total : 0;
+}
+
+extern "C" int rt_paged_decode_attention_grouped(
+    const rt_attn_params_t *p, const rt_attn_group_params_t *gp, const void *q,
+    const void *kv_arena, const int32_t *page_table, const int32_t *seq_lens,
+    const rt_attn_group_t *groups, const uint32_t *n_groups, const uint32_t *skip_pages,
+    float *out, void *workspace, size_t workspace_bytes, void *stream)
+{
+    if (!gp) {
+        rt::set_error("attention: null group params");
+        return RT_EINVAL;
+    }
+    return launch_attention(p, gp, q, kv_arena, page_table, seq_lens, groups, n_groups,
+                            skip_pages, out, workspace, workspace_bytes, stream);
 }
 
 extern "C" int rt_attn_workspace_error(void *workspace, void *stream, int32_t *code)

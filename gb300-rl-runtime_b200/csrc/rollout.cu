@@ -64,7 +64,7 @@ struct SlotExt {
     int32_t cow_src;
     uint64_t seed;
     uint32_t prefix;  // shared-prefix id + 1, 0 = none
-    uint32_t pad;
+    uint32_t shared;  // full prefix pages at the head of the page table (shared, read-only)
 };
 
 struct Dev {
@@ -89,6 +89,11 @@ struct Dev {
     float *logits;        // [max_slots][vocab]
     uint32_t *pf_len, *pf_np, *pf_off;
     int32_t *pf_pages;
+    // shared-prefix attention groups, rebuilt by every schedule pass
+    rt_attn_group_t *groups;  // [max_groups]
+    uint32_t *n_groups;       // [1]
+    uint32_t *skip;           // [max_slots]
+    uint32_t max_groups;      // 0 = per-sequence attention only
 };
 
 __device__ __forceinline__ float reward_for(const Dev &d, uint32_t request_lo, uint32_t tokens)
@@ -177,8 +182,78 @@ struct SchedShared {
     uint32_t fin[kSched];
     uint32_t fin_tokens[kSched];
     uint32_t fin_req[kSched];
+    alignas(16) uint32_t key[kSched];  // grouping key per slot (prefix id + 1, 0 = none)
+    uint32_t gid[kSched];              // group index, at the group's leader slot
+    uint32_t warp_leaders[kSched / 32];
     uint32_t stop, n_fin;
 };
+
+// Shared-prefix groups for the attention.  Active slots decoding from the
+// same prefix, in slot order, are cut into groups of up to 16 (the first
+// of each run of 16 is the leader; a lone slot stays ungrouped).  Groups
+// are numbered in leader slot order, members listed in slot order, so the
+// table is a pure function of the slot state.  All kSched threads call it.
+__device__ void build_groups(const Dev &d, SchedShared &sh, uint32_t key, uint32_t shared)
+{
+    const uint32_t s = threadIdx.x;
+    sh.key[s] = key;
+    __syncthreads();
+    uint32_t rank = 0, leader = s, block_n = 0;
+    if (key) {
+        const uint4 *k4 = reinterpret_cast<const uint4 *>(sh.key);
+        for (uint32_t t4 = 0; t4 < kSched / 4u; t4++) {
+            const uint4 k = k4[t4];
+            const uint32_t kk[4] = {k.x, k.y, k.z, k.w};
+#pragma unroll
+            for (uint32_t j = 0; j < 4u; j++) {
+                const uint32_t t = t4 * 4u + j;
+                if (kk[j] != key)
+                    continue;
+                if (t < s) {
+                    if ((rank & 15u) == 0u)
+                        leader = t;
+                    rank++;
+                } else if (t > s && block_n < 16u) {
+                    block_n++;  // same-key slots after s (capped)
+                }
+            }
+        }
+        if ((rank & 15u) == 0u)
+            leader = s;
+    }
+    // members of this slot's run of 16 (valid at the leader: itself + later ones)
+    const uint32_t n_mem = min(16u, 1u + block_n);
+    const bool is_leader = key && leader == s && n_mem >= 2u;
+    const unsigned ballot = __ballot_sync(0xffffffffu, is_leader);
+    const uint32_t lane = s & 31u, warp = s >> 5;
+    if (lane == 0)
+        sh.warp_leaders[warp] = (uint32_t)__popc(ballot);
+    __syncthreads();
+    uint32_t before = 0, total = 0;
+    for (uint32_t w = 0; w < kSched / 32u; w++) {
+        before += w < warp ? sh.warp_leaders[w] : 0u;
+        total += sh.warp_leaders[w];
+    }
+    const uint32_t gid = before + (uint32_t)__popc(ballot & ((1u << lane) - 1u));
+    if (is_leader) {
+        sh.gid[s] = gid;
+        if (gid < d.max_groups) {
+            d.groups[gid].n_members = n_mem;
+            d.groups[gid].shared_pages = shared;
+        }
+    }
+    __syncthreads();
+    // a non-leader belongs to a group iff its leader leads one (>= 2 members)
+    const bool member = key && (is_leader || leader != s);
+    const uint32_t g = member ? sh.gid[leader] : 0u;
+    const bool in_group = member && g < d.max_groups;
+    if (in_group)
+        d.groups[g].members[rank & 15u] = s;
+    if (s < d.max_slots)
+        d.skip[s] = in_group ? shared : 0u;
+    if (s == 0)
+        *d.n_groups = min(total, d.max_groups);
+}
 
 // One pass of the reference rollout_worker loop (see file comment).
 // Returns true when the loop must stop.  All 256 threads call it.
@@ -273,6 +348,7 @@ __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
                 const uint32_t full_pages = ctx / 16u;
                 for (uint32_t i = 0; i < full_pages && i < np; i++)
                     pt[i] = d.pf_pages[off + i];
+                e.shared = e.prefix ? min(full_pages, np) : 0u;
                 uint32_t next = 0;
                 if ((ctx & 15u) && full_pages < np) {
                     e.cow_src = d.pf_pages[off + full_pages];
@@ -363,6 +439,10 @@ __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
         }
     }
     const uint32_t n_act = __syncthreads_count(act);
+    if (full && d.max_groups) {
+        const bool key_ok = act && d.ext[s].prefix != 0u && d.ext[s].shared != 0u;
+        build_groups(d, sh, key_ok ? d.ext[s].prefix : 0u, key_ok ? d.ext[s].shared : 0u);
+    }
 
     // 5. loop control
     if (s == 0) {
@@ -402,9 +482,15 @@ schedule_kernel(const Dev d, cudaGraphConditionalHandle handle, int in_graph)
     const bool stop = schedule_pass(d, sh);
     if (threadIdx.x == 0) {
         if (stop) {
+            // The decode chain of this pass still runs: make it a no-op.
             d.ctl->stop = 1u;
-            for (uint32_t s = 0; s < d.max_slots; s++)
+            for (uint32_t s = 0; s < d.max_slots; s++) {
                 d.enable[s] = 0u;
+                if (d.seq_lens)
+                    d.seq_lens[s] = 0;
+            }
+            if (d.max_groups)
+                *d.n_groups = 0u;
         }
         if (in_graph)
             cudaGraphSetConditional(handle, stop ? 0u : 1u);
@@ -525,6 +611,7 @@ struct rt_rollout {
     int64_t *priv_blocks;  // host list of reserved arena blocks (released on destroy)
     uint32_t n_priv;
     rt_attn_params_t ap;
+    rt_attn_group_params_t gp;
     void *attn_ws;
     size_t attn_ws_bytes;
     uint32_t pf_used;
@@ -547,8 +634,12 @@ int launch_decode(rt_rollout *e, cudaStream_t st, cudaEvent_t *ev)
     prepare_kernel<<<d.max_slots, 256, 0, st>>>(d);
     if (ev)
         cudaEventRecord(ev[1], st);
-    int rc = rt_paged_decode_attention(&e->ap, d.q, d.arena, d.page_table, d.seq_lens, d.attn_out,
-                                       e->attn_ws, e->attn_ws_bytes, st);
+    int rc = d.max_groups
+                 ? rt_paged_decode_attention_grouped(&e->ap, &e->gp, d.q, d.arena, d.page_table,
+                                                     d.seq_lens, d.groups, d.n_groups, d.skip,
+                                                     d.attn_out, e->attn_ws, e->attn_ws_bytes, st)
+                 : rt_paged_decode_attention(&e->ap, d.q, d.arena, d.page_table, d.seq_lens,
+                                             d.attn_out, e->attn_ws, e->attn_ws_bytes, st);
     if (rc != RT_OK)
         return rc;
     if (ev)
@@ -622,7 +713,8 @@ void engine_free(rt_rollout *e)
         cudaStreamDestroy(e->cap);
     void *bufs[] = {e->d.io, e->d.ctl, e->d.ext, e->d.page_table, e->d.priv, e->d.seq_lens,
                     e->d.enable, e->d.srows, e->d.tokens, e->d.q, e->d.attn_out, e->d.logits,
-                    e->d.pf_len, e->d.pf_np, e->d.pf_off, e->d.pf_pages, e->attn_ws};
+                    e->d.pf_len, e->d.pf_np, e->d.pf_off, e->d.pf_pages, e->d.groups,
+                    e->d.n_groups, e->d.skip, e->attn_ws};
     for (void *p : bufs)
         if (p)
             cudaFree(p);
@@ -712,6 +804,12 @@ extern "C" int rt_rollout_create(const rt_rollout_config_t *cfg, KVArena *arena,
         ok(dalloc(&d.pf_np, npf));
         ok(dalloc(&d.pf_off, npf));
         ok(dalloc(&d.pf_pages, cfg->max_prefix_pages ? cfg->max_prefix_pages : 1u));
+        if (cfg->prefix_attention == RT_PREFIX_ATTN_GROUPED) {
+            d.max_groups = (S + 1u) / 2u;  // groups have at least two members
+            ok(dalloc(&d.groups, d.max_groups));
+            ok(dalloc(&d.n_groups, 1));
+            ok(dalloc(&d.skip, S));
+        }
     }
     if (err != cudaSuccess) {
         engine_free(e);
@@ -753,7 +851,12 @@ extern "C" int rt_rollout_create(const rt_rollout_config_t *cfg, KVArena *arena,
         e->ap.scale = 0.08838834764831845f;  // 1/sqrt(128)
         e->ap.chunk_pages = cfg->chunk_pages;
         e->ap.kv_evict_first = 0u;  // group members re-read shared prefix pages
-        e->attn_ws_bytes = rt_attn_workspace_bytes(&e->ap);
+        e->gp.max_groups = d.max_groups;
+        e->gp.max_shared_pages = d.maxp;
+        e->gp.chunk_pages = 0u;
+        e->gp.reserved = 0u;
+        e->attn_ws_bytes = d.max_groups ? rt_attn_grouped_workspace_bytes(&e->ap, &e->gp)
+                                        : rt_attn_workspace_bytes(&e->ap);
         if (e->attn_ws_bytes == 0) {
             engine_free(e);
             return RT_EINVAL;
@@ -888,6 +991,31 @@ static int rollout_setup(rt_rollout_t *e, const rt_rollout_io_t *io, cudaStream_
 extern "C" int rt_rollout_profile(rt_rollout_t *e, const rt_rollout_io_t *io, void *stream,
                                   rt_rollout_profile_t *out)
 {
+    return rt_rollout_profile_hook(e, io, stream, out, nullptr, nullptr);
+}
+
+extern "C" int rt_rollout_buffers(rt_rollout_t *e, rt_rollout_buffers_t *out)
+{
+    if (!e || !out || e->cfg.decode_mode != RT_ROLLOUT_DECODE_FULL) {
+        rt::set_error("rollout_buffers: needs a full-decode engine and an output struct");
+        return RT_EINVAL;
+    }
+    out->q = e->d.q;
+    out->attn_out = e->d.attn_out;
+    out->page_table = e->d.page_table;
+    out->seq_lens = e->d.seq_lens;
+    out->groups = e->d.groups;
+    out->n_groups = e->d.n_groups;
+    out->skip_pages = e->d.skip;
+    out->max_pages = e->d.maxp;
+    out->max_groups = e->d.max_groups;
+    return RT_OK;
+}
+
+extern "C" int rt_rollout_profile_hook(rt_rollout_t *e, const rt_rollout_io_t *io, void *stream,
+                                       rt_rollout_profile_t *out, rt_rollout_pass_hook_t hook,
+                                       void *user)
+{
     if (!e || !out || e->cfg.decode_mode != RT_ROLLOUT_DECODE_FULL) {
         rt::set_error("rollout_profile: needs a full-decode engine and an output struct");
         return RT_EINVAL;
@@ -957,6 +1085,8 @@ extern "C" int rt_rollout_profile(rt_rollout_t *e, const rt_rollout_io_t *io, vo
         out->sample_rows += active;
         out->attn_launches += active ? 1u : 0u;
         if (c.stop || c.error)
+            break;
+        if (hook && hook(user, pass) != 0)
             break;
     }
     for (auto &x : ev)

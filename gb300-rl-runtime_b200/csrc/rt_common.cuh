@@ -148,6 +148,15 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi)
     return *reinterpret_cast<uint32_t *>(&v);
 }
 
+// Two-term bf16 split of a pair: (a, b) ~= hi + lo with hi = RN(a, b) and
+// lo = RN of the residual, so a product against bf16 operands accumulated
+// as hi.V + lo.V keeps about 16 mantissa bits of a and b instead of 8.
+__device__ __forceinline__ void split_bf16x2(float a, float b, uint32_t &hi, uint32_t &lo)
+{
+    hi = pack_bf16x2(a, b);
+    lo = pack_bf16x2(a - __uint_as_float(hi << 16), b - __uint_as_float(hi & 0xFFFF0000u));
+}
+
 // Philox4x32-10 (Salmon et al., SC'11).
 __host__ __device__ __forceinline__ void philox4x32_10(uint32_t c0, uint32_t c1, uint32_t c2,
                                                        uint32_t c3, uint32_t k0, uint32_t k1,

@@ -100,10 +100,56 @@ int rt_paged_decode_attention_noalloc(const rt_attn_params_t *p,
                                       const int32_t *page_table, const int32_t *seq_lens,
                                       float *out, void *stream);
 
+/* Shared-prefix ("cascade") decode attention.  In a GRPO group every
+ * rollout starts from the same prompt, so its sequences' page tables begin
+ * with the same pages (the copy-on-write prefix of kv_prefix.h).  A group
+ * record lists such sequences; their common full pages are read from HBM once
+ * per group and each page is multiplied against every member's queries in
+ * one tensor-core tile (16 query rows = 16/G sequences x G heads), instead of
+ * once per sequence.  The sequences' remaining pages are processed as in
+ * rt_paged_decode_attention and the two parts merged exactly (log-sum-exp),
+ * so the result equals rt_paged_decode_attention's to fp32 rounding.
+ *
+ * Contract (device-side violations set error 4 and are otherwise skipped):
+ *  - members[i] < num_seqs, 1 <= n_members <= 16, a sequence in at most one
+ *    live group;
+ *  - page_table[m][0 .. shared_pages) is the same for every member m (the
+ *    pages are taken from members[0]'s row) and shared_pages * 16 <=
+ *    seq_lens[m];
+ *  - skip_pages[m] == shared_pages for every member, 0 for a sequence in no
+ *    group, and shared_pages <= gp->max_shared_pages.
+ * groups[0 .. *n_groups) are live; n_groups and skip_pages are read on the
+ * device, so a CUDA graph can rebuild them every step. */
+typedef struct {
+    uint32_t n_members;
+    uint32_t shared_pages;       /* full 16-token pages common to all members */
+    uint32_t members[16];        /* sequence indices */
+} rt_attn_group_t;
+
+typedef struct {
+    uint32_t max_groups;         /* capacity of the groups array */
+    uint32_t max_shared_pages;   /* bound on every shared_pages */
+    uint32_t chunk_pages;        /* shared pages per work item; 0 = auto (8) */
+    uint32_t reserved;
+} rt_attn_group_params_t;
+
+size_t rt_attn_grouped_workspace_bytes(const rt_attn_params_t *p,
+                                       const rt_attn_group_params_t *gp);
+
+int rt_paged_decode_attention_grouped(const rt_attn_params_t *p,
+                                      const rt_attn_group_params_t *gp,
+                                      const void *q, const void *kv_arena,
+                                      const int32_t *page_table, const int32_t *seq_lens,
+                                      const rt_attn_group_t *groups, const uint32_t *n_groups,
+                                      const uint32_t *skip_pages,
+                                      float *out, void *workspace, size_t workspace_bytes,
+                                      void *stream);
+
 /* Read back (and clear) the device error word of a workspace.  0 = no
  * error; otherwise RT_EDEVICE-class codes: 1 = seq_len above
  * max_seq_len / page capacity, 2 = page index outside the arena,
- * 3 = pipeline wait timed out.  Synchronises the stream. */
+ * 3 = pipeline wait timed out, 4 = group record breaks the contract of
+ * rt_paged_decode_attention_grouped.  Synchronises the stream. */
 int rt_attn_workspace_error(void *workspace, void *stream, int32_t *code);
 
 /* Grid/tile parameters the launcher picked for these params (for tests and
@@ -196,6 +242,9 @@ uint32_t rt_sample_uniform24(uint64_t seed, uint32_t rollout_id, uint64_t step);
 #define RT_ROLLOUT_DECODE_FULL  1u
 #define RT_REWARD_MOCK          0u   /* (tokens & 0xFF) / 255 (reference) */
 #define RT_REWARD_PHILOX        1u   /* U(0,1): Philox(key = reward_seed, ctr = {request low 32}) */
+#define RT_PREFIX_ATTN_GROUPED       0u  /* default: rt_paged_decode_attention_grouped over
+                                           groups of slots with the same prefix */
+#define RT_PREFIX_ATTN_PER_SEQUENCE  1u  /* rt_paged_decode_attention, every slot on its own */
 
 typedef struct {
     uint32_t num_q_heads;       /* 32 */
@@ -215,6 +264,7 @@ typedef struct {
     uint64_t max_passes;        /* stop with RT_ETIMEOUT after this many passes */
     uint32_t idle_timeout_ms;   /* ring source: stop with RT_ETIMEOUT when idle this long */
     uint32_t chunk_pages;       /* attention split-K chunk (0 = auto) */
+    uint32_t prefix_attention;  /* RT_PREFIX_ATTN_*: how slots sharing a prefix attend */
 } rt_rollout_config_t;
 
 typedef struct {
@@ -275,6 +325,27 @@ typedef struct {
  * kernel (same kernels and data as rt_rollout_launch); synchronous. */
 int rt_rollout_profile(rt_rollout_t *eng, const rt_rollout_io_t *io, void *stream,
                        rt_rollout_profile_t *out);
+
+/* rt_rollout_profile with a callback after every pass (the stream is
+ * synchronised, the engine's buffers hold that pass's inputs and outputs);
+ * a nonzero return stops the replay there.  For inspection and tests. */
+typedef int (*rt_rollout_pass_hook_t)(void *user, uint64_t pass);
+int rt_rollout_profile_hook(rt_rollout_t *eng, const rt_rollout_io_t *io, void *stream,
+                            rt_rollout_profile_t *out, rt_rollout_pass_hook_t hook, void *user);
+
+/* Device buffers of a full-decode engine (read them between passes). */
+typedef struct {
+    const void *q;                   /* bf16 [max_slots][num_q_heads][128] */
+    const float *attn_out;           /* fp32 [max_slots][num_q_heads][128] */
+    const int32_t *page_table;       /* [max_slots][max_pages] */
+    const int32_t *seq_lens;         /* [max_slots] (0 = idle this pass) */
+    const rt_attn_group_t *groups;   /* [max_groups]; NULL when not grouped */
+    const uint32_t *n_groups;        /* [1] */
+    const uint32_t *skip_pages;      /* [max_slots] */
+    uint32_t max_pages;
+    uint32_t max_groups;
+} rt_rollout_buffers_t;
+int rt_rollout_buffers(rt_rollout_t *eng, rt_rollout_buffers_t *out);
 
 /* Wait for the loop (stream sync) and read its counters. */
 int rt_rollout_wait(rt_rollout_t *eng, void *stream, rt_rollout_stats_t *stats);

@@ -197,3 +197,87 @@ def test_loop_reports_context_overflow(pkg, orc, cuda):
     st = eng.wait(check_errors=False)
     assert st["error"] == pkg.RT_EDEVICE
     eng.close()
+
+
+class _DevView:
+    """A raw device pointer seen as a torch tensor (no copy, no ownership)."""
+
+    def __init__(self, ptr, shape, typestr):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                         "data": (int(ptr), False), "version": 3}
+
+
+def _dev(ptr, shape, typestr, cuda):
+    return torch.as_tensor(_DevView(ptr, shape, typestr), device=cuda)
+
+
+def _check_pass(pkg, orc, cuda, eng, arena, S, maxp, want_groups):
+    b = eng.buffers()
+    lens = _dev(b.seq_lens, (S,), "<i4", cuda).cpu().numpy()
+    pt = _dev(b.page_table, (S, maxp), "<i4", cuda).cpu().numpy()
+    q = _dev(b.q, (S, 32, 128), "<i2", cuda).cpu().numpy().view(np.uint16)
+    out = _dev(b.attn_out, (S, 32, 128), "<f4", cuda).cpu().numpy()
+    act = lens > 0
+    assert act.any()
+    kv = arena.buf.view(torch.int16).cpu().numpy().view(np.uint16)
+    ref = orc.paged_gqa_attention(q, kv, np.where(act[:, None], pt, 0), lens, 32, 8, 128 ** -0.5)
+    err = np.abs(out - ref) * act[:, None, None]
+    bad = err > 2e-3 + 1e-2 * np.abs(ref)
+    if bad.any():
+        s_, h_, d_ = np.argwhere(bad)[0]
+        raise AssertionError(
+            f"{bad.sum()} bad in slots {sorted(set(np.argwhere(bad)[:, 0].tolist()))}; first "
+            f"slot {s_} head {h_} dim {d_}: got {out[s_, h_, d_]:.5f} ref {ref[s_, h_, d_]:.5f} "
+            f"len {lens[s_]} row0 {pt[s_, :4].tolist()}")
+    if not want_groups:
+        assert not b.groups
+        return 0
+    ng = int(_dev(b.n_groups, (1,), "<i4", cuda).cpu().numpy()[0])
+    recs = _dev(b.groups, (b.max_groups, 18), "<i4", cuda).cpu().numpy()[:ng]
+    skip = _dev(b.skip_pages, (S,), "<i4", cuda).cpu().numpy()
+    seen = set()
+    for n_mem, shared, *members in recs:
+        mem = members[:n_mem]
+        assert 2 <= n_mem <= 16 and shared >= 1
+        assert list(mem) == sorted(mem) and not seen & set(mem)
+        seen |= set(mem)
+        for m in mem:
+            assert act[m] and skip[m] == shared and lens[m] >= 16 * shared
+            assert np.array_equal(pt[m, :shared], pt[mem[0], :shared])
+    assert all(skip[s] == 0 for s in range(S) if s not in seen)
+    return ng
+
+
+@pytest.mark.parametrize("mode", ["grouped", "per_sequence"])
+def test_loop_attention_matches_oracle(pkg, orc, cuda, mode):
+    """Pass by pass (host-stepped), the loop's attention output equals the
+    oracle on that pass's q, KV arena, page tables and lengths.  Grouped mode
+    also checks the shared-prefix group table the schedule kernel builds:
+    20 + 17 + 3 slots on three prefixes (2, 4 and 18 full pages; the 40- and
+    300-token ones end in a copy-on-write page), 1 on a fourth, 8 without."""
+    S = 64
+    cfg = full_cfg(max_slots=S)
+    cfg["prefix_attention"] = (pkg.RT_PREFIX_ATTN_GROUPED if mode == "grouped"
+                               else pkg.RT_PREFIX_ATTN_PER_SEQUENCE)
+    arena = pkg.DeviceArena(1024)
+    eng = pkg.RolloutEngine(cfg, arena)
+    setup_prefixes(pkg, arena, eng, [40, 64, 300, 32])
+    pfx = np.array([1] * 20 + [2] * 17 + [3] * 3 + [4] + [0] * 8)
+    np.random.default_rng(3).shuffle(pfx)
+    n = len(pfx)
+    reqs = make_requests(orc, n, np.random.default_rng(4).integers(2, 25, size=n), seed=99,
+                         prefix_plus_one=pfx)
+    req_d = torch.from_numpy(reqs.view(np.uint8).copy()).to(cuda)
+    state = torch.zeros(STATE_BYTES, dtype=torch.uint8, device=cuda)
+    checked = []
+
+    def hook(p):
+        if p in (0, 1, 7, 15):
+            checked.append(_check_pass(pkg, orc, cuda, eng, arena, S, 32, mode == "grouped"))
+        return p >= 15
+
+    eng.step(hook, requests=req_d, n_requests=n, state=state)
+    assert len(checked) == 4
+    if mode == "grouped":
+        assert checked[0] == 2 + 1 + 1  # 20 -> 16 + 4; 17 -> 16 + a lone (ungrouped) one; 3
+    eng.close()
