@@ -9,17 +9,23 @@
 //    `chunk_pages` 16-token pages).  Warps never synchronise with each other,
 //    so a warp in its prologue (page ids, Q fragment, first TMA round trip)
 //    overlaps the steady state of the other warps on the SM.  Items are
-//    numbered sequence-fastest: sequences that share prefix pages (a GRPO
-//    group) run side by side and the shared pages come from L2.
+//    numbered head-fastest: the KV heads of one sequence chunk, whose
+//    (page, head) blocks are adjacent in the arena, run side by side.
 //  * Staging: per page the warp's elected lane issues four 2-D TMA tensor
 //    loads (K and V, two 64-column halves each, 128-byte swizzle) into one
 //    8 KiB stage of the warp's 3-stage ring, completion tracked by a
 //    shared-memory mbarrier with transaction bytes (no multicast).
-//  * Math: the G query heads of the KV group form the rows of one
-//    m16n8k16 bf16 tensor-core tile (rows >= G are zero), so S = Q.K^T and
-//    O += P.V are each 16 mma per page; the S accumulator layout is reused
-//    directly as the A operand of P.V.  Softmax runs in registers in the log2
-//    domain with quad shuffles for the row max.
+//  * Math: per page, S^T = K.Q^T and O^T += V^T.P^T on m16n8k16 bf16 tensor
+//    cores with the page's 16 tokens (or 16 head dimensions) as the M rows
+//    and the KV group's G <= 8 query heads as the N = 8 columns: 8 mma for S
+//    and 8 per P term for O.  Softmax runs in registers in the log2 domain
+//    (column max over the 8 lanes of a head); P is split into two bf16 terms
+//    so that P.V keeps ~16 mantissa bits; movmatrix turns the S^T
+//    accumulator into the B operand of the second product.
+//  * Shared prefixes: a separate group kernel reads a GRPO group's common
+//    prefix pages once and multiplies them against all members' queries
+//    (16 query rows = 16/G sequences x G heads per tile); the sequence kernel
+//    starts each grouped sequence from those partials.
 //  * Split-K: the chunks of one (b, h) write unnormalised partials; the last
 //    warp to arrive (per-(b,h) counter) merges them with the log-sum-exp rule
 //    and resets the counter, so no second kernel launch is needed.
@@ -153,23 +159,16 @@ __device__ __forceinline__ void merge_parts(const AttnArgs &a, size_t bh, uint32
     }
 }
 
-// Pages of sequence b that its group covers, as the sequence's own items see
-// it: skip_pages[b] when it fits the sequence and the planned group chunks,
-// else 0 (flagged).  The group items apply the same rule to every member.
-__device__ __forceinline__ uint32_t seq_skip(const AttnArgs &a, uint32_t b, int n_pages)
-{
-    if (!a.skip_pages)
-        return 0u;
-    const uint32_t skip = a.skip_pages[b];
-    if (skip > (uint32_t)n_pages || skip > a.max_gchunks * a.gchunk_pages) {
-        flag_error(a.error, kErrGroup);
-        return 0u;
-    }
-    return skip;
-}
-
 // One warp processes one item; see the file comment.  Returns false when a
 // pipeline wait expired (the warp then stops taking items).
+//
+// The tile is transposed relative to the usual decode formulation, because
+// a KV group has only G <= 8 query heads: S^T = K.Q^T takes the page's 16
+// tokens as the M rows of m16n8k16 and the G heads as its N = 8 columns, and
+// O^T = V^T.P^T takes 16 head dimensions as M and the heads as N.  That is 8
+// mma for S and 8 per P term for O per page, half of what 16-row query tiles
+// (12 of them zero for G = 4) cost.  The S^T accumulator becomes the B
+// operand of the second product through one movmatrix transpose per 8x8 block.
 template <int G>
 __device__ __forceinline__ bool process_item(const CUtensorMap &kv_map, const AttnArgs &a,
                                              uint64_t item, uint32_t stage0, uint8_t *base_ptr,
@@ -178,11 +177,27 @@ __device__ __forceinline__ bool process_item(const CUtensorMap &kv_map, const At
 {
     const int lane = threadIdx.x & 31;
     const uint32_t B = a.num_seqs, Hq = a.num_q_heads, Hkv = a.num_kv_heads;
-    const uint32_t b = (uint32_t)(item % B);
-    const uint64_t rest = item / B;
-    const uint32_t h = (uint32_t)(rest % Hkv);
-    const int chunk = (int)(rest / Hkv);
+    const uint32_t h = (uint32_t)(item % Hkv);
+    const uint64_t rest = item / Hkv;
+    const uint32_t b = (uint32_t)(rest % B);
+    const int chunk = (int)(rest / B);
+    // Independent loads first (length, group coverage, the Q fragment), so
+    // their round trips overlap.
     const int L = a.seq_lens[b];
+    const uint32_t skip_raw = a.skip_pages ? a.skip_pages[b] : 0u;
+    const int r = lane >> 2, q4 = lane & 3;
+    // Q as the B operand (col-major 16 dims x 8 heads): lane holds head r,
+    // dims 16j + 2q4 (+1) and 16j + 8 + 2q4 (+1); heads >= G are zero.
+    uint32_t qb[8][2];
+    {
+        const uint32_t *qrow = reinterpret_cast<const uint32_t *>(
+            a.q + ((size_t)b * Hq + (size_t)h * G + (r < G ? r : 0)) * 128);
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            qb[j][0] = r < G ? qrow[8 * j + q4] : 0u;
+            qb[j][1] = r < G ? qrow[8 * j + 4 + q4] : 0u;
+        }
+    }
 
     if (L < 0 || (uint32_t)L > a.max_seq_len || (uint32_t)L > a.max_pages * 16u) {
         if (lane == 0 && chunk == 0)
@@ -196,7 +211,11 @@ __device__ __forceinline__ bool process_item(const CUtensorMap &kv_map, const At
         return true;
     }
     const int n_pages = (L + 15) >> 4;
-    const int skip = (int)seq_skip(a, b, n_pages);
+    int skip = (int)skip_raw;
+    if (skip_raw > (uint32_t)n_pages || skip_raw > a.max_gchunks * a.gchunk_pages) {
+        flag_error(a.error, kErrGroup);
+        skip = 0;
+    }
     const int cp = (int)a.chunk_pages;
     const uint32_t n_g = (uint32_t)((skip + (int)a.gchunk_pages - 1) / (int)a.gchunk_pages);
     // This sequence's own chunks; a fully covered sequence still has chunk 0,
@@ -206,6 +225,7 @@ __device__ __forceinline__ bool process_item(const CUtensorMap &kv_map, const At
         return true;
     const int p_begin = skip + chunk * cp;
     const int n_mine = max(0, min(n_pages, p_begin + cp) - p_begin);
+    const size_t bh = (size_t)b * Hkv + h;
 
     // Page ids of this item: lane i holds pages i and 32 + i.
     const int32_t *ptab = a.page_table + (size_t)b * a.max_pages + p_begin;
@@ -214,6 +234,54 @@ __device__ __forceinline__ bool process_item(const CUtensorMap &kv_map, const At
         pg_lo = ptab[lane];
     if (lane + 32 < n_mine)
         pg_hi = ptab[lane + 32];
+    // Group partials to start from (chunk 0 of a grouped sequence): lane
+    // owns heads 2q4, 2q4 + 1 and dims 16dd + r, 16dd + r + 8.
+    float o[8][4];
+#pragma unroll
+    for (int n = 0; n < 8; n++)
+        o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+    const int hd0 = 2 * q4, hd1 = 2 * q4 + 1;
+    if (chunk == 0 && n_g) {
+        const size_t pi0 = (bh * a.slots) * G;
+        for (uint32_t k = 0; k < n_g; k++) {
+            if (hd0 < G)
+                m0 = fmaxf(m0, a.part_ml[(pi0 + (size_t)k * G + hd0) * 2]);
+            if (hd1 < G)
+                m1 = fmaxf(m1, a.part_ml[(pi0 + (size_t)k * G + hd1) * 2]);
+        }
+        for (uint32_t k = 0; k < n_g; k++) {
+            const size_t pa = pi0 + (size_t)k * G;
+            float w0 = 0.0f, w1 = 0.0f;
+            const float *s0 = a.part_o + (pa + (hd0 < G ? hd0 : 0)) * 128 + r;
+            const float *s1 = a.part_o + (pa + (hd1 < G ? hd1 : 0)) * 128 + r;
+            if (hd0 < G) {
+                const float2 ml = *reinterpret_cast<const float2 *>(&a.part_ml[(pa + hd0) * 2]);
+                w0 = rt::fast_exp2(ml.x - m0);
+                l0 += ml.y * w0;
+            }
+            if (hd1 < G) {
+                const float2 ml = *reinterpret_cast<const float2 *>(&a.part_ml[(pa + hd1) * 2]);
+                w1 = rt::fast_exp2(ml.x - m1);
+                l1 += ml.y * w1;
+            }
+#pragma unroll
+            for (int dd = 0; dd < 8; dd++) {
+                if (hd0 < G) {
+                    o[dd][0] += s0[16 * dd] * w0;
+                    o[dd][2] += s0[16 * dd + 8] * w0;
+                }
+                if (hd1 < G) {
+                    o[dd][1] += s1[16 * dd] * w1;
+                    o[dd][3] += s1[16 * dd + 8] * w1;
+                }
+            }
+        }
+        // every lane of a head's 8-lane column holds the full sum; the
+        // column reduction at the end adds 8 copies
+        l0 *= 0.125f;
+        l1 *= 0.125f;
+    }
     const bool bad = (lane < n_mine && (pg_lo < 0 || (uint64_t)pg_lo >= a.arena_pages)) ||
                      (lane + 32 < n_mine && (pg_hi < 0 || (uint64_t)pg_hi >= a.arena_pages));
     if (bad) {
@@ -243,57 +311,11 @@ __device__ __forceinline__ bool process_item(const CUtensorMap &kv_map, const At
     for (int i = 0; i < n_mine && i < kStages; i++)
         issue(i, i);
 
-    // Q fragment: row r = lane/4 is query head h*G + r (rows >= G are zero);
-    // k-step j covers dims 16j..16j+15.
-    const int r = lane >> 2, q4 = lane & 3;
-    uint32_t qa[8][4];
-    {
-        const uint32_t *qrow = reinterpret_cast<const uint32_t *>(
-            a.q + ((size_t)b * Hq + (size_t)h * G + (r < G ? r : 0)) * 128);
-#pragma unroll
-        for (int j = 0; j < 8; j++) {
-            qa[j][0] = r < G ? qrow[8 * j + q4] : 0u;
-            qa[j][2] = r < G ? qrow[8 * j + 4 + q4] : 0u;
-            qa[j][1] = 0u;
-            qa[j][3] = 0u;
-        }
-    }
-
-    float o[16][4];
-#pragma unroll
-    for (int n = 0; n < 16; n++)
-        o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
-    float m_run = -INFINITY, l_run = 0.0f;
-    const size_t bh = (size_t)b * Hkv + h;
-    if (chunk == 0 && n_g && r < G) {
-        // Start from the group's prefix partials (written by the group
-        // kernel): o = sum_k o_k 2^(m_k - M), l = sum_k l_k 2^(m_k - M).
-        const size_t pi0 = (bh * a.slots) * G + r;
-        for (uint32_t k = 0; k < n_g; k++)
-            m_run = fmaxf(m_run, a.part_ml[(pi0 + (size_t)k * G) * 2]);
-        for (uint32_t k = 0; k < n_g; k++) {
-            const size_t pi = pi0 + (size_t)k * G;
-            const float2 ml = *reinterpret_cast<const float2 *>(&a.part_ml[pi * 2]);
-            const float wt = rt::fast_exp2(ml.x - m_run);
-            l_run += ml.y * wt;
-            const float *src = a.part_o + pi * 128 + 2 * q4;
-            float2 v[16];
-#pragma unroll
-            for (int n = 0; n < 16; n++)
-                v[n] = *reinterpret_cast<const float2 *>(src + n * 8);
-#pragma unroll
-            for (int n = 0; n < 16; n++) {
-                o[n][0] += v[n].x * wt;
-                o[n][1] += v[n].y * wt;
-            }
-        }
-        l_run *= 0.25f;  // every lane of the quad adds the full sum; the quad reduction below sums 4x
-    }
-
-    // Per-lane ldmatrix row offsets (swizzled chunk index = chunk ^ row%8).
+    // ldmatrix row addresses (swizzled 16-byte chunk = chunk ^ row%8): lane
+    // l points at token 8*((l/8)>>1) + l%8 and the (l/8)&1 half of a 16-dim
+    // block, so the four 8x8 matrices are (tokens lo|hi) x (dims lo|hi).
     const int mi = lane >> 3, rr = lane & 7;
-    const uint32_t k_row = (uint32_t)((((mi >> 1) << 3) + rr) * 128);
-    const uint32_t v_row = (uint32_t)((((mi & 1) << 3) + rr) * 128);
+    const uint32_t t_row = (uint32_t)((((mi >> 1) << 3) + rr) * 128);
 
     for (int i = 0; i < n_mine; i++) {
         const int s = i % kStages;
@@ -324,61 +346,69 @@ __device__ __forceinline__ bool process_item(const CUtensorMap &kv_map, const At
             __syncwarp();
         }
 
-        // S = Q K^T for 16 tokens (two n-tiles of 8).
-        float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        // S^T = K Q^T: 16 tokens x 8 heads, two accumulators (even / odd
+        // 16-dim steps) to halve the dependent mma chain.
+        float se[4] = {0.f, 0.f, 0.f, 0.f}, so[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int j = 0; j < 8; j++) {
             const int c = ((j & 3) << 1) + (mi & 1);
-            const uint32_t addr = st + (uint32_t)((j >> 2) * 2048) + k_row + (uint32_t)((c ^ rr) << 4);
+            const uint32_t addr = st + (uint32_t)((j >> 2) * 2048) + t_row + (uint32_t)((c ^ rr) << 4);
             uint32_t k0, k1, k2, k3;
             rt::ldsm_x4(addr, k0, k1, k2, k3);
-            rt::mma_bf16_16816(sc[0], qa[j], k0, k1);
-            rt::mma_bf16_16816(sc[1], qa[j], k2, k3);
+            const uint32_t ka[4] = {k0, k2, k1, k3};
+            if (j & 1)
+                rt::mma_bf16_16816(so, ka, qb[j][0], qb[j][1]);
+            else
+                rt::mma_bf16_16816(se, ka, qb[j][0], qb[j][1]);
         }
-
-        float x0 = sc[0][0] * a.scale_log2, x1 = sc[0][1] * a.scale_log2;
-        float x2 = sc[1][0] * a.scale_log2, x3 = sc[1][1] * a.scale_log2;
+        // lane: tokens r (x0: head hd0, x1: head hd1) and r + 8 (x2, x3)
+        float x0 = (se[0] + so[0]) * a.scale_log2, x1 = (se[1] + so[1]) * a.scale_log2;
+        float x2 = (se[2] + so[2]) * a.scale_log2, x3 = (se[3] + so[3]) * a.scale_log2;
         if (valid < 16) {
-            const int t0 = 2 * q4;
-            if (t0 >= valid) x0 = -INFINITY;
-            if (t0 + 1 >= valid) x1 = -INFINITY;
-            if (t0 + 8 >= valid) x2 = -INFINITY;
-            if (t0 + 9 >= valid) x3 = -INFINITY;
+            if (r >= valid) x0 = x1 = -INFINITY;
+            if (r + 8 >= valid) x2 = x3 = -INFINITY;
         }
-        float mx = fmaxf(fmaxf(x0, x1), fmaxf(x2, x3));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-        const float m_new = fmaxf(m_run, mx);
-        const float corr = rt::fast_exp2(m_run - m_new);
-        const float p0 = rt::fast_exp2(x0 - m_new), p1 = rt::fast_exp2(x1 - m_new);
-        const float p2 = rt::fast_exp2(x2 - m_new), p3 = rt::fast_exp2(x3 - m_new);
-        l_run = l_run * corr + ((p0 + p1) + (p2 + p3));
-        m_run = m_new;
+        // max over the 16 tokens of each head: the 8 lanes of a column
+        float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
 #pragma unroll
-        for (int n = 0; n < 16; n++) {
-            o[n][0] *= corr;
-            o[n][1] *= corr;
+        for (int off = 4; off < 32; off <<= 1) {
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
         }
-        // P in two bf16 terms (hi + lo): P.V then carries ~16 mantissa bits
-        // of the probabilities, not bf16's 8.
+        const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
+        const float c0 = rt::fast_exp2(m0 - n0), c1 = rt::fast_exp2(m1 - n1);
+        const float p0 = rt::fast_exp2(x0 - n0), p1 = rt::fast_exp2(x1 - n1);
+        const float p2 = rt::fast_exp2(x2 - n0), p3 = rt::fast_exp2(x3 - n1);
+        l0 = l0 * c0 + (p0 + p2);
+        l1 = l1 * c1 + (p1 + p3);
+        m0 = n0;
+        m1 = n1;
+#pragma unroll
+        for (int dd = 0; dd < 8; dd++) {
+            o[dd][0] *= c0;
+            o[dd][2] *= c0;
+            o[dd][1] *= c1;
+            o[dd][3] *= c1;
+        }
+        // P^T as the B operand: transpose the two 8x8 (token x head) blocks;
+        // P in two bf16 terms (hi + lo) keeps ~16 mantissa bits.
         uint32_t h01, l01, h23, l23;
         rt::split_bf16x2(p0, p1, h01, l01);
         rt::split_bf16x2(p2, p3, h23, l23);
-        const uint32_t pa[4] = {h01, 0u, h23, 0u};
-        const uint32_t pl[4] = {l01, 0u, l23, 0u};
+        const uint32_t bh0 = rt::movmatrix_trans(h01), bh1 = rt::movmatrix_trans(h23);
+        const uint32_t bl0 = rt::movmatrix_trans(l01), bl1 = rt::movmatrix_trans(l23);
 
-        // O += P V over 128 dims (16 n-tiles of 8, two per ldmatrix.x4).
+        // O^T += V^T P^T: 8 tiles of 16 dims; ldmatrix.trans of the V tile
+        // gives the (dims x tokens) A fragments directly.
 #pragma unroll
         for (int dd = 0; dd < 8; dd++) {
-            const int c = ((dd & 3) << 1) + (mi >> 1);
+            const int c = ((dd & 3) << 1) + (mi & 1);
             const uint32_t addr =
-                st + 4096u + (uint32_t)((dd >> 2) * 2048) + v_row + (uint32_t)((c ^ rr) << 4);
-            uint32_t v0, v1, v2, v3;
-            rt::ldsm_x4_trans(addr, v0, v1, v2, v3);
-            rt::mma_bf16_16816(o[2 * dd], pa, v0, v1);
-            rt::mma_bf16_16816(o[2 * dd + 1], pa, v2, v3);
-            rt::mma_bf16_16816(o[2 * dd], pl, v0, v1);
-            rt::mma_bf16_16816(o[2 * dd + 1], pl, v2, v3);
+                st + 4096u + (uint32_t)((dd >> 2) * 2048) + t_row + (uint32_t)((c ^ rr) << 4);
+            uint32_t v[4];
+            rt::ldsm_x4_trans(addr, v[0], v[1], v[2], v[3]);
+            rt::mma_bf16_16816(o[dd], v, bh0, bh1);
+            rt::mma_bf16_16816(o[dd], v, bl0, bl1);
         }
         __syncwarp();
         if (i + kStages < n_mine) {
@@ -390,29 +420,52 @@ __device__ __forceinline__ bool process_item(const CUtensorMap &kv_map, const At
             issue(i + kStages, s);
         }
     }
-    l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
-    l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+        l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+    }
 
     if (n_chunks == 1) {
-        if (r < G) {
-            const float inv = 1.0f / l_run;
-            float *dst = a.out + ((size_t)b * Hq + (size_t)h * G + r) * 128 + 2 * q4;
+        const float i0 = 1.0f / l0, i1 = 1.0f / l1;
+        float *d0 = a.out + ((size_t)b * Hq + (size_t)h * G + hd0) * 128 + r;
+        float *d1 = a.out + ((size_t)b * Hq + (size_t)h * G + hd1) * 128 + r;
 #pragma unroll
-            for (int n = 0; n < 16; n++)
-                *reinterpret_cast<float2 *>(dst + n * 8) = make_float2(o[n][0] * inv, o[n][1] * inv);
+        for (int dd = 0; dd < 8; dd++) {
+            if (hd0 < G) {
+                d0[16 * dd] = o[dd][0] * i0;
+                d0[16 * dd + 8] = o[dd][2] * i0;
+            }
+            if (hd1 < G) {
+                d1[16 * dd] = o[dd][1] * i1;
+                d1[16 * dd + 8] = o[dd][3] * i1;
+            }
         }
         return true;
     }
 
     // ---- split-K: write this chunk's partial; the last part to arrive merges ----
-    if (r < G) {
-        const size_t pi = (bh * a.slots + a.max_gchunks + chunk) * G + r;
-        float *dst = a.part_o + pi * 128 + 2 * q4;
+    {
+        const size_t pi = (bh * a.slots + a.max_gchunks + chunk) * G;
+        float *d0 = a.part_o + (pi + hd0) * 128 + r;
+        float *d1 = a.part_o + (pi + hd1) * 128 + r;
 #pragma unroll
-        for (int n = 0; n < 16; n++)
-            *reinterpret_cast<float2 *>(dst + n * 8) = make_float2(o[n][0], o[n][1]);
-        if (q4 == 0)
-            *reinterpret_cast<float2 *>(a.part_ml + pi * 2) = make_float2(m_run, l_run);
+        for (int dd = 0; dd < 8; dd++) {
+            if (hd0 < G) {
+                d0[16 * dd] = o[dd][0];
+                d0[16 * dd + 8] = o[dd][2];
+            }
+            if (hd1 < G) {
+                d1[16 * dd] = o[dd][1];
+                d1[16 * dd + 8] = o[dd][3];
+            }
+        }
+        if (r == 0) {
+            if (hd0 < G)
+                *reinterpret_cast<float2 *>(a.part_ml + (pi + hd0) * 2) = make_float2(m0, l0);
+            if (hd1 < G)
+                *reinterpret_cast<float2 *>(a.part_ml + (pi + hd1) * 2) = make_float2(m1, l1);
+        }
     }
     __threadfence();
     __syncwarp();
