@@ -180,7 +180,10 @@ __device__ __forceinline__ bool process_item(const CUtensorMap &kv_map, const At
     const uint32_t h = (uint32_t)(item % Hkv);
     const uint64_t rest = item / Hkv;
     const uint32_t b = (uint32_t)(rest % B);
-    const int chunk = (int)(rest / B);
+    // Chunks are handed out from the highest index down: chunk 0 holds the
+    // remainder pages and every other chunk is full, so the last items of a
+    // launch are the short ones and the tail stays short.
+    const int chunk = (int)a.max_chunks - 1 - (int)(rest / B);
     // Independent loads first (length, group coverage, the Q fragment), so
     // their round trips overlap.
     const int L = a.seq_lens[b];
@@ -223,8 +226,9 @@ __device__ __forceinline__ bool process_item(const CUtensorMap &kv_map, const At
     const int n_chunks = max((n_pages - skip + cp - 1) / cp, n_g ? 1 : 0);
     if (chunk >= n_chunks)
         return true;
-    const int p_begin = skip + chunk * cp;
-    const int n_mine = max(0, min(n_pages, p_begin + cp) - p_begin);
+    const int rem = (n_pages - skip) - (n_chunks - 1) * cp;  // pages of chunk 0 (may be 0)
+    const int p_begin = skip + (chunk == 0 ? 0 : rem + (chunk - 1) * cp);
+    const int n_mine = chunk == 0 ? max(0, rem) : cp;
     const size_t bh = (size_t)b * Hkv + h;
 
     // Page ids of this item: lane i holds pages i and 32 + i.
