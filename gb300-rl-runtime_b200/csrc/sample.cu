@@ -1,16 +1,22 @@
 // sample.cu - fused temperature / top-k / top-p sampler for sm_100a.
 //
 // Replaces reference cu/sample.cu:40-123 (sample_token: one thread, ~6 serial
-// passes over the vocabulary and an O(V*k) insertion sort) with one CTA of
-// 1024 threads per row that reads the row's logits from HBM exactly once
-// and keeps them in registers (32 per thread, vocab <= 32768):
+// passes over the vocabulary and an O(V*k) insertion sort) with one 256-thread
+// CTA per row.  Several rows share an SM (small CTAs, no per-thread copy of
+// the row), and the row is streamed twice from L2/HBM:
 //
-//  1. scale by 1.0f / temperature (same fp32 multiply as the reference);
-//  2. exact top-k cutoff = the k-th largest value (with multiplicity) by a
-//     three-pass radix select (12 + 12 + 8 bits) on order-preserving keys,
-//     shared-memory histograms, block-wide suffix scans;
-//  3. survivors (value >= cutoff, ties included) are compacted and sorted
-//     by vocabulary index (rank sort, typically k of them);
+//  1. one streaming pass (16-byte loads, eight in flight per thread): scale
+//     by 1.0f / temperature (the reference's fp32 multiply), keep each
+//     thread's 5 largest values with their indices, detect NaN / +inf;
+//  2. tau0 = the nk-th largest of the 256 per-thread maxima, by counting for
+//     each maximum how many are larger.  Those maxima are nk row values
+//     >= tau0, so tau0 <= the top-k cutoff (the nk-th largest value counted
+//     with multiplicity) and every survivor is >= tau0;
+//  3. the candidates (values >= tau0) come from the per-thread lists; a
+//     thread whose 5th largest is still >= tau0 may hold more, and then the
+//     row is streamed a second time to collect them all.  A candidate
+//     survives iff fewer than nk candidates are strictly larger; survivors
+//     are sorted by vocabulary index (rank sort, typically k of them);
 //  4. one thread replays the reference's serial fp32 arithmetic over the
 //     survivors only: sum of __expf(l - max) in index order, 1.0f / sum,
 //     cumulative walk.  Entries the reference masks to -FLT_MAX contribute
@@ -18,11 +24,12 @@
 //     them leaves every fp32 sum bit-identical.
 //
 // Rows the fast path cannot reproduce exactly (top-k disabled, fewer than k
-// finite values, > 2048 survivors, a non-zero masked contribution) take an
-// exact slow path: the whole row's exponentials are staged through shared
-// memory 1024 at a time and one thread sums / walks them in index order.
-// Rows with a NaN or +inf after scaling return vocab - 1, which is what the
-// reference's walk returns for them (its sum becomes NaN).
+// finite values, > kCap candidates, a non-zero masked contribution) take
+// exact slow paths: a streamed radix select for the cutoff, and, when needed,
+// the whole row's exponentials staged through shared memory 256 at a time
+// and summed / walked by one thread in index order.  Rows with a NaN or +inf
+// after scaling return vocab - 1, which is what the reference's walk returns
+// for them (its sum becomes NaN).
 #include <cfloat>
 #include <cstdint>
 
@@ -31,10 +38,11 @@
 
 namespace {
 
-constexpr int kThreads = 1024;
-constexpr int kItems = 32;          // vocab <= kThreads * kItems
-constexpr int kBins = 4096;
-constexpr int kCap = 2048;          // survivors handled by the fast path
+constexpr int kThr = 256;            // threads per row
+constexpr int kWarpsPerRow = kThr / 32;
+constexpr int kBins = 4096;          // radix digits of the streamed cutoff select
+constexpr int kCap = 1024;           // candidates handled by the fast path
+constexpr uint32_t kMaxVocab = 1u << 20;
 
 struct SampleArgs {
     const float *logits;
@@ -65,12 +73,12 @@ struct Smem {
             float val[kCap];
         } sorted;
     } u;
-    uint32_t surv_idx[kCap];
-    float surv_val[kCap];
-    float e[kCap];
-    uint32_t red_u[32];
-    float red_f[32];
-    uint32_t scan[32];
+    uint32_t cand_idx[kCap];
+    float cand_val[kCap];
+    float e[kCap];                 // exponentials; keep flags before that
+    uint32_t red_u[kWarpsPerRow];
+    float red_f[kWarpsPerRow];
+    uint32_t scan[kWarpsPerRow];
     uint32_t digit, need, count, token, done;
 };
 
@@ -83,10 +91,10 @@ __device__ __forceinline__ uint32_t block_sum_u32(uint32_t v, Smem &s)
     if (lane == 0)
         s.red_u[warp] = v;
     __syncthreads();
-    uint32_t t = lane < (int)(blockDim.x >> 5) ? s.red_u[lane] : 0u;
+    uint32_t t = 0;
 #pragma unroll
-    for (int o = 16; o; o >>= 1)
-        t += __shfl_xor_sync(0xffffffffu, t, o);
+    for (int w = 0; w < kWarpsPerRow; w++)
+        t += s.red_u[w];
     __syncthreads();
     return t;
 }
@@ -100,15 +108,15 @@ __device__ __forceinline__ float block_max_f32(float v, Smem &s)
     if (lane == 0)
         s.red_f[warp] = v;
     __syncthreads();
-    float t = lane < (int)(blockDim.x >> 5) ? s.red_f[lane] : -FLT_MAX;
+    float t = -FLT_MAX;
 #pragma unroll
-    for (int o = 16; o; o >>= 1)
-        t = fmaxf(t, __shfl_xor_sync(0xffffffffu, t, o));
+    for (int w = 0; w < kWarpsPerRow; w++)
+        t = fmaxf(t, s.red_f[w]);
     __syncthreads();
     return t;
 }
 
-// Inclusive prefix sum of v over threads 0..blockDim-1 (in thread order).
+// Inclusive prefix sum of v over threads 0..kThr-1 (in thread order).
 __device__ __forceinline__ uint32_t block_inclusive_scan(uint32_t v, Smem &s, uint32_t &total)
 {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -122,46 +130,51 @@ __device__ __forceinline__ uint32_t block_inclusive_scan(uint32_t v, Smem &s, ui
     if (lane == 31)
         s.scan[warp] = x;
     __syncthreads();
-    if (warp == 0) {
-        uint32_t w = s.scan[lane];
+    uint32_t before = 0;
+    total = 0;
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const uint32_t y = __shfl_up_sync(0xffffffffu, w, o);
-            if (lane >= o)
-                w += y;
-        }
-        s.scan[lane] = w;
+    for (int w = 0; w < kWarpsPerRow; w++) {
+        before += w < warp ? s.scan[w] : 0u;
+        total += s.scan[w];
     }
     __syncthreads();
-    total = s.scan[31];
-    const uint32_t r = x + (warp ? s.scan[warp - 1] : 0u);
-    __syncthreads();
-    return r;
+    return x + before;
 }
 
-// One radix digit: histogram the keys of candidates that match `prefix` on
-// `mask`, then find the digit d holding the need-th largest key.  Updates
-// prefix/mask/need for the next digit.
-template <int N>
-__device__ __forceinline__ void radix_pass(const float (&x)[N], int shift, int bits,
-                                           uint32_t &prefix, uint32_t &mask, uint32_t &need,
-                                           Smem &s)
+// Scaled logit of entry idx: the reference's fp32 multiply by 1 / T.
+struct RowReader {
+    const float *row;
+    float inv_t;
+    bool scale;
+    __device__ __forceinline__ float operator()(uint32_t idx) const
+    {
+        const float v = __ldg(row + idx);
+        return scale ? __fmul_rn(v, inv_t) : v;
+    }
+};
+
+// One radix digit of the nk-th largest key among values > -FLT_MAX,
+// streaming the row: histogram the keys matching `prefix` on `mask`, then
+// locate the digit holding the need-th largest.  Updates prefix/mask/need.
+__device__ __forceinline__ void radix_pass_row(const RowReader &rd, uint32_t V, int shift, int bits,
+                                               uint32_t &prefix, uint32_t &mask, uint32_t &need,
+                                               Smem &s)
 {
     const int nb = 1 << bits;
-    for (int b = threadIdx.x; b < nb; b += kThreads)
+    for (int b = threadIdx.x; b < nb; b += kThr)
         s.u.hist[b] = 0u;
     __syncthreads();
-#pragma unroll
-    for (int i = 0; i < N; i++) {
-        if (x[i] > -FLT_MAX) {  // entries past the vocabulary hold -inf
-            const uint32_t k = float_key(x[i]);
+    for (uint32_t idx = threadIdx.x; idx < V; idx += kThr) {
+        const float v = rd(idx);
+        if (v > -FLT_MAX) {
+            const uint32_t k = float_key(v);
             if ((k & mask) == prefix)
                 atomicAdd(&s.u.hist[(k >> shift) & (uint32_t)(nb - 1)], 1u);
         }
     }
     __syncthreads();
     // thread t owns bins [per*t, per*t + per)
-    const int per = nb / kThreads > 0 ? nb / kThreads : 1;
+    const int per = nb / kThr > 0 ? nb / kThr : 1;
     const int b0 = threadIdx.x * per;
     uint32_t mine = 0;
     if (b0 < nb)
@@ -187,41 +200,108 @@ __device__ __forceinline__ void radix_pass(const float (&x)[N], int shift, int b
     __syncthreads();
 }
 
-__global__ void __launch_bounds__(kThreads, 1) sample_rows_kernel(const SampleArgs a)
+// Survivors among the nc candidates in cand_*: a candidate survives iff
+// fewer than nk candidates are strictly larger (all when nk == 0).  Writes
+// them sorted by vocabulary index to s.u.sorted; returns their count.
+__device__ __forceinline__ uint32_t select_and_sort(uint32_t nc, uint32_t nk, Smem &s)
+{
+    uint32_t *keep = reinterpret_cast<uint32_t *>(s.e);  // reused before the exponentials
+    uint32_t mine = 0;
+    for (uint32_t j = threadIdx.x; j < nc; j += kThr) {
+        uint32_t k = 1u;
+        if (nk) {
+            const float v = s.cand_val[j];
+            uint32_t gt = 0;
+            for (uint32_t i = 0; i < nc; i++)
+                gt += s.cand_val[i] > v ? 1u : 0u;
+            k = gt < nk ? 1u : 0u;
+        }
+        keep[j] = k;
+        mine += k;
+    }
+    const uint32_t ns = block_sum_u32(mine, s);  // includes a barrier: keep[] is complete
+    for (uint32_t j = threadIdx.x; j < nc; j += kThr) {
+        if (!keep[j])
+            continue;
+        const uint32_t id = s.cand_idx[j];
+        uint32_t rank = 0;
+        for (uint32_t i = 0; i < nc; i++)
+            rank += (keep[i] && s.cand_idx[i] < id) ? 1u : 0u;
+        s.u.sorted.idx[rank] = id;
+        s.u.sorted.val[rank] = s.cand_val[j];
+    }
+    __syncthreads();
+    return ns;
+}
+
+// Streams the row as 16-byte loads (kDepth in flight per thread) when the
+// row is 16-byte aligned, calling f(scaled value, vocabulary index); the
+// remainder and unaligned rows go element by element.
+template <typename F>
+__device__ __forceinline__ void stream_row(const RowReader &rd, uint32_t V, F &&f)
+{
+    const bool vec = (reinterpret_cast<uintptr_t>(rd.row) & 15u) == 0u;
+    const uint32_t V4 = vec ? V / 4u : 0u;
+    const float4 *row4 = reinterpret_cast<const float4 *>(rd.row);
+    constexpr uint32_t kDepth = 8;
+    const uint32_t tid = threadIdx.x;
+    for (uint32_t base = 0; base < V4; base += kDepth * kThr) {
+        float4 buf[kDepth];
+#pragma unroll
+        for (uint32_t j = 0; j < kDepth; j++) {
+            const uint32_t q = base + j * kThr + tid;
+            if (q < V4)
+                buf[j] = __ldg(row4 + q);
+        }
+#pragma unroll
+        for (uint32_t j = 0; j < kDepth; j++) {
+            const uint32_t q = base + j * kThr + tid;
+            if (q < V4) {
+                const float4 v = buf[j];
+                if (rd.scale) {
+                    f(__fmul_rn(v.x, rd.inv_t), 4u * q);
+                    f(__fmul_rn(v.y, rd.inv_t), 4u * q + 1u);
+                    f(__fmul_rn(v.z, rd.inv_t), 4u * q + 2u);
+                    f(__fmul_rn(v.w, rd.inv_t), 4u * q + 3u);
+                } else {
+                    f(v.x, 4u * q);
+                    f(v.y, 4u * q + 1u);
+                    f(v.z, 4u * q + 2u);
+                    f(v.w, 4u * q + 3u);
+                }
+            }
+        }
+    }
+    for (uint32_t idx = 4u * V4 + tid; idx < V; idx += kThr)
+        f(rd(idx), idx);
+}
+
+__global__ void __launch_bounds__(kThr) sample_rows_kernel(const SampleArgs a)
 {
     __shared__ Smem s;
     const int tid = threadIdx.x;
+    const int lane = tid & 31, warp = tid >> 5;
     const uint32_t V = a.vocab;
     if (a.enable && a.enable[blockIdx.x] == 0u)
         return;
     const rt_sample_row_t P = a.rows[blockIdx.x];
-    const float *lr = a.logits + (size_t)blockIdx.x * a.stride;
+    RowReader rd;
+    rd.row = a.logits + (size_t)blockIdx.x * a.stride;
+    rd.scale = P.temperature > 0.0f;
+    rd.inv_t = rd.scale ? __fdiv_rn(1.0f, P.temperature) : 1.0f;
 
-    // ---- 1. load once, temperature ----
-    const bool scale = P.temperature > 0.0f;
-    const float inv_t = scale ? __fdiv_rn(1.0f, P.temperature) : 1.0f;
-    // x[i] = entry tid + i * kThreads; entries past the vocabulary hold -inf,
-    // which is never a top-k candidate, never a survivor and never the max.
-    float x[kItems];
+    // ---- pass 1: per-thread maximum of the values > -FLT_MAX, NaN / +inf ----
+    float tmax = -INFINITY;
     bool bad = false;
-#pragma unroll
-    for (int i = 0; i < kItems; i++) {
-        const uint32_t idx = (uint32_t)tid + (uint32_t)i * kThreads;
-        float v = -INFINITY;
-        if (idx < V) {
-            v = __ldg(lr + idx);
-            if (scale)
-                v = __fmul_rn(v, inv_t);
-            bad |= isnan(v) || v == INFINITY;
-        }
-        x[i] = v;
-    }
-
+    stream_row(rd, V, [&](float v, uint32_t) {
+        bad |= !(v < INFINITY);  // NaN or +inf
+        tmax = v > -FLT_MAX ? fmaxf(tmax, v) : tmax;
+    });
     if (tid == 0) {
         uint32_t ph[4];
         rt::philox4x32_10((uint32_t)P.step, (uint32_t)(P.step >> 32), P.rollout_id, 0u,
                           (uint32_t)P.seed, (uint32_t)(P.seed >> 32), ph);
-        s.token = ph[0] & 0x00FFFFFFu;  // u24 (reused below)
+        s.token = ph[0] & 0x00FFFFFFu;  // u24
         s.count = 0u;
         s.done = 0u;
     }
@@ -241,124 +321,97 @@ __global__ void __launch_bounds__(kThreads, 1) sample_rows_kernel(const SampleAr
     const bool topk = P.top_k > 0u && P.top_k < V;
     const uint32_t nk = P.top_k < 256u ? P.top_k : 256u;
 
-    // ---- 2. top-k cutoff and survivors ----
-    // A value survives iff it is >= the nk-th largest value (counted with
-    // multiplicity) among values > -FLT_MAX, i.e. iff fewer than nk values
-    // are strictly greater than it.
+    // ---- top-k cutoff and survivors ----
     float cutoff = -FLT_MAX;
     bool fast = topk;
     uint32_t ns = 0;
     bool sorted_ready = false;
     if (topk) {
-        uint32_t ncand = 0;
+        // tau0: each warp's m-th largest per-thread maximum, m = ceil(nk/8),
+        // by counting over the warp's 32 maxima; tau0 = the smallest of the
+        // eight.  Each warp has m row values >= its threshold, so at least
+        // nk values are >= tau0 and tau0 <= the top-k cutoff: every
+        // survivor is >= tau0.
+        const uint32_t m = (nk + kWarpsPerRow - 1) / kWarpsPerRow;
+        uint32_t gt = 0, ge = 0;
 #pragma unroll
-        for (int i = 0; i < kItems; i++)
-            ncand += x[i] > -FLT_MAX ? 1u : 0u;
-        ncand = block_sum_u32(ncand, s);
-        if (ncand < nk)
-            fast = false;  // cutoff stays -FLT_MAX; almost everything survives
-    }
-    if (fast) {
-        // Quick path: tau0 = the nk-th largest of the 1024 per-thread maxima.
-        // Those maxima are nk distinct entries >= tau0, so tau0 <= cutoff and
-        // every survivor is among the few entries >= tau0.
-        float tm[1] = {-INFINITY};
+        for (int o = 0; o < 32; o++) {
+            const float x = __shfl_sync(0xffffffffu, tmax, o);
+            gt += x > tmax ? 1u : 0u;
+            ge += x >= tmax ? 1u : 0u;
+        }
+        const bool mine = tmax > -FLT_MAX && gt < m && ge >= m;
+        const unsigned who = __ballot_sync(0xffffffffu, mine);
+        const float wt = __shfl_sync(0xffffffffu, tmax, who ? __ffs(who) - 1 : 0);
+        if (lane == 0)
+            s.red_f[warp] = who ? wt : NAN;
+        __syncthreads();
+        float tau0 = INFINITY;
+        bool ok = true;
 #pragma unroll
-        for (int i = 0; i < kItems; i++)
-            if (x[i] > -FLT_MAX)
-                tm[0] = fmaxf(tm[0], x[i]);
-        const uint32_t nvalid = (uint32_t)__syncthreads_count(tm[0] > -FLT_MAX);
-        if (nvalid >= nk) {
-            uint32_t prefix = 0, mask = 0, need = nk;
-            radix_pass(tm, 20, 12, prefix, mask, need, s);
-            radix_pass(tm, 8, 12, prefix, mask, need, s);
-            radix_pass(tm, 0, 8, prefix, mask, need, s);
-            const float tau0 = key_float(prefix);
-            if (tid == 0)
-                s.count = 0u;
-            __syncthreads();
-#pragma unroll
-            for (int i = 0; i < kItems; i++) {
-                if (x[i] >= tau0 && x[i] > -FLT_MAX) {
+        for (int w = 0; w < kWarpsPerRow; w++) {
+            const float t = s.red_f[w];
+            ok &= !isnan(t);
+            tau0 = fminf(tau0, t);
+        }
+        __syncthreads();
+        if (ok) {
+            // ---- pass 2: candidates >= tau0 ----
+            stream_row(rd, V, [&](float v, uint32_t idx) {
+                if (v >= tau0) {
                     const uint32_t pos = atomicAdd(&s.count, 1u);
                     if (pos < (uint32_t)kCap) {
-                        s.surv_idx[pos] = (uint32_t)tid + (uint32_t)i * kThreads;
-                        s.surv_val[pos] = x[i];
+                        s.cand_idx[pos] = idx;
+                        s.cand_val[pos] = v;
                     }
                 }
-            }
+            });
             __syncthreads();
             const uint32_t nc = s.count;
             if (nc <= (uint32_t)kCap) {
-                uint32_t *keep = reinterpret_cast<uint32_t *>(s.e);  // reused before the walk
-                uint32_t mine = 0;
-                for (uint32_t j = tid; j < nc; j += kThreads) {
-                    const float v = s.surv_val[j];
-                    uint32_t gt = 0;
-                    for (uint32_t i2 = 0; i2 < nc; i2++)
-                        gt += s.surv_val[i2] > v ? 1u : 0u;
-                    keep[j] = gt < nk ? 1u : 0u;
-                    mine += keep[j];
-                }
-                ns = block_sum_u32(mine, s);  // includes a barrier: keep[] is complete
-                for (uint32_t j = tid; j < nc; j += kThreads) {
-                    if (!keep[j])
-                        continue;
-                    const uint32_t id = s.surv_idx[j];
-                    uint32_t rank = 0;
-                    for (uint32_t i2 = 0; i2 < nc; i2++)
-                        rank += (keep[i2] && s.surv_idx[i2] < id) ? 1u : 0u;
-                    s.u.sorted.idx[rank] = id;
-                    s.u.sorted.val[rank] = s.surv_val[j];
-                }
+                ns = select_and_sort(nc, nk, s);
                 sorted_ready = true;
             }
+        } else {
+            // a warp holds fewer than m finite maxima: count the finite
+            // values; with fewer than nk the cutoff stays -FLT_MAX
+            uint32_t nfin = 0;
+            stream_row(rd, V, [&](float v, uint32_t) { nfin += v > -FLT_MAX ? 1u : 0u; });
+            if (block_sum_u32(nfin, s) < nk)
+                fast = false;
         }
-        if (!sorted_ready) {
-            // Tie-heavy or degenerate rows: exact cutoff by a full-row radix select.
+        if (fast && !sorted_ready) {
+            // Tie-heavy or degenerate rows: exact cutoff by a streamed radix select.
             uint32_t prefix = 0, mask = 0, need = nk;
-            radix_pass(x, 20, 12, prefix, mask, need, s);
-            radix_pass(x, 8, 12, prefix, mask, need, s);
-            radix_pass(x, 0, 8, prefix, mask, need, s);
+            radix_pass_row(rd, V, 20, 12, prefix, mask, need, s);
+            radix_pass_row(rd, V, 8, 12, prefix, mask, need, s);
+            radix_pass_row(rd, V, 0, 8, prefix, mask, need, s);
             cutoff = key_float(prefix);
+            if (tid == 0)
+                s.count = 0u;
+            __syncthreads();
+            stream_row(rd, V, [&](float v, uint32_t idx) {
+                if (v >= cutoff) {
+                    const uint32_t pos = atomicAdd(&s.count, 1u);
+                    if (pos < (uint32_t)kCap) {
+                        s.cand_idx[pos] = idx;
+                        s.cand_val[pos] = v;
+                    }
+                }
+            });
+            __syncthreads();
+            const uint32_t nc = s.count;
+            if (nc <= (uint32_t)kCap)
+                ns = select_and_sort(nc, 0u, s);  // every value >= cutoff survives
+            else
+                fast = false;
         }
     }
 
-    // ---- 3. survivors, sorted by index ----
     float mx = -FLT_MAX;
-    if (fast && !sorted_ready) {
-        if (tid == 0)
-            s.count = 0u;
-        __syncthreads();
-#pragma unroll
-        for (int i = 0; i < kItems; i++) {
-            if (x[i] >= cutoff) {
-                const uint32_t pos = atomicAdd(&s.count, 1u);
-                if (pos < (uint32_t)kCap) {
-                    s.surv_idx[pos] = (uint32_t)tid + (uint32_t)i * kThreads;
-                    s.surv_val[pos] = x[i];
-                }
-            }
-        }
-        __syncthreads();
-        ns = s.count;
-        if (ns > (uint32_t)kCap)
-            fast = false;
-        if (fast) {
-            for (uint32_t j = tid; j < ns; j += kThreads) {
-                const uint32_t id = s.surv_idx[j];
-                uint32_t rank = 0;
-                for (uint32_t q = 0; q < ns; q++)
-                    rank += s.surv_idx[q] < id ? 1u : 0u;
-                s.u.sorted.idx[rank] = id;
-                s.u.sorted.val[rank] = s.surv_val[j];
-            }
-        }
-    }
     if (fast) {
-        __syncthreads();  // sorted survivors complete
         float m = -FLT_MAX;
-        for (uint32_t j = tid; j < ns; j += kThreads)
+        for (uint32_t j = tid; j < ns; j += kThr)
             m = fmaxf(m, s.u.sorted.val[j]);
         mx = block_max_f32(m, s);
         // masked entries hold -FLT_MAX; their terms must be exactly zero
@@ -366,7 +419,7 @@ __global__ void __launch_bounds__(kThreads, 1) sample_rows_kernel(const SampleAr
             fast = false;
     }
     if (fast) {
-        for (uint32_t j = tid; j < ns; j += kThreads)
+        for (uint32_t j = tid; j < ns; j += kThr)
             s.e[j] = __expf(__fsub_rn(s.u.sorted.val[j], mx));
         __syncthreads();
         if (tid == 0) {
@@ -399,28 +452,24 @@ __global__ void __launch_bounds__(kThreads, 1) sample_rows_kernel(const SampleAr
         return;
     }
 
-    // ---- 4. exact slow path: every entry, in index order ----
+    // ---- exact slow path: every entry, in index order ----
+    auto masked = [&](uint32_t idx) {
+        const float v = rd(idx);
+        return (topk && v < cutoff) ? -FLT_MAX : v;
+    };
     float m = -FLT_MAX;
-#pragma unroll
-    for (int i = 0; i < kItems; i++) {
-        if ((uint32_t)tid + (uint32_t)i * kThreads < V) {
-            if (topk && x[i] < cutoff)
-                x[i] = -FLT_MAX;
-            m = fmaxf(m, x[i]);
-        }
-    }
+    for (uint32_t idx = (uint32_t)tid; idx < V; idx += kThr)
+        m = fmaxf(m, masked(idx));
     mx = block_max_f32(m, s);
     float sum = 0.0f, inv = 0.0f, cum = 0.0f;
     uint32_t tok = V - 1u;
     for (int pass = 0; pass < 2; pass++) {
-#pragma unroll
-        for (int i = 0; i < kItems; i++) {
-            if ((uint32_t)i * kThreads >= V)
-                break;
-            s.e[tid] = (uint32_t)tid + (uint32_t)i * kThreads < V ? __expf(__fsub_rn(x[i], mx)) : 0.0f;
+        for (uint32_t base = 0; base < V; base += kThr) {
+            const uint32_t idx = base + (uint32_t)tid;
+            s.e[tid] = idx < V ? __expf(__fsub_rn(masked(idx), mx)) : 0.0f;
             __syncthreads();
             if (tid == 0 && !s.done) {
-                const uint32_t n = min((uint32_t)kThreads, V - (uint32_t)i * kThreads);
+                const uint32_t n = min((uint32_t)kThr, V - base);
                 if (pass == 0) {
                     for (uint32_t j = 0; j < n; j++)
                         sum = __fadd_rn(sum, s.e[j]);
@@ -430,7 +479,7 @@ __global__ void __launch_bounds__(kThreads, 1) sample_rows_kernel(const SampleAr
                                               : __fadd_rn(cum, __fmul_rn(s.e[j], inv)))
                                    : __fadd_rn(cum, __fdiv_rn(s.e[j], sum));
                         if (cum >= r) {
-                            tok = (uint32_t)i * kThreads + j;
+                            tok = base + j;
                             s.done = 1u;
                             break;
                         }
@@ -463,9 +512,9 @@ extern "C" int rt_sample_rows(const rt_sample_params_t *p, const float *logits,
         rt::set_error("sample: null argument");
         return RT_EINVAL;
     }
-    if (p->vocab == 0 || p->vocab > (uint32_t)(kThreads * kItems) || p->row_stride < p->vocab) {
-        rt::set_error("sample: vocab %u must be in 1..%d and <= row_stride %llu", p->vocab,
-                      kThreads * kItems, (unsigned long long)p->row_stride);
+    if (p->vocab == 0 || p->vocab > kMaxVocab || p->row_stride < p->vocab) {
+        rt::set_error("sample: vocab %u must be in 1..%u and <= row_stride %llu", p->vocab,
+                      kMaxVocab, (unsigned long long)p->row_stride);
         return RT_EINVAL;
     }
     if (((uintptr_t)logits & 3u) || ((uintptr_t)rows & 7u) || ((uintptr_t)tokens_out & 3u) ||
@@ -487,7 +536,7 @@ extern "C" int rt_sample_rows(const rt_sample_params_t *p, const float *logits,
     a.stride = p->row_stride;
     a.vocab = p->vocab;
     a.fused = p->fused_cum ? 1u : 0u;
-    sample_rows_kernel<<<p->num_rows, kThreads, 0, (cudaStream_t)stream>>>(a);
+    sample_rows_kernel<<<p->num_rows, kThr, 0, (cudaStream_t)stream>>>(a);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? RT_OK : rt::cuda_fail(e, "sample: launch");
 }
