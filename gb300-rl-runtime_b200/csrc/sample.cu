@@ -32,17 +32,21 @@
 // for them (its sum becomes NaN).
 #include <cfloat>
 #include <cstdint>
+#include <mutex>
 
 #include "rlrt.h"
 #include "rt_common.cuh"
+#include "rt_internal.h"
 
 namespace {
 
-constexpr int kThr = 256;            // threads per row
+constexpr int kThr = 512;            // threads per row
 constexpr int kWarpsPerRow = kThr / 32;
 constexpr int kBins = 4096;          // radix digits of the streamed cutoff select
 constexpr int kCap = 1024;           // candidates handled by the fast path
 constexpr uint32_t kMaxVocab = 1u << 20;
+
+constexpr uint32_t kKeyCacheMax = 49152;  // vocab whose 16-bit key copy fits in shared memory
 
 struct SampleArgs {
     const float *logits;
@@ -52,6 +56,7 @@ struct SampleArgs {
     uint64_t stride;
     uint32_t vocab;
     uint32_t fused;
+    uint32_t keycache;  // pass 1 keeps the top 16 bits of every key in shared memory
 };
 
 __device__ __forceinline__ uint32_t float_key(float v)
@@ -202,31 +207,49 @@ __device__ __forceinline__ void radix_pass_row(const RowReader &rd, uint32_t V, 
 
 // Survivors among the nc candidates in cand_*: a candidate survives iff
 // fewer than nk candidates are strictly larger (all when nk == 0).  Writes
-// them sorted by vocabulary index to s.u.sorted; returns their count.
+// them sorted by vocabulary index to s.u.sorted; returns their count.  The
+// candidate arrays are padded to a multiple of 4 (-inf, index ~0) so that
+// the all-pairs scans read them 16 bytes at a time.
 __device__ __forceinline__ uint32_t select_and_sort(uint32_t nc, uint32_t nk, Smem &s)
 {
     uint32_t *keep = reinterpret_cast<uint32_t *>(s.e);  // reused before the exponentials
+    const uint32_t n4 = (nc + 3u) & ~3u;
+    for (uint32_t j = nc + threadIdx.x; j < n4; j += kThr) {
+        s.cand_val[j] = -INFINITY;
+        s.cand_idx[j] = 0xFFFFFFFFu;
+        keep[j] = 0u;
+    }
+    __syncthreads();
+    const float4 *cv4 = reinterpret_cast<const float4 *>(s.cand_val);
     uint32_t mine = 0;
     for (uint32_t j = threadIdx.x; j < nc; j += kThr) {
         uint32_t k = 1u;
         if (nk) {
             const float v = s.cand_val[j];
             uint32_t gt = 0;
-            for (uint32_t i = 0; i < nc; i++)
-                gt += s.cand_val[i] > v ? 1u : 0u;
+            for (uint32_t i = 0; i < n4 / 4u; i++) {
+                const float4 c = cv4[i];
+                gt += (c.x > v ? 1u : 0u) + (c.y > v ? 1u : 0u) + (c.z > v ? 1u : 0u) +
+                      (c.w > v ? 1u : 0u);
+            }
             k = gt < nk ? 1u : 0u;
         }
         keep[j] = k;
         mine += k;
     }
     const uint32_t ns = block_sum_u32(mine, s);  // includes a barrier: keep[] is complete
+    const uint4 *ci4 = reinterpret_cast<const uint4 *>(s.cand_idx);
+    const uint4 *kp4 = reinterpret_cast<const uint4 *>(keep);
     for (uint32_t j = threadIdx.x; j < nc; j += kThr) {
         if (!keep[j])
             continue;
         const uint32_t id = s.cand_idx[j];
         uint32_t rank = 0;
-        for (uint32_t i = 0; i < nc; i++)
-            rank += (keep[i] && s.cand_idx[i] < id) ? 1u : 0u;
+        for (uint32_t i = 0; i < n4 / 4u; i++) {
+            const uint4 c = ci4[i], f = kp4[i];
+            rank += (f.x && c.x < id ? 1u : 0u) + (f.y && c.y < id ? 1u : 0u) +
+                    (f.z && c.z < id ? 1u : 0u) + (f.w && c.w < id ? 1u : 0u);
+        }
         s.u.sorted.idx[rank] = id;
         s.u.sorted.val[rank] = s.cand_val[j];
     }
@@ -276,9 +299,10 @@ __device__ __forceinline__ void stream_row(const RowReader &rd, uint32_t V, F &&
         f(rd(idx), idx);
 }
 
-__global__ void __launch_bounds__(kThr) sample_rows_kernel(const SampleArgs a)
+__global__ void __launch_bounds__(kThr, 2) sample_rows_kernel(const SampleArgs a)
 {
     __shared__ Smem s;
+    extern __shared__ uint16_t s_keys[];  // [vocab] top 16 key bits (keycache only)
     const int tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5;
     const uint32_t V = a.vocab;
@@ -293,9 +317,12 @@ __global__ void __launch_bounds__(kThr) sample_rows_kernel(const SampleArgs a)
     // ---- pass 1: per-thread maximum of the values > -FLT_MAX, NaN / +inf ----
     float tmax = -INFINITY;
     bool bad = false;
-    stream_row(rd, V, [&](float v, uint32_t) {
+    const bool kc = a.keycache != 0u;
+    stream_row(rd, V, [&](float v, uint32_t idx) {
         bad |= !(v < INFINITY);  // NaN or +inf
         tmax = v > -FLT_MAX ? fmaxf(tmax, v) : tmax;
+        if (kc)
+            s_keys[idx] = (uint16_t)(float_key(v) >> 16);
     });
     if (tid == 0) {
         uint32_t ph[4];
@@ -356,16 +383,46 @@ __global__ void __launch_bounds__(kThr) sample_rows_kernel(const SampleArgs a)
         }
         __syncthreads();
         if (ok) {
-            // ---- pass 2: candidates >= tau0 ----
-            stream_row(rd, V, [&](float v, uint32_t idx) {
-                if (v >= tau0) {
-                    const uint32_t pos = atomicAdd(&s.count, 1u);
-                    if (pos < (uint32_t)kCap) {
-                        s.cand_idx[pos] = idx;
-                        s.cand_val[pos] = v;
+            if (kc) {
+                // ---- candidates from the shared-memory key copy: every
+                // value >= tau0 has a 16-bit key >= tau0's; the few extra
+                // entries of tau0's key bin are below the cutoff and drop
+                // out in the survivor test.  Exact values come from L2. ----
+                const uint32_t thr = float_key(tau0) >> 16;
+                const uint4 *k8 = reinterpret_cast<const uint4 *>(s_keys);
+                for (uint32_t g = (uint32_t)tid; g < (V + 7u) / 8u; g += kThr) {
+                    const uint4 w = k8[g];
+                    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                    for (int h2 = 0; h2 < 4; h2++) {
+#pragma unroll
+                        for (int hh = 0; hh < 2; hh++) {
+                            const uint32_t key = hh ? (ws[h2] >> 16) : (ws[h2] & 0xFFFFu);
+                            const uint32_t idx = 8u * g + 2u * h2 + hh;
+                            if (key >= thr && idx < V) {
+                                const uint32_t pos = atomicAdd(&s.count, 1u);
+                                if (pos < (uint32_t)kCap)
+                                    s.cand_idx[pos] = idx;
+                            }
+                        }
                     }
                 }
-            });
+                __syncthreads();
+                const uint32_t nf = s.count;
+                for (uint32_t j = tid; j < nf && j < (uint32_t)kCap; j += kThr)
+                    s.cand_val[j] = rd(s.cand_idx[j]);
+            } else {
+                // ---- pass 2: candidates >= tau0 ----
+                stream_row(rd, V, [&](float v, uint32_t idx) {
+                    if (v >= tau0) {
+                        const uint32_t pos = atomicAdd(&s.count, 1u);
+                        if (pos < (uint32_t)kCap) {
+                            s.cand_idx[pos] = idx;
+                            s.cand_val[pos] = v;
+                        }
+                    }
+                });
+            }
             __syncthreads();
             const uint32_t nc = s.count;
             if (nc <= (uint32_t)kCap) {
@@ -497,6 +554,27 @@ __global__ void __launch_bounds__(kThr) sample_rows_kernel(const SampleArgs a)
 
 }  // namespace
 
+// Opt in to the key copy's dynamic shared memory, once per device.
+int rt::sample_prepare()
+{
+    static std::mutex mu;
+    static bool done[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess)
+        return rt::cuda_fail(e, "sample: cudaGetDevice");
+    std::lock_guard<std::mutex> lk(mu);
+    if (dev >= 0 && dev < 64 && done[dev])
+        return RT_OK;
+    e = cudaFuncSetAttribute(sample_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)(kKeyCacheMax * 2u));
+    if (e != cudaSuccess)
+        return rt::cuda_fail(e, "sample: cudaFuncSetAttribute");
+    if (dev >= 0 && dev < 64)
+        done[dev] = true;
+    return RT_OK;
+}
+
 extern "C" uint32_t rt_sample_uniform24(uint64_t seed, uint32_t rollout_id, uint64_t step)
 {
     uint32_t o[4];
@@ -536,7 +614,12 @@ extern "C" int rt_sample_rows(const rt_sample_params_t *p, const float *logits,
     a.stride = p->row_stride;
     a.vocab = p->vocab;
     a.fused = p->fused_cum ? 1u : 0u;
-    sample_rows_kernel<<<p->num_rows, kThr, 0, (cudaStream_t)stream>>>(a);
+    a.keycache = 0u;  // the key copy measured slower than a second L2 pass at 32K vocab
+    const size_t dyn = a.keycache ? (((size_t)p->vocab * 2u + 15u) & ~(size_t)15u) : 0u;
+    const int rc = rt::sample_prepare();
+    if (rc != RT_OK)
+        return rc;
+    sample_rows_kernel<<<p->num_rows, kThr, dyn, (cudaStream_t)stream>>>(a);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? RT_OK : rt::cuda_fail(e, "sample: launch");
 }
