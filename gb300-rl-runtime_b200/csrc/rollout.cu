@@ -57,7 +57,10 @@ struct RtCtl {
     uint32_t consumed, admitted, dropped, done, max_active, sentinel;
     int32_t error;
     uint32_t stop;
+    uint32_t groups_ok;   // the group table matches the active slot set
+    uint32_t groups_act;  // active slots when it was built
 };
+static_assert(sizeof(RtCtl) % 8 == 0, "RtCtl is copied as 64-bit words");
 
 struct SlotExt {
     uint32_t row, request_lo, pos, ctx_len, last_token, decoding, cow_rows;
@@ -159,11 +162,79 @@ __device__ bool sink_push(const RtIo &io, RtCtl *ctl, const RolloutDone &rec)
     return true;
 }
 
+constexpr uint32_t kKeyTable = 1024;  // prefix ids grouped through a table (else a slot scan)
+
+// Shared-memory copy of the loop state one schedule pass works on: loaded
+// in two parallel round trips at the start of a pass, stored back at its
+// end, so that the pass's serial steps (admission, retirement, loop
+// control) touch no global memory except the request source and done sink.
+struct SchedShared {
+    GpuRolloutSlot slot[kSched];  // reference state table (slots < max_slots)
+    SlotExt ext[kSched];
+    uint64_t bitmap[(GPU_MAX_ROLLOUTS + 63) / 64];
+    RtCtl ctl;
+    RtIo io;
+    uint32_t fin[kSched];
+    uint32_t fin_tokens[kSched];
+    uint32_t fin_req[kSched];
+    uint32_t key[kSched];          // grouping key per slot (prefix id + 1, 0 = none)
+    uint32_t rank[kSched];         // rank among the active slots with the same key
+    uint32_t kcount[kKeyTable];    // per key: slot count, then first group id
+    uint32_t stop, n_fin;
+};
+
+__device__ __forceinline__ void copy_words(void *dst, const void *src, size_t bytes)
+{
+    uint64_t *d = static_cast<uint64_t *>(dst);
+    const uint64_t *s = static_cast<const uint64_t *>(src);
+    for (size_t i = 0; i < bytes / 8u; i++)
+        d[i] = s[i];
+}
+
+// Load the pass state (all kSched threads).
+__device__ void load_state(const Dev &d, SchedShared &sh, bool with_ext)
+{
+    const uint32_t s = threadIdx.x;
+    // round trip 1: io block, control block, this slot's extension
+    if (s < sizeof(RtIo) / 8u)
+        reinterpret_cast<uint64_t *>(&sh.io)[s] = reinterpret_cast<const uint64_t *>(d.io)[s];
+    else if (s - 32u < sizeof(RtCtl) / 8u)
+        reinterpret_cast<uint64_t *>(&sh.ctl)[s - 32u] = reinterpret_cast<const uint64_t *>(d.ctl)[s - 32u];
+    if (with_ext && s < d.max_slots)
+        copy_words(&sh.ext[s], &d.ext[s], sizeof(SlotExt));
+    __syncthreads();
+    // round trip 2: the reference state table behind io.state
+    GpuRolloutState *st = sh.io.state;
+    if (s < d.max_slots)
+        copy_words(&sh.slot[s], &st->slots[s], sizeof(GpuRolloutSlot));
+    if (s < (GPU_MAX_ROLLOUTS + 63) / 64)
+        sh.bitmap[s] = st->bitmap[s];
+    __syncthreads();
+}
+
+// Store the pass state back (all kSched threads).
+__device__ void store_state(const Dev &d, SchedShared &sh, bool with_ext)
+{
+    const uint32_t s = threadIdx.x;
+    __syncthreads();
+    GpuRolloutState *st = sh.io.state;
+    if (s < d.max_slots) {
+        copy_words(&st->slots[s], &sh.slot[s], sizeof(GpuRolloutSlot));
+        if (with_ext)
+            copy_words(&d.ext[s], &sh.ext[s], sizeof(SlotExt));
+    }
+    if (s < (GPU_MAX_ROLLOUTS + 63) / 64)
+        st->bitmap[s] = sh.bitmap[s];
+    if (s >= 32u && s - 32u < sizeof(RtCtl) / 8u)
+        reinterpret_cast<uint64_t *>(d.ctl)[s - 32u] = reinterpret_cast<const uint64_t *>(&sh.ctl)[s - 32u];
+    __syncthreads();
+}
+
 // Lowest free slot below max_slots (reference find_free_slot order).
-__device__ int take_lowest_free(GpuRolloutState *st, uint32_t max_slots)
+__device__ int take_lowest_free(uint64_t *bitmap, uint32_t max_slots)
 {
     for (uint32_t w = 0; w < (GPU_MAX_ROLLOUTS + 63) / 64; w++) {
-        uint64_t free_bits = ~st->bitmap[w];
+        uint64_t free_bits = ~bitmap[w];
         const uint32_t lo = w * 64u;
         if (lo >= max_slots)
             break;
@@ -171,105 +242,151 @@ __device__ int take_lowest_free(GpuRolloutState *st, uint32_t max_slots)
             free_bits &= (1ull << (max_slots - lo)) - 1ull;
         if (free_bits) {
             const int b = __ffsll((long long)free_bits) - 1;
-            st->bitmap[w] |= 1ull << b;
+            bitmap[w] |= 1ull << b;
             return (int)(lo + (uint32_t)b);
         }
     }
     return -1;
 }
 
-struct SchedShared {
-    uint32_t fin[kSched];
-    uint32_t fin_tokens[kSched];
-    uint32_t fin_req[kSched];
-    alignas(16) uint32_t key[kSched];  // grouping key per slot (prefix id + 1, 0 = none)
-    uint32_t gid[kSched];              // group index, at the group's leader slot
-    uint32_t warp_leaders[kSched / 32];
-    uint32_t stop, n_fin;
-};
-
 // Shared-prefix groups for the attention.  Active slots decoding from the
-// same prefix, in slot order, are cut into groups of up to 16 (the first
-// of each run of 16 is the leader; a lone slot stays ungrouped).  Groups
-// are numbered in leader slot order, members listed in slot order, so the
+// same prefix, in slot order, are cut into runs of up to 16; a run of one
+// stays ungrouped.  Group ids: per key in key order, then run order, so the
 // table is a pure function of the slot state.  All kSched threads call it.
 __device__ void build_groups(const Dev &d, SchedShared &sh, uint32_t key, uint32_t shared)
 {
     const uint32_t s = threadIdx.x;
+    const bool table = d.max_prefixes + 1u <= kKeyTable;
     sh.key[s] = key;
+    if (table)
+        for (uint32_t k = s; k <= d.max_prefixes; k += kSched)
+            sh.kcount[k] = 0u;
     __syncthreads();
-    uint32_t rank = 0, leader = s, block_n = 0;
-    if (key) {
-        const uint4 *k4 = reinterpret_cast<const uint4 *>(sh.key);
-        for (uint32_t t4 = 0; t4 < kSched / 4u; t4++) {
-            const uint4 k = k4[t4];
-            const uint32_t kk[4] = {k.x, k.y, k.z, k.w};
-#pragma unroll
-            for (uint32_t j = 0; j < 4u; j++) {
-                const uint32_t t = t4 * 4u + j;
-                if (kk[j] != key)
-                    continue;
-                if (t < s) {
-                    if ((rank & 15u) == 0u)
-                        leader = t;
-                    rank++;
-                } else if (t > s && block_n < 16u) {
-                    block_n++;  // same-key slots after s (capped)
-                }
+    uint32_t rank = 0, total = 0;
+    if (table) {
+        // warp 0 walks the slots 32 at a time: rank = same-key slots before
+        if (s < 32u) {
+            for (uint32_t c = 0; c < kSched / 32u; c++) {
+                const uint32_t slot = c * 32u + s;
+                const uint32_t k = sh.key[slot];
+                const unsigned same = __match_any_sync(0xffffffffu, k);
+                const uint32_t before = (uint32_t)__popc(same & ((1u << s) - 1u));
+                if (k)
+                    sh.rank[slot] = sh.kcount[k] + before;
+                __syncwarp();
+                if (k && before == 0u)
+                    sh.kcount[k] += (uint32_t)__popc(same);
+                __syncwarp();
             }
         }
-        if ((rank & 15u) == 0u)
-            leader = s;
+        __syncthreads();
+        if (key) {
+            rank = sh.rank[s];
+            total = sh.kcount[key];
+        }
+        __syncthreads();
+        // kcount[k] := first group id of key k (exclusive scan of group counts, warp 0)
+        if (s < 32u) {
+            uint32_t carry = 0;
+            for (uint32_t base = 0; base <= d.max_prefixes; base += 32u) {
+                const uint32_t k = base + s;
+                const uint32_t n = k <= d.max_prefixes ? sh.kcount[k] : 0u;
+                const uint32_t g = n / 16u + ((n % 16u) >= 2u ? 1u : 0u);
+                uint32_t x = g;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+                    if (s >= (uint32_t)o)
+                        x += y;
+                }
+                if (k <= d.max_prefixes)
+                    sh.kcount[k] = carry + x - g;
+                carry += __shfl_sync(0xffffffffu, x, 31);
+            }
+            if (s == 0)
+                sh.n_fin = carry;  // reused: number of groups
+        }
+        __syncthreads();
+    } else if (key) {
+        // large key spaces: scan the slots
+        for (uint32_t t = 0; t < kSched; t++) {
+            const uint32_t kt = sh.key[t];
+            rank += (kt == key && t < s) ? 1u : 0u;
+            total += kt == key ? 1u : 0u;
+        }
     }
-    // members of this slot's run of 16 (valid at the leader: itself + later ones)
-    const uint32_t n_mem = min(16u, 1u + block_n);
-    const bool is_leader = key && leader == s && n_mem >= 2u;
-    const unsigned ballot = __ballot_sync(0xffffffffu, is_leader);
-    const uint32_t lane = s & 31u, warp = s >> 5;
-    if (lane == 0)
-        sh.warp_leaders[warp] = (uint32_t)__popc(ballot);
-    __syncthreads();
-    uint32_t before = 0, total = 0;
-    for (uint32_t w = 0; w < kSched / 32u; w++) {
-        before += w < warp ? sh.warp_leaders[w] : 0u;
-        total += sh.warp_leaders[w];
+    // run r = rank / 16 of this key is a group when it has >= 2 members
+    const uint32_t run = rank / 16u;
+    const uint32_t run_n = min(16u, total - run * 16u);
+    const bool in_group = key != 0u && run_n >= 2u;
+    if (!table) {
+        // group id = number of group leaders (first slot of a run of >= 2) in lower slots
+        const bool leader = in_group && rank % 16u == 0u;
+        const unsigned ballot = __ballot_sync(0xffffffffu, leader);
+        if ((s & 31u) == 0u)
+            sh.fin[s >> 5] = (uint32_t)__popc(ballot);
+        __syncthreads();
+        uint32_t before = 0, all = 0;
+        for (uint32_t w = 0; w < kSched / 32u; w++) {
+            before += w < (s >> 5) ? sh.fin[w] : 0u;
+            all += sh.fin[w];
+        }
+        const uint32_t gid_leader = before + (uint32_t)__popc(ballot & ((1u << (s & 31u)) - 1u));
+        __syncthreads();
+        if (leader)
+            sh.rank[s] = gid_leader;  // published for the run's members
+        if (s == 0)
+            sh.n_fin = all;
+        __syncthreads();
     }
-    const uint32_t gid = before + (uint32_t)__popc(ballot & ((1u << lane) - 1u));
-    if (is_leader) {
-        sh.gid[s] = gid;
-        if (gid < d.max_groups) {
-            d.groups[gid].n_members = n_mem;
+    uint32_t gid = 0;
+    if (in_group) {
+        if (table) {
+            gid = sh.kcount[key] + run;
+        } else {
+            // the run's leader is the same-key slot of rank run * 16
+            uint32_t cnt = 0;
+            for (uint32_t t = 0; t <= s; t++) {
+                if (sh.key[t] != key)
+                    continue;
+                if (cnt == run * 16u) {
+                    gid = sh.rank[t];
+                    break;
+                }
+                cnt++;
+            }
+        }
+    }
+    const bool ok = in_group && gid < d.max_groups;
+    if (ok) {
+        d.groups[gid].members[rank % 16u] = s;
+        if (rank % 16u == 0u) {
+            d.groups[gid].n_members = run_n;
             d.groups[gid].shared_pages = shared;
         }
     }
-    __syncthreads();
-    // a non-leader belongs to a group iff its leader leads one (>= 2 members)
-    const bool member = key && (is_leader || leader != s);
-    const uint32_t g = member ? sh.gid[leader] : 0u;
-    const bool in_group = member && g < d.max_groups;
-    if (in_group)
-        d.groups[g].members[rank & 15u] = s;
     if (s < d.max_slots)
-        d.skip[s] = in_group ? shared : 0u;
+        d.skip[s] = ok ? shared : 0u;
+    __syncthreads();
     if (s == 0)
-        *d.n_groups = min(total, d.max_groups);
+        *d.n_groups = min(sh.n_fin, d.max_groups);
 }
 
-// One pass of the reference rollout_worker loop (see file comment).
-// Returns true when the loop must stop.  All 256 threads call it.
+// One pass of the reference rollout_worker loop (see file comment) on the
+// shared-memory state.  Returns true when the loop must stop.  All kSched
+// threads call it.
 __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
 {
     const uint32_t s = threadIdx.x;
-    const RtIo io = *d.io;
-    RtCtl *ctl = d.ctl;
-    GpuRolloutState *st = io.state;
+    const RtIo &io = sh.io;
+    RtCtl *ctl = &sh.ctl;
     const bool full = d.decode == RT_ROLLOUT_DECODE_FULL;
 
     // 1. commit the tokens sampled in the previous pass
-    const bool committing = full && s < d.max_slots && d.ext[s].decoding;
+    const bool committing = full && s < d.max_slots && sh.ext[s].decoding;
     if (committing) {
-        SlotExt &e = d.ext[s];
-        GpuRolloutSlot &rs = st->slots[s];
+        SlotExt &e = sh.ext[s];
+        GpuRolloutSlot &rs = sh.slot[s];
         const uint32_t tok = d.tokens[s];
         const uint32_t g = rs.tokens_generated;
         if (io.traj && e.row < io.n_rows && g < d.max_new)
@@ -297,7 +414,7 @@ __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
                 sh.stop = 1u;
                 break;
             }
-            const int slot = take_lowest_free(st, d.max_slots);
+            const int slot = take_lowest_free(sh.bitmap, d.max_slots);
             if (slot < 0) {
                 if (!d.drop)
                     break;              // backpressure: leave it queued
@@ -309,7 +426,8 @@ __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
             src_pop(io);
             const uint32_t row = ctl->consumed++;
             ctl->admitted++;
-            GpuRolloutSlot &rs = st->slots[slot];
+            ctl->groups_ok = 0u;
+            GpuRolloutSlot &rs = sh.slot[slot];
             rs.active = 1u;
             rs.request_id = (uint32_t)(rq.request_id & 0xFFFFFFFFull);
             rs.tokens_generated = 0u;
@@ -323,7 +441,7 @@ __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
             rs.top_k = rq.top_k;
             rs.top_p = rq.top_p;
             if (full) {
-                SlotExt &e = d.ext[slot];
+                SlotExt &e = sh.ext[slot];
                 const uint32_t pfx = RT_REQUEST_PREFIX(rq.request_id);
                 uint32_t ctx = 0, np = 0, off = 0;
                 if (pfx != 0u && pfx - 1u < d.max_prefixes) {
@@ -369,7 +487,7 @@ __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
     // 3. retire finished slots, in slot order
     uint32_t fin = 0;
     if (s < d.max_slots) {
-        const GpuRolloutSlot &rs = st->slots[s];
+        const GpuRolloutSlot &rs = sh.slot[s];
         if (rs.active && rs.tokens_generated >= rs.max_tokens) {
             fin = 1u;
             sh.fin_tokens[s] = rs.tokens_generated;
@@ -378,6 +496,8 @@ __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
     }
     sh.fin[s] = fin;
     const uint32_t n_fin = __syncthreads_count(fin);
+    if (n_fin && s == 0)
+        ctl->groups_ok = 0u;
     if (n_fin && s == 0) {
         for (uint32_t k = 0; k < d.max_slots; k++) {
             if (!sh.fin[k])
@@ -400,11 +520,11 @@ __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
     }
     __syncthreads();
     if (fin) {
-        GpuRolloutSlot &rs = st->slots[s];
+        GpuRolloutSlot &rs = sh.slot[s];
         rs.active = 0u;
-        atomicAnd((unsigned long long *)&st->bitmap[s / 64u], ~(1ull << (s % 64u)));
-        if (io.rewards && full && d.ext[s].row < io.n_rows)
-            io.rewards[d.ext[s].row] = reward_for(d, sh.fin_req[s], sh.fin_tokens[s]);
+        atomicAnd((unsigned long long *)&sh.bitmap[s / 64u], ~(1ull << (s % 64u)));
+        if (io.rewards && full && sh.ext[s].row < io.n_rows)
+            io.rewards[sh.ext[s].row] = reward_for(d, sh.fin_req[s], sh.fin_tokens[s]);
     }
     if (sh.stop)
         return true;
@@ -412,10 +532,10 @@ __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
     // 4. this pass's decode: every slot still active generates one token
     uint32_t act = 0;
     if (s < d.max_slots) {
-        GpuRolloutSlot &rs = st->slots[s];
+        GpuRolloutSlot &rs = sh.slot[s];
         act = rs.active && !fin;
         if (full) {
-            SlotExt &e = d.ext[s];
+            SlotExt &e = sh.ext[s];
             const bool room = e.pos < d.maxp * 16u;
             if (act && !room) {
                 act = 0u;  // context full: counts as an error, slot is left idle
@@ -439,9 +559,16 @@ __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
         }
     }
     const uint32_t n_act = __syncthreads_count(act);
-    if (full && d.max_groups) {
-        const bool key_ok = act && d.ext[s].prefix != 0u && d.ext[s].shared != 0u;
-        build_groups(d, sh, key_ok ? d.ext[s].prefix : 0u, key_ok ? d.ext[s].shared : 0u);
+    // The group table depends only on which slots are active (and their
+    // prefixes): rebuild it when a slot was admitted or retired, or when the
+    // active count changed for another reason (a slot whose context is full).
+    if (full && d.max_groups && !(ctl->groups_ok && ctl->groups_act == n_act)) {
+        const bool key_ok = act && sh.ext[s].prefix != 0u && sh.ext[s].shared != 0u;
+        build_groups(d, sh, key_ok ? sh.ext[s].prefix : 0u, key_ok ? sh.ext[s].shared : 0u);
+        if (s == 0) {
+            ctl->groups_ok = 1u;
+            ctl->groups_act = n_act;
+        }
     }
 
     // 5. loop control
@@ -479,22 +606,27 @@ __global__ void __launch_bounds__(kSched, 1)
 schedule_kernel(const Dev d, cudaGraphConditionalHandle handle, int in_graph)
 {
     __shared__ SchedShared sh;
+    const bool full = d.decode == RT_ROLLOUT_DECODE_FULL;
+    load_state(d, sh, full);
     const bool stop = schedule_pass(d, sh);
-    if (threadIdx.x == 0) {
-        if (stop) {
-            // The decode chain of this pass still runs: make it a no-op.
-            d.ctl->stop = 1u;
-            for (uint32_t s = 0; s < d.max_slots; s++) {
-                d.enable[s] = 0u;
-                if (d.seq_lens)
-                    d.seq_lens[s] = 0;
-            }
-            if (d.max_groups)
-                *d.n_groups = 0u;
+    if (stop) {
+        // The decode chain of this pass still runs: make it a no-op.
+        const uint32_t s = threadIdx.x;
+        if (s == 0)
+            sh.ctl.stop = 1u;
+        if (s < d.max_slots) {
+            d.enable[s] = 0u;
+            if (d.seq_lens)
+                d.seq_lens[s] = 0;
         }
-        if (in_graph)
-            cudaGraphSetConditional(handle, stop ? 0u : 1u);
+        if (s == 0 && d.max_groups) {
+            *d.n_groups = 0u;
+            sh.ctl.groups_ok = 0u;
+        }
     }
+    store_state(d, sh, full);
+    if (threadIdx.x == 0 && in_graph)
+        cudaGraphSetConditional(handle, stop ? 0u : 1u);
 }
 
 __global__ void __launch_bounds__(256) prepare_kernel(const Dev d)
@@ -581,18 +713,22 @@ __global__ void logits_synth_kernel(float *out, uint32_t vocab, uint64_t seed, u
 }
 
 // Persistent single-CTA worker: the reference's pass loop, counter-only.
+// The state table stays in shared memory for the whole run and is stored
+// back when the loop ends.
 __global__ void __launch_bounds__(kSched, 1) persistent_worker_kernel(const Dev d)
 {
     __shared__ SchedShared sh;
+    load_state(d, sh, false);
     for (;;) {
         if (schedule_pass(d, sh))
             break;
-        if (threadIdx.x == 0 && d.ctl->idle_since != 0ull)
+        if (threadIdx.x == 0 && sh.ctl.idle_since != 0ull)
             __nanosleep(1000);
         __syncthreads();
     }
     if (threadIdx.x == 0)
-        d.ctl->stop = 1u;
+        sh.ctl.stop = 1u;
+    store_state(d, sh, false);
 }
 
 template <typename T>
