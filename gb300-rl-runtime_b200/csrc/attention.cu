@@ -238,6 +238,34 @@ __device__ __forceinline__ bool process_item(const CUtensorMap &kv_map, const At
         pg_lo = ptab[lane];
     if (lane + 32 < n_mine)
         pg_hi = ptab[lane + 32];
+    const bool bad = (lane < n_mine && (pg_lo < 0 || (uint64_t)pg_lo >= a.arena_pages)) ||
+                     (lane + 32 < n_mine && (pg_hi < 0 || (uint64_t)pg_hi >= a.arena_pages));
+    if (bad) {
+        flag_error(a.error, kErrPage);
+        if (pg_lo < 0 || (uint64_t)pg_lo >= a.arena_pages)
+            pg_lo = 0;
+        if (pg_hi < 0 || (uint64_t)pg_hi >= a.arena_pages)
+            pg_hi = 0;
+    }
+
+    auto issue = [&](int i, int s) {
+        const int pg = __shfl_sync(0xffffffffu, i < 32 ? pg_lo : pg_hi, i & 31);
+        if (lane == 0) {
+            const uint32_t bar = rt::smem_u32(&bars[s]);
+            const uint32_t dst = stage0 + (uint32_t)(s * kStageBytes);
+            const int32_t row_k = (int32_t)(((int64_t)pg * Hkv + h) * 32);
+            rt::mbar_arrive_expect_tx(bar, (uint32_t)kStageBytes);
+            rt::tma_load_2d(dst, &kv_map, 0, row_k, bar, policy);
+            rt::tma_load_2d(dst + 2048u, &kv_map, 64, row_k, bar, policy);
+            rt::tma_load_2d(dst + 4096u, &kv_map, 0, row_k + 16, bar, policy);
+            rt::tma_load_2d(dst + 6144u, &kv_map, 64, row_k + 16, bar, policy);
+        }
+    };
+    // The stage ring was left idle by the previous item: order this warp's
+    // earlier generic accesses of it before the new TMA writes.
+    rt::fence_proxy_async_smem();
+    for (int i = 0; i < n_mine && i < kStages; i++)
+        issue(i, i);
     // Group partials to start from (chunk 0 of a grouped sequence): lane
     // owns heads 2q4, 2q4 + 1 and dims 16dd + r, 16dd + r + 8.
     float o[8][4];
@@ -247,6 +275,9 @@ __device__ __forceinline__ bool process_item(const CUtensorMap &kv_map, const At
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
     const int hd0 = 2 * q4, hd1 = 2 * q4 + 1;
     if (chunk == 0 && n_g) {
+        // The partials come from the group kernel launched just before this
+        // one (programmatic dependent launch: wait for its completion here).
+        asm volatile("griddepcontrol.wait;" ::: "memory");
         const size_t pi0 = (bh * a.slots) * G;
         for (uint32_t k = 0; k < n_g; k++) {
             if (hd0 < G)
@@ -286,34 +317,6 @@ __device__ __forceinline__ bool process_item(const CUtensorMap &kv_map, const At
         l0 *= 0.125f;
         l1 *= 0.125f;
     }
-    const bool bad = (lane < n_mine && (pg_lo < 0 || (uint64_t)pg_lo >= a.arena_pages)) ||
-                     (lane + 32 < n_mine && (pg_hi < 0 || (uint64_t)pg_hi >= a.arena_pages));
-    if (bad) {
-        flag_error(a.error, kErrPage);
-        if (pg_lo < 0 || (uint64_t)pg_lo >= a.arena_pages)
-            pg_lo = 0;
-        if (pg_hi < 0 || (uint64_t)pg_hi >= a.arena_pages)
-            pg_hi = 0;
-    }
-
-    auto issue = [&](int i, int s) {
-        const int pg = __shfl_sync(0xffffffffu, i < 32 ? pg_lo : pg_hi, i & 31);
-        if (lane == 0) {
-            const uint32_t bar = rt::smem_u32(&bars[s]);
-            const uint32_t dst = stage0 + (uint32_t)(s * kStageBytes);
-            const int32_t row_k = (int32_t)(((int64_t)pg * Hkv + h) * 32);
-            rt::mbar_arrive_expect_tx(bar, (uint32_t)kStageBytes);
-            rt::tma_load_2d(dst, &kv_map, 0, row_k, bar, policy);
-            rt::tma_load_2d(dst + 2048u, &kv_map, 64, row_k, bar, policy);
-            rt::tma_load_2d(dst + 4096u, &kv_map, 0, row_k + 16, bar, policy);
-            rt::tma_load_2d(dst + 6144u, &kv_map, 64, row_k + 16, bar, policy);
-        }
-    };
-    // The stage ring was left idle by the previous item: order this warp's
-    // earlier generic accesses of it before the new TMA writes.
-    rt::fence_proxy_async_smem();
-    for (int i = 0; i < n_mine && i < kStages; i++)
-        issue(i, i);
 
     // ldmatrix row addresses (swizzled 16-byte chunk = chunk ^ row%8): lane
     // l points at token 8*((l/8)>>1) + l%8 and the (l/8)&1 half of a 16-dim
@@ -610,11 +613,21 @@ __device__ __forceinline__ bool process_group_item(const CUtensorMap &kv_map, co
     const int mi = lane >> 3, rr = lane & 7;
     const uint32_t k_row = (uint32_t)((((mi >> 1) << 3) + rr) * 128);
     const uint32_t v_row = (uint32_t)((((mi & 1) << 3) + rr) * 128);
+    // When the whole chunk fits the ring (the usual case) every page is
+    // issued up front and the warps never wait for each other within the
+    // item; longer chunks re-issue stages behind a per-page CTA barrier.
+    const bool refill = np > kGroupStages;
     for (int i = 0; i < np; i++) {
         const int s = i % kGroupStages;
         const bool ok = rt::mbar_wait_bounded(rt::smem_u32(&gbars[s]), (gphases >> s) & 1u,
                                               kWaitLimitNs);
-        if (!__syncthreads_and(ok)) {
+        if (!refill) {
+            if (!__all_sync(0xffffffffu, ok)) {
+                if (lane == 0)
+                    flag_error(a.error, kErrTimeout);
+                return false;  // the caller stops the CTA; issued copies are waited for there
+            }
+        } else if (!__syncthreads_and(ok)) {
             if (threadIdx.x == 0) {
                 flag_error(a.error, kErrTimeout);
                 // Give the copies still in flight (pages i .. i+11) a bounded
@@ -687,11 +700,13 @@ __device__ __forceinline__ bool process_group_item(const CUtensorMap &kv_map, co
                 rt::mma_bf16_16816(o[2 * dd + 1], pl, v2, v3);
             }
         }
-        // Every warp has read stage s (shared-memory reads only, so the TMA
-        // rewrite needs no proxy fence).
-        __syncthreads();
-        if (warp == 0 && i + kGroupStages < np)
-            issue(i + kGroupStages);
+        if (refill) {
+            // Every warp has read stage s (shared-memory reads only, so the
+            // TMA rewrite needs no proxy fence).
+            __syncthreads();
+            if (warp == 0 && i + kGroupStages < np)
+                issue(i + kGroupStages);
+        }
     }
     if (!active)
         return true;
@@ -741,6 +756,9 @@ paged_gqa_group_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnArg
         rt::mbar_fence_init();
     }
     __syncthreads();
+    // The sequence kernel may start on SMs this grid leaves free; it waits
+    // for this grid's completion before it reads the partials.
+    asm volatile("griddepcontrol.launch_dependents;");
     const uint64_t policy = a.evict_first ? rt::l2_policy_evict_first() : rt::l2_policy_evict_normal();
     constexpr int RB = (16 * G + 16 * kWarps - 1) / (16 * kWarps);
     const uint32_t n_live = min(*a.n_groups, a.max_groups);
@@ -754,9 +772,16 @@ paged_gqa_group_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnArg
         __syncthreads();
         if (gi >= n_gi)
             break;
-        // A false return means a wait expired (flagged): stop taking items.
-        if (!process_group_item<G>(kv_map, a, gi, n_live, base_u32, gbars, gphases, policy))
+        // A false return means a wait expired (flagged): stop taking items,
+        // after giving the copies still in flight a bounded chance to land.
+        const bool ok = process_group_item<G>(kv_map, a, gi, n_live, base_u32, gbars, gphases, policy);
+        if (!__syncthreads_and(ok)) {
+            if (threadIdx.x == 0)
+                for (int st = 0; st < kGroupStages; st++)
+                    (void)rt::mbar_wait_bounded(rt::smem_u32(&gbars[st]), (gphases >> st) & 1u,
+                                                kWaitLimitNs / 64);
             break;
+        }
     }
     if (threadIdx.x == 0) {
         __threadfence();
@@ -826,7 +851,7 @@ struct Plan {
     size_t off_counters, off_ml, off_o, total;
 };
 
-constexpr uint32_t kDefaultGroupChunkPages = 8;
+constexpr uint32_t kDefaultGroupChunkPages = 16;
 
 // Workspace header: error word at 0, per-warp item dispenser at 8/16, group
 // item dispenser at 24/32; arrival counters from 256.
@@ -974,14 +999,31 @@ int launch_g(const CUtensorMap &map, const AttnArgs &args, dim3 grid, cudaStream
     int rc = prepare_g<G>();
     if (rc != RT_OK)
         return rc;
-    if (args.groups) {
-        // Group prefixes first; the stream orders their partials before the
-        // sequence kernel that folds them in.
-        const dim3 ggrid((unsigned)rt::num_sms() * 2u);
-        paged_gqa_group_kernel<G><<<ggrid, kWarps * 32, kSmemBytes, s>>>(map, args);
+    if (!args.groups) {
+        paged_gqa_decode_kernel<G><<<grid, kWarps * 32, kSmemBytes, s>>>(map, args);
+        cudaError_t e = cudaGetLastError();
+        return e == cudaSuccess ? RT_OK : rt::cuda_fail(e, "attention: launch");
     }
-    paged_gqa_decode_kernel<G><<<grid, kWarps * 32, kSmemBytes, s>>>(map, args);
+    // Group prefixes first.  The sequence kernel is a programmatic dependent
+    // launch: its CTAs start on SMs the group grid frees and run their own
+    // prologue and suffix pages; each waits for the group grid (griddepcontrol)
+    // only before folding in the prefix partials.
+    const dim3 ggrid((unsigned)rt::num_sms() * 2u);
+    paged_gqa_group_kernel<G><<<ggrid, kWarps * 32, kSmemBytes, s>>>(map, args);
     cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess)
+        return rt::cuda_fail(e, "attention: group launch");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kWarps * 32);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, paged_gqa_decode_kernel<G>, map, args);
     return e == cudaSuccess ? RT_OK : rt::cuda_fail(e, "attention: launch");
 }
 
