@@ -266,57 +266,14 @@ __device__ __forceinline__ bool process_item(const CUtensorMap &kv_map, const At
     rt::fence_proxy_async_smem();
     for (int i = 0; i < n_mine && i < kStages; i++)
         issue(i, i);
-    // Group partials to start from (chunk 0 of a grouped sequence): lane
-    // owns heads 2q4, 2q4 + 1 and dims 16dd + r, 16dd + r + 8.
+    // Online-softmax state: lane owns heads 2q4, 2q4 + 1 and dims 16dd + r,
+    // 16dd + r + 8 of the O^T tiles.
     float o[8][4];
 #pragma unroll
     for (int n = 0; n < 8; n++)
         o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
     const int hd0 = 2 * q4, hd1 = 2 * q4 + 1;
-    if (chunk == 0 && n_g) {
-        // The partials come from the group kernel launched just before this
-        // one (programmatic dependent launch: wait for its completion here).
-        asm volatile("griddepcontrol.wait;" ::: "memory");
-        const size_t pi0 = (bh * a.slots) * G;
-        for (uint32_t k = 0; k < n_g; k++) {
-            if (hd0 < G)
-                m0 = fmaxf(m0, a.part_ml[(pi0 + (size_t)k * G + hd0) * 2]);
-            if (hd1 < G)
-                m1 = fmaxf(m1, a.part_ml[(pi0 + (size_t)k * G + hd1) * 2]);
-        }
-        for (uint32_t k = 0; k < n_g; k++) {
-            const size_t pa = pi0 + (size_t)k * G;
-            float w0 = 0.0f, w1 = 0.0f;
-            const float *s0 = a.part_o + (pa + (hd0 < G ? hd0 : 0)) * 128 + r;
-            const float *s1 = a.part_o + (pa + (hd1 < G ? hd1 : 0)) * 128 + r;
-            if (hd0 < G) {
-                const float2 ml = *reinterpret_cast<const float2 *>(&a.part_ml[(pa + hd0) * 2]);
-                w0 = rt::fast_exp2(ml.x - m0);
-                l0 += ml.y * w0;
-            }
-            if (hd1 < G) {
-                const float2 ml = *reinterpret_cast<const float2 *>(&a.part_ml[(pa + hd1) * 2]);
-                w1 = rt::fast_exp2(ml.x - m1);
-                l1 += ml.y * w1;
-            }
-#pragma unroll
-            for (int dd = 0; dd < 8; dd++) {
-                if (hd0 < G) {
-                    o[dd][0] += s0[16 * dd] * w0;
-                    o[dd][2] += s0[16 * dd + 8] * w0;
-                }
-                if (hd1 < G) {
-                    o[dd][1] += s1[16 * dd] * w1;
-                    o[dd][3] += s1[16 * dd + 8] * w1;
-                }
-            }
-        }
-        // every lane of a head's 8-lane column holds the full sum; the
-        // column reduction at the end adds 8 copies
-        l0 *= 0.125f;
-        l1 *= 0.125f;
-    }
 
     // ldmatrix row addresses (swizzled 16-byte chunk = chunk ^ row%8): lane
     // l points at token 8*((l/8)>>1) + l%8 and the (l/8)&1 half of a 16-dim
@@ -431,6 +388,63 @@ __device__ __forceinline__ bool process_item(const CUtensorMap &kv_map, const At
     for (int off = 4; off < 32; off <<= 1) {
         l0 += __shfl_xor_sync(0xffffffffu, l0, off);
         l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+    }
+
+    if (chunk == 0 && n_g) {
+        // Fold in the group's prefix partials.  They come from the group
+        // kernel launched just before this one as a programmatic dependent
+        // launch, so this is where its completion is awaited - after this
+        // warp's own pages, by when it has usually finished.
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        const size_t pi0 = (bh * a.slots) * G;
+        float M0 = m0, M1 = m1;
+        for (uint32_t k = 0; k < n_g; k++) {
+            if (hd0 < G)
+                M0 = fmaxf(M0, a.part_ml[(pi0 + (size_t)k * G + hd0) * 2]);
+            if (hd1 < G)
+                M1 = fmaxf(M1, a.part_ml[(pi0 + (size_t)k * G + hd1) * 2]);
+        }
+        // rescale this warp's suffix state (exp2(-inf) = 0 when it had no pages)
+        const float c0 = hd0 < G ? rt::fast_exp2(m0 - M0) : 0.0f;
+        const float c1 = hd1 < G ? rt::fast_exp2(m1 - M1) : 0.0f;
+        l0 *= c0;
+        l1 *= c1;
+#pragma unroll
+        for (int dd = 0; dd < 8; dd++) {
+            o[dd][0] *= c0;
+            o[dd][2] *= c0;
+            o[dd][1] *= c1;
+            o[dd][3] *= c1;
+        }
+        for (uint32_t k = 0; k < n_g; k++) {
+            const size_t pa = pi0 + (size_t)k * G;
+            float w0 = 0.0f, w1 = 0.0f;
+            const float *s0 = a.part_o + (pa + (hd0 < G ? hd0 : 0)) * 128 + r;
+            const float *s1 = a.part_o + (pa + (hd1 < G ? hd1 : 0)) * 128 + r;
+            if (hd0 < G) {
+                const float2 ml = *reinterpret_cast<const float2 *>(&a.part_ml[(pa + hd0) * 2]);
+                w0 = rt::fast_exp2(ml.x - M0);
+                l0 += ml.y * w0;
+            }
+            if (hd1 < G) {
+                const float2 ml = *reinterpret_cast<const float2 *>(&a.part_ml[(pa + hd1) * 2]);
+                w1 = rt::fast_exp2(ml.x - M1);
+                l1 += ml.y * w1;
+            }
+#pragma unroll
+            for (int dd = 0; dd < 8; dd++) {
+                if (hd0 < G) {
+                    o[dd][0] += s0[16 * dd] * w0;
+                    o[dd][2] += s0[16 * dd + 8] * w0;
+                }
+                if (hd1 < G) {
+                    o[dd][1] += s1[16 * dd] * w1;
+                    o[dd][3] += s1[16 * dd + 8] * w1;
+                }
+            }
+        }
+        m0 = M0;
+        m1 = M1;
     }
 
     if (n_chunks == 1) {
