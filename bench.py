@@ -44,15 +44,16 @@ def measured_peaks():
         return {"hbm_gbs": HBM_FALLBACK_GBS, "bf16_tflops": 1590.0}, "fallback"
 
 
-def ncu_traffic(kernel: str):
+def ncu_traffic(kernel: str, workload: str):
     """Per-launch DRAM bytes recorded from an ncu capture in profiles/ncu_traffic.txt
-    (lines: <kernel> <workload> <bytes_per_launch>)."""
+    (lines: <kernel> <workload> <bytes_per_launch>); None when not recorded."""
     path = os.path.join(ROOT, "profiles", "ncu_traffic.txt")
     try:
         with open(path) as f:
             for line in f:
                 parts = line.split()
-                if len(parts) >= 3 and not line.startswith("#") and parts[0] == kernel:
+                if (len(parts) >= 3 and not line.startswith("#") and parts[0] == kernel
+                        and parts[1] == workload):
                     return float(parts[2])
     except OSError:
         pass
@@ -337,7 +338,7 @@ class RolloutWorkload:
     (Philox seed 5) allgathered over NCCL, group-normalised advantages."""
 
     name = "grpo_rollouts_c5"
-    kernel = "paged_gqa_decode_kernel"
+    kernel = "paged_gqa_group_kernel+paged_gqa_decode_kernel"  # attention of one pass
     metric = "rollout tokens/s (config 5; value = all GPUs, per GPU = value / n_gpus)"
     unit = "tokens/s"
 
@@ -348,6 +349,8 @@ class RolloutWorkload:
         self.torch = torch
         self.pkg = pkg = ge.load_package()
         self.rank, self.world, self.dev = rank, world, dev
+        if getattr(args, "groups", 0):
+            self.GROUPS = args.groups
         self.g0, self.ng = pkg.shard_groups(self.GROUPS, world, rank)
         self.n = self.ng * self.G
         pages_prompt = self.PROMPT // 16
@@ -589,7 +592,7 @@ def run_mine(args):
         else:
             achieved = wl.bytes / (ms / 1e3) / 1e9
             prof_report = None
-        traffic = ncu_traffic(wl.kernel + ":" + wl.name) or ncu_traffic(wl.kernel)
+        traffic = ncu_traffic(wl.kernel, wl.name)
         line = {
             "metric": wl.metric, "value": wl.units_per_step() / (ms / 1e3) * world,
             "unit": wl.unit, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -649,6 +652,8 @@ def main():
     ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
     ap.add_argument("--chunk-pages", type=int, default=0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--groups", type=int, default=0,
+                    help="rollout only: GRPO groups (default 512; fewer keep ncu captures small)")
     ap.add_argument("--ncu-replay", type=int, default=0,
                     help="rollout only: run the host-stepped replay of this many rollouts and "
                          "exit (plain kernel launches, for ncu captures)")
