@@ -22,11 +22,10 @@
 //    (column max over the 8 lanes of a head); P is split into two bf16 terms
 //    so that P.V keeps ~16 mantissa bits; movmatrix turns the S^T
 //    accumulator into the B operand of the second product.
-//  * Shared prefixes: a separate group kernel on the tcgen05 tensor cores
-//    reads a GRPO group's common prefix pages once and multiplies them
-//    against all members' queries (up to 16 sequences x G heads = 128 rows,
-//    accumulators in TMEM); the sequence kernel folds those partials into
-//    each grouped sequence's own pages.
+//  * Shared prefixes: a separate group kernel reads a GRPO group's common
+//    prefix pages once and multiplies them against all members' queries
+//    (16 query rows = 16/G sequences x G heads per tile); the sequence kernel
+//    starts each grouped sequence from those partials.
 //  * Split-K: the chunks of one (b, h) write unnormalised partials; the last
 //    warp to arrive (per-(b,h) counter) merges them with the log-sum-exp rule
 //    and resets the counter, so no second kernel launch is needed.
@@ -50,9 +49,6 @@ constexpr int kStageBytes = 8192;    // K (2 x 2 KiB halves) + V (2 x 2 KiB)
 constexpr int kMaxChunkPages = 64;   // page ids live in two registers per lane
 constexpr int kSmemBytes = kWarps * kStages * kStageBytes + 1024;  // + 1 KiB alignment slack
 constexpr uint64_t kWaitLimitNs = 2000000000ull;                    // 2 s per pipeline wait
-// Online softmax: the running maximum is raised only when a page exceeds it
-// by more than this (log2 units), so probabilities stay <= 256.
-constexpr float kRescaleLog2 = 8.0f;
 
 enum : int32_t { kErrSeqLen = 1, kErrPage = 2, kErrTimeout = 3, kErrGroup = 4 };
 
@@ -82,6 +78,7 @@ struct AttnArgs {
     uint32_t slots;                    // partial slots per (b, h): max_gchunks + max_chunks
 };
 
+constexpr int kGroupStages = kWarps * kStages;  // the CTA's whole ring, shared by its warps
 constexpr uint32_t kMaxGroupMembers = 16;
 
 __device__ __forceinline__ void flag_error(int32_t *err, int32_t code)
@@ -342,29 +339,21 @@ __device__ __forceinline__ bool process_item(const CUtensorMap &kv_map, const At
             mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
             mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
         }
-        // Lazy rescaling: the reference maximum moves only when a page
-        // exceeds it by more than kRescaleLog2, so P stays <= 2^kRescaleLog2
-        // and most pages skip the rescale of O.
-        const bool up0 = mx0 > m0 + kRescaleLog2, up1 = mx1 > m1 + kRescaleLog2;
-        if (__any_sync(0xffffffffu, up0 || up1)) {
-            const float n0 = up0 ? mx0 : m0, n1 = up1 ? mx1 : m1;
-            const float c0 = rt::fast_exp2(m0 - n0), c1 = rt::fast_exp2(m1 - n1);
-            l0 *= c0;
-            l1 *= c1;
-            m0 = n0;
-            m1 = n1;
+        const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
+        const float c0 = rt::fast_exp2(m0 - n0), c1 = rt::fast_exp2(m1 - n1);
+        const float p0 = rt::fast_exp2(x0 - n0), p1 = rt::fast_exp2(x1 - n1);
+        const float p2 = rt::fast_exp2(x2 - n0), p3 = rt::fast_exp2(x3 - n1);
+        l0 = l0 * c0 + (p0 + p2);
+        l1 = l1 * c1 + (p1 + p3);
+        m0 = n0;
+        m1 = n1;
 #pragma unroll
-            for (int dd = 0; dd < 8; dd++) {
-                o[dd][0] *= c0;
-                o[dd][2] *= c0;
-                o[dd][1] *= c1;
-                o[dd][3] *= c1;
-            }
+        for (int dd = 0; dd < 8; dd++) {
+            o[dd][0] *= c0;
+            o[dd][2] *= c0;
+            o[dd][1] *= c1;
+            o[dd][3] *= c1;
         }
-        const float p0 = rt::fast_exp2(x0 - m0), p1 = rt::fast_exp2(x1 - m1);
-        const float p2 = rt::fast_exp2(x2 - m0), p3 = rt::fast_exp2(x3 - m1);
-        l0 += p0 + p2;
-        l1 += p1 + p3;
         // P^T as the B operand: transpose the two 8x8 (token x head) blocks;
         // P in two bf16 terms (hi + lo) keeps ~16 mantissa bits.
         uint32_t h01, l01, h23, l23;
@@ -514,301 +503,301 @@ __device__ __forceinline__ bool process_item(const CUtensorMap &kv_map, const At
     return true;
 }
 
-// ---------------------------------------------------------------------------
-// Shared-prefix kernel on the 5th-generation tensor cores.  One item =
-// (group, KV head, chunk of up to 8 prefix pages = 128 tokens); one CTA of
-// 4 warps per item, two CTAs per SM.  The group's query rows (member m,
-// head j -> row m*G + j, at most 16 x 8 = 128) form the M = 128 rows of
-//   S = Q K^T   (tcgen05.mma kind::f16, M 128, N = tokens, K = 128 dims,
-//                Q and K K-major in shared memory, S fp32 in TMEM cols 0..127)
-//   O = P V     (M 128, N 128 dims, K = tokens, P K-major in shared memory,
-//                V MN-major (token rows of 64-dim halves), O in TMEM 128..255)
-// with the whole chunk's softmax done in between by the thread that owns
-// the row (TMEM lane = row), so no online rescaling is needed: the partial
-// (O, max, sum) of the chunk goes to the workspace for the sequence kernel.
-// P is written as two bf16 terms (hi + residual) and both are multiplied,
-// keeping ~16 mantissa bits of the probabilities.  Shared memory (96 KiB):
-// [Q | P_hi] [K | P_lo] [V], each two 16 KiB halves of 128 rows x 128 B in
-// the 128-byte-swizzled layout TMA writes and the MMA descriptors read.
-constexpr int kTcPages = 8;                  // prefix pages per item (128 tokens)
-constexpr uint32_t kTcHalf = 16384;          // 128 rows x 128 B
-constexpr uint32_t kTcRegion = 2 * kTcHalf;  // one operand tile (two 64-column halves)
-constexpr uint32_t kTcCols = 256;            // TMEM columns: S [0,128), O [128,256)
-
-// Byte offset of 16-byte chunk c (0..15) of row r in a swizzled tile.
-__device__ __forceinline__ uint32_t tc_tile_off(uint32_t r, uint32_t c)
+// One (group, row block, KV head, prefix chunk) item, processed by the whole
+// CTA: the group's shared prefix pages stream once through the CTA's 12-stage
+// ring (warp 0 loads the page ids, lane 0 issues the TMA copies), and each
+// warp attends 16 query rows to every page - 16/G member sequences x G
+// heads, so for G = 4 every row of the m16n8k16 tile is a real query (4
+// sequences x 4 heads per warp, 16 sequences per CTA).  G = 8 needs two row
+// blocks for 16 members; G = 1, 2 leave warps idle.  Each member's result is
+// an unnormalised partial (o, max, sum) in slot `chunk` of its (b, h); the
+// sequence kernel that runs next folds these into its own online softmax.
+template <int G>
+__device__ __forceinline__ bool process_group_item(const CUtensorMap &kv_map, const AttnArgs &a,
+                                                   uint64_t gi, uint32_t n_live, uint32_t ring0,
+                                                   uint64_t *gbars, uint32_t &gphases,
+                                                   uint64_t policy)
 {
-    return (c >> 3) * kTcHalf + (r >> 3) * 1024u + (r & 7u) * 128u + (((c & 7u) ^ (r & 7u)) << 4);
+    constexpr int MPW = 16 / G;                        // member sequences per warp
+    constexpr int RB = (16 * G + 16 * kWarps - 1) / (16 * kWarps);  // row blocks per group
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t Hkv = a.num_kv_heads, Hq = a.num_q_heads;
+    const uint32_t g = (uint32_t)(gi % n_live);
+    uint64_t rest = gi / n_live;
+    const int rb = (int)(rest % RB);
+    rest /= RB;
+    const uint32_t h = (uint32_t)(rest % Hkv);
+    const int chunk = (int)(rest / Hkv);
+    const rt_attn_group_t &grp = a.groups[g];
+    const uint32_t n_mem = min(grp.n_members, kMaxGroupMembers);
+    const int P = (int)grp.shared_pages;
+    const int cpg = (int)a.gchunk_pages;
+    const int p0 = chunk * cpg;
+    if (n_mem == 0 || P == 0 || p0 >= P)
+        return true;
+    const uint32_t src = grp.members[0];
+    if (src >= a.num_seqs || (uint32_t)P > a.max_gchunks * (uint32_t)cpg ||
+        (uint32_t)P > a.max_pages) {
+        if (threadIdx.x == 0)
+            flag_error(a.error, kErrGroup);
+        return true;
+    }
+    const int np = min(P, p0 + cpg) - p0;
+
+    // Page ids (warp 0): lane i holds pages i and 32 + i of this chunk.
+    int pg_lo = 0, pg_hi = 0;
+    if (warp == 0) {
+        const int32_t *ptab = a.page_table + (size_t)src * a.max_pages + p0;
+        if (lane < np)
+            pg_lo = ptab[lane];
+        if (lane + 32 < np)
+            pg_hi = ptab[lane + 32];
+        const bool bad = (lane < np && (pg_lo < 0 || (uint64_t)pg_lo >= a.arena_pages)) ||
+                         (lane + 32 < np && (pg_hi < 0 || (uint64_t)pg_hi >= a.arena_pages));
+        if (bad) {
+            flag_error(a.error, kErrPage);
+            if (pg_lo < 0 || (uint64_t)pg_lo >= a.arena_pages)
+                pg_lo = 0;
+            if (pg_hi < 0 || (uint64_t)pg_hi >= a.arena_pages)
+                pg_hi = 0;
+        }
+    }
+    auto issue = [&](int i) {  // warp 0 only
+        const int pg = __shfl_sync(0xffffffffu, i < 32 ? pg_lo : pg_hi, i & 31);
+        if (lane == 0) {
+            const int s = i % kGroupStages;
+            const uint32_t bar = rt::smem_u32(&gbars[s]);
+            const uint32_t dst = ring0 + (uint32_t)(s * kStageBytes);
+            const int32_t row_k = (int32_t)(((int64_t)pg * Hkv + h) * 32);
+            rt::mbar_arrive_expect_tx(bar, (uint32_t)kStageBytes);
+            rt::tma_load_2d(dst, &kv_map, 0, row_k, bar, policy);
+            rt::tma_load_2d(dst + 2048u, &kv_map, 64, row_k, bar, policy);
+            rt::tma_load_2d(dst + 4096u, &kv_map, 0, row_k + 16, bar, policy);
+            rt::tma_load_2d(dst + 6144u, &kv_map, 64, row_k + 16, bar, policy);
+        }
+    };
+    if (warp == 0)
+        for (int i = 0; i < np && i < kGroupStages; i++)
+            issue(i);
+
+    // A member takes part when the group covers exactly its skipped pages.
+    auto member_ok = [&](int m) -> bool {
+        if (m >= (int)n_mem)
+            return false;
+        const uint32_t b = grp.members[m];
+        if (b >= a.num_seqs)
+            return false;
+        const int L = a.seq_lens[b];
+        if (L < 0 || (uint32_t)L > a.max_seq_len || (uint32_t)L > a.max_pages * 16u)
+            return false;
+        return a.skip_pages[b] == (uint32_t)P && P <= ((L + 15) >> 4);
+    };
+
+    // Rows of this warp: row r -> member (rb*kWarps + warp)*MPW + r/G, head r%G.
+    const int wm0 = (rb * kWarps + warp) * MPW;
+    const int rA = lane >> 2, rB = rA + 8, q4 = lane & 3;
+    const int mA = wm0 + rA / G, mB = wm0 + rB / G;
+    const bool vA = member_ok(mA), vB = member_ok(mB);
+    if (lane == 0 && chunk == 0 && h == 0)
+        for (int m = wm0; m < wm0 + MPW && m < (int)n_mem; m++)
+            if (!member_ok(m))
+                flag_error(a.error, kErrGroup);
+    const bool active = __any_sync(0xffffffffu, vA || vB);
+    const uint32_t bA = vA ? grp.members[mA] : 0u, bB = vB ? grp.members[mB] : 0u;
+    uint32_t qf[8][4];
+    {
+        const uint32_t *qa = reinterpret_cast<const uint32_t *>(
+            a.q + ((size_t)bA * Hq + (size_t)h * G + rA % G) * 128);
+        const uint32_t *qb = reinterpret_cast<const uint32_t *>(
+            a.q + ((size_t)bB * Hq + (size_t)h * G + rB % G) * 128);
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            qf[j][0] = vA ? qa[8 * j + q4] : 0u;
+            qf[j][1] = vB ? qb[8 * j + q4] : 0u;
+            qf[j][2] = vA ? qa[8 * j + 4 + q4] : 0u;
+            qf[j][3] = vB ? qb[8 * j + 4 + q4] : 0u;
+        }
+    }
+
+    float o[16][4];
+#pragma unroll
+    for (int n = 0; n < 16; n++)
+        o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+    float mA_run = -INFINITY, lA = 0.0f, mB_run = -INFINITY, lB = 0.0f;
+    const int mi = lane >> 3, rr = lane & 7;
+    const uint32_t k_row = (uint32_t)((((mi >> 1) << 3) + rr) * 128);
+    const uint32_t v_row = (uint32_t)((((mi & 1) << 3) + rr) * 128);
+    // When the whole chunk fits the ring (the usual case) every page is
+    // issued up front and the warps never wait for each other within the
+    // item; longer chunks re-issue stages behind a per-page CTA barrier.
+    const bool refill = np > kGroupStages;
+    for (int i = 0; i < np; i++) {
+        const int s = i % kGroupStages;
+        const bool ok = rt::mbar_wait_bounded(rt::smem_u32(&gbars[s]), (gphases >> s) & 1u,
+                                              kWaitLimitNs);
+        if (!refill) {
+            if (!__all_sync(0xffffffffu, ok)) {
+                if (lane == 0)
+                    flag_error(a.error, kErrTimeout);
+                return false;  // the caller stops the CTA; issued copies are waited for there
+            }
+        } else if (!__syncthreads_and(ok)) {
+            if (threadIdx.x == 0) {
+                flag_error(a.error, kErrTimeout);
+                // Give the copies still in flight (pages i .. i+11) a bounded
+                // chance to land before the shared memory is released.
+                for (int j = i; j < np && j < i + kGroupStages; j++) {
+                    const int s2 = j % kGroupStages;
+                    (void)rt::mbar_wait_bounded(rt::smem_u32(&gbars[s2]), (gphases >> s2) & 1u,
+                                                kWaitLimitNs / 4);
+                }
+            }
+            return false;
+        }
+        gphases ^= 1u << s;
+        if (active) {
+            const uint32_t st = ring0 + (uint32_t)(s * kStageBytes);
+            float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const int c = ((j & 3) << 1) + (mi & 1);
+                const uint32_t addr =
+                    st + (uint32_t)((j >> 2) * 2048) + k_row + (uint32_t)((c ^ rr) << 4);
+                uint32_t k0, k1, k2, k3;
+                rt::ldsm_x4(addr, k0, k1, k2, k3);
+                rt::mma_bf16_16816(sc[0], qf[j], k0, k1);
+                rt::mma_bf16_16816(sc[1], qf[j], k2, k3);
+            }
+            // rows rA (c0, c1) and rB (c2, c3); every token of a shared page is valid
+            const float a0 = sc[0][0] * a.scale_log2, a1 = sc[0][1] * a.scale_log2;
+            const float a2 = sc[1][0] * a.scale_log2, a3 = sc[1][1] * a.scale_log2;
+            const float b0 = sc[0][2] * a.scale_log2, b1 = sc[0][3] * a.scale_log2;
+            const float b2 = sc[1][2] * a.scale_log2, b3 = sc[1][3] * a.scale_log2;
+            float xa = fmaxf(fmaxf(a0, a1), fmaxf(a2, a3));
+            float xb = fmaxf(fmaxf(b0, b1), fmaxf(b2, b3));
+            xa = fmaxf(xa, __shfl_xor_sync(0xffffffffu, xa, 1));
+            xa = fmaxf(xa, __shfl_xor_sync(0xffffffffu, xa, 2));
+            xb = fmaxf(xb, __shfl_xor_sync(0xffffffffu, xb, 1));
+            xb = fmaxf(xb, __shfl_xor_sync(0xffffffffu, xb, 2));
+            const float nA = fmaxf(mA_run, xa), nB = fmaxf(mB_run, xb);
+            const float cA = rt::fast_exp2(mA_run - nA), cB = rt::fast_exp2(mB_run - nB);
+            const float pa0 = rt::fast_exp2(a0 - nA), pa1 = rt::fast_exp2(a1 - nA);
+            const float pa2 = rt::fast_exp2(a2 - nA), pa3 = rt::fast_exp2(a3 - nA);
+            const float pb0 = rt::fast_exp2(b0 - nB), pb1 = rt::fast_exp2(b1 - nB);
+            const float pb2 = rt::fast_exp2(b2 - nB), pb3 = rt::fast_exp2(b3 - nB);
+            lA = lA * cA + ((pa0 + pa1) + (pa2 + pa3));
+            lB = lB * cB + ((pb0 + pb1) + (pb2 + pb3));
+            mA_run = nA;
+            mB_run = nB;
+#pragma unroll
+            for (int n = 0; n < 16; n++) {
+                o[n][0] *= cA;
+                o[n][1] *= cA;
+                o[n][2] *= cB;
+                o[n][3] *= cB;
+            }
+            uint32_t pf[4], pl[4];  // P = hi + lo in bf16 (see process_item)
+            rt::split_bf16x2(pa0, pa1, pf[0], pl[0]);
+            rt::split_bf16x2(pb0, pb1, pf[1], pl[1]);
+            rt::split_bf16x2(pa2, pa3, pf[2], pl[2]);
+            rt::split_bf16x2(pb2, pb3, pf[3], pl[3]);
+#pragma unroll
+            for (int dd = 0; dd < 8; dd++) {
+                const int c = ((dd & 3) << 1) + (mi >> 1);
+                const uint32_t addr =
+                    st + 4096u + (uint32_t)((dd >> 2) * 2048) + v_row + (uint32_t)((c ^ rr) << 4);
+                uint32_t v0, v1, v2, v3;
+                rt::ldsm_x4_trans(addr, v0, v1, v2, v3);
+                rt::mma_bf16_16816(o[2 * dd], pf, v0, v1);
+                rt::mma_bf16_16816(o[2 * dd + 1], pf, v2, v3);
+                rt::mma_bf16_16816(o[2 * dd], pl, v0, v1);
+                rt::mma_bf16_16816(o[2 * dd + 1], pl, v2, v3);
+            }
+        }
+        if (refill) {
+            // Every warp has read stage s (shared-memory reads only, so the
+            // TMA rewrite needs no proxy fence).
+            __syncthreads();
+            if (warp == 0 && i + kGroupStages < np)
+                issue(i + kGroupStages);
+        }
+    }
+    if (!active)
+        return true;
+    lA += __shfl_xor_sync(0xffffffffu, lA, 1);
+    lA += __shfl_xor_sync(0xffffffffu, lA, 2);
+    lB += __shfl_xor_sync(0xffffffffu, lB, 1);
+    lB += __shfl_xor_sync(0xffffffffu, lB, 2);
+
+    // Partials of both rows of this lane; the kernel boundary publishes them.
+    if (vA) {
+        const size_t pi = (((size_t)bA * Hkv + h) * a.slots + chunk) * G + rA % G;
+        float *dst = a.part_o + pi * 128 + 2 * q4;
+#pragma unroll
+        for (int n = 0; n < 16; n++)
+            *reinterpret_cast<float2 *>(dst + n * 8) = make_float2(o[n][0], o[n][1]);
+        if (q4 == 0)
+            *reinterpret_cast<float2 *>(a.part_ml + pi * 2) = make_float2(mA_run, lA);
+    }
+    if (vB) {
+        const size_t pi = (((size_t)bB * Hkv + h) * a.slots + chunk) * G + rB % G;
+        float *dst = a.part_o + pi * 128 + 2 * q4;
+#pragma unroll
+        for (int n = 0; n < 16; n++)
+            *reinterpret_cast<float2 *>(dst + n * 8) = make_float2(o[n][2], o[n][3]);
+        if (q4 == 0)
+            *reinterpret_cast<float2 *>(a.part_ml + pi * 2) = make_float2(mB_run, lB);
+    }
+    return true;
 }
 
-// What one group item needs across the pipeline stages, per thread (row).
-struct TcItem {
-    uint64_t gi;          // dispenser index (>= n_gi: none)
-    uint32_t h, np, brow;  // KV head, pages, this row's sequence
-    int chunk, jrow;
-    bool vrow;            // this row is a valid member query
-};
-
+// Shared-prefix kernel of the grouped entry point: persistent CTAs take
+// (group, row block, head, chunk) items from a dispenser; the last CTA out
+// resets it for the next launch.
 template <int G>
 __global__ void __launch_bounds__(kWarps * 32, 2)
-paged_gqa_group_tc_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnArgs a)
+paged_gqa_group_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnArgs a)
 {
     extern __shared__ uint8_t smem_raw[];
-    __shared__ __align__(8) uint64_t tma_bar, mma_bar;
+    __shared__ __align__(8) uint64_t gbars[kGroupStages];
     __shared__ unsigned long long s_gitem;
-    __shared__ uint32_t s_tmem, s_ok;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t raw_u32 = rt::smem_u32(smem_raw);
-    const uint32_t base = (raw_u32 + 1023u) & ~1023u;  // 1 KiB-aligned swizzle atoms
-    uint8_t *base_ptr = smem_raw + (base - raw_u32);
-    const uint32_t QP = base, KP = base + kTcRegion, VV = base + 2 * kTcRegion;
-
-    if (warp == 0) {
-        rt::tmem_alloc(rt::smem_u32(&s_tmem), kTcCols);
-        rt::tmem_relinquish();
-    }
-    if (tid == 0) {
+    const uint32_t base_u32 = (raw_u32 + 1023u) & ~1023u;  // 128-byte swizzle: 1 KiB aligned
+    if (threadIdx.x == 0) {
         rt::prefetch_tensormap(&kv_map);
-        rt::mbar_init(rt::smem_u32(&tma_bar), 1u);
-        rt::mbar_init(rt::smem_u32(&mma_bar), 1u);
+        for (int s = 0; s < kGroupStages; s++)
+            rt::mbar_init(rt::smem_u32(&gbars[s]), 1u);
         rt::mbar_fence_init();
     }
-    rt::tc_fence_before_sync();
     __syncthreads();
-    rt::tc_fence_after_sync();
-    const uint32_t tmem = s_tmem;
     // The sequence kernel may start on SMs this grid leaves free; it waits
     // for this grid's completion before it reads the partials.
     asm volatile("griddepcontrol.launch_dependents;");
     const uint64_t policy = a.evict_first ? rt::l2_policy_evict_first() : rt::l2_policy_evict_normal();
-    const uint32_t Hkv = a.num_kv_heads, Hq = a.num_q_heads;
+    constexpr int RB = (16 * G + 16 * kWarps - 1) / (16 * kWarps);
     const uint32_t n_live = min(*a.n_groups, a.max_groups);
-    const uint64_t n_gi = (uint64_t)n_live * Hkv * a.max_gchunks;
-    const uint32_t idesc_s_base = rt::umma_idesc_bf16(128, 16, 0) & ~(0x3Fu << 17);
-    const uint32_t idesc_o = rt::umma_idesc_bf16(128, 128, 1);
-    const uint32_t r = (uint32_t)tid;
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
-    uint32_t tma_phase = 0, mma_phase = 0;
-
-    // Stage A of the next live item: take indices from the dispenser until
-    // one has work, load its page ids and issue its K/V TMA copies (warp 0),
-    // and stage its query rows into the Q tile.  Uniform across the CTA.
-    auto stage_a = [&](TcItem &it) {
-        for (;;) {
-            if (tid == 0)
-                s_gitem = atomicAdd(a.group_next, 1ull);
-            __syncthreads();
-            it.gi = s_gitem;
-            __syncthreads();
-            if (it.gi >= n_gi)
-                return;
-            const uint32_t g = (uint32_t)(it.gi % n_live);
-            const uint64_t rest = it.gi / n_live;
-            it.h = (uint32_t)(rest % Hkv);
-            it.chunk = (int)(rest / Hkv);
-            const rt_attn_group_t &grp = a.groups[g];
-            const uint32_t n_mem = min(grp.n_members, kMaxGroupMembers);
-            const int P = (int)grp.shared_pages;
-            const int p0 = it.chunk * (int)a.gchunk_pages;
-            const uint32_t src = grp.members[0];
-            if (n_mem == 0 || P == 0 || p0 >= P)
-                continue;
-            if (src >= a.num_seqs || (uint32_t)P > a.max_gchunks * a.gchunk_pages ||
-                (uint32_t)P > a.max_pages) {
-                if (tid == 0)
-                    flag_error(a.error, kErrGroup);
-                continue;
-            }
-            it.np = (uint32_t)(min(P, p0 + (int)a.gchunk_pages) - p0);
-            if (warp == 0) {
-                int pg = 0;
-                if ((uint32_t)lane < it.np) {
-                    pg = a.page_table[(size_t)src * a.max_pages + p0 + lane];
-                    if (pg < 0 || (uint64_t)pg >= a.arena_pages) {
-                        flag_error(a.error, kErrPage);
-                        pg = 0;
-                    }
-                }
-                if (lane == 0)
-                    rt::mbar_arrive_expect_tx(rt::smem_u32(&tma_bar), it.np * 8192u);
-                __syncwarp();
-                if ((uint32_t)lane < it.np) {
-                    const uint32_t bar = rt::smem_u32(&tma_bar);
-                    const int32_t row_k = (int32_t)(((int64_t)pg * Hkv + it.h) * 32);
-                    const uint32_t off = (uint32_t)lane * 2048u;
-                    rt::tma_load_2d(KP + off, &kv_map, 0, row_k, bar, policy);
-                    rt::tma_load_2d(KP + kTcHalf + off, &kv_map, 64, row_k, bar, policy);
-                    rt::tma_load_2d(VV + off, &kv_map, 0, row_k + 16, bar, policy);
-                    rt::tma_load_2d(VV + kTcHalf + off, &kv_map, 64, row_k + 16, bar, policy);
-                }
-            }
-            // query row r = member r/G, head r%G: the member's length,
-            // group coverage and q row load in one round trip
-            const int mrow = (int)(r / G);
-            it.jrow = (int)(r % G);
-            const bool inr = r < 16u * G && mrow < (int)n_mem;
-            uint32_t b = inr ? grp.members[mrow] : 0u;
-            const bool bok = inr && b < a.num_seqs;
-            if (!bok)
-                b = 0u;
-            const int L = a.seq_lens[b];
-            const uint32_t sk = a.skip_pages[b];
-            const uint4 *qrow = reinterpret_cast<const uint4 *>(
-                a.q + ((size_t)b * Hq + (size_t)it.h * G + it.jrow) * 128);
-            uint4 qv[16];
-#pragma unroll
-            for (int c = 0; c < 16; c++)
-                qv[c] = qrow[c];
-            it.vrow = bok && L >= 0 && (uint32_t)L <= a.max_seq_len &&
-                      (uint32_t)L <= a.max_pages * 16u && sk == (uint32_t)P && P <= ((L + 15) >> 4);
-            if (it.chunk == 0 && it.h == 0 && inr && it.jrow == 0 && !it.vrow)
-                flag_error(a.error, kErrGroup);
-            it.brow = b;
-#pragma unroll
-            for (int c = 0; c < 16; c++)
-                *reinterpret_cast<uint4 *>(base_ptr + tc_tile_off(r, (uint32_t)c)) =
-                    it.vrow ? qv[c] : make_uint4(0u, 0u, 0u, 0u);
-            rt::fence_proxy_async_smem();  // generic writes of Q before the MMA reads them
-            __syncthreads();
-            return;
-        }
-    };
-
-    TcItem cur;
-    stage_a(cur);
-    bool ok = true;
-    while (cur.gi < n_gi) {
-        const uint32_t ntok = cur.np * 16u;
-        // ---- S = Q K^T (one thread issues) ----
-        if (tid == 0) {
-            bool good = rt::mbar_wait_bounded(rt::smem_u32(&tma_bar), tma_phase, kWaitLimitNs);
-            if (good) {
-                rt::tc_fence_after_sync();
-                const uint32_t idesc_s = idesc_s_base | ((ntok >> 3) << 17);
-#pragma unroll
-                for (int kk = 0; kk < 8; kk++) {
-                    const uint32_t koff = (uint32_t)(kk >> 2) * kTcHalf + (uint32_t)(kk & 3) * 32u;
-                    rt::umma_bf16_ss(tmem, rt::umma_desc_sw128(QP + koff, 16u, 1024u),
-                                     rt::umma_desc_sw128(KP + koff, 16u, 1024u), idesc_s,
-                                     kk > 0 ? 1u : 0u);
-                }
-                rt::umma_commit(rt::smem_u32(&mma_bar));
-                good = rt::mbar_wait_bounded(rt::smem_u32(&mma_bar), mma_phase, kWaitLimitNs);
-            }
-            s_ok = good ? 1u : 0u;
-            rt::tc_fence_before_sync();
-        }
+    const uint64_t n_gi = (uint64_t)n_live * RB * a.num_kv_heads * a.max_gchunks;
+    uint32_t gphases = 0;
+    while (n_gi) {
+        if (threadIdx.x == 0)
+            s_gitem = atomicAdd(a.group_next, 1ull);
         __syncthreads();
-        rt::tc_fence_after_sync();
-        tma_phase ^= 1u;
-        mma_phase ^= 1u;
-        if (!s_ok) {
-            ok = false;
+        const uint64_t gi = s_gitem;
+        __syncthreads();
+        if (gi >= n_gi)
+            break;
+        // A false return means a wait expired (flagged): stop taking items,
+        // after giving the copies still in flight a bounded chance to land.
+        const bool ok = process_group_item<G>(kv_map, a, gi, n_live, base_u32, gbars, gphases, policy);
+        if (!__syncthreads_and(ok)) {
+            if (threadIdx.x == 0)
+                for (int st = 0; st < kGroupStages; st++)
+                    (void)rt::mbar_wait_bounded(rt::smem_u32(&gbars[st]), (gphases >> st) & 1u,
+                                                kWaitLimitNs / 64);
             break;
         }
-
-        // ---- softmax of row r over the chunk's tokens (log2 domain) ----
-        float x[128];
-#pragma unroll
-        for (int c4 = 0; c4 < 4; c4++) {
-            uint32_t v[32];
-            rt::tmem_ld32(lane_base + (uint32_t)(c4 * 32), v);
-            rt::tmem_ld_wait();
-#pragma unroll
-            for (int k = 0; k < 32; k++)
-                x[c4 * 32 + k] = __uint_as_float(v[k]) * a.scale_log2;
-        }
-        float mrun = -INFINITY;
-#pragma unroll
-        for (int c = 0; c < 128; c++)
-            if ((uint32_t)c < ntok)
-                mrun = fmaxf(mrun, x[c]);
-        float lsum = 0.0f;
-#pragma unroll
-        for (int c8 = 0; c8 < 16; c8++) {
-            if ((uint32_t)c8 * 8u >= ntok)
-                break;
-            uint32_t hi[4], lo[4];
-#pragma unroll
-            for (int k = 0; k < 4; k++) {
-                const float p0v = rt::fast_exp2(x[c8 * 8 + 2 * k] - mrun);
-                const float p1v = rt::fast_exp2(x[c8 * 8 + 2 * k + 1] - mrun);
-                lsum += p0v + p1v;
-                rt::split_bf16x2(p0v, p1v, hi[k], lo[k]);
-            }
-            const uint32_t off = tc_tile_off(r, (uint32_t)c8);
-            *reinterpret_cast<uint4 *>(base_ptr + (QP - base) + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-            *reinterpret_cast<uint4 *>(base_ptr + (KP - base) + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-        }
-        rt::fence_proxy_async_smem();  // P (generic writes) before the MMA reads it
-        rt::tc_fence_before_sync();
-        __syncthreads();
-
-        // ---- O = P_hi V + P_lo V ----
-        if (tid == 0) {
-            rt::tc_fence_after_sync();
-            for (int pass = 0; pass < 2; pass++) {
-                const uint32_t A = pass ? KP : QP;
-                for (int kk = 0; kk < (int)cur.np; kk++) {
-                    const uint32_t aoff = (uint32_t)(kk >> 2) * kTcHalf + (uint32_t)(kk & 3) * 32u;
-                    rt::umma_bf16_ss(tmem + 128u, rt::umma_desc_sw128(A + aoff, 16u, 1024u),
-                                     rt::umma_desc_sw128(VV + (uint32_t)kk * 2048u, kTcHalf, 1024u),
-                                     idesc_o, (pass > 0 || kk > 0) ? 1u : 0u);
-                }
-            }
-            rt::umma_commit(rt::smem_u32(&mma_bar));
-            s_ok = rt::mbar_wait_bounded(rt::smem_u32(&mma_bar), mma_phase, kWaitLimitNs) ? 1u : 0u;
-            rt::tc_fence_before_sync();
-        }
-        __syncthreads();
-        rt::tc_fence_after_sync();
-        mma_phase ^= 1u;
-        if (!s_ok) {
-            ok = false;
-            break;
-        }
-
-        // ---- next item's stage A (the tiles are free once O is complete),
-        // overlapping this item's epilogue below ----
-        TcItem nxt;
-        stage_a(nxt);
-
-        // ---- partial of row r: (O, max, sum); the TMEM loads are
-        // warp-collective, only the stores depend on the row ----
-        {
-            const size_t pi = (((size_t)cur.brow * Hkv + cur.h) * a.slots + cur.chunk) * G + cur.jrow;
-            float4 *dst = reinterpret_cast<float4 *>(a.part_o + pi * 128);
-#pragma unroll
-            for (int c4 = 0; c4 < 4; c4++) {
-                uint32_t v[32];
-                rt::tmem_ld32(lane_base + 128u + (uint32_t)(c4 * 32), v);
-                rt::tmem_ld_wait();
-                if (cur.vrow) {
-#pragma unroll
-                    for (int k = 0; k < 8; k++)
-                        dst[c4 * 8 + k] =
-                            make_float4(__uint_as_float(v[4 * k]), __uint_as_float(v[4 * k + 1]),
-                                        __uint_as_float(v[4 * k + 2]), __uint_as_float(v[4 * k + 3]));
-                }
-            }
-            if (cur.vrow)
-                *reinterpret_cast<float2 *>(a.part_ml + pi * 2) = make_float2(mrun, lsum);
-        }
-        rt::tc_fence_before_sync();
-        __syncthreads();  // O has been read: the next item's MMAs may overwrite TMEM
-        rt::tc_fence_after_sync();
-        cur = nxt;
     }
-    if (!ok) {
-        if (tid == 0) {
-            flag_error(a.error, kErrTimeout);
-            // a bounded chance for copies and MMAs still in flight to land
-            (void)rt::mbar_wait_bounded(rt::smem_u32(&tma_bar), tma_phase, kWaitLimitNs / 16);
-            (void)rt::mbar_wait_bounded(rt::smem_u32(&mma_bar), mma_phase, kWaitLimitNs / 16);
-        }
-    }
-
-    if (tid == 0) {
+    if (threadIdx.x == 0) {
         __threadfence();
         if (atomicAdd(a.group_done, 1u) == gridDim.x - 1u) {
             *a.group_next = 0ull;
@@ -816,11 +805,6 @@ paged_gqa_group_tc_kernel(const __grid_constant__ CUtensorMap kv_map, const Attn
             __threadfence();
         }
     }
-    rt::tc_fence_before_sync();
-    __syncthreads();
-    rt::tc_fence_after_sync();
-    if (warp == 0)
-        rt::tmem_dealloc(tmem, kTcCols);
 }
 
 // Persistent warps take items in increasing order from a global dispenser
@@ -881,7 +865,7 @@ struct Plan {
     size_t off_counters, off_ml, off_o, total;
 };
 
-constexpr uint32_t kDefaultGroupChunkPages = 8;
+constexpr uint32_t kDefaultGroupChunkPages = 16;
 
 // Workspace header: error word at 0, per-warp item dispenser at 8/16, group
 // item dispenser at 24/32; arrival counters from 256.
@@ -938,8 +922,6 @@ int make_plan(const rt_attn_params_t *p, Plan *pl, const rt_attn_group_params_t 
     pl->max_gchunks = 0;
     if (gp) {
         uint32_t cpg = gp->chunk_pages ? gp->chunk_pages : kDefaultGroupChunkPages;
-        if (cpg > (uint32_t)kTcPages)
-            cpg = (uint32_t)kTcPages;  // one tensor-core item covers at most 128 tokens
         if (gp->max_groups == 0 || gp->max_groups > (1u << 24) || cpg > (uint32_t)kMaxChunkPages ||
             gp->max_shared_pages > pages_max) {
             rt::set_error("attention: group params out of range (max_groups %u, "
@@ -1006,7 +988,7 @@ int prepare_g()
     e = cudaFuncSetAttribute(paged_gqa_decode_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kSmemBytes);
     if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(paged_gqa_group_tc_kernel<G>,
+        e = cudaFuncSetAttribute(paged_gqa_group_kernel<G>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess)
         return rt::cuda_fail(e, "attention: cudaFuncSetAttribute");
@@ -1041,7 +1023,7 @@ int launch_g(const CUtensorMap &map, const AttnArgs &args, dim3 grid, cudaStream
     // prologue and suffix pages; each waits for the group grid (griddepcontrol)
     // only before folding in the prefix partials.
     const dim3 ggrid((unsigned)rt::num_sms() * 2u);
-    paged_gqa_group_tc_kernel<G><<<ggrid, kWarps * 32, kSmemBytes, s>>>(map, args);
+    paged_gqa_group_kernel<G><<<ggrid, kWarps * 32, kSmemBytes, s>>>(map, args);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess)
         return rt::cuda_fail(e, "attention: group launch");

@@ -105,8 +105,8 @@ int rt_paged_decode_attention_noalloc(const rt_attn_params_t *p,
  * with the same pages (the copy-on-write prefix of kv_prefix.h).  A group
  * record lists such sequences; their common full pages are read from HBM once
  * per group and each page is multiplied against every member's queries in
- * one tensor-core tile (up to 16 sequences x G heads = 128 query rows,
- * tcgen05 with TMEM accumulators), instead of once per sequence.  The sequences' remaining pages are processed as in
+ * one tensor-core tile (16 query rows = 16/G sequences x G heads), instead of
+ * once per sequence.  The sequences' remaining pages are processed as in
  * rt_paged_decode_attention and the two parts merged exactly (log-sum-exp),
  * so the result equals rt_paged_decode_attention's to fp32 rounding.
  *
@@ -129,7 +129,7 @@ typedef struct {
 typedef struct {
     uint32_t max_groups;         /* capacity of the groups array */
     uint32_t max_shared_pages;   /* bound on every shared_pages */
-    uint32_t chunk_pages;        /* shared pages per work item, at most 8; 0 = 8 */
+    uint32_t chunk_pages;        /* shared pages per work item; 0 = auto (16) */
     uint32_t reserved;
 } rt_attn_group_params_t;
 
