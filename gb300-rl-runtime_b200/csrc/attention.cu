@@ -395,7 +395,7 @@ __device__ __forceinline__ bool process_item(const CUtensorMap &kv_map, const At
         // kernel launched just before this one as a programmatic dependent
         // launch, so this is where its completion is awaited - after this
         // warp's own pages, by when it has usually finished.
-        asm volatile("griddepcontrol.wait;" ::: "memory");
+        rt::grid_dep_wait();
         const size_t pi0 = (bh * a.slots) * G;
         float M0 = m0, M1 = m1;
         for (uint32_t k = 0; k < n_g; k++) {
@@ -770,9 +770,12 @@ paged_gqa_group_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnArg
         rt::mbar_fence_init();
     }
     __syncthreads();
+    // Launched as a programmatic dependent of the kernel that wrote the
+    // queries and tables: wait for it before reading anything.
+    rt::grid_dep_wait();
     // The sequence kernel may start on SMs this grid leaves free; it waits
     // for this grid's completion before it reads the partials.
-    asm volatile("griddepcontrol.launch_dependents;");
+    rt::grid_dep_launch();
     const uint64_t policy = a.evict_first ? rt::l2_policy_evict_first() : rt::l2_policy_evict_normal();
     constexpr int RB = (16 * G + 16 * kWarps - 1) / (16 * kWarps);
     const uint32_t n_live = min(*a.n_groups, a.max_groups);
@@ -834,6 +837,9 @@ paged_gqa_decode_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnAr
         rt::fence_proxy_async_smem();
     }
     __syncwarp();
+    // The next kernel of the stream (launched as a programmatic dependent)
+    // may be scheduled once every CTA of this grid has started.
+    rt::grid_dep_launch();
     const uint64_t policy = a.evict_first ? rt::l2_policy_evict_first() : rt::l2_policy_evict_normal();
     uint32_t phases = 0;
     unsigned long long grab = 0;
@@ -1022,9 +1028,19 @@ int launch_g(const CUtensorMap &map, const AttnArgs &args, dim3 grid, cudaStream
     // launch: its CTAs start on SMs the group grid frees and run their own
     // prologue and suffix pages; each waits for the group grid (griddepcontrol)
     // only before folding in the prefix partials.
-    const dim3 ggrid((unsigned)rt::num_sms() * 2u);
-    paged_gqa_group_kernel<G><<<ggrid, kWarps * 32, kSmemBytes, s>>>(map, args);
-    cudaError_t e = cudaGetLastError();
+    // The group kernel itself is a programmatic dependent of whatever ran
+    // before it (it waits for that kernel before reading its inputs).
+    cudaLaunchAttribute pdl[1];
+    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t gcfg = {};
+    gcfg.gridDim = dim3((unsigned)rt::num_sms() * 2u);
+    gcfg.blockDim = dim3(kWarps * 32);
+    gcfg.dynamicSmemBytes = kSmemBytes;
+    gcfg.stream = s;
+    gcfg.attrs = pdl;
+    gcfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&gcfg, paged_gqa_group_kernel<G>, map, args);
     if (e != cudaSuccess)
         return rt::cuda_fail(e, "attention: group launch");
     cudaLaunchConfig_t cfg = {};

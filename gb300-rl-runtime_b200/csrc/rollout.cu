@@ -607,6 +607,9 @@ schedule_kernel(const Dev d, cudaGraphConditionalHandle handle, int in_graph)
 {
     __shared__ SchedShared sh;
     const bool full = d.decode == RT_ROLLOUT_DECODE_FULL;
+    // The prepare kernel (a programmatic dependent launch) may be scheduled
+    // now; it waits for this kernel to complete before reading its outputs.
+    rt::grid_dep_launch();
     load_state(d, sh, full);
     const bool stop = schedule_pass(d, sh);
     if (stop) {
@@ -632,6 +635,8 @@ schedule_kernel(const Dev d, cudaGraphConditionalHandle handle, int in_graph)
 __global__ void __launch_bounds__(256) prepare_kernel(const Dev d)
 {
     const uint32_t s = blockIdx.x;
+    rt::grid_dep_wait();    // the schedule kernel's plan is complete
+    rt::grid_dep_launch();  // the attention kernels may be scheduled
     if (!d.enable[s])
         return;
     SlotExt &e = d.ext[s];
@@ -698,11 +703,32 @@ __device__ __forceinline__ void logits_row(float *out, uint32_t vocab, uint64_t 
 __global__ void __launch_bounds__(256) logits_kernel(const Dev d)
 {
     const uint32_t s = blockIdx.y;
-    if (!d.enable[s])
-        return;
-    const rt_sample_row_t r = d.srows[s];
-    logits_row(d.logits + (size_t)s * d.vocab, d.vocab, r.seed, r.rollout_id, r.step, d.logit_std,
-               blockIdx.x * blockDim.x + threadIdx.x, gridDim.x * blockDim.x);
+    rt::grid_dep_wait();  // launched as a programmatic dependent of the attention
+    if (d.enable[s]) {
+        const rt_sample_row_t r = d.srows[s];
+        logits_row(d.logits + (size_t)s * d.vocab, d.vocab, r.seed, r.rollout_id, r.step,
+                   d.logit_std, blockIdx.x * blockDim.x + threadIdx.x, gridDim.x * blockDim.x);
+    }
+    // The sampler may be scheduled once every CTA has written its logits.
+    rt::grid_dep_launch();
+}
+
+// Launch as a programmatic dependent of the previous kernel in the stream.
+template <typename... Args>
+cudaError_t launch_pdl(void (*kernel)(Args...), dim3 grid, dim3 block, cudaStream_t st,
+                       const Args &...args)
+{
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
 __global__ void logits_synth_kernel(float *out, uint32_t vocab, uint64_t seed, uint32_t rq,
@@ -767,7 +793,11 @@ int launch_decode(rt_rollout *e, cudaStream_t st, cudaEvent_t *ev)
     const Dev &d = e->d;
     if (ev)
         cudaEventRecord(ev[0], st);
-    prepare_kernel<<<d.max_slots, 256, 0, st>>>(d);
+    // Every kernel of the chain is a programmatic dependent launch: it may be
+    // scheduled while its predecessor finishes and waits for it on the GPU.
+    cudaError_t err = launch_pdl(prepare_kernel, dim3(d.max_slots), dim3(256), st, d);
+    if (err != cudaSuccess)
+        return rt::cuda_fail(err, "rollout: prepare launch");
     if (ev)
         cudaEventRecord(ev[1], st);
     int rc = d.max_groups
@@ -781,7 +811,9 @@ int launch_decode(rt_rollout *e, cudaStream_t st, cudaEvent_t *ev)
     if (ev)
         cudaEventRecord(ev[2], st);
     const dim3 lg((d.vocab / 4u + 1023u) / 1024u, d.max_slots);
-    logits_kernel<<<lg, 256, 0, st>>>(d);
+    err = launch_pdl(logits_kernel, lg, dim3(256), st, d);
+    if (err != cudaSuccess)
+        return rt::cuda_fail(err, "rollout: logits launch");
     if (ev)
         cudaEventRecord(ev[3], st);
     rt_sample_params_t sp;
@@ -790,7 +822,7 @@ int launch_decode(rt_rollout *e, cudaStream_t st, cudaEvent_t *ev)
     sp.row_stride = d.vocab;
     sp.fused_cum = 1u;
     sp.row_enable = d.enable;
-    rc = rt_sample_rows(&sp, d.logits, d.srows, d.tokens, st);
+    rc = rt::sample_rows_launch(&sp, d.logits, d.srows, d.tokens, st, true);
     if (ev)
         cudaEventRecord(ev[4], st);
     return rc;

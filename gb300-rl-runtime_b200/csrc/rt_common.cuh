@@ -163,6 +163,20 @@ __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x)
     return y;
 }
 
+// Programmatic dependent launch: a kernel launched with the programmatic
+// stream-serialization attribute may start before its predecessor in the
+// stream has finished; grid_dep_wait() blocks until that predecessor has
+// completed and its memory is visible (a no-op for an ordinary launch), and
+// grid_dep_launch() lets the next such kernel start early.
+__device__ __forceinline__ void grid_dep_wait()
+{
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dep_launch()
+{
+    asm volatile("griddepcontrol.launch_dependents;");
+}
+
 // 2^x with the SFU (ex2.approx, flush-to-zero); 2^-inf = +0.
 __device__ __forceinline__ float fast_exp2(float x)
 {

@@ -1,5 +1,7 @@
 // rt_internal.h - cross-file hooks inside librlrt_b200.so (not exported).
 #pragma once
+#include <cuda_runtime.h>
+
 #include "rlrt.h"
 
 namespace rt {
@@ -8,4 +10,9 @@ namespace rt {
 int attn_prepare(const rt_attn_params_t *p);
 // Same for the sampler (its shared-memory opt-in).
 int sample_prepare();
+// rt_sample_rows with an optional programmatic dependent launch (the kernel
+// waits for the previous kernel of the stream before reading the logits).
+int sample_rows_launch(const rt_sample_params_t *p, const float *logits,
+                       const rt_sample_row_t *rows, uint32_t *tokens_out, cudaStream_t stream,
+                       bool pdl);
 }  // namespace rt

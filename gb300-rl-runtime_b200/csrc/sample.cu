@@ -306,6 +306,9 @@ __global__ void __launch_bounds__(kThr, 2) sample_rows_kernel(const SampleArgs a
     const int tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5;
     const uint32_t V = a.vocab;
+    // When launched as a programmatic dependent of the kernel that wrote the
+    // logits, wait for it before reading them (a no-op otherwise).
+    rt::grid_dep_wait();
     if (a.enable && a.enable[blockIdx.x] == 0u)
         return;
     const rt_sample_row_t P = a.rows[blockIdx.x];
@@ -586,6 +589,13 @@ extern "C" uint32_t rt_sample_uniform24(uint64_t seed, uint32_t rollout_id, uint
 extern "C" int rt_sample_rows(const rt_sample_params_t *p, const float *logits,
                               const rt_sample_row_t *rows, uint32_t *tokens_out, void *stream)
 {
+    return rt::sample_rows_launch(p, logits, rows, tokens_out, (cudaStream_t)stream, false);
+}
+
+int rt::sample_rows_launch(const rt_sample_params_t *p, const float *logits,
+                           const rt_sample_row_t *rows, uint32_t *tokens_out, cudaStream_t stream,
+                           bool pdl)
+{
     if (!p || !logits || !rows || !tokens_out) {
         rt::set_error("sample: null argument");
         return RT_EINVAL;
@@ -619,7 +629,22 @@ extern "C" int rt_sample_rows(const rt_sample_params_t *p, const float *logits,
     const int rc = rt::sample_prepare();
     if (rc != RT_OK)
         return rc;
-    sample_rows_kernel<<<p->num_rows, kThr, dyn, (cudaStream_t)stream>>>(a);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e;
+    if (pdl) {
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(p->num_rows);
+        cfg.blockDim = dim3(kThr);
+        cfg.dynamicSmemBytes = dyn;
+        cfg.stream = stream;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, sample_rows_kernel, a);
+    } else {
+        sample_rows_kernel<<<p->num_rows, kThr, dyn, stream>>>(a);
+        e = cudaGetLastError();
+    }
     return e == cudaSuccess ? RT_OK : rt::cuda_fail(e, "sample: launch");
 }
