@@ -151,6 +151,16 @@ class rt_rollout_buffers_t(ctypes.Structure):
         ("max_pages", ctypes.c_uint32), ("max_groups", ctypes.c_uint32)]
 
 
+class rt_decode_worker_stats_t(ctypes.Structure):
+    _fields_ = [("consumed", ctypes.c_uint64), ("completed", ctypes.c_uint64)] + [
+        (n, ctypes.c_uint32) for n in ("published", "sentinels", "comp_ring_full")] + [
+        ("error", ctypes.c_int32)] + [
+        (n, ctypes.c_uint32) for n in ("bad_block", "workers", "finished", "pad")]
+
+    def as_dict(self):
+        return {n: getattr(self, n) for n, _ in self._fields_ if n != "pad"}
+
+
 PASS_HOOK = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_uint64)
 
 
@@ -213,6 +223,16 @@ _SIGS = {
     "rt_rollout_worker_stats": (ctypes.c_int, [_P, ctypes.POINTER(rt_rollout_stats_t)]),
     "rt_host_pump": (ctypes.c_int64, [_P, _P, ctypes.c_uint32, _P, _P, ctypes.c_uint32,
                                       ctypes.c_int, ctypes.c_uint32]),
+    "rt_launch_decode_worker": (ctypes.c_int, [_P, ctypes.POINTER(KVArena), _P, _P, _P, _P,
+                                               ctypes.c_uint32, _P, ctypes.c_uint32,
+                                               ctypes.c_uint32, _P]),
+    "rt_decode_worker_stats": (ctypes.c_int, [_P, ctypes.POINTER(rt_decode_worker_stats_t)]),
+    "rt_attention_fixed128": (ctypes.c_int, [_P, ctypes.c_uint32, ctypes.POINTER(KVArena), _P,
+                                             _P, _P, ctypes.c_uint32, _P, _P]),
+    "rt_host_decode_pump": (ctypes.c_int64, [_P, _P, ctypes.c_uint32, ctypes.c_uint32, _P, _P,
+                                             ctypes.c_uint32, ctypes.c_uint32]),
+    "ring_create": (_P, []), "ring_destroy": (None, [_P]),
+    "comp_ring_create": (_P, []), "comp_ring_destroy": (None, [_P]),
     "req_ring_create": (_P, []), "req_ring_destroy": (None, [_P]),
     "done_ring_create": (_P, []), "done_ring_destroy": (None, [_P]),
     "arena_init": (None, [ctypes.POINTER(KVArena), ctypes.c_size_t, ctypes.c_size_t]),
@@ -259,7 +279,7 @@ def _stream_ptr(stream):
 
 
 def _ptr(t) -> ctypes.c_void_p:
-    return ctypes.c_void_p(t.data_ptr())
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
 
 
 # --------------------------------------------------------------- attention
@@ -589,6 +609,93 @@ class HostRings:
             lib().req_ring_destroy(self.req)
             lib().done_ring_destroy(self.done)
             self.req = self.done = None
+
+
+class CommandRings:
+    """A CommandRing and a CompletionRing in pinned, device-mapped host
+    memory (the per-step decode path's rings)."""
+
+    def __init__(self):
+        self.cmd = lib().ring_create()
+        self.comp = lib().comp_ring_create()
+        if not self.cmd or not self.comp:
+            raise RuntimeErrorRT("ring allocation failed")
+
+    def header(self, which):
+        """(head, tail) of 'cmd' or 'comp' (plus the comp overflow counter)."""
+        base = self.cmd if which == "cmd" else self.comp
+        head = ctypes.c_uint32.from_address(base).value
+        tail = ctypes.c_uint32.from_address(base + 64).value
+        if which == "cmd":
+            return head, tail
+        return head, tail, ctypes.c_uint32.from_address(base + 128).value
+
+    def pump(self, descs, n_sentinels, n_expected, timeout_ms=60000):
+        """rt_host_decode_pump: descs holds 32-byte Descriptor records;
+        returns (n drained, Completion bytes)."""
+        import numpy as np
+        d = np.ascontiguousarray(descs)
+        if d.nbytes % 32:
+            raise ValueError("descs must be whole 32-byte Descriptor records")
+        out = np.zeros(max(n_expected, 1) * 32, dtype=np.uint8)
+        n = lib().rt_host_decode_pump(self.cmd, d.ctypes.data_as(ctypes.c_void_p), d.nbytes // 32,
+                                      n_sentinels, self.comp,
+                                      out.ctypes.data_as(ctypes.c_void_p), n_expected, timeout_ms)
+        return n, out
+
+    def close(self):
+        if self.cmd:
+            lib().ring_destroy(self.cmd)
+            lib().comp_ring_destroy(self.comp)
+            self.cmd = self.comp = None
+
+
+def device_arena(arena_u8, block_size):
+    """A KVArena describing an existing device buffer (torch uint8) of
+    whole blocks; the bitmap stays empty (no allocation through it)."""
+    a = KVArena()
+    a.base = arena_u8.data_ptr()
+    a.capacity = arena_u8.numel()
+    a.block_size = block_size
+    return a
+
+
+def launch_decode_worker(rings, arena, sample_st=None, q_buffer=None, o_buffer=None,
+                         io_slots=0, step_count=None, stop_sentinels=1, idle_timeout_ms=0,
+                         stream=None):
+    check(lib().rt_launch_decode_worker(rings.cmd, ctypes.byref(arena), rings.comp,
+                                        _ptr(sample_st), _ptr(q_buffer), _ptr(o_buffer),
+                                        io_slots, _ptr(step_count), stop_sentinels,
+                                        idle_timeout_ms, _stream_ptr(stream)),
+          "rt_launch_decode_worker")
+
+
+def decode_worker_stats(stream=None):
+    st = rt_decode_worker_stats_t()
+    check(lib().rt_decode_worker_stats(_stream_ptr(stream), ctypes.byref(st)),
+          "rt_decode_worker_stats")
+    return st.as_dict()
+
+
+def attention_fixed128(descs, arena, sample_st=None, q_buffer=None, o_buffer=None, io_slots=0,
+                       stream=None):
+    """rt_attention_fixed128 over a numpy array of 32-byte Descriptor
+    records; returns the DecodeStepResult records as numpy
+    (path_kind, token_id, bytes_touched, tile_count, cycle_estimate)."""
+    import numpy as np
+    import torch
+    d = np.ascontiguousarray(descs)
+    n = d.nbytes // 32
+    dev = torch.device("cuda", torch.cuda.current_device())
+    dd = torch.from_numpy(d.view(np.uint8).copy()).to(dev)
+    res = torch.zeros(max(n, 1) * 24, dtype=torch.uint8, device=dev)
+    check(lib().rt_attention_fixed128(_ptr(dd) if n else None, n, ctypes.byref(arena),
+                                      _ptr(sample_st), _ptr(q_buffer), _ptr(o_buffer), io_slots,
+                                      _ptr(res), _stream_ptr(stream)), "rt_attention_fixed128")
+    torch.cuda.synchronize()
+    dt = np.dtype([("path_kind", "<u4"), ("token_id", "<u4"), ("bytes_touched", "<u4"),
+                   ("tile_count", "<u4"), ("cycle_estimate", "<u8")])
+    return res.cpu().numpy().view(dt)[:n]
 
 
 # ----------------------------------------------------------- rewards / NCCL

@@ -57,3 +57,49 @@ rt_host_pump(RequestRing *rq, const RolloutRequest *reqs, uint32_t n, DoneRing *
     }
     return (int64_t)drained;
 }
+
+int64_t
+rt_host_decode_pump(CommandRing *ring, const Descriptor *descs, uint32_t n, uint32_t n_sentinels,
+                    CompletionRing *comp, Completion *out, uint32_t n_expected,
+                    uint32_t timeout_ms)
+{
+    uint32_t pushed = 0, sent = 0, drained = 0;
+    const uint64_t t0 = pump_now_ms();
+
+    if (!ring || !comp || (n && !descs) || (n_expected && !out))
+        return -1;
+    while (drained < n_expected || pushed < n || sent < n_sentinels) {
+        int progress = 0;
+        /* descriptors first, then the stop records, as many as fit; one
+         * tail release per batch (reference decode_batch_submit) */
+        uint32_t head = rt_load_acquire_u32(&ring->cons.head);
+        uint32_t tail = rt_load_relaxed_u32(&ring->prod.tail);
+        uint32_t room = (uint32_t)RING_SIZE - (tail - head);
+        uint32_t k = 0;
+        while (k < room && (pushed < n || sent < n_sentinels)) {
+            Descriptor *slot = &ring->slots[(tail + k) & (RING_SIZE - 1u)];
+            if (pushed < n) {
+                *slot = descs[pushed++];
+            } else {
+                memset(slot, 0, sizeof(*slot));
+                slot->seq_id = UINT64_MAX;
+                sent++;
+            }
+            k++;
+        }
+        if (k) {
+            ring_commit(ring, k);
+            progress = 1;
+        }
+        while (drained < n_expected && comp_ring_poll(comp, &out[drained]))
+            drained++, progress = 1;
+        if (!progress) {
+            if (timeout_ms && pump_now_ms() - t0 > timeout_ms)
+                return -1;
+#if defined(__x86_64__)
+            __asm__ volatile("pause" ::: "memory");
+#endif
+        }
+    }
+    return (int64_t)drained;
+}

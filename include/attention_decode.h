@@ -5,7 +5,7 @@
  *
  * The reference's __device__ attention_decode_step_fixed128() is not an
  * exported symbol; its B200 replacement runs inside the persistent decode
- * worker (rlrt.h rt_decode_worker_launch) and as the standalone launcher
+ * worker (rlrt.h rt_launch_decode_worker) and as the standalone launcher
  * rt_attention_fixed128().
  */
 #pragma once

@@ -18,6 +18,7 @@
 #include "kv_prefix.h"
 #include "arena.h"
 #include "reward.h"
+#include "attention_decode.h"
 
 #ifdef __cplusplus
 extern "C" {
@@ -378,6 +379,80 @@ int rt_launch_rollout_worker(RequestRing *req_ring, DoneRing *done_ring,
 /* Counters of the last rt_launch_rollout_worker on the current device
  * (reads device memory on `stream`; safe while the worker runs). */
 int rt_rollout_worker_stats(void *stream, rt_rollout_stats_t *stats);
+
+/* ------------------------------------------------------------------------
+ * Per-step CommandRing decode path: the persistent decode worker and the
+ * fixed128 attention step (reference cu/worker.cu:25-131,
+ * cu/attention_decode.cu:16-204).
+ *
+ * The step, per Descriptor: seq_len = num_kv_blocks (0 -> 1) clamped to 32
+ * tokens of the 16 KiB fp16 block arena[kv_block_offset] (K plane then V
+ * plane, kv_layout.h); slot = io_slots ? output_token_offset & (io_slots-1)
+ * : 0; q = q_buffer[slot] (fp16 [128]) or, when q_buffer is NULL, the
+ * reference's synthesized query (seq_id, reward_cookie and, when sample_st
+ * is given, sample_st->rng_state); o = softmax(q.K^T / sqrt(128)).V,
+ * written to o_buffer[slot] (fp32 [128]) when given; token_id = argmax o
+ * with the reference's tie order (lowest d mod 32, then lowest d / 32);
+ * cycle_estimate = ceil(seq_len/16) * 128 * 24.  The fp32 evaluation order
+ * is the reference kernel's, so o and token_id are identical to it.
+ * ---------------------------------------------------------------------- */
+typedef struct {
+    uint64_t consumed;        /* CommandRing records taken, sentinels included (final) */
+    uint64_t completed;       /* Completion records pushed (== step_count increments) */
+    uint32_t published;       /* work descriptors handed to the worker warps */
+    uint32_t sentinels;       /* stop sentinels taken (final) */
+    uint32_t comp_ring_full;  /* times a finished completion found the CompletionRing full */
+    int32_t  error;           /* RT_OK, RT_ETIMEOUT (a bounded wait expired) or
+                                 RT_EDEVICE (kv_block_offset outside the arena) */
+    uint32_t bad_block;       /* first out-of-range kv_block_offset */
+    uint32_t workers;         /* worker warps in the grid */
+    uint32_t finished;        /* 1 once the worker kernel has stopped */
+    uint32_t pad;
+} rt_decode_worker_stats_t;
+
+/* Drop-in for the reference launch
+ *     decode_worker<<<num_SMs, 32, 3 * 16384>>>(cmd_ring, &kv_arena, comp_ring,
+ *         sample_st, q_buffer, o_buffer, io_slots, step_count)
+ * (reference src/main.c:229-235, kernel cu/worker.cu:77-131).  Returns
+ * after the launch.  One pump warp takes CommandRing records in batches
+ * (the ring keeps one consumer) and delivers Completions in ring order
+ * (the CompletionRing keeps one producer); the other warps of one CTA per
+ * SM run the step.  `arena` is the host KVArena (its device base and
+ * block_size, >= 16 KiB, are read here); sample_st, q_buffer, o_buffer and
+ * step_count are device pointers (each may be NULL).  The worker stops at
+ * the stop_sentinels-th record with seq_id == UINT64_MAX (0 = the device's
+ * SM count, one per reference worker warp as src/main.c:179-190 pushes);
+ * records behind it stay in the ring.  A kv_block_offset outside the
+ * arena yields a Completion with token_id = UINT32_MAX, cycles_taken = 0
+ * and flags RT_EDEVICE; idle_timeout_ms (0 = 10 s) without progress ends
+ * the worker with RT_ETIMEOUT.  One decode worker per device at a time. */
+int rt_launch_decode_worker(CommandRing *ring, const KVArena *arena, CompletionRing *comp_ring,
+                            const SampleState *sample_st, const void *q_buffer, float *o_buffer,
+                            uint32_t io_slots, uint64_t *step_count, uint32_t stop_sentinels,
+                            uint32_t idle_timeout_ms, void *stream);
+
+/* Counters of the last rt_launch_decode_worker on the current device
+ * (reads device memory on `stream`; safe while the worker runs). */
+int rt_decode_worker_stats(void *stream, rt_decode_worker_stats_t *stats);
+
+/* The fixed128 step over n device-resident Descriptors (16-byte aligned),
+ * one warp each, without rings: the reference's
+ * attention_decode_step_fixed128 as called by process_descriptor
+ * (cu/worker.cu:30-51), results[i] as its DecodeStepResult
+ * (include/attention_decode.h).  A record whose block lies outside the
+ * arena gets path_kind DECODE_PATH_STUB and token_id UINT32_MAX. */
+int rt_attention_fixed128(const Descriptor *descs, uint32_t n, const KVArena *arena,
+                          const SampleState *sample_st, const void *q_buffer, float *o_buffer,
+                          uint32_t io_slots, DecodeStepResult *results, void *stream);
+
+/* Host side of a CommandRing run, in C (the dispatch / poll / shutdown
+ * loop of reference src/main.c:121-190): push the n descriptors as ring
+ * space allows, then n_sentinels stop records, while draining the
+ * CompletionRing into `out` until n_expected records arrived.  Returns
+ * the number drained, or -1 when timeout_ms passed first. */
+int64_t rt_host_decode_pump(CommandRing *ring, const Descriptor *descs, uint32_t n,
+                            uint32_t n_sentinels, CompletionRing *comp, Completion *out,
+                            uint32_t n_expected, uint32_t timeout_ms);
 
 /* ------------------------------------------------------------------------
  * Rewards and group-normalised advantages (new; the reference has only the

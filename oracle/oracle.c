@@ -183,9 +183,11 @@ orc_paged_gqa_attention(const uint16_t *q, const uint16_t *arena,
 }
 
 /* ----------------------------------------------------- fixed128 (ref v0.2) */
-void
-orc_fixed128_attention(const uint16_t *q_f16, const uint16_t *block_f16,
-                       uint32_t seq_len, float *out, uint32_t *token_id)
+/* Plain softmax attention of one fp32 query over the first seq_len tokens
+ * of a 16 KiB fp16 block (K plane, then V plane), in the order of the
+ * reference test's CPU reference (test/test_bench.cu:109-150). */
+static void
+fixed128_core(const float *q, const uint16_t *block_f16, uint32_t seq_len, float *out)
 {
     float scores[32], probs[32];
     const uint16_t *v = block_f16 + 32u * 128u;
@@ -196,7 +198,7 @@ orc_fixed128_attention(const uint16_t *q_f16, const uint16_t *block_f16,
     for (uint32_t t = 0; t < seq_len; t++) {
         float dot = 0.0f;
         for (uint32_t d = 0; d < 128u; d++)
-            dot += orc_f16_to_f32(q_f16[d]) * orc_f16_to_f32(block_f16[t * 128u + d]);
+            dot += q[d] * orc_f16_to_f32(block_f16[t * 128u + d]);
         scores[t] = dot * scale;
         if (scores[t] > mx)
             mx = scores[t];
@@ -214,10 +216,95 @@ orc_fixed128_attention(const uint16_t *q_f16, const uint16_t *block_f16,
         for (uint32_t d = 0; d < 128u; d++)
             out[d] += p * orc_f16_to_f32(v[t * 128u + d]);
     }
+}
+
+void
+orc_fixed128_attention(const uint16_t *q_f16, const uint16_t *block_f16,
+                       uint32_t seq_len, float *out, uint32_t *token_id)
+{
+    float q[128];
+    for (uint32_t d = 0; d < 128u; d++)
+        q[d] = orc_f16_to_f32(q_f16[d]);
+    fixed128_core(q, block_f16, seq_len, out);
+    /* test/test_bench.cu:151-155: lowest index wins ties */
     *token_id = 0;
     for (uint32_t d = 1; d < 128u; d++)
         if (out[d] > out[*token_id])
             *token_id = d;
+}
+
+/* Reference cu/attention_decode.cu:16-28 (decode_synth_query_component). */
+float
+orc_decode_synth_q(uint64_t seq_id, uint64_t cookie, const uint64_t *rng4, uint32_t idx)
+{
+    uint64_t seed = seq_id ^ cookie ^ ((uint64_t)(idx + 1u) * 0x9e3779b97f4a7c15ull);
+    if (rng4)
+        seed ^= rng4[idx & 3u];
+    const uint32_t bits = (uint32_t)(seed ^ (seed >> 32));
+    const int centered = (int)(bits & 0xFFu) - 127;
+    return (float)centered / 127.0f;
+}
+
+/* Reference cu/attention_decode.cu:171-194: each lane keeps the first
+ * strict maximum of d = lane, lane+32, ...; lane 0 then keeps the first
+ * strict maximum over lanes 0..31.  Equivalent: scan d in (d mod 32,
+ * d / 32) order with a strict '>' from -inf; nothing above -inf -> 0. */
+static uint32_t
+kernel_argmax(const float *o)
+{
+    float best = -INFINITY;
+    uint32_t tok = 0;
+    for (uint32_t lane = 0; lane < 32u; lane++)
+        for (uint32_t j = 0; j < 4u; j++) {
+            const uint32_t d = lane + 32u * j;
+            if (o[d] > best) {
+                best = o[d];
+                tok = d;
+            }
+        }
+    return tok;
+}
+
+uint32_t
+orc_decode_steps(const Descriptor *descs, uint32_t n, const uint8_t *arena, uint64_t block_size,
+                 uint64_t n_blocks, const uint64_t *rng4, const uint16_t *q_buf,
+                 uint32_t io_slots, float *o_rows, Completion *comps)
+{
+    uint32_t bad = 0;
+    for (uint32_t i = 0; i < n; i++) {
+        const Descriptor *d = &descs[i];
+        Completion c;
+        float o[128], q[128];
+        /* cu/worker.cu:34-39 */
+        const uint32_t slot = io_slots == 0u ? 0u : (d->output_token_offset & (io_slots - 1u));
+        uint32_t seq_len = d->num_kv_blocks == 0u ? 1u : d->num_kv_blocks;
+        if (seq_len > 32u)
+            seq_len = 32u;
+        c.seq_id = d->seq_id;
+        c.kv_block_offset = d->kv_block_offset;
+        c.reward_cookie = d->reward_cookie;
+        if ((uint64_t)d->kv_block_offset >= n_blocks) {
+            /* out-of-range block: flagged record, no output row */
+            c.token_id = UINT32_MAX;
+            c.cycles_taken = 0;
+            bad++;
+            if (o_rows)
+                memset(o_rows + (size_t)i * 128u, 0, 128u * sizeof(float));
+        } else {
+            for (uint32_t k = 0; k < 128u; k++)
+                q[k] = q_buf ? orc_f16_to_f32(q_buf[(size_t)slot * 128u + k])
+                             : orc_decode_synth_q(d->seq_id, d->reward_cookie, rng4, k);
+            fixed128_core(q, (const uint16_t *)(arena + (uint64_t)d->kv_block_offset * block_size),
+                          seq_len, o);
+            c.token_id = kernel_argmax(o);
+            /* cu/attention_decode.cu:196-201 */
+            c.cycles_taken = (uint64_t)((seq_len + 15u) / 16u) * 128u * 24u;
+            if (o_rows)
+                memcpy(o_rows + (size_t)i * 128u, o, sizeof(o));
+        }
+        comps[i] = c;
+    }
+    return bad;
 }
 
 /* ---------------------------------------------------------- worker sim */

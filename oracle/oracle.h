@@ -26,6 +26,8 @@
 #include <stdint.h>
 #include "hw_desc.h"
 #include "request.h"
+#include "descriptor.h"
+#include "completion.h"
 
 #ifdef __cplusplus
 extern "C" {
@@ -52,6 +54,23 @@ void orc_paged_gqa_attention(const uint16_t *q, const uint16_t *arena,
 void orc_fixed128_attention(const uint16_t *q_f16, const uint16_t *block_f16,
                             uint32_t seq_len, float *out, uint32_t *token_id);
 float orc_f16_to_f32(uint16_t h);
+
+/* Reference cu/attention_decode.cu:16-28: component idx of the synthesized
+ * query (rng4 = SampleState.rng_state, or NULL). */
+float orc_decode_synth_q(uint64_t seq_id, uint64_t cookie, const uint64_t *rng4, uint32_t idx);
+
+/* n descriptors through the reference's process_descriptor
+ * (cu/worker.cu:25-64) and attention_decode_step_fixed128
+ * (cu/attention_decode.cu:60-204): slot and seq_len rules, fp16 q from
+ * q_buf[slot] or the synthesized query, the attention of
+ * test/test_bench.cu:109-150 (fp32), the kernel's argmax tie order, the
+ * cycle estimate.  o_rows (fp32 [n][128], may be NULL) gets each
+ * descriptor's output.  A block index >= n_blocks gives token_id
+ * UINT32_MAX and cycles 0.  Returns the number of such records. */
+uint32_t orc_decode_steps(const Descriptor *descs, uint32_t n, const uint8_t *arena,
+                          uint64_t block_size, uint64_t n_blocks, const uint64_t *rng4,
+                          const uint16_t *q_buf, uint32_t io_slots, float *o_rows,
+                          Completion *comps);
 uint16_t orc_f32_to_f16_rne(float f);
 
 /* reference src/hw_worker_sim.c:22-59 run over a FIFO stream; returns the

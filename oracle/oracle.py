@@ -44,6 +44,11 @@ DESCRIPTOR_DTYPE = np.dtype([
     ("reward_cookie", "<u8"), ("batch_size", "<u2"), ("batch_index", "<u2")])
 assert DESCRIPTOR_DTYPE.itemsize == 32
 
+COMPLETION_DTYPE = np.dtype([
+    ("seq_id", "<u8"), ("token_id", "<u4"), ("kv_block_offset", "<u4"),
+    ("reward_cookie", "<u8"), ("cycles_taken", "<u8")])
+assert COMPLETION_DTYPE.itemsize == 32
+
 GPU_STATE_BYTES = 72 * 256 + 32
 
 _P = ctypes.c_void_p
@@ -78,6 +83,8 @@ def oracle_lib() -> ctypes.CDLL:
             "orc_scheduler_run": (_u32, [_P, _u32, _P, _u32, _int, _u32, _P, _P, _P, _P]),
             "orc_grpo_advantages": (None, [_P, _u32, _u32, _f32, _P]),
             "orc_reward_u01": (_f32, [_u64, _u32]),
+            "orc_decode_synth_q": (_f32, [_u64, _u64, _P, _u32]),
+            "orc_decode_steps": (_u32, [_P, _u32, _P, _u64, _u64, _P, _P, _u32, _P, _P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(l, name)
@@ -117,6 +124,25 @@ def fixed128_attention(q_f16_bits, block_f16_bits, seq_len):
         _ptr(np.ascontiguousarray(q_f16_bits, dtype=np.uint16)),
         _ptr(np.ascontiguousarray(block_f16_bits, dtype=np.uint16)), seq_len, _ptr(out), _ptr(tok))
     return out, int(tok[0])
+
+
+def decode_steps(descs, arena_u8, block_size, rng4=None, q_buf=None, io_slots=0):
+    """The reference decode step (process_descriptor + fixed128 attention)
+    over DESCRIPTOR_DTYPE records; arena_u8 is the arena's bytes.  Returns
+    (COMPLETION_DTYPE records, fp32 output rows [n][128], number of
+    out-of-range blocks)."""
+    descs = np.ascontiguousarray(descs, dtype=DESCRIPTOR_DTYPE)
+    arena_u8 = np.ascontiguousarray(arena_u8, dtype=np.uint8)
+    n = len(descs)
+    comps = np.zeros(n, dtype=COMPLETION_DTYPE)
+    o = np.zeros((n, 128), dtype=np.float32)
+    rng = None if rng4 is None else np.ascontiguousarray(rng4, dtype=np.uint64)
+    q = None if q_buf is None else np.ascontiguousarray(q_buf, dtype=np.uint16)
+    bad = oracle_lib().orc_decode_steps(
+        _ptr(descs), n, _ptr(arena_u8), block_size, arena_u8.nbytes // block_size,
+        None if rng is None else _ptr(rng), None if q is None else _ptr(q), io_slots,
+        _ptr(o), _ptr(comps))
+    return comps, o, int(bad)
 
 
 def worker_sim_stream(descs: np.ndarray):
@@ -262,7 +288,42 @@ class RefCuda:
         l = ctypes.CDLL(path)
         l.hx_ref_sample_rows.restype = _int
         l.hx_ref_sample_rows.argtypes = [_P, _u32, _u64, _P, _P, _P, _P, _P, _u32]
+        l.hx_ref_fixed128.restype = _int
+        l.hx_ref_fixed128.argtypes = [_P, _u32, _P, _u64, _P, _P, _u32, _P, _P, _P, _P, _P]
         self.lib = l
+
+    def fixed128(self, descs, arena, block_size, sample_st=None, q_buf=None, io_slots=0):
+        """The reference's attention_decode_step_fixed128 (cu/attention_decode.cu,
+        unmodified) over DESCRIPTOR_DTYPE records.  arena: torch uint8 on the
+        GPU; sample_st: torch 48-byte SampleState on the GPU or None; q_buf:
+        torch fp16 [rows][128] on the GPU or None.  Returns numpy (o [n][128],
+        token, bytes, tiles, cycles)."""
+        import torch
+        descs = np.ascontiguousarray(descs, dtype=DESCRIPTOR_DTYPE)
+        n = len(descs)
+        n_blocks = arena.numel() // block_size
+        # the harness reads whole 16 KiB blocks and q rows: check bounds here
+        assert block_size >= 16384 and n_blocks > 0
+        assert np.all(descs["kv_block_offset"] < n_blocks), "block outside the arena"
+        if q_buf is not None:
+            rows = q_buf.shape[0]
+            slots = descs["output_token_offset"] & (io_slots - 1) if io_slots else np.zeros(n)
+            assert q_buf.shape[1] == 128 and np.all(slots < rows)
+        dev = arena.device
+        d = torch.from_numpy(descs.view(np.uint8).copy()).to(dev)
+        o = torch.zeros(n, 128, dtype=torch.float32, device=dev)
+        tok = torch.zeros(n, dtype=torch.int32, device=dev)
+        byt = torch.zeros(n, dtype=torch.int32, device=dev)
+        til = torch.zeros(n, dtype=torch.int32, device=dev)
+        cyc = torch.zeros(n, dtype=torch.int64, device=dev)
+        rc = self.lib.hx_ref_fixed128(
+            d.data_ptr(), n, arena.data_ptr(), block_size,
+            None if sample_st is None else sample_st.data_ptr(),
+            None if q_buf is None else q_buf.data_ptr(), io_slots, o.data_ptr(), tok.data_ptr(),
+            byt.data_ptr(), til.data_ptr(), cyc.data_ptr())
+        assert rc == 0, f"reference fixed128 step failed: {rc}"
+        u32 = lambda t: t.cpu().numpy().view(np.uint32)
+        return o.cpu().numpy(), u32(tok), u32(byt), u32(til), cyc.cpu().numpy().view(np.uint64)
 
     def sample_rows(self, logits, vocab, temperature, top_k, top_p, u24):
         """logits: torch fp32 [R, stride] on the GPU (copied; the reference
