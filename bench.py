@@ -12,6 +12,10 @@ Workloads (synthetic, seeded):
              scattered in the arena, Q/K/V ~ N(0,1).  One step = one decode
              attention call over the batch.  Two arena copies (>1 GB in
              total, larger than the 126 MB L2) alternate between steps.
+  sampling   config 3: 256 rows x 32,000 fp32 logits, fused sampling.
+  rollout    config 5 (default): GRPO rollouts, the GPU-resident loop.
+  decode_ring  the reference's per-step CommandRing benchmark (src/main.c):
+             10,000 descriptors through the decode worker and its rings.
 
 --impl reference times the reference path's CPU implementation (the CPU
 oracle port of the same computation; the reference has no CPU
@@ -514,8 +518,174 @@ class RolloutWorkload:
                 "l2": f"KV arena {self.arena.buf.numel() / 1e9:.2f} GB > 126 MB L2"}
 
 
+class DecodeRingWorkload:
+    """The reference's per-step CommandRing benchmark (src/main.c:201-260):
+    10,000 decode descriptors of one trajectory, kv_block_offset = i % 128
+    over 16 KiB fp16 blocks, num_kv_blocks 1, output slot i & 4095 of a
+    4,096-slot q / o buffer.  The q buffer is filled once with N(0,1) fp16
+    (the reference's synthetic model_state / query_producer kernels are not
+    part of the path).
+
+    value: one step = the fixed128 step over the 10,000 descriptors resident
+    in HBM, one rt_attention_fixed128 launch; 64 copies of the blocks, q and
+    o buffers, descriptors and results (371 MB > 126 MB L2) rotate between
+    steps.
+    e2e: one step = launch the persistent decode worker, push the 10,000
+    descriptors and a stop sentinel through the mapped CommandRing, drain
+    the 10,000 Completions from the mapped CompletionRing
+    (rt_host_decode_pump), join the worker."""
+
+    name = "command_ring_decode_main_c"
+    kernel = "fixed128_batch_kernel"
+    metric = "decode steps/s (fixed128 step, reference src/main.c shape)"
+    unit = "steps/s"
+    dtype = "fp16 KV, fp32 math"
+    launches_per_step = 1
+    roofline_note = ("latency-bound: 10,000 warps each stage 512 B of KV with one bulk copy "
+                     "and run a one-token step; the HBM bytes are incidental")
+    N, BLOCKS, SLOTS, BLOCK, COPIES = 10000, 128, 4096, 16384, 64
+
+    def __init__(self, args, rank, world, dev):
+        import ctypes
+        import torch
+        self.torch, self.ctypes = torch, ctypes
+        self.pkg = pkg = ge.load_package()
+        orc = ge.load_oracle()
+        rng = np.random.default_rng(7 + rank)
+        self.arena_host = rng.standard_normal(self.BLOCKS * self.BLOCK // 2).astype(np.float16).view(np.uint8)
+        self.q_bits = rng.standard_normal((self.SLOTS, 128)).astype(np.float16).view(np.uint16)
+        d = np.zeros(self.N, orc.DESCRIPTOR_DTYPE)
+        i = np.arange(self.N, dtype=np.uint64)
+        d["seq_id"] = 1 + rank
+        d["kv_block_offset"] = i % self.BLOCKS
+        d["num_kv_blocks"] = 1
+        d["output_token_offset"] = i
+        d["reward_cookie"] = (np.uint64(1 + rank) << np.uint64(32)) | i
+        self.descs = d
+        C = self.COPIES
+        self.arena_t = torch.from_numpy(self.arena_host.copy()).to(dev).repeat(C).view(C, -1)
+        self.arenas = [pkg.device_arena(self.arena_t[c], self.BLOCK) for c in range(C)]
+        q1 = torch.from_numpy(self.q_bits.view(np.int16)).to(dev).view(torch.float16)
+        self.q = q1.repeat(C, 1).view(C, self.SLOTS, 128)
+        self.o = torch.zeros(C, self.SLOTS, 128, dtype=torch.float32, device=dev)
+        self.desc_d = torch.from_numpy(d.view(np.uint8).copy()).to(dev).repeat(C).view(C, -1)
+        self.res = torch.zeros(C, self.N * 24, dtype=torch.uint8, device=dev)
+        self.step_count = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.rings = pkg.CommandRings()
+        # HBM bytes per descriptor: the descriptor, the K and V rows read
+        # (seq_len 1), q, o, the 24-byte result
+        self.bytes = self.N * (32 + 2 * 256 + 256 + 512 + 24)
+        self.i = 0
+        self.last = None
+        torch.cuda.synchronize()
+
+    def step(self):
+        c = self.i % self.COPIES
+        self.i += 1
+        rc = self.pkg.lib().rt_attention_fixed128(
+            self.ctypes.c_void_p(self.desc_d[c].data_ptr()), self.N,
+            self.ctypes.byref(self.arenas[c]), None, self.ctypes.c_void_p(self.q[c].data_ptr()),
+            self.ctypes.c_void_p(self.o[c].data_ptr()), self.SLOTS,
+            self.ctypes.c_void_p(self.res[c].data_ptr()),
+            self.ctypes.c_void_p(self.torch.cuda.current_stream().cuda_stream))
+        self.pkg.check(rc, "rt_attention_fixed128")
+
+    def _ring_once(self):
+        self.pkg.launch_decode_worker(self.rings, self.arenas[0], q_buffer=self.q[0],
+                                      o_buffer=self.o[0], io_slots=self.SLOTS,
+                                      step_count=self.step_count, stop_sentinels=1,
+                                      idle_timeout_ms=20000)
+        got, raw = self.rings.pump(self.descs, 1, self.N, timeout_ms=60000)
+        if got != self.N:
+            raise RuntimeError(f"decode ring drained {got} of {self.N}")
+        self.torch.cuda.current_stream().synchronize()  # the worker exits at the sentinel
+        self.last = raw
+
+    def units_per_step(self):
+        return float(self.N)
+
+    def check_errors(self):
+        """Batch results (and, after e2e, the ring's Completions) against the
+        CPU restatement: records equal except token ids, which must be
+        near-ties of the oracle where they differ."""
+        orc = ge.load_oracle()
+        want, o_orc, _ = orc.decode_steps(self.descs, self.arena_host, self.BLOCK,
+                                          q_buf=self.q_bits, io_slots=self.SLOTS)
+        dt = np.dtype([("path_kind", "<u4"), ("token_id", "<u4"), ("bytes_touched", "<u4"),
+                       ("tile_count", "<u4"), ("cycle_estimate", "<u8")])
+        res = self.res[0].cpu().numpy().view(dt)
+        ok = np.array_equal(res["cycle_estimate"], want["cycles_taken"])
+        ok &= self._tokens_ok(res["token_id"], want["token_id"], o_orc)
+        self._want = (want, o_orc)
+        return 0 if ok else -100
+
+    def _check_ring(self):
+        orc = ge.load_oracle()
+        want, o_orc = self._want if getattr(self, "_want", None) else orc.decode_steps(
+            self.descs, self.arena_host, self.BLOCK, q_buf=self.q_bits, io_slots=self.SLOTS)[:2]
+        comps = self.last.view(orc.COMPLETION_DTYPE)[:self.N]
+        ok = all(np.array_equal(comps[f], want[f]) for f in
+                 ("seq_id", "kv_block_offset", "reward_cookie", "cycles_taken"))
+        ok &= self._tokens_ok(comps["token_id"], want["token_id"], o_orc)
+        st = self.pkg.decode_worker_stats()
+        if not ok or st["error"] != 0:
+            raise RuntimeError(f"decode ring completions differ from the oracle (stats {st})")
+
+    @staticmethod
+    def _tokens_ok(tok, want, o_orc):
+        bad = np.nonzero(tok != want)[0]
+        return all(o_orc[i][tok[i]] >= o_orc[i].max() - 2e-4 for i in bad)
+
+    def e2e(self, steps, warmup):
+        """Through the decode worker and the mapped rings (host buffers by
+        construction: descriptors read from pinned host memory, Completions
+        written back to it, inside every step)."""
+        torch = self.torch
+        s = torch.cuda.current_stream()
+        for _ in range(min(warmup, 3)):
+            self._ring_once()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(steps):
+            self._ring_once()
+        e1.record(s)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        self._check_ring()
+        return {"value": self.N / (ms / 1e3), "unit": self.unit, "ms_per_step": ms,
+                "h2d_bytes_per_step": (self.N + 1) * 32, "d2h_bytes_per_step": self.N * 32}
+
+    def cpu_sample(self, threads, budget_s=10.0):
+        """The reference step on the host (oracle/oracle.c orc_decode_steps:
+        process_descriptor + the fixed128 attention of test/test_bench.cu:
+        109-155), one core, whole 10,000-descriptor batches until the
+        budget is spent."""
+        orc = ge.load_oracle()
+        t0 = time.perf_counter()
+        reps = 0
+        while reps == 0 or time.perf_counter() - t0 < budget_s:
+            orc.decode_steps(self.descs, self.arena_host, self.BLOCK, q_buf=self.q_bits,
+                             io_slots=self.SLOTS)
+            reps += 1
+        dt = time.perf_counter() - t0
+        return {"value": reps * self.N / dt, "unit": self.unit, "cores": 1, "kind": "port",
+                "seconds": dt,
+                "sample": f"{reps} batch(es) of the 10,000 descriptors, serial C restatement"}
+
+    def config(self):
+        return {"workload": self.name, "descriptors": self.N, "kv_blocks": self.BLOCKS,
+                "block_bytes": self.BLOCK, "num_kv_blocks": 1, "io_slots": self.SLOTS,
+                "value_step": "rt_attention_fixed128 over HBM-resident descriptors",
+                "e2e_step": "decode worker launch + ring dispatch + poll + stop sentinel + join",
+                "rings": "CommandRing / CompletionRing, 4,096 slots, pinned mapped host memory",
+                "l2": "%d rotating copies of blocks, q, o, descriptors and results (%.0f MB > "
+                      "126 MB L2)" % (self.COPIES, self.COPIES * (self.arena_t[0].numel()
+                                      + self.q[0].numel() * 2 + self.o[0].numel() * 4
+                                      + self.desc_d[0].numel() + self.res[0].numel()) / 1e6)}
+
+
 WORKLOADS = {"rollout": RolloutWorkload, "attention": AttentionWorkload,
-             "sampling": SamplingWorkload}
+             "sampling": SamplingWorkload, "decode_ring": DecodeRingWorkload}
 
 
 # -------------------------------------------------------------------- main
@@ -559,8 +729,8 @@ def run_mine(args):
     n_launch = wl.gpu_launches(args.steps) if wl.launches_per_step is None else \
         wl.launches_per_step * args.steps
     prof = wl.kernel_profile() if hasattr(wl, "kernel_profile") else None
-    e2e = wl.e2e(args.steps, args.warmup)
-    if world > 1:
+    e2e = None if args.no_e2e else wl.e2e(args.steps, args.warmup)
+    if world > 1 and e2e is not None:
         t = torch.tensor([e2e["ms_per_step"]], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e["value"] = wl.units_per_step() / (float(t.item()) / 1e3) * world
@@ -598,16 +768,19 @@ def run_mine(args):
             "unit": wl.unit, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms, "higher_is_better": True,
             "scaling": "strong" if wl.name == "grpo_rollouts_c5" else "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (Philox N(0,1), seeded)",
+            "vs_baseline": None, "dtype": getattr(wl, "dtype", "bf16"),
+            "data": "synthetic (Philox N(0,1), seeded)",
             "config": wl.config() | {"parallelism": f"replicas{world}" if world > 1 else "single"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
                          "peak_source": f"{src} copy bandwidth (MEASURED_PEAKS.json hbm_gbs)"
                          if src == "measured" else "fallback 6.65 TB/s",
                          "frac_of_nominal_8tbs": achieved / 8000.0,
-                         "traffic": traffic, "kernel": wl.kernel},
+                         "traffic": traffic, "kernel": wl.kernel}
+                        | ({"note": wl.roofline_note} if hasattr(wl, "roofline_note") else {}),
             "cpu_baseline": cpu,
-            "e2e": {k: e2e[k] for k in ("value", "unit", "h2d_bytes_per_step", "d2h_bytes_per_step")},
+            "e2e": None if e2e is None else {k: e2e[k] for k in ("value", "unit", "h2d_bytes_per_step",
+                                                                 "d2h_bytes_per_step")},
             "gpu_launches": n_launch,
             "kernels": prof_report,
             "clocks": clocks.report(),
@@ -652,6 +825,9 @@ def main():
     ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
     ap.add_argument("--chunk-pages", type=int, default=0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true",
+                    help="skip the end-to-end leg (for ncu runs: the decode_ring e2e leg needs "
+                         "its persistent worker to run beside the host pump)")
     ap.add_argument("--groups", type=int, default=0,
                     help="rollout only: GRPO groups (default 512; fewer keep ncu captures small)")
     ap.add_argument("--ncu-replay", type=int, default=0,

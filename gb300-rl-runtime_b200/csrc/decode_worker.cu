@@ -10,12 +10,14 @@
 // their one-consumer / one-producer contracts:
 //
 //   pump warp (CTA 0, warp 0)
-//     takes up to 256 ring records per pass in one batch of 16-byte reads
-//     (one PCIe round trip instead of one per record), copies the work
-//     into a device queue, releases cons.head once per batch, and stops
-//     at the stop_sentinels-th UINT64_MAX sentinel; it also delivers the
-//     finished completions to the CompletionRing in ring order, one tail
-//     release per batch.
+//     takes up to 256 ring records per pass with all reads in flight at
+//     once (whole 512-byte spans per warp instruction: one host-link round
+//     trip per batch, not one per record), reads prod.tail only when the
+//     last value seen cannot fill a batch, copies the work into a device
+//     queue, releases cons.head once per batch, and stops at the
+//     stop_sentinels-th UINT64_MAX sentinel.  While a batch's reads are in
+//     flight it delivers finished completions to the CompletionRing in
+//     ring order, up to a batch per tail release.
 //   worker warps (every other warp of the grid)
 //     claim queue tickets with an atomic, stage the descriptor's KV rows
 //     into their own shared-memory stage with a bulk async copy (mbarrier
@@ -143,22 +145,24 @@ __device__ __forceinline__ void st_release_gpu(uint32_t *p, uint32_t v)
     asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Ring records live in pinned host memory written by the CPU: volatile
-// 16-byte loads (never served from a stale L1 line).
-__device__ __forceinline__ uint4 ld_volatile_v4(const void *p)
+// Ring records live in pinned host memory shared with the CPU:
+// system-scope relaxed 16-byte accesses (never served from a stale L1
+// line, and free to be in flight together); ordering comes from the
+// acquire of prod.tail / cons.head and the release of the indices.
+__device__ __forceinline__ uint4 ld_relaxed_sys_v4(const void *p)
 {
     uint4 r;
-    asm volatile("ld.volatile.global.v4.u32 {%0,%1,%2,%3}, [%4];"
+    asm volatile("ld.relaxed.sys.global.v4.u32 {%0,%1,%2,%3}, [%4];"
                  : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
                  : "l"(p)
                  : "memory");
     return r;
 }
 
-__device__ __forceinline__ void st_volatile_v4(void *p, uint4 v)
+__device__ __forceinline__ void st_relaxed_sys_v4(void *p, uint4 v)
 {
-    asm volatile("st.volatile.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y),
-                 "r"(v.z), "r"(v.w)
+    asm volatile("st.relaxed.sys.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x),
+                 "r"(v.y), "r"(v.z), "r"(v.w)
                  : "memory");
 }
 
@@ -269,8 +273,8 @@ __device__ StepResult fixed128_step(const StepEnv &env, const DescF &f, uint8_t 
 
     // score of token `lane`: eight ascending-d fma chains, d = i (mod 8)
     const float scale = rsqrtf((float)DECODE_FIXED_HEAD_DIM);
-    float s;
-    {
+    float s = 0.0f;
+    if (lane < seq_len) {  // lanes past seq_len would read rows that were not copied
         const uint8_t *krow = stage + lane * kRowBytes;
         float p[8];
 #pragma unroll
@@ -384,6 +388,18 @@ __device__ void init_stage_barrier(uint8_t *stage, uint32_t lane)
 }
 
 // ---------------------------------------------------------------- pump
+// Bits 0, 2, 4, ... 30 of x packed into bits 0..15.
+__device__ __forceinline__ uint32_t even_bits(uint32_t x)
+{
+    x &= 0x55555555u;
+    x = (x | (x >> 1)) & 0x33333333u;
+    x = (x | (x >> 2)) & 0x0F0F0F0Fu;
+    x = (x | (x >> 4)) & 0x00FF00FFu;
+    return (x | (x >> 8)) & 0x0000FFFFu;
+}
+
+constexpr uint32_t kPieces = kPumpBatch * 2u / 32u;  // 16-byte ring pieces per lane per batch
+
 __device__ void pump_loop(const DwArgs &a, uint32_t lane)
 {
     DwCtl *ctl = a.ctl;
@@ -393,60 +409,159 @@ __device__ void pump_loop(const DwArgs &a, uint32_t lane)
         head = rt_load_relaxed_u32(&a.ring->cons.head);
         ctail = rt_load_relaxed_u32(&a.comp->prod.tail);
         chead = rt_load_acquire_u32(&a.comp->cons.head);
+        ctl->workers = gridDim.x * kWarpsPerCta - 1u;
     }
     head = __shfl_sync(0xFFFFFFFFu, head, 0);
     ctail = __shfl_sync(0xFFFFFFFFu, ctail, 0);
     chead = __shfl_sync(0xFFFFFFFFu, chead, 0);
+    uint32_t tail_seen = head;  // last prod.tail observed: records below it are published
     uint32_t published = 0, drained = 0, sentinels = 0;
     unsigned long long consumed = 0;
     bool consuming = true, full_noted = false;
     int32_t err = 0;
     uint32_t nap = 32;
     uint64_t t_last = rt::globaltimer_ns();
-    const uint32_t lt_mask = (1u << lane) - 1u;
 
     while (true) {
         bool progress = false;
+
+        // 1. issue this pass's ring reads; they complete while the drain runs.
+        //    Instruction j, lane l reads 16-byte piece 32j + l of the batch
+        //    (half l & 1 of record 16j + l / 2): 512 contiguous bytes per
+        //    instruction, whole lines over the host link.
+        uint32_t n = 0;
+        uint4 piece[kPieces];
         if (consuming) {
-            uint32_t tail = 0;
-            if (lane == 0)
-                tail = rt_load_acquire_u32(&a.ring->prod.tail);
-            tail = __shfl_sync(0xFFFFFFFFu, tail, 0);
-            const uint32_t avail = tail - head;
+            if (tail_seen - head < kPumpBatch) {  // the cached tail cannot fill a batch
+                uint32_t t = 0;
+                if (lane == 0)
+                    t = rt_load_acquire_u32(&a.ring->prod.tail);
+                tail_seen = __shfl_sync(0xFFFFFFFFu, t, 0);
+            }
+            const uint32_t avail = tail_seen - head;
             if (avail > (uint32_t)RING_SIZE) {  // the host broke the ring contract
                 err = RT_EDEVICE;
                 break;
             }
-            const uint32_t room = kQueue - (published - drained);
-            const uint32_t n = min(min(avail, room), kPumpBatch);
-            uint32_t taken = 0;
-            for (uint32_t b = 0; b < n && consuming; b += 32u) {
-                const uint32_t i = b + lane;
-                const bool valid = i < n;
-                uint4 x = make_uint4(0, 0, 0, 0), y = x;
-                if (valid) {
-                    const Descriptor *src = &a.ring->slots[(head + i) & (RING_SIZE - 1u)];
-                    x = ld_volatile_v4(src);
-                    y = ld_volatile_v4(reinterpret_cast<const uint8_t *>(src) + 16);
+            n = min(min(avail, kQueue - (published - drained)), kPumpBatch);
+#pragma unroll
+            for (uint32_t j = 0; j < kPieces; j++) {
+                const uint32_t r = 16u * j + (lane >> 1);
+                piece[j] = make_uint4(0, 0, 0, 0);
+                if (r < n)
+                    piece[j] = ld_relaxed_sys_v4(
+                        reinterpret_cast<const uint8_t *>(
+                            &a.ring->slots[(head + r) & (RING_SIZE - 1u)]) + 16u * (lane & 1u));
+            }
+        }
+
+        // 2. deliver finished completions in ticket (= ring) order: a batch's
+        //    ready words and records are read with all loads in flight, then
+        //    written to the CompletionRing with one tail release
+        bool ring_full = false;
+        if (drained != published) {
+            const uint32_t look = min(published - drained, kPumpBatch);
+            uint32_t rbits = 0;
+#pragma unroll
+            for (uint32_t j = 0; j < kPumpBatch / 32u; j++) {
+                const uint32_t e = 32u * j + lane;
+                if (e < look &&
+                    ld_relaxed_gpu(&qu->ready[(drained + e) & (kQueue - 1u)]) == drained + e + 1u)
+                    rbits |= 1u << j;
+            }
+            uint32_t k = 0;
+#pragma unroll
+            for (uint32_t j = 0; j < kPumpBatch / 32u; j++) {
+                const uint32_t m = __ballot_sync(0xFFFFFFFFu, (rbits >> j) & 1u);
+                const uint32_t t = m == 0xFFFFFFFFu ? 32u : (uint32_t)(__ffs(~m) - 1);
+                k += t;
+                if (t < 32u)
+                    break;
+            }
+            if (k) {
+                __threadfence();  // the ready words observed before the records are read
+                uint32_t room = (uint32_t)COMP_RING_SIZE - (ctail - chead);
+                if (room < k) {
+                    if (lane == 0)
+                        chead = rt_load_acquire_u32(&a.comp->cons.head);
+                    chead = __shfl_sync(0xFFFFFFFFu, chead, 0);
+                    room = (uint32_t)COMP_RING_SIZE - (ctail - chead);
                 }
-                const bool sent = valid && x.x == 0xFFFFFFFFu && x.y == 0xFFFFFFFFu;
-                const uint32_t smask = __ballot_sync(0xFFFFFFFFu, sent);
-                uint32_t take = __ballot_sync(0xFFFFFFFFu, valid);
+                ring_full = room < k;
+                k = min(k, room);
+            }
+            if (k) {
+                uint4 c[kPumpBatch / 16u];
+#pragma unroll
+                for (uint32_t j = 0; j < kPumpBatch / 16u; j++) {
+                    // piece e = 32j + lane: half (e & 1) of entry e / 2
+                    const uint32_t e = (32u * j + lane) >> 1;
+                    c[j] = make_uint4(0, 0, 0, 0);
+                    if (e < k)
+                        c[j] = __ldcg(&qu->comp[2u * ((drained + e) & (kQueue - 1u)) + (lane & 1u)]);
+                }
+#pragma unroll
+                for (uint32_t j = 0; j < kPumpBatch / 16u; j++) {
+                    const uint32_t e = (32u * j + lane) >> 1;
+                    if (e < k)
+                        st_relaxed_sys_v4(reinterpret_cast<uint8_t *>(
+                                              &a.comp->slots[(ctail + e) & (COMP_RING_SIZE - 1u)]) +
+                                              16u * (lane & 1u),
+                                          c[j]);
+                }
+                __syncwarp();
+                __threadfence_system();
+                if (lane == 0) {
+                    rt_store_release_u32(&a.comp->prod.tail, ctail + k);
+                    if (a.step_count)
+                        atomicAdd(a.step_count, (unsigned long long)k);
+                    st_release_gpu(&ctl->drained.v, drained + k);
+                }
+                ctail += k;
+                drained += k;
+                progress = true;
+                full_noted = false;
+            }
+        }
+        if (ring_full) {
+            // one count per stall (the reference counts every retry)
+            if (!full_noted && lane == 0) {
+                comp_ring_record_overflow(&a.comp->overflow.value);
+                ctl->comp_full++;
+            }
+            full_noted = true;
+        }
+
+        // 3. take the ring records read in step 1: compact the work into the
+        //    queue, stop after the stop_sentinels-th sentinel
+        if (n) {
+            uint32_t taken = 0;
+            const uint32_t m = lane >> 1;  // record of this lane within an instruction
+#pragma unroll
+            for (uint32_t j = 0; j < kPieces; j++) {
+                const uint32_t rb = 16u * j;
+                if (rb >= n || !consuming)
+                    break;
+                const bool valid = rb + m < n;
+                const bool even = (lane & 1u) == 0u;
+                const uint32_t smask = even_bits(__ballot_sync(
+                    0xFFFFFFFFu, even && valid && piece[j].x == 0xFFFFFFFFu &&
+                                     piece[j].y == 0xFFFFFFFFu));
+                uint32_t take = even_bits(__ballot_sync(0xFFFFFFFFu, even && valid));
                 const uint32_t need = a.stop_sentinels - sentinels;
                 if ((uint32_t)__popc(smask) >= need) {
-                    // cut right after the need-th sentinel of this chunk
-                    uint32_t m = smask;
-                    for (uint32_t k = 1; k < need; k++)
-                        m &= m - 1u;
-                    const uint32_t last = __ffs(m) - 1u;
-                    take &= last == 31u ? 0xFFFFFFFFu : ((2u << last) - 1u);
+                    // cut right after the need-th sentinel of this group
+                    uint32_t mm = smask;
+                    for (uint32_t q = 1; q < need; q++)
+                        mm &= mm - 1u;
+                    const uint32_t last = __ffs(mm) - 1u;
+                    take &= (2u << last) - 1u;
                     consuming = false;
                 }
                 const uint32_t work = take & ~smask;
-                if ((work >> lane) & 1u) {
-                    const uint32_t qi = (published + __popc(work & lt_mask)) & (kQueue - 1u);
-                    qu->desc[2u * qi] = x;
-                    qu->desc[2u * qi + 1u] = y;
+                if ((work >> m) & 1u) {
+                    const uint32_t qi = (published + __popc(work & ((1u << m) - 1u))) & (kQueue - 1u);
+                    qu->desc[2u * qi + (lane & 1u)] = piece[j];
                 }
                 published += __popc(work);
                 sentinels += __popc(take & smask);
@@ -467,55 +582,6 @@ __device__ void pump_loop(const DwArgs &a, uint32_t lane)
                 st_release_gpu(&ctl->stop.v, 1u);
         }
 
-        // deliver finished completions in ticket (= ring) order
-        while (drained != published) {
-            const uint32_t look = min(published - drained, 32u);
-            bool rdy = false;
-            if (lane < look)
-                rdy = ld_acquire_gpu(&qu->ready[(drained + lane) & (kQueue - 1u)]) ==
-                      drained + lane + 1u;
-            const uint32_t rm = __ballot_sync(0xFFFFFFFFu, rdy);
-            uint32_t k = rm == 0xFFFFFFFFu ? 32u : (uint32_t)(__ffs(~rm) - 1);
-            if (k == 0u)
-                break;
-            uint32_t room = (uint32_t)COMP_RING_SIZE - (ctail - chead);
-            if (room < k) {
-                if (lane == 0)
-                    chead = rt_load_acquire_u32(&a.comp->cons.head);
-                chead = __shfl_sync(0xFFFFFFFFu, chead, 0);
-                room = (uint32_t)COMP_RING_SIZE - (ctail - chead);
-            }
-            if (room == 0u) {
-                if (!full_noted && lane == 0) {
-                    comp_ring_record_overflow(&a.comp->overflow.value);
-                    ctl->comp_full++;
-                }
-                full_noted = true;
-                break;
-            }
-            full_noted = false;
-            k = min(k, room);
-            if (lane < k) {
-                const uint32_t qi = (drained + lane) & (kQueue - 1u);
-                const uint4 c0 = __ldcg(&qu->comp[2u * qi]);
-                const uint4 c1 = __ldcg(&qu->comp[2u * qi + 1u]);
-                uint8_t *dst = reinterpret_cast<uint8_t *>(
-                    &a.comp->slots[(ctail + lane) & (COMP_RING_SIZE - 1u)]);
-                st_volatile_v4(dst, c0);
-                st_volatile_v4(dst + 16, c1);
-            }
-            __syncwarp();
-            __threadfence_system();
-            if (lane == 0) {
-                rt_store_release_u32(&a.comp->prod.tail, ctail + k);
-                if (a.step_count)
-                    atomicAdd(a.step_count, (unsigned long long)k);
-                st_release_gpu(&ctl->drained.v, drained + k);
-            }
-            ctail += k;
-            drained += k;
-            progress = true;
-        }
         if (!consuming && drained == published)
             break;
         uint64_t now = 0;
@@ -531,7 +597,7 @@ __device__ void pump_loop(const DwArgs &a, uint32_t lane)
                 break;
             }
             __nanosleep(nap);
-            nap = min(nap * 2u, 1024u);
+            nap = min(nap * 2u, 256u);
         }
     }
     if (lane == 0) {
@@ -584,7 +650,7 @@ __device__ void worker_loop(const DwArgs &a, uint8_t *stage, uint32_t lane)
                     break;
                 }
                 __nanosleep(nap);
-                nap = min(nap * 2u, 2048u);
+                nap = min(nap * 2u, 512u);
             }
         }
         have = __shfl_sync(0xFFFFFFFFu, have, 0);
@@ -799,17 +865,11 @@ extern "C" int rt_launch_decode_worker(CommandRing *ring, const KVArena *arena,
     a.idle_ns = (uint64_t)(idle_timeout_ms ? idle_timeout_ms : 10000u) * 1000000ull;
     a.ctl = g_dw_ctl[dev];
     a.queue = g_dw_queue[dev];
-    DwCtl init;
-    memset(&init, 0, sizeof(init));
-    init.workers = grid * kWarpsPerCta - 1u;
-    err = cudaMemcpyAsync(a.ctl, &init, sizeof(init), cudaMemcpyHostToDevice, s);
+    // stream-ordered resets (no host synchronisation): the control block
+    // (the pump fills in the worker count) and the ready words
+    err = cudaMemsetAsync(a.ctl, 0, sizeof(DwCtl), s);
     if (err == cudaSuccess)
         err = cudaMemsetAsync(a.queue->ready, 0, sizeof(a.queue->ready), s);
-    if (err != cudaSuccess)
-        return rt::cuda_fail(err, "decode_worker: setup");
-    // the control block is read back by rt_decode_worker_stats; the copy
-    // above must finish before `init` leaves scope
-    err = cudaStreamSynchronize(s);
     if (err != cudaSuccess)
         return rt::cuda_fail(err, "decode_worker: setup");
     decode_worker_kernel<<<grid, kWarpsPerCta * 32, kWarpsPerCta * kStageBytes, s>>>(a);

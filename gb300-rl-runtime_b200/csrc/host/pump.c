@@ -91,8 +91,22 @@ rt_host_decode_pump(CommandRing *ring, const Descriptor *descs, uint32_t n, uint
             ring_commit(ring, k);
             progress = 1;
         }
-        while (drained < n_expected && comp_ring_poll(comp, &out[drained]))
-            drained++, progress = 1;
+        /* drain: one tail read and one head release per batch (the
+         * comp_ring_poll contract, k records at a time) */
+        if (drained < n_expected) {
+            uint32_t chead = rt_load_relaxed_u32(&comp->cons.head);
+            uint32_t ctail = rt_load_acquire_u32(&comp->prod.tail);
+            uint32_t avail = ctail - chead;
+            if (avail > n_expected - drained)
+                avail = n_expected - drained;
+            for (uint32_t i = 0; i < avail; i++)
+                out[drained + i] = comp->slots[(chead + i) & (COMP_RING_SIZE - 1u)];
+            if (avail) {
+                rt_store_release_u32(&comp->cons.head, chead + avail);
+                drained += avail;
+                progress = 1;
+            }
+        }
         if (!progress) {
             if (timeout_ms && pump_now_ms() - t0 > timeout_ms)
                 return -1;
