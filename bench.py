@@ -688,6 +688,32 @@ WORKLOADS = {"rollout": RolloutWorkload, "attention": AttentionWorkload,
              "sampling": SamplingWorkload, "decode_ring": DecodeRingWorkload}
 
 
+def config1_cpu_path(reps=5):
+    """BASELINE config 1, the reference's CPU path: 10,000 hw_desc_t decode
+    descriptors (seed 0, max_tokens 2048) through hw_ring + hw_worker_sim,
+    producer and worker on two host threads, command depth capped at 1,024.
+    The reference's own C sources (compiled unmodified into oracle/_ref)
+    are timed beside this repo's C implementation of the same API, and the
+    two 64-byte completion streams are compared byte for byte."""
+    orc = ge.load_oracle()
+    try:
+        ref = orc.Harness("ref")
+    except OSError as e:
+        return {"unavailable": f"reference build absent: {e}"}
+    mine = orc.Harness("mine")
+    descs = mine.gen_c1(10000, seed=0, max_tokens=2048)
+    r = [ref.run_c1(descs, depth_cap=1024) for _ in range(reps)]
+    m = [mine.run_c1(descs, depth_cap=1024) for _ in range(reps)]
+    rs, ms = statistics.median(x[3] for x in r), statistics.median(x[3] for x in m)
+    return {"workload": "BASELINE config 1: 10,000 hw_desc_t, seed 0, depth 1,024",
+            "kind": "reference", "cores": 2,
+            "reference_descs_per_s": len(descs) / rs, "reference_tokens_per_s": r[0][1] / rs,
+            "mine_descs_per_s": len(descs) / ms, "mine_tokens_per_s": m[0][1] / ms,
+            "completion_stream_equal": bool(np.array_equal(r[0][0].view(np.uint8),
+                                                           m[0][0].view(np.uint8))),
+            "reps": reps}
+
+
 # -------------------------------------------------------------------- main
 def run_mine(args):
     import torch
@@ -735,9 +761,10 @@ def run_mine(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e["value"] = wl.units_per_step() / (float(t.item()) / 1e3) * world
         e2e["ms_per_step"] = float(t.item())
-    cpu = None
+    cpu = c1 = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = wl.cpu_sample(os.cpu_count() or 1)
+        c1 = config1_cpu_path()
 
     if rank == 0:
         peaks, src = measured_peaks()
@@ -779,6 +806,7 @@ def run_mine(args):
                          "traffic": traffic, "kernel": wl.kernel}
                         | ({"note": wl.roofline_note} if hasattr(wl, "roofline_note") else {}),
             "cpu_baseline": cpu,
+            "cpu_path_config1": c1,
             "e2e": None if e2e is None else {k: e2e[k] for k in ("value", "unit", "h2d_bytes_per_step",
                                                                  "d2h_bytes_per_step")},
             "gpu_launches": n_launch,
