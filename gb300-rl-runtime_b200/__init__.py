@@ -151,6 +151,11 @@ class rt_rollout_buffers_t(ctypes.Structure):
         ("max_pages", ctypes.c_uint32), ("max_groups", ctypes.c_uint32)]
 
 
+class rt_gemm_params_t(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_uint32) for n in ("M", "N", "K", "lda", "ldb", "ldc", "split_k",
+                                               "flags")]
+
+
 class rt_decode_worker_stats_t(ctypes.Structure):
     _fields_ = [("consumed", ctypes.c_uint64), ("completed", ctypes.c_uint64)] + [
         (n, ctypes.c_uint32) for n in ("published", "sentinels", "comp_ring_full")] + [
@@ -231,6 +236,7 @@ _SIGS = {
                                              _P, _P, ctypes.c_uint32, _P, _P]),
     "rt_host_decode_pump": (ctypes.c_int64, [_P, _P, ctypes.c_uint32, ctypes.c_uint32, _P, _P,
                                              ctypes.c_uint32, ctypes.c_uint32]),
+    "rt_gemm_bf16": (ctypes.c_int, [ctypes.POINTER(rt_gemm_params_t), _P, _P, _P, _P, _P]),
     "ring_create": (_P, []), "ring_destroy": (None, [_P]),
     "comp_ring_create": (_P, []), "comp_ring_destroy": (None, [_P]),
     "req_ring_create": (_P, []), "req_ring_destroy": (None, [_P]),

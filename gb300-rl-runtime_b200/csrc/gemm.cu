@@ -1,0 +1,332 @@
+// gemm.cu - bf16 GEMM on the 5th-generation tensor cores (tcgen05, sm_100a)
+// for the decode step's projections: C[m][n] = sum_k A[m][k] * B[n][k],
+// A = activations (one row per rollout slot), B = a weight matrix stored
+// [out][in] (K contiguous), C fp32.
+//
+// Reference: none.  The reference synthesises its decode query with one
+// <<<1, 128>>> launch per slot and step (cu/model_state.cu:6-52,
+// cu/query_producer.cu:5-26) and has no LM head; this is the batched
+// projection those per-slot launches stand in for.
+//
+// Kernel: one persistent CTA per SM walking (tile, K-split) units,
+// 128 x 224 output tiles (32,000 / 224 gives 286 tiles: two full waves on
+// 148 SMs), three warp roles:
+//   warp 0   one thread issues TMA loads of the A (128 x 64) and B
+//            (224 x 64) K-slices into a 4-stage shared-memory ring
+//            (128-byte swizzle, no multicast);
+//   warp 1   allocates 512 TMEM columns (two fp32 accumulators of 128
+//            lanes x 256 columns) and one thread issues tcgen05.mma
+//            (M 128, N 224, K 16; four per K-slice), committing each
+//            stage back to the producer and each finished tile to the
+//            epilogue;
+//   warps 2-5  read the accumulator out of TMEM (tcgen05.ld, one row per
+//            thread) and store C, or add into C for K-splits, while the
+//            MMAs of the next tile fill the other accumulator.
+// Every mbarrier wait is bounded; an expired wait sets the error word and
+// the CTA winds down (waiting, bounded, for its own MMAs) and frees its TMEM.
+#include <cuda_bf16.h>
+#include <stdint.h>
+#include <string.h>
+
+#include "rlrt.h"
+#include "rt_common.cuh"
+
+namespace {
+
+constexpr uint32_t kBM = 128, kBN = 224, kBK = 64, kStages = 4;
+constexpr uint32_t kABytes = kBM * kBK * 2;         // 16 KiB
+constexpr uint32_t kBBytes = kBN * kBK * 2;         // 28 KiB
+constexpr uint32_t kStageBytes = kABytes + kBBytes;  // multiple of 1024 (swizzle atoms)
+constexpr uint32_t kAccCols = 256;                   // TMEM columns per accumulator
+constexpr uint32_t kTmemCols = 2 * kAccCols;
+constexpr uint32_t kThreads = 192;
+constexpr uint64_t kWaitNs = 2000000000ull;
+constexpr uint32_t kSmemBytes = kStages * kStageBytes + 1024 /* alignment */ + 256 /* barriers */;
+
+static_assert(kABytes % 1024 == 0 && kBBytes % 1024 == 0, "stage buffers stay 1024-byte aligned");
+static_assert(kBN % 16 == 0 && kBN <= 256 && kBN <= kAccCols, "UMMA N for M = 128");
+
+struct GemmArgs {
+    float *C;
+    uint32_t M, N, K, ldc;
+    uint32_t m_tiles, n_tiles, splits, kb_per_split, kb_total;
+    uint32_t units;
+    uint32_t accumulate;  // 1: add into C (K-splits always add)
+    uint32_t vec_ok;      // C rows allow 16-byte stores
+    int32_t *error;
+};
+
+struct Shared {
+    uint64_t full[kStages], empty[kStages];
+    uint64_t acc_full[2], acc_empty[2];
+    uint32_t tmem_base;
+    uint32_t abort;
+};
+
+__device__ __forceinline__ void unit_coords(const GemmArgs &g, uint32_t u, uint32_t &m0,
+                                            uint32_t &n0, uint32_t &kb0, uint32_t &kb1)
+{
+    // tiles sharing a B slab (same n) are adjacent, so concurrently running
+    // CTAs read each weight slab from HBM once
+    const uint32_t split = u % g.splits;
+    const uint32_t t = u / g.splits;
+    m0 = (t % g.m_tiles) * kBM;
+    n0 = (t / g.m_tiles) * kBN;
+    kb0 = split * g.kb_per_split;
+    kb1 = min(kb0 + g.kb_per_split, g.kb_total);
+}
+
+__device__ __forceinline__ bool wait_or_abort(Shared *sh, uint32_t bar, uint32_t parity,
+                                              const GemmArgs &g)
+{
+    if (rt::mbar_try_wait(bar, parity))
+        return true;
+    const uint64_t t0 = rt::globaltimer_ns();
+    while (!rt::mbar_try_wait(bar, parity)) {
+        if (*(volatile uint32_t *)&sh->abort)
+            return false;
+        if (rt::globaltimer_ns() - t0 > kWaitNs) {
+            atomicCAS(g.error, 0, 1);
+            *(volatile uint32_t *)&sh->abort = 1u;
+            return false;
+        }
+    }
+    return true;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap map_a,
+                        const __grid_constant__ CUtensorMap map_b, const GemmArgs g)
+{
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~uintptr_t(1023u));
+    Shared *sh = reinterpret_cast<Shared *>(smem + kStages * kStageBytes);
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t smem_base = rt::smem_u32(smem);
+
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < kStages; s++) {
+            rt::mbar_init(rt::smem_u32(&sh->full[s]), 1u);
+            rt::mbar_init(rt::smem_u32(&sh->empty[s]), 1u);
+        }
+        for (uint32_t b = 0; b < 2; b++) {
+            rt::mbar_init(rt::smem_u32(&sh->acc_full[b]), 1u);
+            rt::mbar_init(rt::smem_u32(&sh->acc_empty[b]), 128u);
+        }
+        sh->abort = 0u;
+        rt::mbar_fence_init();
+        rt::prefetch_tensormap(&map_a);
+        rt::prefetch_tensormap(&map_b);
+    }
+    if (warp == 1) {
+        rt::tmem_alloc(rt::smem_u32(&sh->tmem_base), kTmemCols);
+        rt::tmem_relinquish();
+    }
+    rt::tc_fence_before_sync();
+    __syncthreads();
+    rt::tc_fence_after_sync();
+    const uint32_t tmem = sh->tmem_base;
+
+    if (warp == 0) {
+        // ---------------------------------------------------- TMA producer
+        if (lane == 0) {
+            uint32_t stage = 0, phase = 0;
+            for (uint32_t u = blockIdx.x; u < g.units; u += gridDim.x) {
+                uint32_t m0, n0, kb0, kb1;
+                unit_coords(g, u, m0, n0, kb0, kb1);
+                bool ok = true;
+                for (uint32_t kb = kb0; kb < kb1; kb++) {
+                    if (!(ok = wait_or_abort(sh, rt::smem_u32(&sh->empty[stage]), phase ^ 1u, g)))
+                        break;
+                    const uint32_t full = rt::smem_u32(&sh->full[stage]);
+                    const uint32_t sa = smem_base + stage * kStageBytes;
+                    rt::mbar_arrive_expect_tx(full, kStageBytes);
+                    rt::tma_load_2d(sa, &map_a, (int32_t)(kb * kBK), (int32_t)m0, full,
+                                    rt::l2_policy_evict_normal());
+                    rt::tma_load_2d(sa + kABytes, &map_b, (int32_t)(kb * kBK), (int32_t)n0, full,
+                                    rt::l2_policy_evict_first());
+                    if (++stage == kStages) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok)
+                    break;
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            const uint32_t idesc = rt::umma_idesc_bf16(kBM, kBN, 0u);
+            uint32_t stage = 0, phase = 0, buf = 0, acc_phase = 0;
+            for (uint32_t u = blockIdx.x; u < g.units; u += gridDim.x) {
+                uint32_t m0, n0, kb0, kb1;
+                unit_coords(g, u, m0, n0, kb0, kb1);
+                if (!wait_or_abort(sh, rt::smem_u32(&sh->acc_empty[buf]), acc_phase ^ 1u, g))
+                    break;
+                rt::tc_fence_after_sync();
+                const uint32_t d_tmem = tmem + buf * kAccCols;
+                bool ok = true;
+                for (uint32_t kb = kb0; kb < kb1; kb++) {
+                    if (!(ok = wait_or_abort(sh, rt::smem_u32(&sh->full[stage]), phase, g)))
+                        break;
+                    rt::tc_fence_after_sync();
+                    const uint32_t sa = smem_base + stage * kStageBytes;
+#pragma unroll
+                    for (uint32_t kk = 0; kk < kBK / 16u; kk++) {
+                        // K-major SW128: 16 bf16 = 32 bytes further along each row
+                        const uint64_t da = rt::umma_desc_sw128(sa + kk * 32u, 16u, 1024u);
+                        const uint64_t db = rt::umma_desc_sw128(sa + kABytes + kk * 32u, 16u, 1024u);
+                        rt::umma_bf16_ss(d_tmem, da, db, idesc, (kb > kb0 || kk > 0u) ? 1u : 0u);
+                    }
+                    rt::umma_commit(rt::smem_u32(&sh->empty[stage]));
+                    if (++stage == kStages) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok)
+                    break;
+                rt::umma_commit(rt::smem_u32(&sh->acc_full[buf]));
+                if (++buf == 2u) {
+                    buf = 0;
+                    acc_phase ^= 1u;
+                }
+            }
+        }
+    } else {
+        // ------------------------------------------------------- epilogue
+        const uint32_t quarter = warp & 3u;  // TMEM lanes 32*quarter .. +31
+        const uint32_t row = quarter * 32u + lane;
+        uint32_t buf = 0, acc_phase = 0;
+        for (uint32_t u = blockIdx.x; u < g.units; u += gridDim.x) {
+            uint32_t m0, n0, kb0, kb1;
+            unit_coords(g, u, m0, n0, kb0, kb1);
+            if (!wait_or_abort(sh, rt::smem_u32(&sh->acc_full[buf]), acc_phase, g))
+                break;
+            rt::tc_fence_after_sync();
+            const uint32_t m = m0 + row;
+            float *crow = g.C + (uint64_t)m * g.ldc;
+            const bool add = g.accumulate || g.splits > 1u;
+#pragma unroll 1
+            for (uint32_t c = 0; c < kBN; c += 32u) {
+                uint32_t r[32];
+                rt::tmem_ld32(tmem + buf * kAccCols + ((quarter * 32u) << 16) + c, r);
+                rt::tmem_ld_wait();
+                if (m < g.M) {
+                    const uint32_t n = n0 + c;
+                    if (!add && n + 32u <= g.N && g.vec_ok) {
+                        float4 *dst = reinterpret_cast<float4 *>(crow + n);
+#pragma unroll
+                        for (uint32_t j = 0; j < 8; j++)
+                            dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                                 __uint_as_float(r[4 * j + 2]),
+                                                 __uint_as_float(r[4 * j + 3]));
+                    } else {
+#pragma unroll
+                        for (uint32_t j = 0; j < 32; j++) {
+                            if (n + j < g.N) {
+                                if (add)
+                                    atomicAdd(crow + n + j, __uint_as_float(r[j]));
+                                else
+                                    crow[n + j] = __uint_as_float(r[j]);
+                            }
+                        }
+                    }
+                }
+            }
+            rt::tc_fence_before_sync();
+            rt::mbar_arrive(rt::smem_u32(&sh->acc_empty[buf]));
+            if (++buf == 2u) {
+                buf = 0;
+                acc_phase ^= 1u;
+            }
+        }
+    }
+
+    // wind down: every MMA this CTA issued has completed before TMEM is freed
+    rt::tc_fence_before_sync();
+    __syncthreads();
+    if (warp == 1) {
+        rt::tc_fence_after_sync();
+        rt::tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+}  // namespace
+
+extern "C" int rt_gemm_bf16(const rt_gemm_params_t *p, const void *A, const void *B, float *C,
+                            int32_t *error, void *stream)
+{
+    if (!p || !A || !B || !C || !error) {
+        rt::set_error("gemm_bf16: null argument");
+        return RT_EINVAL;
+    }
+    if (p->M == 0 || p->N == 0 || p->K == 0)
+        return RT_OK;
+    if (p->K % kBK || p->lda < p->K || p->ldb < p->K || p->ldc < p->N || (p->lda % 8u) ||
+        (p->ldb % 8u) || ((uintptr_t)A % 16u) || ((uintptr_t)B % 16u) || ((uintptr_t)C % 4u)) {
+        rt::set_error("gemm_bf16: K must be a multiple of 64, lda/ldb multiples of 8 elements "
+                      "(>= K), ldc >= N, A and B 16-byte aligned (M %u N %u K %u)",
+                      p->M, p->N, p->K);
+        return RT_EINVAL;
+    }
+    CUtensorMap ma, mb;
+    int rc = rt::encode_bf16_kmajor_map(&ma, A, p->K, p->M, (uint64_t)p->lda * 2u, kBM);
+    if (rc == RT_OK)
+        rc = rt::encode_bf16_kmajor_map(&mb, B, p->K, p->N, (uint64_t)p->ldb * 2u, kBN);
+    if (rc != RT_OK)
+        return rc;
+    GemmArgs g;
+    memset(&g, 0, sizeof(g));
+    g.C = C;
+    g.M = p->M;
+    g.N = p->N;
+    g.K = p->K;
+    g.ldc = p->ldc;
+    g.m_tiles = (p->M + kBM - 1) / kBM;
+    g.n_tiles = (p->N + kBN - 1) / kBN;
+    g.kb_total = p->K / kBK;
+    const uint32_t splits = p->split_k ? min(p->split_k, g.kb_total) : 1u;
+    g.kb_per_split = (g.kb_total + splits - 1) / splits;
+    g.splits = (g.kb_total + g.kb_per_split - 1) / g.kb_per_split;  // no empty split
+    g.units = g.m_tiles * g.n_tiles * g.splits;
+    g.accumulate = p->flags & RT_GEMM_ACCUMULATE;
+    g.error = error;
+    g.vec_ok = ((uintptr_t)C % 16u) == 0u && (p->ldc % 4u) == 0u;
+    cudaStream_t s = (cudaStream_t)stream;
+    cudaError_t err;
+    if (g.splits > 1u && !g.accumulate) {
+        // K-splits add their partial sums into C
+        if (p->ldc == p->N)
+            err = cudaMemsetAsync(C, 0, (size_t)p->M * p->N * sizeof(float), s);
+        else
+            err = cudaMemset2DAsync(C, (size_t)p->ldc * sizeof(float), 0, (size_t)p->N * sizeof(float),
+                                    p->M, s);
+        if (err != cudaSuccess)
+            return rt::cuda_fail(err, "gemm_bf16: zero C");
+    }
+    static int sms_of[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) {
+        rt::set_error("gemm_bf16: device index %d out of range", dev);
+        return RT_EINVAL;
+    }
+    int &sms = sms_of[dev];
+    if (!sms) {
+        err = cudaFuncSetAttribute(gemm_bf16_tn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)kSmemBytes);
+        if (err == cudaSuccess)
+            err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (err != cudaSuccess) {
+            sms = 0;
+            return rt::cuda_fail(err, "gemm_bf16: setup");
+        }
+    }
+    const uint32_t grid = min(g.units, (uint32_t)sms);
+    gemm_bf16_tn_kernel<<<grid, kThreads, kSmemBytes, s>>>(ma, mb, g);
+    err = cudaGetLastError();
+    return err == cudaSuccess ? RT_OK : rt::cuda_fail(err, "gemm_bf16: launch");
+}

@@ -177,6 +177,105 @@ __device__ __forceinline__ void grid_dep_launch()
     asm volatile("griddepcontrol.launch_dependents;");
 }
 
+// ---------------------------------------------------------------- tcgen05
+// Tensor memory (TMEM) and the 5th-generation tensor-core MMA.  Formats
+// follow the PTX ISA for sm_100a: shared-memory matrix descriptors (start
+// >> 4 at [0,14), leading byte offset >> 4 at [16,30), stride byte offset
+// >> 4 at [32,46), version 1 at [46,48), layout at [61,64)) and the
+// kind::f16 instruction descriptor.
+
+// Allocate `ncols` TMEM columns (power of two >= 32) for this CTA; one full
+// warp executes it.  The TMEM address is written to shared memory at dst.
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols)
+{
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish()
+{
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols)
+{
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_before_sync()
+{
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after_sync()
+{
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// SWIZZLE_128B shared-memory matrix descriptor (version 1, base offset 0).
+// K-major operand: rows of 128 bytes, 8-row groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr, uint32_t lbo_bytes,
+                                                     uint32_t sbo_bytes)
+{
+    uint64_t d = 0;
+    d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1u << 46;  // version
+    d |= (uint64_t)2u << 61;  // SWIZZLE_128B
+    return d;
+}
+
+// kind::f16 instruction descriptor: bf16 A and B, fp32 accumulator, A
+// K-major, B K-major (b_mn_major = 0) or MN-major (1), M x N.
+__host__ __device__ constexpr uint32_t umma_idesc_bf16(uint32_t M, uint32_t N, uint32_t b_mn_major)
+{
+    return (1u << 4)              // D format: f32
+           | (1u << 7)            // A format: bf16
+           | (1u << 10)           // B format: bf16
+           | (b_mn_major << 16)   // B major
+           | ((N >> 3) << 17)     // N / 8
+           | ((M >> 4) << 24);    // M / 16
+}
+
+// D[tmem] (+)= A[smem desc] * B[smem desc]; issued by one thread.
+__device__ __forceinline__ void umma_bf16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                             uint32_t idesc, uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrive on a shared-memory mbarrier once this thread's earlier tcgen05.mma
+// operations have completed.
+__device__ __forceinline__ void umma_commit(uint32_t bar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+
+// 32 consecutive TMEM columns of this warp's 32 lanes (lane i of the warp
+// reads TMEM lane taddr.lane + i); complete after tmem_ld_wait().
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32])
+{
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+          "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+          "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait()
+{
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
 // 2^x with the SFU (ex2.approx, flush-to-zero); 2^-inf = +0.
 __device__ __forceinline__ float fast_exp2(float x)
 {
@@ -256,5 +355,10 @@ int num_sms();
 // Encode a 2-D bf16 tensor map over rows of 128 elements (256 B), box
 // 64 x 16 with 128-byte swizzle.  Returns 0 or RT_* error.
 int encode_kv_rows_map(CUtensorMap *map, const void *base, uint64_t rows);
+// 2-D map over a row-major bf16 matrix [rows][k] (k contiguous), box of 64
+// columns (128 bytes) x box_rows rows, 128-byte swizzle: the K-major
+// operand tile of a tcgen05 MMA.  Out-of-range rows and columns read zero.
+int encode_bf16_kmajor_map(CUtensorMap *map, const void *base, uint64_t k, uint64_t rows,
+                           uint64_t row_stride_bytes, uint32_t box_rows);
 
 }  // namespace rt

@@ -455,6 +455,33 @@ int64_t rt_host_decode_pump(CommandRing *ring, const Descriptor *descs, uint32_t
                             uint32_t n_expected, uint32_t timeout_ms);
 
 /* ------------------------------------------------------------------------
+ * Projections of the decode step on the tensor cores (new: the reference
+ * synthesises its query with one <<<1,128>>> launch per slot and step,
+ * cu/model_state.cu:6-52 and cu/query_producer.cu:5-26, and has no LM
+ * head).
+ *
+ *   C[m][n] (+)= sum_k A[m][k] * B[n][k]
+ *
+ * A bf16 [M][lda] (activations, K contiguous), B bf16 [N][ldb] (a weight
+ * stored [out][in], K contiguous), C fp32 [M][ldc]; fp32 accumulation.
+ * K a multiple of 64; lda, ldb multiples of 8 elements; A, B 16-byte
+ * aligned.  split_k > 1 divides K among CTAs that add into C (C is zeroed
+ * first unless RT_GEMM_ACCUMULATE).  `error` is a device int32 set to 1 if
+ * a bounded wait inside the kernel expired (never expected).
+ * ---------------------------------------------------------------------- */
+#define RT_GEMM_ACCUMULATE 1u
+
+typedef struct {
+    uint32_t M, N, K;
+    uint32_t lda, ldb, ldc;  /* row strides in elements */
+    uint32_t split_k;        /* 0 or 1: none */
+    uint32_t flags;          /* RT_GEMM_ACCUMULATE */
+} rt_gemm_params_t;
+
+int rt_gemm_bf16(const rt_gemm_params_t *p, const void *A, const void *B, float *C,
+                 int32_t *error, void *stream);
+
+/* ------------------------------------------------------------------------
  * Rewards and group-normalised advantages (new; the reference has only the
  * mock scorer, cu/reward.cu:4-15, never launched).
  * ---------------------------------------------------------------------- */

@@ -1,0 +1,85 @@
+"""bf16 GEMM on the tensor cores (rt_gemm_bf16, tcgen05) against a float64
+product of the same bf16 inputs computed by torch.
+
+Tolerance: fp32 accumulation of exact bf16 products, so the error of each
+output is bounded by a small multiple of 2^-24 * K * sum_k |a_k b_k|; the
+test allows |C - C64| <= 2^-16 * sum_k |a_k b_k| + 1e-6 (far inside that
+bound for K <= 4096, far outside any layout or indexing error)."""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def gemm(pkg, A, B, C=None, split_k=0, accumulate=False, ldc=None):
+    M, K = A.shape
+    N = B.shape[0]
+    if C is None:
+        C = torch.full((M, ldc or N), float("nan"), dtype=torch.float32, device=A.device)
+    p = pkg.rt_gemm_params_t(M, N, K, A.stride(0), B.stride(0), C.stride(0), split_k,
+                             1 if accumulate else 0)
+    err = torch.zeros(1, dtype=torch.int32, device=A.device)
+    pkg.check(pkg.lib().rt_gemm_bf16(ctypes.byref(p), pkg._ptr(A), pkg._ptr(B), pkg._ptr(C),
+                                     pkg._ptr(err), pkg._stream_ptr(None)), "rt_gemm_bf16")
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    return C
+
+
+def check(C, A, B, base=None):
+    A64, B64 = A.double(), B.double()
+    ref = A64 @ B64.T
+    if base is not None:
+        ref = ref + base.double()
+    bound = (A64.abs() @ B64.abs().T) * 2.0 ** -16 + 1e-6
+    err = (C.double() - ref).abs()
+    bad = err > bound
+    assert not bool(bad.any()), f"{int(bad.sum())} of {bad.numel()} outside; max err {err.max():.3e}"
+
+
+def rand(shape, seed, dev, scale=1.0):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    return (torch.randn(shape, generator=g, device=dev) * scale).to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 224, 64), (1, 1, 64), (130, 300, 128), (256, 448, 640),
+                                   (200, 1000, 256), (384, 32, 4096)])
+def test_gemm_shapes(pkg, cuda, M, N, K):
+    A, B = rand((M, K), 1, cuda), rand((N, K), 2, cuda)
+    check(gemm(pkg, A, B), A, B)
+
+
+def test_gemm_lm_head_shape(pkg, cuda):
+    """The decode step's LM head: 256 slots x 4096 -> 32,000 logits."""
+    A, B = rand((256, 4096), 3, cuda), rand((32000, 4096), 4, cuda, scale=0.02)
+    check(gemm(pkg, A, B), A, B)
+
+
+@pytest.mark.parametrize("split", [2, 4, 7, 64])
+def test_gemm_split_k(pkg, cuda, split):
+    """The QKV projection shape (N = 6,144) with K divided among CTAs."""
+    A, B = rand((256, 4096), 5, cuda), rand((6144, 4096), 6, cuda, scale=0.02)
+    check(gemm(pkg, A, B, split_k=split), A, B)
+
+
+def test_gemm_accumulate_and_strides(pkg, cuda):
+    """C += A B^T into a wider C; A and B are row slices of larger buffers."""
+    Abig, Bbig = rand((160, 1024), 7, cuda), rand((520, 640), 8, cuda)
+    A, B = Abig[:, 64:64 + 512], Bbig[:, :512]
+    base = torch.randn(160, 600, device=cuda)
+    C = base.clone()
+    gemm(pkg, A, B, C=C, accumulate=True)
+    check(C[:, :520], A, B, base=base[:, :520])
+    assert torch.equal(C[:, 520:], base[:, 520:])   # columns past N untouched
+    C2 = base.clone()
+    gemm(pkg, A, B, C=C2, accumulate=True, split_k=3)
+    check(C2[:, :520], A, B, base=base[:, :520])
+
+
+def test_gemm_rejects_bad_shapes(pkg, cuda):
+    A, B = rand((8, 100), 9, cuda), rand((8, 100), 10, cuda)
+    with pytest.raises(pkg.RuntimeErrorRT, match="multiple of 64"):
+        gemm(pkg, A, B)
