@@ -8,20 +8,22 @@
 // cu/query_producer.cu:5-26) and has no LM head; this is the batched
 // projection those per-slot launches stand in for.
 //
-// Kernel: one persistent CTA per SM walking (tile, K-split) units,
-// 128 x 224 output tiles (32,000 / 224 gives 286 tiles: two full waves on
-// 148 SMs), three warp roles:
-//   warp 0   one thread issues TMA loads of the A (128 x 64) and B
-//            (224 x 64) K-slices into a 4-stage shared-memory ring
-//            (128-byte swizzle, no multicast);
+// Kernel: one persistent CTA per SM walking (tile, K-split) units of
+// 256 x 224 outputs: the decode batch (256 slots) is one M tile, so each
+// CTA fetches its weight slab exactly once and 32,000 / 224 gives 143
+// units, one wave on 148 SMs.  Three warp roles:
+//   warp 0   one thread issues TMA loads of the A (256 x 64) and B
+//            (224 x 64) K-slices into a 3-stage shared-memory ring
+//            (60 KiB per stage, 128-byte swizzle, no multicast);
 //   warp 1   allocates 512 TMEM columns (two fp32 accumulators of 128
-//            lanes x 256 columns) and one thread issues tcgen05.mma
-//            (M 128, N 224, K 16; four per K-slice), committing each
-//            stage back to the producer and each finished tile to the
+//            lanes x 224 columns, one per 128-row half of the tile) and
+//            one thread issues tcgen05.mma (M 128, N 224, K 16: two halves
+//            x four per K-slice, sharing the B slice), committing each
+//            stage back to the producer and each finished unit to the
 //            epilogue;
-//   warps 2-5  read the accumulator out of TMEM (tcgen05.ld, one row per
-//            thread) and store C, or add into C for K-splits, while the
-//            MMAs of the next tile fill the other accumulator.
+//   warps 2-9  read the accumulators out of TMEM (tcgen05.ld, one row per
+//            thread, four warps per half) and store C, or add into C for
+//            K-splits.
 // Every mbarrier wait is bounded; an expired wait sets the error word and
 // the CTA winds down (waiting, bounded, for its own MMAs) and frees its TMEM.
 #include <cuda_bf16.h>
@@ -33,13 +35,14 @@
 
 namespace {
 
-constexpr uint32_t kBM = 128, kBN = 224, kBK = 64, kStages = 4;
-constexpr uint32_t kABytes = kBM * kBK * 2;         // 16 KiB
+constexpr uint32_t kBM = 256, kBN = 224, kBK = 64, kStages = 3;
+constexpr uint32_t kHalf = 128;                      // rows per UMMA (M 128)
+constexpr uint32_t kABytes = kBM * kBK * 2;         // 32 KiB
 constexpr uint32_t kBBytes = kBN * kBK * 2;         // 28 KiB
 constexpr uint32_t kStageBytes = kABytes + kBBytes;  // multiple of 1024 (swizzle atoms)
-constexpr uint32_t kAccCols = 256;                   // TMEM columns per accumulator
+constexpr uint32_t kAccCols = 256;                   // TMEM columns per accumulator (half)
 constexpr uint32_t kTmemCols = 2 * kAccCols;
-constexpr uint32_t kThreads = 192;
+constexpr uint32_t kThreads = 320;
 constexpr uint64_t kWaitNs = 2000000000ull;
 constexpr uint32_t kSmemBytes = kStages * kStageBytes + 1024 /* alignment */ + 256 /* barriers */;
 
@@ -58,7 +61,7 @@ struct GemmArgs {
 
 struct Shared {
     uint64_t full[kStages], empty[kStages];
-    uint64_t acc_full[2], acc_empty[2];
+    uint64_t acc_full, acc_empty;
     uint32_t tmem_base;
     uint32_t abort;
 };
@@ -110,10 +113,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             rt::mbar_init(rt::smem_u32(&sh->full[s]), 1u);
             rt::mbar_init(rt::smem_u32(&sh->empty[s]), 1u);
         }
-        for (uint32_t b = 0; b < 2; b++) {
-            rt::mbar_init(rt::smem_u32(&sh->acc_full[b]), 1u);
-            rt::mbar_init(rt::smem_u32(&sh->acc_empty[b]), 128u);
-        }
+        rt::mbar_init(rt::smem_u32(&sh->acc_full), 1u);
+        rt::mbar_init(rt::smem_u32(&sh->acc_empty), 256u);
         sh->abort = 0u;
         rt::mbar_fence_init();
         rt::prefetch_tensormap(&map_a);
@@ -158,15 +159,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         // ------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            const uint32_t idesc = rt::umma_idesc_bf16(kBM, kBN, 0u);
-            uint32_t stage = 0, phase = 0, buf = 0, acc_phase = 0;
+            const uint32_t idesc = rt::umma_idesc_bf16(kHalf, kBN, 0u);
+            uint32_t stage = 0, phase = 0, acc_phase = 0;
             for (uint32_t u = blockIdx.x; u < g.units; u += gridDim.x) {
                 uint32_t m0, n0, kb0, kb1;
                 unit_coords(g, u, m0, n0, kb0, kb1);
-                if (!wait_or_abort(sh, rt::smem_u32(&sh->acc_empty[buf]), acc_phase ^ 1u, g))
+                const uint32_t halves = m0 + kHalf < g.M ? 2u : 1u;  // rows past M: no MMA
+                if (!wait_or_abort(sh, rt::smem_u32(&sh->acc_empty), acc_phase ^ 1u, g))
                     break;
                 rt::tc_fence_after_sync();
-                const uint32_t d_tmem = tmem + buf * kAccCols;
                 bool ok = true;
                 for (uint32_t kb = kb0; kb < kb1; kb++) {
                     if (!(ok = wait_or_abort(sh, rt::smem_u32(&sh->full[stage]), phase, g)))
@@ -176,9 +177,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (uint32_t kk = 0; kk < kBK / 16u; kk++) {
                         // K-major SW128: 16 bf16 = 32 bytes further along each row
-                        const uint64_t da = rt::umma_desc_sw128(sa + kk * 32u, 16u, 1024u);
                         const uint64_t db = rt::umma_desc_sw128(sa + kABytes + kk * 32u, 16u, 1024u);
-                        rt::umma_bf16_ss(d_tmem, da, db, idesc, (kb > kb0 || kk > 0u) ? 1u : 0u);
+                        for (uint32_t h = 0; h < halves; h++) {
+                            const uint64_t da = rt::umma_desc_sw128(
+                                sa + h * (kHalf * kBK * 2u) + kk * 32u, 16u, 1024u);
+                            rt::umma_bf16_ss(tmem + h * kAccCols, da, db, idesc,
+                                             (kb > kb0 || kk > 0u) ? 1u : 0u);
+                        }
                     }
                     rt::umma_commit(rt::smem_u32(&sh->empty[stage]));
                     if (++stage == kStages) {
@@ -188,22 +193,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 if (!ok)
                     break;
-                rt::umma_commit(rt::smem_u32(&sh->acc_full[buf]));
-                if (++buf == 2u) {
-                    buf = 0;
-                    acc_phase ^= 1u;
-                }
+                rt::umma_commit(rt::smem_u32(&sh->acc_full));
+                acc_phase ^= 1u;
             }
         }
     } else {
         // ------------------------------------------------------- epilogue
         const uint32_t quarter = warp & 3u;  // TMEM lanes 32*quarter .. +31
-        const uint32_t row = quarter * 32u + lane;
-        uint32_t buf = 0, acc_phase = 0;
+        const uint32_t half = (warp - 2u) >> 2;
+        const uint32_t row = half * kHalf + quarter * 32u + lane;
+        uint32_t acc_phase = 0;
         for (uint32_t u = blockIdx.x; u < g.units; u += gridDim.x) {
             uint32_t m0, n0, kb0, kb1;
             unit_coords(g, u, m0, n0, kb0, kb1);
-            if (!wait_or_abort(sh, rt::smem_u32(&sh->acc_full[buf]), acc_phase, g))
+            if (!wait_or_abort(sh, rt::smem_u32(&sh->acc_full), acc_phase, g))
                 break;
             rt::tc_fence_after_sync();
             const uint32_t m = m0 + row;
@@ -212,7 +215,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
             for (uint32_t c = 0; c < kBN; c += 32u) {
                 uint32_t r[32];
-                rt::tmem_ld32(tmem + buf * kAccCols + ((quarter * 32u) << 16) + c, r);
+                rt::tmem_ld32(tmem + half * kAccCols + ((quarter * 32u) << 16) + c, r);
                 rt::tmem_ld_wait();
                 if (m < g.M) {
                     const uint32_t n = n0 + c;
@@ -237,11 +240,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             rt::tc_fence_before_sync();
-            rt::mbar_arrive(rt::smem_u32(&sh->acc_empty[buf]));
-            if (++buf == 2u) {
-                buf = 0;
-                acc_phase ^= 1u;
-            }
+            rt::mbar_arrive(rt::smem_u32(&sh->acc_empty));
+            acc_phase ^= 1u;
         }
     }
 
