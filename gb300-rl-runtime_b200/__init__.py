@@ -139,16 +139,24 @@ class rt_rollout_stats_t(ctypes.Structure):
                 ("consumed", ctypes.c_uint32), ("admitted", ctypes.c_uint32),
                 ("dropped", ctypes.c_uint32), ("done", ctypes.c_uint32),
                 ("max_active", ctypes.c_uint32), ("stopped_by_sentinel", ctypes.c_uint32),
-                ("error", ctypes.c_int32), ("attn_error", ctypes.c_int32)]
+                ("error", ctypes.c_int32), ("attn_error", ctypes.c_int32),
+                ("model_error", ctypes.c_int32), ("pad", ctypes.c_uint32)]
 
     def as_dict(self):
-        return {n: getattr(self, n) for n, _ in self._fields_}
+        return {n: getattr(self, n) for n, _ in self._fields_ if n != "pad"}
 
 
 class rt_rollout_buffers_t(ctypes.Structure):
     _fields_ = [(n, ctypes.c_void_p) for n in ("q", "attn_out", "page_table", "seq_lens",
                                                "groups", "n_groups", "skip_pages")] + [
-        ("max_pages", ctypes.c_uint32), ("max_groups", ctypes.c_uint32)]
+        ("max_pages", ctypes.c_uint32), ("max_groups", ctypes.c_uint32)] + [
+        (n, ctypes.c_void_p) for n in ("logits", "tokens", "enable", "sample_rows", "hidden_in",
+                                       "qkv", "hidden_out", "embed_tokens")]
+
+
+class rt_model_weights_t(ctypes.Structure):
+    _fields_ = [("embed", ctypes.c_void_p), ("w_qkv", ctypes.c_void_p), ("w_lm", ctypes.c_void_p),
+                ("d_model", ctypes.c_uint32), ("reserved", ctypes.c_uint32)]
 
 
 class rt_gemm_params_t(ctypes.Structure):
@@ -236,6 +244,7 @@ _SIGS = {
                                              _P, _P, ctypes.c_uint32, _P, _P]),
     "rt_host_decode_pump": (ctypes.c_int64, [_P, _P, ctypes.c_uint32, ctypes.c_uint32, _P, _P,
                                              ctypes.c_uint32, ctypes.c_uint32]),
+    "rt_rollout_set_model": (ctypes.c_int, [_P, ctypes.POINTER(rt_model_weights_t)]),
     "rt_gemm_bf16": (ctypes.c_int, [ctypes.POINTER(rt_gemm_params_t), _P, _P, _P, _P, _P]),
     "ring_create": (_P, []), "ring_destroy": (None, [_P]),
     "comp_ring_create": (_P, []), "comp_ring_destroy": (None, [_P]),
@@ -433,7 +442,7 @@ def sample_uniform24(seed, rollout_id, step) -> int:
 
 
 # ------------------------------------------------------------ rollout loop
-RT_ROLLOUT_DECODE_NONE, RT_ROLLOUT_DECODE_FULL = 0, 1
+RT_ROLLOUT_DECODE_NONE, RT_ROLLOUT_DECODE_FULL, RT_ROLLOUT_DECODE_MODEL = 0, 1, 2
 RT_REWARD_MOCK, RT_REWARD_PHILOX = 0, 1
 RT_PREFIX_ATTN_GROUPED = 0
 RT_PREFIX_ATTN_PER_SEQUENCE = 1
@@ -556,6 +565,14 @@ class RolloutEngine:
             raise err[0]
         check(rc, "rt_rollout_profile_hook")
         return out.as_dict()
+
+    def set_model(self, embed, w_qkv, w_lm):
+        """rt_rollout_set_model: bf16 device tensors embed [vocab][d],
+        w_qkv [(hq + 2 hkv) * 128][d], w_lm [vocab][d] (kept referenced)."""
+        self._weights = (embed, w_qkv, w_lm)
+        w = rt_model_weights_t(embed.data_ptr(), w_qkv.data_ptr(), w_lm.data_ptr(),
+                               embed.shape[1], 0)
+        check(lib().rt_rollout_set_model(self.h, ctypes.byref(w)), "rt_rollout_set_model")
 
     def buffers(self):
         b = rt_rollout_buffers_t()

@@ -22,8 +22,12 @@
 //            stage back to the producer and each finished unit to the
 //            epilogue;
 //   warps 2-9  read the accumulators out of TMEM (tcgen05.ld, one row per
-//            thread, four warps per half) and store C, or add into C for
-//            K-splits.
+//            thread, four warps per half) and store C.
+// K-splits of one output tile add into C in split order: split s waits
+// (bounded) for the tile's order counter to reach s, stores (s = 0, unless
+// accumulating) or adds its partial sums with plain loads and stores, and
+// passes the counter on; the last split resets it.  Results are therefore
+// independent of scheduling, and no workspace or atomics are needed.
 // Every mbarrier wait is bounded; an expired wait sets the error word and
 // the CTA winds down (waiting, bounded, for its own MMAs) and frees its TMEM.
 #include <cuda_bf16.h>
@@ -32,6 +36,7 @@
 
 #include "rlrt.h"
 #include "rt_common.cuh"
+#include "rt_internal.h"
 
 namespace {
 
@@ -45,6 +50,10 @@ constexpr uint32_t kTmemCols = 2 * kAccCols;
 constexpr uint32_t kThreads = 320;
 constexpr uint64_t kWaitNs = 2000000000ull;
 constexpr uint32_t kSmemBytes = kStages * kStageBytes + 1024 /* alignment */ + 256 /* barriers */;
+constexpr uint32_t kMaxSplitTiles = 4096;  // output tiles of one split-K call
+
+// Per-tile split order counters (zero at load, reset by each tile's last split).
+__device__ uint32_t g_split_order[kMaxSplitTiles];
 
 static_assert(kABytes % 1024 == 0 && kBBytes % 1024 == 0, "stage buffers stay 1024-byte aligned");
 static_assert(kBN % 16 == 0 && kBN <= 256 && kBN <= kAccCols, "UMMA N for M = 128");
@@ -64,6 +73,7 @@ struct Shared {
     uint64_t acc_full, acc_empty;
     uint32_t tmem_base;
     uint32_t abort;
+    uint32_t ep_ok[8];  // epilogue warps' wait outcomes for the current unit
 };
 
 __device__ __forceinline__ void unit_coords(const GemmArgs &g, uint32_t u, uint32_t &m0,
@@ -77,6 +87,24 @@ __device__ __forceinline__ void unit_coords(const GemmArgs &g, uint32_t u, uint3
     n0 = (t / g.m_tiles) * kBN;
     kb0 = split * g.kb_per_split;
     kb1 = min(kb0 + g.kb_per_split, g.kb_total);
+}
+
+__device__ __forceinline__ uint32_t ld_acquire(const uint32_t *p)
+{
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release(uint32_t *p, uint32_t v)
+{
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Barrier of the 256 epilogue threads (warps 2-9) only.
+__device__ __forceinline__ void epilogue_sync()
+{
+    asm volatile("bar.sync 1, 256;" ::: "memory");
 }
 
 __device__ __forceinline__ bool wait_or_abort(Shared *sh, uint32_t bar, uint32_t parity,
@@ -206,12 +234,40 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (uint32_t u = blockIdx.x; u < g.units; u += gridDim.x) {
             uint32_t m0, n0, kb0, kb1;
             unit_coords(g, u, m0, n0, kb0, kb1);
-            if (!wait_or_abort(sh, rt::smem_u32(&sh->acc_full), acc_phase, g))
+            const uint32_t split = u % g.splits, tile = u / g.splits;
+            // Exits are decided uniformly by all 256 epilogue threads (the
+            // TMEM loads are warp-collective and the named barriers need
+            // every epilogue warp): one lane per warp waits, the outcomes
+            // meet in shared memory, everyone reads them after a barrier.
+            bool ok = true;
+            if (lane == 0u)
+                ok = wait_or_abort(sh, rt::smem_u32(&sh->acc_full), acc_phase, g);
+            if (ok && g.splits > 1u && warp == 2u && lane == 0u) {
+                // this split's turn on the tile (its predecessor is unit u - 1)
+                const uint64_t t0 = rt::globaltimer_ns();
+                while (ld_acquire(&g_split_order[tile]) != split) {
+                    if (*(volatile uint32_t *)&sh->abort || rt::globaltimer_ns() - t0 > kWaitNs) {
+                        atomicCAS(g.error, 0, 2);
+                        *(volatile uint32_t *)&sh->abort = 1u;
+                        ok = false;
+                        break;
+                    }
+                    __nanosleep(64);
+                }
+            }
+            if (lane == 0u)
+                sh->ep_ok[warp - 2u] = ok ? 1u : 0u;
+            epilogue_sync();
+            bool go = true;
+#pragma unroll
+            for (uint32_t w = 0; w < 8u; w++)
+                go &= sh->ep_ok[w] != 0u;
+            if (!go)
                 break;
             rt::tc_fence_after_sync();
             const uint32_t m = m0 + row;
             float *crow = g.C + (uint64_t)m * g.ldc;
-            const bool add = g.accumulate || g.splits > 1u;
+            const bool add = g.accumulate || split > 0u;
 #pragma unroll 1
             for (uint32_t c = 0; c < kBN; c += 32u) {
                 uint32_t r[32];
@@ -219,21 +275,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                 rt::tmem_ld_wait();
                 if (m < g.M) {
                     const uint32_t n = n0 + c;
-                    if (!add && n + 32u <= g.N && g.vec_ok) {
+                    if (n + 32u <= g.N && g.vec_ok) {
                         float4 *dst = reinterpret_cast<float4 *>(crow + n);
 #pragma unroll
-                        for (uint32_t j = 0; j < 8; j++)
-                            dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                                                 __uint_as_float(r[4 * j + 2]),
-                                                 __uint_as_float(r[4 * j + 3]));
+                        for (uint32_t j = 0; j < 8; j++) {
+                            float4 v = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                                   __uint_as_float(r[4 * j + 2]),
+                                                   __uint_as_float(r[4 * j + 3]));
+                            if (add) {
+                                const float4 c = __ldcg(dst + j);
+                                v = make_float4(c.x + v.x, c.y + v.y, c.z + v.z, c.w + v.w);
+                            }
+                            dst[j] = v;
+                        }
                     } else {
 #pragma unroll
                         for (uint32_t j = 0; j < 32; j++) {
                             if (n + j < g.N) {
-                                if (add)
-                                    atomicAdd(crow + n + j, __uint_as_float(r[j]));
-                                else
-                                    crow[n + j] = __uint_as_float(r[j]);
+                                const float v = __uint_as_float(r[j]);
+                                crow[n + j] = add ? __ldcg(crow + n + j) + v : v;
                             }
                         }
                     }
@@ -242,6 +302,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             rt::tc_fence_before_sync();
             rt::mbar_arrive(rt::smem_u32(&sh->acc_empty));
             acc_phase ^= 1u;
+            // every row of the unit is stored (and ep_ok may be rewritten)
+            __threadfence();
+            epilogue_sync();
+            if (g.splits > 1u && warp == 2u && lane == 0u)
+                st_release(&g_split_order[tile], split + 1u == g.splits ? 0u : split + 1u);
         }
     }
 
@@ -254,7 +319,41 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// Shared-memory opt-in of the kernel on the current device (once per
+// device) and the device's SM count.
+int gemm_setup(int *sms_out)
+{
+    static int sms_of[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) {
+        rt::set_error("gemm_bf16: device index %d out of range", dev);
+        return RT_EINVAL;
+    }
+    int &sms = sms_of[dev];
+    if (!sms) {
+        cudaError_t err = cudaFuncSetAttribute(
+            gemm_bf16_tn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+        if (err == cudaSuccess)
+            err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (err != cudaSuccess) {
+            sms = 0;
+            return rt::cuda_fail(err, "gemm_bf16: setup");
+        }
+    }
+    *sms_out = sms;
+    return RT_OK;
+}
+
 }  // namespace
+
+namespace rt {
+int gemm_prepare()
+{
+    int sms = 0;
+    return gemm_setup(&sms);
+}
+}  // namespace rt
 
 extern "C" int rt_gemm_bf16(const rt_gemm_params_t *p, const void *A, const void *B, float *C,
                             int32_t *error, void *stream)
@@ -297,34 +396,14 @@ extern "C" int rt_gemm_bf16(const rt_gemm_params_t *p, const void *A, const void
     g.vec_ok = ((uintptr_t)C % 16u) == 0u && (p->ldc % 4u) == 0u;
     cudaStream_t s = (cudaStream_t)stream;
     cudaError_t err;
-    if (g.splits > 1u && !g.accumulate) {
-        // K-splits add their partial sums into C
-        if (p->ldc == p->N)
-            err = cudaMemsetAsync(C, 0, (size_t)p->M * p->N * sizeof(float), s);
-        else
-            err = cudaMemset2DAsync(C, (size_t)p->ldc * sizeof(float), 0, (size_t)p->N * sizeof(float),
-                                    p->M, s);
-        if (err != cudaSuccess)
-            return rt::cuda_fail(err, "gemm_bf16: zero C");
-    }
-    static int sms_of[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64) {
-        rt::set_error("gemm_bf16: device index %d out of range", dev);
+    if (g.splits > 1u && g.m_tiles * g.n_tiles > kMaxSplitTiles) {
+        rt::set_error("gemm_bf16: split-K over more than %u output tiles", kMaxSplitTiles);
         return RT_EINVAL;
     }
-    int &sms = sms_of[dev];
-    if (!sms) {
-        err = cudaFuncSetAttribute(gemm_bf16_tn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)kSmemBytes);
-        if (err == cudaSuccess)
-            err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        if (err != cudaSuccess) {
-            sms = 0;
-            return rt::cuda_fail(err, "gemm_bf16: setup");
-        }
-    }
+    int sms = 0;
+    int rc2 = gemm_setup(&sms);
+    if (rc2 != RT_OK)
+        return rc2;
     const uint32_t grid = min(g.units, (uint32_t)sms);
     gemm_bf16_tn_kernel<<<grid, kThreads, kSmemBytes, s>>>(ma, mb, g);
     err = cudaGetLastError();

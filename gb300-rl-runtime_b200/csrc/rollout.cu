@@ -23,6 +23,7 @@
 // Counter-only decode (the reference's mock) uses the same schedule pass
 // with tokens_generated++ in place of the decode chain; the drop-in launcher
 // rt_launch_rollout_worker runs that pass in a persistent single-CTA kernel.
+#include <algorithm>
 #include <cstdint>
 #include <cstring>
 #include <mutex>
@@ -97,6 +98,13 @@ struct Dev {
     uint32_t *n_groups;       // [1]
     uint32_t *skip;           // [max_slots]
     uint32_t max_groups;      // 0 = per-sequence attention only
+    // model decode (RT_ROLLOUT_DECODE_MODEL)
+    const __nv_bfloat16 *w_embed, *w_qkv, *w_lm;
+    __nv_bfloat16 *hin, *hout;  // [max_slots][dm]: embeddings in, attention out as bf16
+    float *qkv;                 // [max_slots][qkv_n]
+    uint32_t *emb_tok;          // [max_slots] token embedded this pass
+    int32_t *gemm_err;          // projection kernels' error word
+    uint32_t dm, qkv_n;
 };
 
 __device__ __forceinline__ float reward_for(const Dev &d, uint32_t request_lo, uint32_t tokens)
@@ -380,7 +388,7 @@ __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
     const uint32_t s = threadIdx.x;
     const RtIo &io = sh.io;
     RtCtl *ctl = &sh.ctl;
-    const bool full = d.decode == RT_ROLLOUT_DECODE_FULL;
+    const bool full = d.decode != RT_ROLLOUT_DECODE_NONE;
 
     // 1. commit the tokens sampled in the previous pass
     const bool committing = full && s < d.max_slots && sh.ext[s].decoding;
@@ -606,7 +614,7 @@ __global__ void __launch_bounds__(kSched, 1)
 schedule_kernel(const Dev d, cudaGraphConditionalHandle handle, int in_graph)
 {
     __shared__ SchedShared sh;
-    const bool full = d.decode == RT_ROLLOUT_DECODE_FULL;
+    const bool full = d.decode != RT_ROLLOUT_DECODE_NONE;
     // The prepare kernel (a programmatic dependent launch) may be scheduled
     // now; it waits for this kernel to complete before reading its outputs.
     rt::grid_dep_launch();
@@ -632,18 +640,12 @@ schedule_kernel(const Dev d, cudaGraphConditionalHandle handle, int in_graph)
         cudaGraphSetConditional(handle, stop ? 0u : 1u);
 }
 
-__global__ void __launch_bounds__(256) prepare_kernel(const Dev d)
+// First write into a shared prefix's partial page: the slot's private copy
+// (one CTA; the copy is complete when this returns).
+__device__ __forceinline__ void cow_copy(const Dev &d, SlotExt &e, const int32_t *pt)
 {
-    const uint32_t s = blockIdx.x;
-    rt::grid_dep_wait();    // the schedule kernel's plan is complete
-    rt::grid_dep_launch();  // the attention kernels may be scheduled
-    if (!d.enable[s])
-        return;
-    SlotExt &e = d.ext[s];
-    const int32_t *pt = d.page_table + (size_t)s * d.maxp;
     const int32_t cow = e.cow_src;
     if (cow >= 0) {
-        // first write into a shared prefix's partial page: private copy
         const uint64_t page_elems = rt_page_bytes(d.hkv) / 2u;
         const uint4 *src = reinterpret_cast<const uint4 *>(d.arena + (uint64_t)cow * page_elems);
         uint4 *dst = reinterpret_cast<uint4 *>(d.arena + (uint64_t)pt[e.ctx_len >> 4] * page_elems);
@@ -654,6 +656,18 @@ __global__ void __launch_bounds__(256) prepare_kernel(const Dev d)
         if (threadIdx.x == 0)
             e.cow_src = -1;
     }
+}
+
+__global__ void __launch_bounds__(256) prepare_kernel(const Dev d)
+{
+    const uint32_t s = blockIdx.x;
+    rt::grid_dep_wait();    // the schedule kernel's plan is complete
+    rt::grid_dep_launch();  // the attention kernels may be scheduled
+    if (!d.enable[s])
+        return;
+    SlotExt &e = d.ext[s];
+    const int32_t *pt = d.page_table + (size_t)s * d.maxp;
+    cow_copy(d, e, pt);
     const uint32_t pos = e.pos, lt = e.last_token, rq = e.request_lo;
     const uint64_t seed = e.seed;
     const uint64_t page = (uint64_t)pt[pos >> 4];
@@ -676,6 +690,73 @@ __global__ void __launch_bounds__(256) prepare_kernel(const Dev d)
         reinterpret_cast<uint2 *>(dst)[0] =
             make_uint2(rt::pack_bf16x2(z[0], z[1]), rt::pack_bf16x2(z[2], z[3]));
     }
+}
+
+// ---- model decode: embedding gather, q / K / V from the QKV projection,
+// attention output to bf16 (the projections themselves are rt_gemm_bf16)
+
+// x_s = embed[last token of slot s] (token 0 before the slot's first token).
+__global__ void __launch_bounds__(256) embed_kernel(const Dev d)
+{
+    const uint32_t s = blockIdx.x;
+    rt::grid_dep_wait();  // the schedule kernel's plan is complete
+    rt::grid_dep_launch();
+    if (!d.enable[s])
+        return;
+    const uint32_t tok = min(d.ext[s].last_token, d.vocab - 1u);
+    if (threadIdx.x == 0)
+        d.emb_tok[s] = tok;
+    const uint4 *src = reinterpret_cast<const uint4 *>(d.w_embed + (size_t)tok * d.dm);
+    uint4 *dst = reinterpret_cast<uint4 *>(d.hin + (size_t)s * d.dm);
+    for (uint32_t i = threadIdx.x; i < d.dm / 8u; i += blockDim.x)
+        dst[i] = __ldg(src + i);
+}
+
+// The slot's copy-on-write page, then q (bf16) and the new token's K and V
+// (bf16, into its page row) from the fp32 QKV projection.
+__global__ void __launch_bounds__(256) model_prepare_kernel(const Dev d)
+{
+    const uint32_t s = blockIdx.x;
+    rt::grid_dep_wait();  // the QKV projection is complete
+    rt::grid_dep_launch();
+    if (!d.enable[s])
+        return;
+    SlotExt &e = d.ext[s];
+    const int32_t *pt = d.page_table + (size_t)s * d.maxp;
+    cow_copy(d, e, pt);
+    const float4 *row = reinterpret_cast<const float4 *>(d.qkv + (size_t)s * d.qkv_n);
+    const uint32_t nq4 = d.hq * 32u;  // q: hq heads x 128 dims, 4 per float4
+    for (uint32_t g = threadIdx.x; g < nq4; g += blockDim.x) {
+        const float4 v = row[g];
+        reinterpret_cast<uint2 *>(d.q + (size_t)s * d.hq * 128u)[g] =
+            make_uint2(rt::pack_bf16x2(v.x, v.y), rt::pack_bf16x2(v.z, v.w));
+    }
+    const uint32_t pos = e.pos;
+    const uint64_t page = (uint64_t)pt[pos >> 4];
+    const uint32_t prow = pos & 15u;
+    for (uint32_t g = threadIdx.x; g < d.hkv * 2u * 32u; g += blockDim.x) {
+        const uint32_t plane = g / (d.hkv * 32u), h = (g >> 5) % d.hkv, d4 = g & 31u;
+        const float4 v = row[nq4 + g];  // k rows of every kv head, then v rows
+        __nv_bfloat16 *dst = d.arena + rt_page_elem_offset(page, h, plane, prow, d.hkv) + d4 * 4u;
+        reinterpret_cast<uint2 *>(dst)[0] =
+            make_uint2(rt::pack_bf16x2(v.x, v.y), rt::pack_bf16x2(v.z, v.w));
+    }
+}
+
+// hidden_out = bf16(attention output), the LM head's input.
+__global__ void __launch_bounds__(256) hidden_kernel(const Dev d)
+{
+    const uint32_t s = blockIdx.x;
+    rt::grid_dep_wait();  // the attention is complete
+    if (d.enable[s]) {
+        const float4 *src = reinterpret_cast<const float4 *>(d.attn_out + (size_t)s * d.dm);
+        uint2 *dst = reinterpret_cast<uint2 *>(d.hout + (size_t)s * d.dm);
+        for (uint32_t i = threadIdx.x; i < d.dm / 4u; i += blockDim.x) {
+            const float4 v = src[i];
+            dst[i] = make_uint2(rt::pack_bf16x2(v.x, v.y), rt::pack_bf16x2(v.z, v.w));
+        }
+    }
+    rt::grid_dep_launch();
 }
 
 // logits[v] = std * N(0,1), Philox key = seed, counter = (token index lo,
@@ -788,9 +869,73 @@ namespace {
 
 // The decode chain of one pass (after the schedule kernel).  When `ev` is
 // given, events are recorded around each of the four launches.
+// K-splits that fill the GPU for an M x N projection (each split >= 4
+// K-slices of 64).
+uint32_t gemm_splits(uint32_t M, uint32_t N, uint32_t K)
+{
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const uint32_t units = ((M + 255u) / 256u) * ((N + 223u) / 224u);
+    const uint32_t by_sm = (uint32_t)sms / units;
+    return std::max(1u, std::min(by_sm, K / 256u));
+}
+
+int launch_decode_model(rt_rollout *e, cudaStream_t st, cudaEvent_t *ev)
+{
+    const Dev &d = e->d;
+    if (ev)
+        cudaEventRecord(ev[0], st);
+    cudaError_t err = launch_pdl(embed_kernel, dim3(d.max_slots), dim3(256), st, d);
+    if (err != cudaSuccess)
+        return rt::cuda_fail(err, "rollout: embed launch");
+    rt_gemm_params_t gq = {d.max_slots, d.qkv_n, d.dm, d.dm, d.dm, d.qkv_n,
+                           gemm_splits(d.max_slots, d.qkv_n, d.dm), 0u};
+    int rc = rt_gemm_bf16(&gq, d.hin, d.w_qkv, d.qkv, d.gemm_err, st);
+    if (rc != RT_OK)
+        return rc;
+    err = launch_pdl(model_prepare_kernel, dim3(d.max_slots), dim3(256), st, d);
+    if (err != cudaSuccess)
+        return rt::cuda_fail(err, "rollout: model prepare launch");
+    if (ev)
+        cudaEventRecord(ev[1], st);
+    rc = d.max_groups
+             ? rt_paged_decode_attention_grouped(&e->ap, &e->gp, d.q, d.arena, d.page_table,
+                                                 d.seq_lens, d.groups, d.n_groups, d.skip,
+                                                 d.attn_out, e->attn_ws, e->attn_ws_bytes, st)
+             : rt_paged_decode_attention(&e->ap, d.q, d.arena, d.page_table, d.seq_lens,
+                                         d.attn_out, e->attn_ws, e->attn_ws_bytes, st);
+    if (rc != RT_OK)
+        return rc;
+    if (ev)
+        cudaEventRecord(ev[2], st);
+    err = launch_pdl(hidden_kernel, dim3(d.max_slots), dim3(256), st, d);
+    if (err != cudaSuccess)
+        return rt::cuda_fail(err, "rollout: hidden launch");
+    rt_gemm_params_t gl = {d.max_slots, d.vocab, d.dm, d.dm, d.dm, d.vocab,
+                           gemm_splits(d.max_slots, d.vocab, d.dm), 0u};
+    rc = rt_gemm_bf16(&gl, d.hout, d.w_lm, d.logits, d.gemm_err, st);
+    if (rc != RT_OK)
+        return rc;
+    if (ev)
+        cudaEventRecord(ev[3], st);
+    rt_sample_params_t sp;
+    sp.num_rows = d.max_slots;
+    sp.vocab = d.vocab;
+    sp.row_stride = d.vocab;
+    sp.fused_cum = 1u;
+    sp.row_enable = d.enable;
+    rc = rt::sample_rows_launch(&sp, d.logits, d.srows, d.tokens, st, true);
+    if (ev)
+        cudaEventRecord(ev[4], st);
+    return rc;
+}
+
 int launch_decode(rt_rollout *e, cudaStream_t st, cudaEvent_t *ev)
 {
     const Dev &d = e->d;
+    if (d.decode == RT_ROLLOUT_DECODE_MODEL)
+        return launch_decode_model(e, st, ev);
     if (ev)
         cudaEventRecord(ev[0], st);
     // Every kernel of the chain is a programmatic dependent launch: it may be
@@ -856,7 +1001,7 @@ int engine_build_graph(rt_rollout *e)
     int rc = RT_OK;
     const Dev &d = e->d;
     schedule_kernel<<<1, kSched, 0, e->cap>>>(d, h, 1);
-    if (e->cfg.decode_mode == RT_ROLLOUT_DECODE_FULL)
+    if (e->cfg.decode_mode != RT_ROLLOUT_DECODE_NONE)
         rc = launch_decode(e, e->cap, nullptr);
     cudaGraph_t captured = nullptr;
     err = cudaStreamEndCapture(e->cap, &captured);
@@ -882,7 +1027,8 @@ void engine_free(rt_rollout *e)
     void *bufs[] = {e->d.io, e->d.ctl, e->d.ext, e->d.page_table, e->d.priv, e->d.seq_lens,
                     e->d.enable, e->d.srows, e->d.tokens, e->d.q, e->d.attn_out, e->d.logits,
                     e->d.pf_len, e->d.pf_np, e->d.pf_off, e->d.pf_pages, e->d.groups,
-                    e->d.n_groups, e->d.skip, e->attn_ws};
+                    e->d.n_groups, e->d.skip, e->attn_ws, e->d.hin, e->d.hout, e->d.qkv,
+                    e->d.emb_tok, e->d.gemm_err};
     for (void *p : bufs)
         if (p)
             cudaFree(p);
@@ -904,10 +1050,11 @@ extern "C" int rt_rollout_create(const rt_rollout_config_t *cfg, KVArena *arena,
         return RT_EINVAL;
     }
     *out = nullptr;
-    const bool full = cfg->decode_mode == RT_ROLLOUT_DECODE_FULL;
+    const bool full = cfg->decode_mode != RT_ROLLOUT_DECODE_NONE;
     if (cfg->max_slots == 0 || cfg->max_slots > GPU_MAX_ROLLOUTS || cfg->max_admit == 0 ||
-        (cfg->decode_mode != RT_ROLLOUT_DECODE_FULL && cfg->decode_mode != RT_ROLLOUT_DECODE_NONE)) {
-        rt::set_error("rollout: max_slots 1..%d, max_admit >= 1, decode_mode 0/1", GPU_MAX_ROLLOUTS);
+        cfg->decode_mode > RT_ROLLOUT_DECODE_MODEL) {
+        rt::set_error("rollout: max_slots 1..%d, max_admit >= 1, decode_mode 0/1/2",
+                      GPU_MAX_ROLLOUTS);
         return RT_EINVAL;
     }
     if (full) {
@@ -1046,13 +1193,67 @@ extern "C" int rt_rollout_create(const rt_rollout_config_t *cfg, KVArena *arena,
         engine_free(e);
         return rt::cuda_fail(err, "rollout: setup");
     }
-    int rc = engine_build_graph(e);
-    if (rc != RT_OK) {
-        engine_free(e);
-        return rc;
+    // a model-decode engine builds its graph once its weights are attached
+    if (cfg->decode_mode != RT_ROLLOUT_DECODE_MODEL) {
+        int rc = engine_build_graph(e);
+        if (rc != RT_OK) {
+            engine_free(e);
+            return rc;
+        }
     }
     *out = e;
     return RT_OK;
+}
+
+extern "C" int rt_rollout_set_model(rt_rollout_t *e, const rt_model_weights_t *w)
+{
+    if (!e || !w || e->cfg.decode_mode != RT_ROLLOUT_DECODE_MODEL || !w->embed || !w->w_qkv ||
+        !w->w_lm) {
+        rt::set_error("rollout_set_model: needs a model-decode engine and three weight matrices");
+        return RT_EINVAL;
+    }
+    Dev &d = e->d;
+    if (w->d_model != d.hq * 128u || ((uintptr_t)w->embed | (uintptr_t)w->w_qkv |
+                                       (uintptr_t)w->w_lm) % 16u) {
+        rt::set_error("rollout_set_model: d_model must be num_q_heads * 128 (%u), weights "
+                      "16-byte aligned", d.hq * 128u);
+        return RT_EINVAL;
+    }
+    cudaError_t err = cudaDeviceSynchronize();  // no launch of this engine in flight
+    if (err != cudaSuccess)
+        return rt::cuda_fail(err, "rollout_set_model: sync");
+    const uint32_t S = d.max_slots;
+    d.dm = w->d_model;
+    d.qkv_n = (d.hq + 2u * d.hkv) * 128u;
+    if (!d.hin) {
+        auto ok = [&](cudaError_t x) { if (err == cudaSuccess) err = x; };
+        ok(dalloc(&d.hin, (size_t)S * d.dm));
+        ok(dalloc(&d.hout, (size_t)S * d.dm));
+        ok(dalloc(&d.qkv, (size_t)S * d.qkv_n));
+        ok(dalloc(&d.emb_tok, S));
+        ok(dalloc(&d.gemm_err, 1));
+        ok(cudaMemset(d.hin, 0, sizeof(__nv_bfloat16) * S * d.dm));
+        ok(cudaMemset(d.hout, 0, sizeof(__nv_bfloat16) * S * d.dm));
+        ok(cudaMemset(d.gemm_err, 0, sizeof(int32_t)));
+        if (err != cudaSuccess)
+            return rt::cuda_fail(err, "rollout_set_model: buffers");
+    }
+    d.w_embed = static_cast<const __nv_bfloat16 *>(w->embed);
+    d.w_qkv = static_cast<const __nv_bfloat16 *>(w->w_qkv);
+    d.w_lm = static_cast<const __nv_bfloat16 *>(w->w_lm);
+    // kernel attributes before capture (the graph bakes the weight pointers in)
+    int rc = rt::gemm_prepare();
+    if (rc != RT_OK)
+        return rc;
+    if (e->exec) {
+        cudaGraphExecDestroy(e->exec);
+        e->exec = nullptr;
+    }
+    if (e->graph) {
+        cudaGraphDestroy(e->graph);
+        e->graph = nullptr;
+    }
+    return engine_build_graph(e);
 }
 
 extern "C" int rt_rollout_destroy(rt_rollout_t *e)
@@ -1067,7 +1268,7 @@ extern "C" int rt_rollout_destroy(rt_rollout_t *e)
 extern "C" int rt_rollout_set_prefix(rt_rollout_t *e, uint32_t prefix_id, const int32_t *pages,
                                      uint32_t n_pages, uint32_t token_len)
 {
-    if (!e || (!pages && n_pages) || e->cfg.decode_mode != RT_ROLLOUT_DECODE_FULL) {
+    if (!e || (!pages && n_pages) || e->cfg.decode_mode == RT_ROLLOUT_DECODE_NONE) {
         rt::set_error("rollout_set_prefix: needs a full-decode engine and a page list");
         return RT_EINVAL;
     }
@@ -1107,6 +1308,10 @@ static int rollout_setup(rt_rollout_t *e, const rt_rollout_io_t *io, cudaStream_
 
 extern "C" int rt_rollout_launch(rt_rollout_t *e, const rt_rollout_io_t *io, void *stream)
 {
+    if (e && !e->exec) {
+        rt::set_error("rollout_launch: a model-decode engine needs rt_rollout_set_model first");
+        return RT_EINVAL;
+    }
     cudaStream_t s = (cudaStream_t)stream;
     int rc = rollout_setup(e, io, s);
     if (rc != RT_OK)
@@ -1166,7 +1371,7 @@ extern "C" int rt_rollout_profile(rt_rollout_t *e, const rt_rollout_io_t *io, vo
 
 extern "C" int rt_rollout_buffers(rt_rollout_t *e, rt_rollout_buffers_t *out)
 {
-    if (!e || !out || e->cfg.decode_mode != RT_ROLLOUT_DECODE_FULL) {
+    if (!e || !out || e->cfg.decode_mode == RT_ROLLOUT_DECODE_NONE) {
         rt::set_error("rollout_buffers: needs a full-decode engine and an output struct");
         return RT_EINVAL;
     }
@@ -1179,6 +1384,14 @@ extern "C" int rt_rollout_buffers(rt_rollout_t *e, rt_rollout_buffers_t *out)
     out->skip_pages = e->d.skip;
     out->max_pages = e->d.maxp;
     out->max_groups = e->d.max_groups;
+    out->logits = e->d.logits;
+    out->tokens = e->d.tokens;
+    out->enable = e->d.enable;
+    out->sample_rows = e->d.srows;
+    out->hidden_in = e->d.hin;
+    out->qkv = e->d.qkv;
+    out->hidden_out = e->d.hout;
+    out->embed_tokens = e->d.emb_tok;
     return RT_OK;
 }
 
@@ -1186,8 +1399,12 @@ extern "C" int rt_rollout_profile_hook(rt_rollout_t *e, const rt_rollout_io_t *i
                                        rt_rollout_profile_t *out, rt_rollout_pass_hook_t hook,
                                        void *user)
 {
-    if (!e || !out || e->cfg.decode_mode != RT_ROLLOUT_DECODE_FULL) {
+    if (!e || !out || e->cfg.decode_mode == RT_ROLLOUT_DECODE_NONE) {
         rt::set_error("rollout_profile: needs a full-decode engine and an output struct");
+        return RT_EINVAL;
+    }
+    if (!e->exec) {
+        rt::set_error("rollout_profile: a model-decode engine needs rt_rollout_set_model first");
         return RT_EINVAL;
     }
     cudaStream_t s = (cudaStream_t)stream;
@@ -1281,9 +1498,12 @@ extern "C" int rt_rollout_wait(rt_rollout_t *e, void *stream, rt_rollout_stats_t
         err = cudaMemcpy(&c, e->d.ctl, sizeof(c), cudaMemcpyDeviceToHost);
     if (err != cudaSuccess)
         return rt::cuda_fail(err, "rollout_wait");
-    int32_t attn_err = 0;
+    int32_t attn_err = 0, model_err = 0;
     if (e->attn_ws && rt_attn_workspace_error(e->attn_ws, stream, &attn_err) != RT_OK)
         return RT_ECUDA;
+    if (e->d.gemm_err && (err = cudaMemcpy(&model_err, e->d.gemm_err, sizeof(int32_t),
+                                           cudaMemcpyDeviceToHost)) != cudaSuccess)
+        return rt::cuda_fail(err, "rollout_wait: model error word");
     if (st) {
         st->passes = c.passes;
         st->tokens = c.tokens;
@@ -1295,6 +1515,8 @@ extern "C" int rt_rollout_wait(rt_rollout_t *e, void *stream, rt_rollout_stats_t
         st->stopped_by_sentinel = c.sentinel;
         st->error = c.error;
         st->attn_error = attn_err;
+        st->model_error = model_err;
+        st->pad = 0;
     }
     if (c.error) {
         rt::set_error("rollout: loop stopped with error %d after %llu passes", c.error,
@@ -1303,6 +1525,10 @@ extern "C" int rt_rollout_wait(rt_rollout_t *e, void *stream, rt_rollout_stats_t
     }
     if (attn_err) {
         rt::set_error("rollout: attention reported device error %d", attn_err);
+        return RT_EDEVICE;
+    }
+    if (model_err) {
+        rt::set_error("rollout: a projection kernel reported device error %d", model_err);
         return RT_EDEVICE;
     }
     return RT_OK;

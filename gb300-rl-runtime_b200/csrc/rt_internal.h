@@ -10,6 +10,8 @@ namespace rt {
 int attn_prepare(const rt_attn_params_t *p);
 // Same for the sampler (its shared-memory opt-in).
 int sample_prepare();
+// Same for the tensor-core GEMM (its shared-memory opt-in on this device).
+int gemm_prepare();
 // rt_sample_rows with an optional programmatic dependent launch (the kernel
 // waits for the previous kernel of the stream before reading the logits).
 int sample_rows_launch(const rt_sample_params_t *p, const float *logits,

@@ -241,6 +241,8 @@ uint32_t rt_sample_uniform24(uint64_t seed, uint32_t rollout_id, uint64_t step);
  * ---------------------------------------------------------------------- */
 #define RT_ROLLOUT_DECODE_NONE  0u
 #define RT_ROLLOUT_DECODE_FULL  1u
+#define RT_ROLLOUT_DECODE_MODEL 2u   /* as FULL, with q/K/V and logits from model weights
+                                        (rt_rollout_set_model) instead of Philox */
 #define RT_REWARD_MOCK          0u   /* (tokens & 0xFF) / 255 (reference) */
 #define RT_REWARD_PHILOX        1u   /* U(0,1): Philox(key = reward_seed, ctr = {request low 32}) */
 #define RT_PREFIX_ATTN_GROUPED       0u  /* default: rt_paged_decode_attention_grouped over
@@ -292,6 +294,8 @@ typedef struct {
     uint32_t stopped_by_sentinel;
     int32_t  error;           /* 0, or RT_ETIMEOUT / RT_EDEVICE */
     int32_t  attn_error;      /* attention workspace error word */
+    int32_t  model_error;     /* model decode: projection kernel error word */
+    uint32_t pad;
 } rt_rollout_stats_t;
 
 typedef struct rt_rollout rt_rollout_t;
@@ -345,8 +349,37 @@ typedef struct {
     const uint32_t *skip_pages;      /* [max_slots] */
     uint32_t max_pages;
     uint32_t max_groups;
+    const float *logits;             /* fp32 [max_slots][vocab] */
+    const uint32_t *tokens;          /* [max_slots] sampled this pass */
+    const uint32_t *enable;          /* [max_slots] 1 = decoded this pass */
+    const rt_sample_row_t *sample_rows; /* [max_slots] sampling parameters of this pass */
+    const void *hidden_in;           /* model decode: bf16 [max_slots][d_model] embeddings */
+    const float *qkv;                /* model decode: fp32 [max_slots][(q + 2 kv heads) * 128] */
+    const void *hidden_out;          /* model decode: bf16 [max_slots][d_model] = attn_out */
+    const uint32_t *embed_tokens;    /* model decode: [max_slots] token embedded this pass */
 } rt_rollout_buffers_t;
 int rt_rollout_buffers(rt_rollout_t *eng, rt_rollout_buffers_t *out);
+
+/* Model weights of a RT_ROLLOUT_DECODE_MODEL engine (device bf16, rows of
+ * d_model = num_q_heads * 128 elements, K contiguous; the engine keeps the
+ * pointers).  Each pass then runs, for every decoding slot s:
+ *   x_s      = embed[last token of s]            (token 0 before the first)
+ *   [q|k|v]  = x_s . w_qkv^T                     (tensor-core GEMM, fp32)
+ *   q, and k / v written into the slot's page at its position (bf16)
+ *   o_s      = paged GQA attention (as FULL)
+ *   logits_s = bf16(o_s) . w_lm^T                (tensor-core GEMM, fp32)
+ *   token    = fused sampling of logits_s (as FULL).
+ * embed [vocab][d_model]; w_qkv [(num_q_heads + 2 num_kv_heads) * 128]
+ * [d_model] (q rows, then k rows per kv head, then v rows per kv head);
+ * w_lm [vocab][d_model].  Must be called before the first launch. */
+typedef struct {
+    const void *embed;
+    const void *w_qkv;
+    const void *w_lm;
+    uint32_t d_model;
+    uint32_t reserved;
+} rt_model_weights_t;
+int rt_rollout_set_model(rt_rollout_t *eng, const rt_model_weights_t *w);
 
 /* Wait for the loop (stream sync) and read its counters. */
 int rt_rollout_wait(rt_rollout_t *eng, void *stream, rt_rollout_stats_t *stats);

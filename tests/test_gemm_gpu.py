@@ -83,3 +83,12 @@ def test_gemm_rejects_bad_shapes(pkg, cuda):
     A, B = rand((8, 100), 9, cuda), rand((8, 100), 10, cuda)
     with pytest.raises(pkg.RuntimeErrorRT, match="multiple of 64"):
         gemm(pkg, A, B)
+
+
+def test_gemm_split_k_is_deterministic(pkg, cuda):
+    """K-splits add in split order: repeated calls give identical bits."""
+    A, B = rand((256, 4096), 11, cuda), rand((2048, 4096), 12, cuda, scale=0.05)
+    first = gemm(pkg, A, B, split_k=14)
+    for _ in range(3):
+        assert torch.equal(gemm(pkg, A, B, split_k=14), first)
+    check(first, A, B)
