@@ -347,6 +347,7 @@ class RolloutWorkload:
     unit = "tokens/s"
 
     GROUPS, G, PROMPT, GEN, VOCAB = 512, 16, 512, 256, 32000
+    DECODE_MODE = 1  # q, K/V and logits from Philox (the reference has no model)
 
     def __init__(self, args, rank, world, dev):
         import torch
@@ -362,7 +363,8 @@ class RolloutWorkload:
         self.arena = pkg.DeviceArena(self.ng * pages_prompt + priv + 64, device=dev)
         cfg = dict(num_q_heads=32, num_kv_heads=8, vocab=self.VOCAB, max_slots=256,
                    max_context=self.PROMPT + self.GEN, max_new_tokens=self.GEN, max_admit=256,
-                   drop_when_full=0, decode_mode=1, reward_mode=1, reward_seed=5, logit_std=2.0,
+                   drop_when_full=0, decode_mode=self.DECODE_MODE, reward_mode=1, reward_seed=5,
+                   logit_std=2.0,
                    max_prefixes=self.ng, max_prefix_pages=self.ng * pages_prompt,
                    max_passes=1 << 24, idle_timeout_ms=20000, chunk_pages=args.chunk_pages)
         self.eng = pkg.RolloutEngine(cfg, self.arena)
@@ -370,6 +372,7 @@ class RolloutWorkload:
         self.arena.fill_pages(prompt_pages, seed=4 + rank, stream_id=0)  # synthetic prefill (untimed)
         for g in range(self.ng):
             self.eng.set_prefix(g, prompt_pages[g * pages_prompt:(g + 1) * pages_prompt], self.PROMPT)
+        self._attach_model(torch, dev, rank)
         orc_dtype = np.dtype([("request_id", "<u8"), ("max_tokens", "<u4"), ("kv_blocks", "<u4"),
                               ("temperature", "<f4"), ("top_k", "<u2"), ("top_p", "<f4"),
                               ("rng_seed", "<u8")])
@@ -401,6 +404,10 @@ class RolloutWorkload:
         torch.cuda.synchronize()
 
     launches_per_step = None  # counted from the loop's pass counter
+    launches_per_pass = 5
+
+    def _attach_model(self, torch, dev, rank):
+        pass
 
     def _post(self, stream=None):
         if self.nccl:
@@ -425,7 +432,7 @@ class RolloutWorkload:
     def gpu_launches(self, steps):
         # per pass: schedule, prepare, attention, logits, sampler; per step:
         # one allgather (when N > 1) and one advantage kernel
-        return int(self.last_stats["passes"]) * 5 * steps + 2 * steps
+        return int(self.last_stats["passes"]) * self.launches_per_pass * steps + 2 * steps
 
     def e2e(self, steps, warmup):
         """Through the C ABI with host buffers: requests pushed into a mapped
@@ -721,7 +728,7 @@ class LmHeadWorkload:
         c = self.ctypes
         rc = self.pkg.lib().rt_gemm_bf16(c.byref(self.p), c.c_void_p(self.A.data_ptr()),
                                          c.c_void_p(self.W.data_ptr()), c.c_void_p(self.C.data_ptr()),
-                                         c.c_void_p(self.err.data_ptr()),
+                                         None, 0, c.c_void_p(self.err.data_ptr()),
                                          c.c_void_p(self.torch.cuda.current_stream().cuda_stream))
         self.pkg.check(rc, "rt_gemm_bf16")
 
@@ -802,7 +809,81 @@ class LmHeadWorkload:
                 "cublas_bf16_out_ms": round(self.cublas_ms(), 4)}
 
 
-WORKLOADS = {"lm_head": LmHeadWorkload, "rollout": RolloutWorkload, "attention": AttentionWorkload,
+class RolloutModelWorkload(RolloutWorkload):
+    """Config 5 with a model behind the decode step (RT_ROLLOUT_DECODE_MODEL)
+    instead of Philox q / K / V and logits: per pass the slots' last-token
+    embeddings (table 32,000 x 4,096 bf16), the QKV projection (4,096 ->
+    6,144) and the LM head (4,096 -> 32,000) run as tensor-core GEMMs
+    (rt_gemm_bf16) around the same paged attention and sampler.  Weights
+    are seeded N(0, s) bf16 (no checkpoint exists offline): embedding s = 1,
+    QKV 1/64, LM head 0.05."""
+
+    name = "grpo_rollouts_c5_model"
+    metric = "rollout tokens/s (config 5, model decode: QKV + LM-head GEMMs)"
+    DECODE_MODE = 2
+    launches_per_pass = 8  # schedule, embed, QKV GEMM, prepare, attention, hidden, LM GEMM, sampler
+
+    def _attach_model(self, torch, dev, rank):
+        D, NQKV = 32 * 128, (32 + 2 * 8) * 128
+        self.emb = torch.empty(self.VOCAB, D, dtype=torch.bfloat16, device=dev)
+        self.wqkv = torch.empty(NQKV, D, dtype=torch.bfloat16, device=dev)
+        self.wlm = torch.empty(self.VOCAB, D, dtype=torch.bfloat16, device=dev)
+        self.pkg.fill_normal_bf16(self.emb, seed=31 + rank, stream_id=1)
+        self.pkg.fill_normal_bf16(self.wqkv, seed=31 + rank, stream_id=2, std=1.0 / 64)
+        self.pkg.fill_normal_bf16(self.wlm, seed=31 + rank, stream_id=3, std=0.05)
+        self.eng.set_model(self.emb, self.wqkv, self.wlm)
+        self.gemm_flops_per_token = 2.0 * D * (NQKV + self.VOCAB)
+
+    def cpu_sample(self, threads, budget_s=10.0):
+        """The model decode step on the host for one GRPO group (16
+        rollouts, shared 512-token prompt): embedding rows, QKV and LM-head
+        projections (numpy float32 matmul, multithreaded BLAS), paged GQA
+        attention (oracle/oracle.c, OpenMP), the reference sampling
+        algorithm per row, until the budget is spent."""
+        from concurrent.futures import ThreadPoolExecutor
+        orc = ge.load_oracle()
+        B, Hq, Hkv, D = self.G, 32, 8, 32 * 128
+        n_pages = (self.PROMPT + self.GEN + 15) // 16
+        rng = np.random.default_rng(11)
+        arena = rng.standard_normal(B * n_pages * Hkv * 2 * 16 * 128, dtype=np.float32)
+        arena_b = (arena.view(np.uint32) >> 16).astype(np.uint16)
+        pt = np.arange(B * n_pages, dtype=np.int32).reshape(B, n_pages)
+        emb = self.emb.float().cpu().numpy()
+        wqkv = self.wqkv.float().cpu().numpy()
+        wlm = self.wlm.float().cpu().numpy()
+        pool = ThreadPoolExecutor(max_workers=threads)
+        tok = np.zeros(B, dtype=np.int64)
+        t0 = time.perf_counter()
+        steps = 0
+        while steps == 0 or time.perf_counter() - t0 < budget_s:
+            x = emb[tok]
+            qkv = x @ wqkv.T
+            q = (qkv[:, :D].astype(np.float32).view(np.uint32) >> 16).astype(np.uint16)
+            lens = np.full(B, self.PROMPT + steps + 1, dtype=np.int32)
+            o = orc.paged_gqa_attention(q.reshape(B, Hq, 128), arena_b, pt, lens, Hq, Hkv,
+                                        128 ** -0.5, n_threads=threads)
+            logits = (o.reshape(B, D) @ wlm.T).astype(np.float32)
+            tok = np.array(list(pool.map(lambda b: orc.sample_row(
+                logits[b], 0.8, 50, 0.9, orc.sample_u24(1234, b, steps)), range(B))))
+            steps += 1
+            if steps >= self.GEN:
+                break
+        dt = time.perf_counter() - t0
+        pool.shutdown()
+        return {"value": B * steps / dt, "unit": self.unit, "cores": threads, "kind": "port",
+                "seconds": dt,
+                "sample": f"1 group x 16 rollouts, {steps} model decode steps from a 512-token "
+                          f"prompt (embedding, QKV and LM-head matmuls, attention, sampling)"}
+
+    def config(self):
+        return super().config() | {
+            "model": "embedding 32,000 x 4,096, QKV 4,096 -> 6,144, LM head 4,096 -> 32,000; "
+                     "bf16 weights N(0, s), fp32 accumulation",
+            "gemm_flops_per_token": self.gemm_flops_per_token}
+
+
+WORKLOADS = {"lm_head": LmHeadWorkload, "rollout": RolloutWorkload,
+             "rollout_model": RolloutModelWorkload, "attention": AttentionWorkload,
              "sampling": SamplingWorkload, "decode_ring": DecodeRingWorkload}
 
 
@@ -934,7 +1015,7 @@ def run_mine(args):
             "metric": wl.metric, "value": wl.units_per_step() / (ms / 1e3) * world,
             "unit": wl.unit, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "strong" if wl.name == "grpo_rollouts_c5" else "weak",
+            "scaling": "strong" if wl.name.startswith("grpo_rollouts_c5") else "weak",
             "vs_baseline": None, "dtype": getattr(wl, "dtype", "bf16"),
             "data": "synthetic (Philox N(0,1), seeded)",
             "config": wl.config() | {"parallelism": f"replicas{world}" if world > 1 else "single"},
@@ -1003,7 +1084,7 @@ def main():
         prof = wl.kernel_profile(args.ncu_replay)
         print(json.dumps({"ncu_replay": args.ncu_replay, "profile": prof}), flush=True)
         return
-    quick = args.workload != "rollout"   # rollout steps are whole RL steps (~seconds)
+    quick = not args.workload.startswith("rollout")   # rollout steps are whole RL steps (~seconds)
     if args.steps is None:
         args.steps = 200 if quick else 3
     if args.warmup is None:

@@ -245,7 +245,9 @@ _SIGS = {
     "rt_host_decode_pump": (ctypes.c_int64, [_P, _P, ctypes.c_uint32, ctypes.c_uint32, _P, _P,
                                              ctypes.c_uint32, ctypes.c_uint32]),
     "rt_rollout_set_model": (ctypes.c_int, [_P, ctypes.POINTER(rt_model_weights_t)]),
-    "rt_gemm_bf16": (ctypes.c_int, [ctypes.POINTER(rt_gemm_params_t), _P, _P, _P, _P, _P]),
+    "rt_gemm_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(rt_gemm_params_t)]),
+    "rt_gemm_bf16": (ctypes.c_int, [ctypes.POINTER(rt_gemm_params_t), _P, _P, _P, _P,
+                                    ctypes.c_size_t, _P, _P]),
     "ring_create": (_P, []), "ring_destroy": (None, [_P]),
     "comp_ring_create": (_P, []), "comp_ring_destroy": (None, [_P]),
     "req_ring_create": (_P, []), "req_ring_destroy": (None, [_P]),

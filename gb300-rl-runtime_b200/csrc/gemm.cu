@@ -23,13 +23,13 @@
 //            epilogue;
 //   warps 2-9  read the accumulators out of TMEM (tcgen05.ld, one row per
 //            thread, four warps per half) and store C.
-// K-splits of one output tile add into C in split order: split s waits
-// (bounded) for the tile's order counter to reach s, stores (s = 0, unless
-// accumulating) or adds its partial sums with plain loads and stores, and
-// passes the counter on; the last split resets it.  Results are therefore
-// independent of scheduling, and no workspace or atomics are needed.
+// With K-splits every split stores its partial tile into a workspace
+// [split][M][N] in parallel, and a second kernel sums the partials in
+// split order into C: results do not depend on scheduling, and no split
+// waits for another.
 // Every mbarrier wait is bounded; an expired wait sets the error word and
 // the CTA winds down (waiting, bounded, for its own MMAs) and frees its TMEM.
+#include <algorithm>
 #include <cuda_bf16.h>
 #include <stdint.h>
 #include <string.h>
@@ -49,22 +49,23 @@ constexpr uint32_t kAccCols = 256;                   // TMEM columns per accumul
 constexpr uint32_t kTmemCols = 2 * kAccCols;
 constexpr uint32_t kThreads = 320;
 constexpr uint64_t kWaitNs = 2000000000ull;
-constexpr uint32_t kSmemBytes = kStages * kStageBytes + 1024 /* alignment */ + 256 /* barriers */;
-constexpr uint32_t kMaxSplitTiles = 4096;  // output tiles of one split-K call
+constexpr uint32_t kOutBytes = kBM * 32u * 4u;      // one 32-column fp32 slab of a tile
+constexpr uint32_t kSmemBytes = kStages * kStageBytes + kOutBytes + 1024 /* alignment */ +
+                                256 /* barriers */;
 
-// Per-tile split order counters (zero at load, reset by each tile's last split).
-__device__ uint32_t g_split_order[kMaxSplitTiles];
 
 static_assert(kABytes % 1024 == 0 && kBBytes % 1024 == 0, "stage buffers stay 1024-byte aligned");
 static_assert(kBN % 16 == 0 && kBN <= 256 && kBN <= kAccCols, "UMMA N for M = 128");
 
 struct GemmArgs {
     float *C;
+    float *ws;  // K-split partials [splits][m_tiles * 256][N] (splits > 1)
     uint32_t M, N, K, ldc;
+    uint32_t tma_out;  // 1: the output goes out through map_c (TMA tensor stores)
     uint32_t m_tiles, n_tiles, splits, kb_per_split, kb_total;
     uint32_t units;
     uint32_t accumulate;  // 1: add into C (K-splits always add)
-    uint32_t vec_ok;      // C rows allow 16-byte stores
+    uint32_t vec_ok;      // the output rows allow 16-byte stores
     int32_t *error;
 };
 
@@ -87,18 +88,6 @@ __device__ __forceinline__ void unit_coords(const GemmArgs &g, uint32_t u, uint3
     n0 = (t / g.m_tiles) * kBN;
     kb0 = split * g.kb_per_split;
     kb1 = min(kb0 + g.kb_per_split, g.kb_total);
-}
-
-__device__ __forceinline__ uint32_t ld_acquire(const uint32_t *p)
-{
-    uint32_t v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
-__device__ __forceinline__ void st_release(uint32_t *p, uint32_t v)
-{
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 // Barrier of the 256 epilogue threads (warps 2-9) only.
@@ -125,14 +114,35 @@ __device__ __forceinline__ bool wait_or_abort(Shared *sh, uint32_t bar, uint32_t
     return true;
 }
 
+// TMA tensor store / reduce-add of a shared-memory box (bulk-group completion).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, uint32_t src, int32_t x,
+                                             int32_t y, bool add)
+{
+    if (add)
+        asm volatile(
+            "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                map),
+            "r"(x), "r"(y), "r"(src)
+            : "memory");
+    else
+        asm volatile(
+            "cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                map),
+            "r"(x), "r"(y), "r"(src)
+            : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap map_a,
-                        const __grid_constant__ CUtensorMap map_b, const GemmArgs g)
+                        const __grid_constant__ CUtensorMap map_b,
+                        const __grid_constant__ CUtensorMap map_c, const GemmArgs g)
 {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~uintptr_t(1023u));
-    Shared *sh = reinterpret_cast<Shared *>(smem + kStages * kStageBytes);
+    uint8_t *out_buf = smem + kStages * kStageBytes;  // 1024-aligned, 128-byte swizzled rows
+    Shared *sh = reinterpret_cast<Shared *>(out_buf + kOutBytes);
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t smem_base = rt::smem_u32(smem);
 
@@ -234,7 +244,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (uint32_t u = blockIdx.x; u < g.units; u += gridDim.x) {
             uint32_t m0, n0, kb0, kb1;
             unit_coords(g, u, m0, n0, kb0, kb1);
-            const uint32_t split = u % g.splits, tile = u / g.splits;
+            const uint32_t split = u % g.splits;
             // Exits are decided uniformly by all 256 epilogue threads (the
             // TMEM loads are warp-collective and the named barriers need
             // every epilogue warp): one lane per warp waits, the outcomes
@@ -242,19 +252,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = true;
             if (lane == 0u)
                 ok = wait_or_abort(sh, rt::smem_u32(&sh->acc_full), acc_phase, g);
-            if (ok && g.splits > 1u && warp == 2u && lane == 0u) {
-                // this split's turn on the tile (its predecessor is unit u - 1)
-                const uint64_t t0 = rt::globaltimer_ns();
-                while (ld_acquire(&g_split_order[tile]) != split) {
-                    if (*(volatile uint32_t *)&sh->abort || rt::globaltimer_ns() - t0 > kWaitNs) {
-                        atomicCAS(g.error, 0, 2);
-                        *(volatile uint32_t *)&sh->abort = 1u;
-                        ok = false;
-                        break;
-                    }
-                    __nanosleep(64);
-                }
-            }
             if (lane == 0u)
                 sh->ep_ok[warp - 2u] = ok ? 1u : 0u;
             epilogue_sync();
@@ -266,8 +263,37 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             rt::tc_fence_after_sync();
             const uint32_t m = m0 + row;
-            float *crow = g.C + (uint64_t)m * g.ldc;
-            const bool add = g.accumulate || split > 0u;
+            // a K-split stores its partial tile into its workspace slice
+            const uint32_t m_pad = g.m_tiles * kBM;
+            float *crow = g.splits > 1u ? g.ws + ((uint64_t)split * m_pad + m) * g.N
+                                        : g.C + (uint64_t)m * g.ldc;
+            const bool add = g.accumulate && g.splits == 1u;
+            if (g.tma_out) {
+                // 32-column slabs: each thread writes its row into the
+                // swizzled buffer, one thread stores the 256 x 32 box
+                const uint32_t y = g.splits > 1u ? split * m_pad + m0 : m0;
+                uint8_t *my_row = out_buf + row * 128u;
+#pragma unroll 1
+                for (uint32_t c = 0; c < kBN; c += 32u) {
+                    uint32_t r[32];
+                    rt::tmem_ld32(tmem + half * kAccCols + ((quarter * 32u) << 16) + c, r);
+                    rt::tmem_ld_wait();
+#pragma unroll
+                    for (uint32_t j = 0; j < 8u; j++)
+                        *reinterpret_cast<uint4 *>(my_row + ((j ^ (row & 7u)) << 4)) =
+                            make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+                    rt::fence_proxy_async_smem();
+                    epilogue_sync();
+                    if (warp == 2u && lane == 0u) {
+                        if (n0 + c < g.N)
+                            tma_store_2d(&map_c, rt::smem_u32(out_buf), (int32_t)(n0 + c),
+                                         (int32_t)y, add);
+                        // the buffer is reused by the next slab
+                        asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+                    }
+                    epilogue_sync();
+                }
+            } else
 #pragma unroll 1
             for (uint32_t c = 0; c < kBN; c += 32u) {
                 uint32_t r[32];
@@ -302,20 +328,57 @@ __global__ void __launch_bounds__(kThreads, 1)
             rt::tc_fence_before_sync();
             rt::mbar_arrive(rt::smem_u32(&sh->acc_empty));
             acc_phase ^= 1u;
-            // every row of the unit is stored (and ep_ok may be rewritten)
-            __threadfence();
+            // every warp has read ep_ok before it is rewritten for the next unit
             epilogue_sync();
-            if (g.splits > 1u && warp == 2u && lane == 0u)
-                st_release(&g_split_order[tile], split + 1u == g.splits ? 0u : split + 1u);
         }
     }
 
-    // wind down: every MMA this CTA issued has completed before TMEM is freed
+    // wind down: every MMA this CTA issued has completed before TMEM is
+    // freed, and every tensor store has completed before the CTA exits
+    if (warp == 2u && lane == 0u)
+        asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     rt::tc_fence_before_sync();
     __syncthreads();
     if (warp == 1) {
         rt::tc_fence_after_sync();
         rt::tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// C = (C if accumulating) + sum over splits of the partials, in split order.
+__global__ void __launch_bounds__(256) split_reduce_kernel(float *C, uint32_t ldc,
+                                                           const float *ws, uint32_t M,
+                                                           uint32_t N, uint32_t splits,
+                                                           uint32_t accumulate, uint32_t m_pad)
+{
+    const uint64_t MN = (uint64_t)M * N;
+    const uint64_t slice = (uint64_t)m_pad * N;  // one split's partials (rows padded to tiles)
+    if ((N & 3u) == 0u && (ldc & 3u) == 0u && ((uintptr_t)C & 15u) == 0u) {
+        const uint64_t n4 = MN / 4u;
+        for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n4;
+             i += (uint64_t)gridDim.x * blockDim.x) {
+            const uint64_t e = i * 4u, m = e / N, n = e % N;
+            float4 v = __ldcg(reinterpret_cast<const float4 *>(ws) + i);
+            for (uint32_t sp = 1; sp < splits; sp++) {
+                const float4 w = __ldcg(reinterpret_cast<const float4 *>(ws + sp * slice) + i);
+                v = make_float4(v.x + w.x, v.y + w.y, v.z + w.z, v.w + w.w);
+            }
+            float4 *dst = reinterpret_cast<float4 *>(C + m * ldc + n);
+            if (accumulate) {
+                const float4 c = *dst;
+                v = make_float4(c.x + v.x, c.y + v.y, c.z + v.z, c.w + v.w);
+            }
+            *dst = v;
+        }
+        return;
+    }
+    for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < MN;
+         e += (uint64_t)gridDim.x * blockDim.x) {
+        float v = ws[e];
+        for (uint32_t sp = 1; sp < splits; sp++)
+            v += ws[sp * slice + e];
+        float *dst = C + (e / N) * ldc + e % N;
+        *dst = accumulate ? *dst + v : v;
     }
 }
 
@@ -355,8 +418,26 @@ int gemm_prepare()
 }
 }  // namespace rt
 
+// K-splits the call will use (after clamping to the K-slices).
+static uint32_t effective_splits(const rt_gemm_params_t *p)
+{
+    const uint32_t kb_total = p->K / kBK;
+    const uint32_t splits = p->split_k ? std::min(p->split_k, kb_total) : 1u;
+    const uint32_t per = (kb_total + splits - 1) / splits;
+    return (kb_total + per - 1) / per;
+}
+
+extern "C" size_t rt_gemm_workspace_bytes(const rt_gemm_params_t *p)
+{
+    if (!p || p->K == 0 || p->K % kBK)
+        return 0;
+    const uint32_t splits = effective_splits(p);
+    const size_t m_pad = (size_t)((p->M + kBM - 1) / kBM) * kBM;
+    return splits > 1u ? (size_t)splits * m_pad * p->N * sizeof(float) : 0u;
+}
+
 extern "C" int rt_gemm_bf16(const rt_gemm_params_t *p, const void *A, const void *B, float *C,
-                            int32_t *error, void *stream)
+                            void *workspace, size_t workspace_bytes, int32_t *error, void *stream)
 {
     if (!p || !A || !B || !C || !error) {
         rt::set_error("gemm_bf16: null argument");
@@ -390,22 +471,53 @@ extern "C" int rt_gemm_bf16(const rt_gemm_params_t *p, const void *A, const void
     const uint32_t splits = p->split_k ? min(p->split_k, g.kb_total) : 1u;
     g.kb_per_split = (g.kb_total + splits - 1) / splits;
     g.splits = (g.kb_total + g.kb_per_split - 1) / g.kb_per_split;  // no empty split
+    if (g.splits > 1u) {
+        const size_t need = (size_t)g.splits * g.m_tiles * kBM * p->N * sizeof(float);
+        if (!workspace || workspace_bytes < need || ((uintptr_t)workspace % 16u)) {
+            rt::set_error("gemm_bf16: %u K-splits need a 16-byte aligned workspace of %zu bytes",
+                          g.splits, need);
+            return RT_ENOMEM;
+        }
+        g.ws = static_cast<float *>(workspace);
+    }
     g.units = g.m_tiles * g.n_tiles * g.splits;
     g.accumulate = p->flags & RT_GEMM_ACCUMULATE;
     g.error = error;
-    g.vec_ok = ((uintptr_t)C % 16u) == 0u && (p->ldc % 4u) == 0u;
+    g.vec_ok = g.splits > 1u ? (p->N % 4u) == 0u
+                             : ((uintptr_t)C % 16u) == 0u && (p->ldc % 4u) == 0u;
+    // TMA stores need 16-byte aligned rows; otherwise plain stores
+    CUtensorMap mc;
+    memset(&mc, 0, sizeof(mc));
+    g.tma_out = 0u;
+    if (g.vec_ok) {
+        const int rc3 = g.splits > 1u
+                            ? rt::encode_f32_store_map(&mc, g.ws, p->N, (uint64_t)g.splits * g.m_tiles * kBM,
+                                                       (uint64_t)p->N * 4u, kBM)
+                            : rt::encode_f32_store_map(&mc, C, p->N, p->M, (uint64_t)p->ldc * 4u, kBM);
+        if (rc3 != RT_OK)
+            return rc3;
+        g.tma_out = 1u;
+    }
     cudaStream_t s = (cudaStream_t)stream;
     cudaError_t err;
-    if (g.splits > 1u && g.m_tiles * g.n_tiles > kMaxSplitTiles) {
-        rt::set_error("gemm_bf16: split-K over more than %u output tiles", kMaxSplitTiles);
-        return RT_EINVAL;
-    }
     int sms = 0;
     int rc2 = gemm_setup(&sms);
     if (rc2 != RT_OK)
         return rc2;
     const uint32_t grid = min(g.units, (uint32_t)sms);
-    gemm_bf16_tn_kernel<<<grid, kThreads, kSmemBytes, s>>>(ma, mb, g);
+    gemm_bf16_tn_kernel<<<grid, kThreads, kSmemBytes, s>>>(ma, mb, mc, g);
     err = cudaGetLastError();
-    return err == cudaSuccess ? RT_OK : rt::cuda_fail(err, "gemm_bf16: launch");
+    if (err != cudaSuccess)
+        return rt::cuda_fail(err, "gemm_bf16: launch");
+    if (g.splits > 1u) {
+        const uint64_t work = (uint64_t)p->M * p->N / 4u;
+        const uint32_t blocks = (uint32_t)std::min<uint64_t>((work + 255u) / 256u, 4u * (uint64_t)sms);
+        split_reduce_kernel<<<std::max(blocks, 1u), 256, 0, s>>>(C, p->ldc, g.ws, p->M, p->N,
+                                                                 g.splits, g.accumulate,
+                                                                 g.m_tiles * kBM);
+        err = cudaGetLastError();
+        if (err != cudaSuccess)
+            return rt::cuda_fail(err, "gemm_bf16: split reduction launch");
+    }
+    return RT_OK;
 }

@@ -105,6 +105,9 @@ struct Dev {
     uint32_t *emb_tok;          // [max_slots] token embedded this pass
     int32_t *gemm_err;          // projection kernels' error word
     uint32_t dm, qkv_n;
+    float *gemm_ws;             // K-split partials of the projections
+    uint64_t gemm_ws_bytes;
+    uint32_t split_qkv, split_lm;
 };
 
 __device__ __forceinline__ float reward_for(const Dev &d, uint32_t request_lo, uint32_t tokens)
@@ -889,9 +892,8 @@ int launch_decode_model(rt_rollout *e, cudaStream_t st, cudaEvent_t *ev)
     cudaError_t err = launch_pdl(embed_kernel, dim3(d.max_slots), dim3(256), st, d);
     if (err != cudaSuccess)
         return rt::cuda_fail(err, "rollout: embed launch");
-    rt_gemm_params_t gq = {d.max_slots, d.qkv_n, d.dm, d.dm, d.dm, d.qkv_n,
-                           gemm_splits(d.max_slots, d.qkv_n, d.dm), 0u};
-    int rc = rt_gemm_bf16(&gq, d.hin, d.w_qkv, d.qkv, d.gemm_err, st);
+    rt_gemm_params_t gq = {d.max_slots, d.qkv_n, d.dm, d.dm, d.dm, d.qkv_n, d.split_qkv, 0u};
+    int rc = rt_gemm_bf16(&gq, d.hin, d.w_qkv, d.qkv, d.gemm_ws, d.gemm_ws_bytes, d.gemm_err, st);
     if (rc != RT_OK)
         return rc;
     err = launch_pdl(model_prepare_kernel, dim3(d.max_slots), dim3(256), st, d);
@@ -912,9 +914,8 @@ int launch_decode_model(rt_rollout *e, cudaStream_t st, cudaEvent_t *ev)
     err = launch_pdl(hidden_kernel, dim3(d.max_slots), dim3(256), st, d);
     if (err != cudaSuccess)
         return rt::cuda_fail(err, "rollout: hidden launch");
-    rt_gemm_params_t gl = {d.max_slots, d.vocab, d.dm, d.dm, d.dm, d.vocab,
-                           gemm_splits(d.max_slots, d.vocab, d.dm), 0u};
-    rc = rt_gemm_bf16(&gl, d.hout, d.w_lm, d.logits, d.gemm_err, st);
+    rt_gemm_params_t gl = {d.max_slots, d.vocab, d.dm, d.dm, d.dm, d.vocab, d.split_lm, 0u};
+    rc = rt_gemm_bf16(&gl, d.hout, d.w_lm, d.logits, d.gemm_ws, d.gemm_ws_bytes, d.gemm_err, st);
     if (rc != RT_OK)
         return rc;
     if (ev)
@@ -1028,7 +1029,7 @@ void engine_free(rt_rollout *e)
                     e->d.enable, e->d.srows, e->d.tokens, e->d.q, e->d.attn_out, e->d.logits,
                     e->d.pf_len, e->d.pf_np, e->d.pf_off, e->d.pf_pages, e->d.groups,
                     e->d.n_groups, e->d.skip, e->attn_ws, e->d.hin, e->d.hout, e->d.qkv,
-                    e->d.emb_tok, e->d.gemm_err};
+                    e->d.emb_tok, e->d.gemm_err, e->d.gemm_ws};
     for (void *p : bufs)
         if (p)
             cudaFree(p);
@@ -1237,6 +1238,21 @@ extern "C" int rt_rollout_set_model(rt_rollout_t *e, const rt_model_weights_t *w
         ok(cudaMemset(d.gemm_err, 0, sizeof(int32_t)));
         if (err != cudaSuccess)
             return rt::cuda_fail(err, "rollout_set_model: buffers");
+    }
+    // K-splits that fill the GPU, and their shared partial-sum workspace
+    d.split_qkv = gemm_splits(S, d.qkv_n, d.dm);
+    d.split_lm = gemm_splits(S, d.vocab, d.dm);
+    rt_gemm_params_t gq = {S, d.qkv_n, d.dm, d.dm, d.dm, d.qkv_n, d.split_qkv, 0u};
+    rt_gemm_params_t gl = {S, d.vocab, d.dm, d.dm, d.dm, d.vocab, d.split_lm, 0u};
+    const uint64_t need = std::max(rt_gemm_workspace_bytes(&gq), rt_gemm_workspace_bytes(&gl));
+    if (need > d.gemm_ws_bytes) {
+        if (d.gemm_ws)
+            cudaFree(d.gemm_ws);
+        d.gemm_ws = nullptr;
+        d.gemm_ws_bytes = 0;
+        if ((err = cudaMalloc(&d.gemm_ws, need)) != cudaSuccess)
+            return rt::cuda_fail(err, "rollout_set_model: projection workspace");
+        d.gemm_ws_bytes = need;
     }
     d.w_embed = static_cast<const __nv_bfloat16 *>(w->embed);
     d.w_qkv = static_cast<const __nv_bfloat16 *>(w->w_qkv);

@@ -360,5 +360,10 @@ int encode_kv_rows_map(CUtensorMap *map, const void *base, uint64_t rows);
 // operand tile of a tcgen05 MMA.  Out-of-range rows and columns read zero.
 int encode_bf16_kmajor_map(CUtensorMap *map, const void *base, uint64_t k, uint64_t rows,
                            uint64_t row_stride_bytes, uint32_t box_rows);
+// 2-D map over a row-major fp32 matrix [rows][cols] for TMA stores: box of
+// 32 columns (128 bytes) x box_rows rows, 128-byte swizzle.  Stores are
+// clipped at the matrix edge.
+int encode_f32_store_map(CUtensorMap *map, const void *base, uint64_t cols, uint64_t rows,
+                         uint64_t row_stride_bytes, uint32_t box_rows);
 
 }  // namespace rt

@@ -115,6 +115,34 @@ int encode_bf16_kmajor_map(CUtensorMap *map, const void *base, uint64_t k, uint6
     return RT_OK;
 }
 
+int encode_f32_store_map(CUtensorMap *map, const void *base, uint64_t cols, uint64_t rows,
+                         uint64_t row_stride_bytes, uint32_t box_rows)
+{
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) {
+        set_error("cuTensorMapEncodeTiled unavailable from the driver");
+        return RT_ECUDA;
+    }
+    if (((uintptr_t)base & 15u) != 0u || (row_stride_bytes & 15u) != 0u || cols == 0 ||
+        rows == 0 || box_rows == 0 || box_rows > 256u) {
+        set_error("fp32 output: base and row stride must be 16-byte aligned, box rows 1..256");
+        return RT_EINVAL;
+    }
+    cuuint64_t gdim[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t gstride[1] = {(cuuint64_t)row_stride_bytes};
+    cuuint32_t box[2] = {32u, box_rows};
+    cuuint32_t estride[2] = {1u, 1u};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void *>(base), gdim,
+                    gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("cuTensorMapEncodeTiled failed (CUresult %d)", (int)r);
+        return RT_ECUDA;
+    }
+    return RT_OK;
+}
+
 }  // namespace rt
 
 // ------------------------------------------------------------ fill kernels

@@ -498,9 +498,11 @@ int64_t rt_host_decode_pump(CommandRing *ring, const Descriptor *descs, uint32_t
  * A bf16 [M][lda] (activations, K contiguous), B bf16 [N][ldb] (a weight
  * stored [out][in], K contiguous), C fp32 [M][ldc]; fp32 accumulation.
  * K a multiple of 64; lda, ldb multiples of 8 elements; A, B 16-byte
- * aligned.  split_k > 1 divides K among CTAs that add into C (C is zeroed
- * first unless RT_GEMM_ACCUMULATE).  `error` is a device int32 set to 1 if
- * a bounded wait inside the kernel expired (never expected).
+ * aligned.  split_k > 1 divides K among CTAs: each stores its partial
+ * sums into `workspace` (rt_gemm_workspace_bytes, 16-byte aligned) and a
+ * second kernel adds them into C in split order, so results are
+ * deterministic.  `error` is a device int32 set to 1 if a bounded wait
+ * inside the kernel expired (never expected).
  * ---------------------------------------------------------------------- */
 #define RT_GEMM_ACCUMULATE 1u
 
@@ -511,8 +513,9 @@ typedef struct {
     uint32_t flags;          /* RT_GEMM_ACCUMULATE */
 } rt_gemm_params_t;
 
+size_t rt_gemm_workspace_bytes(const rt_gemm_params_t *p);  /* 0 without K-splits */
 int rt_gemm_bf16(const rt_gemm_params_t *p, const void *A, const void *B, float *C,
-                 int32_t *error, void *stream);
+                 void *workspace, size_t workspace_bytes, int32_t *error, void *stream);
 
 /* ------------------------------------------------------------------------
  * Rewards and group-normalised advantages (new; the reference has only the

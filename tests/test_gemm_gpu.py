@@ -22,8 +22,11 @@ def gemm(pkg, A, B, C=None, split_k=0, accumulate=False, ldc=None):
     p = pkg.rt_gemm_params_t(M, N, K, A.stride(0), B.stride(0), C.stride(0), split_k,
                              1 if accumulate else 0)
     err = torch.zeros(1, dtype=torch.int32, device=A.device)
+    wsb = pkg.lib().rt_gemm_workspace_bytes(ctypes.byref(p))
+    ws = torch.full((max(wsb, 4) // 4,), float("nan"), device=A.device) if wsb else None
     pkg.check(pkg.lib().rt_gemm_bf16(ctypes.byref(p), pkg._ptr(A), pkg._ptr(B), pkg._ptr(C),
-                                     pkg._ptr(err), pkg._stream_ptr(None)), "rt_gemm_bf16")
+                                     pkg._ptr(ws), wsb, pkg._ptr(err), pkg._stream_ptr(None)),
+              "rt_gemm_bf16")
     torch.cuda.synchronize()
     assert int(err.item()) == 0
     return C
@@ -83,6 +86,13 @@ def test_gemm_rejects_bad_shapes(pkg, cuda):
     A, B = rand((8, 100), 9, cuda), rand((8, 100), 10, cuda)
     with pytest.raises(pkg.RuntimeErrorRT, match="multiple of 64"):
         gemm(pkg, A, B)
+    A, B = rand((8, 128), 9, cuda), rand((8, 128), 10, cuda)
+    p = pkg.rt_gemm_params_t(8, 8, 128, 128, 128, 8, 2, 0)
+    C = torch.empty(8, 8, device=cuda)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    rc = pkg.lib().rt_gemm_bf16(ctypes.byref(p), pkg._ptr(A), pkg._ptr(B), pkg._ptr(C), None, 0,
+                                pkg._ptr(err), pkg._stream_ptr(None))
+    assert rc == pkg.RT_ENOMEM
 
 
 def test_gemm_split_k_is_deterministic(pkg, cuda):
