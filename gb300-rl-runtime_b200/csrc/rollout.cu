@@ -121,31 +121,7 @@ __device__ __forceinline__ float reward_for(const Dev &d, uint32_t request_lo, u
     return reward_score_mock_inline(tokens);
 }
 
-// ---- request source / done sink (thread 0 only) ----
-__device__ bool src_peek(const RtIo &io, const RtCtl *ctl, RolloutRequest *out)
-{
-    if (io.ring) {
-        const uint32_t head = rt_load_relaxed_u32(&io.ring->cons.head);
-        const uint32_t tail = rt_load_acquire_u32(&io.ring->prod.tail);
-        if (head == tail)
-            return false;
-        rt_copy_bytes(out, &io.ring->slots[head & (REQUEST_RING_SIZE - 1)], sizeof(RolloutRequest));
-        return true;
-    }
-    if (ctl->consumed + ctl->sentinel >= io.n_reqs)
-        return false;
-    rt_copy_bytes(out, &io.reqs[ctl->consumed + ctl->sentinel], sizeof(RolloutRequest));
-    return true;
-}
-
-__device__ void src_pop(const RtIo &io)
-{
-    if (io.ring) {
-        const uint32_t head = rt_load_relaxed_u32(&io.ring->cons.head);
-        rt_store_release_u32(&io.ring->cons.head, head + 1u);
-    }
-}
-
+// ---- request source / done sink (thread 0 only; admission reads ahead) ----
 __device__ bool src_empty(const RtIo &io, const RtCtl *ctl)
 {
     if (io.ring)
@@ -175,6 +151,73 @@ __device__ bool sink_push(const RtIo &io, RtCtl *ctl, const RolloutDone &rec)
 
 constexpr uint32_t kKeyTable = 1024;  // prefix ids grouped through a table (else a slot scan)
 
+__device__ __forceinline__ uint32_t ld_sys_u32(const void *p)
+{
+    uint32_t v;
+    asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ uint16_t ld_sys_u16(const void *p)
+{
+    uint16_t v;
+    asm volatile("ld.relaxed.sys.global.u16 %0, [%1];" : "=h"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_sys_u64(void *p, uint64_t v)
+{
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// One 34-byte ring record (2-byte aligned) from host memory into shared
+// memory: nine independent loads in flight together, not 34 serial ones.
+__device__ __forceinline__ void load_request(const RolloutRequest *src, RolloutRequest *dst)
+{
+    const uint8_t *a = reinterpret_cast<const uint8_t *>(src);
+    uint16_t *o = reinterpret_cast<uint16_t *>(dst);
+    const uint32_t lead = (reinterpret_cast<uintptr_t>(a) & 3u) ? 1u : 0u;  // u16 before the words
+    uint32_t w[8];
+    uint16_t edge;
+    if (lead) {
+        edge = ld_sys_u16(a);
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+            w[i] = ld_sys_u32(a + 2 + 4 * i);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+            w[i] = ld_sys_u32(a + 4 * i);
+        edge = ld_sys_u16(a + 32);
+    }
+    uint32_t k = 0;
+    if (lead)
+        o[k++] = edge;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        o[k++] = (uint16_t)(w[i] & 0xFFFFu);
+        o[k++] = (uint16_t)(w[i] >> 16);
+    }
+    if (!lead)
+        o[k] = edge;
+}
+
+__device__ __forceinline__ uint32_t free_slot_count(const uint64_t *bitmap, uint32_t max_slots)
+{
+    uint32_t n = 0;
+    for (uint32_t w = 0; w < (GPU_MAX_ROLLOUTS + 63) / 64; w++) {
+        const uint32_t lo = w * 64u;
+        if (lo >= max_slots)
+            break;
+        uint64_t free_bits = ~bitmap[w];
+        if (max_slots - lo < 64u)
+            free_bits &= (1ull << (max_slots - lo)) - 1ull;
+        n += (uint32_t)__popcll(free_bits);
+    }
+    return n;
+}
+
+
 // Shared-memory copy of the loop state one schedule pass works on: loaded
 // in two parallel round trips at the start of a pass, stored back at its
 // end, so that the pass's serial steps (admission, retirement, loop
@@ -185,14 +228,58 @@ struct SchedShared {
     uint64_t bitmap[(GPU_MAX_ROLLOUTS + 63) / 64];
     RtCtl ctl;
     RtIo io;
-    uint32_t fin[kSched];
-    uint32_t fin_tokens[kSched];
-    uint32_t fin_req[kSched];
-    uint32_t key[kSched];          // grouping key per slot (prefix id + 1, 0 = none)
-    uint32_t rank[kSched];         // rank among the active slots with the same key
-    uint32_t kcount[kKeyTable];    // per key: slot count, then first group id
+    union {
+        // admission: requests read ahead from a RequestRing in one round trip
+        RolloutRequest rq_buf[kSched];
+        // retirement and grouping (after admission)
+        struct {
+            uint32_t fin[kSched];
+            uint32_t fin_tokens[kSched];
+            uint32_t fin_req[kSched];
+            uint32_t key[kSched];        // grouping key per slot (prefix id + 1, 0 = none)
+            uint32_t rank[kSched];       // rank among the active slots with the same key
+            uint32_t kcount[kKeyTable];  // per key: slot count, then first group id
+        };
+    };
+    uint32_t rq_head, rq_n;        // ring head at the start of admission, records read ahead
     uint32_t stop, n_fin;
 };
+
+// Admission, first part (all kSched threads): the records this pass can
+// take, read ahead in one parallel round trip (nine loads per record, all
+// in flight) from the RequestRing (head and tail read once) or the request
+// array.  With backpressure and no free slot nothing can be admitted, and
+// the source is not touched at all.
+__device__ void prefetch_requests(const Dev &d, SchedShared &sh)
+{
+    const RtIo &io = sh.io;
+    if (threadIdx.x == 0) {
+        uint32_t n = 0, head;
+        const uint32_t free_n = free_slot_count(sh.bitmap, d.max_slots);
+        const bool can = d.drop || free_n > 0u;
+        if (io.ring) {
+            head = rt_load_relaxed_u32(&io.ring->cons.head);
+            if (can)
+                n = rt_load_acquire_u32(&io.ring->prod.tail) - head;
+        } else {
+            head = sh.ctl.consumed + sh.ctl.sentinel;
+            n = can && head < io.n_reqs ? io.n_reqs - head : 0u;
+        }
+        n = min(n, min(d.max_admit, kSched));
+        if (!d.drop)
+            n = min(n, free_n + 1u);  // + 1: a stop sentinel right behind them
+        sh.rq_head = head;
+        sh.rq_n = n;
+    }
+    __syncthreads();
+    if (threadIdx.x < sh.rq_n) {
+        const RolloutRequest *src =
+            io.ring ? &io.ring->slots[(sh.rq_head + threadIdx.x) & (REQUEST_RING_SIZE - 1)]
+                    : &io.reqs[sh.rq_head + threadIdx.x];
+        load_request(src, &sh.rq_buf[threadIdx.x]);
+    }
+    __syncthreads();
+}
 
 __device__ __forceinline__ void copy_words(void *dst, const void *src, size_t bytes)
 {
@@ -413,14 +500,18 @@ __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
     if (s == 0)
         ctl->tokens += n_commit;
 
-    // 2. admission, in source order, lowest free slot first
+    // 2. admission, in source order, lowest free slot first.  The source is
+    //    read ahead (prefetch_requests); a ring's head is released once.
+    prefetch_requests(d, sh);
     if (s == 0) {
+        uint32_t taken = 0;  // source records consumed this pass
         for (uint32_t a = 0; a < d.max_admit; a++) {
-            RolloutRequest rq;
-            if (!src_peek(io, ctl, &rq))
+            // the read-ahead covers every record this pass can take
+            if (taken >= sh.rq_n)
                 break;
+            const RolloutRequest rq = sh.rq_buf[taken];
             if (rq.request_id == RT_REQUEST_SENTINEL) {
-                src_pop(io);
+                taken++;
                 ctl->sentinel = 1u;
                 sh.stop = 1u;
                 break;
@@ -429,12 +520,12 @@ __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
             if (slot < 0) {
                 if (!d.drop)
                     break;              // backpressure: leave it queued
-                src_pop(io);            // reference: consumed and lost
+                taken++;                // reference: consumed and lost
                 ctl->consumed++;
                 ctl->dropped++;
                 continue;
             }
-            src_pop(io);
+            taken++;
             const uint32_t row = ctl->consumed++;
             ctl->admitted++;
             ctl->groups_ok = 0u;
@@ -490,6 +581,8 @@ __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
                     pt[i] = priv[next++];
             }
         }
+        if (io.ring && taken)
+            rt_store_release_u32(&io.ring->cons.head, sh.rq_head + taken);
     }
     __syncthreads();
     if (sh.stop)
@@ -510,6 +603,14 @@ __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
     if (n_fin && s == 0)
         ctl->groups_ok = 0u;
     if (n_fin && s == 0) {
+        // a DoneRing takes the batch with one head read and one tail release
+        // while it has room (done_ring_push per record otherwise)
+        uint32_t dn_tail = 0, dn_room = 0, dn_pushed = 0;
+        if (io.done_ring) {
+            const uint32_t head = rt_load_acquire_u32(&io.done_ring->cons.head);
+            dn_tail = rt_load_relaxed_u32(&io.done_ring->prod.tail);
+            dn_room = (uint32_t)REQUEST_RING_SIZE - (dn_tail - head);
+        }
         for (uint32_t k = 0; k < d.max_slots; k++) {
             if (!sh.fin[k])
                 continue;
@@ -519,6 +620,23 @@ __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
             rec.tokens_generated = sh.fin_tokens[k];
             rec.reward = reward_for(d, sh.fin_req[k], sh.fin_tokens[k]);
             rec.status = 0u;
+            if (io.done_ring && dn_room) {
+                uint64_t *dst = reinterpret_cast<uint64_t *>(
+                    &io.done_ring->slots[(dn_tail + dn_pushed) & (REQUEST_RING_SIZE - 1)]);
+                const uint64_t *src = reinterpret_cast<const uint64_t *>(&rec);
+                st_sys_u64(dst, src[0]);
+                st_sys_u64(dst + 1, src[1]);
+                st_sys_u64(dst + 2, src[2]);
+                dn_pushed++;
+                dn_room--;
+                ctl->done++;
+                continue;
+            }
+            if (dn_pushed) {  // publish the batch before the slow path
+                rt_store_release_u32(&io.done_ring->prod.tail, dn_tail + dn_pushed);
+                dn_tail += dn_pushed;
+                dn_pushed = 0;
+            }
             if (!sink_push(io, ctl, rec)) {
                 ctl->error = RT_ETIMEOUT;
                 sh.stop = 1u;
@@ -526,6 +644,8 @@ __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
             }
             ctl->done++;
         }
+        if (dn_pushed)
+            rt_store_release_u32(&io.done_ring->prod.tail, dn_tail + dn_pushed);
         if (io.step_count)
             atomicAdd(io.step_count, (unsigned long long)n_fin);
     }
