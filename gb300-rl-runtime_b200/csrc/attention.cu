@@ -43,8 +43,15 @@
 
 namespace {
 
+#ifndef RT_ATTN_STAGES
+#define RT_ATTN_STAGES 2
+#endif
+#ifndef RT_ATTN_CTAS_PER_SM
+#define RT_ATTN_CTAS_PER_SM 3
+#endif
 constexpr int kWarps = 4;            // warps (independent items) per CTA
-constexpr int kStages = 3;           // pipeline depth per warp
+constexpr int kStages = RT_ATTN_STAGES;          // pipeline depth per warp
+constexpr int kCtasPerSm = RT_ATTN_CTAS_PER_SM;  // resident CTAs per SM (shared memory)
 constexpr int kStageBytes = 8192;    // K (2 x 2 KiB halves) + V (2 x 2 KiB)
 constexpr int kMaxChunkPages = 64;   // page ids live in two registers per lane
 constexpr int kSmemBytes = kWarps * kStages * kStageBytes + 1024;  // + 1 KiB alignment slack
@@ -755,7 +762,7 @@ __device__ __forceinline__ bool process_group_item(const CUtensorMap &kv_map, co
 // (group, row block, head, chunk) items from a dispenser; the last CTA out
 // resets it for the next launch.
 template <int G>
-__global__ void __launch_bounds__(kWarps * 32, 2)
+__global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
 paged_gqa_group_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnArgs a)
 {
     extern __shared__ uint8_t smem_raw[];
@@ -816,7 +823,7 @@ paged_gqa_group_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnArg
 // items of a GRPO group's sequences run side by side.  The last warp to
 // leave resets the dispenser for the next launch.
 template <int G>
-__global__ void __launch_bounds__(kWarps * 32, 2)
+__global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
 paged_gqa_decode_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnArgs a)
 {
     extern __shared__ uint8_t smem_raw[];
@@ -912,7 +919,7 @@ int make_plan(const rt_attn_params_t *p, Plan *pl, const rt_attn_group_params_t 
         // the ragged config-2 batch and the rollout loop); smaller when there
         // are too few items to give every warp slot of the GPU several.
         cp = 48;
-        const uint64_t warp_slots = (uint64_t)rt::num_sms() * 2u * kWarps;
+        const uint64_t warp_slots = (uint64_t)rt::num_sms() * kCtasPerSm * kWarps;
         while (cp > 4 && (uint64_t)p->num_seqs * p->num_kv_heads * ((pages_max + cp - 1) / cp) <
                              2u * warp_slots)
             cp /= 2;
@@ -1034,7 +1041,7 @@ int launch_g(const CUtensorMap &map, const AttnArgs &args, dim3 grid, cudaStream
     pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     pdl[0].val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t gcfg = {};
-    gcfg.gridDim = dim3((unsigned)rt::num_sms() * 2u);
+    gcfg.gridDim = dim3((unsigned)rt::num_sms() * kCtasPerSm);
     gcfg.blockDim = dim3(kWarps * 32);
     gcfg.dynamicSmemBytes = kSmemBytes;
     gcfg.stream = s;
@@ -1093,7 +1100,7 @@ extern "C" int rt_attn_plan(const rt_attn_params_t *p, uint32_t *chunk_pages, ui
     if (max_chunks) *max_chunks = pl.max_chunks;
     if (ctas) {
         const uint64_t need = ((uint64_t)pl.max_chunks * p->num_kv_heads * p->num_seqs + kWarps - 1) / kWarps;
-        const uint64_t resident = (uint64_t)rt::num_sms() * 2u;
+        const uint64_t resident = (uint64_t)rt::num_sms() * kCtasPerSm;
         *ctas = need < resident ? need : resident;
     }
     return RT_OK;
@@ -1175,7 +1182,7 @@ int launch_attention(const rt_attn_params_t *p, const rt_attn_group_params_t *gp
     // Persistent grid: two CTAs per SM (the shared-memory limit), never
     // more CTAs than there are items to hand out.
     uint64_t ctas = (args.n_items + kWarps - 1) / kWarps;
-    const uint64_t resident = (uint64_t)rt::num_sms() * 2u;
+    const uint64_t resident = (uint64_t)rt::num_sms() * kCtasPerSm;
     if (ctas > resident)
         ctas = resident;
     const dim3 grid((unsigned)ctas);
