@@ -13,7 +13,7 @@
 //    (page, head) blocks are adjacent in the arena, run side by side.
 //  * Staging: per page the warp's elected lane issues four 2-D TMA tensor
 //    loads (K and V, two 64-column halves each, 128-byte swizzle) into one
-//    8 KiB stage of the warp's 3-stage ring, completion tracked by a
+//    8 KiB stage of the warp's kStages-deep ring, completion tracked by a
 //    shared-memory mbarrier with transaction bytes (no multicast).
 //  * Math: per page, S^T = K.Q^T and O^T += V^T.P^T on m16n8k16 bf16 tensor
 //    cores with the page's 16 tokens (or 16 head dimensions) as the M rows
@@ -511,8 +511,8 @@ __device__ __forceinline__ bool process_item(const CUtensorMap &kv_map, const At
 }
 
 // One (group, row block, KV head, prefix chunk) item, processed by the whole
-// CTA: the group's shared prefix pages stream once through the CTA's 12-stage
-// ring (warp 0 loads the page ids, lane 0 issues the TMA copies), and each
+// CTA: the group's shared prefix pages stream once through the CTA's
+// kWarps x kStages-stage ring (warp 0 loads the page ids, lane 0 issues the TMA copies), and each
 // warp attends 16 query rows to every page - 16/G member sequences x G
 // heads, so for G = 4 every row of the m16n8k16 tile is a real query (4
 // sequences x 4 heads per warp, 16 sequences per CTA).  G = 8 needs two row
@@ -1179,7 +1179,7 @@ int launch_attention(const rt_attn_params_t *p, const rt_attn_group_params_t *gp
     args.gchunk_pages = gp ? pl.gchunk_pages : 1u;
     args.max_gchunks = pl.max_gchunks;
     args.slots = pl.slots;
-    // Persistent grid: two CTAs per SM (the shared-memory limit), never
+    // Persistent grid: kCtasPerSm CTAs per SM (the shared-memory limit), never
     // more CTAs than there are items to hand out.
     uint64_t ctas = (args.n_items + kWarps - 1) / kWarps;
     const uint64_t resident = (uint64_t)rt::num_sms() * kCtasPerSm;
