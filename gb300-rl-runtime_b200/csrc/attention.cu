@@ -512,7 +512,8 @@ __device__ __forceinline__ bool process_item(const CUtensorMap &kv_map, const At
 
 // One (group, row block, KV head, prefix chunk) item, processed by the whole
 // CTA: the group's shared prefix pages stream once through the CTA's
-// kWarps x kStages-stage ring (warp 0 loads the page ids, lane 0 issues the TMA copies), and each
+// kWarps x kStages-stage ring (warp 0 loads the page ids, lane 0 issues the
+// TMA copies), and each
 // warp attends 16 query rows to every page - 16/G member sequences x G
 // heads, so for G = 4 every row of the m16n8k16 tile is a real query (4
 // sequences x 4 heads per warp, 16 sequences per CTA).  G = 8 needs two row
