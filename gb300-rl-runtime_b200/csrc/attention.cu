@@ -85,7 +85,14 @@ struct AttnArgs {
     uint32_t slots;                    // partial slots per (b, h): max_gchunks + max_chunks
 };
 
+// The shared-prefix (group) kernel uses the CTA's whole ring.  Alone it is
+// faster with 2 CTAs per SM and 12 stages, but in the loop the sequence
+// kernel (a programmatic dependent) overlaps it, and 3 CTAs per SM, whose
+// idle CTAs exit at once and free their SMs, gave the shorter pass
+// (attention 60.3 against 64.0 us per pass, same box).
 constexpr int kGroupStages = kWarps * kStages;  // the CTA's whole ring, shared by its warps
+constexpr int kGroupCtasPerSm = kCtasPerSm;
+constexpr int kGroupSmemBytes = kGroupStages * kStageBytes + 1024;
 constexpr uint32_t kMaxGroupMembers = 16;
 
 __device__ __forceinline__ void flag_error(int32_t *err, int32_t code)
@@ -763,7 +770,7 @@ __device__ __forceinline__ bool process_group_item(const CUtensorMap &kv_map, co
 // (group, row block, head, chunk) items from a dispenser; the last CTA out
 // resets it for the next launch.
 template <int G>
-__global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
+__global__ void __launch_bounds__(kWarps * 32, kGroupCtasPerSm)
 paged_gqa_group_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnArgs a)
 {
     extern __shared__ uint8_t smem_raw[];
@@ -1003,7 +1010,7 @@ int prepare_g()
                              kSmemBytes);
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(paged_gqa_group_kernel<G>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, kGroupSmemBytes);
     if (e != cudaSuccess)
         return rt::cuda_fail(e, "attention: cudaFuncSetAttribute");
     if (dev < 64)
@@ -1042,9 +1049,9 @@ int launch_g(const CUtensorMap &map, const AttnArgs &args, dim3 grid, cudaStream
     pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     pdl[0].val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t gcfg = {};
-    gcfg.gridDim = dim3((unsigned)rt::num_sms() * kCtasPerSm);
+    gcfg.gridDim = dim3((unsigned)rt::num_sms() * kGroupCtasPerSm);
     gcfg.blockDim = dim3(kWarps * 32);
-    gcfg.dynamicSmemBytes = kSmemBytes;
+    gcfg.dynamicSmemBytes = kGroupSmemBytes;
     gcfg.stream = s;
     gcfg.attrs = pdl;
     gcfg.numAttrs = 1;
