@@ -886,7 +886,10 @@ struct Plan {
     size_t off_counters, off_ml, off_o, total;
 };
 
-constexpr uint32_t kDefaultGroupChunkPages = 16;
+#ifndef RT_ATTN_GROUP_CHUNK_PAGES
+#define RT_ATTN_GROUP_CHUNK_PAGES 16
+#endif
+constexpr uint32_t kDefaultGroupChunkPages = RT_ATTN_GROUP_CHUNK_PAGES;
 
 // Workspace header: error word at 0, per-warp item dispenser at 8/16, group
 // item dispenser at 24/32; arrival counters from 256.
