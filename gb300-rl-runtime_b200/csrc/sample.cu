@@ -1,21 +1,21 @@
 // sample.cu - fused temperature / top-k / top-p sampler for sm_100a.
 //
 // Replaces reference cu/sample.cu:40-123 (sample_token: one thread, ~6 serial
-// passes over the vocabulary and an O(V*k) insertion sort) with one 256-thread
-// CTA per row.  Several rows share an SM (small CTAs, no per-thread copy of
-// the row), and the row is streamed twice from L2/HBM:
+// passes over the vocabulary and an O(V*k) insertion sort) with one 512-thread
+// CTA per row, two CTAs per SM (all 256 rows of a decode pass run at once),
+// the row streamed twice (the second time from L2):
 //
 //  1. one streaming pass (16-byte loads, eight in flight per thread): scale
 //     by 1.0f / temperature (the reference's fp32 multiply), keep each
-//     thread's 5 largest values with their indices, detect NaN / +inf;
-//  2. tau0 = the nk-th largest of the 256 per-thread maxima, by counting for
-//     each maximum how many are larger.  Those maxima are nk row values
-//     >= tau0, so tau0 <= the top-k cutoff (the nk-th largest value counted
-//     with multiplicity) and every survivor is >= tau0;
-//  3. the candidates (values >= tau0) come from the per-thread lists; a
-//     thread whose 5th largest is still >= tau0 may hold more, and then the
-//     row is streamed a second time to collect them all.  A candidate
-//     survives iff fewer than nk candidates are strictly larger; survivors
+//     thread's maximum, detect NaN / +inf;
+//  2. tau0 = the smallest of the 16 warps' m-th largest per-thread maxima,
+//     m = ceil(nk / 16), by counting over each warp's 32 maxima.  Every warp
+//     has m row values >= its threshold, so at least nk values are >= tau0:
+//     tau0 <= the top-k cutoff (the nk-th largest value counted with
+//     multiplicity) and every survivor is >= tau0;
+//  3. a second streaming pass collects the candidates (values >= tau0,
+//     typically 100-200).  A candidate survives iff fewer than nk candidates
+//     are strictly larger (an all-pairs scan, 16 bytes at a time); survivors
 //     are sorted by vocabulary index (rank sort, typically k of them);
 //  4. one thread replays the reference's serial fp32 arithmetic over the
 //     survivors only: sum of __expf(l - max) in index order, 1.0f / sum,
