@@ -926,9 +926,10 @@ int make_plan(const rt_attn_params_t *p, Plan *pl, const rt_attn_group_params_t 
     const uint32_t pages_max = (p->max_seq_len + 15u) / 16u;
     uint32_t cp = p->chunk_pages;
     if (cp == 0) {
-        // 48 pages (768 tokens) per warp item (measured best on B200 for both
-        // the ragged config-2 batch and the rollout loop); smaller when there
-        // are too few items to give every warp slot of the GPU several.
+        // Up to 48 pages (768 tokens) per warp item, halved while there are
+        // fewer than two items per warp slot of the GPU: the ragged config-2
+        // batch and the rollout loop both land on 24 (config 2: 5,418 GB/s
+        // against 4,695 with 48-page items, 3 CTAs x 4 warps per SM).
         cp = 48;
         const uint64_t warp_slots = (uint64_t)rt::num_sms() * kCtasPerSm * kWarps;
         while (cp > 4 && (uint64_t)p->num_seqs * p->num_kv_heads * ((pages_max + cp - 1) / cp) <

@@ -1301,8 +1301,6 @@ extern "C" int rt_rollout_create(const rt_rollout_config_t *cfg, KVArena *arena,
         ok(cudaMemset(e->attn_ws, 0, e->attn_ws_bytes));
         if (err == cudaSuccess) {
             int rc = rt::attn_prepare(&e->ap);
-            if (rc == RT_OK)
-                rc = rt::sample_prepare();
             if (rc != RT_OK) {
                 engine_free(e);
                 return rc;

@@ -8,8 +8,6 @@ namespace rt {
 // Set kernel attributes of the attention launch for these params so a later
 // launch (e.g. inside stream capture) issues no attribute calls.
 int attn_prepare(const rt_attn_params_t *p);
-// Same for the sampler (its shared-memory opt-in).
-int sample_prepare();
 // Same for the tensor-core GEMM (its shared-memory opt-in on this device).
 int gemm_prepare();
 // rt_sample_rows with an optional programmatic dependent launch (the kernel

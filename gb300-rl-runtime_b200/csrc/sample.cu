@@ -46,7 +46,6 @@ constexpr int kBins = 4096;          // radix digits of the streamed cutoff sele
 constexpr int kCap = 1024;           // candidates handled by the fast path
 constexpr uint32_t kMaxVocab = 1u << 20;
 
-constexpr uint32_t kKeyCacheMax = 49152;  // vocab whose 16-bit key copy fits in shared memory
 
 struct SampleArgs {
     const float *logits;
@@ -56,7 +55,6 @@ struct SampleArgs {
     uint64_t stride;
     uint32_t vocab;
     uint32_t fused;
-    uint32_t keycache;  // pass 1 keeps the top 16 bits of every key in shared memory
 };
 
 __device__ __forceinline__ uint32_t float_key(float v)
@@ -302,7 +300,6 @@ __device__ __forceinline__ void stream_row(const RowReader &rd, uint32_t V, F &&
 __global__ void __launch_bounds__(kThr, 2) sample_rows_kernel(const SampleArgs a)
 {
     __shared__ Smem s;
-    extern __shared__ uint16_t s_keys[];  // [vocab] top 16 key bits (keycache only)
     const int tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5;
     const uint32_t V = a.vocab;
@@ -320,12 +317,9 @@ __global__ void __launch_bounds__(kThr, 2) sample_rows_kernel(const SampleArgs a
     // ---- pass 1: per-thread maximum of the values > -FLT_MAX, NaN / +inf ----
     float tmax = -INFINITY;
     bool bad = false;
-    const bool kc = a.keycache != 0u;
-    stream_row(rd, V, [&](float v, uint32_t idx) {
+    stream_row(rd, V, [&](float v, uint32_t) {
         bad |= !(v < INFINITY);  // NaN or +inf
         tmax = v > -FLT_MAX ? fmaxf(tmax, v) : tmax;
-        if (kc)
-            s_keys[idx] = (uint16_t)(float_key(v) >> 16);
     });
     if (tid == 0) {
         uint32_t ph[4];
@@ -386,46 +380,16 @@ __global__ void __launch_bounds__(kThr, 2) sample_rows_kernel(const SampleArgs a
         }
         __syncthreads();
         if (ok) {
-            if (kc) {
-                // ---- candidates from the shared-memory key copy: every
-                // value >= tau0 has a 16-bit key >= tau0's; the few extra
-                // entries of tau0's key bin are below the cutoff and drop
-                // out in the survivor test.  Exact values come from L2. ----
-                const uint32_t thr = float_key(tau0) >> 16;
-                const uint4 *k8 = reinterpret_cast<const uint4 *>(s_keys);
-                for (uint32_t g = (uint32_t)tid; g < (V + 7u) / 8u; g += kThr) {
-                    const uint4 w = k8[g];
-                    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-                    for (int h2 = 0; h2 < 4; h2++) {
-#pragma unroll
-                        for (int hh = 0; hh < 2; hh++) {
-                            const uint32_t key = hh ? (ws[h2] >> 16) : (ws[h2] & 0xFFFFu);
-                            const uint32_t idx = 8u * g + 2u * h2 + hh;
-                            if (key >= thr && idx < V) {
-                                const uint32_t pos = atomicAdd(&s.count, 1u);
-                                if (pos < (uint32_t)kCap)
-                                    s.cand_idx[pos] = idx;
-                            }
-                        }
+            // ---- pass 2: candidates >= tau0 ----
+            stream_row(rd, V, [&](float v, uint32_t idx) {
+                if (v >= tau0) {
+                    const uint32_t pos = atomicAdd(&s.count, 1u);
+                    if (pos < (uint32_t)kCap) {
+                        s.cand_idx[pos] = idx;
+                        s.cand_val[pos] = v;
                     }
                 }
-                __syncthreads();
-                const uint32_t nf = s.count;
-                for (uint32_t j = tid; j < nf && j < (uint32_t)kCap; j += kThr)
-                    s.cand_val[j] = rd(s.cand_idx[j]);
-            } else {
-                // ---- pass 2: candidates >= tau0 ----
-                stream_row(rd, V, [&](float v, uint32_t idx) {
-                    if (v >= tau0) {
-                        const uint32_t pos = atomicAdd(&s.count, 1u);
-                        if (pos < (uint32_t)kCap) {
-                            s.cand_idx[pos] = idx;
-                            s.cand_val[pos] = v;
-                        }
-                    }
-                });
-            }
+            });
             __syncthreads();
             const uint32_t nc = s.count;
             if (nc <= (uint32_t)kCap) {
@@ -557,27 +521,6 @@ __global__ void __launch_bounds__(kThr, 2) sample_rows_kernel(const SampleArgs a
 
 }  // namespace
 
-// Opt in to the key copy's dynamic shared memory, once per device.
-int rt::sample_prepare()
-{
-    static std::mutex mu;
-    static bool done[64] = {};
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess)
-        return rt::cuda_fail(e, "sample: cudaGetDevice");
-    std::lock_guard<std::mutex> lk(mu);
-    if (dev >= 0 && dev < 64 && done[dev])
-        return RT_OK;
-    e = cudaFuncSetAttribute(sample_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)(kKeyCacheMax * 2u));
-    if (e != cudaSuccess)
-        return rt::cuda_fail(e, "sample: cudaFuncSetAttribute");
-    if (dev >= 0 && dev < 64)
-        done[dev] = true;
-    return RT_OK;
-}
-
 extern "C" uint32_t rt_sample_uniform24(uint64_t seed, uint32_t rollout_id, uint64_t step)
 {
     uint32_t o[4];
@@ -624,11 +567,6 @@ int rt::sample_rows_launch(const rt_sample_params_t *p, const float *logits,
     a.stride = p->row_stride;
     a.vocab = p->vocab;
     a.fused = p->fused_cum ? 1u : 0u;
-    a.keycache = 0u;  // the key copy measured slower than a second L2 pass at 32K vocab
-    const size_t dyn = a.keycache ? (((size_t)p->vocab * 2u + 15u) & ~(size_t)15u) : 0u;
-    const int rc = rt::sample_prepare();
-    if (rc != RT_OK)
-        return rc;
     cudaError_t e;
     if (pdl) {
         cudaLaunchAttribute attr[1];
@@ -637,13 +575,13 @@ int rt::sample_rows_launch(const rt_sample_params_t *p, const float *logits,
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(p->num_rows);
         cfg.blockDim = dim3(kThr);
-        cfg.dynamicSmemBytes = dyn;
+        cfg.dynamicSmemBytes = 0;
         cfg.stream = stream;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
         e = cudaLaunchKernelEx(&cfg, sample_rows_kernel, a);
     } else {
-        sample_rows_kernel<<<p->num_rows, kThr, dyn, stream>>>(a);
+        sample_rows_kernel<<<p->num_rows, kThr, 0, stream>>>(a);
         e = cudaGetLastError();
     }
     return e == cudaSuccess ? RT_OK : rt::cuda_fail(e, "sample: launch");

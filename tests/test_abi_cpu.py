@@ -88,4 +88,6 @@ def test_attention_params_validation_on_cpu(pkg):
     bad = pkg.rt_attn_params_t(64, 32, 8, 128, 16, 4096, 100000, 1.0, 0)   # 16 pages < 4096 tok
     assert pkg.lib().rt_attn_workspace_bytes(ctypes.byref(bad)) == 0
     cp, mc, ctas = pkg.PagedDecodeAttention.plan(type("X", (), {"params": p})())
-    assert cp == 48 and mc == 6 and ctas == min(6 * 8 * 64 // 4, 148 * 2)
+    # 48-page items would leave fewer than two per warp slot (148 SMs x 3 CTAs
+    # x 4 warps), so the plan halves them to 24
+    assert cp == 24 and mc == 11 and ctas == min(11 * 8 * 64 // 4, 148 * 3)
