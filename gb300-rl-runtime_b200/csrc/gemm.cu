@@ -40,7 +40,16 @@
 
 namespace {
 
-constexpr uint32_t kBM = 256, kBN = 224, kBK = 64, kStages = 3;
+#ifndef RT_GEMM_BK
+#define RT_GEMM_BK 64
+#endif
+// K-slice per stage: 64 bf16 (128-byte rows, 128-byte swizzle, 3 stages of
+// 60 KiB) or 32 (64-byte rows, 64-byte swizzle, 6 stages of 30 KiB).
+constexpr uint32_t kBM = 256, kBN = 224, kBK = RT_GEMM_BK, kStages = kBK == 64u ? 3u : 6u;
+constexpr uint32_t kRowBytes = kBK * 2u;                   // one operand row of a stage
+constexpr uint32_t kAtomBytes = 8u * kRowBytes;            // 8-row swizzle atom
+constexpr uint32_t kSwizzleMode = kBK == 64u ? 2u : 4u;    // descriptor layout: 128B / 64B
+static_assert(kBK == 64u || kBK == 32u, "K-slice of 32 or 64");
 constexpr uint32_t kHalf = 128;                      // rows per UMMA (M 128)
 constexpr uint32_t kABytes = kBM * kBK * 2;         // 32 KiB
 constexpr uint32_t kBBytes = kBN * kBK * 2;         // 28 KiB
@@ -94,6 +103,20 @@ __device__ __forceinline__ void unit_coords(const GemmArgs &g, uint32_t u, uint3
 __device__ __forceinline__ void epilogue_sync()
 {
     asm volatile("bar.sync 1, 256;" ::: "memory");
+}
+
+// K-major operand descriptor of a stage: swizzled rows of kRowBytes,
+// 8-row atoms kAtomBytes apart (16 bf16 = 32 bytes further along a row per
+// MMA K step).
+__device__ __forceinline__ uint64_t umma_desc(uint32_t smem_addr)
+{
+    uint64_t d = 0;
+    d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+    d |= (uint64_t)(16u >> 4) << 16;
+    d |= (uint64_t)((kAtomBytes >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1u << 46;  // version
+    d |= (uint64_t)kSwizzleMode << 61;
+    return d;
 }
 
 __device__ __forceinline__ bool wait_or_abort(Shared *sh, uint32_t bar, uint32_t parity,
@@ -215,10 +238,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (uint32_t kk = 0; kk < kBK / 16u; kk++) {
                         // K-major SW128: 16 bf16 = 32 bytes further along each row
-                        const uint64_t db = rt::umma_desc_sw128(sa + kABytes + kk * 32u, 16u, 1024u);
+                        const uint64_t db = umma_desc(sa + kABytes + kk * 32u);
                         for (uint32_t h = 0; h < halves; h++) {
-                            const uint64_t da = rt::umma_desc_sw128(
-                                sa + h * (kHalf * kBK * 2u) + kk * 32u, 16u, 1024u);
+                            const uint64_t da = umma_desc(sa + h * (kHalf * kRowBytes) + kk * 32u);
                             rt::umma_bf16_ss(tmem + h * kAccCols, da, db, idesc,
                                              (kb > kb0 || kk > 0u) ? 1u : 0u);
                         }
@@ -453,9 +475,9 @@ extern "C" int rt_gemm_bf16(const rt_gemm_params_t *p, const void *A, const void
         return RT_EINVAL;
     }
     CUtensorMap ma, mb;
-    int rc = rt::encode_bf16_kmajor_map(&ma, A, p->K, p->M, (uint64_t)p->lda * 2u, kBM);
+    int rc = rt::encode_bf16_kmajor_map(&ma, A, p->K, p->M, (uint64_t)p->lda * 2u, kBM, kBK);
     if (rc == RT_OK)
-        rc = rt::encode_bf16_kmajor_map(&mb, B, p->K, p->N, (uint64_t)p->ldb * 2u, kBN);
+        rc = rt::encode_bf16_kmajor_map(&mb, B, p->K, p->N, (uint64_t)p->ldb * 2u, kBN, kBK);
     if (rc != RT_OK)
         return rc;
     GemmArgs g;

@@ -355,11 +355,12 @@ int num_sms();
 // Encode a 2-D bf16 tensor map over rows of 128 elements (256 B), box
 // 64 x 16 with 128-byte swizzle.  Returns 0 or RT_* error.
 int encode_kv_rows_map(CUtensorMap *map, const void *base, uint64_t rows);
-// 2-D map over a row-major bf16 matrix [rows][k] (k contiguous), box of 64
-// columns (128 bytes) x box_rows rows, 128-byte swizzle: the K-major
-// operand tile of a tcgen05 MMA.  Out-of-range rows and columns read zero.
+// 2-D map over a row-major bf16 matrix [rows][k] (k contiguous), box of
+// box_k (64 or 32) columns x box_rows rows with 128- or 64-byte swizzle: the
+// K-major operand tile of a tcgen05 MMA.  Out-of-range rows and columns
+// read zero.
 int encode_bf16_kmajor_map(CUtensorMap *map, const void *base, uint64_t k, uint64_t rows,
-                           uint64_t row_stride_bytes, uint32_t box_rows);
+                           uint64_t row_stride_bytes, uint32_t box_rows, uint32_t box_k);
 // 2-D map over a row-major fp32 matrix [rows][cols] for TMA stores: box of
 // 32 columns (128 bytes) x box_rows rows, 128-byte swizzle.  Stores are
 // clipped at the matrix edge.

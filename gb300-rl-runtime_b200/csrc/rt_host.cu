@@ -88,7 +88,7 @@ int encode_kv_rows_map(CUtensorMap *map, const void *base, uint64_t rows)
 }
 
 int encode_bf16_kmajor_map(CUtensorMap *map, const void *base, uint64_t k, uint64_t rows,
-                           uint64_t row_stride_bytes, uint32_t box_rows)
+                           uint64_t row_stride_bytes, uint32_t box_rows, uint32_t box_k)
 {
     EncodeTiledFn fn = encode_fn();
     if (!fn) {
@@ -100,14 +100,18 @@ int encode_bf16_kmajor_map(CUtensorMap *map, const void *base, uint64_t k, uint6
         set_error("bf16 operand: base and row stride must be 16-byte aligned, box rows 1..256");
         return RT_EINVAL;
     }
+    if (box_k != 64u && box_k != 32u) {
+        set_error("bf16 operand: K box of 32 or 64 elements");
+        return RT_EINVAL;
+    }
     cuuint64_t gdim[2] = {(cuuint64_t)k, (cuuint64_t)rows};
     cuuint64_t gstride[1] = {(cuuint64_t)row_stride_bytes};
-    cuuint32_t box[2] = {64u, box_rows};
+    cuuint32_t box[2] = {box_k, box_rows};
     cuuint32_t estride[2] = {1u, 1u};
     CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), gdim,
                     gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                    box_k == 64u ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         set_error("cuTensorMapEncodeTiled failed (CUresult %d)", (int)r);
         return RT_ECUDA;
