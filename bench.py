@@ -814,7 +814,8 @@ class RolloutModelWorkload(RolloutWorkload):
     instead of Philox q / K / V and logits: per pass the slots' last-token
     embeddings (table 32,000 x 4,096 bf16), the QKV projection (4,096 ->
     6,144) and the LM head (4,096 -> 32,000) run as tensor-core GEMMs
-    (rt_gemm_bf16) around the same paged attention and sampler.  Weights
+    (rt_gemm_bf16) around the same paged attention and sampler; the
+    prompts' K / V come from the same model (rt_rollout_prefill).  Weights
     are seeded N(0, s) bf16 (no checkpoint exists offline): embedding s = 1,
     QKV 1/64, LM head 0.05."""
 
@@ -833,6 +834,18 @@ class RolloutModelWorkload(RolloutWorkload):
         self.pkg.fill_normal_bf16(self.wlm, seed=31 + rank, stream_id=3, std=0.05)
         self.eng.set_model(self.emb, self.wqkv, self.wlm)
         self.gemm_flops_per_token = 2.0 * D * (NQKV + self.VOCAB)
+        # the prompts' K / V from the model (seeded token ids), untimed setup,
+        # its rate measured once with CUDA events
+        g = torch.Generator(device=dev).manual_seed(41 + rank)
+        toks = torch.randint(0, self.VOCAB, (self.ng, self.PROMPT), generator=g, device=dev,
+                             dtype=torch.int32)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for gi in range(self.ng):
+            self.eng.prefill(gi, toks[gi])
+        e1.record()
+        torch.cuda.synchronize()
+        self.prefill_tokens_per_s = self.ng * self.PROMPT / (e0.elapsed_time(e1) / 1e3)
 
     def cpu_sample(self, threads, budget_s=10.0):
         """The model decode step on the host for one GRPO group (16
@@ -879,6 +892,9 @@ class RolloutModelWorkload(RolloutWorkload):
         return super().config() | {
             "model": "embedding 32,000 x 4,096, QKV 4,096 -> 6,144, LM head 4,096 -> 32,000; "
                      "bf16 weights N(0, s), fp32 accumulation",
+            "prompts": "seeded token ids, K / V prefilled by the model (rt_rollout_prefill, "
+                       "untimed setup)",
+            "prefill_tokens_per_s": round(self.prefill_tokens_per_s),
             "gemm_flops_per_token": self.gemm_flops_per_token}
 
 

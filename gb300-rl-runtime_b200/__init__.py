@@ -245,6 +245,7 @@ _SIGS = {
     "rt_host_decode_pump": (ctypes.c_int64, [_P, _P, ctypes.c_uint32, ctypes.c_uint32, _P, _P,
                                              ctypes.c_uint32, ctypes.c_uint32]),
     "rt_rollout_set_model": (ctypes.c_int, [_P, ctypes.POINTER(rt_model_weights_t)]),
+    "rt_rollout_prefill": (ctypes.c_int, [_P, ctypes.c_uint32, _P, ctypes.c_uint32, _P]),
     "rt_gemm_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(rt_gemm_params_t)]),
     "rt_gemm_bf16": (ctypes.c_int, [ctypes.POINTER(rt_gemm_params_t), _P, _P, _P, _P,
                                     ctypes.c_size_t, _P, _P]),
@@ -575,6 +576,12 @@ class RolloutEngine:
         w = rt_model_weights_t(embed.data_ptr(), w_qkv.data_ptr(), w_lm.data_ptr(),
                                embed.shape[1], 0)
         check(lib().rt_rollout_set_model(self.h, ctypes.byref(w)), "rt_rollout_set_model")
+
+    def prefill(self, prefix_id, tokens, stream=None):
+        """rt_rollout_prefill: K / V of the prefix's prompt tokens (device
+        uint32 / int32 tensor) from the model weights."""
+        check(lib().rt_rollout_prefill(self.h, prefix_id, ctypes.c_void_p(tokens.data_ptr()),
+                                       tokens.numel(), _stream_ptr(stream)), "rt_rollout_prefill")
 
     def buffers(self):
         b = rt_rollout_buffers_t()

@@ -150,6 +150,7 @@ __device__ bool sink_push(const RtIo &io, RtCtl *ctl, const RolloutDone &rec)
 }
 
 constexpr uint32_t kKeyTable = 1024;  // prefix ids grouped through a table (else a slot scan)
+constexpr uint32_t kPrefillChunk = 4096;  // prompt tokens per prefill projection
 
 __device__ __forceinline__ uint32_t ld_sys_u32(const void *p)
 {
@@ -882,6 +883,46 @@ __global__ void __launch_bounds__(256) hidden_kernel(const Dev d)
     rt::grid_dep_launch();
 }
 
+// ---- model prefill of a registered prefix (rt_rollout_prefill) ----
+
+// x_i = embed[tokens[i]] for the chunk's tokens (one CTA per token).
+__global__ void __launch_bounds__(256) prefill_embed_kernel(const uint32_t *tokens,
+                                                            const __nv_bfloat16 *embed,
+                                                            __nv_bfloat16 *x, uint32_t dm,
+                                                            uint32_t vocab, int32_t *error)
+{
+    const uint32_t i = blockIdx.x;
+    uint32_t tok = tokens[i];
+    if (tok >= vocab) {
+        if (threadIdx.x == 0)
+            atomicCAS(error, 0, RT_EDEVICE);
+        tok = 0u;
+    }
+    const uint4 *src = reinterpret_cast<const uint4 *>(embed + (size_t)tok * dm);
+    uint4 *dst = reinterpret_cast<uint4 *>(x + (size_t)i * dm);
+    for (uint32_t j = threadIdx.x; j < dm / 8u; j += blockDim.x)
+        dst[j] = __ldg(src + j);
+}
+
+// K and V rows of token (first + i) (fp32 projection [k heads | v heads] x
+// 128) into the prefix page holding that position, as bf16.
+__global__ void __launch_bounds__(256) prefill_scatter_kernel(const float *kv, const int32_t *pages,
+                                                              uint32_t first, uint32_t hkv,
+                                                              __nv_bfloat16 *arena)
+{
+    const uint32_t i = blockIdx.x, pos = first + i;
+    const uint64_t page = (uint64_t)pages[pos >> 4];
+    const uint32_t prow = pos & 15u;
+    const float4 *row = reinterpret_cast<const float4 *>(kv + (size_t)i * hkv * 256u);
+    for (uint32_t g = threadIdx.x; g < hkv * 2u * 32u; g += blockDim.x) {
+        const uint32_t plane = g / (hkv * 32u), h = (g >> 5) % hkv, d4 = g & 31u;
+        const float4 v = row[g];
+        __nv_bfloat16 *dst = arena + rt_page_elem_offset(page, h, plane, prow, hkv) + d4 * 4u;
+        reinterpret_cast<uint2 *>(dst)[0] =
+            make_uint2(rt::pack_bf16x2(v.x, v.y), rt::pack_bf16x2(v.z, v.w));
+    }
+}
+
 // logits[v] = std * N(0,1), Philox key = seed, counter = (token index lo,
 // request low 32, tag | token index hi, v / 4).
 __device__ __forceinline__ void logits_row(float *out, uint32_t vocab, uint64_t seed,
@@ -986,6 +1027,11 @@ struct rt_rollout {
     cudaGraph_t graph;
     cudaGraphExec_t exec;
     RtIo *io_stage;  // pinned host staging of the io block
+    // registered prefixes (host copies): token length and page-list offset
+    uint32_t *pf_len_h, *pf_off_h;
+    // model prefill scratch: embeddings and K/V projections of a token chunk
+    __nv_bfloat16 *pre_x;
+    float *pre_kv;
 };
 
 namespace {
@@ -1149,7 +1195,7 @@ void engine_free(rt_rollout *e)
                     e->d.enable, e->d.srows, e->d.tokens, e->d.q, e->d.attn_out, e->d.logits,
                     e->d.pf_len, e->d.pf_np, e->d.pf_off, e->d.pf_pages, e->d.groups,
                     e->d.n_groups, e->d.skip, e->attn_ws, e->d.hin, e->d.hout, e->d.qkv,
-                    e->d.emb_tok, e->d.gemm_err, e->d.gemm_ws};
+                    e->d.emb_tok, e->d.gemm_err, e->d.gemm_ws, e->pre_x, e->pre_kv};
     for (void *p : bufs)
         if (p)
             cudaFree(p);
@@ -1159,10 +1205,17 @@ void engine_free(rt_rollout *e)
         for (uint32_t i = 0; i < e->n_priv; i++)
             arena_release(e->arena, e->priv_blocks[i]);
     free(e->priv_blocks);
+    delete[] e->pf_len_h;
+    delete[] e->pf_off_h;
     delete e;
 }
 
 }  // namespace
+
+static uint32_t npf_h(const rt_rollout_config_t *cfg)
+{
+    return cfg->max_prefixes ? cfg->max_prefixes : 1u;
+}
 
 extern "C" int rt_rollout_create(const rt_rollout_config_t *cfg, KVArena *arena, rt_rollout_t **out)
 {
@@ -1251,7 +1304,15 @@ extern "C" int rt_rollout_create(const rt_rollout_config_t *cfg, KVArena *arena,
         engine_free(e);
         return rt::cuda_fail(err, "rollout: device allocation");
     }
+    ok(cudaMemset(d.ctl, 0, sizeof(RtCtl)));  // counters read before a first launch are zero
     if (full) {
+        e->pf_len_h = new (std::nothrow) uint32_t[npf_h(cfg)]();
+        e->pf_off_h = new (std::nothrow) uint32_t[npf_h(cfg)]();
+        if (!e->pf_len_h || !e->pf_off_h) {
+            engine_free(e);
+            rt::set_error("rollout: out of host memory");
+            return RT_ENOMEM;
+        }
         ok(cudaMemset(d.pf_len, 0, sizeof(uint32_t) * (cfg->max_prefixes ? cfg->max_prefixes : 1u)));
         ok(cudaMemset(d.pf_np, 0, sizeof(uint32_t) * (cfg->max_prefixes ? cfg->max_prefixes : 1u)));
         d.arena = reinterpret_cast<__nv_bfloat16 *>(arena->base);
@@ -1372,6 +1433,13 @@ extern "C" int rt_rollout_set_model(rt_rollout_t *e, const rt_model_weights_t *w
             return rt::cuda_fail(err, "rollout_set_model: projection workspace");
         d.gemm_ws_bytes = need;
     }
+    if (!e->pre_x) {
+        auto ok = [&](cudaError_t x) { if (err == cudaSuccess) err = x; };
+        ok(dalloc(&e->pre_x, (size_t)kPrefillChunk * d.dm));
+        ok(dalloc(&e->pre_kv, (size_t)kPrefillChunk * d.hkv * 256u));
+        if (err != cudaSuccess)
+            return rt::cuda_fail(err, "rollout_set_model: prefill scratch");
+    }
     d.w_embed = static_cast<const __nv_bfloat16 *>(w->embed);
     d.w_qkv = static_cast<const __nv_bfloat16 *>(w->w_qkv);
     d.w_lm = static_cast<const __nv_bfloat16 *>(w->w_lm);
@@ -1408,8 +1476,10 @@ extern "C" int rt_rollout_set_prefix(rt_rollout_t *e, uint32_t prefix_id, const 
     }
     if (prefix_id >= e->cfg.max_prefixes || (token_len + 15u) / 16u > n_pages ||
         token_len > e->d.maxp * 16u) {
-        rt::set_error("rollout_set_prefix: prefix %u (max %u) with %u tokens needs %u pages, got %u",
-                      prefix_id, e->cfg.max_prefixes, token_len, (token_len + 15u) / 16u, n_pages);
+        rt::set_error("rollout_set_prefix: prefix %u (max %u) with %u tokens needs %u pages (got %u) "
+                      "and at most %u tokens (the context)",
+                      prefix_id, e->cfg.max_prefixes, token_len, (token_len + 15u) / 16u, n_pages,
+                      e->d.maxp * 16u);
         return RT_EINVAL;
     }
     if (e->pf_used + n_pages > e->cfg.max_prefix_pages) {
@@ -1434,11 +1504,53 @@ extern "C" int rt_rollout_set_prefix(rt_rollout_t *e, uint32_t prefix_id, const 
         err = cudaMemcpy(e->d.pf_off + prefix_id, &off, 4, cudaMemcpyHostToDevice);
     if (err != cudaSuccess)
         return rt::cuda_fail(err, "rollout_set_prefix: copy");
+    e->pf_len_h[prefix_id] = token_len;
+    e->pf_off_h[prefix_id] = off;
     e->pf_used += n_pages;
     return RT_OK;
 }
 
 static int rollout_setup(rt_rollout_t *e, const rt_rollout_io_t *io, cudaStream_t s);
+
+extern "C" int rt_rollout_prefill(rt_rollout_t *e, uint32_t prefix_id, const uint32_t *tokens,
+                                  uint32_t n_tokens, void *stream)
+{
+    if (!e || e->cfg.decode_mode != RT_ROLLOUT_DECODE_MODEL || !e->d.w_embed) {
+        rt::set_error("rollout_prefill: needs a model-decode engine with its weights attached");
+        return RT_EINVAL;
+    }
+    if (prefix_id >= e->cfg.max_prefixes || e->pf_len_h[prefix_id] != n_tokens ||
+        (n_tokens && !tokens)) {
+        rt::set_error("rollout_prefill: prefix %u must be registered with exactly %u tokens",
+                      prefix_id, n_tokens);
+        return RT_EINVAL;
+    }
+    const Dev &d = e->d;
+    cudaStream_t s = (cudaStream_t)stream;
+    const int32_t *pages = d.pf_pages + e->pf_off_h[prefix_id];
+    const uint32_t nkv = d.hkv * 256u;  // k then v rows of every kv head
+    for (uint32_t c0 = 0; c0 < n_tokens; c0 += kPrefillChunk) {
+        const uint32_t m = std::min(kPrefillChunk, n_tokens - c0);
+        prefill_embed_kernel<<<m, 256, 0, s>>>(tokens + c0, d.w_embed, e->pre_x, d.dm, d.vocab,
+                                               d.gemm_err);
+        cudaError_t err = cudaGetLastError();
+        if (err != cudaSuccess)
+            return rt::cuda_fail(err, "rollout_prefill: embed launch");
+        // the K / V rows of the QKV weight follow its hq * 128 q rows
+        rt_gemm_params_t gp = {m, nkv, d.dm, d.dm, d.dm, nkv, gemm_splits(m, nkv, d.dm), 0u};
+        while (gp.split_k > 1u && rt_gemm_workspace_bytes(&gp) > d.gemm_ws_bytes)
+            gp.split_k--;  // K-splits only as far as the engine's workspace holds them
+        int rc = rt_gemm_bf16(&gp, e->pre_x, d.w_qkv + (size_t)d.hq * 128u * d.dm, e->pre_kv,
+                              d.gemm_ws, d.gemm_ws_bytes, d.gemm_err, s);
+        if (rc != RT_OK)
+            return rc;
+        prefill_scatter_kernel<<<m, 256, 0, s>>>(e->pre_kv, pages, c0, d.hkv, d.arena);
+        err = cudaGetLastError();
+        if (err != cudaSuccess)
+            return rt::cuda_fail(err, "rollout_prefill: scatter launch");
+    }
+    return RT_OK;
+}
 
 extern "C" int rt_rollout_launch(rt_rollout_t *e, const rt_rollout_io_t *io, void *stream)
 {

@@ -381,6 +381,18 @@ typedef struct {
 } rt_model_weights_t;
 int rt_rollout_set_model(rt_rollout_t *eng, const rt_model_weights_t *w);
 
+/* Model prefill of a registered prefix (RT_ROLLOUT_DECODE_MODEL engine with
+ * its weights attached): `tokens` (device, uint32 [n_tokens]) are the
+ * prompt's token ids and n_tokens the token length the prefix was
+ * registered with; for every position i the K and V rows
+ *   [k | v] = bf16(embed[tokens[i]] . w_qkv[k and v rows]^T)
+ * are written into the prefix's page holding i (a tensor-core GEMM over
+ * 4,096 positions at a time).  A token id >= vocab is replaced by 0 and
+ * flags RT_EDEVICE in the model error word.  Stream-ordered; it shares
+ * scratch with the engine's launches, so it must not overlap one. */
+int rt_rollout_prefill(rt_rollout_t *eng, uint32_t prefix_id, const uint32_t *tokens,
+                       uint32_t n_tokens, void *stream);
+
 /* Wait for the loop (stream sync) and read its counters. */
 int rt_rollout_wait(rt_rollout_t *eng, void *stream, rt_rollout_stats_t *stats);
 

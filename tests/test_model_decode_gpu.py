@@ -55,11 +55,11 @@ def make_requests(orc, n, seed):
     return r
 
 
-def build(pkg, cuda):
-    cfg = dict(num_q_heads=HQ, num_kv_heads=HKV, vocab=V, max_slots=S, max_context=512,
+def build(pkg, cuda, max_context=512):
+    cfg = dict(num_q_heads=HQ, num_kv_heads=HKV, vocab=V, max_slots=S, max_context=max_context,
                max_new_tokens=16, max_admit=256, drop_when_full=0,
                decode_mode=pkg.RT_ROLLOUT_DECODE_MODEL, reward_mode=0, logit_std=2.0,
-               max_prefixes=4, max_prefix_pages=64, max_passes=1 << 20, idle_timeout_ms=2000)
+               max_prefixes=4, max_prefix_pages=512, max_passes=1 << 20, idle_timeout_ms=2000)
     arena = pkg.DeviceArena(1024)
     eng = pkg.RolloutEngine(cfg, arena)
     for pid, L in enumerate([40, 64]):
@@ -161,4 +161,40 @@ def test_model_decode_pass_by_pass(pkg, orc, cuda):
     lens = reqs["max_tokens"]
     t = traj2.cpu().numpy()
     assert all((t[i, :lens[i]] >= 0).all() and (t[i, :lens[i]] < V).all() for i in range(n))
+    eng.close()
+
+
+def test_prefill_writes_prompt_kv(pkg, orc, cuda):
+    """rt_rollout_prefill: every position of a 4,100-token prompt (two
+    4,096-token projection chunks) gets bf16(embed[token] . w_kv^T) in its
+    prefix page; an out-of-range token id is flagged."""
+    eng, arena, emb, wqkv, wlm = build(pkg, cuda, max_context=4352)
+    eng.set_model(emb, wqkv, wlm)
+    L = 4100
+    pages = arena.acquire((L + 15) // 16)
+    eng.set_prefix(2, pages, L)
+    g = torch.Generator(device=cuda).manual_seed(5)
+    toks = torch.randint(0, V, (L,), generator=g, device=cuda, dtype=torch.int32)
+    eng.prefill(2, toks)
+    torch.cuda.synchronize()
+    x = emb[toks.long()]
+    wkv = wqkv[HQ * 128:]
+    ref = x.double() @ wkv.double().T                     # [L][k heads | v heads]
+    bound = (x.double().abs() @ wkv.double().abs().T) * 2.0 ** -16 + ref.abs() * 2.0 ** -8
+    kvp = arena.buf.view(torch.bfloat16).view(-1, HKV, 2, 16, 128)
+    pg = torch.as_tensor(np.asarray(pages)[np.arange(L) // 16], device=cuda).long()
+    row = torch.arange(L, device=cuda) % 16
+    got = kvp[pg, :, :, row, :]                            # [L][HKV][2][128]
+    want = ref.view(L, 2, HKV, 128).permute(0, 2, 1, 3)
+    bnd = bound.view(L, 2, HKV, 128).permute(0, 2, 1, 3)
+    assert bool(((got.double() - want).abs() <= bnd).all())
+    st = eng.wait()
+    assert st["model_error"] == 0
+    bad = toks.clone()
+    bad[7] = V + 3
+    eng.prefill(2, bad)
+    st = eng.wait(check_errors=False)
+    assert st["model_error"] == pkg.RT_EDEVICE
+    with pytest.raises(pkg.RuntimeErrorRT, match="registered"):
+        eng.prefill(2, toks[:100])
     eng.close()
