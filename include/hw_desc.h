@@ -71,18 +71,47 @@ RT_STATIC_ASSERT(sizeof(completion_t) == 7, "completion_t is 56 bits");
  * precedence over REWARD_NEEDED, as in the RTL FSM (reference
  * rtl/rollout_worker_fsm.sv:61-75); a STOP descriptor maps to STOPPED.
  * A descriptor with neither flag (echoed unchanged) reports status 0. */
+static inline RT_HD uint8_t
+hw_completion_status(const hw_desc_t *d)
+{
+    if (d->opcode == DESC_OP_STOP)
+        return (uint8_t)HW_COMP_STATUS_STOPPED;
+    if (d->flags & DESC_FLAG_DONE)
+        return (uint8_t)HW_COMP_STATUS_DONE;
+    if (d->flags & DESC_FLAG_NEEDS_REWARD)
+        return (uint8_t)HW_COMP_STATUS_REWARD_NEEDED;
+    return 0;
+}
+
 static inline RT_HD void
 hw_completion_from_desc(const hw_desc_t *d, completion_t *out)
 {
-    uint8_t st = 0;
-    if (d->opcode == DESC_OP_STOP)
-        st = (uint8_t)HW_COMP_STATUS_STOPPED;
-    else if (d->flags & DESC_FLAG_DONE)
-        st = (uint8_t)HW_COMP_STATUS_DONE;
-    else if (d->flags & DESC_FLAG_NEEDS_REWARD)
-        st = (uint8_t)HW_COMP_STATUS_REWARD_NEEDED;
     out->rollout_id = (uint16_t)d->rollout_id;
-    out->status = st;
+    out->status = hw_completion_status(d);
     out->final_seq_len = (uint16_t)d->seq_len;
     out->reward_id = (uint16_t)d->reward_model_id;
 }
+
+/*
+ * hw_completion_wire_t - one 64-byte completion record for both the C done
+ * ring and a 512-bit RTL completion output (the byte-identical completion
+ * definition the reference lists as a gap, docs/descriptor_contract.md
+ * "Gaps To Close" 2 and the 64-byte roadmap).  It is the done descriptor
+ * itself, every field at its hw_desc_t offset, with the completion status
+ * (HW_COMP_STATUS_*, one namespace with the RTL's completion_t) in the high
+ * byte of `flags`, which the descriptor flags (bits 0-2) leave free; the
+ * compact completion_t is derived from it without loss of its fields.
+ */
+typedef hw_desc_t hw_completion_wire_t;
+#define HW_WIRE_STATUS_SHIFT 8u
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+/* Encode a done descriptor as a wire record; decode a wire record into the
+ * compact completion_t (equal to hw_completion_from_desc of the descriptor). */
+void hw_completion_wire_encode(const hw_desc_t *done, hw_completion_wire_t *wire);
+void hw_completion_wire_decode(const hw_completion_wire_t *wire, completion_t *out);
+#ifdef __cplusplus
+}
+#endif

@@ -120,3 +120,47 @@ def test_arena_never_exceeds_capacity(mine):
     # capacity of 10 blocks: ids 0..9 then -1 (the reference hands out ids
     # past the allocation; this runtime bounds them)
     assert [int(x) for x in log[:11]] == list(range(10)) + [-1]
+
+
+def test_completion_wire_record(pkg, mine, golden):
+    """The 64-byte completion wire record (hw_desc.h): the done descriptor
+    byte for byte with the completion status in the high byte of flags; it
+    decodes to the compact completion_t of the RTL."""
+    import ctypes
+    import __graft_entry__ as ge
+    dt = ge.load_oracle().HW_DESC_DTYPE
+    lib = pkg.lib()
+    enc, dec = lib.hw_completion_wire_encode, lib.hw_completion_wire_decode
+    enc.argtypes = dec.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+    enc.restype = dec.restype = None
+    descs = mine.gen_c1(2000, seed=3, max_tokens=300)
+    done, _, _, _ = mine.run_c1(descs, depth_cap=256)
+    stop = np.zeros(1, dt)
+    stop["opcode"], stop["rollout_id"], stop["seq_len"] = 255, 70000, 5
+    recs = np.concatenate([done, stop])
+    for d in recs:
+        d = np.array([d], dt)
+        w = np.zeros(1, dt)
+        enc(d.ctypes.data, w.ctypes.data)
+        f = int(d["flags"][0])
+        want = (0xFF if d["opcode"][0] == 255 else 1 if f & 2 else 2 if f & 1 else 0)
+        assert int(w["flags"][0]) == (f & 0xFF) | (want << 8)
+        a, b = d.copy(), w.copy()
+        a["flags"] = b["flags"] = 0
+        assert a.tobytes() == b.tobytes()  # every other field at its offset, unchanged
+        c = pkg.completion_t()
+        dec(w.ctypes.data, ctypes.addressof(c))
+        assert (c.rollout_id, c.status, c.final_seq_len, c.reward_id) == (
+            int(d["rollout_id"][0]) & 0xFFFF, want, int(d["seq_len"][0]) & 0xFFFF,
+            int(d["reward_model_id"][0]) & 0xFFFF)
+    # RTL known answers (reference rtl/tb_rl_runtime_top.sv:80-147) through the wire
+    w_out = {k["in"]["rollout_id"]: k["out"] for k in golden["worker"]}
+    for rid, status, seq in [(77, 2, 32), (7, 1, 10), (11, 1, 12), (5, 0, 64)]:
+        d = np.zeros(1, dt)
+        for f, v in w_out[rid].items():
+            d[f] = v
+        w = np.zeros(1, dt)
+        enc(d.ctypes.data, w.ctypes.data)
+        c = pkg.completion_t()
+        dec(w.ctypes.data, ctypes.addressof(c))
+        assert (c.rollout_id, c.status, c.final_seq_len) == (rid, status, seq)
