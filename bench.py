@@ -471,6 +471,41 @@ class RolloutWorkload:
                 "h2d_bytes_per_step": self.n * 34,
                 "d2h_bytes_per_step": self.n * 24 + traj_h.numel() * 4 + adv_h.numel() * 4}
 
+    def trace_report(self):
+        """One more RL step, untimed, with the device trace attached
+        (rt_rollout_set_trace): device-clock latencies in the manner of the
+        reference's trace report (docs/tracing.md), from the schedule
+        kernel's records: rollout alloc -> trajectory done, and the interval
+        between decode passes."""
+        tr = self.pkg.DeviceTrace(1 << 17)
+        self.eng.set_trace(tr)
+        self.step()
+        self.eng.wait()
+        self.eng.set_trace(None)
+        rec, total = tr.read()
+        pk = self.pkg
+
+        def pct(x):
+            x = np.sort(np.asarray(x, dtype=np.float64))
+            if not len(x):
+                return None
+            q = lambda f: round(float(x[min(len(x) - 1, int(f * len(x)))]) / 1e3, 2)
+            return {"n": int(len(x)), "p50": q(0.5), "p90": q(0.9), "p99": q(0.99),
+                    "max": round(float(x[-1]) / 1e3, 2)}
+
+        alloc = {}
+        life = []
+        for r in rec:
+            t = int(r["type"])
+            if t == pk.TRACE_ROLLOUT_ALLOC:
+                alloc[int(r["rollout_id"])] = int(r["tsc"])
+            elif t == pk.TRACE_TRAJECTORY_DONE and int(r["rollout_id"]) in alloc:
+                life.append(int(r["tsc"]) - alloc.pop(int(r["rollout_id"])))
+        passes = rec[rec["type"] == pk.TRACE_DECODE_BATCH]["tsc"].astype(np.int64)
+        return {"clock": "GPU globaltimer, ns -> us", "records": int(total),
+                "rollout_alloc_to_done_us": pct(life),
+                "decode_pass_interval_us": pct(np.diff(passes))}
+
     def kernel_profile(self, n_rollouts=512):
         """Per-kernel device time from a host-stepped replay (rt_rollout_profile)
         of the first n_rollouts of the step."""
@@ -998,10 +1033,12 @@ def run_mine(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e["value"] = wl.units_per_step() / (float(t.item()) / 1e3) * world
         e2e["ms_per_step"] = float(t.item())
-    cpu = c1 = None
+    cpu = c1 = trace = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = wl.cpu_sample(os.cpu_count() or 1)
         c1 = config1_cpu_path()
+        if hasattr(wl, "trace_report"):
+            trace = wl.trace_report()
 
     if rank == 0:
         peaks, src = measured_peaks()
@@ -1042,6 +1079,7 @@ def run_mine(args):
                                                                  "d2h_bytes_per_step")},
             "gpu_launches": n_launch,
             "kernels": prof_report,
+            "device_trace": trace,
             "clocks": clocks.report(),
             "device_error_code": err,
         }

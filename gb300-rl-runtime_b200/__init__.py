@@ -245,6 +245,10 @@ _SIGS = {
     "rt_host_decode_pump": (ctypes.c_int64, [_P, _P, ctypes.c_uint32, ctypes.c_uint32, _P, _P,
                                              ctypes.c_uint32, ctypes.c_uint32]),
     "rt_rollout_set_model": (ctypes.c_int, [_P, ctypes.POINTER(rt_model_weights_t)]),
+    "rt_trace_bytes": (ctypes.c_size_t, [ctypes.c_uint32]),
+    "rt_trace_init": (ctypes.c_int, [_P, ctypes.c_uint32, _P]),
+    "rt_rollout_set_trace": (ctypes.c_int, [_P, _P]),
+    "rt_trace_read": (ctypes.c_int, [_P, _P, ctypes.c_uint32, ctypes.POINTER(ctypes.c_uint64), _P]),
     "rt_rollout_prefill": (ctypes.c_int, [_P, ctypes.c_uint32, _P, ctypes.c_uint32, _P]),
     "rt_gemm_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(rt_gemm_params_t)]),
     "rt_gemm_bf16": (ctypes.c_int, [ctypes.POINTER(rt_gemm_params_t), _P, _P, _P, _P,
@@ -583,6 +587,13 @@ class RolloutEngine:
         check(lib().rt_rollout_prefill(self.h, prefix_id, ctypes.c_void_p(tokens.data_ptr()),
                                        tokens.numel(), _stream_ptr(stream)), "rt_rollout_prefill")
 
+    def set_trace(self, trace):
+        """rt_rollout_set_trace: a DeviceTrace, or None to detach."""
+        self._trace = trace
+        check(lib().rt_rollout_set_trace(self.h, None if trace is None else
+                                         ctypes.c_void_p(trace.buf.data_ptr())),
+              "rt_rollout_set_trace")
+
     def buffers(self):
         b = rt_rollout_buffers_t()
         check(lib().rt_rollout_buffers(self.h, ctypes.byref(b)), "rt_rollout_buffers")
@@ -605,6 +616,36 @@ class RolloutEngine:
             self.close()
         except Exception:  # noqa: BLE001 - interpreter shutdown
             pass
+
+
+TRACE_ROLLOUT_ALLOC, TRACE_ROLLOUT_FREE, TRACE_DESC_CONSUMED = 0, 1, 4
+TRACE_DECODE_BATCH, TRACE_REWARD_POSTED, TRACE_TRAJECTORY_DONE = 7, 8, 10
+
+
+class DeviceTrace:
+    """A device trace ring (rt_trace_*) of `capacity` records (power of two)."""
+
+    def __init__(self, capacity, device="cuda"):
+        import torch
+        n = lib().rt_trace_bytes(capacity)
+        if n == 0:
+            raise RuntimeErrorRT(lib().rt_last_error().decode())
+        self.capacity = capacity
+        self.buf = torch.zeros(n, dtype=torch.uint8, device=device)
+        check(lib().rt_trace_init(ctypes.c_void_p(self.buf.data_ptr()), capacity,
+                                  _stream_ptr(None)), "rt_trace_init")
+
+    def read(self, max_records=None):
+        """(records as a numpy structured array in append order, appended)."""
+        import numpy as np
+        dt = np.dtype([("tsc", "<u8"), ("type", "<u4"), ("rollout_id", "<u4"), ("seq", "<u4")])
+        n = self.capacity if max_records is None else max_records
+        out = np.zeros(n, dtype=dt)
+        total = ctypes.c_uint64()
+        check(lib().rt_trace_read(ctypes.c_void_p(self.buf.data_ptr()),
+                                  out.ctypes.data_as(ctypes.c_void_p), n, ctypes.byref(total),
+                                  _stream_ptr(None)), "rt_trace_read")
+        return out[:min(n, total.value, self.capacity)], total.value
 
 
 def logits_synth(out, vocab, seed, request_lo, token_index, logit_std, stream=None):

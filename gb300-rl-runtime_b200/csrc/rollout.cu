@@ -24,6 +24,7 @@
 // with tokens_generated++ in place of the decode chain; the drop-in launcher
 // rt_launch_rollout_worker runs that pass in a persistent single-CTA kernel.
 #include <algorithm>
+#include <cstddef>
 #include <cstdint>
 #include <cstring>
 #include <mutex>
@@ -71,6 +72,30 @@ struct SlotExt {
     uint32_t shared;  // full prefix pages at the head of the page table (shared, read-only)
 };
 
+// Device trace ring (rt_trace_*): append counter, capacity (power of two),
+// records in the reference's trace_entry_t layout.
+struct TraceRing {
+    unsigned long long head;
+    uint32_t capacity;
+    uint32_t reserved;
+    rt_trace_entry_t entries[1];  // capacity records
+};
+static_assert(offsetof(TraceRing, entries) == 16, "trace records start at 16 bytes");
+
+__device__ __forceinline__ void trace_push(TraceRing *t, uint32_t type, uint32_t rid, uint32_t seq)
+{
+    if (!t)
+        return;
+    const unsigned long long i = atomicAdd(&t->head, 1ull);
+    uint32_t *w = reinterpret_cast<uint32_t *>(&t->entries[i & (t->capacity - 1u)]);
+    const uint64_t ts = rt::globaltimer_ns();
+    w[0] = (uint32_t)ts;
+    w[1] = (uint32_t)(ts >> 32);
+    w[2] = type;
+    w[3] = rid;
+    w[4] = seq;
+}
+
 struct Dev {
     // configuration
     uint32_t max_slots, max_admit, drop, decode, reward_mode, vocab, maxp, ppriv, max_new;
@@ -108,6 +133,7 @@ struct Dev {
     float *gemm_ws;             // K-split partials of the projections
     uint64_t gemm_ws_bytes;
     uint32_t split_qkv, split_lm;
+    TraceRing *trace;           // device trace ring, or NULL
 };
 
 __device__ __forceinline__ float reward_for(const Dev &d, uint32_t request_lo, uint32_t tokens)
@@ -529,6 +555,9 @@ __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
             taken++;
             const uint32_t row = ctl->consumed++;
             ctl->admitted++;
+            const uint32_t rq_lo = (uint32_t)(rq.request_id & 0xFFFFFFFFull);
+            trace_push(d.trace, RT_TRACE_ROLLOUT_ALLOC, rq_lo, (uint32_t)slot);
+            trace_push(d.trace, RT_TRACE_DESC_CONSUMED, rq_lo, row);
             ctl->groups_ok = 0u;
             GpuRolloutSlot &rs = sh.slot[slot];
             rs.active = 1u;
@@ -621,6 +650,9 @@ __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
             rec.tokens_generated = sh.fin_tokens[k];
             rec.reward = reward_for(d, sh.fin_req[k], sh.fin_tokens[k]);
             rec.status = 0u;
+            trace_push(d.trace, RT_TRACE_REWARD_POSTED, sh.fin_req[k], sh.fin_tokens[k]);
+            trace_push(d.trace, RT_TRACE_TRAJECTORY_DONE, sh.fin_req[k], sh.fin_tokens[k]);
+            trace_push(d.trace, RT_TRACE_ROLLOUT_FREE, sh.fin_req[k], k);
             if (io.done_ring && dn_room) {
                 uint64_t *dst = reinterpret_cast<uint64_t *>(
                     &io.done_ring->slots[(dn_tail + dn_pushed) & (REQUEST_RING_SIZE - 1)]);
@@ -705,6 +737,7 @@ __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
 
     // 5. loop control
     if (s == 0) {
+        trace_push(d.trace, RT_TRACE_DECODE_BATCH, n_act, (uint32_t)ctl->passes);
         ctl->passes++;
         if (!full)
             ctl->tokens += n_act;  // full decode counts tokens when they are committed
@@ -1550,6 +1583,90 @@ extern "C" int rt_rollout_prefill(rt_rollout_t *e, uint32_t prefix_id, const uin
             return rt::cuda_fail(err, "rollout_prefill: scatter launch");
     }
     return RT_OK;
+}
+
+extern "C" size_t rt_trace_bytes(uint32_t capacity)
+{
+    if (capacity == 0 || (capacity & (capacity - 1u))) {
+        rt::set_error("trace: capacity %u must be a power of two", capacity);
+        return 0;
+    }
+    return offsetof(TraceRing, entries) + (size_t)capacity * sizeof(rt_trace_entry_t);
+}
+
+extern "C" int rt_trace_init(void *trace, uint32_t capacity, void *stream)
+{
+    if (!trace || rt_trace_bytes(capacity) == 0) {
+        rt::set_error("trace_init: needs a buffer of rt_trace_bytes(capacity)");
+        return RT_EINVAL;
+    }
+    TraceRing hdr;
+    memset(&hdr, 0, offsetof(TraceRing, entries));
+    hdr.capacity = capacity;
+    cudaError_t err = cudaMemcpyAsync(trace, &hdr, offsetof(TraceRing, entries),
+                                      cudaMemcpyHostToDevice, (cudaStream_t)stream);
+    if (err == cudaSuccess)
+        err = cudaStreamSynchronize((cudaStream_t)stream);
+    return err == cudaSuccess ? RT_OK : rt::cuda_fail(err, "trace_init");
+}
+
+extern "C" int rt_trace_read(const void *trace, rt_trace_entry_t *out, uint32_t max,
+                             uint64_t *appended, void *stream)
+{
+    if (!trace || (max && !out)) {
+        rt::set_error("trace_read: null argument");
+        return RT_EINVAL;
+    }
+    cudaStream_t s = (cudaStream_t)stream;
+    TraceRing hdr;
+    cudaError_t err = cudaMemcpyAsync(&hdr, trace, offsetof(TraceRing, entries),
+                                      cudaMemcpyDeviceToHost, s);
+    if (err == cudaSuccess)
+        err = cudaStreamSynchronize(s);
+    if (err != cudaSuccess)
+        return rt::cuda_fail(err, "trace_read: header");
+    if (appended)
+        *appended = hdr.head;
+    if (hdr.capacity == 0 || (hdr.capacity & (hdr.capacity - 1u))) {
+        rt::set_error("trace_read: the buffer was not initialised with rt_trace_init");
+        return RT_EINVAL;
+    }
+    const uint64_t avail = std::min<uint64_t>(hdr.head, hdr.capacity);
+    const uint64_t n = std::min<uint64_t>(avail, max);
+    const rt_trace_entry_t *ent =
+        reinterpret_cast<const rt_trace_entry_t *>(static_cast<const uint8_t *>(trace) +
+                                                   offsetof(TraceRing, entries));
+    // the newest n records in append order: start at head - n (mod capacity)
+    const uint64_t first = hdr.head - n;
+    const uint64_t i0 = first & (hdr.capacity - 1u);
+    const uint64_t run = std::min<uint64_t>(n, hdr.capacity - i0);
+    if (run)
+        err = cudaMemcpyAsync(out, ent + i0, run * sizeof(rt_trace_entry_t), cudaMemcpyDeviceToHost, s);
+    if (err == cudaSuccess && n > run)
+        err = cudaMemcpyAsync(out + run, ent, (n - run) * sizeof(rt_trace_entry_t),
+                              cudaMemcpyDeviceToHost, s);
+    if (err == cudaSuccess)
+        err = cudaStreamSynchronize(s);
+    return err == cudaSuccess ? RT_OK : rt::cuda_fail(err, "trace_read: records");
+}
+
+extern "C" int rt_rollout_set_trace(rt_rollout_t *e, void *trace)
+{
+    if (!e) {
+        rt::set_error("rollout_set_trace: null engine");
+        return RT_EINVAL;
+    }
+    cudaError_t err = cudaDeviceSynchronize();  // no launch of this engine in flight
+    if (err != cudaSuccess)
+        return rt::cuda_fail(err, "rollout_set_trace: sync");
+    e->d.trace = static_cast<TraceRing *>(trace);
+    if (!e->exec)
+        return RT_OK;  // a model-decode engine captures its graph at rt_rollout_set_model
+    cudaGraphExecDestroy(e->exec);
+    e->exec = nullptr;
+    cudaGraphDestroy(e->graph);
+    e->graph = nullptr;
+    return engine_build_graph(e);
 }
 
 extern "C" int rt_rollout_launch(rt_rollout_t *e, const rt_rollout_io_t *io, void *stream)

@@ -500,6 +500,44 @@ int64_t rt_host_decode_pump(CommandRing *ring, const Descriptor *descs, uint32_t
                             uint32_t n_expected, uint32_t timeout_ms);
 
 /* ------------------------------------------------------------------------
+ * Device-side trace of the rollout loop (the GPU-side trace buffer with
+ * post-hoc copyback of reference docs/tracing.md "Future").  The schedule
+ * kernel appends records in the reference's 20-byte trace_entry_t layout
+ * and event numbering (include/trace.h: tsc, type, rollout_id, seq), with
+ * tsc the GPU's globaltimer in nanoseconds:
+ *   ROLLOUT_ALLOC (request low 32, slot) and DESC_CONSUMED (request low 32,
+ *   consume index) at admission; REWARD_POSTED and TRAJECTORY_DONE
+ *   (request low 32, tokens generated) and ROLLOUT_FREE (request low 32,
+ *   slot) at retirement; DECODE_BATCH (active slots, pass) every pass.
+ * The ring lives in device memory (rt_trace_bytes(capacity), capacity a
+ * power of two); when it wraps the oldest records are overwritten.
+ * ---------------------------------------------------------------------- */
+#define RT_TRACE_ROLLOUT_ALLOC     0u
+#define RT_TRACE_ROLLOUT_FREE      1u
+#define RT_TRACE_DESC_CONSUMED     4u
+#define RT_TRACE_DECODE_BATCH      7u
+#define RT_TRACE_REWARD_POSTED     8u
+#define RT_TRACE_TRAJECTORY_DONE   10u
+
+typedef struct __attribute__((packed)) {
+    uint64_t tsc;
+    uint32_t type;
+    uint32_t rollout_id;
+    uint32_t seq;
+} rt_trace_entry_t;
+
+size_t rt_trace_bytes(uint32_t capacity);
+/* Empty the device trace ring (stream-ordered). */
+int rt_trace_init(void *trace, uint32_t capacity, void *stream);
+/* Attach a trace ring to an engine (NULL detaches); stream-ordered with its
+ * launches, it must not be called while one is in flight. */
+int rt_rollout_set_trace(rt_rollout_t *eng, void *trace);
+/* Copy the ring's records back in append order: the newest min(appended,
+ * capacity, max) of them into out; *appended = records appended in all. */
+int rt_trace_read(const void *trace, rt_trace_entry_t *out, uint32_t max, uint64_t *appended,
+                  void *stream);
+
+/* ------------------------------------------------------------------------
  * Projections of the decode step on the tensor cores (new: the reference
  * synthesises its query with one <<<1,128>>> launch per slot and step,
  * cu/model_state.cu:6-52 and cu/query_producer.cu:5-26, and has no LM
