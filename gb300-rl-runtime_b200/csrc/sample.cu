@@ -8,13 +8,13 @@
 //  1. one streaming pass (16-byte loads, eight in flight per thread): scale
 //     by 1.0f / temperature (the reference's fp32 multiply), keep each
 //     thread's maximum, detect NaN / +inf;
-//  2. tau0 = the smallest of the 16 warps' m-th largest per-thread maxima,
-//     m = ceil(nk / 16), by counting over each warp's 32 maxima.  Every warp
-//     has m row values >= its threshold, so at least nk values are >= tau0:
-//     tau0 <= the top-k cutoff (the nk-th largest value counted with
-//     multiplicity) and every survivor is >= tau0;
+//  2. each of the 16 warps ranks its 32 per-thread maxima and keeps the
+//     m = ceil(nk / 16) largest; tau0 = the nk-th largest of those 16 m
+//     values.  They are distinct row entries, so at least nk values are
+//     >= tau0: tau0 <= the top-k cutoff (the nk-th largest value counted
+//     with multiplicity) and every survivor is >= tau0;
 //  3. a second streaming pass collects the candidates (values >= tau0,
-//     typically 100-200).  A candidate survives iff fewer than nk candidates
+//     typically 50-90 for k = 50).  A candidate survives iff fewer than nk candidates
 //     are strictly larger (an all-pairs scan, 16 bytes at a time); survivors
 //     are sorted by vocabulary index (rank sort, typically k of them);
 //  4. one thread replays the reference's serial fp32 arithmetic over the
@@ -81,6 +81,7 @@ struct Smem {
     float e[kCap];                 // exponentials; keep flags before that
     uint32_t red_u[kWarpsPerRow];
     float red_f[kWarpsPerRow];
+    float top[kWarpsPerRow * 16];  // each warp's m largest per-thread maxima (m <= 16)
     uint32_t scan[kWarpsPerRow];
     uint32_t digit, need, count, token, done;
 };
@@ -351,33 +352,41 @@ __global__ void __launch_bounds__(kThr, 2) sample_rows_kernel(const SampleArgs a
     uint32_t ns = 0;
     bool sorted_ready = false;
     if (topk) {
-        // tau0: each warp's m-th largest per-thread maximum, m = ceil(nk/8),
-        // by counting over the warp's 32 maxima; tau0 = the smallest of the
-        // eight.  Each warp has m row values >= its threshold, so at least
-        // nk values are >= tau0 and tau0 <= the top-k cutoff: every
-        // survivor is >= tau0.
+        // tau0: every warp contributes its m largest per-thread maxima
+        // (m = ceil(nk / 16), so 16 m >= nk values, each from a different
+        // thread and so a different row entry); tau0 = the nk-th largest of
+        // them.  At least nk row values are >= tau0, so tau0 <= the top-k
+        // cutoff and every survivor is >= tau0.  (About 60 candidates
+        // survive the threshold at config 3, against ~140 for the smallest
+        // of the warps' m-th largest maxima.)
         const uint32_t m = (nk + kWarpsPerRow - 1) / kWarpsPerRow;
-        uint32_t gt = 0, ge = 0;
+        uint32_t gt = 0, eq_lo = 0;
 #pragma unroll
         for (int o = 0; o < 32; o++) {
             const float x = __shfl_sync(0xffffffffu, tmax, o);
             gt += x > tmax ? 1u : 0u;
-            ge += x >= tmax ? 1u : 0u;
+            eq_lo += (x == tmax && o < lane) ? 1u : 0u;
         }
-        const bool mine = tmax > -FLT_MAX && gt < m && ge >= m;
-        const unsigned who = __ballot_sync(0xffffffffu, mine);
-        const float wt = __shfl_sync(0xffffffffu, tmax, who ? __ffs(who) - 1 : 0);
-        if (lane == 0)
-            s.red_f[warp] = who ? wt : NAN;
+        const uint32_t rank = gt + eq_lo;  // unique within the warp
+        if (rank < m)
+            s.top[warp * m + rank] = tmax;
         __syncthreads();
-        float tau0 = INFINITY;
-        bool ok = true;
-#pragma unroll
-        for (int w = 0; w < kWarpsPerRow; w++) {
-            const float t = s.red_f[w];
-            ok &= !isnan(t);
-            tau0 = fminf(tau0, t);
+        const uint32_t n_top = m * kWarpsPerRow;
+        if ((uint32_t)tid < n_top) {
+            const float v = s.top[tid];
+            uint32_t g2 = 0, e2 = 0;
+            for (uint32_t i = 0; i < n_top; i++) {
+                const float x = s.top[i];
+                g2 += x > v ? 1u : 0u;
+                e2 += x >= v ? 1u : 0u;
+            }
+            if (g2 < nk && e2 >= nk)
+                s.red_f[0] = v;  // every such thread holds the same value
         }
+        __syncthreads();
+        const float tau0 = s.red_f[0];
+        // fewer than nk finite maxima: the fallback below counts the values
+        const bool ok = tau0 > -FLT_MAX;
         __syncthreads();
         if (ok) {
             // ---- pass 2: candidates >= tau0 ----
