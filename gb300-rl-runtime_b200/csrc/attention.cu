@@ -68,6 +68,7 @@ struct AttnArgs {
     float *part_ml;     // [B][Hkv][max_chunks][G][2]  (max, sum) in log2 domain
     int32_t *counters;  // [B][Hkv]
     int32_t *error;
+    uint32_t *n_counters;  // header word: counters used by this call
     unsigned long long *work_next;  // item dispenser (dynamic scheduling)
     unsigned int *work_done;        // warps that left the loop
     uint32_t num_seqs, num_q_heads, num_kv_heads, max_pages, max_chunks, chunk_pages, max_seq_len;
@@ -844,6 +845,8 @@ paged_gqa_decode_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnAr
     uint8_t *base_ptr = smem_raw + (base_u32 - raw_u32);
     const uint32_t stage0 = base_u32 + (uint32_t)(warp * kStages * kStageBytes);
 
+    if (threadIdx.x == 0 && blockIdx.x == 0)
+        *a.n_counters = a.num_seqs * a.num_kv_heads;
     if (lane == 0) {
         rt::prefetch_tensormap(&kv_map);
         for (int s = 0; s < kStages; s++)
@@ -892,7 +895,8 @@ struct Plan {
 constexpr uint32_t kDefaultGroupChunkPages = RT_ATTN_GROUP_CHUNK_PAGES;
 
 // Workspace header: error word at 0, per-warp item dispenser at 8/16, group
-// item dispenser at 24/32; arrival counters from 256.
+// item dispenser at 24/32, number of arrival counters of the last call at 40
+// (written by the sequence kernel); arrival counters from 256.
 int make_plan(const rt_attn_params_t *p, Plan *pl, const rt_attn_group_params_t *gp = nullptr)
 {
     if (!p) {
@@ -1169,6 +1173,7 @@ int launch_attention(const rt_attn_params_t *p, const rt_attn_group_params_t *gp
     args.part_ml = reinterpret_cast<float *>(ws + pl.off_ml);
     args.counters = reinterpret_cast<int32_t *>(ws + pl.off_counters);
     args.error = reinterpret_cast<int32_t *>(ws);
+    args.n_counters = reinterpret_cast<uint32_t *>(ws + 40);
     args.work_next = reinterpret_cast<unsigned long long *>(ws + 8);
     args.work_done = reinterpret_cast<unsigned int *>(ws + 16);
     args.num_q_heads = p->num_q_heads;
@@ -1247,16 +1252,19 @@ extern "C" int rt_attn_workspace_error(void *workspace, void *stream, int32_t *c
         rt::set_error("attention: null argument");
         return RT_EINVAL;
     }
-    int32_t v = 0;
+    uint32_t hdr[12] = {};
     cudaStream_t s = (cudaStream_t)stream;
-    cudaError_t e = cudaMemcpyAsync(&v, workspace, sizeof(v), cudaMemcpyDeviceToHost, s);
+    cudaError_t e = cudaMemcpyAsync(hdr, workspace, sizeof(hdr), cudaMemcpyDeviceToHost, s);
     if (e == cudaSuccess)
         e = cudaStreamSynchronize(s);
     if (e == cudaSuccess)
-        e = cudaMemsetAsync(workspace, 0, sizeof(v), s);
+        e = cudaMemsetAsync(workspace, 0, 4, s);
+    // A failed call may have left arrival counters part-counted.
+    if (e == cudaSuccess && hdr[0] != 0u && hdr[10] != 0u)
+        e = cudaMemsetAsync(static_cast<uint8_t *>(workspace) + 256, 0, (size_t)hdr[10] * 4u, s);
     if (e != cudaSuccess)
         return rt::cuda_fail(e, "attention: read error word");
-    *code = v;
+    *code = (int32_t)hdr[0];
     return RT_OK;
 }
 

@@ -150,7 +150,10 @@ int rt_paged_decode_attention_grouped(const rt_attn_params_t *p,
  * error; otherwise RT_EDEVICE-class codes: 1 = seq_len above
  * max_seq_len / page capacity, 2 = page index outside the arena,
  * 3 = pipeline wait timed out, 4 = group record breaks the contract of
- * rt_paged_decode_attention_grouped.  Synchronises the stream. */
+ * rt_paged_decode_attention_grouped.  After a non-zero code the split-K
+ * arrival counters of the last call may be left part-counted; this call
+ * clears them too, so the workspace is ready for the next call.
+ * Synchronises the stream. */
 int rt_attn_workspace_error(void *workspace, void *stream, int32_t *code);
 
 /* Grid/tile parameters the launcher picked for these params (for tests and

@@ -142,13 +142,21 @@ def test_grpo_shape(pkg, orc, cuda):
     check_oracle(orc, case, 32, 8, got)
 
 
-def test_group_contract_violation_is_flagged(pkg, cuda):
+def test_group_contract_violation_is_flagged(pkg, orc, cuda):
     """A member whose skip_pages disagrees with its group record is skipped
-    and error 4 is reported; nothing faults."""
+    and error 4 is reported; nothing faults.  Reading the error clears the
+    part-counted arrival counters: the next good call on the same workspace
+    matches the oracle."""
     case = make_grouped_case(pkg, cuda, [(4, [10, 20, 30])], [50], 32, 8, seed=9)
     q, arena, pt, lens, skip, recs, ap, P = case
-    skip = skip.copy()
-    skip[recs[0][1][1]] = 3
-    bad = (q, arena, pt, lens, skip, recs, ap, P)
+    bad_skip = skip.copy()
+    bad_skip[recs[0][1][1]] = 3
+    bad = (q, arena, pt, lens, bad_skip, recs, ap, P)
     _, attn = run_grouped(pkg, cuda, bad, 32, 8)
     assert attn.error_code() == 4
+    tab = torch.from_numpy(pkg.group_table(recs, 1).view(np.int32)).to(cuda)
+    ng = torch.tensor([len(recs)], dtype=torch.int32, device=cuda)
+    out = attn(q, arena, torch.from_numpy(pt).to(cuda), torch.from_numpy(lens).to(cuda), tab, ng,
+               torch.from_numpy(skip.view(np.int32)).to(cuda)).cpu().numpy()
+    assert attn.error_code() == 0
+    check_oracle(orc, case, 32, 8, out)
