@@ -61,7 +61,8 @@ def test_c3_bit_exact_against_reference_kernel(pkg, orc, cuda, refcuda):
 @pytest.mark.parametrize("case", ["topk_off", "topk_ge_vocab", "topk_over_256", "no_topp",
                                   "no_temperature", "k1", "small_vocab", "vocab_32768",
                                   "ties_at_cutoff", "all_equal", "neg_inf", "nan_row",
-                                  "pos_inf_row", "huge_negative"])
+                                  "pos_inf_row", "huge_negative", "clustered_top",
+                                  "clustered_top_32000"])
 def test_edge_cases_bit_exact(pkg, cuda, refcuda, case):
     R, V, T, k, p = 64, 4096, 0.8, 50, 0.9
     stride = None
@@ -69,6 +70,8 @@ def test_edge_cases_bit_exact(pkg, cuda, refcuda, case):
         V = 7
     if case == "vocab_32768":
         V, R = 32768, 32
+    if case == "clustered_top_32000":
+        V, R = 32000, 32
     logits = normal_logits(pkg, cuda, R, V, seed=hash(case) & 0xFFFF, stride=stride)
     if case == "topk_off":
         k = 0
@@ -95,6 +98,13 @@ def test_edge_cases_bit_exact(pkg, cuda, refcuda, case):
     elif case == "huge_negative":
         logits.fill_(-3.0e38)
         logits[:, 3] = -3.3e38
+    elif case.startswith("clustered_top"):
+        # The largest values all in the stream of one thread (16-byte chunks
+        # 0, 512, 1024, ... of the row): more of them than the 4 a thread
+        # keeps in the first pass, so the kernel must take its second pass.
+        idx = torch.arange(0, V // 4, 512, device=cuda)[:, None] * 4 + torch.arange(4, device=cuda)
+        idx = idx.flatten()
+        logits[:, idx] = 8.0 + torch.arange(idx.numel(), device=cuda, dtype=torch.float32) * 0.01
     rid = np.arange(R, dtype=np.uint32) + 77
     step = np.arange(R, dtype=np.uint64) * 3 + 5
     u = u24s(pkg, rid, step)
