@@ -13,8 +13,8 @@
 //     values.  They are distinct row entries, so at least nk values are
 //     >= tau0: tau0 <= the top-k cutoff (the nk-th largest value counted
 //     with multiplicity) and every survivor is >= tau0;
-//  3. a second streaming pass collects the candidates (values >= tau0,
-//     typically 50-90 for k = 50).  A candidate survives iff fewer than nk candidates
+//  3. a second pass, by the threads whose own maximum reaches tau0 only,
+//     collects the candidates (values >= tau0, typically 50-90 for k = 50).  A candidate survives iff fewer than nk candidates
 //     are strictly larger (an all-pairs scan, 16 bytes at a time); survivors
 //     are sorted by vocabulary index (rank sort, typically k of them);
 //  4. one thread replays the reference's serial fp32 arithmetic over the
@@ -389,16 +389,19 @@ __global__ void __launch_bounds__(kThr, 2) sample_rows_kernel(const SampleArgs a
         const bool ok = tau0 > -FLT_MAX;
         __syncthreads();
         if (ok) {
-            // ---- pass 2: candidates >= tau0 ----
-            stream_row(rd, V, [&](float v, uint32_t idx) {
-                if (v >= tau0) {
-                    const uint32_t pos = atomicAdd(&s.count, 1u);
-                    if (pos < (uint32_t)kCap) {
-                        s.cand_idx[pos] = idx;
-                        s.cand_val[pos] = v;
+            // ---- pass 2: candidates >= tau0, re-read only by the threads
+            // whose own maximum reaches tau0 (the others hold none: about
+            // one thread in eight re-reads its share of the row) ----
+            if (tmax >= tau0)
+                stream_row(rd, V, [&](float v, uint32_t idx) {
+                    if (v >= tau0) {
+                        const uint32_t pos = atomicAdd(&s.count, 1u);
+                        if (pos < (uint32_t)kCap) {
+                            s.cand_idx[pos] = idx;
+                            s.cand_val[pos] = v;
+                        }
                     }
-                }
-            });
+                });
             __syncthreads();
             const uint32_t nc = s.count;
             if (nc <= (uint32_t)kCap) {
