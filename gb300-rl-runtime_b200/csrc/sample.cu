@@ -68,7 +68,7 @@ __device__ __forceinline__ float key_float(uint32_t k)
     return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
 }
 
-struct Smem {
+struct __align__(16) Smem {
     union {
         uint32_t hist[kBins];
         struct {
@@ -455,32 +455,51 @@ __global__ void __launch_bounds__(kThr, 2) sample_rows_kernel(const SampleArgs a
             fast = false;
     }
     if (fast) {
-        for (uint32_t j = tid; j < ns; j += kThr)
-            s.e[j] = __expf(__fsub_rn(s.u.sorted.val[j], mx));
+        // exponentials, zero-padded to a multiple of 8: adding +0 leaves the
+        // sum and the cumulative walk unchanged, so the serial loops below
+        // can read 8 values per step
+        const uint32_t ns8 = (ns + 7u) & ~7u;
+        for (uint32_t j = tid; j < ns8; j += kThr)
+            s.e[j] = j < ns ? __expf(__fsub_rn(s.u.sorted.val[j], mx)) : 0.0f;
         __syncthreads();
         if (tid == 0) {
+            // the reference's serial fp32 order, 8 loads ahead of the adds
+            const float4 *e4 = reinterpret_cast<const float4 *>(s.e);
             float sum = 0.0f;
-            for (uint32_t j = 0; j < ns; j++)
-                sum = __fadd_rn(sum, s.e[j]);
+#pragma unroll 2
+            for (uint32_t b = 0; b < ns8 / 8u; b++) {
+                const float4 x = e4[2 * b], y = e4[2 * b + 1];
+                sum = __fadd_rn(sum, x.x);
+                sum = __fadd_rn(sum, x.y);
+                sum = __fadd_rn(sum, x.z);
+                sum = __fadd_rn(sum, x.w);
+                sum = __fadd_rn(sum, y.x);
+                sum = __fadd_rn(sum, y.y);
+                sum = __fadd_rn(sum, y.z);
+                sum = __fadd_rn(sum, y.w);
+            }
+            const float inv = topp ? __fdiv_rn(1.0f, sum) : 0.0f;
+            auto step = [&](float c, float e) {
+                return topp ? (a.fused ? __fmaf_rn(e, inv, c) : __fadd_rn(c, __fmul_rn(e, inv)))
+                            : __fadd_rn(c, __fdiv_rn(e, sum));
+            };
+            // cum never decreases, and a padding entry repeats the previous
+            // value, so the first entry with cum >= r lies below ns
             uint32_t tok = V - 1u;
             float cum = 0.0f;
-            if (topp) {
-                const float inv = __fdiv_rn(1.0f, sum);
-                for (uint32_t j = 0; j < ns; j++) {
-                    cum = a.fused ? __fmaf_rn(s.e[j], inv, cum)
-                                  : __fadd_rn(cum, __fmul_rn(s.e[j], inv));
-                    if (cum >= r) {
-                        tok = s.u.sorted.idx[j];
-                        break;
-                    }
+            for (uint32_t b = 0; b < ns8 / 8u; b++) {
+                const float4 x = e4[2 * b], y = e4[2 * b + 1];
+                const float ev[8] = {x.x, x.y, x.z, x.w, y.x, y.y, y.z, y.w};
+                int hit = -1;
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    cum = step(cum, ev[i]);
+                    if (hit < 0 && cum >= r)
+                        hit = i;
                 }
-            } else {
-                for (uint32_t j = 0; j < ns; j++) {
-                    cum = __fadd_rn(cum, __fdiv_rn(s.e[j], sum));
-                    if (cum >= r) {
-                        tok = s.u.sorted.idx[j];
-                        break;
-                    }
+                if (hit >= 0) {
+                    tok = s.u.sorted.idx[8u * b + (uint32_t)hit];
+                    break;
                 }
             }
             a.out[blockIdx.x] = tok;
