@@ -270,7 +270,13 @@ struct SchedShared {
     };
     uint32_t rq_head, rq_n;        // ring head at the start of admission, records read ahead
     uint32_t stop, n_fin;
+    // Read ahead by load_state for the first pass after it: the tokens the
+    // previous pass sampled (kAheadTokens) and the RequestRing's head and
+    // tail (kAheadRing).  A persistent caller's later passes read them live.
+    uint32_t tok[kSched];
+    uint32_t ring_head, ring_tail, ahead;
 };
+constexpr uint32_t kAheadTokens = 1u, kAheadRing = 2u;
 
 // Admission, first part (all kSched threads): the records this pass can
 // take, read ahead in one parallel round trip (nine loads per record, all
@@ -284,7 +290,11 @@ __device__ void prefetch_requests(const Dev &d, SchedShared &sh)
         uint32_t n = 0, head;
         const uint32_t free_n = free_slot_count(sh.bitmap, d.max_slots);
         const bool can = d.drop || free_n > 0u;
-        if (io.ring) {
+        if (io.ring && (sh.ahead & kAheadRing)) {
+            head = sh.ring_head;
+            if (can)
+                n = sh.ring_tail - head;
+        } else if (io.ring) {
             head = rt_load_relaxed_u32(&io.ring->cons.head);
             if (can)
                 n = rt_load_acquire_u32(&io.ring->prod.tail) - head;
@@ -297,6 +307,7 @@ __device__ void prefetch_requests(const Dev &d, SchedShared &sh)
             n = min(n, free_n + 1u);  // + 1: a stop sentinel right behind them
         sh.rq_head = head;
         sh.rq_n = n;
+        sh.ahead &= ~kAheadRing;
     }
     __syncthreads();
     if (threadIdx.x < sh.rq_n) {
@@ -320,20 +331,33 @@ __device__ __forceinline__ void copy_words(void *dst, const void *src, size_t by
 __device__ void load_state(const Dev &d, SchedShared &sh, bool with_ext)
 {
     const uint32_t s = threadIdx.x;
-    // round trip 1: io block, control block, this slot's extension
+    // round trip 1: io block, control block, this slot's extension and the
+    // token it sampled last pass
     if (s < sizeof(RtIo) / 8u)
         reinterpret_cast<uint64_t *>(&sh.io)[s] = reinterpret_cast<const uint64_t *>(d.io)[s];
     else if (s - 32u < sizeof(RtCtl) / 8u)
         reinterpret_cast<uint64_t *>(&sh.ctl)[s - 32u] = reinterpret_cast<const uint64_t *>(d.ctl)[s - 32u];
-    if (with_ext && s < d.max_slots)
+    if (with_ext && s < d.max_slots) {
         copy_words(&sh.ext[s], &d.ext[s], sizeof(SlotExt));
+        sh.tok[s] = d.tokens[s];
+    }
     __syncthreads();
-    // round trip 2: the reference state table behind io.state
+    // round trip 2: the reference state table behind io.state, and the
+    // RequestRing's head and tail
     GpuRolloutState *st = sh.io.state;
     if (s < d.max_slots)
         copy_words(&sh.slot[s], &st->slots[s], sizeof(GpuRolloutSlot));
     if (s < (GPU_MAX_ROLLOUTS + 63) / 64)
         sh.bitmap[s] = st->bitmap[s];
+    if (s == kSched - 1u) {
+        uint32_t ahead = with_ext ? kAheadTokens : 0u;
+        if (sh.io.ring) {
+            sh.ring_head = rt_load_relaxed_u32(&sh.io.ring->cons.head);
+            sh.ring_tail = rt_load_acquire_u32(&sh.io.ring->prod.tail);
+            ahead |= kAheadRing;
+        }
+        sh.ahead = ahead;
+    }
     __syncthreads();
 }
 
@@ -512,7 +536,7 @@ __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
     if (committing) {
         SlotExt &e = sh.ext[s];
         GpuRolloutSlot &rs = sh.slot[s];
-        const uint32_t tok = d.tokens[s];
+        const uint32_t tok = (sh.ahead & kAheadTokens) ? sh.tok[s] : d.tokens[s];
         const uint32_t g = rs.tokens_generated;
         if (io.traj && e.row < io.n_rows && g < d.max_new)
             io.traj[(size_t)e.row * d.max_new + g] = tok;
@@ -524,8 +548,10 @@ __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
     if (s == 0)
         sh.stop = 0u;
     const uint32_t n_commit = __syncthreads_count(committing);
-    if (s == 0)
+    if (s == 0) {
         ctl->tokens += n_commit;
+        sh.ahead &= ~kAheadTokens;
+    }
 
     // 2. admission, in source order, lowest free slot first.  The source is
     //    read ahead (prefetch_requests); a ring's head is released once.
@@ -799,9 +825,8 @@ schedule_kernel(const Dev d, cudaGraphConditionalHandle handle, int in_graph)
 
 // First write into a shared prefix's partial page: the slot's private copy
 // (one CTA; the copy is complete when this returns).
-__device__ __forceinline__ void cow_copy(const Dev &d, SlotExt &e, const int32_t *pt)
+__device__ __forceinline__ void cow_copy(const Dev &d, SlotExt &e, const int32_t *pt, int32_t cow)
 {
-    const int32_t cow = e.cow_src;
     if (cow >= 0) {
         const uint64_t page_elems = rt_page_bytes(d.hkv) / 2u;
         const uint4 *src = reinterpret_cast<const uint4 *>(d.arena + (uint64_t)cow * page_elems);
@@ -820,14 +845,17 @@ __global__ void __launch_bounds__(256) prepare_kernel(const Dev d)
     const uint32_t s = blockIdx.x;
     rt::grid_dep_wait();    // the schedule kernel's plan is complete
     rt::grid_dep_launch();  // the attention kernels may be scheduled
-    if (!d.enable[s])
-        return;
+    // the slot's flag and its extension in one round trip
     SlotExt &e = d.ext[s];
-    const int32_t *pt = d.page_table + (size_t)s * d.maxp;
-    cow_copy(d, e, pt);
+    const uint32_t en = d.enable[s];
     const uint32_t pos = e.pos, lt = e.last_token, rq = e.request_lo;
     const uint64_t seed = e.seed;
+    const int32_t cow = e.cow_src;
+    if (!en)
+        return;
+    const int32_t *pt = d.page_table + (size_t)s * d.maxp;
     const uint64_t page = (uint64_t)pt[pos >> 4];
+    cow_copy(d, e, pt, cow);
     const uint32_t row = pos & 15u;
     // new token's K and V: hkv heads x 2 planes x 128 dims, 4 per Philox block
     for (uint32_t g = threadIdx.x; g < d.hkv * 2u * 32u; g += blockDim.x) {
@@ -876,11 +904,13 @@ __global__ void __launch_bounds__(256) model_prepare_kernel(const Dev d)
     const uint32_t s = blockIdx.x;
     rt::grid_dep_wait();  // the QKV projection is complete
     rt::grid_dep_launch();
-    if (!d.enable[s])
-        return;
     SlotExt &e = d.ext[s];
+    const uint32_t en = d.enable[s];
+    const int32_t cow = e.cow_src;
+    if (!en)
+        return;
     const int32_t *pt = d.page_table + (size_t)s * d.maxp;
-    cow_copy(d, e, pt);
+    cow_copy(d, e, pt, cow);
     const float4 *row = reinterpret_cast<const float4 *>(d.qkv + (size_t)s * d.qkv_n);
     const uint32_t nq4 = d.hq * 32u;  // q: hq heads x 128 dims, 4 per float4
     for (uint32_t g = threadIdx.x; g < nq4; g += blockDim.x) {
