@@ -275,6 +275,10 @@ struct SchedShared {
     // tail (kAheadRing).  A persistent caller's later passes read them live.
     uint32_t tok[kSched];
     uint32_t ring_head, ring_tail, ahead;
+    // this pass's admissions (full decode): slot and prefix id, for the
+    // parallel page-table fill that follows the serial admission loop
+    uint32_t adm_slot[kSched], adm_pfx[kSched];
+    uint32_t n_adm;
 };
 constexpr uint32_t kAheadTokens = 1u, kAheadRing = 2u;
 
@@ -557,6 +561,7 @@ __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
     //    read ahead (prefetch_requests); a ring's head is released once.
     prefetch_requests(d, sh);
     if (s == 0) {
+        sh.n_adm = 0u;
         uint32_t taken = 0;  // source records consumed this pass
         for (uint32_t a = 0; a < d.max_admit; a++) {
             // the read-ahead covers every record this pass can take
@@ -599,33 +604,56 @@ __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
             rs.top_k = rq.top_k;
             rs.top_p = rq.top_p;
             if (full) {
+                // the slot's page table and context are filled in parallel below
                 SlotExt &e = sh.ext[slot];
                 const uint32_t pfx = RT_REQUEST_PREFIX(rq.request_id);
-                uint32_t ctx = 0, np = 0, off = 0;
-                if (pfx != 0u && pfx - 1u < d.max_prefixes) {
-                    ctx = d.pf_len[pfx - 1u];
-                    np = d.pf_np[pfx - 1u];
-                    off = d.pf_off[pfx - 1u];
-                }
-                // keep the context inside the page table / private pages
-                const uint32_t cap = d.maxp * 16u;
-                if (ctx > cap)
-                    ctx = cap;
                 e.row = row;
                 e.prefix = (pfx != 0u && pfx - 1u < d.max_prefixes) ? pfx : 0u;
                 e.request_lo = rs.request_id;
-                e.ctx_len = ctx;
-                e.pos = ctx;
                 e.last_token = 0u;
                 e.decoding = 0u;
                 e.seed = rq.rng_seed;
-                int32_t *pt = d.page_table + (size_t)slot * d.maxp;
-                const int32_t *priv = d.priv + (size_t)slot * d.ppriv;
-                const uint32_t full_pages = ctx / 16u;
-                for (uint32_t i = 0; i < full_pages && i < np; i++)
-                    pt[i] = d.pf_pages[off + i];
-                e.shared = e.prefix ? min(full_pages, np) : 0u;
-                uint32_t next = 0;
+                sh.adm_slot[sh.n_adm] = (uint32_t)slot;
+                sh.adm_pfx[sh.n_adm] = e.prefix;
+                sh.n_adm++;
+            }
+        }
+        if (io.ring && taken)
+            rt_store_release_u32(&io.ring->cons.head, sh.rq_head + taken);
+    }
+    __syncthreads();
+    // Admitted slots' context and page tables, one warp per slot: the
+    // prefix's pages first (up to its full pages), then the slot's private
+    // pages; a partial last prefix page is copied on the first write.
+    if (full) {
+        const uint32_t lane = s & 31u, warp = s >> 5;
+        for (uint32_t k = warp; k < sh.n_adm; k += kSched / 32u) {
+            const uint32_t slot = sh.adm_slot[k], pfx = sh.adm_pfx[k];
+            uint32_t ctx = 0, np = 0, off = 0;
+            if (pfx != 0u) {
+                ctx = d.pf_len[pfx - 1u];
+                np = d.pf_np[pfx - 1u];
+                off = d.pf_off[pfx - 1u];
+            }
+            // keep the context inside the page table / private pages
+            const uint32_t cap = d.maxp * 16u;
+            if (ctx > cap)
+                ctx = cap;
+            int32_t *pt = d.page_table + (size_t)slot * d.maxp;
+            const int32_t *priv = d.priv + (size_t)slot * d.ppriv;
+            const uint32_t full_pages = ctx / 16u;
+            const uint32_t n_pf = min(full_pages, np);
+            for (uint32_t i = lane; i < n_pf; i += 32u)
+                pt[i] = d.pf_pages[off + i];
+            // private pages fill entries full_pages .. maxp - 1, at most ppriv of them
+            const uint32_t n_pv = min(d.maxp - min(full_pages, d.maxp), d.ppriv);
+            for (uint32_t j = lane; j < n_pv; j += 32u)
+                pt[full_pages + j] = priv[j];
+            if (lane == 0) {
+                SlotExt &e = sh.ext[slot];
+                e.ctx_len = ctx;
+                e.pos = ctx;
+                e.shared = pfx ? n_pf : 0u;
                 if ((ctx & 15u) && full_pages < np) {
                     e.cow_src = d.pf_pages[off + full_pages];
                     e.cow_rows = ctx & 15u;
@@ -633,14 +661,10 @@ __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
                     e.cow_src = -1;
                     e.cow_rows = 0u;
                 }
-                for (uint32_t i = full_pages; i < d.maxp && next < d.ppriv; i++)
-                    pt[i] = priv[next++];
             }
         }
-        if (io.ring && taken)
-            rt_store_release_u32(&io.ring->cons.head, sh.rq_head + taken);
+        __syncthreads();
     }
-    __syncthreads();
     if (sh.stop)
         return true;  // reference: the sentinel ends the worker before the scan
 
