@@ -323,13 +323,36 @@ __device__ void prefetch_requests(const Dev &d, SchedShared &sh)
     __syncthreads();
 }
 
-__device__ __forceinline__ void copy_words(void *dst, const void *src, size_t bytes)
+// Copy of a table of records as one flat array of 8-byte words, word i by
+// thread i % kSched (all kSched threads call it): consecutive threads touch
+// consecutive words, so every warp access is coalesced, where a record per
+// thread (72 bytes apart) made each access touch 32 separate sectors.  A
+// thread's words are all loaded before any is stored, so its loads are in
+// flight together.
+constexpr uint32_t kCopyWords = 12;  // words per thread: up to 12 x 8 x kSched bytes
+__device__ __forceinline__ void copy_table(void *dst, const void *src, size_t bytes)
 {
     uint64_t *d = static_cast<uint64_t *>(dst);
     const uint64_t *s = static_cast<const uint64_t *>(src);
-    for (size_t i = 0; i < bytes / 8u; i++)
-        d[i] = s[i];
+    const size_t n = bytes / 8u;
+    uint64_t v[kCopyWords];
+#pragma unroll
+    for (uint32_t j = 0; j < kCopyWords; j++) {
+        const size_t i = threadIdx.x + (size_t)j * kSched;
+        if (i < n)
+            v[j] = s[i];
+    }
+#pragma unroll
+    for (uint32_t j = 0; j < kCopyWords; j++) {
+        const size_t i = threadIdx.x + (size_t)j * kSched;
+        if (i < n)
+            d[i] = v[j];
+    }
 }
+static_assert(sizeof(GpuRolloutSlot) <= 8u * kCopyWords && sizeof(SlotExt) <= 8u * kCopyWords,
+              "a table of kSched records fits kCopyWords words per thread");
+static_assert(sizeof(GpuRolloutSlot) % 8 == 0 && sizeof(SlotExt) % 8 == 0,
+              "slot records copy as whole 8-byte words");
 
 // Load the pass state (all kSched threads).
 __device__ void load_state(const Dev &d, SchedShared &sh, bool with_ext)
@@ -341,16 +364,16 @@ __device__ void load_state(const Dev &d, SchedShared &sh, bool with_ext)
         reinterpret_cast<uint64_t *>(&sh.io)[s] = reinterpret_cast<const uint64_t *>(d.io)[s];
     else if (s - 32u < sizeof(RtCtl) / 8u)
         reinterpret_cast<uint64_t *>(&sh.ctl)[s - 32u] = reinterpret_cast<const uint64_t *>(d.ctl)[s - 32u];
-    if (with_ext && s < d.max_slots) {
-        copy_words(&sh.ext[s], &d.ext[s], sizeof(SlotExt));
-        sh.tok[s] = d.tokens[s];
+    if (with_ext) {
+        copy_table(sh.ext, d.ext, (size_t)d.max_slots * sizeof(SlotExt));
+        if (s < d.max_slots)
+            sh.tok[s] = d.tokens[s];
     }
     __syncthreads();
     // round trip 2: the reference state table behind io.state, and the
     // RequestRing's head and tail
     GpuRolloutState *st = sh.io.state;
-    if (s < d.max_slots)
-        copy_words(&sh.slot[s], &st->slots[s], sizeof(GpuRolloutSlot));
+    copy_table(sh.slot, st->slots, (size_t)d.max_slots * sizeof(GpuRolloutSlot));
     if (s < (GPU_MAX_ROLLOUTS + 63) / 64)
         sh.bitmap[s] = st->bitmap[s];
     if (s == kSched - 1u) {
@@ -371,11 +394,9 @@ __device__ void store_state(const Dev &d, SchedShared &sh, bool with_ext)
     const uint32_t s = threadIdx.x;
     __syncthreads();
     GpuRolloutState *st = sh.io.state;
-    if (s < d.max_slots) {
-        copy_words(&st->slots[s], &sh.slot[s], sizeof(GpuRolloutSlot));
-        if (with_ext)
-            copy_words(&d.ext[s], &sh.ext[s], sizeof(SlotExt));
-    }
+    copy_table(st->slots, sh.slot, (size_t)d.max_slots * sizeof(GpuRolloutSlot));
+    if (with_ext)
+        copy_table(d.ext, sh.ext, (size_t)d.max_slots * sizeof(SlotExt));
     if (s < (GPU_MAX_ROLLOUTS + 63) / 64)
         st->bitmap[s] = sh.bitmap[s];
     if (s >= 32u && s - 32u < sizeof(RtCtl) / 8u)
