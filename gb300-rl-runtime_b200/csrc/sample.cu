@@ -3,7 +3,7 @@
 // Replaces reference cu/sample.cu:40-123 (sample_token: one thread, ~6 serial
 // passes over the vocabulary and an O(V*k) insertion sort) with one 512-thread
 // CTA per row, two CTAs per SM (all 256 rows of a decode pass run at once),
-// the row streamed twice (the second time from L2):
+// the row streamed once, with a second, partial read from L2:
 //
 //  1. one streaming pass (16-byte loads, eight in flight per thread): scale
 //     by 1.0f / temperature (the reference's fp32 multiply), keep each
@@ -13,13 +13,15 @@
 //     values.  They are distinct row entries, so at least nk values are
 //     >= tau0: tau0 <= the top-k cutoff (the nk-th largest value counted
 //     with multiplicity) and every survivor is >= tau0;
-//  3. a second pass, by the threads whose own maximum reaches tau0 only,
-//     collects the candidates (values >= tau0, typically 50-90 for k = 50).  A candidate survives iff fewer than nk candidates
-//     are strictly larger (an all-pairs scan, 16 bytes at a time); survivors
-//     are sorted by vocabulary index (rank sort, typically k of them);
+//  3. a second pass, by the threads whose own maximum reaches tau0 only
+//     (about one in eight), collects the candidates (values >= tau0,
+//     typically 50-90 for k = 50).  A candidate survives iff fewer than nk
+//     candidates are strictly larger (an all-pairs scan, 16 bytes at a
+//     time); survivors are sorted by vocabulary index (rank sort, typically
+//     k of them);
 //  4. one thread replays the reference's serial fp32 arithmetic over the
 //     survivors only: sum of __expf(l - max) in index order, 1.0f / sum,
-//     cumulative walk.  Entries the reference masks to -FLT_MAX contribute
+//     cumulative walk, reading the exponentials eight at a time.  Entries the reference masks to -FLT_MAX contribute
 //     __expf(-FLT_MAX - max) which is checked to be exactly 0, so skipping
 //     them leaves every fp32 sum bit-identical.
 //
