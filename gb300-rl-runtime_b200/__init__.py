@@ -15,6 +15,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "librlrt_b200.so")
 
 RT_OK, RT_EINVAL, RT_ECUDA, RT_ETIMEOUT, RT_ENOMEM, RT_EDEVICE = 0, -1, -2, -3, -4, -5
+RT_ARRIVAL_PASS, RT_ARRIVAL_NS = 0, 1
 
 # ----------------------------------------------------------------- records
 class hw_desc_t(ctypes.Structure):
@@ -131,7 +132,8 @@ class rt_rollout_io_t(ctypes.Structure):
                 ("n_requests", ctypes.c_uint32), ("done_ring", ctypes.c_void_p),
                 ("dones", ctypes.c_void_p), ("state", ctypes.c_void_p),
                 ("step_count", ctypes.c_void_p), ("trajectories", ctypes.c_void_p),
-                ("rewards", ctypes.c_void_p), ("n_rows", ctypes.c_uint32)]
+                ("rewards", ctypes.c_void_p), ("n_rows", ctypes.c_uint32),
+                ("arrival_unit", ctypes.c_uint32), ("arrivals", ctypes.c_void_p)]
 
 
 class rt_rollout_stats_t(ctypes.Structure):
@@ -222,6 +224,11 @@ _SIGS = {
                                                ctypes.POINTER(rt_rollout_profile_t), _P, _P]),
     "rt_rollout_buffers": (ctypes.c_int, [_P, ctypes.POINTER(rt_rollout_buffers_t)]),
     "rt_reward_score": (ctypes.c_int, [_P, ctypes.c_uint32, _P, _P]),
+    "rt_kv_branch_resolve": (ctypes.c_int, [_P, _P, _P, ctypes.c_uint32, _P]),
+    "rt_paged_decode_attention_noalloc": (ctypes.c_int, [ctypes.POINTER(rt_attn_params_t)]
+                                          + [_P] * 6),
+    "rt_paged_decode_attention_noalloc_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int32),
+                                                               _P]),
     "rt_grpo_advantages": (ctypes.c_int, [_P, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_float,
                                           _P, _P]),
     "rt_nccl_unique_id": (ctypes.c_int, [_P]),
@@ -236,6 +243,8 @@ _SIGS = {
     "rt_rollout_worker_stats": (ctypes.c_int, [_P, ctypes.POINTER(rt_rollout_stats_t)]),
     "rt_host_pump": (ctypes.c_int64, [_P, _P, ctypes.c_uint32, _P, _P, ctypes.c_uint32,
                                       ctypes.c_int, ctypes.c_uint32]),
+    "rt_host_pump_paced": (ctypes.c_int64, [_P, _P, _P, ctypes.c_uint32, _P, _P, _P,
+                                            ctypes.c_uint32, ctypes.c_int, ctypes.c_uint32]),
     "rt_launch_decode_worker": (ctypes.c_int, [_P, ctypes.POINTER(KVArena), _P, _P, _P, _P,
                                                ctypes.c_uint32, _P, ctypes.c_uint32,
                                                ctypes.c_uint32, _P]),
@@ -524,36 +533,41 @@ class RolloutEngine:
 
     @staticmethod
     def _io(ring, requests, n_requests, done_ring, dones, state, step_count, trajectories,
-            rewards, n_rows):
+            rewards, n_rows, arrivals=None, arrival_unit=RT_ARRIVAL_PASS):
         ptr = lambda t: None if t is None else (t if isinstance(t, int) else t.data_ptr())
         return rt_rollout_io_t(ptr(ring), ptr(requests), n_requests, ptr(done_ring), ptr(dones),
                                ptr(state), ptr(step_count), ptr(trajectories), ptr(rewards),
-                               n_rows)
+                               n_rows, arrival_unit, ptr(arrivals))
 
     def launch(self, *, requests=None, n_requests=0, ring=None, done_ring=None, dones=None,
                state=None, step_count=None, trajectories=None, rewards=None, n_rows=0,
-               stream=None):
+               arrivals=None, arrival_unit=RT_ARRIVAL_PASS, stream=None):
+        """rt_rollout_launch.  arrivals: optional uint64 device tensor, one
+        arrival per request of an array source, in passes (RT_ARRIVAL_PASS)
+        or ns since the first pass (RT_ARRIVAL_NS)."""
         io = self._io(ring, requests, n_requests, done_ring, dones, state, step_count,
-                      trajectories, rewards, n_rows)
+                      trajectories, rewards, n_rows, arrivals, arrival_unit)
         check(lib().rt_rollout_launch(self.h, ctypes.byref(io), _stream_ptr(stream)),
               "rt_rollout_launch")
 
     def profile(self, *, requests=None, n_requests=0, dones=None, state=None, trajectories=None,
-                rewards=None, n_rows=0, stream=None):
+                rewards=None, n_rows=0, arrivals=None, arrival_unit=RT_ARRIVAL_PASS,
+                stream=None):
         """rt_rollout_profile: host-stepped replay with per-kernel CUDA events."""
         io = self._io(None, requests, n_requests, None, dones, state, None, trajectories,
-                      rewards, n_rows)
+                      rewards, n_rows, arrivals, arrival_unit)
         out = rt_rollout_profile_t()
         check(lib().rt_rollout_profile(self.h, ctypes.byref(io), _stream_ptr(stream),
                                        ctypes.byref(out)), "rt_rollout_profile")
         return out.as_dict()
 
     def step(self, hook, *, requests=None, n_requests=0, dones=None, state=None,
-             trajectories=None, rewards=None, n_rows=0, stream=None):
+             trajectories=None, rewards=None, n_rows=0, arrivals=None,
+             arrival_unit=RT_ARRIVAL_PASS, stream=None):
         """rt_rollout_profile_hook: host-stepped replay calling hook(pass) after
         every pass; a truthy return stops it."""
         io = self._io(None, requests, n_requests, None, dones, state, None, trajectories,
-                      rewards, n_rows)
+                      rewards, n_rows, arrivals, arrival_unit)
         out = rt_rollout_profile_t()
         err = []
 
@@ -676,6 +690,28 @@ class HostRings:
                                self.done, out.ctypes.data_as(ctypes.c_void_p), n_expected,
                                1 if send_sentinel else 0, timeout_ms)
         return n, out
+
+    def pump_paced(self, requests, arrival_ns, n_expected, send_sentinel=True,
+                   timeout_ms=60000):
+        """rt_host_pump_paced: push request i no earlier than arrival_ns[i]
+        after the call starts; returns (n drained, RolloutDone bytes, drain
+        time of each record in ns on the same clock)."""
+        import numpy as np
+        reqs = np.ascontiguousarray(requests)
+        if reqs.nbytes % 34:
+            raise ValueError("requests must be whole 34-byte RolloutRequest records")
+        n_req = reqs.nbytes // 34
+        arr = np.ascontiguousarray(arrival_ns, dtype=np.uint64)
+        if arr.size != n_req:
+            raise ValueError("one arrival per request")
+        out = np.zeros(max(n_expected, 1) * 24, dtype=np.uint8)
+        t = np.zeros(max(n_expected, 1), dtype=np.uint64)
+        n = lib().rt_host_pump_paced(self.req, reqs.ctypes.data_as(ctypes.c_void_p),
+                                     arr.ctypes.data_as(ctypes.c_void_p), n_req, self.done,
+                                     out.ctypes.data_as(ctypes.c_void_p),
+                                     t.ctypes.data_as(ctypes.c_void_p), n_expected,
+                                     1 if send_sentinel else 0, timeout_ms)
+        return n, out, t
 
     def close(self):
         if self.req:

@@ -1282,11 +1282,43 @@ namespace {
 constexpr size_t kStaticScratchBytes = (size_t)32 << 20;  // 32 MiB per device
 __device__ __align__(256) uint8_t g_attn_static_scratch[kStaticScratchBytes];
 
-// Device address of g_attn_static_scratch, resolved once per device.
+// Device address of g_attn_static_scratch, resolved once per device and
+// context.  In host code the symbol names a host-side stand-in, not device
+// memory, so the kernels must be given this address.  The cache is keyed by
+// the driver's context id as well as the device, so a context created after
+// cudaDeviceReset (where the library's module, and the array, are loaded
+// afresh) gets its own lookup instead of a stale address.
+typedef int (*ctx_get_current_fn)(void **ctx);
+typedef int (*ctx_get_id_fn)(void *ctx, unsigned long long *id);
+
+// Id of the calling thread's current context; false when none is current
+// yet (before the first runtime call on the device) or the driver entry
+// points are unavailable.
+bool current_context_id(unsigned long long *id)
+{
+    static ctx_get_current_fn get_current = nullptr;
+    static ctx_get_id_fn get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<ctx_get_current_fn>(f);
+        f = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<ctx_get_id_fn>(f);
+    });
+    void *ctx = nullptr;
+    return get_current && get_id && get_current(&ctx) == 0 && ctx && get_id(ctx, id) == 0;
+}
+
 int static_scratch_ptr(void **out)
 {
     static std::mutex mu;
     static void *ptrs[64] = {};
+    static unsigned long long ctx_ids[64] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess)
@@ -1295,13 +1327,22 @@ int static_scratch_ptr(void **out)
         rt::set_error("attention_noalloc: device index %d out of range", dev);
         return RT_EINVAL;
     }
+    unsigned long long ctx = 0;
+    const bool have_ctx = current_context_id(&ctx);
     std::lock_guard<std::mutex> lk(mu);
-    if (!ptrs[dev]) {
+    if (!have_ctx || !ptrs[dev] || ctx_ids[dev] != ctx) {
+        // The lookup also initialises the device's context when none is
+        // current yet; the id is read after it in that case.
         void *p = nullptr;
         e = cudaGetSymbolAddress(&p, g_attn_static_scratch);
         if (e != cudaSuccess)
             return rt::cuda_fail(e, "attention_noalloc: cudaGetSymbolAddress");
+        if (!have_ctx && !current_context_id(&ctx)) {
+            rt::set_error("attention_noalloc: cannot identify the current CUDA context");
+            return RT_ECUDA;
+        }
         ptrs[dev] = p;
+        ctx_ids[dev] = ctx;
     }
     *out = ptrs[dev];
     return RT_OK;
@@ -1335,4 +1376,17 @@ extern "C" int rt_paged_decode_attention_noalloc(const rt_attn_params_t *p, cons
         return rt::cuda_fail(e, "attention_noalloc: clear counters");
     return rt_paged_decode_attention(p, q, kv_arena, page_table, seq_lens, out, scratch,
                                      kStaticScratchBytes, stream);
+}
+
+extern "C" int rt_paged_decode_attention_noalloc_error(int32_t *code, void *stream)
+{
+    if (!code) {
+        rt::set_error("attention_noalloc_error: null code");
+        return RT_EINVAL;
+    }
+    void *scratch = nullptr;
+    const int rc = static_scratch_ptr(&scratch);
+    if (rc != RT_OK)
+        return rc;
+    return rt_attn_workspace_error(scratch, stream, code);
 }

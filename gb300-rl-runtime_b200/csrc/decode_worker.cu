@@ -414,6 +414,7 @@ __device__ void pump_loop(const DwArgs &a, uint32_t lane)
     head = __shfl_sync(0xFFFFFFFFu, head, 0);
     ctail = __shfl_sync(0xFFFFFFFFu, ctail, 0);
     chead = __shfl_sync(0xFFFFFFFFu, chead, 0);
+    __syncwarp();  // every lane's ring accesses after lane 0's acquire
     uint32_t tail_seen = head;  // last prod.tail observed: records below it are published
     uint32_t published = 0, drained = 0, sentinels = 0;
     unsigned long long consumed = 0;
@@ -437,6 +438,10 @@ __device__ void pump_loop(const DwArgs &a, uint32_t lane)
                 if (lane == 0)
                     t = rt_load_acquire_u32(&a.ring->prod.tail);
                 tail_seen = __shfl_sync(0xFFFFFFFFu, t, 0);
+                // __shfl_sync moves the value but orders no memory; the warp
+                // barrier puts every lane's record loads below after lane 0's
+                // acquire of the tail.
+                __syncwarp();
             }
             const uint32_t avail = tail_seen - head;
             if (avail > (uint32_t)RING_SIZE) {  // the host broke the ring contract
@@ -485,6 +490,7 @@ __device__ void pump_loop(const DwArgs &a, uint32_t lane)
                     if (lane == 0)
                         chead = rt_load_acquire_u32(&a.comp->cons.head);
                     chead = __shfl_sync(0xFFFFFFFFu, chead, 0);
+                    __syncwarp();  // slot stores below after lane 0's acquire
                     room = (uint32_t)COMP_RING_SIZE - (ctail - chead);
                 }
                 ring_full = room < k;
@@ -654,6 +660,9 @@ __device__ void worker_loop(const DwArgs &a, uint8_t *stage, uint32_t lane)
             }
         }
         have = __shfl_sync(0xFFFFFFFFu, have, 0);
+        // orders the other lanes' queue reads after lane 0's acquire of
+        // `published` (a shuffle alone orders no memory)
+        __syncwarp();
         if (!have)
             break;
         t = __shfl_sync(0xFFFFFFFFu, t, 0);

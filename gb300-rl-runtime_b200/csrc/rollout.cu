@@ -52,10 +52,14 @@ struct RtIo {
     uint32_t *traj;
     float *rewards;
     uint32_t n_rows;
+    uint32_t arrival_unit;      // RT_ARRIVAL_* of `arrivals`
+    const uint64_t *arrivals;   // array source: per-request arrival gate, or NULL
 };
+static_assert(sizeof(RtIo) % 8 == 0 && sizeof(RtIo) / 8 <= 32, "RtIo is copied by one warp");
 
 struct RtCtl {
     unsigned long long passes, tokens, idle_since;
+    unsigned long long t0;  // globaltimer at the first pass (arrival clock origin)
     uint32_t consumed, admitted, dropped, done, max_active, sentinel;
     int32_t error;
     uint32_t stop;
@@ -269,6 +273,8 @@ struct SchedShared {
         };
     };
     uint32_t rq_head, rq_n;        // ring head at the start of admission, records read ahead
+    uint32_t rq_late;              // first read-ahead record that has not arrived yet
+    unsigned long long now;        // arrival clock of this pass (passes or ns since t0)
     uint32_t stop, n_fin;
     // Read ahead by load_state for the first pass after it: the tokens the
     // previous pass sampled (kAheadTokens) and the RequestRing's head and
@@ -311,7 +317,11 @@ __device__ void prefetch_requests(const Dev &d, SchedShared &sh)
             n = min(n, free_n + 1u);  // + 1: a stop sentinel right behind them
         sh.rq_head = head;
         sh.rq_n = n;
+        sh.rq_late = n;
         sh.ahead &= ~kAheadRing;
+        if (io.arrivals && !io.ring)
+            sh.now = io.arrival_unit == RT_ARRIVAL_NS ? rt::globaltimer_ns() - sh.ctl.t0
+                                                      : sh.ctl.passes;
     }
     __syncthreads();
     if (threadIdx.x < sh.rq_n) {
@@ -319,7 +329,14 @@ __device__ void prefetch_requests(const Dev &d, SchedShared &sh)
             io.ring ? &io.ring->slots[(sh.rq_head + threadIdx.x) & (REQUEST_RING_SIZE - 1)]
                     : &io.reqs[sh.rq_head + threadIdx.x];
         load_request(src, &sh.rq_buf[threadIdx.x]);
+        // Arrival gate (array source): requests are taken in order, so the
+        // pass may admit only those before the first one still to arrive.
+        if (io.arrivals && !io.ring && io.arrivals[sh.rq_head + threadIdx.x] > sh.now)
+            atomicMin(&sh.rq_late, threadIdx.x);
     }
+    __syncthreads();
+    if (threadIdx.x == 0)
+        sh.rq_n = sh.rq_late;
     __syncthreads();
 }
 
@@ -570,8 +587,11 @@ __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
         e.last_token = tok;
         e.decoding = 0u;
     }
-    if (s == 0)
+    if (s == 0) {
         sh.stop = 0u;
+        if (ctl->passes == 0ull)
+            ctl->t0 = rt::globaltimer_ns();
+    }
     const uint32_t n_commit = __syncthreads_count(committing);
     if (s == 0) {
         ctl->tokens += n_commit;
@@ -1770,6 +1790,10 @@ static int rollout_setup(rt_rollout_t *e, const rt_rollout_io_t *io, cudaStream_
         rt::set_error("rollout_launch: give either a request ring or a request array");
         return RT_EINVAL;
     }
+    if (io->arrivals && (io->ring || io->arrival_unit > RT_ARRIVAL_NS)) {
+        rt::set_error("rollout_launch: arrivals gate an array source only, in passes or ns");
+        return RT_EINVAL;
+    }
     // Pageable staging: cudaMemcpyAsync copies it before returning, so a
     // later launch cannot overwrite the block of an earlier one in flight.
     RtIo stage;
@@ -1784,6 +1808,8 @@ static int rollout_setup(rt_rollout_t *e, const rt_rollout_io_t *io, cudaStream_
     x->traj = io->trajectories;
     x->rewards = io->rewards;
     x->n_rows = io->n_rows;
+    x->arrival_unit = io->arrival_unit;
+    x->arrivals = io->ring ? nullptr : io->arrivals;
     cudaError_t err = cudaMemcpyAsync(e->d.io, x, sizeof(RtIo), cudaMemcpyHostToDevice, s);
     if (err == cudaSuccess)
         err = cudaMemsetAsync(e->d.ctl, 0, sizeof(RtCtl), s);

@@ -90,16 +90,26 @@ int rt_paged_decode_attention(const rt_attn_params_t *p,
  * The split-K scratch is a 32 MiB array in the library's own device memory
  * (every GPU that loads the library holds it until exit); shapes needing
  * more (rt_attn_workspace_bytes > 32 MiB) are rejected with RT_ENOMEM.  It
- * calls no allocator.  The first call on a device looks up the array's
- * address with that device current; make that first call before any stream
- * capture.  All calls share the one array and each call clears its counters,
- * so calls that overlap on the GPU (any streams) race and must be
- * serialised by the caller.  Index errors are still caught on the device but
- * are not reported by this variant. */
+ * calls no allocator.  The first call on a device (and the first after a
+ * cudaDeviceReset there) looks up the array's address with that device
+ * current; make that first call before any stream capture.  All calls share
+ * the one array and each call clears its error word and counters, so calls
+ * that overlap on the GPU (any streams) race and must be serialised by the
+ * caller.  Index errors (a page id outside the arena, a length above
+ * max_seq_len) are caught on the device, the access is clamped, and the
+ * code is kept in the array until the next call: read it with
+ * rt_paged_decode_attention_noalloc_error before calling again. */
 int rt_paged_decode_attention_noalloc(const rt_attn_params_t *p,
                                       const void *q, const void *kv_arena,
                                       const int32_t *page_table, const int32_t *seq_lens,
                                       float *out, void *stream);
+
+/* Error word of the last rt_paged_decode_attention_noalloc call on the
+ * current device, with the codes of rt_attn_workspace_error; reads and
+ * clears it (and any part-counted arrival counters) in the built-in array.
+ * Allocates nothing; synchronises the stream.  No counterpart in the
+ * reference. */
+int rt_paged_decode_attention_noalloc_error(int32_t *code, void *stream);
 
 /* Shared-prefix ("cascade") decode attention.  In a GRPO group every
  * rollout starts from the same prompt, so its sequences' page tables begin
@@ -237,6 +247,9 @@ uint32_t rt_sample_uniform24(uint64_t seed, uint32_t rollout_id, uint64_t step);
  *      rng_seed, counter = (token index, request low 32)), fused sampling
  *      with the slot's temperature/top_k/top_p;
  *      RT_ROLLOUT_DECODE_NONE: no math (the reference's counter).
+ * An array source may carry per-request arrival times (rt_rollout_io_t
+ * arrivals): a request is admitted no earlier than its arrival, which
+ * replays an open-loop arrival process (e.g. Poisson) on the device.
  * A request routes to a shared prefix through request_id bits 32..63
  * (prefix id + 1, see request.h); the prefix's pages are registered with
  * rt_rollout_set_prefix.  Token ids land in `trajectories` row r =
@@ -251,6 +264,8 @@ uint32_t rt_sample_uniform24(uint64_t seed, uint32_t rollout_id, uint64_t step);
 #define RT_PREFIX_ATTN_GROUPED       0u  /* default: rt_paged_decode_attention_grouped over
                                            groups of slots with the same prefix */
 #define RT_PREFIX_ATTN_PER_SEQUENCE  1u  /* rt_paged_decode_attention, every slot on its own */
+#define RT_ARRIVAL_PASS  0u  /* arrivals[i] is a pass index (0 = the first pass): deterministic */
+#define RT_ARRIVAL_NS    1u  /* arrivals[i] is ns of GPU global time since the first pass began */
 
 typedef struct {
     uint32_t num_q_heads;       /* 32 */
@@ -284,6 +299,12 @@ typedef struct {
     uint32_t *trajectories;            /* device [n_rows][max_new_tokens], may be NULL */
     float *rewards;                    /* device [n_rows], may be NULL */
     uint32_t n_rows;
+    uint32_t arrival_unit;             /* RT_ARRIVAL_* of `arrivals` */
+    const uint64_t *arrivals;          /* array source only: device [n_requests] or NULL.
+                                          Request i may be admitted only in a pass that
+                                          starts at or after arrivals[i]; requests are
+                                          taken in order, so a request that has not
+                                          arrived holds back the ones behind it. */
 } rt_rollout_io_t;
 
 typedef struct {
@@ -413,6 +434,15 @@ int rt_logits_synth(float *out, uint32_t vocab, uint64_t seed, uint32_t request_
 int64_t rt_host_pump(RequestRing *rq, const RolloutRequest *reqs, uint32_t n, DoneRing *dn,
                      RolloutDone *dones, uint32_t n_expected, int send_sentinel,
                      uint32_t timeout_ms);
+
+/* rt_host_pump with open-loop pacing: request i is pushed no earlier than
+ * arrival_ns[i] nanoseconds (CLOCK_MONOTONIC) after the call starts, in
+ * order (arrival_ns non-decreasing; NULL = as fast as the ring allows).
+ * When done_ns is given, done_ns[k] receives the time, on the same clock,
+ * at which dones[k] was drained.  Returns as rt_host_pump. */
+int64_t rt_host_pump_paced(RequestRing *rq, const RolloutRequest *reqs, const uint64_t *arrival_ns,
+                           uint32_t n, DoneRing *dn, RolloutDone *dones, uint64_t *done_ns,
+                           uint32_t n_expected, int send_sentinel, uint32_t timeout_ms);
 
 /* Drop-in for the reference launch
  *     rollout_worker<<<1, 32>>>(req_ring, done_ring, state, step_count)
@@ -578,6 +608,23 @@ int rt_gemm_bf16(const rt_gemm_params_t *p, const void *A, const void *B, float 
  * (descs[i].token_count & 0xFF) / 255 for i < n (device pointers; scores
  * may be NULL). */
 int rt_reward_score(RewardDesc *descs, uint32_t n, float *scores, void *stream);
+
+/* ------------------------------------------------------------------------
+ * Device-side branch resolution over the copy-on-write prefix table
+ * (replaces reference cu/kv_prefix.cu:17-23, kv_branch_resolve, and its
+ * d_kv_branch_total_offset, cu/kv_prefix.cu:4-15).
+ *
+ * `table` is a KVPrefixTable (kv_prefix.h) in device or mapped memory, the
+ * host table's bytes unchanged; branch_ids uint32 [n] and out_offsets int64
+ * [n] are device pointers.  out_offsets[i] is
+ *   -1                           if branch_ids[i] >= MAX_BRANCHES,
+ *   branch.delta_kv_offset       if the branch's prefix id >= MAX_PREFIXES
+ *                                or that prefix's refcnt is 0,
+ *   prefix.kv_block_offset       otherwise.
+ * These are the device kernel's semantics; the host kv_branch_total_offset
+ * returns the prefix's offset whatever its refcount. */
+int rt_kv_branch_resolve(const KVPrefixTable *table, const uint32_t *branch_ids,
+                         int64_t *out_offsets, uint32_t n, void *stream);
 
 /* A_i = (r_i - mean_g) / (std_g + eps) over consecutive groups of G,
  * population std; per group: fp32 sum in index order, mean = sum / G,

@@ -422,11 +422,18 @@ orc_sample_row(const float *logits, uint32_t V, float temperature, uint32_t top_
 }
 
 /* ------------------------------------------------------------ scheduler */
+/* Lowest free slot (reference find_free_slot, cu/gpu_scheduler.cu:4-16),
+ * restricted to slots below max_slots (the reference always has 256). */
 static int
-sched_take_slot(GpuRolloutState *st)
+sched_take_slot(GpuRolloutState *st, uint32_t max_slots)
 {
     for (int w = 0; w < (GPU_MAX_ROLLOUTS + 63) / 64; w++) {
         uint64_t free_bits = ~st->bitmap[w];
+        const uint32_t lo = (uint32_t)w * 64u;
+        if (lo >= max_slots)
+            break;
+        if (max_slots - lo < 64u)
+            free_bits &= (1ull << (max_slots - lo)) - 1ull;
         if (free_bits) {
             int b = __builtin_ctzll(free_bits);
             st->bitmap[w] |= 1ull << b;
@@ -441,10 +448,16 @@ orc_scheduler_run(const RolloutRequest *reqs, uint32_t n_reqs,
                   const uint32_t *arrival_pass, uint32_t max_admit,
                   int drop_when_full, uint32_t max_passes,
                   RolloutDone *dones, uint32_t *done_pass,
-                  GpuRolloutState *st, uint32_t *passes_run)
+                  GpuRolloutState *st, uint32_t *passes_run, uint32_t *admit_pass,
+                  uint32_t max_slots)
 {
+    if (max_slots == 0 || max_slots > GPU_MAX_ROLLOUTS)
+        max_slots = GPU_MAX_ROLLOUTS;
     uint32_t next = 0, nd = 0, pass = 0, active = 0;
     memset(st, 0, sizeof(*st));
+    if (admit_pass)
+        for (uint32_t i = 0; i < n_reqs; i++)
+            admit_pass[i] = UINT32_MAX;
     for (pass = 0; pass < max_passes; pass++) {
         int stop = 0;
         for (uint32_t a = 0; a < max_admit; a++) {
@@ -456,7 +469,7 @@ orc_scheduler_run(const RolloutRequest *reqs, uint32_t n_reqs,
                 stop = 1;
                 break;
             }
-            int s = sched_take_slot(st);
+            int s = sched_take_slot(st, max_slots);
             if (s < 0) {
                 if (drop_when_full) {
                     next++;
@@ -464,6 +477,8 @@ orc_scheduler_run(const RolloutRequest *reqs, uint32_t n_reqs,
                 }
                 break;
             }
+            if (admit_pass)
+                admit_pass[next] = pass;
             next++;
             GpuRolloutSlot *rs = &st->slots[s];
             rs->active = 1;

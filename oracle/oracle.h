@@ -105,7 +105,8 @@ uint32_t orc_scheduler_run(const RolloutRequest *reqs, uint32_t n_reqs,
                            const uint32_t *arrival_pass, uint32_t max_admit,
                            int drop_when_full, uint32_t max_passes,
                            RolloutDone *dones, uint32_t *done_pass,
-                           GpuRolloutState *state, uint32_t *passes_run);
+                           GpuRolloutState *state, uint32_t *passes_run,
+                           uint32_t *admit_pass, uint32_t max_slots);
 
 /* Philox U(0,1) reward of the rollout loop's RT_REWARD_PHILOX mode. */
 float orc_reward_u01(uint64_t seed, uint32_t request_lo);

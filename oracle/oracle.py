@@ -80,7 +80,7 @@ def oracle_lib() -> ctypes.CDLL:
             "orc_submit_desc": (None, [_u32, _u32, _u32, _u64, _u64, _u32, _u32, _u32, _P]),
             "orc_sample_row": (_u32, [_P, _u32, _f32, _u32, _f32, _u32, _int, _P]),
             "orc_sample_u24": (_u32, [_u64, _u32, _u64]),
-            "orc_scheduler_run": (_u32, [_P, _u32, _P, _u32, _int, _u32, _P, _P, _P, _P]),
+            "orc_scheduler_run": (_u32, [_P, _u32, _P, _u32, _int, _u32, _P, _P, _P, _P, _P, _u32]),
             "orc_grpo_advantages": (None, [_P, _u32, _u32, _f32, _P]),
             "orc_reward_u01": (_f32, [_u64, _u32]),
             "orc_decode_synth_q": (_f32, [_u64, _u64, _P, _u32]),
@@ -165,18 +165,27 @@ def sample_u24(seed, rollout_id, step) -> int:
 
 
 def scheduler_run(reqs: np.ndarray, arrival_pass=None, max_admit=1, drop_when_full=True,
-                  max_passes=1 << 20):
+                  max_passes=1 << 20, with_admit=False, max_slots=256):
+    """The reference pass loop (cu/gpu_scheduler.cu:33-82) with max_admit /
+    drop switches, an optional per-request arrival pass and a slot count
+    below the reference's 256 (lowest free slot below max_slots).  Returns (dones,
+    done pass of each, final GpuRolloutState bytes, passes run) and, with
+    with_admit, the pass in which each request was admitted (UINT32_MAX if
+    never)."""
     reqs = np.ascontiguousarray(reqs, dtype=REQUEST_DTYPE)
     n = len(reqs)
     dones = np.zeros(max(n, 1), dtype=DONE_DTYPE)
     done_pass = np.zeros(max(n, 1), dtype=np.uint32)
+    admit = np.zeros(max(n, 1), dtype=np.uint32)
     state = np.zeros(GPU_STATE_BYTES, dtype=np.uint8)
     passes = np.zeros(1, dtype=np.uint32)
     arr = None if arrival_pass is None else np.ascontiguousarray(arrival_pass, dtype=np.uint32)
     nd = oracle_lib().orc_scheduler_run(
         _ptr(reqs), n, None if arr is None else _ptr(arr), max_admit, int(drop_when_full),
-        max_passes, _ptr(dones), _ptr(done_pass), _ptr(state), _ptr(passes))
-    return dones[:nd], done_pass[:nd], state, int(passes[0])
+        max_passes, _ptr(dones), _ptr(done_pass), _ptr(state), _ptr(passes), _ptr(admit),
+        max_slots)
+    out = (dones[:nd], done_pass[:nd], state, int(passes[0]))
+    return out + (admit[:n],) if with_admit else out
 
 
 def reward_u01(seed, request_lo) -> float:
@@ -290,7 +299,45 @@ class RefCuda:
         l.hx_ref_sample_rows.argtypes = [_P, _u32, _u64, _P, _P, _P, _P, _P, _u32]
         l.hx_ref_fixed128.restype = _int
         l.hx_ref_fixed128.argtypes = [_P, _u32, _P, _u64, _P, _P, _u32, _P, _P, _P, _P, _P]
+        l.hx_ref_rollout_worker.restype = _int
+        l.hx_ref_rollout_worker.argtypes = [_P, _P, _P, _P]
+        l.hx_ref_reward_score.restype = _int
+        l.hx_ref_reward_score.argtypes = [_P, _int, _P]
+        l.hx_ref_kv_branch_resolve.restype = _int
+        l.hx_ref_kv_branch_resolve.argtypes = [_P, _P, _P, _int]
+        l.hx_ref_sizeof.restype = _u64
+        l.hx_ref_sizeof.argtypes = [_int]
         self.lib = l
+
+    def sizeof(self, what):
+        """sizeof of the reference's RequestRing (0), DoneRing (1),
+        GpuRolloutState (2), KVPrefixTable (3), RewardDesc (4)."""
+        return int(self.lib.hx_ref_sizeof(what))
+
+    def rollout_worker(self, req_ring, done_ring, state, step_count):
+        """The reference rollout_worker<<<1, 32>>> (cu/gpu_scheduler.cu:26-83,
+        unmodified) on torch uint8 device buffers holding a RequestRing
+        filled before the launch (ending with the stop sentinel), an empty
+        DoneRing, a GpuRolloutState and a uint64 step counter.  The harness
+        refuses ring contents on which the kernel could wait forever."""
+        rc = self.lib.hx_ref_rollout_worker(req_ring.data_ptr(), done_ring.data_ptr(),
+                                            state.data_ptr(), step_count.data_ptr())
+        assert rc == 0, f"reference rollout_worker not run / failed: {rc}"
+
+    def reward_score(self, descs, scores):
+        """reference reward_score_kernel (cu/reward.cu:4-15) over torch device
+        buffers: descs uint8 [n * 24] (RewardDesc), scores fp32 [n]."""
+        n = descs.numel() // 24
+        rc = self.lib.hx_ref_reward_score(descs.data_ptr(), n,
+                                          None if scores is None else scores.data_ptr())
+        assert rc == 0, f"reference reward_score_kernel failed: {rc}"
+
+    def kv_branch_resolve(self, table, ids, out):
+        """reference kv_branch_resolve (cu/kv_prefix.cu:17-23) over torch
+        device buffers: table uint8 (a KVPrefixTable), ids int32, out int64."""
+        rc = self.lib.hx_ref_kv_branch_resolve(table.data_ptr(), ids.data_ptr(), out.data_ptr(),
+                                               ids.numel())
+        assert rc == 0, f"reference kv_branch_resolve failed: {rc}"
 
     def fixed128(self, descs, arena, block_size, sample_st=None, q_buf=None, io_slots=0):
         """The reference's attention_decode_step_fixed128 (cu/attention_decode.cu,

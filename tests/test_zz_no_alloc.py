@@ -5,8 +5,10 @@ attention (a no-allocation hot path, a host that owns all device memory, a
 loop where cudaMalloc would synchronise) use this entry point: its split-K
 scratch is a fixed array inside the library.  These checks call it through
 the C ABI and compare it with the workspace entry point on the same inputs,
-twice in a row, since the array keeps the previous call's contents.  The file
-is named to be collected last and depends on no other test."""
+twice in a row, since the array keeps the previous call's contents, and
+check that the calls after the first leave device memory untouched (the
+driver's free bytes and torch's allocator).  The file is named to be
+collected last and depends on no other test."""
 import ctypes
 
 import numpy as np
@@ -46,6 +48,20 @@ def _case(pkg, dev, seed, n_seqs=24, max_len=3000):
         arena_pages
 
 
+def _call(pkg, fn, params, q, arena, pt, lens_d, out, stream):
+    rc = fn(ctypes.byref(params), q.data_ptr(), arena.data_ptr(), pt.data_ptr(),
+            lens_d.data_ptr(), out.data_ptr(), ctypes.c_void_p(stream.cuda_stream))
+    assert rc == 0, pkg.lib().rt_last_error()
+
+
+def _error(pkg, stream):
+    code = ctypes.c_int32(-99)
+    rc = pkg.lib().rt_paged_decode_attention_noalloc_error(ctypes.byref(code),
+                                                           ctypes.c_void_p(stream.cuda_stream))
+    assert rc == 0, pkg.lib().rt_last_error()
+    return code.value
+
+
 def test_noalloc_matches_workspace_entry_point_twice(pkg, cuda):
     fn = _bind(pkg)
     q, arena, pt, lens_d, lens, P, ap = _case(pkg, cuda, seed=31)
@@ -54,14 +70,46 @@ def test_noalloc_matches_workspace_entry_point_twice(pkg, cuda):
     torch.cuda.synchronize()
     assert attn.error_code() == 0
     stream = torch.cuda.current_stream()
-    for _ in range(2):
-        out = torch.full_like(want, float("nan"))
-        rc = fn(ctypes.byref(attn.params), q.data_ptr(), arena.data_ptr(), pt.data_ptr(),
-                lens_d.data_ptr(), out.data_ptr(), ctypes.c_void_p(stream.cuda_stream))
-        assert rc == 0, pkg.lib().rt_last_error()
+    outs = [torch.full_like(want, float("nan")) for _ in range(2)]
+    # the first call on the device resolves the array's address; the calls
+    # after it must leave device memory untouched (no allocation anywhere)
+    _call(pkg, fn, attn.params, q, arena, pt, lens_d, outs[0], stream)
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    torch_bytes0 = torch.cuda.memory_allocated()
+    for i in range(2):
+        out = outs[i]
+        out.fill_(float("nan"))
         torch.cuda.synchronize()
+        free_a, _ = torch.cuda.mem_get_info()
+        _call(pkg, fn, attn.params, q, arena, pt, lens_d, out, stream)
+        torch.cuda.synchronize()
+        free_b, _ = torch.cuda.mem_get_info()
+        assert free_b == free_a == free0, "device memory changed across a no-alloc call"
+        assert torch.cuda.memory_allocated() == torch_bytes0
+        assert _error(pkg, stream) == 0
         got, ref = out.cpu().numpy(), want.cpu().numpy()
         assert np.all(np.abs(got - ref) <= ATOL + RTOL * np.abs(ref))
+
+
+def test_noalloc_error_word_is_readable(pkg, cuda):
+    """A page id outside the arena is caught by the kernel's bounds check
+    (the load is clamped into the arena) and reported through
+    rt_paged_decode_attention_noalloc_error until the next call clears it."""
+    fn = _bind(pkg)
+    q, arena, pt, lens_d, lens, P, ap = _case(pkg, cuda, seed=37, n_seqs=8, max_len=400)
+    attn = pkg.PagedDecodeAttention(len(lens), 32, 8, P, int(lens.max()), ap)
+    stream = torch.cuda.current_stream()
+    out = torch.zeros(len(lens), 32, 128, dtype=torch.float32, device=cuda)
+    bad = pt.clone()
+    b = int(np.argmax(lens))
+    bad[b, 0] = ap + 5  # outside the arena
+    _call(pkg, fn, attn.params, q, arena, bad, lens_d, out, stream)
+    assert _error(pkg, stream) == 2
+    assert _error(pkg, stream) == 0  # read and cleared
+    _call(pkg, fn, attn.params, q, arena, bad, lens_d, out, stream)
+    _call(pkg, fn, attn.params, q, arena, pt, lens_d, out, stream)  # clears the earlier code
+    assert _error(pkg, stream) == 0
 
 
 def test_noalloc_rejects_shapes_beyond_its_scratch(pkg):
