@@ -2,24 +2,31 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl mine|reference]
 
-Under torchrun (N > 1) every rank runs its own shard (weak scaling: a fixed
-per-GPU share) with no data-path collective; the step time is the maximum
-over ranks.  Rank 0 prints one JSON line.
-
 Workloads (synthetic, seeded):
+  rollout    config 5 (default): 8,192 GRPO rollouts, the GPU-resident loop.
+             Under torchrun the fixed 8,192 rollouts are split by group over
+             the N GPUs (strong scaling: the total work is the same for every
+             N); the only collective is the NCCL allgather of rewards.  At
+             N = 1 the line also carries blocks for configs 2, 3 and 4.
+  rollout_c4 config 4: 1,024 rollouts with Poisson arrivals (8 per ms), a
+             shared 1,024-token copy-on-write prefix plus per-group prompts
+             of U[64,1024] tokens, max_new U[32,512] (one GPU; under
+             torchrun every rank runs its own replica: weak scaling).
   attention  config 2: paged GQA decode attention, B=64 ragged sequences
              L ~ U[128,4096], 32 q / 8 kv heads, d=128, bf16 16-token pages
-             scattered in the arena, Q/K/V ~ N(0,1).  One step = one decode
-             attention call over the batch.  Two arena copies (>1 GB in
-             total, larger than the 126 MB L2) alternate between steps.
+             scattered in the arena.  Two arena copies (> L2) alternate.
   sampling   config 3: 256 rows x 32,000 fp32 logits, fused sampling.
-  rollout    config 5 (default): GRPO rollouts, the GPU-resident loop.
-  decode_ring  the reference's per-step CommandRing benchmark (src/main.c):
-             10,000 descriptors through the decode worker and its rings.
+  decode_ring  the reference's per-step CommandRing benchmark (src/main.c).
+  lm_head, rollout_model  the model-decode extension (tensor-core GEMMs).
+  Except for rollout, every rank runs its own replica (weak scaling).
 
---impl reference times the reference path's CPU implementation (the CPU
-oracle port of the same computation; the reference has no CPU
-implementation of paged attention) on this host's cores.
+--impl reference times the CPU implementation of the same workload on this
+host's cores: the reference project has no CPU implementation of paged
+attention or of the rollout loop, so it is the CPU restatement of the
+reference's algorithms (oracle/), fed numpy inputs of the same shapes and
+distributions, without loading this runtime or touching the GPU.  Its line
+has the same config, steps and warm-up as the GPU arm; each step is a
+bounded sample of the workload.
 """
 from __future__ import annotations
 
@@ -50,7 +57,8 @@ def measured_peaks():
 
 def ncu_traffic(kernel: str, workload: str):
     """Per-launch DRAM bytes recorded from an ncu capture in profiles/ncu_traffic.txt
-    (lines: <kernel> <workload> <bytes_per_launch>); None when not recorded."""
+    (lines: <kernel> <workload> <bytes_per_launch> <commit of the capture>);
+    (None, None) when not recorded."""
     path = os.path.join(ROOT, "profiles", "ncu_traffic.txt")
     try:
         with open(path) as f:
@@ -58,10 +66,10 @@ def ncu_traffic(kernel: str, workload: str):
                 parts = line.split()
                 if (len(parts) >= 3 and not line.startswith("#") and parts[0] == kernel
                         and parts[1] == workload):
-                    return float(parts[2])
+                    return float(parts[2]), (parts[3] if len(parts) > 3 else None)
     except OSError:
         pass
-    return None
+    return None, None
 
 
 # ----------------------------------------------------------------- clocks
@@ -128,38 +136,160 @@ class ClockSampler:
                 "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
+# ------------------------------------------------- CPU ports (no GPU, no runtime)
+def _bf16_normal(rng, shape, std=1.0):
+    """bf16 bit patterns of N(0, std) values (truncated float32), generated
+    in chunks to bound the float32 temporaries."""
+    out = np.empty(int(np.prod(shape)), dtype=np.uint16)
+    step = 1 << 24
+    for i in range(0, out.size, step):
+        x = rng.standard_normal(min(step, out.size - i), dtype=np.float32)
+        if std != 1.0:
+            x *= np.float32(std)
+        out[i:i + x.size] = x.view(np.uint32) >> 16
+    return out.reshape(shape)
+
+
+_PORT_INPUTS = {}
+
+
+def _cached(key, make):
+    """Port inputs are built once per process: the reference arm calls a
+    port once per step."""
+    if key not in _PORT_INPUTS:
+        _PORT_INPUTS[key] = make()
+    return _PORT_INPUTS[key]
+
+
+def _port_rollout_decode(threads, budget_s, n_rollouts, ctx, gen, vocab, seed):
+    """The loop's decode step on the host for one GRPO group: `n_rollouts`
+    rollouts whose first ctx tokens are one shared prompt (the same page ids
+    in every page table) and whose private pages are scattered through the
+    arena; per token paged GQA attention over the whole context
+    (oracle/oracle.c, OpenMP over (rollout, kv head)), N(0, 2) logits, and
+    the reference sampling algorithm (cu/sample.cu:40-123 restated,
+    insertion top-k) per rollout on a thread pool.  Decodes until the time
+    budget is spent (at least one token).  Returns (tokens, steps, seconds)."""
+    from concurrent.futures import ThreadPoolExecutor
+    orc = ge.load_oracle()
+    B, Hq, Hkv = n_rollouts, 32, 8
+    rng = np.random.default_rng(seed)
+    shared = ctx // 16
+    own = (ctx + gen + 15) // 16 - shared
+
+    def make():
+        n_pages = shared + B * own
+        arena_pages = int(n_pages * 1.25) + 1
+        perm = rng.permutation(arena_pages).astype(np.int32)
+        pt = np.zeros((B, shared + own), dtype=np.int32)
+        pt[:, :shared] = perm[:shared]
+        pt[:, shared:] = perm[shared:shared + B * own].reshape(B, own)
+        return pt, _bf16_normal(rng, arena_pages * Hkv * 2 * 16 * 128)
+    pt, arena = _cached(("rollout", B, ctx, gen, seed), make)
+    pool = ThreadPoolExecutor(max_workers=threads)
+    t0 = time.perf_counter()
+    steps = 0
+    while steps == 0 or (time.perf_counter() - t0 < budget_s and steps < gen):
+        q = _bf16_normal(rng, (B, Hq, 128))
+        lens = np.full(B, ctx + steps + 1, dtype=np.int32)
+        orc.paged_gqa_attention(q, arena, pt, lens, Hq, Hkv, 128 ** -0.5, n_threads=threads)
+        logits = rng.standard_normal((B, vocab), dtype=np.float32) * np.float32(2.0)
+        list(pool.map(lambda b: orc.sample_row(logits[b], 0.8, 50, 0.9,
+                                               orc.sample_u24(1234, b, steps)), range(B)))
+        steps += 1
+    dt = time.perf_counter() - t0
+    pool.shutdown()
+    return B * steps, steps, dt
+
+
+def _port_result(value, unit, threads, dt, sample):
+    return {"value": value, "unit": unit, "cores": threads, "kind": "port", "seconds": dt,
+            "sample": sample}
+
+
 # ------------------------------------------------------------- workloads
-class AttentionWorkload:
+class Workload:
+    """Common surface: a GPU step plus class-level facts that the reference
+    arm uses without the GPU (static_config, cpu_port)."""
+
+    scaling = "weak"          # every rank runs its own replica
+    dtype = "bf16"
+    bound = "hbm"
+    launches_per_step = 1
+
+    @classmethod
+    def line_config(cls, args, world):
+        """The config object of both arms' JSON lines (GPU-independent)."""
+        par = (f"dp{world} (groups split by rank)" if cls.scaling == "strong"
+               else f"replicas{world}") if world > 1 else "single"
+        return cls.static_config(args, world) | {"parallelism": par}
+
+    def config(self):
+        return self.line_config(self.args, self.world)
+
+    def details(self):
+        return {}
+
+    def gpu_launches(self, steps):
+        return self.launches_per_step * steps
+
+    def check_errors(self):
+        return 0
+
+
+def _c2_inputs(rank):
+    """Config-2 lengths and scattered page table (numpy, seeded)."""
+    B = 64
+    lens = np.random.default_rng(2 + 1000 * rank).integers(128, 4097, size=B).astype(np.int32)
+    rng = np.random.default_rng(20 + rank)
+    n_pages = (lens + 15) // 16
+    P = int(n_pages.max())
+    arena_pages = int(int(n_pages.sum()) * 1.25) + 1
+    pt = np.full((B, P), -1, dtype=np.int32)
+    perm = rng.permutation(arena_pages).astype(np.int32)
+    k = 0
+    for b, n in enumerate(n_pages):
+        pt[b, :n] = perm[k:k + n]
+        k += n
+    return lens, pt, arena_pages
+
+
+class AttentionWorkload(Workload):
     """BASELINE config 2 (paged GQA decode attention)."""
 
     name = "paged_gqa_decode_attention_c2"
     kernel = "paged_gqa_decode_kernel"
+    metric = "decode-attn HBM GB/s (paged GQA, config 2)"
+    unit = "GB/s"
+    B, Hq, Hkv = 64, 32, 8
+
+    @classmethod
+    def static_config(cls, args, world):
+        return {"workload": cls.name, "batch": cls.B, "seq_len": "U[128,4096], seed 2 (+1000 x rank)",
+                "q_heads": cls.Hq, "kv_heads": cls.Hkv, "head_dim": 128, "page_tokens": 16,
+                "kv_dtype": "bf16", "pages": "scattered (random permutation of a 1.25x arena)",
+                "l2": "two arena copies alternate (2 x ~0.55 GB > 126 MB L2)",
+                "chunk_pages": args.chunk_pages or "auto"}
+
+    @staticmethod
+    def algorithmic_bytes(lens, Hq=32, Hkv=8):
+        n_pages = (lens + 15) // 16
+        return (int(lens.sum()) * Hkv * 128 * 2 * 2 + len(lens) * Hq * 128 * (2 + 4)
+                + int(n_pages.sum()) * 4)
 
     def __init__(self, args, rank, world, dev):
         import torch
+        self.args, self.world = args, world
         self.torch = torch
         self.pkg = ge.load_package()
         self.dev = dev
-        self.B, self.Hq, self.Hkv = 64, 32, 8
-        # each rank owns its own batch (seeded by rank): weak scaling
-        self.lens = np.random.default_rng(2 + 1000 * rank).integers(128, 4097, size=self.B).astype(np.int32)
-        rng = np.random.default_rng(20 + rank)
-        n_pages = (self.lens + 15) // 16
-        self.P = int(n_pages.max())
-        total = int(n_pages.sum())
-        self.arena_pages = int(total * 1.25) + 1
-        pt = np.full((self.B, self.P), -1, dtype=np.int32)
-        perm = rng.permutation(self.arena_pages).astype(np.int32)
-        k = 0
-        for b, n in enumerate(n_pages):
-            pt[b, :n] = perm[k:k + n]
-            k += n
-        self.pt_host = pt
+        self.lens, pt, self.arena_pages = _c2_inputs(rank)
+        self.P = pt.shape[1]
         self.page_table = torch.from_numpy(pt).to(dev)
         self.seq_lens = torch.from_numpy(self.lens).to(dev)
         elems = self.arena_pages * self.Hkv * 2 * 16 * 128
         self.arenas = []
-        for c in range(2):
+        for _ in range(2):
             a = torch.empty(elems, dtype=torch.bfloat16, device=dev)
             self.pkg.fill_normal_bf16(a, seed=2 + rank, stream_id=1)   # same contents, two copies
             self.arenas.append(a)
@@ -171,9 +301,8 @@ class AttentionWorkload:
                                                   int(self.lens.max()), self.arena_pages,
                                                   chunk_pages=args.chunk_pages, evict_first=True)
         self.i = 0
-        # algorithmic bytes per launch: KV once + q + out + page-table entries
         self.kv_bytes = int(self.lens.sum()) * self.Hkv * 128 * 2 * 2
-        self.bytes = (self.kv_bytes + self.B * self.Hq * 128 * (2 + 4) + int(n_pages.sum()) * 4)
+        self.bytes = self.algorithmic_bytes(self.lens)
         self.flops = 4 * self.Hq * 128 * int(self.lens.sum())
         torch.cuda.synchronize()
 
@@ -181,13 +310,8 @@ class AttentionWorkload:
         self.attn(self.q, self.arenas[self.i & 1], self.page_table, self.seq_lens, out=self.out)
         self.i += 1
 
-    launches_per_step = 1
-
     def units_per_step(self):
         return self.bytes / 1e9  # GB
-
-    metric = "decode-attn HBM GB/s (paged GQA, config 2)"
-    unit = "GB/s"
 
     def e2e(self, steps, warmup):
         """Same metric through the C ABI with host buffers: the step's query is
@@ -220,33 +344,38 @@ class AttentionWorkload:
     def check_errors(self):
         return self.attn.error_code()
 
-    def cpu_sample(self, threads, budget_s=10.0):
-        """CPU oracle port on a bounded sample: whole config-2 batches repeated
-        until the time budget is spent (at least one)."""
+    @classmethod
+    def cpu_port(cls, args, threads, budget_s):
+        """The CPU restatement (oracle/oracle.c, fp64 accumulate, OpenMP over
+        (sequence, kv head)) on config-2 inputs built with numpy: batches of
+        8 of the 64 sequences, in turn, until the budget is spent."""
         orc = ge.load_oracle()
-        torch = self.torch
-        q = self.q.view(torch.int16).cpu().numpy().view(np.uint16)
-        arena = self.arenas[0].view(torch.int16).cpu().numpy().view(np.uint16)
+
+        def make():
+            lens, pt, arena_pages = _c2_inputs(0)
+            rng = np.random.default_rng(21)
+            return (lens, pt, _bf16_normal(rng, arena_pages * cls.Hkv * 2 * 16 * 128),
+                    _bf16_normal(rng, (cls.B, cls.Hq, 128)))
+        lens, pt, arena, q = _cached("c2", make)
         t0 = time.perf_counter()
-        reps = 0
-        while reps == 0 or time.perf_counter() - t0 < budget_s:
-            orc.paged_gqa_attention(q, arena, self.pt_host, self.lens, self.Hq, self.Hkv,
-                                    128 ** -0.5, n_threads=threads)
-            reps += 1
+        done_bytes, k, seqs = 0, 0, 0
+        while k == 0 or time.perf_counter() - t0 < budget_s:
+            sl = slice(8 * (k % 8), 8 * (k % 8) + 8)
+            orc.paged_gqa_attention(q[sl], arena, pt[sl], lens[sl], cls.Hq, cls.Hkv, 128 ** -0.5,
+                                    n_threads=threads)
+            done_bytes += cls.algorithmic_bytes(lens[sl])
+            seqs += 8
+            k += 1
         dt = time.perf_counter() - t0
-        return {"value": reps * self.bytes / 1e9 / dt, "unit": self.unit, "cores": threads,
-                "kind": "port", "seconds": dt,
-                "sample": f"{reps} full config-2 batch(es) (64 sequences, {int(self.lens.sum())} tokens), "
-                          f"oracle/oracle.c fp64-accumulate restatement, OpenMP"}
+        return _port_result(done_bytes / 1e9 / dt, cls.unit, threads, dt,
+                            f"{seqs} config-2 sequences in batches of 8, oracle/oracle.c "
+                            f"fp64-accumulate restatement, OpenMP")
 
-    def config(self):
-        return {"workload": self.name, "batch": self.B, "seq_len": "U[128,4096] seed 2",
-                "q_heads": self.Hq, "kv_heads": self.Hkv, "head_dim": 128, "page_tokens": 16,
-                "kv_dtype": "bf16", "l2": "two arena copies alternate (2 x %.0f MB > 126 MB L2)"
-                % (self.kv_bytes / 1e6), "chunk_pages": self.attn.plan()[0]}
+    def details(self):
+        return {"chunk_pages_used": self.attn.plan()[0], "tokens": int(self.lens.sum())}
 
 
-class SamplingWorkload:
+class SamplingWorkload(Workload):
     """256 rows x 32,000 fp32 logits ~ N(0, 2), T=0.8,
     top-k 50, top-p 0.9, Philox seed 1234, counter = (rollout_id = row, step).
     Eight logits buffers (262 MB > 126 MB L2) rotate between steps."""
@@ -255,28 +384,34 @@ class SamplingWorkload:
     kernel = "sample_rows_kernel"
     metric = "sampling logits HBM GB/s (config 3)"
     unit = "GB/s"
-    launches_per_step = 1
+    dtype = "fp32"
+    R, V, NBUF = 256, 32000, 8
+
+    @classmethod
+    def static_config(cls, args, world):
+        return {"workload": cls.name, "rows": cls.R, "vocab": cls.V, "temperature": 0.8,
+                "top_k": 50, "top_p": 0.9, "seed": 1234, "logits": "N(0, 2)",
+                "l2": "8 logits buffers rotate (262 MB > 126 MB L2)"}
 
     def __init__(self, args, rank, world, dev):
         import torch
+        self.args, self.world = args, world
         self.torch = torch
         self.pkg = ge.load_package()
-        self.R, self.V, self.nbuf = 256, 32000, 8
         self.bufs = []
-        for i in range(self.nbuf):
+        for i in range(self.NBUF):
             t = torch.empty(self.R, self.V, dtype=torch.float32, device=dev)
             self.pkg.fill_normal_f32(t, seed=3 + rank, stream_id=100 + i, std=2.0)
             self.bufs.append(t)
         rows = self.pkg.sample_row_table(0.8, 50, 0.9, np.arange(self.R, dtype=np.uint32), 0, 1234)
-        self.rows_np = rows
         self.rows = torch.from_numpy(rows.view(np.uint8)).to(dev)
         self.out = torch.empty(self.R, dtype=torch.int32, device=dev)
-        self.bytes = self.R * self.V * 4 + self.R * (24 + 4)
+        self.bytes = self.R * self.V * 4 + self.R * (32 + 4)
         self.i = 0
         torch.cuda.synchronize()
 
     def step(self):
-        self.pkg.sample_rows(self.bufs[self.i % self.nbuf], self.rows, self.V, out=self.out)
+        self.pkg.sample_rows(self.bufs[self.i % self.NBUF], self.rows, self.V, out=self.out)
         self.i += 1
 
     def units_per_step(self):
@@ -307,32 +442,40 @@ class SamplingWorkload:
         return {"value": self.units_per_step() / (ms / 1e3), "unit": self.unit, "ms_per_step": ms,
                 "h2d_bytes_per_step": int(host.numel() * 4), "d2h_bytes_per_step": self.R * 4}
 
-    def check_errors(self):
-        return 0
-
-    def cpu_sample(self, threads, budget_s=10.0):
+    @classmethod
+    def cpu_port(cls, args, threads, budget_s):
         """The reference algorithm (cu/sample.cu:40-123 restated in
-        oracle/oracle.c, insertion top-k) on host rows, one core, until the
-        time budget is spent."""
+        oracle/oracle.c, insertion top-k) over numpy N(0, 2) rows, rows in
+        parallel on a thread pool, until the budget is spent."""
+        from concurrent.futures import ThreadPoolExecutor
         orc = ge.load_oracle()
-        host = self.bufs[0].cpu().numpy()
+        rows = _cached("c3", lambda: np.random.default_rng(3).standard_normal(
+            (cls.R, cls.V), dtype=np.float32) * np.float32(2.0))
+        pool = ThreadPoolExecutor(max_workers=threads)
         t0 = time.perf_counter()
         n = 0
-        while time.perf_counter() - t0 < budget_s and n < self.R:
-            orc.sample_row(host[n], 0.8, 50, 0.9, orc.sample_u24(1234, n, 0))
-            n += 1
+        while n == 0 or time.perf_counter() - t0 < budget_s:
+            batch = [(n + j) % cls.R for j in range(threads)]
+            list(pool.map(lambda r: orc.sample_row(rows[r], 0.8, 50, 0.9,
+                                                   orc.sample_u24(1234, r, 0)), batch))
+            n += len(batch)
         dt = time.perf_counter() - t0
-        return {"value": n * self.V * 4 / 1e9 / dt, "unit": self.unit, "cores": 1, "kind": "port",
-                "seconds": dt, "sample": f"{n} of 256 rows of config 3, serial reference algorithm"}
-
-    def config(self):
-        return {"workload": self.name, "rows": self.R, "vocab": self.V, "temperature": 0.8,
-                "top_k": 50, "top_p": 0.9, "seed": 1234,
-                "l2": "8 logits buffers rotate (262 MB > 126 MB L2)"}
+        pool.shutdown()
+        return _port_result(n * cls.V * 4 / 1e9 / dt, cls.unit, threads, dt,
+                            f"{n} config-3 rows, reference algorithm, {threads} rows at a time")
 
 
-class RolloutWorkload:
-    """BASELINE config 5 (config 4's attention shape and config-3 sampling):
+def _traj_checksum(torch, traj, lengths):
+    """Order-sensitive checksum of the written part of a trajectory buffer
+    (row r holds lengths[r] tokens; the rest of the row is never written)."""
+    width = traj.shape[1]
+    valid = torch.arange(width, device=traj.device)[None, :] < lengths[:, None]
+    w = torch.arange(1, traj.numel() + 1, device=traj.device, dtype=torch.int64) % 1000003
+    return int((traj.to(torch.int64) * valid * w.view(traj.shape)).sum().item())
+
+
+class RolloutWorkload(Workload):
+    """BASELINE config 5 (config 2's attention shape and config-3 sampling):
     8,192 rollouts = 512 GRPO groups x 16, split by group across the N GPUs
     (strong scaling: the same 8,192 rollouts whatever N).  Each group's 16
     rollouts share a 512-token prompt held once in the KV arena
@@ -345,15 +488,29 @@ class RolloutWorkload:
     kernel = "paged_gqa_group_kernel+paged_gqa_decode_kernel"  # attention of one pass
     metric = "rollout tokens/s (config 5; value = all GPUs, per GPU = value / n_gpus)"
     unit = "tokens/s"
+    scaling = "strong"
+    launches_per_step = None  # counted from the loop's pass counter
+    launches_per_pass = 5
 
     GROUPS, G, PROMPT, GEN, VOCAB = 512, 16, 512, 256, 32000
     DECODE_MODE = 1  # q, K/V and logits from Philox (the reference has no model)
 
+    @classmethod
+    def static_config(cls, args, world):
+        groups = args.groups or cls.GROUPS
+        return {"workload": cls.name, "rollouts": groups * cls.G, "groups": groups,
+                "group_size": cls.G, "prompt_tokens": cls.PROMPT, "new_tokens": cls.GEN,
+                "q_heads": 32, "kv_heads": 8, "head_dim": 128, "page_tokens": 16,
+                "vocab": cls.VOCAB, "sampling": "T=0.8 top-k 50 top-p 0.9", "slots": 256,
+                "reward": "U(0,1) Philox seed 5, NCCL allgather, GRPO advantages",
+                "l2": "KV arena > 126 MB L2 (prompts + 256 slots x 17 private pages)"}
+
     def __init__(self, args, rank, world, dev):
         import torch
+        self.args, self.world = args, world
         self.torch = torch
         self.pkg = pkg = ge.load_package()
-        self.rank, self.world, self.dev = rank, world, dev
+        self.rank, self.dev = rank, dev
         if getattr(args, "groups", 0):
             self.GROUPS = args.groups
         self.g0, self.ng = pkg.shard_groups(self.GROUPS, world, rank)
@@ -373,38 +530,37 @@ class RolloutWorkload:
         for g in range(self.ng):
             self.eng.set_prefix(g, prompt_pages[g * pages_prompt:(g + 1) * pages_prompt], self.PROMPT)
         self._attach_model(torch, dev, rank)
-        orc_dtype = np.dtype([("request_id", "<u8"), ("max_tokens", "<u4"), ("kv_blocks", "<u4"),
-                              ("temperature", "<f4"), ("top_k", "<u2"), ("top_p", "<f4"),
-                              ("rng_seed", "<u8")])
-        r = np.zeros(self.n, dtype=orc_dtype)
+        r = np.zeros(self.n, dtype=np.dtype(pkg.REQUEST_RECORD))
         gid = np.arange(self.n) // self.G                       # local group
         r["request_id"] = (np.arange(self.n, dtype=np.uint64) + np.uint64(self.g0 * self.G + 1)) | \
             ((gid.astype(np.uint64) + np.uint64(1)) << np.uint64(32))
         r["max_tokens"] = self.GEN
         r["kv_blocks"] = pages_prompt
         r["temperature"], r["top_k"], r["top_p"], r["rng_seed"] = 0.8, 50, 0.9, 1234
+        self._make_buffers(torch, dev, r)
+        self.arrivals = None
+        self.tokens_per_step = self.n * self.GEN
+        torch.cuda.synchronize()
+
+    def _make_buffers(self, torch, dev, r):
         self.reqs_host = r
         self.req_d = torch.from_numpy(r.view(np.uint8).copy()).to(dev)
         self.dones = torch.zeros(self.n * 24, dtype=torch.uint8, device=dev)
         self.state = torch.zeros(72 * 256 + 32, dtype=torch.uint8, device=dev)
-        self.traj = torch.zeros(self.n, self.GEN, dtype=torch.int32, device=dev)
+        self.traj = torch.zeros(self.n, int(r["max_tokens"].max()), dtype=torch.int32, device=dev)
         self.rewards = torch.zeros(self.n, dtype=torch.float32, device=dev)
-        self.all_rewards = torch.zeros(self.GROUPS * self.G, dtype=torch.float32, device=dev)
+        total = self.GROUPS * self.G if self.scaling == "strong" else self.n
+        self.all_rewards = torch.zeros(total, dtype=torch.float32, device=dev)
         self.adv = torch.zeros_like(self.all_rewards)
         self.nccl = None
-        if world > 1:
+        if self.world > 1 and self.scaling == "strong":
             import torch.distributed as dist
 
             def exchange(b):
                 obj = [b]
                 dist.broadcast_object_list(obj, src=0)
                 return obj[0]
-            self.nccl = pkg.NcclRewards(rank, world, exchange)
-        self.tokens_per_step = self.n * self.GEN
-        torch.cuda.synchronize()
-
-    launches_per_step = None  # counted from the loop's pass counter
-    launches_per_pass = 5
+            self.nccl = self.pkg.NcclRewards(self.rank, self.world, exchange)
 
     def _attach_model(self, torch, dev, rank):
         pass
@@ -416,9 +572,13 @@ class RolloutWorkload:
             self.all_rewards.copy_(self.rewards)
         self.pkg.grpo_advantages(self.all_rewards, self.G, out=self.adv, stream=stream)
 
-    def step(self):
+    def _launch(self, **kw):
         self.eng.launch(requests=self.req_d, n_requests=self.n, dones=self.dones, state=self.state,
-                        trajectories=self.traj, rewards=self.rewards, n_rows=self.n)
+                        trajectories=self.traj, rewards=self.rewards, n_rows=self.n,
+                        arrivals=self.arrivals, arrival_unit=self.pkg.RT_ARRIVAL_NS, **kw)
+
+    def step(self):
+        self._launch()
         self._post()
 
     def units_per_step(self):
@@ -432,7 +592,46 @@ class RolloutWorkload:
     def gpu_launches(self, steps):
         # per pass: schedule, prepare, attention, logits, sampler; per step:
         # one allgather (when N > 1) and one advantage kernel
-        return int(self.last_stats["passes"]) * self.launches_per_pass * steps + 2 * steps
+        per_step = 2 if self.nccl else 1
+        return int(self.last_stats["passes"]) * self.launches_per_pass * steps + per_step * steps
+
+    def trajectory_check(self, sample_rows=64):
+        """After the timed steps: the trajectories of one more step (buffer
+        cleared first) equal those the timed steps left (the run is seeded
+        and deterministic), and a sample of rollouts (every n/64-th) equals a
+        token-by-token replay of the loop's logits through the standalone
+        sampler."""
+        torch = self.torch
+        lengths = torch.from_numpy(self.reqs_host["max_tokens"].astype(np.int64)).to(self.traj.device)
+        before = _traj_checksum(torch, self.traj, lengths)
+        self.traj.fill_(-1)
+        self.step()
+        self.eng.wait()
+        after = _traj_checksum(torch, self.traj, lengths)
+        rows = range(0, self.n, max(1, self.n // sample_rows))
+        total, bad = self.pkg.replay_trajectories(self.reqs_host, self.traj.cpu().numpy(), rows,
+                                                  self.VOCAB)
+        ok = before == after and not bad
+        return {"result": "equal" if ok else "DIFFERENT", "checksum_timed": before,
+                "checksum_check_step": after, "replayed_rollouts": len(rows),
+                "replayed_tokens": total, "mismatches": len(bad), "first_mismatches": bad[:3]}
+
+    def rank_diagnostics(self):
+        """One more step with CUDA events around the loop and around the
+        reward exchange + advantages (the allgather waits for the slowest
+        rank, so its time shows imbalance), plus passes and waves."""
+        torch = self.torch
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        e[0].record()
+        self._launch()
+        e[1].record()
+        self._post()
+        e[2].record()
+        torch.cuda.synchronize()
+        st = self.eng.wait()
+        return {"rank": self.rank, "rollouts": self.n, "waves": -(-self.n // 256),
+                "passes": int(st["passes"]), "loop_ms": e[0].elapsed_time(e[1]),
+                "allgather_adv_ms": e[1].elapsed_time(e[2])}
 
     def e2e(self, steps, warmup):
         """Through the C ABI with host buffers: requests pushed into a mapped
@@ -471,28 +670,28 @@ class RolloutWorkload:
                 "h2d_bytes_per_step": self.n * 34,
                 "d2h_bytes_per_step": self.n * 24 + traj_h.numel() * 4 + adv_h.numel() * 4}
 
+    @staticmethod
+    def _pct(x, scale=1e3):
+        x = np.sort(np.asarray(x, dtype=np.float64))
+        if not len(x):
+            return None
+        q = lambda f: round(float(x[min(len(x) - 1, int(f * len(x)))]) / scale, 2)
+        return {"n": int(len(x)), "p50": q(0.5), "p90": q(0.9), "p99": q(0.99),
+                "max": round(float(x[-1]) / scale, 2)}
+
     def trace_report(self):
         """One more RL step, untimed, with the device trace attached
         (rt_rollout_set_trace): device-clock latencies in the manner of the
         reference's trace report (docs/tracing.md), from the schedule
         kernel's records: rollout alloc -> trajectory done, and the interval
         between decode passes."""
-        tr = self.pkg.DeviceTrace(1 << 17)
+        tr = self.pkg.DeviceTrace(1 << 18)
         self.eng.set_trace(tr)
         self.step()
         self.eng.wait()
         self.eng.set_trace(None)
         rec, total = tr.read()
         pk = self.pkg
-
-        def pct(x):
-            x = np.sort(np.asarray(x, dtype=np.float64))
-            if not len(x):
-                return None
-            q = lambda f: round(float(x[min(len(x) - 1, int(f * len(x)))]) / 1e3, 2)
-            return {"n": int(len(x)), "p50": q(0.5), "p90": q(0.9), "p99": q(0.99),
-                    "max": round(float(x[-1]) / 1e3, 2)}
-
         alloc = {}
         life = []
         for r in rec:
@@ -503,64 +702,205 @@ class RolloutWorkload:
                 life.append(int(r["tsc"]) - alloc.pop(int(r["rollout_id"])))
         passes = rec[rec["type"] == pk.TRACE_DECODE_BATCH]["tsc"].astype(np.int64)
         return {"clock": "GPU globaltimer, ns -> us", "records": int(total),
-                "rollout_alloc_to_done_us": pct(life),
-                "decode_pass_interval_us": pct(np.diff(passes))}
+                "rollout_alloc_to_done_us": self._pct(life),
+                "decode_pass_interval_us": self._pct(np.diff(passes))}
 
     def kernel_profile(self, n_rollouts=512):
         """Per-kernel device time from a host-stepped replay (rt_rollout_profile)
         of the first n_rollouts of the step."""
         n = min(n_rollouts, self.n)
-        prof = self.eng.profile(requests=self.req_d, n_requests=n, dones=self.dones,
+        return self.eng.profile(requests=self.req_d, n_requests=n, dones=self.dones,
                                 state=self.state, trajectories=self.traj, rewards=self.rewards,
                                 n_rows=self.n)
-        return prof
 
-    def cpu_sample(self, threads, budget_s=10.0):
-        """The same decode step on the host: one GRPO group (16 rollouts, shared
-        512-token prompt) generating tokens with the CPU oracle - paged GQA
-        attention (oracle/oracle.c, OpenMP) + N(0,2) logits + the reference
-        sampling algorithm (cu/sample.cu:40-123, insertion top-k) - until the
-        time budget is spent."""
-        from concurrent.futures import ThreadPoolExecutor
-        orc = ge.load_oracle()
+    @classmethod
+    def cpu_port(cls, args, threads, budget_s):
+        tokens, steps, dt = _port_rollout_decode(threads, budget_s, cls.G, cls.PROMPT, cls.GEN,
+                                                 cls.VOCAB, seed=11)
+        return _port_result(tokens / dt, cls.unit, threads, dt,
+                            f"1 group x 16 rollouts, {steps} decode steps from a shared 512-token "
+                            f"prompt, scattered private pages (attention + logits + reference "
+                            f"sampling per token)")
+
+    def details(self):
+        return {"rollouts_per_gpu": self.n,
+                "arena_gb": round(self.arena.buf.numel() / 1e9, 3)}
+
+
+class RolloutC4Workload(RolloutWorkload):
+    """BASELINE config 4, continuous batching on one GPU: 1,024 rollouts in
+    64 GRPO groups of 16 arriving as a Poisson process (exponential gaps,
+    mean 1/8 ms, seed 4, in group order).  Every context starts with the
+    same registered 1,024-token copy-on-write prefix followed by the group's
+    prompt of U[64,1024] tokens (one per group, seed 4), so most groups'
+    contexts end mid-page; each rollout generates U[32,512] tokens (seed 4).
+    Attention shape of config 2, sampling of config 3, synthetic logits.
+
+    value: one step = the loop over the 1,024 requests held in a device
+    array, each admitted no earlier than its arrival time (the schedule
+    kernel reads the GPU clock), then rewards and advantages; tokens/s is
+    the generated tokens over that device time, so it includes the arrival
+    span (~128 ms) and the drain.
+    e2e: the host C pump pushes the requests into the mapped RequestRing at
+    their arrival times (rt_host_pump_paced) and drains the DoneRing; the
+    latency of each rollout (arrival -> done record drained) is reported."""
+
+    name = "continuous_batching_c4"
+    metric = "rollout tokens/s (config 4: Poisson arrivals, continuous batching)"
+    scaling = "weak"
+    N_ROLLOUTS, G, BASE, GEN, VOCAB, RATE_PER_MS = 1024, 16, 1024, 512, 32000, 8.0
+
+    @classmethod
+    def inputs(cls, seed=4):
+        rng = np.random.default_rng(seed)
+        prompt = rng.integers(64, 1025, size=cls.N_ROLLOUTS // cls.G)
+        max_new = rng.integers(32, 513, size=cls.N_ROLLOUTS)
+        gaps = rng.exponential(1e6 / cls.RATE_PER_MS, size=cls.N_ROLLOUTS)
+        arrival_ns = np.cumsum(gaps) - gaps[0]
+        return prompt, max_new, arrival_ns.astype(np.uint64)
+
+    @classmethod
+    def static_config(cls, args, world):
+        prompt, max_new, arr = cls.inputs()
+        return {"workload": cls.name, "rollouts": cls.N_ROLLOUTS, "groups": cls.N_ROLLOUTS // cls.G,
+                "group_size": cls.G, "arrivals": "Poisson, mean 8 per ms (exponential gaps, seed 4)",
+                "arrival_span_ms": round(float(arr[-1]) / 1e6, 2),
+                "shared_prefix_tokens": cls.BASE, "prompt_tokens": "U[64,1024] per group, seed 4",
+                "new_tokens": "U[32,512] per rollout, seed 4",
+                "generated_tokens": int(max_new.sum()), "q_heads": 32, "kv_heads": 8,
+                "head_dim": 128, "page_tokens": 16, "vocab": cls.VOCAB,
+                "sampling": "T=0.8 top-k 50 top-p 0.9", "slots": 256,
+                "admission": "all free slots per pass, backpressure (requests wait, none dropped)",
+                "l2": "KV arena ~0.7 GB > 126 MB L2"}
+
+    def __init__(self, args, rank, world, dev):
+        import torch
+        self.args, self.world = args, world
+        self.torch = torch
+        self.pkg = pkg = ge.load_package()
+        self.rank, self.dev = rank, dev
+        prompt, max_new, arrival = self.inputs()
+        self.prompt, self.arrival_ns = prompt, arrival
+        self.n = self.N_ROLLOUTS
+        self.ng = self.n // self.G
+        self.GROUPS = self.ng
+        base_pages = self.BASE // 16
+        grp_pages = [(int(p) + 15) // 16 for p in prompt]
+        priv = 256 * ((self.GEN + 16 + 15) // 16)
+        self.arena = pkg.DeviceArena(base_pages + sum(grp_pages) + priv + 64, device=dev)
+        cfg = dict(num_q_heads=32, num_kv_heads=8, vocab=self.VOCAB, max_slots=256,
+                   max_context=self.BASE + 1024 + self.GEN, max_new_tokens=self.GEN,
+                   max_admit=256, drop_when_full=0, decode_mode=1, reward_mode=1, reward_seed=5,
+                   logit_std=2.0, max_prefixes=self.ng,
+                   max_prefix_pages=self.ng * (base_pages + 64), max_passes=1 << 26,
+                   idle_timeout_ms=20000, chunk_pages=args.chunk_pages)
+        self.eng = pkg.RolloutEngine(cfg, self.arena)
+        base = self.arena.acquire(base_pages)
+        self.arena.fill_pages(base, seed=4 + rank, stream_id=0)      # synthetic prefill (untimed)
+        for g in range(self.ng):
+            own = self.arena.acquire(grp_pages[g])
+            self.arena.fill_pages(own, seed=4 + rank, stream_id=1000000 * (g + 1))
+            self.eng.set_prefix(g, list(base) + list(own), self.BASE + int(prompt[g]))
+        r = np.zeros(self.n, dtype=np.dtype(pkg.REQUEST_RECORD))
+        gid = np.arange(self.n) // self.G
+        r["request_id"] = np.arange(1, self.n + 1, dtype=np.uint64) | \
+            ((gid.astype(np.uint64) + np.uint64(1)) << np.uint64(32))
+        r["max_tokens"] = max_new
+        r["kv_blocks"] = (self.BASE + prompt[gid] + 15) // 16
+        r["temperature"], r["top_k"], r["top_p"], r["rng_seed"] = 0.8, 50, 0.9, 1234
+        self._make_buffers(torch, dev, r)
+        self.arrivals = torch.from_numpy(arrival.astype(np.int64)).to(dev)
+        self.tokens_per_step = int(max_new.sum())
+        torch.cuda.synchronize()
+
+    def e2e(self, steps, warmup):
+        """Ring-fed and paced: requests enter the mapped RequestRing at their
+        arrival times (rt_host_pump_paced), dones are drained from the mapped
+        DoneRing, then the trajectories and advantages are copied to pinned
+        host memory; all inside the timed region."""
         torch = self.torch
-        B, Hq, Hkv = self.G, 32, 8
-        ctx = self.PROMPT
-        n_pages = (ctx + self.GEN + 15) // 16
-        rng = np.random.default_rng(11)
-        arena = rng.standard_normal(B * n_pages * Hkv * 2 * 16 * 128, dtype=np.float32)
-        arena_b = (arena.view(np.uint32) >> 16).astype(np.uint16)
-        pt = np.arange(B * n_pages, dtype=np.int32).reshape(B, n_pages)
-        pool = ThreadPoolExecutor(max_workers=threads)
-        t0 = time.perf_counter()
-        steps = 0
-        while steps == 0 or time.perf_counter() - t0 < budget_s:
-            q = (rng.standard_normal((B, Hq, 128), dtype=np.float32).view(np.uint32) >> 16).astype(np.uint16)
-            lens = np.full(B, ctx + steps + 1, dtype=np.int32)
-            orc.paged_gqa_attention(q, arena_b, pt, lens, Hq, Hkv, 128 ** -0.5, n_threads=threads)
-            logits = rng.standard_normal((B, self.VOCAB), dtype=np.float32) * 2.0
-            list(pool.map(lambda b: orc.sample_row(logits[b], 0.8, 50, 0.9,
-                                                   orc.sample_u24(1234, b, steps)), range(B)))
-            steps += 1
-            if steps >= self.GEN:
-                break
-        dt = time.perf_counter() - t0
-        pool.shutdown()
-        return {"value": B * steps / dt, "unit": self.unit, "cores": threads, "kind": "port",
-                "seconds": dt,
-                "sample": f"1 group x 16 rollouts, {steps} decode steps from a 512-token prompt "
-                          f"(attention + logits + reference sampling per token)"}
+        rings = self.pkg.HostRings()
+        traj_h = torch.empty(self.traj.shape, dtype=torch.int32).pin_memory()
+        adv_h = torch.empty(self.adv.shape, dtype=torch.float32).pin_memory()
+        s = torch.cuda.current_stream()
+        lat = []
 
-    def config(self):
-        return {"workload": self.name, "rollouts": self.GROUPS * self.G, "groups": self.GROUPS,
-                "group_size": self.G, "prompt_tokens": self.PROMPT, "new_tokens": self.GEN,
-                "rollouts_per_gpu": self.n, "q_heads": 32, "kv_heads": 8, "head_dim": 128,
-                "page_tokens": 16, "vocab": self.VOCAB, "sampling": "T=0.8 top-k 50 top-p 0.9",
-                "slots": 256, "reward": "U(0,1) Philox seed 5, NCCL allgather, GRPO advantages",
-                "l2": f"KV arena {self.arena.buf.numel() / 1e9:.2f} GB > 126 MB L2"}
+        def one():
+            self.eng.launch(ring=rings.req, done_ring=rings.done, state=self.state,
+                            trajectories=self.traj, rewards=self.rewards, n_rows=self.n)
+            got, raw, done_ns = rings.pump_paced(self.reqs_host, self.arrival_ns, self.n,
+                                                 send_sentinel=True, timeout_ms=120000)
+            if got != self.n:
+                raise RuntimeError(f"e2e pump drained {got} of {self.n}")
+            d = raw[: self.n * 24].view(np.dtype([("request_id", "<u8"), ("rollout_id", "<u4"),
+                                                    ("tokens_generated", "<u4"), ("reward", "<f4"),
+                                                    ("status", "<u4")]))
+            idx = d["request_id"].astype(np.int64) - 1
+            lat.append(done_ns[:self.n].astype(np.float64) - self.arrival_ns[idx].astype(np.float64))
+            self._post()
+            traj_h.copy_(self.traj, non_blocking=True)
+            adv_h.copy_(self.adv, non_blocking=True)
+
+        for _ in range(min(warmup, 1)):
+            one()
+        torch.cuda.synchronize()
+        lat.clear()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(steps):
+            one()
+        e1.record(s)
+        torch.cuda.synchronize()
+        self.eng.wait()
+        rings.close()
+        ms = e0.elapsed_time(e1) / steps
+        return {"value": self.units_per_step() / (ms / 1e3), "unit": self.unit, "ms_per_step": ms,
+                "h2d_bytes_per_step": self.n * 34,
+                "d2h_bytes_per_step": self.n * 24 + traj_h.numel() * 4 + adv_h.numel() * 4,
+                "latency_arrival_to_done_ms": self._pct(np.concatenate(lat), 1e6)}
+
+    def kernel_profile(self, n_rollouts=None):
+        """Host-stepped replay of all 1,024 rollouts with the arrivals given
+        in passes (arrival time / the timed run's mean pass interval), so the
+        replay admits in the same rhythm as the timed loop."""
+        st = getattr(self, "last_stats", None)
+        pass_ns = (self.last_ms * 1e6 / st["passes"]) if st and st["passes"] else 100e3
+        arr = self.torch.from_numpy((self.arrival_ns / pass_ns).astype(np.int64)).to(self.dev)
+        return self.eng.profile(requests=self.req_d, n_requests=self.n, dones=self.dones,
+                                state=self.state, trajectories=self.traj, rewards=self.rewards,
+                                n_rows=self.n, arrivals=arr,
+                                arrival_unit=self.pkg.RT_ARRIVAL_PASS)
+
+    @classmethod
+    def cpu_port(cls, args, threads, budget_s):
+        prompt, _, _ = cls.inputs()
+        ctx = cls.BASE + int(prompt[0])
+        tokens, steps, dt = _port_rollout_decode(threads, budget_s, cls.G, ctx, cls.GEN,
+                                                 cls.VOCAB, seed=12)
+        return _port_result(tokens / dt, cls.unit, threads, dt,
+                            f"group 0 (16 rollouts, {ctx}-token shared context), {steps} decode "
+                            f"steps (attention + logits + reference sampling per token)")
+
+    def details(self):
+        return {"arena_gb": round(self.arena.buf.numel() / 1e9, 3)}
 
 
-class DecodeRingWorkload:
+def _decode_ring_inputs(rank, N=10000, BLOCKS=128, SLOTS=4096, BLOCK=16384):
+    orc = ge.load_oracle()
+    rng = np.random.default_rng(7 + rank)
+    arena_host = rng.standard_normal(BLOCKS * BLOCK // 2).astype(np.float16).view(np.uint8)
+    q_bits = rng.standard_normal((SLOTS, 128)).astype(np.float16).view(np.uint16)
+    d = np.zeros(N, orc.DESCRIPTOR_DTYPE)
+    i = np.arange(N, dtype=np.uint64)
+    d["seq_id"] = 1 + rank
+    d["kv_block_offset"] = i % BLOCKS
+    d["num_kv_blocks"] = 1
+    d["output_token_offset"] = i
+    d["reward_cookie"] = (np.uint64(1 + rank) << np.uint64(32)) | i
+    return d, arena_host, q_bits
+
+
+class DecodeRingWorkload(Workload):
     """The reference's per-step CommandRing benchmark (src/main.c:201-260):
     10,000 decode descriptors of one trajectory, kv_block_offset = i % 128
     over 16 KiB fp16 blocks, num_kv_blocks 1, output slot i & 4095 of a
@@ -582,27 +922,26 @@ class DecodeRingWorkload:
     metric = "decode steps/s (fixed128 step, reference src/main.c shape)"
     unit = "steps/s"
     dtype = "fp16 KV, fp32 math"
-    launches_per_step = 1
     roofline_note = ("latency-bound: 10,000 warps each stage 512 B of KV with one bulk copy "
                      "and run a one-token step; the HBM bytes are incidental")
     N, BLOCKS, SLOTS, BLOCK, COPIES = 10000, 128, 4096, 16384, 64
 
+    @classmethod
+    def static_config(cls, args, world):
+        return {"workload": cls.name, "descriptors": cls.N, "kv_blocks": cls.BLOCKS,
+                "block_bytes": cls.BLOCK, "num_kv_blocks": 1, "io_slots": cls.SLOTS,
+                "value_step": "rt_attention_fixed128 over HBM-resident descriptors",
+                "e2e_step": "decode worker launch + ring dispatch + poll + stop sentinel + join",
+                "rings": "CommandRing / CompletionRing, 4,096 slots, pinned mapped host memory",
+                "l2": "64 rotating copies of blocks, q, o, descriptors and results (> 126 MB L2)"}
+
     def __init__(self, args, rank, world, dev):
         import ctypes
         import torch
+        self.args, self.world = args, world
         self.torch, self.ctypes = torch, ctypes
         self.pkg = pkg = ge.load_package()
-        orc = ge.load_oracle()
-        rng = np.random.default_rng(7 + rank)
-        self.arena_host = rng.standard_normal(self.BLOCKS * self.BLOCK // 2).astype(np.float16).view(np.uint8)
-        self.q_bits = rng.standard_normal((self.SLOTS, 128)).astype(np.float16).view(np.uint16)
-        d = np.zeros(self.N, orc.DESCRIPTOR_DTYPE)
-        i = np.arange(self.N, dtype=np.uint64)
-        d["seq_id"] = 1 + rank
-        d["kv_block_offset"] = i % self.BLOCKS
-        d["num_kv_blocks"] = 1
-        d["output_token_offset"] = i
-        d["reward_cookie"] = (np.uint64(1 + rank) << np.uint64(32)) | i
+        d, self.arena_host, self.q_bits = _decode_ring_inputs(rank)
         self.descs = d
         C = self.COPIES
         self.arena_t = torch.from_numpy(self.arena_host.copy()).to(dev).repeat(C).view(C, -1)
@@ -697,36 +1036,31 @@ class DecodeRingWorkload:
         return {"value": self.N / (ms / 1e3), "unit": self.unit, "ms_per_step": ms,
                 "h2d_bytes_per_step": (self.N + 1) * 32, "d2h_bytes_per_step": self.N * 32}
 
-    def cpu_sample(self, threads, budget_s=10.0):
+    @classmethod
+    def cpu_port(cls, args, threads, budget_s):
         """The reference step on the host (oracle/oracle.c orc_decode_steps:
         process_descriptor + the fixed128 attention of test/test_bench.cu:
-        109-155), one core, whole 10,000-descriptor batches until the
-        budget is spent."""
+        109-155) over the same descriptors, split into contiguous chunks run
+        on a thread pool, whole batches until the budget is spent."""
+        from concurrent.futures import ThreadPoolExecutor
         orc = ge.load_oracle()
+        d, arena, q = _cached("ring", lambda: _decode_ring_inputs(0))
+        chunks = np.array_split(np.arange(cls.N), threads)
+        pool = ThreadPoolExecutor(max_workers=threads)
         t0 = time.perf_counter()
         reps = 0
         while reps == 0 or time.perf_counter() - t0 < budget_s:
-            orc.decode_steps(self.descs, self.arena_host, self.BLOCK, q_buf=self.q_bits,
-                             io_slots=self.SLOTS)
+            list(pool.map(lambda c: orc.decode_steps(d[c], arena, cls.BLOCK, q_buf=q,
+                                                     io_slots=cls.SLOTS), chunks))
             reps += 1
         dt = time.perf_counter() - t0
-        return {"value": reps * self.N / dt, "unit": self.unit, "cores": 1, "kind": "port",
-                "seconds": dt,
-                "sample": f"{reps} batch(es) of the 10,000 descriptors, serial C restatement"}
-
-    def config(self):
-        return {"workload": self.name, "descriptors": self.N, "kv_blocks": self.BLOCKS,
-                "block_bytes": self.BLOCK, "num_kv_blocks": 1, "io_slots": self.SLOTS,
-                "value_step": "rt_attention_fixed128 over HBM-resident descriptors",
-                "e2e_step": "decode worker launch + ring dispatch + poll + stop sentinel + join",
-                "rings": "CommandRing / CompletionRing, 4,096 slots, pinned mapped host memory",
-                "l2": "%d rotating copies of blocks, q, o, descriptors and results (%.0f MB > "
-                      "126 MB L2)" % (self.COPIES, self.COPIES * (self.arena_t[0].numel()
-                                      + self.q[0].numel() * 2 + self.o[0].numel() * 4
-                                      + self.desc_d[0].numel() + self.res[0].numel()) / 1e6)}
+        pool.shutdown()
+        return _port_result(reps * cls.N / dt, cls.unit, threads, dt,
+                            f"{reps} batch(es) of the 10,000 descriptors, C restatement on "
+                            f"{threads} threads")
 
 
-class LmHeadWorkload:
+class LmHeadWorkload(Workload):
     """The decode step's LM head as a tensor-core GEMM (rt_gemm_bf16,
     tcgen05): logits fp32 [256 slots][32,000] = hidden bf16 [256][4096] x
     W bf16 [32,000][4096]^T.  The 262 MB weight exceeds the 126 MB L2, so
@@ -739,12 +1073,18 @@ class LmHeadWorkload:
     unit = "TFLOP/s"
     dtype = "bf16 in, fp32 accumulate and out"
     bound = "tensor"
-    launches_per_step = 1
     M, N, K = 256, 32000, 4096
+
+    @classmethod
+    def static_config(cls, args, world):
+        return {"workload": cls.name, "M": cls.M, "N": cls.N, "K": cls.K,
+                "tile": "256 x 224 unit, 3-stage TMA ring, double-buffered TMEM accumulator",
+                "l2": "W 262 MB > 126 MB L2 (streamed from HBM every step)"}
 
     def __init__(self, args, rank, world, dev):
         import ctypes
         import torch
+        self.args, self.world = args, world
         self.torch, self.ctypes = torch, ctypes
         self.pkg = pkg = ge.load_package()
         self.A = torch.empty(self.M, self.K, dtype=torch.bfloat16, device=dev)
@@ -821,27 +1161,27 @@ class LmHeadWorkload:
         return {"value": self.units_per_step() / (ms / 1e3), "unit": self.unit, "ms_per_step": ms,
                 "h2d_bytes_per_step": self.M * self.K * 2, "d2h_bytes_per_step": self.M * self.N * 4}
 
-    def cpu_sample(self, threads, budget_s=10.0):
+    @classmethod
+    def cpu_port(cls, args, threads, budget_s):
         """The same product on the host (numpy float32 matmul, multithreaded
-        BLAS) over row blocks of the hidden state until the budget is spent;
-        the reference has no LM head."""
-        a = self.A.float().cpu().numpy()
-        w = self.W.float().cpu().numpy()
+        BLAS) over row blocks of a numpy hidden state and weight, until the
+        budget is spent; the reference has no LM head."""
+        def make():
+            rng = np.random.default_rng(21)
+            return (rng.standard_normal((cls.M, cls.K), dtype=np.float32),
+                    rng.standard_normal((cls.N, cls.K), dtype=np.float32) * np.float32(0.02))
+        a, w = _cached("lm", make)
         t0 = time.perf_counter()
         rows = 0
-        while rows < self.M and (rows == 0 or time.perf_counter() - t0 < budget_s):
+        while rows < cls.M and (rows == 0 or time.perf_counter() - t0 < budget_s):
             _ = a[rows:rows + 16] @ w.T
             rows += 16
         dt = time.perf_counter() - t0
-        return {"value": 2.0 * rows * self.N * self.K / dt / 1e12, "unit": self.unit,
-                "cores": threads, "kind": "port", "seconds": dt,
-                "sample": f"{rows} of 256 rows, numpy float32 matmul"}
+        return _port_result(2.0 * rows * cls.N * cls.K / dt / 1e12, cls.unit, threads, dt,
+                            f"{rows} of 256 rows, numpy float32 matmul")
 
-    def config(self):
-        return {"workload": self.name, "M": self.M, "N": self.N, "K": self.K,
-                "tile": "128 x 224, 4-stage TMA ring, double-buffered TMEM accumulator",
-                "l2": "W 262 MB > 126 MB L2 (streamed from HBM every step)",
-                "cublas_bf16_out_ms": round(self.cublas_ms(), 4)}
+    def details(self):
+        return {"cublas_bf16_out_ms": round(self.cublas_ms(), 4)}
 
 
 class RolloutModelWorkload(RolloutWorkload):
@@ -858,6 +1198,15 @@ class RolloutModelWorkload(RolloutWorkload):
     metric = "rollout tokens/s (config 5, model decode: QKV + LM-head GEMMs)"
     DECODE_MODE = 2
     launches_per_pass = 8  # schedule, embed, QKV GEMM, prepare, attention, hidden, LM GEMM, sampler
+
+    @classmethod
+    def static_config(cls, args, world):
+        return super().static_config(args, world) | {
+            "workload": cls.name,
+            "model": "embedding 32,000 x 4,096, QKV 4,096 -> 6,144, LM head 4,096 -> 32,000; "
+                     "bf16 weights N(0, s), fp32 accumulation",
+            "prompts": "seeded token ids, K / V prefilled by the model (rt_rollout_prefill, "
+                       "untimed setup)"}
 
     def _attach_model(self, torch, dev, rank):
         D, NQKV = 32 * 128, (32 + 2 * 8) * 128
@@ -882,7 +1231,22 @@ class RolloutModelWorkload(RolloutWorkload):
         torch.cuda.synchronize()
         self.prefill_tokens_per_s = self.ng * self.PROMPT / (e0.elapsed_time(e1) / 1e3)
 
-    def cpu_sample(self, threads, budget_s=10.0):
+    def trajectory_check(self, sample_rows=64):
+        """Model decode feeds sampled tokens back, so there is no closed-form
+        replay; the check is that one more step reproduces the timed
+        trajectories bit for bit."""
+        torch = self.torch
+        lengths = torch.from_numpy(self.reqs_host["max_tokens"].astype(np.int64)).to(self.traj.device)
+        before = _traj_checksum(torch, self.traj, lengths)
+        self.traj.fill_(-1)
+        self.step()
+        self.eng.wait()
+        after = _traj_checksum(torch, self.traj, lengths)
+        return {"result": "equal" if before == after else "DIFFERENT",
+                "checksum_timed": before, "checksum_check_step": after}
+
+    @classmethod
+    def cpu_port(cls, args, threads, budget_s):
         """The model decode step on the host for one GRPO group (16
         rollouts, shared 512-token prompt): embedding rows, QKV and LM-head
         projections (numpy float32 matmul, multithreaded BLAS), paged GQA
@@ -890,61 +1254,63 @@ class RolloutModelWorkload(RolloutWorkload):
         algorithm per row, until the budget is spent."""
         from concurrent.futures import ThreadPoolExecutor
         orc = ge.load_oracle()
-        B, Hq, Hkv, D = self.G, 32, 8, 32 * 128
-        n_pages = (self.PROMPT + self.GEN + 15) // 16
+        B, Hq, Hkv, D = cls.G, 32, 8, 32 * 128
+        n_pages = (cls.PROMPT + cls.GEN + 15) // 16
         rng = np.random.default_rng(11)
-        arena = rng.standard_normal(B * n_pages * Hkv * 2 * 16 * 128, dtype=np.float32)
-        arena_b = (arena.view(np.uint32) >> 16).astype(np.uint16)
-        pt = np.arange(B * n_pages, dtype=np.int32).reshape(B, n_pages)
-        emb = self.emb.float().cpu().numpy()
-        wqkv = self.wqkv.float().cpu().numpy()
-        wlm = self.wlm.float().cpu().numpy()
+
+        def make():
+            arena_b = _bf16_normal(rng, B * n_pages * Hkv * 2 * 16 * 128)
+            pt = rng.permutation(B * n_pages).astype(np.int32).reshape(B, n_pages)
+            pt[:, :cls.PROMPT // 16] = pt[0, :cls.PROMPT // 16]
+            emb = rng.standard_normal((cls.VOCAB, D), dtype=np.float32)
+            wqkv = rng.standard_normal(((Hq + 2 * Hkv) * 128, D), dtype=np.float32) / np.float32(64)
+            wlm = rng.standard_normal((cls.VOCAB, D), dtype=np.float32) * np.float32(0.05)
+            return arena_b, pt, emb, wqkv, wlm
+        arena_b, pt, emb, wqkv, wlm = _cached("model", make)
         pool = ThreadPoolExecutor(max_workers=threads)
         tok = np.zeros(B, dtype=np.int64)
         t0 = time.perf_counter()
         steps = 0
-        while steps == 0 or time.perf_counter() - t0 < budget_s:
+        while steps == 0 or (time.perf_counter() - t0 < budget_s and steps < cls.GEN):
             x = emb[tok]
             qkv = x @ wqkv.T
             q = (qkv[:, :D].astype(np.float32).view(np.uint32) >> 16).astype(np.uint16)
-            lens = np.full(B, self.PROMPT + steps + 1, dtype=np.int32)
+            lens = np.full(B, cls.PROMPT + steps + 1, dtype=np.int32)
             o = orc.paged_gqa_attention(q.reshape(B, Hq, 128), arena_b, pt, lens, Hq, Hkv,
                                         128 ** -0.5, n_threads=threads)
             logits = (o.reshape(B, D) @ wlm.T).astype(np.float32)
             tok = np.array(list(pool.map(lambda b: orc.sample_row(
                 logits[b], 0.8, 50, 0.9, orc.sample_u24(1234, b, steps)), range(B))))
             steps += 1
-            if steps >= self.GEN:
-                break
         dt = time.perf_counter() - t0
         pool.shutdown()
-        return {"value": B * steps / dt, "unit": self.unit, "cores": threads, "kind": "port",
-                "seconds": dt,
-                "sample": f"1 group x 16 rollouts, {steps} model decode steps from a 512-token "
-                          f"prompt (embedding, QKV and LM-head matmuls, attention, sampling)"}
+        return _port_result(B * steps / dt, cls.unit, threads, dt,
+                            f"1 group x 16 rollouts, {steps} model decode steps from a 512-token "
+                            f"prompt (embedding, QKV and LM-head matmuls, attention, sampling)")
 
-    def config(self):
-        return super().config() | {
-            "model": "embedding 32,000 x 4,096, QKV 4,096 -> 6,144, LM head 4,096 -> 32,000; "
-                     "bf16 weights N(0, s), fp32 accumulation",
-            "prompts": "seeded token ids, K / V prefilled by the model (rt_rollout_prefill, "
-                       "untimed setup)",
-            "prefill_tokens_per_s": round(self.prefill_tokens_per_s),
-            "gemm_flops_per_token": self.gemm_flops_per_token}
+    def details(self):
+        return super().details() | {"prefill_tokens_per_s": round(self.prefill_tokens_per_s),
+                                    "gemm_flops_per_token": self.gemm_flops_per_token}
 
 
 WORKLOADS = {"lm_head": LmHeadWorkload, "rollout": RolloutWorkload,
-             "rollout_model": RolloutModelWorkload, "attention": AttentionWorkload,
-             "sampling": SamplingWorkload, "decode_ring": DecodeRingWorkload}
+             "rollout_c4": RolloutC4Workload, "rollout_model": RolloutModelWorkload,
+             "attention": AttentionWorkload, "sampling": SamplingWorkload,
+             "decode_ring": DecodeRingWorkload}
 
 
 def config1_cpu_path(reps=5):
-    """BASELINE config 1, the reference's CPU path: 10,000 hw_desc_t decode
-    descriptors (seed 0, max_tokens 2048) through hw_ring + hw_worker_sim,
-    producer and worker on two host threads, command depth capped at 1,024.
-    The reference's own C sources (compiled unmodified into oracle/_ref)
-    are timed beside this repo's C implementation of the same API, and the
-    two 64-byte completion streams are compared byte for byte."""
+    """BASELINE config 1, the reference's CPU path:
+    - 10,000 hw_desc_t decode descriptors (seed 0, max_tokens 2048) through
+      hw_ring + hw_worker_sim, producer and worker on two host threads,
+      command depth capped at 1,024;
+    - host batching: the reference benchmark's 10,000 step descriptors
+      (src/main.c shape) submitted by decode_batch_submit in windows of 32
+      into a CommandRing and consumed by a second thread.
+    The reference's own C sources (compiled unmodified into oracle/_ref) are
+    timed beside this repo's C implementation of the same API, and the
+    output streams (64-byte completions; CommandRing records with their
+    batch stamps) are compared byte for byte."""
     orc = ge.load_oracle()
     try:
         ref = orc.Harness("ref")
@@ -955,19 +1321,31 @@ def config1_cpu_path(reps=5):
     r = [ref.run_c1(descs, depth_cap=1024) for _ in range(reps)]
     m = [mine.run_c1(descs, depth_cap=1024) for _ in range(reps)]
     rs, ms = statistics.median(x[3] for x in r), statistics.median(x[3] for x in m)
+    d, _, _ = _decode_ring_inputs(0)
+    rb = [ref.run_decode_batch(d, 32) for _ in range(4 * reps)]
+    mb = [mine.run_decode_batch(d, 32) for _ in range(4 * reps)]
+    rbs, mbs = statistics.median(x[1] for x in rb), statistics.median(x[1] for x in mb)
     return {"workload": "BASELINE config 1: 10,000 hw_desc_t, seed 0, depth 1,024",
             "kind": "reference", "cores": 2,
             "reference_descs_per_s": len(descs) / rs, "reference_tokens_per_s": r[0][1] / rs,
             "mine_descs_per_s": len(descs) / ms, "mine_tokens_per_s": m[0][1] / ms,
             "completion_stream_equal": bool(np.array_equal(r[0][0].view(np.uint8),
                                                            m[0][0].view(np.uint8))),
-            "reps": reps}
+            "reps": reps,
+            "decode_batch": {
+                "workload": "10,000 src/main.c step descriptors, decode_batch_submit windows of 32, "
+                            "CommandRing 4,096 slots, consumer thread",
+                "reference_descs_per_s": len(d) / rbs, "mine_descs_per_s": len(d) / mbs,
+                "command_ring_stream_equal": bool(rb[0][0].tobytes() == mb[0][0].tobytes()),
+                "reps": 4 * reps}}
 
 
-def roofline_block(wl, achieved_gbs, ms, peaks, src, traffic):
+def roofline_block(wl, achieved_gbs, ms, peaks, src, traffic, traffic_commit=None):
     """The dominant kernel against its bound: HBM GB/s, or for a tensor-core
     workload bf16 TFLOP/s against the burst GEMM peak (the kernel is timed
     alone), with its HBM fraction beside it."""
+    tsrc = (f"profiles/ncu_traffic.txt (one ncu capture at commit {traffic_commit})"
+            if traffic is not None else None)
     if getattr(wl, "bound", "hbm") == "tensor":
         tf = wl.flops / (ms / 1e3) / 1e12
         peak = peaks.get("bf16_tflops", 1590.0)
@@ -977,13 +1355,84 @@ def roofline_block(wl, achieved_gbs, ms, peaks, src, traffic):
                 if src == "measured" else "fallback 1.59 PFLOP/s",
                 "frac_of_nominal_2250": tf / 2250.0,
                 "hbm_achieved_gbs": achieved_gbs, "hbm_frac": achieved_gbs / peaks["hbm_gbs"],
-                "traffic": traffic, "kernel": wl.kernel}
+                "traffic": traffic, "traffic_source": tsrc, "kernel": wl.kernel}
     return ({"bound": "hbm", "achieved": achieved_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
              "frac": achieved_gbs / peaks["hbm_gbs"],
              "peak_source": f"{src} copy bandwidth (MEASURED_PEAKS.json hbm_gbs)"
              if src == "measured" else "fallback 6.65 TB/s",
-             "frac_of_nominal_8tbs": achieved_gbs / 8000.0, "traffic": traffic, "kernel": wl.kernel}
+             "frac_of_nominal_8tbs": achieved_gbs / 8000.0, "traffic": traffic,
+             "traffic_source": tsrc, "kernel": wl.kernel}
             | ({"note": wl.roofline_note} if hasattr(wl, "roofline_note") else {}))
+
+
+def loop_kernel_report(prof):
+    """Per-kernel averages of a host-stepped replay; attention GB/s over the
+    deduplicated KV bytes (each shared prefix once per pass)."""
+    attn_s = prof["ms_attention"] / 1e3
+    keys = ("ms_schedule", "ms_prepare", "ms_attention", "ms_logits", "ms_sample")
+    tot = sum(prof[k] for k in keys)
+    return prof["attn_bytes_unique"] / attn_s / 1e9, {
+        "source": "rt_rollout_profile host-stepped replay, CUDA events per kernel",
+        "passes": prof["passes"],
+        "avg_us": {k[3:]: 1e3 * prof[k] / max(prof["passes"], 1) for k in keys},
+        "share": {k[3:]: prof[k] / tot for k in keys},
+        "attn_logical_GBps": prof["attn_bytes_logical"] / attn_s / 1e9,
+        "attn_unique_bytes_per_launch": prof["attn_bytes_unique"] / max(prof["attn_launches"], 1),
+    }
+
+
+def timed_steps(torch, wl, steps, warmup, dev_index):
+    """W untimed steps, then K steps between CUDA events on the launching
+    stream with a synchronize on both sides; clocks sampled meanwhile."""
+    for _ in range(warmup):
+        wl.step()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(dev_index)
+    clocks.start()
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(s)
+    for _ in range(steps):
+        wl.step()
+    e1.record(s)
+    torch.cuda.synchronize()
+    clocks.stop()
+    return e0.elapsed_time(e1) / steps, clocks.report()
+
+
+def extra_block(cls, args, dev, steps, warmup, peaks, src):
+    """One more BASELINE config measured in the same run (N = 1): device
+    value with its roofline, e2e through host buffers, clocks, error word,
+    and for config 4 the latency and trajectory checks."""
+    import torch
+    wl = cls(args, 0, 1, dev)
+    ms, clocks = timed_steps(torch, wl, steps, warmup, 0)
+    wl.last_ms = ms
+    err = wl.check_errors()
+    out = {"config": wl.config(), "metric": wl.metric, "unit": wl.unit,
+           "value": wl.units_per_step() / (ms / 1e3), "ms_per_step": ms, "steps": steps,
+           "warmup": warmup, "device_error_code": err, "clocks": clocks}
+    traffic, commit = ncu_traffic(wl.kernel, wl.name)
+    if isinstance(wl, RolloutWorkload):
+        achieved, rep = loop_kernel_report(wl.kernel_profile())
+        out["kernels"] = rep
+        out["gpu_launches"] = wl.gpu_launches(steps)
+        out["roofline"] = roofline_block(wl, achieved, rep["avg_us"]["attention"] / 1e3, peaks, src,
+                                         traffic, commit)
+        out["trajectory_check"] = wl.trajectory_check()
+        out["device_trace"] = wl.trace_report()
+    else:
+        out["roofline"] = roofline_block(wl, wl.bytes / (ms / 1e3) / 1e9, ms, peaks, src,
+                                         traffic, commit)
+        out["gpu_launches"] = wl.gpu_launches(steps)
+    e2e = wl.e2e(max(3, min(steps, 20)), min(warmup, 3))
+    out["e2e"] = {k: v for k, v in e2e.items() if k != "ms_per_step"}
+    out["details"] = wl.details()
+    del wl
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return out
 
 
 # -------------------------------------------------------------------- main
@@ -1000,7 +1449,8 @@ def run_mine(args):
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
-    wl = WORKLOADS[args.workload](args, rank, world, dev)
+    cls = WORKLOADS[args.workload]
+    wl = cls(args, rank, world, dev)
     for _ in range(args.warmup):
         wl.step()
     torch.cuda.synchronize()
@@ -1023,9 +1473,18 @@ def run_mine(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
         dist.barrier()
+    wl.last_ms = ms
+    # every rank's share is the same size (groups split evenly), so the
+    # whole-job rate is the per-rank units over the slowest rank's time x N
+    value = wl.units_per_step() / (ms / 1e3) * world
     err = wl.check_errors()
-    n_launch = wl.gpu_launches(args.steps) if wl.launches_per_step is None else \
-        wl.launches_per_step * args.steps
+    n_launch = wl.gpu_launches(args.steps)
+    traj = wl.trajectory_check() if hasattr(wl, "trajectory_check") else None
+    diag = None
+    if world > 1 and hasattr(wl, "rank_diagnostics"):
+        mine_d = wl.rank_diagnostics()
+        diag = [None] * world
+        dist.all_gather_object(diag, mine_d)
     prof = wl.kernel_profile() if hasattr(wl, "kernel_profile") else None
     e2e = None if args.no_e2e else wl.e2e(args.steps, args.warmup)
     if world > 1 and e2e is not None:
@@ -1034,83 +1493,91 @@ def run_mine(args):
         e2e["value"] = wl.units_per_step() / (float(t.item()) / 1e3) * world
         e2e["ms_per_step"] = float(t.item())
     cpu = c1 = trace = None
+    peaks, src = measured_peaks()
     if rank == 0 and world == 1 and not args.no_cpu:
-        cpu = wl.cpu_sample(os.cpu_count() or 1)
+        cpu = cls.cpu_port(args, os.cpu_count() or 1, 10.0)
+        cpu.pop("seconds", None)
         c1 = config1_cpu_path()
         if hasattr(wl, "trace_report"):
             trace = wl.trace_report()
-
+    details = wl.details()
+    if prof is not None:
+        # dominant kernel of the loop: paged attention, per-launch average
+        # from the host-stepped replay's CUDA events
+        achieved, prof_report = loop_kernel_report(prof)
+        roof_ms = prof_report["avg_us"]["attention"] / 1e3
+    else:
+        achieved = wl.bytes / (ms / 1e3) / 1e9
+        prof_report, roof_ms = None, ms
+    traffic, commit = ncu_traffic(cls.kernel, cls.name)
+    roof = roofline_block(wl, achieved, roof_ms, peaks, src, traffic, commit)
+    if world > 1 and getattr(wl, "nccl", None):
+        wl.nccl.close()
+    del wl
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    extra = {}
+    if world == 1 and args.workload == "rollout" and not args.no_extra:
+        extra["attention_c2"] = extra_block(AttentionWorkload, args, dev, 50, 10, peaks, src)
+        extra["sampling_c3"] = extra_block(SamplingWorkload, args, dev, 50, 10, peaks, src)
+        extra["continuous_batching_c4"] = extra_block(RolloutC4Workload, args, dev, 3, 3, peaks,
+                                                      src)
     if rank == 0:
-        peaks, src = measured_peaks()
-        if prof is not None:
-            # dominant kernel of the loop: paged attention, per-launch average
-            # from the host-stepped replay's CUDA events
-            attn_s = prof["ms_attention"] / 1e3
-            achieved = prof["attn_bytes_unique"] / attn_s / 1e9
-            tot = sum(prof[k] for k in ("ms_schedule", "ms_prepare", "ms_attention", "ms_logits",
-                                        "ms_sample"))
-            prof_report = {
-                "source": "rt_rollout_profile host-stepped replay, CUDA events per kernel",
-                "passes": prof["passes"],
-                "avg_us": {k[3:]: 1e3 * prof[k] / max(prof["passes"], 1)
-                           for k in ("ms_schedule", "ms_prepare", "ms_attention", "ms_logits",
-                                     "ms_sample")},
-                "share": {k[3:]: prof[k] / tot for k in ("ms_schedule", "ms_prepare",
-                                                         "ms_attention", "ms_logits", "ms_sample")},
-                "attn_logical_GBps": prof["attn_bytes_logical"] / attn_s / 1e9,
-                "attn_unique_bytes_per_launch": prof["attn_bytes_unique"] / max(prof["attn_launches"], 1),
-            }
-        else:
-            achieved = wl.bytes / (ms / 1e3) / 1e9
-            prof_report = None
-        traffic = ncu_traffic(wl.kernel, wl.name)
         line = {
-            "metric": wl.metric, "value": wl.units_per_step() / (ms / 1e3) * world,
-            "unit": wl.unit, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "strong" if wl.name.startswith("grpo_rollouts_c5") else "weak",
-            "vs_baseline": None, "dtype": getattr(wl, "dtype", "bf16"),
-            "data": "synthetic (Philox N(0,1), seeded)",
-            "config": wl.config() | {"parallelism": f"replicas{world}" if world > 1 else "single"},
-            "roofline": roofline_block(wl, achieved, ms, peaks, src, traffic),
+            "metric": cls.metric, "value": value, "unit": cls.unit, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": cls.scaling, "vs_baseline": None,
+            "dtype": cls.dtype, "data": "synthetic (Philox N(0,1), seeded)",
+            "config": cls.line_config(args, world),
+            "roofline": roof,
             "cpu_baseline": cpu,
             "cpu_path_config1": c1,
-            "e2e": None if e2e is None else {k: e2e[k] for k in ("value", "unit", "h2d_bytes_per_step",
-                                                                 "d2h_bytes_per_step")},
+            "e2e": None if e2e is None else {k: e2e[k] for k in e2e if k != "ms_per_step"},
             "gpu_launches": n_launch,
+            "trajectory_check": traj,
             "kernels": prof_report,
+            "per_rank": diag,
             "device_trace": trace,
             "clocks": clocks.report(),
             "device_error_code": err,
-        }
+            "details": details,
+        } | extra
         print(json.dumps(line), flush=True)
+    failed = bool(err) or (traj is not None and traj["result"] != "equal") or any(
+        b.get("device_error_code") or (b.get("trajectory_check") or {}).get("result", "equal")
+        != "equal" for b in extra.values())
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    return 3 if failed else 0
 
 
 def run_reference(args):
+    """The CPU implementation of the same workload on this host's cores,
+    rank 0 only (other ranks exit without work): W warm-up samples, then K
+    timed samples, each a bounded sample of the workload sized so the whole
+    run stays within a few minutes; value = the median sample.  Inputs are
+    numpy; this runtime is not loaded and the GPU is not touched."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
-        return
-    import torch
-    dev = torch.device("cuda", 0) if torch.cuda.is_available() else None
-    if dev is None:
-        print(json.dumps({"impl": "reference", "unavailable": "needs a GPU box to build inputs"}))
-        return
-    wl = WORKLOADS[args.workload](args, 0, 1, dev)
+        return 0
+    cls = WORKLOADS[args.workload]
     threads = os.cpu_count() or 1
-    samples = [wl.cpu_sample(threads) for _ in range(max(1, min(args.steps, 3)))]
-    v = statistics.median(s["value"] for s in samples)
-    cpu = samples[0] | {"value": v}
+    budget = max(0.5, min(10.0, 90.0 / (args.steps + args.warmup)))
+    for _ in range(args.warmup):
+        cls.cpu_port(args, threads, budget)
+    samples = [cls.cpu_port(args, threads, budget) for _ in range(args.steps)]
+    v = statistics.median(x["value"] for x in samples)
+    cpu = samples[0] | {"value": v, "budget_s_per_step": budget}
     cpu.pop("seconds", None)
     print(json.dumps({
-        "impl": "reference", "metric": wl.metric, "value": v, "unit": wl.unit, "n_gpus": world,
-        "steps": len(samples), "warmup": 0, "higher_is_better": True,
-        "config": wl.config(), "cpu_baseline": cpu,
-        "e2e": {"value": v, "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "impl": "reference", "metric": cls.metric, "value": v, "unit": cls.unit, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+        "scaling": cls.scaling, "config": cls.line_config(args, world), "cpu_baseline": cpu,
+        "e2e": {"value": v, "unit": cls.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
+    return 0
 
 
 def main():
@@ -1122,23 +1589,26 @@ def main():
     ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
     ap.add_argument("--chunk-pages", type=int, default=0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="rollout at N = 1: skip the config-2/3/4 blocks")
     ap.add_argument("--no-e2e", action="store_true",
                     help="skip the end-to-end leg (for ncu runs: the decode_ring e2e leg needs "
                          "its persistent worker to run beside the host pump)")
     ap.add_argument("--groups", type=int, default=0,
                     help="rollout only: GRPO groups (default 512; fewer keep ncu captures small)")
     ap.add_argument("--ncu-replay", type=int, default=0,
-                    help="rollout only: run the host-stepped replay of this many rollouts and "
-                         "exit (plain kernel launches, for ncu captures)")
+                    help="rollout workloads: run the host-stepped replay of this many rollouts "
+                         "and exit (plain kernel launches, for ncu captures)")
     args = ap.parse_args()
     if args.ncu_replay:
         import torch
         torch.cuda.set_device(0)
-        wl = WORKLOADS["rollout"](args, 0, 1, torch.device("cuda", 0))
+        name = args.workload if args.workload.startswith("rollout") else "rollout"
+        wl = WORKLOADS[name](args, 0, 1, torch.device("cuda", 0))
         prof = wl.kernel_profile(args.ncu_replay)
         print(json.dumps({"ncu_replay": args.ncu_replay, "profile": prof}), flush=True)
-        return
-    quick = not args.workload.startswith("rollout")   # rollout steps are whole RL steps (~seconds)
+        return 0
+    quick = not args.workload.startswith("rollout")   # rollout steps are whole RL steps
     if args.steps is None:
         args.steps = 200 if quick else 3
     if args.warmup is None:
@@ -1146,10 +1616,9 @@ def main():
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
-        run_reference(args)
-    else:
-        run_mine(args)
+        return run_reference(args)
+    return run_mine(args)
 
 
 if __name__ == "__main__":
-    main()
+    sys.exit(main())

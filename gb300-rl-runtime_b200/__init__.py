@@ -662,6 +662,38 @@ class DeviceTrace:
         return out[:min(n, total.value, self.capacity)], total.value
 
 
+def replay_trajectories(requests, traj, rows, vocab, logit_std=2.0, chunk=2048, device="cuda"):
+    """Re-derive the tokens a synthetic-logits loop (RT_ROLLOUT_DECODE_FULL)
+    must have produced for the trajectory rows `rows` (consume indices into
+    the request array) and compare them with `traj` (a host int array
+    [n_rows][max_new]): the loop's logits for (request rng_seed, request low
+    32 bits, token index) are regenerated with rt_logits_synth and sampled by
+    rt_sample_rows with the request's parameters.  Returns (tokens checked,
+    list of (row, token index, expected, got) mismatches)."""
+    import numpy as np
+    import torch
+    meta = [(int(i), t) for i in rows for t in range(int(requests["max_tokens"][i]))]
+    bad = []
+    for c0 in range(0, len(meta), chunk):
+        part = meta[c0:c0 + chunk]
+        logits = torch.empty(len(part), vocab, dtype=torch.float32, device=device)
+        rq = [int(requests["request_id"][i]) & 0xFFFFFFFF for i, _ in part]
+        seed = [int(requests["rng_seed"][i]) for i, _ in part]
+        for k, (_, t) in enumerate(part):
+            logits_synth(logits[k], vocab, seed[k], rq[k], t, logit_std)
+        tab = sample_row_table(np.array([float(requests["temperature"][i]) for i, _ in part]),
+                               np.array([int(requests["top_k"][i]) for i, _ in part]),
+                               np.array([float(requests["top_p"][i]) for i, _ in part]),
+                               np.array(rq, dtype=np.uint32), np.array([t for _, t in part]),
+                               np.array(seed, dtype=np.uint64))
+        tok = sample_rows(logits, torch.from_numpy(tab.view(np.uint8)).to(device), vocab)
+        tok = tok.cpu().numpy()
+        for k, (i, t) in enumerate(part):
+            if int(tok[k]) != int(traj[i, t]):
+                bad.append((i, t, int(tok[k]), int(traj[i, t])))
+    return len(meta), bad
+
+
 def logits_synth(out, vocab, seed, request_lo, token_index, logit_std, stream=None):
     check(lib().rt_logits_synth(_ptr(out), vocab, seed, request_lo, token_index, logit_std,
                                 _stream_ptr(stream)), "rt_logits_synth")

@@ -73,14 +73,23 @@ rt_count_u32(volatile uint32_t *p)
 #endif
 }
 
-/* Byte copy used for packed ring records.  Packed structs such as the 34-byte
- * RolloutRequest sit at unaligned addresses, so the copy must not assume any
- * alignment beyond one byte. */
+/* Copy of one packed ring record.  Packed structs such as the 34-byte
+ * RolloutRequest sit at unaligned addresses, so the copy assumes no
+ * alignment beyond one byte.  On the host it is a plain memcpy: the ring
+ * index load before it (acquire) or the index store after it (release)
+ * orders it, so the record needs no volatile access of its own, and the
+ * compiler may move it in whole words.  On the device (only the done-ring
+ * slow path copies records this way) it stays a byte loop of volatile
+ * accesses to the mapped host memory. */
 static inline RT_HD void
 rt_copy_bytes(void *dst, const volatile void *src, uint32_t n)
 {
+#if defined(__CUDA_ARCH__)
     const volatile uint8_t *s = (const volatile uint8_t *)src;
     uint8_t *d = (uint8_t *)dst;
     for (uint32_t i = 0; i < n; i++)
         d[i] = s[i];
+#else
+    __builtin_memcpy(dst, (const void *)src, n);
+#endif
 }

@@ -185,6 +185,64 @@ hx_run_c1(const hw_desc_t *in, uint32_t n, uint32_t depth_cap, uint32_t doorbell
     return 0;
 }
 
+/* ---- host batching (host side): decode_batch_push /
+ * decode_batch_submit windows of `window` descriptors into a CommandRing
+ * (reference src/decode_batch.c:12-42) on this thread, ring_consume of every
+ * record on a second thread into out[] (ring order).  Returns 0 and the
+ * seconds from the first push to the last record consumed. ---- */
+typedef struct {
+    CommandRing *ring;
+    Descriptor *out;
+    uint32_t n;
+} hx_consumer_arg;
+
+static void *
+hx_consumer_main(void *p)
+{
+    hx_consumer_arg *a = (hx_consumer_arg *)p;
+    uint32_t got = 0;
+    while (got < a->n) {
+        if (ring_consume(a->ring, &a->out[got]))
+            got++;
+        else
+            hx_relax();
+    }
+    return NULL;
+}
+
+int
+hx_run_decode_batch(const Descriptor *in, uint32_t n, uint32_t window, Descriptor *out,
+                    double *seconds)
+{
+    CommandRing *ring = ring_create();
+    DecodeDispatchBatch batch;
+    hx_consumer_arg arg;
+    pthread_t th;
+    double t0, t1;
+
+    if (!ring || window == 0 || window > DECODE_DESCRIPTOR_BATCH_LIMIT)
+        return -1;
+    arg.ring = ring;
+    arg.out = out;
+    arg.n = n;
+    if (pthread_create(&th, NULL, hx_consumer_main, &arg) != 0)
+        return -1;
+    t0 = hx_now();
+    for (uint32_t i = 0; i < n; i += window) {
+        const uint32_t k = n - i < window ? n - i : window;
+        decode_batch_reset(&batch);
+        for (uint32_t j = 0; j < k; j++)
+            decode_batch_push(&batch, &in[i + j]);
+        while (decode_batch_submit(ring, &batch) != 0)   /* ring full: wait for the consumer */
+            hx_relax();
+    }
+    pthread_join(th, NULL);
+    t1 = hx_now();
+    *seconds = t1 - t0;
+    ring_destroy(ring);
+    return 0;
+}
+
 /* ---- known-answer scripts (reference test/test_hw_ring.c:98-154) ---- */
 int
 hx_kat_submit(uint32_t gpu_group, uint32_t arena_id, uint32_t rollout, uint64_t kv,

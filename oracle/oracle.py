@@ -222,12 +222,24 @@ class Harness:
             "hx_script_kv_prefix": (_u32, [_P]),
             "hx_script_reward": (_u32, [_P, _P]),
             "hx_script_arena_bitmap": (_u32, [_P, _u32]),
+            "hx_run_decode_batch": (_int, [_P, _u32, _u32, _P, _P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(l, name)
             fn.restype = res
             fn.argtypes = args
         self.lib = l
+
+    def run_decode_batch(self, descs, window=32):
+        """decode_batch_submit windows of `window` into a CommandRing with a
+        consumer thread; returns (the consumed records in ring order, seconds)."""
+        descs = np.ascontiguousarray(descs, dtype=DESCRIPTOR_DTYPE)
+        out = np.zeros(len(descs), dtype=DESCRIPTOR_DTYPE)
+        secs = np.zeros(1, dtype=np.float64)
+        rc = self.lib.hx_run_decode_batch(_ptr(descs), len(descs), window, _ptr(out), _ptr(secs))
+        if rc != 0:
+            raise RuntimeError(f"hx_run_decode_batch failed ({rc})")
+        return out, float(secs[0])
 
     def gen_c1(self, n=10000, seed=0, max_tokens=2048):
         out = np.zeros(n, dtype=HW_DESC_DTYPE)
