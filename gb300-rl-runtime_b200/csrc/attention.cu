@@ -532,7 +532,8 @@ template <int G>
 __device__ __forceinline__ bool process_group_item(const CUtensorMap &kv_map, const AttnArgs &a,
                                                    uint64_t gi, uint32_t n_live, uint32_t ring0,
                                                    uint64_t *gbars, uint32_t &gphases,
-                                                   uint64_t policy)
+                                                   uint64_t policy, int32_t *s_pg,
+                                                   uint32_t *s_cnt)
 {
     constexpr int MPW = 16 / G;                        // member sequences per warp
     constexpr int RB = (16 * G + 16 * kWarps - 1) / (16 * kWarps);  // row blocks per group
@@ -578,23 +579,35 @@ __device__ __forceinline__ bool process_group_item(const CUtensorMap &kv_map, co
                 pg_hi = 0;
         }
     }
-    auto issue = [&](int i) {  // warp 0 only
-        const int pg = __shfl_sync(0xffffffffu, i < 32 ? pg_lo : pg_hi, i & 31);
-        if (lane == 0) {
-            const int s = i % kGroupStages;
-            const uint32_t bar = rt::smem_u32(&gbars[s]);
-            const uint32_t dst = ring0 + (uint32_t)(s * kStageBytes);
-            const int32_t row_k = (int32_t)(((int64_t)pg * Hkv + h) * 32);
-            rt::mbar_arrive_expect_tx(bar, (uint32_t)kStageBytes);
-            rt::tma_load_2d(dst, &kv_map, 0, row_k, bar, policy);
-            rt::tma_load_2d(dst + 2048u, &kv_map, 64, row_k, bar, policy);
-            rt::tma_load_2d(dst + 4096u, &kv_map, 0, row_k + 16, bar, policy);
-            rt::tma_load_2d(dst + 6144u, &kv_map, 64, row_k + 16, bar, policy);
-        }
+    // One page into its stage (a single thread).
+    auto issue_page = [&](int i, int pg) {
+        const int s = i % kGroupStages;
+        const uint32_t bar = rt::smem_u32(&gbars[s]);
+        const uint32_t dst = ring0 + (uint32_t)(s * kStageBytes);
+        const int32_t row_k = (int32_t)(((int64_t)pg * Hkv + h) * 32);
+        rt::mbar_arrive_expect_tx(bar, (uint32_t)kStageBytes);
+        rt::tma_load_2d(dst, &kv_map, 0, row_k, bar, policy);
+        rt::tma_load_2d(dst + 2048u, &kv_map, 64, row_k, bar, policy);
+        rt::tma_load_2d(dst + 4096u, &kv_map, 0, row_k + 16, bar, policy);
+        rt::tma_load_2d(dst + 6144u, &kv_map, 64, row_k + 16, bar, policy);
     };
-    if (warp == 0)
-        for (int i = 0; i < np && i < kGroupStages; i++)
-            issue(i);
+    // When the chunk is longer than the ring, stages are refilled while the
+    // item runs, by whichever warp finishes a stage last (below), so the page
+    // ids go to shared memory where every warp can read them.
+    const bool refill = np > kGroupStages;
+    if (warp == 0) {
+        if (refill) {
+            s_pg[lane] = pg_lo;
+            s_pg[lane + 32] = pg_hi;
+        }
+        for (int i = 0; i < np && i < kGroupStages; i++) {
+            const int pg = __shfl_sync(0xffffffffu, i < 32 ? pg_lo : pg_hi, i & 31);
+            if (lane == 0)
+                issue_page(i, pg);
+        }
+    }
+    if (refill)
+        __syncthreads();  // s_pg is complete
 
     // A member takes part when the group covers exactly its skipped pages.
     auto member_ok = [&](int m) -> bool {
@@ -643,31 +656,19 @@ __device__ __forceinline__ bool process_group_item(const CUtensorMap &kv_map, co
     const int mi = lane >> 3, rr = lane & 7;
     const uint32_t k_row = (uint32_t)((((mi >> 1) << 3) + rr) * 128);
     const uint32_t v_row = (uint32_t)((((mi & 1) << 3) + rr) * 128);
-    // When the whole chunk fits the ring (the usual case) every page is
-    // issued up front and the warps never wait for each other within the
-    // item; longer chunks re-issue stages behind a per-page CTA barrier.
-    const bool refill = np > kGroupStages;
+    // The warps never wait for each other within the item: when the whole
+    // chunk fits the ring every page is issued up front; otherwise each stage
+    // is refilled by the last warp to finish reading it.
     for (int i = 0; i < np; i++) {
         const int s = i % kGroupStages;
         const bool ok = rt::mbar_wait_bounded(rt::smem_u32(&gbars[s]), (gphases >> s) & 1u,
                                               kWaitLimitNs);
-        if (!refill) {
-            if (!__all_sync(0xffffffffu, ok)) {
-                if (lane == 0)
-                    flag_error(a.error, kErrTimeout);
-                return false;  // the caller stops the CTA; issued copies are waited for there
-            }
-        } else if (!__syncthreads_and(ok)) {
-            if (threadIdx.x == 0) {
+        if (!__all_sync(0xffffffffu, ok)) {
+            if (lane == 0)
                 flag_error(a.error, kErrTimeout);
-                // Give the copies still in flight (pages i .. i+11) a bounded
-                // chance to land before the shared memory is released.
-                for (int j = i; j < np && j < i + kGroupStages; j++) {
-                    const int s2 = j % kGroupStages;
-                    (void)rt::mbar_wait_bounded(rt::smem_u32(&gbars[s2]), (gphases >> s2) & 1u,
-                                                kWaitLimitNs / 4);
-                }
-            }
+            // the caller stops the CTA; the copies issued so far are waited
+            // for there (bounded), and warps still waiting on pages that will
+            // not be refilled run into their own bounded waits
             return false;
         }
         gphases ^= 1u << s;
@@ -731,11 +732,18 @@ __device__ __forceinline__ bool process_group_item(const CUtensorMap &kv_map, co
             }
         }
         if (refill) {
-            // Every warp has read stage s (shared-memory reads only, so the
-            // TMA rewrite needs no proxy fence).
-            __syncthreads();
-            if (warp == 0 && i + kGroupStages < np)
-                issue(i + kGroupStages);
+            // The warp is done with stage s (shared-memory reads only, so the
+            // TMA rewrite needs no proxy fence); the fourth warp to say so
+            // resets the count and refills the stage with page i + stages.
+            __syncwarp();
+            if (lane == 0) {
+                __threadfence_block();
+                if (atomicAdd(&s_cnt[s], 1u) == (uint32_t)kWarps - 1u) {
+                    s_cnt[s] = 0u;
+                    if (i + kGroupStages < np)
+                        issue_page(i + kGroupStages, s_pg[i + kGroupStages]);
+                }
+            }
         }
     }
     if (!active)
@@ -777,12 +785,16 @@ paged_gqa_group_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnArg
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t gbars[kGroupStages];
     __shared__ unsigned long long s_gitem;
+    __shared__ int32_t s_pg[kMaxChunkPages];        // page ids of the current item
+    __shared__ uint32_t s_cnt[kGroupStages];        // warps done with each stage
     const uint32_t raw_u32 = rt::smem_u32(smem_raw);
     const uint32_t base_u32 = (raw_u32 + 1023u) & ~1023u;  // 128-byte swizzle: 1 KiB aligned
     if (threadIdx.x == 0) {
         rt::prefetch_tensormap(&kv_map);
-        for (int s = 0; s < kGroupStages; s++)
+        for (int s = 0; s < kGroupStages; s++) {
             rt::mbar_init(rt::smem_u32(&gbars[s]), 1u);
+            s_cnt[s] = 0u;
+        }
         rt::mbar_fence_init();
     }
     __syncthreads();
@@ -807,7 +819,8 @@ paged_gqa_group_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnArg
             break;
         // A false return means a wait expired (flagged): stop taking items,
         // after giving the copies still in flight a bounded chance to land.
-        const bool ok = process_group_item<G>(kv_map, a, gi, n_live, base_u32, gbars, gphases, policy);
+        const bool ok = process_group_item<G>(kv_map, a, gi, n_live, base_u32, gbars, gphases, policy,
+                                              s_pg, s_cnt);
         if (!__syncthreads_and(ok)) {
             if (threadIdx.x == 0)
                 for (int st = 0; st < kGroupStages; st++)

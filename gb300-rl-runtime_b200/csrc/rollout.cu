@@ -40,6 +40,7 @@ namespace {
 
 constexpr int kSched = 256;  // schedule CTA: one thread per slot (GPU_MAX_ROLLOUTS)
 constexpr uint64_t kDonePushLimitNs = 10000000000ull;  // 10 s bounded wait on a full done ring
+constexpr int kPassesPerIteration = 4;  // passes captured in one graph-loop body
 
 struct RtIo {
     RequestRing *ring;
@@ -863,10 +864,22 @@ schedule_kernel(const Dev d, cudaGraphConditionalHandle handle, int in_graph)
 {
     __shared__ SchedShared sh;
     const bool full = d.decode != RT_ROLLOUT_DECODE_NONE;
+    // Inside the graph loop this kernel is a programmatic dependent of the
+    // previous pass's sampler: wait for its tokens before reading anything
+    // (a no-op for an ordinary launch).
+    rt::grid_dep_wait();
     // The prepare kernel (a programmatic dependent launch) may be scheduled
     // now; it waits for this kernel to complete before reading its outputs.
     rt::grid_dep_launch();
     load_state(d, sh, full);
+    if (sh.ctl.stop) {
+        // An earlier pass of this graph iteration ended the loop (the body
+        // holds several passes): run nothing.  That pass left every slot
+        // disabled, so this pass's decode chain is a no-op too.
+        if (threadIdx.x == 0 && in_graph)
+            cudaGraphSetConditional(handle, 0u);
+        return;
+    }
     const bool stop = schedule_pass(d, sh);
     if (stop) {
         // The decode chain of this pass still runs: make it a no-op.
@@ -1289,15 +1302,31 @@ int engine_build_graph(rt_rollout *e)
     if ((err = cudaGraphAddNode(&node, e->graph, nullptr, 0, &cp)) != cudaSuccess)
         return rt::cuda_fail(err, "rollout: cudaGraphAddNode(conditional)");
     cudaGraph_t body = cp.conditional.phGraph_out[0];
+    // The body holds kPassesPerIteration passes: every iteration of a
+    // conditional WHILE node costs several microseconds of relaunch on top
+    // of the kernels' own boundaries, so one iteration per pass would add it
+    // to every token.  A pass after the one that stopped the loop does
+    // nothing (schedule_kernel returns at once, the decode chain finds every
+    // slot disabled).
 
     if ((err = cudaStreamBeginCaptureToGraph(e->cap, body, nullptr, nullptr, 0,
                                              cudaStreamCaptureModeThreadLocal)) != cudaSuccess)
         return rt::cuda_fail(err, "rollout: cudaStreamBeginCaptureToGraph");
     int rc = RT_OK;
     const Dev &d = e->d;
-    schedule_kernel<<<1, kSched, 0, e->cap>>>(d, h, 1);
-    if (e->cfg.decode_mode != RT_ROLLOUT_DECODE_NONE)
-        rc = launch_decode(e, e->cap, nullptr);
+    for (int k = 0; k < kPassesPerIteration && rc == RT_OK; k++) {
+        // after the first, each pass's schedule kernel is a programmatic
+        // dependent of the previous pass's sampler
+        if (k == 0 || e->cfg.decode_mode == RT_ROLLOUT_DECODE_NONE)
+            schedule_kernel<<<1, kSched, 0, e->cap>>>(d, h, 1);
+        else if ((err = launch_pdl(schedule_kernel, dim3(1), dim3(kSched), e->cap, d, h, 1)) !=
+                 cudaSuccess)
+            rc = rt::cuda_fail(err, "rollout: schedule launch");
+        if (rc != RT_OK)
+            break;
+        if (e->cfg.decode_mode != RT_ROLLOUT_DECODE_NONE)
+            rc = launch_decode(e, e->cap, nullptr);
+    }
     cudaGraph_t captured = nullptr;
     err = cudaStreamEndCapture(e->cap, &captured);
     if (rc != RT_OK)

@@ -46,6 +46,8 @@ constexpr int kThr = 512;            // threads per row
 constexpr int kWarpsPerRow = kThr / 32;
 constexpr int kBins = 4096;          // radix digits of the streamed cutoff select
 constexpr int kCap = 1024;           // candidates handled by the fast path
+constexpr int kCmax = 8192;          // 16-byte chunks whose maxima pass 1 keeps (vocab <= 32768)
+constexpr uint32_t kWarpCap = 160;   // candidates handled by the one-warp tail
 constexpr uint32_t kMaxVocab = 1u << 20;
 
 
@@ -77,6 +79,10 @@ struct __align__(16) Smem {
             uint32_t idx[kCap];
             float val[kCap];
         } sorted;
+        // pass 1 -> pass 2: each 16-byte chunk's maximum (scaled), as bf16
+        // rounded toward +inf, so a chunk whose bf16 maximum is below a
+        // threshold holds no value at or above it
+        uint16_t cmax[kCmax];
     } u;
     uint32_t cand_idx[kCap];
     float cand_val[kCap];
@@ -86,7 +92,23 @@ struct __align__(16) Smem {
     float top[kWarpsPerRow * 16];  // each warp's m largest per-thread maxima (m <= 16)
     uint32_t scan[kWarpsPerRow];
     uint32_t digit, need, count, token, done;
+    float rowmax;                  // largest value > -FLT_MAX of the row (scaled)
 };
+
+// bf16 bits of the smallest bf16 >= x (x not NaN).
+__device__ __forceinline__ uint16_t bf16_round_up(float x)
+{
+    const uint32_t u = __float_as_uint(x);
+    if ((u & 0x7FFFFFFFu) >= 0x7F800000u || (u & 0xFFFFu) == 0u)
+        return (uint16_t)(u >> 16);                     // +-inf, or exact
+    return (u & 0x80000000u) ? (uint16_t)(u >> 16)        // negative: truncation is up
+                             : (uint16_t)((u >> 16) + 1u);  // positive: next bf16 up
+}
+
+__device__ __forceinline__ float bf16_bits_float(uint16_t b)
+{
+    return __uint_as_float((uint32_t)b << 16);
+}
 
 __device__ __forceinline__ uint32_t block_sum_u32(uint32_t v, Smem &s)
 {
@@ -300,6 +322,111 @@ __device__ __forceinline__ void stream_row(const RowReader &rd, uint32_t V, F &&
         f(rd(idx), idx);
 }
 
+// The reference's serial fp32 sum and cumulative walk over the survivors'
+// exponentials e[0 .. ns8) (zero-padded to a multiple of 8; adding +0 leaves
+// the sum and the walk unchanged), one thread; returns the token.
+__device__ __forceinline__ uint32_t serial_walk(const Smem &s, uint32_t ns8, bool topp, float r,
+                                                uint32_t fused, uint32_t V)
+{
+    const float4 *e4 = reinterpret_cast<const float4 *>(s.e);
+    float sum = 0.0f;
+#pragma unroll 2
+    for (uint32_t b = 0; b < ns8 / 8u; b++) {
+        const float4 x = e4[2 * b], y = e4[2 * b + 1];
+        sum = __fadd_rn(sum, x.x);
+        sum = __fadd_rn(sum, x.y);
+        sum = __fadd_rn(sum, x.z);
+        sum = __fadd_rn(sum, x.w);
+        sum = __fadd_rn(sum, y.x);
+        sum = __fadd_rn(sum, y.y);
+        sum = __fadd_rn(sum, y.z);
+        sum = __fadd_rn(sum, y.w);
+    }
+    const float inv = topp ? __fdiv_rn(1.0f, sum) : 0.0f;
+    auto step = [&](float c, float e) {
+        return topp ? (fused ? __fmaf_rn(e, inv, c) : __fadd_rn(c, __fmul_rn(e, inv)))
+                    : __fadd_rn(c, __fdiv_rn(e, sum));
+    };
+    // cum never decreases, and a padding entry repeats the previous value,
+    // so the first entry with cum >= r lies below ns
+    float cum = 0.0f;
+    for (uint32_t b = 0; b < ns8 / 8u; b++) {
+        const float4 x = e4[2 * b], y = e4[2 * b + 1];
+        const float ev[8] = {x.x, x.y, x.z, x.w, y.x, y.y, y.z, y.w};
+        int hit = -1;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            cum = step(cum, ev[i]);
+            if (hit < 0 && cum >= r)
+                hit = i;
+        }
+        if (hit >= 0)
+            return s.u.sorted.idx[8u * b + (uint32_t)hit];
+    }
+    return V - 1u;
+}
+
+// Survivor selection, index sort, exponentials and the serial walk by one
+// warp, for nc <= kWarpCap candidates (cand_*), with no block barrier.  A
+// candidate survives iff fewer than nk candidates are strictly larger; mx is
+// the row maximum (the largest survivor).  Same arithmetic as the block path.
+__device__ __forceinline__ uint32_t warp_tail(Smem &s, uint32_t nc, uint32_t nk, float mx,
+                                              bool topp, float r, uint32_t fused, uint32_t V)
+{
+    const uint32_t lane = threadIdx.x & 31u;
+    uint32_t *keep = reinterpret_cast<uint32_t *>(s.e);  // reused before the exponentials
+    const uint32_t n4 = (nc + 3u) & ~3u;
+    for (uint32_t j = nc + lane; j < n4; j += 32u) {
+        s.cand_val[j] = -INFINITY;
+        s.cand_idx[j] = 0xFFFFFFFFu;
+    }
+    __syncwarp();
+    const float4 *cv4 = reinterpret_cast<const float4 *>(s.cand_val);
+    uint32_t ns = 0;
+    for (uint32_t j0 = 0; j0 < n4; j0 += 32u) {
+        const uint32_t j = j0 + lane;
+        uint32_t k = 0u;
+        if (j < nc) {
+            const float v = s.cand_val[j];
+            uint32_t gt = 0;
+            for (uint32_t i = 0; i < n4 / 4u; i++) {
+                const float4 c = cv4[i];
+                gt += (c.x > v ? 1u : 0u) + (c.y > v ? 1u : 0u) + (c.z > v ? 1u : 0u) +
+                      (c.w > v ? 1u : 0u);
+            }
+            k = gt < nk ? 1u : 0u;
+        }
+        if (j < n4)
+            keep[j] = k;
+        ns += (uint32_t)__popc(__ballot_sync(0xffffffffu, k != 0u));
+    }
+    __syncwarp();
+    const uint4 *ci4 = reinterpret_cast<const uint4 *>(s.cand_idx);
+    const uint4 *kp4 = reinterpret_cast<const uint4 *>(keep);
+    for (uint32_t j = lane; j < nc; j += 32u) {
+        if (!keep[j])
+            continue;
+        const uint32_t id = s.cand_idx[j];
+        uint32_t rank = 0;
+        for (uint32_t i = 0; i < n4 / 4u; i++) {
+            const uint4 c = ci4[i], f = kp4[i];
+            rank += (f.x && c.x < id ? 1u : 0u) + (f.y && c.y < id ? 1u : 0u) +
+                    (f.z && c.z < id ? 1u : 0u) + (f.w && c.w < id ? 1u : 0u);
+        }
+        s.u.sorted.idx[rank] = id;
+        s.u.sorted.val[rank] = s.cand_val[j];
+    }
+    __syncwarp();
+    const uint32_t ns8 = (ns + 7u) & ~7u;
+    for (uint32_t j = lane; j < ns8; j += 32u)
+        s.e[j] = j < ns ? __expf(__fsub_rn(s.u.sorted.val[j], mx)) : 0.0f;
+    __syncwarp();
+    uint32_t tok = 0;
+    if (lane == 0)
+        tok = serial_walk(s, ns8, topp, r, fused, V);
+    return tok;
+}
+
 __global__ void __launch_bounds__(kThr, 2) sample_rows_kernel(const SampleArgs a)
 {
     __shared__ Smem s;
@@ -309,6 +436,9 @@ __global__ void __launch_bounds__(kThr, 2) sample_rows_kernel(const SampleArgs a
     // When launched as a programmatic dependent of the kernel that wrote the
     // logits, wait for it before reading them (a no-op otherwise).
     rt::grid_dep_wait();
+    // A dependent launch after this one (the rollout loop's next schedule
+    // kernel) may be scheduled; it waits for this grid's completion itself.
+    rt::grid_dep_launch();
     if (a.enable && a.enable[blockIdx.x] == 0u)
         return;
     const rt_sample_row_t P = a.rows[blockIdx.x];
@@ -317,13 +447,52 @@ __global__ void __launch_bounds__(kThr, 2) sample_rows_kernel(const SampleArgs a
     rd.scale = P.temperature > 0.0f;
     rd.inv_t = rd.scale ? __fdiv_rn(1.0f, P.temperature) : 1.0f;
 
-    // ---- pass 1: per-thread maximum of the values > -FLT_MAX, NaN / +inf ----
+    // ---- pass 1: per-thread maximum of the values > -FLT_MAX, NaN / +inf,
+    // and (rows of up to kCmax 16-byte chunks, 16-byte aligned) each chunk's
+    // maximum for pass 2 ----
     float tmax = -INFINITY;
     bool bad = false;
-    stream_row(rd, V, [&](float v, uint32_t) {
-        bad |= !(v < INFINITY);  // NaN or +inf
-        tmax = v > -FLT_MAX ? fmaxf(tmax, v) : tmax;
-    });
+    const bool vec = (reinterpret_cast<uintptr_t>(rd.row) & 15u) == 0u;
+    const uint32_t V4 = vec ? V / 4u : 0u;
+    const bool track = vec && V4 <= (uint32_t)kCmax;
+    {
+        const float4 *row4 = reinterpret_cast<const float4 *>(rd.row);
+        constexpr uint32_t kDepth = 8;
+        for (uint32_t base = 0; base < V4; base += kDepth * kThr) {
+            float4 buf[kDepth];
+#pragma unroll
+            for (uint32_t j = 0; j < kDepth; j++) {
+                const uint32_t q = base + j * kThr + (uint32_t)tid;
+                if (q < V4)
+                    buf[j] = __ldg(row4 + q);
+            }
+#pragma unroll
+            for (uint32_t j = 0; j < kDepth; j++) {
+                const uint32_t q = base + j * kThr + (uint32_t)tid;
+                if (q < V4) {
+                    float4 v = buf[j];
+                    if (rd.scale) {
+                        v.x = __fmul_rn(v.x, rd.inv_t);
+                        v.y = __fmul_rn(v.y, rd.inv_t);
+                        v.z = __fmul_rn(v.z, rd.inv_t);
+                        v.w = __fmul_rn(v.w, rd.inv_t);
+                    }
+                    bad |= !(v.x < INFINITY) || !(v.y < INFINITY) || !(v.z < INFINITY) ||
+                           !(v.w < INFINITY);
+                    const float cm = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
+                    // cm > -FLT_MAX: cm is a value > -FLT_MAX of the chunk
+                    tmax = cm > -FLT_MAX ? fmaxf(tmax, cm) : tmax;
+                    if (track)
+                        s.u.cmax[q] = bf16_round_up(cm);
+                }
+            }
+        }
+        for (uint32_t idx = 4u * V4 + (uint32_t)tid; idx < V; idx += kThr) {
+            const float v = rd(idx);
+            bad |= !(v < INFINITY);  // NaN or +inf
+            tmax = v > -FLT_MAX ? fmaxf(tmax, v) : tmax;
+        }
+    }
     if (tid == 0) {
         uint32_t ph[4];
         rt::philox4x32_10((uint32_t)P.step, (uint32_t)(P.step >> 32), P.rollout_id, 0u,
@@ -384,6 +553,8 @@ __global__ void __launch_bounds__(kThr, 2) sample_rows_kernel(const SampleArgs a
             }
             if (g2 < nk && e2 >= nk)
                 s.red_f[0] = v;  // every such thread holds the same value
+            if (g2 == 0u)
+                s.rowmax = v;    // the largest per-thread maximum: the row maximum
         }
         __syncthreads();
         const float tau0 = s.red_f[0];
@@ -394,18 +565,72 @@ __global__ void __launch_bounds__(kThr, 2) sample_rows_kernel(const SampleArgs a
             // ---- pass 2: candidates >= tau0, re-read only by the threads
             // whose own maximum reaches tau0 (the others hold none: about
             // one thread in eight re-reads its share of the row) ----
-            if (tmax >= tau0)
-                stream_row(rd, V, [&](float v, uint32_t idx) {
-                    if (v >= tau0) {
-                        const uint32_t pos = atomicAdd(&s.count, 1u);
-                        if (pos < (uint32_t)kCap) {
-                            s.cand_idx[pos] = idx;
-                            s.cand_val[pos] = v;
+            auto add = [&](float v, uint32_t idx) {
+                if (v >= tau0) {
+                    const uint32_t pos = atomicAdd(&s.count, 1u);
+                    if (pos < (uint32_t)kCap) {
+                        s.cand_idx[pos] = idx;
+                        s.cand_val[pos] = v;
+                    }
+                }
+            };
+            if (track) {
+                // only the chunks whose maximum reaches tau0, loaded together
+                // (a thread rarely has more than one)
+                const float4 *row4 = reinterpret_cast<const float4 *>(rd.row);
+                uint32_t q = (uint32_t)tid;
+                while (q < V4) {
+                    uint32_t sel[4] = {0u, 0u, 0u, 0u};
+                    uint32_t n = 0;
+                    for (; q < V4 && n < 4u; q += kThr) {
+                        if (bf16_bits_float(s.u.cmax[q]) >= tau0) {
+                            // register slots, no local-memory array
+                            sel[0] = n == 0u ? q : sel[0];
+                            sel[1] = n == 1u ? q : sel[1];
+                            sel[2] = n == 2u ? q : sel[2];
+                            sel[3] = n == 3u ? q : sel[3];
+                            n++;
                         }
                     }
-                });
+                    float4 v[4];
+#pragma unroll
+                    for (uint32_t k = 0; k < 4u; k++)
+                        if (k < n)
+                            v[k] = __ldg(row4 + sel[k]);
+#pragma unroll
+                    for (uint32_t k = 0; k < 4u; k++) {
+                        if (k < n) {
+                            float4 x = v[k];
+                            if (rd.scale) {
+                                x.x = __fmul_rn(x.x, rd.inv_t);
+                                x.y = __fmul_rn(x.y, rd.inv_t);
+                                x.z = __fmul_rn(x.z, rd.inv_t);
+                                x.w = __fmul_rn(x.w, rd.inv_t);
+                            }
+                            add(x.x, 4u * sel[k]);
+                            add(x.y, 4u * sel[k] + 1u);
+                            add(x.z, 4u * sel[k] + 2u);
+                            add(x.w, 4u * sel[k] + 3u);
+                        }
+                    }
+                }
+                for (uint32_t idx = 4u * V4 + (uint32_t)tid; idx < V; idx += kThr)
+                    add(rd(idx), idx);
+            } else if (tmax >= tau0) {
+                stream_row(rd, V, add);
+            }
             __syncthreads();
             const uint32_t nc = s.count;
+            const float rmx = s.rowmax;
+            if (nc <= kWarpCap && __expf(__fsub_rn(-FLT_MAX, rmx)) == 0.0f) {
+                // small candidate set: one warp finishes the row
+                if (warp == 0) {
+                    const uint32_t tok = warp_tail(s, nc, nk, rmx, topp, r, a.fused, V);
+                    if (lane == 0)
+                        a.out[blockIdx.x] = tok;
+                }
+                return;
+            }
             if (nc <= (uint32_t)kCap) {
                 ns = select_and_sort(nc, nk, s);
                 sorted_ready = true;
@@ -464,48 +689,8 @@ __global__ void __launch_bounds__(kThr, 2) sample_rows_kernel(const SampleArgs a
         for (uint32_t j = tid; j < ns8; j += kThr)
             s.e[j] = j < ns ? __expf(__fsub_rn(s.u.sorted.val[j], mx)) : 0.0f;
         __syncthreads();
-        if (tid == 0) {
-            // the reference's serial fp32 order, 8 loads ahead of the adds
-            const float4 *e4 = reinterpret_cast<const float4 *>(s.e);
-            float sum = 0.0f;
-#pragma unroll 2
-            for (uint32_t b = 0; b < ns8 / 8u; b++) {
-                const float4 x = e4[2 * b], y = e4[2 * b + 1];
-                sum = __fadd_rn(sum, x.x);
-                sum = __fadd_rn(sum, x.y);
-                sum = __fadd_rn(sum, x.z);
-                sum = __fadd_rn(sum, x.w);
-                sum = __fadd_rn(sum, y.x);
-                sum = __fadd_rn(sum, y.y);
-                sum = __fadd_rn(sum, y.z);
-                sum = __fadd_rn(sum, y.w);
-            }
-            const float inv = topp ? __fdiv_rn(1.0f, sum) : 0.0f;
-            auto step = [&](float c, float e) {
-                return topp ? (a.fused ? __fmaf_rn(e, inv, c) : __fadd_rn(c, __fmul_rn(e, inv)))
-                            : __fadd_rn(c, __fdiv_rn(e, sum));
-            };
-            // cum never decreases, and a padding entry repeats the previous
-            // value, so the first entry with cum >= r lies below ns
-            uint32_t tok = V - 1u;
-            float cum = 0.0f;
-            for (uint32_t b = 0; b < ns8 / 8u; b++) {
-                const float4 x = e4[2 * b], y = e4[2 * b + 1];
-                const float ev[8] = {x.x, x.y, x.z, x.w, y.x, y.y, y.z, y.w};
-                int hit = -1;
-#pragma unroll
-                for (int i = 0; i < 8; i++) {
-                    cum = step(cum, ev[i]);
-                    if (hit < 0 && cum >= r)
-                        hit = i;
-                }
-                if (hit >= 0) {
-                    tok = s.u.sorted.idx[8u * b + (uint32_t)hit];
-                    break;
-                }
-            }
-            a.out[blockIdx.x] = tok;
-        }
+        if (tid == 0)
+            a.out[blockIdx.x] = serial_walk(s, ns8, topp, r, a.fused, V);
         return;
     }
 
