@@ -263,11 +263,19 @@ struct SchedShared {
     union {
         // admission: requests read ahead from a RequestRing in one round trip
         RolloutRequest rq_buf[kSched];
+        // after admission: the admitted slots' page-table fill, flattened
+        struct {
+            uint32_t f_pre[kSched + 1];  // exclusive prefix sum of entries per admission
+            uint32_t f_npf[kSched];      // prefix pages copied
+            uint32_t f_full[kSched];     // full prefix pages (private pages start there)
+            uint32_t f_off[kSched];      // offset of the prefix's page list
+        };
         // retirement and grouping (after admission)
         struct {
             uint32_t fin[kSched];
             uint32_t fin_tokens[kSched];
             uint32_t fin_req[kSched];
+            uint32_t fin_list[kSched];   // finished slots in slot order
             uint32_t key[kSched];        // grouping key per slot (prefix id + 1, 0 = none)
             uint32_t rank[kSched];       // rank among the active slots with the same key
             uint32_t kcount[kKeyTable];  // per key: slot count, then first group id
@@ -286,6 +294,8 @@ struct SchedShared {
     // parallel page-table fill that follows the serial admission loop
     uint32_t adm_slot[kSched], adm_pfx[kSched];
     uint32_t n_adm;
+    uint32_t first_sent;             // parallel admission: first stop sentinel read ahead
+    uint32_t wcount[kSched / 32];    // per-warp counts (free slots, scan totals)
 };
 constexpr uint32_t kAheadTokens = 1u, kAheadRing = 2u;
 
@@ -564,6 +574,172 @@ __device__ void build_groups(const Dev &d, SchedShared &sh, uint32_t key, uint32
         *d.n_groups = min(sh.n_fin, d.max_groups);
 }
 
+// Admission with backpressure, all kSched threads at once (the serial loop
+// below is kept for the reference's drop-when-full pacing and for traced
+// runs, whose records keep their order).  The result is the serial loop's:
+// requests are taken in source order, the k-th admitted one into the k-th
+// lowest free slot, until a stop sentinel (consumed), max_admit, the read-
+// ahead or the free slots run out.
+__device__ void admit_parallel(const Dev &d, SchedShared &sh, bool full)
+{
+    const uint32_t s = threadIdx.x, lane = s & 31u, warp = s >> 5;
+    RtCtl *ctl = &sh.ctl;
+    if (s == 0)
+        sh.first_sent = sh.rq_n;
+    __syncthreads();
+    if (s < sh.rq_n && sh.rq_buf[s].request_id == RT_REQUEST_SENTINEL)
+        atomicMin(&sh.first_sent, s);
+    const bool is_free =
+        s < d.max_slots && ((sh.bitmap[s >> 6] >> (s & 63u)) & 1ull) == 0ull;
+    const unsigned ball = __ballot_sync(0xffffffffu, is_free);
+    if (lane == 0)
+        sh.wcount[warp] = (uint32_t)__popc(ball);
+    __syncthreads();
+    uint32_t before = 0, free_n = 0;
+#pragma unroll
+    for (uint32_t w = 0; w < kSched / 32u; w++) {
+        before += w < warp ? sh.wcount[w] : 0u;
+        free_n += sh.wcount[w];
+    }
+    const uint32_t rank = before + (uint32_t)__popc(ball & ((1u << lane) - 1u));
+    const uint32_t fs = sh.first_sent;
+    const uint32_t n_adm = min(min(fs, sh.rq_n), min(free_n, d.max_admit));
+    const bool take_sent = fs < sh.rq_n && n_adm == fs && fs < d.max_admit;
+    const bool mine = is_free && rank < n_adm;
+    if (mine) {
+        const RolloutRequest rq = sh.rq_buf[rank];
+        GpuRolloutSlot &rs = sh.slot[s];
+        rs.active = 1u;
+        rs.request_id = (uint32_t)(rq.request_id & 0xFFFFFFFFull);
+        rs.tokens_generated = 0u;
+        rs.max_tokens = rq.max_tokens;
+        rs.kv_blocks = rq.kv_blocks;
+        rs.rng_state[0] = rq.rng_seed;
+        rs.rng_state[1] = rq.rng_seed ^ 0x9e3779b97f4a7c15ULL;
+        rs.rng_state[2] = (rq.rng_seed << 17) ^ 0x3c6ef372fe94f82aULL;
+        rs.rng_state[3] = ~rq.rng_seed;
+        rs.temperature = rq.temperature;
+        rs.top_k = rq.top_k;
+        rs.top_p = rq.top_p;
+        if (full) {
+            SlotExt &e = sh.ext[s];
+            const uint32_t pfx = RT_REQUEST_PREFIX(rq.request_id);
+            e.row = ctl->consumed + rank;
+            e.prefix = (pfx != 0u && pfx - 1u < d.max_prefixes) ? pfx : 0u;
+            e.request_lo = rs.request_id;
+            e.last_token = 0u;
+            e.decoding = 0u;
+            e.seed = rq.rng_seed;
+            sh.adm_slot[rank] = s;
+            sh.adm_pfx[rank] = e.prefix;
+        }
+    }
+    const unsigned took = __ballot_sync(0xffffffffu, mine);
+    if (lane == 0 && took)
+        atomicOr((unsigned long long *)&sh.bitmap[warp >> 1],
+                 (unsigned long long)took << (32u * (warp & 1u)));
+    __syncthreads();
+    if (s == 0) {
+        ctl->consumed += n_adm;
+        ctl->admitted += n_adm;
+        if (n_adm)
+            ctl->groups_ok = 0u;
+        if (take_sent) {
+            ctl->sentinel = 1u;
+            sh.stop = 1u;
+        }
+        sh.n_adm = full ? n_adm : 0u;
+        const uint32_t taken = n_adm + (take_sent ? 1u : 0u);
+        if (sh.io.ring && taken)
+            rt_store_release_u32(&sh.io.ring->cons.head, sh.rq_head + taken);
+    }
+    __syncthreads();
+}
+
+// The admitted slots' context and page-table rows (all kSched threads): the
+// prefix's full pages first, then the slot's private pages; a partial last
+// prefix page is noted for its copy on the first write.  The entries of all
+// admissions form one flat range, so every load is in flight at once
+// whatever the number of admissions.
+__device__ void fill_admitted(const Dev &d, SchedShared &sh)
+{
+    const uint32_t s = threadIdx.x, lane = s & 31u, warp = s >> 5;
+    const uint32_t n_adm = sh.n_adm;
+    uint32_t cnt = 0;
+    if (s < n_adm) {
+        const uint32_t slot = sh.adm_slot[s], pfx = sh.adm_pfx[s];
+        uint32_t ctx = 0, np = 0, off = 0;
+        if (pfx != 0u) {
+            ctx = d.pf_len[pfx - 1u];
+            np = d.pf_np[pfx - 1u];
+            off = d.pf_off[pfx - 1u];
+        }
+        // keep the context inside the page table / private pages
+        const uint32_t cap = d.maxp * 16u;
+        if (ctx > cap)
+            ctx = cap;
+        const uint32_t full_pages = ctx / 16u;
+        const uint32_t n_pf = min(full_pages, np);
+        // private pages fill entries full_pages .. maxp - 1, at most ppriv of them
+        const uint32_t n_pv = min(d.maxp - min(full_pages, d.maxp), d.ppriv);
+        cnt = n_pf + n_pv;
+        sh.f_npf[s] = n_pf;
+        sh.f_full[s] = full_pages;
+        sh.f_off[s] = off;
+        SlotExt &e = sh.ext[slot];
+        e.ctx_len = ctx;
+        e.pos = ctx;
+        e.shared = pfx ? n_pf : 0u;
+        if ((ctx & 15u) && full_pages < np) {
+            e.cow_src = d.pf_pages[off + full_pages];
+            e.cow_rows = ctx & 15u;
+        } else {
+            e.cow_src = -1;
+            e.cow_rows = 0u;
+        }
+    }
+    // exclusive prefix sum of the entry counts (n_adm <= kSched)
+    uint32_t x = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= (uint32_t)o)
+            x += y;
+    }
+    if (lane == 31u)
+        sh.wcount[warp] = x;
+    __syncthreads();
+    uint32_t before = 0, total = 0;
+#pragma unroll
+    for (uint32_t w = 0; w < kSched / 32u; w++) {
+        before += w < warp ? sh.wcount[w] : 0u;
+        total += sh.wcount[w];
+    }
+    sh.f_pre[s] = before + x - cnt;
+    if (s == 0)
+        sh.f_pre[kSched] = total;
+    __syncthreads();
+    for (uint32_t e = s; e < total; e += kSched) {
+        // the admission k holding entry e: largest k < n_adm with f_pre[k] <= e
+        uint32_t lo = 0, hi = n_adm - 1u;
+        while (lo < hi) {
+            const uint32_t mid = (lo + hi + 1u) >> 1;
+            if (sh.f_pre[mid] <= e)
+                lo = mid;
+            else
+                hi = mid - 1u;
+        }
+        const uint32_t k = lo, j = e - sh.f_pre[k], slot = sh.adm_slot[k];
+        int32_t *pt = d.page_table + (size_t)slot * d.maxp;
+        const uint32_t n_pf = sh.f_npf[k];
+        if (j < n_pf)
+            pt[j] = d.pf_pages[sh.f_off[k] + j];
+        else
+            pt[sh.f_full[k] + (j - n_pf)] = d.priv[(size_t)slot * d.ppriv + (j - n_pf)];
+    }
+    __syncthreads();
+}
+
 // One pass of the reference rollout_worker loop (see file comment) on the
 // shared-memory state.  Returns true when the loop must stop.  All kSched
 // threads call it.
@@ -602,110 +778,116 @@ __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
     // 2. admission, in source order, lowest free slot first.  The source is
     //    read ahead (prefetch_requests); a ring's head is released once.
     prefetch_requests(d, sh);
-    if (s == 0) {
-        sh.n_adm = 0u;
-        uint32_t taken = 0;  // source records consumed this pass
-        for (uint32_t a = 0; a < d.max_admit; a++) {
-            // the read-ahead covers every record this pass can take
-            if (taken >= sh.rq_n)
-                break;
-            const RolloutRequest rq = sh.rq_buf[taken];
-            if (rq.request_id == RT_REQUEST_SENTINEL) {
+    if (!d.drop && !d.trace) {
+        admit_parallel(d, sh, full);
+        if (full && sh.n_adm)
+            fill_admitted(d, sh);
+    } else {
+        if (s == 0) {
+            sh.n_adm = 0u;
+            uint32_t taken = 0;  // source records consumed this pass
+            for (uint32_t a = 0; a < d.max_admit; a++) {
+                // the read-ahead covers every record this pass can take
+                if (taken >= sh.rq_n)
+                    break;
+                const RolloutRequest rq = sh.rq_buf[taken];
+                if (rq.request_id == RT_REQUEST_SENTINEL) {
+                    taken++;
+                    ctl->sentinel = 1u;
+                    sh.stop = 1u;
+                    break;
+                }
+                const int slot = take_lowest_free(sh.bitmap, d.max_slots);
+                if (slot < 0) {
+                    if (!d.drop)
+                        break;              // backpressure: leave it queued
+                    taken++;                // reference: consumed and lost
+                    ctl->consumed++;
+                    ctl->dropped++;
+                    continue;
+                }
                 taken++;
-                ctl->sentinel = 1u;
-                sh.stop = 1u;
-                break;
-            }
-            const int slot = take_lowest_free(sh.bitmap, d.max_slots);
-            if (slot < 0) {
-                if (!d.drop)
-                    break;              // backpressure: leave it queued
-                taken++;                // reference: consumed and lost
-                ctl->consumed++;
-                ctl->dropped++;
-                continue;
-            }
-            taken++;
-            const uint32_t row = ctl->consumed++;
-            ctl->admitted++;
-            const uint32_t rq_lo = (uint32_t)(rq.request_id & 0xFFFFFFFFull);
-            trace_push(d.trace, RT_TRACE_ROLLOUT_ALLOC, rq_lo, (uint32_t)slot);
-            trace_push(d.trace, RT_TRACE_DESC_CONSUMED, rq_lo, row);
-            ctl->groups_ok = 0u;
-            GpuRolloutSlot &rs = sh.slot[slot];
-            rs.active = 1u;
-            rs.request_id = (uint32_t)(rq.request_id & 0xFFFFFFFFull);
-            rs.tokens_generated = 0u;
-            rs.max_tokens = rq.max_tokens;
-            rs.kv_blocks = rq.kv_blocks;
-            rs.rng_state[0] = rq.rng_seed;
-            rs.rng_state[1] = rq.rng_seed ^ 0x9e3779b97f4a7c15ULL;
-            rs.rng_state[2] = (rq.rng_seed << 17) ^ 0x3c6ef372fe94f82aULL;
-            rs.rng_state[3] = ~rq.rng_seed;
-            rs.temperature = rq.temperature;
-            rs.top_k = rq.top_k;
-            rs.top_p = rq.top_p;
-            if (full) {
-                // the slot's page table and context are filled in parallel below
-                SlotExt &e = sh.ext[slot];
-                const uint32_t pfx = RT_REQUEST_PREFIX(rq.request_id);
-                e.row = row;
-                e.prefix = (pfx != 0u && pfx - 1u < d.max_prefixes) ? pfx : 0u;
-                e.request_lo = rs.request_id;
-                e.last_token = 0u;
-                e.decoding = 0u;
-                e.seed = rq.rng_seed;
-                sh.adm_slot[sh.n_adm] = (uint32_t)slot;
-                sh.adm_pfx[sh.n_adm] = e.prefix;
-                sh.n_adm++;
-            }
-        }
-        if (io.ring && taken)
-            rt_store_release_u32(&io.ring->cons.head, sh.rq_head + taken);
-    }
-    __syncthreads();
-    // Admitted slots' context and page tables, one warp per slot: the
-    // prefix's pages first (up to its full pages), then the slot's private
-    // pages; a partial last prefix page is copied on the first write.
-    if (full) {
-        const uint32_t lane = s & 31u, warp = s >> 5;
-        for (uint32_t k = warp; k < sh.n_adm; k += kSched / 32u) {
-            const uint32_t slot = sh.adm_slot[k], pfx = sh.adm_pfx[k];
-            uint32_t ctx = 0, np = 0, off = 0;
-            if (pfx != 0u) {
-                ctx = d.pf_len[pfx - 1u];
-                np = d.pf_np[pfx - 1u];
-                off = d.pf_off[pfx - 1u];
-            }
-            // keep the context inside the page table / private pages
-            const uint32_t cap = d.maxp * 16u;
-            if (ctx > cap)
-                ctx = cap;
-            int32_t *pt = d.page_table + (size_t)slot * d.maxp;
-            const int32_t *priv = d.priv + (size_t)slot * d.ppriv;
-            const uint32_t full_pages = ctx / 16u;
-            const uint32_t n_pf = min(full_pages, np);
-            for (uint32_t i = lane; i < n_pf; i += 32u)
-                pt[i] = d.pf_pages[off + i];
-            // private pages fill entries full_pages .. maxp - 1, at most ppriv of them
-            const uint32_t n_pv = min(d.maxp - min(full_pages, d.maxp), d.ppriv);
-            for (uint32_t j = lane; j < n_pv; j += 32u)
-                pt[full_pages + j] = priv[j];
-            if (lane == 0) {
-                SlotExt &e = sh.ext[slot];
-                e.ctx_len = ctx;
-                e.pos = ctx;
-                e.shared = pfx ? n_pf : 0u;
-                if ((ctx & 15u) && full_pages < np) {
-                    e.cow_src = d.pf_pages[off + full_pages];
-                    e.cow_rows = ctx & 15u;
-                } else {
-                    e.cow_src = -1;
-                    e.cow_rows = 0u;
+                const uint32_t row = ctl->consumed++;
+                ctl->admitted++;
+                const uint32_t rq_lo = (uint32_t)(rq.request_id & 0xFFFFFFFFull);
+                trace_push(d.trace, RT_TRACE_ROLLOUT_ALLOC, rq_lo, (uint32_t)slot);
+                trace_push(d.trace, RT_TRACE_DESC_CONSUMED, rq_lo, row);
+                ctl->groups_ok = 0u;
+                GpuRolloutSlot &rs = sh.slot[slot];
+                rs.active = 1u;
+                rs.request_id = (uint32_t)(rq.request_id & 0xFFFFFFFFull);
+                rs.tokens_generated = 0u;
+                rs.max_tokens = rq.max_tokens;
+                rs.kv_blocks = rq.kv_blocks;
+                rs.rng_state[0] = rq.rng_seed;
+                rs.rng_state[1] = rq.rng_seed ^ 0x9e3779b97f4a7c15ULL;
+                rs.rng_state[2] = (rq.rng_seed << 17) ^ 0x3c6ef372fe94f82aULL;
+                rs.rng_state[3] = ~rq.rng_seed;
+                rs.temperature = rq.temperature;
+                rs.top_k = rq.top_k;
+                rs.top_p = rq.top_p;
+                if (full) {
+                    // the slot's page table and context are filled in parallel below
+                    SlotExt &e = sh.ext[slot];
+                    const uint32_t pfx = RT_REQUEST_PREFIX(rq.request_id);
+                    e.row = row;
+                    e.prefix = (pfx != 0u && pfx - 1u < d.max_prefixes) ? pfx : 0u;
+                    e.request_lo = rs.request_id;
+                    e.last_token = 0u;
+                    e.decoding = 0u;
+                    e.seed = rq.rng_seed;
+                    sh.adm_slot[sh.n_adm] = (uint32_t)slot;
+                    sh.adm_pfx[sh.n_adm] = e.prefix;
+                    sh.n_adm++;
                 }
             }
+            if (io.ring && taken)
+                rt_store_release_u32(&io.ring->cons.head, sh.rq_head + taken);
         }
         __syncthreads();
+        // Admitted slots' context and page tables, one warp per slot: the
+        // prefix's pages first (up to its full pages), then the slot's private
+        // pages; a partial last prefix page is copied on the first write.
+        if (full) {
+            const uint32_t lane = s & 31u, warp = s >> 5;
+            for (uint32_t k = warp; k < sh.n_adm; k += kSched / 32u) {
+                const uint32_t slot = sh.adm_slot[k], pfx = sh.adm_pfx[k];
+                uint32_t ctx = 0, np = 0, off = 0;
+                if (pfx != 0u) {
+                    ctx = d.pf_len[pfx - 1u];
+                    np = d.pf_np[pfx - 1u];
+                    off = d.pf_off[pfx - 1u];
+                }
+                // keep the context inside the page table / private pages
+                const uint32_t cap = d.maxp * 16u;
+                if (ctx > cap)
+                    ctx = cap;
+                int32_t *pt = d.page_table + (size_t)slot * d.maxp;
+                const int32_t *priv = d.priv + (size_t)slot * d.ppriv;
+                const uint32_t full_pages = ctx / 16u;
+                const uint32_t n_pf = min(full_pages, np);
+                for (uint32_t i = lane; i < n_pf; i += 32u)
+                    pt[i] = d.pf_pages[off + i];
+                // private pages fill entries full_pages .. maxp - 1, at most ppriv of them
+                const uint32_t n_pv = min(d.maxp - min(full_pages, d.maxp), d.ppriv);
+                for (uint32_t j = lane; j < n_pv; j += 32u)
+                    pt[full_pages + j] = priv[j];
+                if (lane == 0) {
+                    SlotExt &e = sh.ext[slot];
+                    e.ctx_len = ctx;
+                    e.pos = ctx;
+                    e.shared = pfx ? n_pf : 0u;
+                    if ((ctx & 15u) && full_pages < np) {
+                        e.cow_src = d.pf_pages[off + full_pages];
+                        e.cow_rows = ctx & 15u;
+                    } else {
+                        e.cow_src = -1;
+                        e.cow_rows = 0u;
+                    }
+                }
+            }
+            __syncthreads();
+        }
     }
     if (sh.stop)
         return true;  // reference: the sentinel ends the worker before the scan
@@ -721,6 +903,21 @@ __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
         }
     }
     sh.fin[s] = fin;
+    // compact list of the finished slots, in slot order, so the serial
+    // part below visits only them
+    {
+        const uint32_t lane = s & 31u, warp = s >> 5;
+        const unsigned ball = __ballot_sync(0xffffffffu, fin != 0u);
+        if (lane == 0)
+            sh.wcount[warp] = (uint32_t)__popc(ball);
+        __syncthreads();
+        uint32_t before = 0;
+#pragma unroll
+        for (uint32_t w = 0; w < kSched / 32u; w++)
+            before += w < warp ? sh.wcount[w] : 0u;
+        if (fin)
+            sh.fin_list[before + (uint32_t)__popc(ball & ((1u << lane) - 1u))] = s;
+    }
     const uint32_t n_fin = __syncthreads_count(fin);
     if (n_fin && s == 0)
         ctl->groups_ok = 0u;
@@ -733,9 +930,8 @@ __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
             dn_tail = rt_load_relaxed_u32(&io.done_ring->prod.tail);
             dn_room = (uint32_t)REQUEST_RING_SIZE - (dn_tail - head);
         }
-        for (uint32_t k = 0; k < d.max_slots; k++) {
-            if (!sh.fin[k])
-                continue;
+        for (uint32_t j = 0; j < n_fin; j++) {
+            const uint32_t k = sh.fin_list[j];
             RolloutDone rec;
             rec.request_id = sh.fin_req[k];
             rec.rollout_id = k;
