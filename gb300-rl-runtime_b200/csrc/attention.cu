@@ -963,7 +963,13 @@ int make_plan(const rt_attn_params_t *p, Plan *pl, const rt_attn_group_params_t 
     pl->gchunk_pages = 0;
     pl->max_gchunks = 0;
     if (gp) {
-        uint32_t cpg = gp->chunk_pages ? gp->chunk_pages : kDefaultGroupChunkPages;
+        // Auto: 16-page items; 32 when prefixes can be long (max_shared_pages
+        // > 64), where 16-page items multiply the per-item prologue (config
+        // 4's 1,024-token base + prompt: 119 against 109 us of attention per
+        // pass), while short prefixes need the smaller items to fill the GPU.
+        uint32_t cpg = gp->chunk_pages ? gp->chunk_pages
+                                       : (gp->max_shared_pages > 64u ? 2u * kDefaultGroupChunkPages
+                                                                      : kDefaultGroupChunkPages);
         if (gp->max_groups == 0 || gp->max_groups > (1u << 24) || cpg > (uint32_t)kMaxChunkPages ||
             gp->max_shared_pages > pages_max) {
             rt::set_error("attention: group params out of range (max_groups %u, "

@@ -7,15 +7,19 @@
 //
 //  1. one streaming pass (16-byte loads, eight in flight per thread): scale
 //     by 1.0f / temperature (the reference's fp32 multiply), keep each
-//     thread's maximum, detect NaN / +inf;
+//     thread's maximum and each 16-byte chunk's maximum (in shared memory,
+//     as bf16 rounded up), detect NaN / +inf;
 //  2. each of the 16 warps ranks its 32 per-thread maxima and keeps the
 //     m = ceil(nk / 16) largest; tau0 = the nk-th largest of those 16 m
 //     values.  They are distinct row entries, so at least nk values are
 //     >= tau0: tau0 <= the top-k cutoff (the nk-th largest value counted
 //     with multiplicity) and every survivor is >= tau0;
-//  3. a second pass, by the threads whose own maximum reaches tau0 only
-//     (about one in eight), collects the candidates (values >= tau0,
-//     typically 50-90 for k = 50).  A candidate survives iff fewer than nk
+//  3. a second, partial pass loads only the chunks whose maximum reaches
+//     tau0 (one L2 round trip; about 60 of 8,000 chunks at config 3) and
+//     collects the candidates (values >= tau0, typically 50-90 for k = 50).
+//     Rows too long for the chunk table, or not 16-byte aligned, re-read the
+//     shares of the threads whose own maximum reaches tau0 instead.  A
+//     candidate survives iff fewer than nk
 //     candidates are strictly larger (an all-pairs scan, 16 bytes at a
 //     time); survivors are sorted by vocabulary index (rank sort, typically
 //     k of them);
@@ -47,7 +51,6 @@ constexpr int kWarpsPerRow = kThr / 32;
 constexpr int kBins = 4096;          // radix digits of the streamed cutoff select
 constexpr int kCap = 1024;           // candidates handled by the fast path
 constexpr int kCmax = 8192;          // 16-byte chunks whose maxima pass 1 keeps (vocab <= 32768)
-constexpr uint32_t kWarpCap = 160;   // candidates handled by the one-warp tail
 constexpr uint32_t kMaxVocab = 1u << 20;
 
 
@@ -92,7 +95,6 @@ struct __align__(16) Smem {
     float top[kWarpsPerRow * 16];  // each warp's m largest per-thread maxima (m <= 16)
     uint32_t scan[kWarpsPerRow];
     uint32_t digit, need, count, token, done;
-    float rowmax;                  // largest value > -FLT_MAX of the row (scaled)
 };
 
 // bf16 bits of the smallest bf16 >= x (x not NaN).
@@ -366,67 +368,6 @@ __device__ __forceinline__ uint32_t serial_walk(const Smem &s, uint32_t ns8, boo
     return V - 1u;
 }
 
-// Survivor selection, index sort, exponentials and the serial walk by one
-// warp, for nc <= kWarpCap candidates (cand_*), with no block barrier.  A
-// candidate survives iff fewer than nk candidates are strictly larger; mx is
-// the row maximum (the largest survivor).  Same arithmetic as the block path.
-__device__ __forceinline__ uint32_t warp_tail(Smem &s, uint32_t nc, uint32_t nk, float mx,
-                                              bool topp, float r, uint32_t fused, uint32_t V)
-{
-    const uint32_t lane = threadIdx.x & 31u;
-    uint32_t *keep = reinterpret_cast<uint32_t *>(s.e);  // reused before the exponentials
-    const uint32_t n4 = (nc + 3u) & ~3u;
-    for (uint32_t j = nc + lane; j < n4; j += 32u) {
-        s.cand_val[j] = -INFINITY;
-        s.cand_idx[j] = 0xFFFFFFFFu;
-    }
-    __syncwarp();
-    const float4 *cv4 = reinterpret_cast<const float4 *>(s.cand_val);
-    uint32_t ns = 0;
-    for (uint32_t j0 = 0; j0 < n4; j0 += 32u) {
-        const uint32_t j = j0 + lane;
-        uint32_t k = 0u;
-        if (j < nc) {
-            const float v = s.cand_val[j];
-            uint32_t gt = 0;
-            for (uint32_t i = 0; i < n4 / 4u; i++) {
-                const float4 c = cv4[i];
-                gt += (c.x > v ? 1u : 0u) + (c.y > v ? 1u : 0u) + (c.z > v ? 1u : 0u) +
-                      (c.w > v ? 1u : 0u);
-            }
-            k = gt < nk ? 1u : 0u;
-        }
-        if (j < n4)
-            keep[j] = k;
-        ns += (uint32_t)__popc(__ballot_sync(0xffffffffu, k != 0u));
-    }
-    __syncwarp();
-    const uint4 *ci4 = reinterpret_cast<const uint4 *>(s.cand_idx);
-    const uint4 *kp4 = reinterpret_cast<const uint4 *>(keep);
-    for (uint32_t j = lane; j < nc; j += 32u) {
-        if (!keep[j])
-            continue;
-        const uint32_t id = s.cand_idx[j];
-        uint32_t rank = 0;
-        for (uint32_t i = 0; i < n4 / 4u; i++) {
-            const uint4 c = ci4[i], f = kp4[i];
-            rank += (f.x && c.x < id ? 1u : 0u) + (f.y && c.y < id ? 1u : 0u) +
-                    (f.z && c.z < id ? 1u : 0u) + (f.w && c.w < id ? 1u : 0u);
-        }
-        s.u.sorted.idx[rank] = id;
-        s.u.sorted.val[rank] = s.cand_val[j];
-    }
-    __syncwarp();
-    const uint32_t ns8 = (ns + 7u) & ~7u;
-    for (uint32_t j = lane; j < ns8; j += 32u)
-        s.e[j] = j < ns ? __expf(__fsub_rn(s.u.sorted.val[j], mx)) : 0.0f;
-    __syncwarp();
-    uint32_t tok = 0;
-    if (lane == 0)
-        tok = serial_walk(s, ns8, topp, r, fused, V);
-    return tok;
-}
-
 __global__ void __launch_bounds__(kThr, 2) sample_rows_kernel(const SampleArgs a)
 {
     __shared__ Smem s;
@@ -553,8 +494,6 @@ __global__ void __launch_bounds__(kThr, 2) sample_rows_kernel(const SampleArgs a
             }
             if (g2 < nk && e2 >= nk)
                 s.red_f[0] = v;  // every such thread holds the same value
-            if (g2 == 0u)
-                s.rowmax = v;    // the largest per-thread maximum: the row maximum
         }
         __syncthreads();
         const float tau0 = s.red_f[0];
@@ -621,16 +560,6 @@ __global__ void __launch_bounds__(kThr, 2) sample_rows_kernel(const SampleArgs a
             }
             __syncthreads();
             const uint32_t nc = s.count;
-            const float rmx = s.rowmax;
-            if (nc <= kWarpCap && __expf(__fsub_rn(-FLT_MAX, rmx)) == 0.0f) {
-                // small candidate set: one warp finishes the row
-                if (warp == 0) {
-                    const uint32_t tok = warp_tail(s, nc, nk, rmx, topp, r, a.fused, V);
-                    if (lane == 0)
-                        a.out[blockIdx.x] = tok;
-                }
-                return;
-            }
             if (nc <= (uint32_t)kCap) {
                 ns = select_and_sort(nc, nk, s);
                 sorted_ready = true;

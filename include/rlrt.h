@@ -140,7 +140,8 @@ typedef struct {
 typedef struct {
     uint32_t max_groups;         /* capacity of the groups array */
     uint32_t max_shared_pages;   /* bound on every shared_pages */
-    uint32_t chunk_pages;        /* shared pages per work item; 0 = auto (16) */
+    uint32_t chunk_pages;        /* shared pages per work item; 0 = auto (16, or 32
+                                    when max_shared_pages > 64) */
     uint32_t reserved;
 } rt_attn_group_params_t;
 
