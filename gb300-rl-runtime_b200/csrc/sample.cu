@@ -377,9 +377,9 @@ __global__ void __launch_bounds__(kThr, 2) sample_rows_kernel(const SampleArgs a
     // When launched as a programmatic dependent of the kernel that wrote the
     // logits, wait for it before reading them (a no-op otherwise).
     rt::grid_dep_wait();
-    // A dependent launch after this one (the rollout loop's next schedule
-    // kernel) may be scheduled; it waits for this grid's completion itself.
-    rt::grid_dep_launch();
+    // (No early trigger for a dependent launch after this one: the rollout
+    // loop's next schedule kernel, launched as a programmatic dependent,
+    // measured 2% faster passes when released only at this grid's end.)
     if (a.enable && a.enable[blockIdx.x] == 0u)
         return;
     const rt_sample_row_t P = a.rows[blockIdx.x];
