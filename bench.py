@@ -1416,6 +1416,9 @@ def extra_block(cls, args, dev, steps, warmup, peaks, src):
     traffic, commit = ncu_traffic(wl.kernel, wl.name)
     if isinstance(wl, RolloutWorkload):
         achieved, rep = loop_kernel_report(wl.kernel_profile())
+        if isinstance(wl, RolloutModelWorkload):
+            rep["note"] = ("model decode: 'prepare' = embedding gather + QKV GEMM + q/K/V "
+                           "scatter, 'logits' = bf16 hidden + LM-head GEMM")
         out["kernels"] = rep
         out["gpu_launches"] = wl.gpu_launches(steps)
         out["roofline"] = roofline_block(wl, achieved, rep["avg_us"]["attention"] / 1e3, peaks, src,
@@ -1522,6 +1525,7 @@ def run_mine(args):
         extra["sampling_c3"] = extra_block(SamplingWorkload, args, dev, 50, 10, peaks, src)
         extra["continuous_batching_c4"] = extra_block(RolloutC4Workload, args, dev, 3, 3, peaks,
                                                       src)
+        extra["model_decode_c5"] = extra_block(RolloutModelWorkload, args, dev, 2, 3, peaks, src)
     if rank == 0:
         line = {
             "metric": cls.metric, "value": value, "unit": cls.unit, "n_gpus": world,
