@@ -145,3 +145,73 @@ def test_xoshiro_inversion(orc):
     for v in [0, 1, 0xFFFFFF, 0x123456, 12345678]:
         s1 = orc.xoshiro_s1_for_first_output(v)
         assert (rotl((s1 * 5) % M, 7) * 9) % M == v
+
+
+def test_scheduler_oracle_arrivals_and_slot_limit(orc):
+    """The arrival gate and a slot count below 256 (the device loop's
+    rt_rollout_io_t.arrivals and max_slots): a request is admitted no earlier
+    than its arrival pass, in order, into the lowest free slot below
+    max_slots; admission precedes retirement within a pass."""
+    reqs = np.zeros(3, dtype=orc.REQUEST_DTYPE)
+    reqs["request_id"] = [1, 2, 3]
+    reqs["max_tokens"] = [2, 1, 1]
+    dones, dpass, _, passes, admit = orc.scheduler_run(
+        reqs, arrival_pass=[0, 3, 3], max_admit=256, drop_when_full=False, with_admit=True,
+        max_slots=1)
+    # r1 holds the only slot until it retires in pass 2; r2 arrives in pass 3
+    # and is admitted at once; r3 waits for the slot r2 frees in pass 4
+    assert admit.tolist() == [0, 3, 5]
+    assert dpass.tolist() == [2, 4, 6]
+    assert dones["rollout_id"].tolist() == [0, 0, 0] and passes == 7
+
+
+def test_scheduler_oracle_arrival_properties(orc):
+    rng = np.random.default_rng(12)
+    n = 200
+    reqs = np.zeros(n, dtype=orc.REQUEST_DTYPE)
+    reqs["request_id"] = np.arange(1, n + 1)
+    reqs["max_tokens"] = rng.integers(0, 40, size=n)
+    arrival = np.sort(rng.integers(0, 300, size=n)).astype(np.uint32)
+    for slots in (256, 16, 3):
+        dones, dpass, _, _, admit = orc.scheduler_run(
+            reqs, arrival_pass=arrival, max_admit=256, drop_when_full=False, with_admit=True,
+            max_slots=slots)
+        assert len(dones) == n
+        assert np.all(admit >= arrival) and np.all(np.diff(admit.astype(np.int64)) >= 0)
+        assert np.all(dones["rollout_id"] < slots)
+        # each rollout is done max(1, max_tokens) + ... passes after admission:
+        # tokens reach max_tokens after max_tokens decode passes
+        by_id = {int(d["request_id"]): int(p) for d, p in zip(dones, dpass)}
+        for i in range(n):
+            assert by_id[i + 1] == int(admit[i]) + int(reqs["max_tokens"][i])
+
+
+def test_paced_pump_pushes_at_arrival_times(pkg, orc):
+    """rt_host_pump_paced on the host alone (no consumer): every request and
+    then the stop sentinel are pushed in order, none before its arrival
+    time, so the call takes at least the last arrival."""
+    import time
+    n = 40
+    reqs = np.zeros(n, dtype=orc.REQUEST_DTYPE)
+    reqs["request_id"] = np.arange(1, n + 1)
+    arrival = (np.arange(n, dtype=np.uint64) * 500_000).astype(np.uint64)  # every 0.5 ms
+    rings = pkg.HostRings()
+    try:
+        t0 = time.perf_counter()
+        got, _, _ = rings.pump_paced(reqs, arrival, 0, send_sentinel=True, timeout_ms=5000)
+        dt = time.perf_counter() - t0
+        assert got == 0
+        assert dt >= float(arrival[-1]) / 1e9
+        raw = (ctypes_bytes(rings.req, 128 + 1024 * 34))
+        tail = int(np.frombuffer(raw[64:68], dtype=np.uint32)[0])
+        assert tail == n + 1
+        recs = np.frombuffer(raw[128:128 + (n + 1) * 34], dtype=orc.REQUEST_DTYPE)
+        assert recs["request_id"][:n].tolist() == list(range(1, n + 1))
+        assert int(recs["request_id"][n]) == np.iinfo(np.uint64).max
+    finally:
+        rings.close()
+
+
+def ctypes_bytes(ptr, n):
+    import ctypes
+    return ctypes.string_at(ptr, n)
