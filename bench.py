@@ -417,6 +417,43 @@ class SamplingWorkload(Workload):
     def units_per_step(self):
         return self.bytes / 1e9
 
+    def details(self):
+        """The same calls given each buffer's 16-column chunk maxima
+        (rt_sample_rows_cmax, the rollout loop's path: its logits kernel
+        writes them), CUDA events over 50 calls on the rotating buffers, and
+        the standalone chunk-maximum kernel; tokens compared with the
+        full-row path."""
+        torch, pkg = self.torch, self.pkg
+        cms = [pkg.logits_chunk_max(b, self.V) for b in self.bufs]
+        full = [pkg.sample_rows(b, self.rows, self.V).clone() for b in self.bufs]
+        got = [pkg.sample_rows_cmax(b, c, self.rows, self.V).clone()
+               for b, c in zip(self.bufs, cms)]
+        equal = all(bool(torch.equal(a, b)) for a, b in zip(full, got))
+        s = torch.cuda.current_stream()
+
+        def timed(fn, n=50):
+            for i in range(5):
+                fn(i)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            for i in range(n):
+                fn(i)
+            e1.record(s)
+            torch.cuda.synchronize()
+            return e0.elapsed_time(e1) * 1e3 / n
+
+        us = timed(lambda i: pkg.sample_rows_cmax(self.bufs[i % self.NBUF], cms[i % self.NBUF],
+                                                  self.rows, self.V, out=self.out))
+        us_cm = timed(lambda i: pkg.logits_chunk_max(self.bufs[i % self.NBUF], self.V,
+                                                     out=cms[i % self.NBUF]))
+        return {"producer_maxima": {
+            "us_per_call": us, "tokens_equal_full_path": equal,
+            "chunk_max_kernel_us": us_cm,
+            "note": "rt_sample_rows_cmax reads each row's 2,000 chunk maxima and only the "
+                    "chunks that can hold a top-k survivor; the value above is the full-row "
+                    "path (rt_sample_rows)"}}
+
     def e2e(self, steps, warmup):
         """Logits rows copied from pinned host memory each step, tokens read back."""
         torch = self.torch

@@ -212,6 +212,11 @@ _SIGS = {
     "rt_attn_workspace_error": (ctypes.c_int, [_P, _P, ctypes.POINTER(ctypes.c_int32)]),
     "rt_sample_rows": (ctypes.c_int, [ctypes.POINTER(rt_sample_params_t), _P, _P, _P, _P]),
     "rt_sample_uniform24": (ctypes.c_uint32, [ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint64]),
+    "rt_chunk_max_stride": (ctypes.c_uint32, [ctypes.c_uint32]),
+    "rt_logits_chunk_max": (ctypes.c_int, [_P, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint64,
+                                           _P, ctypes.c_uint32, _P]),
+    "rt_sample_rows_cmax": (ctypes.c_int, [ctypes.POINTER(rt_sample_params_t), _P, _P,
+                                           ctypes.c_uint32, _P, _P, _P]),
     "rt_rollout_create": (ctypes.c_int, [ctypes.POINTER(rt_rollout_config_t),
                                          ctypes.POINTER(KVArena), ctypes.POINTER(_P)]),
     "rt_rollout_destroy": (ctypes.c_int, [_P]),
@@ -450,6 +455,41 @@ def sample_rows(logits, rows, vocab, fused_cum=True, out=None, row_enable=None, 
                            None if row_enable is None else row_enable.data_ptr())
     check(lib().rt_sample_rows(ctypes.byref(p), _ptr(logits), _ptr(rows), _ptr(out),
                                _stream_ptr(stream)), "rt_sample_rows")
+    return out
+
+
+def chunk_max_stride(vocab) -> int:
+    """Floats per row of a chunk-maximum array (rt_chunk_max_stride)."""
+    return int(lib().rt_chunk_max_stride(vocab))
+
+
+def logits_chunk_max(logits, vocab, out=None, stream=None):
+    """rt_logits_chunk_max: each 16-column chunk's maximum (NaN if the chunk
+    holds a NaN) of fp32 logits [R, stride] (device); returns fp32
+    [R, chunk_max_stride(vocab)]."""
+    import torch
+    R = logits.shape[0]
+    cs = chunk_max_stride(vocab)
+    if out is None:
+        out = torch.empty(R, cs, dtype=torch.float32, device=logits.device)
+    check(lib().rt_logits_chunk_max(_ptr(logits), R, vocab, logits.stride(0), _ptr(out),
+                                    out.stride(0), _stream_ptr(stream)), "rt_logits_chunk_max")
+    return out
+
+
+def sample_rows_cmax(logits, chunk_max, rows, vocab, fused_cum=True, out=None, row_enable=None,
+                     stream=None):
+    """rt_sample_rows_cmax: rt_sample_rows given the logits' chunk maxima
+    (fp32 [R, chunk_max_stride(vocab)], device); returns int32 tokens [R]."""
+    import torch
+    R = logits.shape[0]
+    if out is None:
+        out = torch.empty(R, dtype=torch.int32, device=logits.device)
+    p = rt_sample_params_t(R, vocab, logits.stride(0), 1 if fused_cum else 0,
+                           None if row_enable is None else row_enable.data_ptr())
+    check(lib().rt_sample_rows_cmax(ctypes.byref(p), _ptr(logits), _ptr(chunk_max),
+                                    chunk_max.stride(0), _ptr(rows), _ptr(out),
+                                    _stream_ptr(stream)), "rt_sample_rows_cmax")
     return out
 
 

@@ -121,6 +121,8 @@ struct Dev {
     float *attn_out;      // [max_slots][hq][128]
     __nv_bfloat16 *arena;
     float *logits;        // [max_slots][vocab]
+    float *cmax;          // [max_slots][cstride] 16-column maxima of the synthetic logits
+    uint32_t cstride;
     uint32_t *pf_len, *pf_np, *pf_off;
     int32_t *pf_pages;
     // shared-prefix attention groups, rebuilt by every schedule pass
@@ -1261,23 +1263,41 @@ __global__ void __launch_bounds__(256) prefill_scatter_kernel(const float *kv, c
 }
 
 // logits[v] = std * N(0,1), Philox key = seed, counter = (token index lo,
-// request low 32, tag | token index hi, v / 4).
-__device__ __forceinline__ void logits_row(float *out, uint32_t vocab, uint64_t seed,
-                                           uint32_t request_lo, uint64_t tix, float stdv,
-                                           uint32_t start, uint32_t stride)
+// request low 32, tag | token index hi, v / 4).  With cmax, also each
+// 16-column chunk's maximum (rt_logits_chunk_max's layout) for the sampler.
+// A warp walks 32 consecutive 4-column groups at a time (start - lane is its
+// first group; blockDim and stride are multiples of 32), so the four groups
+// of a chunk sit in four adjacent lanes and meet with two shuffles.
+__device__ __forceinline__ void logits_row(float *out, float *cmax, uint32_t vocab,
+                                           uint64_t seed, uint32_t request_lo, uint64_t tix,
+                                           float stdv, uint32_t start, uint32_t stride)
 {
     const uint32_t groups = (vocab + 3u) / 4u;
-    for (uint32_t g = start; g < groups; g += stride) {
-        float z[4];
-        rt::philox_normal4(seed, (uint32_t)tix, request_lo,
-                           0x4C000000u | (uint32_t)((tix >> 32) & 0xFFFFu), z, g);
-        const uint32_t v = g * 4u;
-        if (v + 3u < vocab && ((reinterpret_cast<uintptr_t>(out + v) & 15u) == 0u)) {
-            reinterpret_cast<float4 *>(out + v)[0] =
-                make_float4(stdv * z[0], stdv * z[1], stdv * z[2], stdv * z[3]);
-        } else {
-            for (uint32_t k = 0; k < 4u && v + k < vocab; k++)
-                out[v + k] = stdv * z[k];
+    const uint32_t lane = threadIdx.x & 31u;
+    for (uint32_t g0 = start - lane; g0 < groups; g0 += stride) {
+        const uint32_t g = g0 + lane;
+        float m = -INFINITY;
+        if (g < groups) {
+            float z[4];
+            rt::philox_normal4(seed, (uint32_t)tix, request_lo,
+                               0x4C000000u | (uint32_t)((tix >> 32) & 0xFFFFu), z, g);
+            const uint32_t v = g * 4u;
+            const float x[4] = {stdv * z[0], stdv * z[1], stdv * z[2], stdv * z[3]};
+            if (v + 3u < vocab && ((reinterpret_cast<uintptr_t>(out + v) & 15u) == 0u)) {
+                reinterpret_cast<float4 *>(out + v)[0] = make_float4(x[0], x[1], x[2], x[3]);
+                m = rt::nan_max(rt::nan_max(x[0], x[1]), rt::nan_max(x[2], x[3]));
+            } else {
+                for (uint32_t k = 0; k < 4u && v + k < vocab; k++) {
+                    out[v + k] = x[k];
+                    m = rt::nan_max(m, x[k]);
+                }
+            }
+        }
+        if (cmax) {
+            m = rt::nan_max(m, __shfl_xor_sync(0xffffffffu, m, 1));
+            m = rt::nan_max(m, __shfl_xor_sync(0xffffffffu, m, 2));
+            if ((g & 3u) == 0u && g < groups)
+                cmax[g / 4u] = m;
         }
     }
 }
@@ -1288,8 +1308,9 @@ __global__ void __launch_bounds__(256) logits_kernel(const Dev d)
     rt::grid_dep_wait();  // launched as a programmatic dependent of the attention
     if (d.enable[s]) {
         const rt_sample_row_t r = d.srows[s];
-        logits_row(d.logits + (size_t)s * d.vocab, d.vocab, r.seed, r.rollout_id, r.step,
-                   d.logit_std, blockIdx.x * blockDim.x + threadIdx.x, gridDim.x * blockDim.x);
+        logits_row(d.logits + (size_t)s * d.vocab, d.cmax + (size_t)s * d.cstride, d.vocab,
+                   r.seed, r.rollout_id, r.step, d.logit_std, blockIdx.x * blockDim.x + threadIdx.x,
+                   gridDim.x * blockDim.x);
     }
     // The sampler may be scheduled once every CTA has written its logits.
     rt::grid_dep_launch();
@@ -1316,7 +1337,7 @@ cudaError_t launch_pdl(void (*kernel)(Args...), dim3 grid, dim3 block, cudaStrea
 __global__ void logits_synth_kernel(float *out, uint32_t vocab, uint64_t seed, uint32_t rq,
                                     uint64_t tix, float stdv)
 {
-    logits_row(out, vocab, seed, rq, tix, stdv, blockIdx.x * blockDim.x + threadIdx.x,
+    logits_row(out, nullptr, vocab, seed, rq, tix, stdv, blockIdx.x * blockDim.x + threadIdx.x,
                gridDim.x * blockDim.x);
 }
 
@@ -1471,7 +1492,8 @@ int launch_decode(rt_rollout *e, cudaStream_t st, cudaEvent_t *ev)
     sp.row_stride = d.vocab;
     sp.fused_cum = 1u;
     sp.row_enable = d.enable;
-    rc = rt::sample_rows_launch(&sp, d.logits, d.srows, d.tokens, st, true);
+    // the logits kernel wrote each row's 16-column maxima beside it
+    rc = rt::sample_rows_launch(&sp, d.logits, d.srows, d.tokens, st, true, d.cmax, d.cstride);
     if (ev)
         cudaEventRecord(ev[4], st);
     return rc;
@@ -1546,7 +1568,7 @@ void engine_free(rt_rollout *e)
         cudaStreamDestroy(e->cap);
     void *bufs[] = {e->d.io, e->d.ctl, e->d.ext, e->d.page_table, e->d.priv, e->d.seq_lens,
                     e->d.enable, e->d.srows, e->d.tokens, e->d.q, e->d.attn_out, e->d.logits,
-                    e->d.pf_len, e->d.pf_np, e->d.pf_off, e->d.pf_pages, e->d.groups,
+                    e->d.cmax, e->d.pf_len, e->d.pf_np, e->d.pf_off, e->d.pf_pages, e->d.groups,
                     e->d.n_groups, e->d.skip, e->attn_ws, e->d.hin, e->d.hout, e->d.qkv,
                     e->d.emb_tok, e->d.gemm_err, e->d.gemm_ws, e->pre_x, e->pre_kv};
     for (void *p : bufs)
@@ -1641,6 +1663,8 @@ extern "C" int rt_rollout_create(const rt_rollout_config_t *cfg, KVArena *arena,
         ok(dalloc(&d.q, (size_t)S * d.hq * 128u));
         ok(dalloc(&d.attn_out, (size_t)S * d.hq * 128u));
         ok(dalloc(&d.logits, (size_t)S * d.vocab));
+        d.cstride = rt_chunk_max_stride(d.vocab);
+        ok(dalloc(&d.cmax, (size_t)S * d.cstride));
         const uint32_t npf = cfg->max_prefixes ? cfg->max_prefixes : 1u;
         ok(dalloc(&d.pf_len, npf));
         ok(dalloc(&d.pf_np, npf));

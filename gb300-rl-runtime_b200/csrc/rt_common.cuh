@@ -284,6 +284,15 @@ __device__ __forceinline__ float fast_exp2(float x)
     return y;
 }
 
+// Maximum that is NaN when either operand is NaN (the chunk maxima a logits
+// producer hands to the sampler flag NaN this way).
+__device__ __forceinline__ float nan_max(float x, float y)
+{
+    float r;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(x), "f"(y));
+    return r;
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi)
 {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);

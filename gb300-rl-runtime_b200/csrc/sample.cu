@@ -9,25 +9,36 @@
 //     by 1.0f / temperature (the reference's fp32 multiply), keep each
 //     thread's maximum and each 16-byte chunk's maximum (in shared memory,
 //     as bf16 rounded up), detect NaN / +inf;
-//  2. each of the 16 warps ranks its 32 per-thread maxima and keeps the
-//     m = ceil(nk / 16) largest; tau0 = the nk-th largest of those 16 m
-//     values.  They are distinct row entries, so at least nk values are
-//     >= tau0: tau0 <= the top-k cutoff (the nk-th largest value counted
-//     with multiplicity) and every survivor is >= tau0;
+//  2. each of the 16 warps takes its m = ceil(nk / 16) largest per-thread
+//     maxima (m rounds of a warp-wide max); tau0 = the nk-th largest of
+//     those 16 m values.  They are distinct row entries, so at least nk
+//     values are >= tau0: tau0 <= the top-k cutoff (the nk-th largest value
+//     counted with multiplicity) and every survivor is >= tau0.  The largest
+//     of them is the row maximum, the softmax's max;
 //  3. a second, partial pass loads only the chunks whose maximum reaches
 //     tau0 (one L2 round trip; about 60 of 8,000 chunks at config 3) and
 //     collects the candidates (values >= tau0, typically 50-90 for k = 50).
 //     Rows too long for the chunk table, or not 16-byte aligned, re-read the
-//     shares of the threads whose own maximum reaches tau0 instead.  A
-//     candidate survives iff fewer than nk
-//     candidates are strictly larger (an all-pairs scan, 16 bytes at a
-//     time); survivors are sorted by vocabulary index (rank sort, typically
-//     k of them);
-//  4. one thread replays the reference's serial fp32 arithmetic over the
-//     survivors only: sum of __expf(l - max) in index order, 1.0f / sum,
-//     cumulative walk, reading the exponentials eight at a time.  Entries the reference masks to -FLT_MAX contribute
-//     __expf(-FLT_MAX - max) which is checked to be exactly 0, so skipping
-//     them leaves every fp32 sum bit-identical.
+//     shares of the threads whose own maximum reaches tau0 instead.  One
+//     all-pairs scan of the candidates (16 bytes at a time) gives each its
+//     rank by vocabulary index and whether it survives (fewer than nk
+//     candidates strictly larger); it is stored at that rank as
+//     __expf(l - max) if it survives, else as +0;
+//  4. one thread replays the reference's serial fp32 arithmetic over those
+//     entries in index order: sum of the exponentials, 1.0f / sum,
+//     cumulative walk, reading eight values at a time.  Adding +0 leaves a
+//     sum unchanged, and so do the entries the reference masks to -FLT_MAX:
+//     their __expf(-FLT_MAX - max) is checked to be exactly 0.  Skipping
+//     them keeps every fp32 sum bit-identical.
+//
+// Producer maxima (rt_sample_rows_cmax): when the kernel that wrote the
+// logits also wrote each 16-column chunk's maximum (NaN if the chunk holds a
+// NaN), pass 1 reads those 2,000 floats per row instead of the row itself:
+// the per-thread maxima, NaN / +inf detection and tau0 follow from them
+// unchanged (1 / T > 0, so scaling is monotone and a chunk's scaled maximum
+// is the maximum of its scaled values), and pass 2 loads only the chunks
+// whose scaled maximum reaches tau0, four lanes per chunk.  The logits row
+// is then read only where candidates can be.
 //
 // Rows the fast path cannot reproduce exactly (top-k disabled, fewer than k
 // finite values, > kCap candidates, a non-zero masked contribution) take
@@ -36,6 +47,7 @@
 // and summed / walked by one thread in index order.  Rows with a NaN or +inf
 // after scaling return vocab - 1, which is what the reference's walk returns
 // for them (its sum becomes NaN).
+#include <algorithm>
 #include <cfloat>
 #include <cstdint>
 #include <mutex>
@@ -52,6 +64,7 @@ constexpr int kBins = 4096;          // radix digits of the streamed cutoff sele
 constexpr int kCap = 1024;           // candidates handled by the fast path
 constexpr int kCmax = 8192;          // 16-byte chunks whose maxima pass 1 keeps (vocab <= 32768)
 constexpr uint32_t kMaxVocab = 1u << 20;
+constexpr uint32_t kChunk = 16;      // logits per producer chunk maximum
 
 
 struct SampleArgs {
@@ -62,7 +75,11 @@ struct SampleArgs {
     uint64_t stride;
     uint32_t vocab;
     uint32_t fused;
+    const float *cmax;   // producer chunk maxima [num_rows][cstride], or nullptr
+    uint32_t cstride;
 };
+
+using rt::nan_max;
 
 __device__ __forceinline__ uint32_t float_key(float v)
 {
@@ -86,13 +103,15 @@ struct __align__(16) Smem {
         // rounded toward +inf, so a chunk whose bf16 maximum is below a
         // threshold holds no value at or above it
         uint16_t cmax[kCmax];
+        // pass 2 with producer maxima: each warp's list of chunks to load
+        uint32_t wl[kWarpsPerRow][128];
     } u;
     uint32_t cand_idx[kCap];
     float cand_val[kCap];
     float e[kCap];                 // exponentials; keep flags before that
     uint32_t red_u[kWarpsPerRow];
     float red_f[kWarpsPerRow];
-    float top[kWarpsPerRow * 16];  // each warp's m largest per-thread maxima (m <= 16)
+    alignas(16) float top[kWarpsPerRow * 16];  // each warp's m largest per-thread maxima (m <= 16)
     uint32_t scan[kWarpsPerRow];
     uint32_t digit, need, count, token, done;
 };
@@ -282,6 +301,48 @@ __device__ __forceinline__ uint32_t select_and_sort(uint32_t nc, uint32_t nk, Sm
     return ns;
 }
 
+// The nc candidates of cand_* in vocabulary order, in one all-pairs pass:
+// candidate j goes to position (its index's rank among the candidates) with
+// s.e = __expf(value - mx) if it survives (fewer than nk candidates strictly
+// larger; all when nk == 0), else +0, which leaves the serial sum and the
+// cumulative walk unchanged.  Zero-padded to a multiple of 8 entries (the
+// candidate arrays to a multiple of 4, -inf at index ~0, so the scans read
+// 16 bytes at a time); returns the padded count.
+__device__ __forceinline__ uint32_t survivors_by_index(uint32_t nc, uint32_t nk, float mx,
+                                                       Smem &s)
+{
+    const uint32_t n4 = (nc + 3u) & ~3u, n8 = (nc + 7u) & ~7u;
+    for (uint32_t j = nc + threadIdx.x; j < n8; j += kThr) {
+        if (j < n4) {
+            s.cand_val[j] = -INFINITY;
+            s.cand_idx[j] = 0xFFFFFFFFu;
+        }
+        s.e[j] = 0.0f;
+        s.u.sorted.idx[j] = 0u;
+    }
+    __syncthreads();
+    const float4 *cv4 = reinterpret_cast<const float4 *>(s.cand_val);
+    const uint4 *ci4 = reinterpret_cast<const uint4 *>(s.cand_idx);
+    for (uint32_t j = threadIdx.x; j < nc; j += kThr) {
+        const float v = s.cand_val[j];
+        const uint32_t id = s.cand_idx[j];
+        uint32_t gt = 0, lo = 0;
+#pragma unroll 4
+        for (uint32_t i = 0; i < n4 / 4u; i++) {
+            const float4 c = cv4[i];
+            const uint4 d = ci4[i];
+            gt += (c.x > v ? 1u : 0u) + (c.y > v ? 1u : 0u) + (c.z > v ? 1u : 0u) +
+                  (c.w > v ? 1u : 0u);
+            lo += (d.x < id ? 1u : 0u) + (d.y < id ? 1u : 0u) + (d.z < id ? 1u : 0u) +
+                  (d.w < id ? 1u : 0u);
+        }
+        s.u.sorted.idx[lo] = id;
+        s.e[lo] = (nk == 0u || gt < nk) ? __expf(__fsub_rn(v, mx)) : 0.0f;
+    }
+    __syncthreads();
+    return n8;
+}
+
 // Streams the row as 16-byte loads (kDepth in flight per thread) when the
 // row is 16-byte aligned, calling f(scaled value, vocabulary index); the
 // remainder and unaligned rows go element by element.
@@ -331,9 +392,10 @@ __device__ __forceinline__ uint32_t serial_walk(const Smem &s, uint32_t ns8, boo
                                                 uint32_t fused, uint32_t V)
 {
     const float4 *e4 = reinterpret_cast<const float4 *>(s.e);
+    const uint32_t nb = ns8 / 8u;
     float sum = 0.0f;
 #pragma unroll 2
-    for (uint32_t b = 0; b < ns8 / 8u; b++) {
+    for (uint32_t b = 0; b < nb; b++) {
         const float4 x = e4[2 * b], y = e4[2 * b + 1];
         sum = __fadd_rn(sum, x.x);
         sum = __fadd_rn(sum, x.y);
@@ -349,10 +411,11 @@ __device__ __forceinline__ uint32_t serial_walk(const Smem &s, uint32_t ns8, boo
         return topp ? (fused ? __fmaf_rn(e, inv, c) : __fadd_rn(c, __fmul_rn(e, inv)))
                     : __fadd_rn(c, __fdiv_rn(e, sum));
     };
-    // cum never decreases, and a padding entry repeats the previous value,
-    // so the first entry with cum >= r lies below ns
+    // cum never decreases, and a +0 entry (padding, or a candidate that did
+    // not survive) repeats the previous value (r > 0), so the first entry
+    // with cum >= r is a survivor
     float cum = 0.0f;
-    for (uint32_t b = 0; b < ns8 / 8u; b++) {
+    for (uint32_t b = 0; b < nb; b++) {
         const float4 x = e4[2 * b], y = e4[2 * b + 1];
         const float ev[8] = {x.x, x.y, x.z, x.w, y.x, y.y, y.z, y.w};
         int hit = -1;
@@ -396,7 +459,27 @@ __global__ void __launch_bounds__(kThr, 2) sample_rows_kernel(const SampleArgs a
     const bool vec = (reinterpret_cast<uintptr_t>(rd.row) & 15u) == 0u;
     const uint32_t V4 = vec ? V / 4u : 0u;
     const bool track = vec && V4 <= (uint32_t)kCmax;
-    {
+    // producer maxima: thread t owns the chunks 4g .. 4g+3 for g = t, t + kThr, ...
+    const float *crow = a.cmax ? a.cmax + (size_t)blockIdx.x * a.cstride : nullptr;
+    const uint32_t nch = (V + kChunk - 1u) / kChunk;
+    const uint32_t ngr = (nch + 3u) / 4u;
+    float4 cm0 = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);  // group g = t
+    if (crow) {
+        for (uint32_t g = (uint32_t)tid; g < ngr; g += kThr) {
+            const float4 c = __ldg(reinterpret_cast<const float4 *>(crow) + g);
+            if (g == (uint32_t)tid)
+                cm0 = c;
+            const float cv[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+            for (uint32_t j = 0; j < 4u; j++) {
+                if (4u * g + j < nch) {
+                    const float x = rd.scale ? __fmul_rn(cv[j], rd.inv_t) : cv[j];
+                    bad |= !(x < INFINITY);  // NaN or +inf in the chunk
+                    tmax = x > -FLT_MAX ? fmaxf(tmax, x) : tmax;
+                }
+            }
+        }
+    } else {
         const float4 *row4 = reinterpret_cast<const float4 *>(rd.row);
         constexpr uint32_t kDepth = 8;
         for (uint32_t base = 0; base < V4; base += kDepth * kThr) {
@@ -472,34 +555,43 @@ __global__ void __launch_bounds__(kThr, 2) sample_rows_kernel(const SampleArgs a
         // survive the threshold at config 3, against ~140 for the smallest
         // of the warps' m-th largest maxima.)
         const uint32_t m = (nk + kWarpsPerRow - 1) / kWarpsPerRow;
-        uint32_t gt = 0, eq_lo = 0;
-#pragma unroll
-        for (int o = 0; o < 32; o++) {
-            const float x = __shfl_sync(0xffffffffu, tmax, o);
-            gt += x > tmax ? 1u : 0u;
-            eq_lo += (x == tmax && o < lane) ? 1u : 0u;
+        // the warp's m largest per-thread maxima, one warp-wide max a round
+        // (a tie goes to the lowest lane, which then drops out: keys of
+        // values are > 0, a removed lane holds 0)
+        uint32_t key = float_key(tmax);
+        for (uint32_t j = 0; j < m; j++) {
+            const uint32_t kmax = __reduce_max_sync(0xffffffffu, key);
+            const uint32_t who = __ballot_sync(0xffffffffu, key == kmax);
+            if (lane == __ffs(who) - 1) {
+                s.top[warp * m + j] = key_float(kmax);
+                key = 0u;
+            }
         }
-        const uint32_t rank = gt + eq_lo;  // unique within the warp
-        if (rank < m)
-            s.top[warp * m + rank] = tmax;
         __syncthreads();
-        const uint32_t n_top = m * kWarpsPerRow;
+        const uint32_t n_top = m * kWarpsPerRow;  // a multiple of 16
         if ((uint32_t)tid < n_top) {
             const float v = s.top[tid];
+            const float4 *t4 = reinterpret_cast<const float4 *>(s.top);
             uint32_t g2 = 0, e2 = 0;
-            for (uint32_t i = 0; i < n_top; i++) {
-                const float x = s.top[i];
-                g2 += x > v ? 1u : 0u;
-                e2 += x >= v ? 1u : 0u;
+#pragma unroll 4
+            for (uint32_t i = 0; i < n_top / 4u; i++) {
+                const float4 x = t4[i];
+                g2 += (x.x > v ? 1u : 0u) + (x.y > v ? 1u : 0u) + (x.z > v ? 1u : 0u) +
+                      (x.w > v ? 1u : 0u);
+                e2 += (x.x >= v ? 1u : 0u) + (x.y >= v ? 1u : 0u) + (x.z >= v ? 1u : 0u) +
+                      (x.w >= v ? 1u : 0u);
             }
             if (g2 < nk && e2 >= nk)
                 s.red_f[0] = v;  // every such thread holds the same value
+            if (g2 == 0u)
+                s.red_f[1] = v;  // the row maximum (of the values > -FLT_MAX)
         }
         __syncthreads();
         const float tau0 = s.red_f[0];
+        const float rowmax = s.red_f[1];
         // fewer than nk finite maxima: the fallback below counts the values
+        // (red_f is next written by a block reduction behind later barriers)
         const bool ok = tau0 > -FLT_MAX;
-        __syncthreads();
         if (ok) {
             // ---- pass 2: candidates >= tau0, re-read only by the threads
             // whose own maximum reaches tau0 (the others hold none: about
@@ -513,7 +605,65 @@ __global__ void __launch_bounds__(kThr, 2) sample_rows_kernel(const SampleArgs a
                     }
                 }
             };
-            if (track) {
+            if (crow) {
+                // chunks whose scaled producer maximum reaches tau0: each
+                // warp lists its lanes' chunks, then loads them four lanes
+                // per chunk (one 16-byte load per lane, 8 chunks a round)
+                uint32_t *wl = s.u.wl[warp];
+                for (uint32_t g0 = 0; g0 < ngr; g0 += kThr) {  // uniform over the block
+                    const uint32_t g = g0 + (uint32_t)tid;
+                    uint32_t bits = 0;
+                    if (g < ngr) {
+                        const float4 c = g0 == 0u ? cm0
+                                                  : __ldg(reinterpret_cast<const float4 *>(crow) + g);
+                        const float cv[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+                        for (uint32_t j = 0; j < 4u; j++) {
+                            const float x = rd.scale ? __fmul_rn(cv[j], rd.inv_t) : cv[j];
+                            bits |= (4u * g + j < nch && x >= tau0) ? 1u << j : 0u;
+                        }
+                    }
+                    const uint32_t n = __popc(bits);
+                    uint32_t incl = n;
+#pragma unroll
+                    for (int o = 1; o < 32; o <<= 1) {
+                        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+                        if (lane >= o)
+                            incl += y;
+                    }
+                    const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
+                    uint32_t pos = incl - n;
+                    while (bits) {
+                        const uint32_t j = (uint32_t)__ffs(bits) - 1u;
+                        bits &= bits - 1u;
+                        wl[pos++] = 4u * g + j;
+                    }
+                    __syncwarp();
+                    for (uint32_t i = (uint32_t)lane >> 2; i < ((total + 7u) & ~7u); i += 8u) {
+                        if (i < total) {
+                            const uint32_t i0 = wl[i] * kChunk + 4u * ((uint32_t)lane & 3u);
+                            if (vec && i0 + 3u < V) {
+                                float4 x = __ldg(reinterpret_cast<const float4 *>(rd.row + i0));
+                                if (rd.scale) {
+                                    x.x = __fmul_rn(x.x, rd.inv_t);
+                                    x.y = __fmul_rn(x.y, rd.inv_t);
+                                    x.z = __fmul_rn(x.z, rd.inv_t);
+                                    x.w = __fmul_rn(x.w, rd.inv_t);
+                                }
+                                add(x.x, i0);
+                                add(x.y, i0 + 1u);
+                                add(x.z, i0 + 2u);
+                                add(x.w, i0 + 3u);
+                            } else {
+                                for (uint32_t k = 0; k < 4u; k++)
+                                    if (i0 + k < V)
+                                        add(rd(i0 + k), i0 + k);
+                            }
+                        }
+                    }
+                    __syncwarp();  // the list is rewritten by the next round
+                }
+            } else if (track) {
                 // only the chunks whose maximum reaches tau0, loaded together
                 // (a thread rarely has more than one)
                 const float4 *row4 = reinterpret_cast<const float4 *>(rd.row);
@@ -561,6 +711,16 @@ __global__ void __launch_bounds__(kThr, 2) sample_rows_kernel(const SampleArgs a
             __syncthreads();
             const uint32_t nc = s.count;
             if (nc <= (uint32_t)kCap) {
+                // The masked entries' terms __expf(-FLT_MAX - max) must be
+                // exactly 0 (the maximum is the row maximum: it survives).
+                // Then every candidate goes in index order, non-survivors
+                // as +0 terms, and one barrier precedes the walk.
+                if (__expf(__fsub_rn(-FLT_MAX, rowmax)) == 0.0f) {
+                    const uint32_t nc8 = survivors_by_index(nc, nk, rowmax, s);
+                    if (tid == 0)
+                        a.out[blockIdx.x] = serial_walk(s, nc8, topp, r, a.fused, V);
+                    return;
+                }
                 ns = select_and_sort(nc, nk, s);
                 sorted_ready = true;
             }
@@ -666,7 +826,90 @@ __global__ void __launch_bounds__(kThr, 2) sample_rows_kernel(const SampleArgs a
         a.out[blockIdx.x] = tok;
 }
 
+// chunk_max[r][c] = max of logits[r][16c .. 16c+15] (NaN if one is NaN):
+// lanes read consecutive 16-byte groups of the row and the four lanes of a
+// chunk reduce it with two shuffles.  Grid (x: chunks of the row, y: rows).
+__global__ void __launch_bounds__(256) chunk_max_kernel(const float *logits, uint32_t V,
+                                                        uint64_t stride, float *cmax,
+                                                        uint32_t cstride)
+{
+    const float *row = logits + (size_t)blockIdx.y * stride;
+    float *crow = cmax + (size_t)blockIdx.y * cstride;
+    const uint32_t nq = (V + 3u) / 4u;
+    const bool vec = (reinterpret_cast<uintptr_t>(row) & 15u) == 0u;
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint32_t step = gridDim.x * blockDim.x;
+    for (uint32_t q0 = blockIdx.x * blockDim.x + threadIdx.x - lane; q0 < nq; q0 += step) {
+        const uint32_t q = q0 + lane;
+        float m = -INFINITY;
+        if (q < nq) {
+            const uint32_t i = 4u * q;
+            if (vec && i + 3u < V) {
+                const float4 v = __ldg(reinterpret_cast<const float4 *>(row + i));
+                m = nan_max(nan_max(v.x, v.y), nan_max(v.z, v.w));
+            } else {
+                for (uint32_t k = 0; k < 4u; k++)
+                    if (i + k < V)
+                        m = nan_max(m, __ldg(row + i + k));
+            }
+        }
+        m = nan_max(m, __shfl_xor_sync(0xffffffffu, m, 1));
+        m = nan_max(m, __shfl_xor_sync(0xffffffffu, m, 2));
+        if ((q & 3u) == 0u && q < nq)
+            crow[q / 4u] = m;
+    }
+}
+
 }  // namespace
+
+extern "C" uint32_t rt_chunk_max_stride(uint32_t vocab)
+{
+    const uint32_t nch = (vocab + kChunk - 1u) / kChunk;
+    return (nch + 3u) & ~3u;
+}
+
+extern "C" int rt_logits_chunk_max(const float *logits, uint32_t num_rows, uint32_t vocab,
+                                   uint64_t row_stride, float *chunk_max, uint32_t cmax_stride,
+                                   void *stream)
+{
+    if (!logits || !chunk_max) {
+        rt::set_error("chunk_max: null argument");
+        return RT_EINVAL;
+    }
+    if (vocab == 0 || vocab > kMaxVocab || row_stride < vocab ||
+        cmax_stride < rt_chunk_max_stride(vocab)) {
+        rt::set_error("chunk_max: vocab %u must be in 1..%u, <= row_stride %llu, and "
+                      "cmax_stride %u >= %u",
+                      vocab, kMaxVocab, (unsigned long long)row_stride, cmax_stride,
+                      rt_chunk_max_stride(vocab));
+        return RT_EINVAL;
+    }
+    if (((uintptr_t)logits & 3u) || ((uintptr_t)chunk_max & 3u) || num_rows > 65535u) {
+        rt::set_error("chunk_max: misaligned pointer or more than 65535 rows");
+        return RT_EINVAL;
+    }
+    if (num_rows == 0)
+        return RT_OK;
+    const uint32_t nq = (vocab + 3u) / 4u;
+    const dim3 grid(std::min((nq + 255u) / 256u, 64u), num_rows);
+    chunk_max_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(logits, vocab, row_stride, chunk_max,
+                                                              cmax_stride);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? RT_OK : rt::cuda_fail(e, "chunk_max: launch");
+}
+
+extern "C" int rt_sample_rows_cmax(const rt_sample_params_t *p, const float *logits,
+                                   const float *chunk_max, uint32_t cmax_stride,
+                                   const rt_sample_row_t *rows, uint32_t *tokens_out,
+                                   void *stream)
+{
+    if (!chunk_max) {
+        rt::set_error("sample: null chunk_max");
+        return RT_EINVAL;
+    }
+    return rt::sample_rows_launch(p, logits, rows, tokens_out, (cudaStream_t)stream, false,
+                                  chunk_max, cmax_stride);
+}
 
 extern "C" uint32_t rt_sample_uniform24(uint64_t seed, uint32_t rollout_id, uint64_t step)
 {
@@ -684,7 +927,7 @@ extern "C" int rt_sample_rows(const rt_sample_params_t *p, const float *logits,
 
 int rt::sample_rows_launch(const rt_sample_params_t *p, const float *logits,
                            const rt_sample_row_t *rows, uint32_t *tokens_out, cudaStream_t stream,
-                           bool pdl)
+                           bool pdl, const float *cmax, uint32_t cmax_stride)
 {
     if (!p || !logits || !rows || !tokens_out) {
         rt::set_error("sample: null argument");
@@ -698,6 +941,13 @@ int rt::sample_rows_launch(const rt_sample_params_t *p, const float *logits,
     if (((uintptr_t)logits & 3u) || ((uintptr_t)rows & 7u) || ((uintptr_t)tokens_out & 3u) ||
         ((uintptr_t)p->row_enable & 3u)) {
         rt::set_error("sample: misaligned pointer");
+        return RT_EINVAL;
+    }
+    if (cmax && (((uintptr_t)cmax & 15u) || (cmax_stride & 3u) ||
+                 cmax_stride < rt_chunk_max_stride(p->vocab))) {
+        rt::set_error("sample: chunk_max must be 16-byte aligned with a stride that is a "
+                      "multiple of 4 and >= %u (got %u)",
+                      rt_chunk_max_stride(p->vocab), cmax_stride);
         return RT_EINVAL;
     }
     if (p->num_rows == 0)
@@ -714,6 +964,8 @@ int rt::sample_rows_launch(const rt_sample_params_t *p, const float *logits,
     a.stride = p->row_stride;
     a.vocab = p->vocab;
     a.fused = p->fused_cum ? 1u : 0u;
+    a.cmax = cmax;
+    a.cstride = cmax_stride;
     cudaError_t e;
     if (pdl) {
         cudaLaunchAttribute attr[1];

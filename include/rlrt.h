@@ -221,6 +221,25 @@ int rt_sample_rows(const rt_sample_params_t *p, const float *logits,
 /* The 24-bit uniform rt_sample_rows uses for (seed, rollout_id, step). */
 uint32_t rt_sample_uniform24(uint64_t seed, uint32_t rollout_id, uint64_t step);
 
+/* Producer chunk maxima.  chunk_max fp32 [num_rows][cmax_stride] (device)
+ * holds, for chunk c of a row, the maximum of logits[16c .. 16c+15] (the
+ * last chunk is partial), or NaN when one of them is NaN.  The kernel that
+ * writes the logits can write them at little cost (the rollout loop's
+ * logits kernel does); rt_logits_chunk_max computes them from the logits.
+ * cmax_stride >= rt_chunk_max_stride(vocab), a multiple of 4. */
+uint32_t rt_chunk_max_stride(uint32_t vocab);
+int rt_logits_chunk_max(const float *logits, uint32_t num_rows, uint32_t vocab,
+                        uint64_t row_stride, float *chunk_max, uint32_t cmax_stride,
+                        void *stream);
+
+/* rt_sample_rows given the logits' chunk maxima (16-byte aligned): the same
+ * tokens, bit for bit, for any logits; the common row reads its chunk
+ * maxima and only the chunks that can hold a top-k survivor, not the whole
+ * row.  Chunk maxima that do not match the logits give undefined tokens. */
+int rt_sample_rows_cmax(const rt_sample_params_t *p, const float *logits,
+                        const float *chunk_max, uint32_t cmax_stride,
+                        const rt_sample_row_t *rows, uint32_t *tokens_out, void *stream);
+
 /* ------------------------------------------------------------------------
  * GPU-resident rollout loop.
  *
