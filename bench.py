@@ -409,9 +409,31 @@ class SamplingWorkload(Workload):
         self.bytes = self.R * self.V * 4 + self.R * (32 + 4)
         self.i = 0
         torch.cuda.synchronize()
+        # the kernel is shorter than a Python ctypes call: steps replay one
+        # captured call per buffer so the launch gaps do not set the time
+        self.graphs = self._graphs(lambda i: self.pkg.sample_rows(
+            self.bufs[i], self.rows, self.V, out=self.out))
+
+    def _graphs(self, call):
+        """One CUDA graph per logits buffer holding call(buffer index)."""
+        torch = self.torch
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for i in range(self.NBUF):
+                call(i)
+        torch.cuda.current_stream().wait_stream(side)
+        graphs = []
+        for i in range(self.NBUF):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                call(i)
+            graphs.append(g)
+        torch.cuda.synchronize()
+        return graphs
 
     def step(self):
-        self.pkg.sample_rows(self.bufs[self.i % self.NBUF], self.rows, self.V, out=self.out)
+        self.graphs[self.i % self.NBUF].replay()
         self.i += 1
 
     def units_per_step(self):
@@ -420,9 +442,9 @@ class SamplingWorkload(Workload):
     def details(self):
         """The same calls given each buffer's 16-column chunk maxima
         (rt_sample_rows_cmax, the rollout loop's path: its logits kernel
-        writes them), CUDA events over 50 calls on the rotating buffers, and
-        the standalone chunk-maximum kernel; tokens compared with the
-        full-row path."""
+        writes them), CUDA events over 50 graph-replayed calls on the
+        rotating buffers, and the standalone chunk-maximum kernel; tokens
+        compared with the full-row path."""
         torch, pkg = self.torch, self.pkg
         cms = [pkg.logits_chunk_max(b, self.V) for b in self.bufs]
         full = [pkg.sample_rows(b, self.rows, self.V).clone() for b in self.bufs]
@@ -443,10 +465,11 @@ class SamplingWorkload(Workload):
             torch.cuda.synchronize()
             return e0.elapsed_time(e1) * 1e3 / n
 
-        us = timed(lambda i: pkg.sample_rows_cmax(self.bufs[i % self.NBUF], cms[i % self.NBUF],
-                                                  self.rows, self.V, out=self.out))
-        us_cm = timed(lambda i: pkg.logits_chunk_max(self.bufs[i % self.NBUF], self.V,
-                                                     out=cms[i % self.NBUF]))
+        g_s = self._graphs(lambda i: pkg.sample_rows_cmax(self.bufs[i], cms[i], self.rows,
+                                                          self.V, out=self.out))
+        g_c = self._graphs(lambda i: pkg.logits_chunk_max(self.bufs[i], self.V, out=cms[i]))
+        us_cm = timed(lambda i: g_c[i % self.NBUF].replay())
+        us = timed(lambda i: g_s[i % self.NBUF].replay())
         return {"producer_maxima": {
             "us_per_call": us, "tokens_equal_full_path": equal,
             "chunk_max_kernel_us": us_cm,
