@@ -55,6 +55,14 @@ constexpr int kCtasPerSm = RT_ATTN_CTAS_PER_SM;  // resident CTAs per SM (shared
 constexpr int kStageBytes = 8192;    // K (2 x 2 KiB halves) + V (2 x 2 KiB)
 constexpr int kMaxChunkPages = 64;   // page ids live in two registers per lane
 constexpr int kSmemBytes = kWarps * kStages * kStageBytes + 1024;  // + 1 KiB alignment slack
+// The sequence kernel adds each warp's G query rows, kQRowWords words a row
+// (64 + 4 padding, so that the fragment reads of 8 rows hit 8 banks).
+constexpr int kQRowWords = 68;
+template <int G>
+constexpr int seq_smem_bytes()
+{
+    return kSmemBytes + kWarps * G * kQRowWords * 4;
+}
 constexpr uint64_t kWaitLimitNs = 2000000000ull;                    // 2 s per pipeline wait
 
 enum : int32_t { kErrSeqLen = 1, kErrPage = 2, kErrTimeout = 3, kErrGroup = 4 };
@@ -84,6 +92,7 @@ struct AttnArgs {
     unsigned int *group_done;          // CTAs that left the group phase
     uint32_t max_groups, gchunk_pages, max_gchunks;
     uint32_t slots;                    // partial slots per (b, h): max_gchunks + max_chunks
+    const uint32_t *dyn_chunks;        // this launch's largest chunk count (device), or nullptr
 };
 
 // The shared-prefix (group) kernel uses the CTA's whole ring.  Alone it is
@@ -174,8 +183,7 @@ __device__ __forceinline__ void merge_parts(const AttnArgs &a, size_t bh, uint32
     }
 }
 
-// One warp processes one item; see the file comment.  Returns false when a
-// pipeline wait expired (the warp then stops taking items).
+// Sequence items: one warp per item; see the file comment.
 //
 // The tile is transposed relative to the usual decode formulation, because
 // a KV group has only G <= 8 query heads: S^T = K.Q^T takes the page's 16
@@ -184,221 +192,171 @@ __device__ __forceinline__ void merge_parts(const AttnArgs &a, size_t bh, uint32
 // mma for S and 8 per P term for O per page, half of what 16-row query tiles
 // (12 of them zero for G = 4) cost.  The S^T accumulator becomes the B
 // operand of the second product through one movmatrix transpose per 8x8 block.
+// A sequence item as one warp sees it: which (sequence, KV head, chunk), its
+// page range and page ids (lane i holds item pages i and 32 + i), and what
+// is left to do.  Filled by seq_setup from the item number alone plus three
+// small loads (length, group coverage, the page-table row).
+struct SeqItem {
+    uint32_t b, h, n_g;
+    int chunk, L, n_chunks, p_begin, n_mine;
+    int pg_lo, pg_hi;
+    uint32_t kind;  // kSeqNone: nothing; kSeqZero: write a zero output; kSeqWork: pages or a group fold
+};
+enum : uint32_t { kSeqNone = 0, kSeqZero = 1, kSeqWork = 2 };
+
+// The launch's items: (chunk from the highest index down, sequence, KV
+// head), so the full chunks go first and chunk 0 - the remainders, folds and
+// zero outputs, the short items - last, which keeps the tail short.  The
+// chunk count is the plan's (from max_seq_len) or, when the caller publishes
+// this launch's largest chunk count on the device (the rollout loop's
+// schedule kernel does), that count: chunks past a sequence's end are empty
+// items, and the published count leaves none when every sequence has the
+// same number of chunks.
+struct SeqPlan {
+    uint32_t max_chunks;
+    uint64_t n_items;
+};
+__device__ __forceinline__ SeqPlan seq_plan(const AttnArgs &a)
+{
+    SeqPlan pl;
+    pl.max_chunks = a.max_chunks;
+    if (a.dyn_chunks) {
+        const uint32_t c = *a.dyn_chunks;
+        pl.max_chunks = c < 1u ? 1u : (c < a.max_chunks ? c : a.max_chunks);
+    }
+    pl.n_items = (uint64_t)a.num_seqs * a.num_kv_heads * pl.max_chunks;
+    return pl;
+}
+
 template <int G>
-__device__ __forceinline__ bool process_item(const CUtensorMap &kv_map, const AttnArgs &a,
-                                             uint64_t item, uint32_t stage0, uint8_t *base_ptr,
-                                             uint32_t base_u32, uint64_t (&bars)[kStages],
-                                             uint32_t &phases, uint64_t policy)
+__device__ __forceinline__ SeqItem seq_setup(const AttnArgs &a, const SeqPlan &pl, uint64_t item)
 {
     const int lane = threadIdx.x & 31;
-    const uint32_t B = a.num_seqs, Hq = a.num_q_heads, Hkv = a.num_kv_heads;
-    const uint32_t h = (uint32_t)(item % Hkv);
-    const uint64_t rest = item / Hkv;
-    const uint32_t b = (uint32_t)(rest % B);
-    // Chunks are handed out from the highest index down: chunk 0 holds the
-    // remainder pages and every other chunk is full, so the last items of a
-    // launch are the short ones and the tail stays short.
-    const int chunk = (int)a.max_chunks - 1 - (int)(rest / B);
-    // Independent loads first (length, group coverage, the Q fragment), so
-    // their round trips overlap.
-    const int L = a.seq_lens[b];
-    const uint32_t skip_raw = a.skip_pages ? a.skip_pages[b] : 0u;
-    const int r = lane >> 2, q4 = lane & 3;
-    // Q as the B operand (col-major 16 dims x 8 heads): lane holds head r,
-    // dims 16j + 2q4 (+1) and 16j + 8 + 2q4 (+1); heads >= G are zero.
-    uint32_t qb[8][2];
-    {
-        const uint32_t *qrow = reinterpret_cast<const uint32_t *>(
-            a.q + ((size_t)b * Hq + (size_t)h * G + (r < G ? r : 0)) * 128);
-#pragma unroll
-        for (int j = 0; j < 8; j++) {
-            qb[j][0] = r < G ? qrow[8 * j + q4] : 0u;
-            qb[j][1] = r < G ? qrow[8 * j + 4 + q4] : 0u;
-        }
-    }
-
-    if (L < 0 || (uint32_t)L > a.max_seq_len || (uint32_t)L > a.max_pages * 16u) {
-        if (lane == 0 && chunk == 0)
+    SeqItem it;
+    it.kind = kSeqNone;
+    it.n_mine = 0;
+    it.n_g = 0;
+    it.n_chunks = 0;
+    it.p_begin = 0;
+    it.pg_lo = it.pg_hi = 0;
+    it.L = 0;
+    it.b = it.h = 0;
+    it.chunk = 1;
+    if (item >= pl.n_items)
+        return it;
+    const uint32_t B = a.num_seqs, Hkv = a.num_kv_heads;
+    it.h = (uint32_t)(item % Hkv);
+    const uint64_t unit = item / Hkv;
+    it.b = (uint32_t)(unit % B);
+    it.chunk = (int)pl.max_chunks - 1 - (int)(unit / B);
+    const int L = a.seq_lens[it.b];
+    const uint32_t skip_raw = a.skip_pages ? a.skip_pages[it.b] : 0u;
+    it.L = L;
+    const rt::AttnSeqShape sh = rt::attn_seq_shape(L, skip_raw, a.max_seq_len, a.max_pages,
+                                                   a.gchunk_pages, a.max_gchunks, a.chunk_pages);
+    if (sh.bad_len) {
+        if (lane == 0 && it.chunk == 0)
             flag_error(a.error, kErrSeqLen);
-        return true;
+        return it;
     }
     if (L == 0) {
-        if (chunk == 0)
-            for (int i = lane; i < G * 128; i += 32)
-                a.out[((size_t)b * Hq + (size_t)h * G) * 128 + i] = 0.0f;
-        return true;
+        if (it.chunk == 0)
+            it.kind = kSeqZero;
+        return it;
     }
-    const int n_pages = (L + 15) >> 4;
-    int skip = (int)skip_raw;
-    if (skip_raw > (uint32_t)n_pages || skip_raw > a.max_gchunks * a.gchunk_pages) {
+    if (sh.bad_skip)
         flag_error(a.error, kErrGroup);
-        skip = 0;
-    }
+    // a published chunk count below this sequence's would drop its top chunks
+    if (sh.n_chunks > (int)pl.max_chunks && it.chunk == 0 && lane == 0)
+        flag_error(a.error, kErrSeqLen);
     const int cp = (int)a.chunk_pages;
-    const uint32_t n_g = (uint32_t)((skip + (int)a.gchunk_pages - 1) / (int)a.gchunk_pages);
-    // This sequence's own chunks; a fully covered sequence still has chunk 0,
-    // which folds the group's partials into the output.
-    const int n_chunks = max((n_pages - skip + cp - 1) / cp, n_g ? 1 : 0);
-    if (chunk >= n_chunks)
-        return true;
-    const int rem = (n_pages - skip) - (n_chunks - 1) * cp;  // pages of chunk 0 (may be 0)
-    const int p_begin = skip + (chunk == 0 ? 0 : rem + (chunk - 1) * cp);
-    const int n_mine = chunk == 0 ? max(0, rem) : cp;
-    const size_t bh = (size_t)b * Hkv + h;
-
-    // Page ids of this item: lane i holds pages i and 32 + i.
-    const int32_t *ptab = a.page_table + (size_t)b * a.max_pages + p_begin;
-    int pg_lo = 0, pg_hi = 0;
-    if (lane < n_mine)
-        pg_lo = ptab[lane];
-    if (lane + 32 < n_mine)
-        pg_hi = ptab[lane + 32];
-    const bool bad = (lane < n_mine && (pg_lo < 0 || (uint64_t)pg_lo >= a.arena_pages)) ||
-                     (lane + 32 < n_mine && (pg_hi < 0 || (uint64_t)pg_hi >= a.arena_pages));
+    it.n_g = sh.n_g;
+    it.n_chunks = sh.n_chunks;
+    if (it.chunk < 0 || it.chunk >= it.n_chunks)
+        return it;
+    const int rem = (sh.n_pages - sh.skip) - (it.n_chunks - 1) * cp;  // pages of chunk 0 (may be 0)
+    it.p_begin = sh.skip + (it.chunk == 0 ? 0 : rem + (it.chunk - 1) * cp);
+    it.n_mine = it.chunk == 0 ? max(0, rem) : cp;
+    it.kind = kSeqWork;
+    const int32_t *ptab = a.page_table + (size_t)it.b * a.max_pages + it.p_begin;
+    if (lane < it.n_mine)
+        it.pg_lo = ptab[lane];
+    if (lane + 32 < it.n_mine)
+        it.pg_hi = ptab[lane + 32];
+    const bool bad = (lane < it.n_mine && (it.pg_lo < 0 || (uint64_t)it.pg_lo >= a.arena_pages)) ||
+                     (lane + 32 < it.n_mine && (it.pg_hi < 0 || (uint64_t)it.pg_hi >= a.arena_pages));
     if (bad) {
         flag_error(a.error, kErrPage);
-        if (pg_lo < 0 || (uint64_t)pg_lo >= a.arena_pages)
-            pg_lo = 0;
-        if (pg_hi < 0 || (uint64_t)pg_hi >= a.arena_pages)
-            pg_hi = 0;
+        if (it.pg_lo < 0 || (uint64_t)it.pg_lo >= a.arena_pages)
+            it.pg_lo = 0;
+        if (it.pg_hi < 0 || (uint64_t)it.pg_hi >= a.arena_pages)
+            it.pg_hi = 0;
     }
+    return it;
+}
 
-    auto issue = [&](int i, int s) {
-        const int pg = __shfl_sync(0xffffffffu, i < 32 ? pg_lo : pg_hi, i & 31);
-        if (lane == 0) {
-            const uint32_t bar = rt::smem_u32(&bars[s]);
-            const uint32_t dst = stage0 + (uint32_t)(s * kStageBytes);
-            const int32_t row_k = (int32_t)(((int64_t)pg * Hkv + h) * 32);
-            rt::mbar_arrive_expect_tx(bar, (uint32_t)kStageBytes);
-            rt::tma_load_2d(dst, &kv_map, 0, row_k, bar, policy);
-            rt::tma_load_2d(dst + 2048u, &kv_map, 64, row_k, bar, policy);
-            rt::tma_load_2d(dst + 4096u, &kv_map, 0, row_k + 16, bar, policy);
-            rt::tma_load_2d(dst + 6144u, &kv_map, 64, row_k + 16, bar, policy);
-        }
-    };
-    // The stage ring was left idle by the previous item: order this warp's
-    // earlier generic accesses of it before the new TMA writes.
-    rt::fence_proxy_async_smem();
-    for (int i = 0; i < n_mine && i < kStages; i++)
-        issue(i, i);
-    // Online-softmax state: lane owns heads 2q4, 2q4 + 1 and dims 16dd + r,
-    // 16dd + r + 8 of the O^T tiles.
-    float o[8][4];
+// Page i of the item into ring slot `ctr` (the warp's ctr-th issued page):
+// lane 0 issues the four 2-D TMA loads (K and V halves) on that stage's
+// mbarrier.
+__device__ __forceinline__ void seq_issue(const CUtensorMap &kv_map, const AttnArgs &a,
+                                          const SeqItem &it, int i, uint32_t ctr, uint32_t stage0,
+                                          uint64_t (&bars)[kStages], uint64_t policy)
+{
+    const int pg = __shfl_sync(0xffffffffu, i < 32 ? it.pg_lo : it.pg_hi, i & 31);
+    if ((threadIdx.x & 31) == 0) {
+        const uint32_t s = ctr % (uint32_t)kStages;
+        const uint32_t bar = rt::smem_u32(&bars[s]);
+        const uint32_t dst = stage0 + s * (uint32_t)kStageBytes;
+        const int32_t row_k = (int32_t)(((int64_t)pg * a.num_kv_heads + it.h) * 32);
+        rt::mbar_arrive_expect_tx(bar, (uint32_t)kStageBytes);
+        rt::tma_load_2d(dst, &kv_map, 0, row_k, bar, policy);
+        rt::tma_load_2d(dst + 2048u, &kv_map, 64, row_k, bar, policy);
+        rt::tma_load_2d(dst + 4096u, &kv_map, 0, row_k + 16, bar, policy);
+        rt::tma_load_2d(dst + 6144u, &kv_map, 64, row_k + 16, bar, policy);
+    }
+}
+
+// The item's G query rows (bf16 pairs) into the warp's shared buffer: row r
+// at qs + r * kQRowWords.  Plain loads: the warp waits for them while the
+// pages already issued are in flight.
+template <int G>
+__device__ __forceinline__ void seq_copy_q(const AttnArgs &a, const SeqItem &it, uint32_t *qs)
+{
+    const int lane = threadIdx.x & 31;
+    const uint32_t *src = reinterpret_cast<const uint32_t *>(
+        a.q + ((size_t)it.b * a.num_q_heads + (size_t)it.h * G) * 128);
+    uint32_t v[2 * G];
 #pragma unroll
-    for (int n = 0; n < 8; n++)
-        o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
-    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+    for (int k = 0; k < 2 * G; k++)
+        v[k] = src[k * 32 + lane];
+#pragma unroll
+    for (int k = 0; k < 2 * G; k++) {
+        const int w = k * 32 + lane;  // word w of the G x 64-word block
+        qs[(w >> 6) * kQRowWords + (w & 63)] = v[k];
+    }
+}
+
+// The end of an item: the lane sums of the softmax denominators, the fold of
+// the group's prefix partials (chunk 0 of a grouped sequence), then either
+// the normalised output (one chunk) or this chunk's partial, merged by the
+// last chunk to arrive.
+template <int G>
+__device__ __forceinline__ void seq_finalize(const AttnArgs &a, const SeqItem &it, float (&o)[8][4],
+                                             float m0, float m1, float l0, float l1)
+{
+    const int lane = threadIdx.x & 31;
+    const int r = lane >> 2, q4 = lane & 3;
     const int hd0 = 2 * q4, hd1 = 2 * q4 + 1;
-
-    // ldmatrix row addresses (swizzled 16-byte chunk = chunk ^ row%8): lane
-    // l points at token 8*((l/8)>>1) + l%8 and the (l/8)&1 half of a 16-dim
-    // block, so the four 8x8 matrices are (tokens lo|hi) x (dims lo|hi).
-    const int mi = lane >> 3, rr = lane & 7;
-    const uint32_t t_row = (uint32_t)((((mi >> 1) << 3) + rr) * 128);
-
-    for (int i = 0; i < n_mine; i++) {
-        const int s = i % kStages;
-        const bool ok = rt::mbar_wait_bounded(rt::smem_u32(&bars[s]), (phases >> s) & 1u,
-                                              kWaitLimitNs);
-        if (!__all_sync(0xffffffffu, ok)) {
-            if (lane == 0)
-                flag_error(a.error, kErrTimeout);
-            // Give copies still in flight a bounded chance to land before the
-            // shared memory is released.
-            for (int s2 = 0; s2 < kStages; s2++)
-                (void)rt::mbar_wait_bounded(rt::smem_u32(&bars[s2]), (phases >> s2) & 1u,
-                                            kWaitLimitNs / 4);
-            return false;
-        }
-        phases ^= 1u << s;
-        const uint32_t st = stage0 + (uint32_t)(s * kStageBytes);
-        const int valid = min(16, L - (p_begin + i) * 16);
-        if (valid < 16) {
-            // Tail page: zero the V rows past the sequence end so that
-            // P = 0 never meets non-finite stale data.
-            uint8_t *vbase = base_ptr + (st - base_u32) + 4096;
-            for (int idx = lane; idx < (16 - valid) * 2 * 8; idx += 32) {
-                const int row = valid + idx / 16, halfc = idx % 16;
-                *reinterpret_cast<uint4 *>(vbase + (halfc >> 3) * 2048 + row * 128 +
-                                           (halfc & 7) * 16) = make_uint4(0, 0, 0, 0);
-            }
-            __syncwarp();
-        }
-
-        // S^T = K Q^T: 16 tokens x 8 heads, two accumulators (even / odd
-        // 16-dim steps) to halve the dependent mma chain.
-        float se[4] = {0.f, 0.f, 0.f, 0.f}, so[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int j = 0; j < 8; j++) {
-            const int c = ((j & 3) << 1) + (mi & 1);
-            const uint32_t addr = st + (uint32_t)((j >> 2) * 2048) + t_row + (uint32_t)((c ^ rr) << 4);
-            uint32_t k0, k1, k2, k3;
-            rt::ldsm_x4(addr, k0, k1, k2, k3);
-            const uint32_t ka[4] = {k0, k2, k1, k3};
-            if (j & 1)
-                rt::mma_bf16_16816(so, ka, qb[j][0], qb[j][1]);
-            else
-                rt::mma_bf16_16816(se, ka, qb[j][0], qb[j][1]);
-        }
-        // lane: tokens r (x0: head hd0, x1: head hd1) and r + 8 (x2, x3)
-        float x0 = (se[0] + so[0]) * a.scale_log2, x1 = (se[1] + so[1]) * a.scale_log2;
-        float x2 = (se[2] + so[2]) * a.scale_log2, x3 = (se[3] + so[3]) * a.scale_log2;
-        if (valid < 16) {
-            if (r >= valid) x0 = x1 = -INFINITY;
-            if (r + 8 >= valid) x2 = x3 = -INFINITY;
-        }
-        // max over the 16 tokens of each head: the 8 lanes of a column
-        float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
-#pragma unroll
-        for (int off = 4; off < 32; off <<= 1) {
-            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
-            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
-        }
-        const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
-        const float c0 = rt::fast_exp2(m0 - n0), c1 = rt::fast_exp2(m1 - n1);
-        const float p0 = rt::fast_exp2(x0 - n0), p1 = rt::fast_exp2(x1 - n1);
-        const float p2 = rt::fast_exp2(x2 - n0), p3 = rt::fast_exp2(x3 - n1);
-        l0 = l0 * c0 + (p0 + p2);
-        l1 = l1 * c1 + (p1 + p3);
-        m0 = n0;
-        m1 = n1;
-#pragma unroll
-        for (int dd = 0; dd < 8; dd++) {
-            o[dd][0] *= c0;
-            o[dd][2] *= c0;
-            o[dd][1] *= c1;
-            o[dd][3] *= c1;
-        }
-        // P^T as the B operand: transpose the two 8x8 (token x head) blocks;
-        // P in two bf16 terms (hi + lo) keeps ~16 mantissa bits.
-        uint32_t h01, l01, h23, l23;
-        rt::split_bf16x2(p0, p1, h01, l01);
-        rt::split_bf16x2(p2, p3, h23, l23);
-        const uint32_t bh0 = rt::movmatrix_trans(h01), bh1 = rt::movmatrix_trans(h23);
-        const uint32_t bl0 = rt::movmatrix_trans(l01), bl1 = rt::movmatrix_trans(l23);
-
-        // O^T += V^T P^T: 8 tiles of 16 dims; ldmatrix.trans of the V tile
-        // gives the (dims x tokens) A fragments directly.
-#pragma unroll
-        for (int dd = 0; dd < 8; dd++) {
-            const int c = ((dd & 3) << 1) + (mi & 1);
-            const uint32_t addr =
-                st + 4096u + (uint32_t)((dd >> 2) * 2048) + t_row + (uint32_t)((c ^ rr) << 4);
-            uint32_t v[4];
-            rt::ldsm_x4_trans(addr, v[0], v[1], v[2], v[3]);
-            rt::mma_bf16_16816(o[dd], v, bh0, bh1);
-            rt::mma_bf16_16816(o[dd], v, bl0, bl1);
-        }
-        __syncwarp();
-        if (i + kStages < n_mine) {
-            // The stage's shared memory was only read (ldmatrix, consumed by
-            // the mma above) unless this was a tail page whose V rows were
-            // zeroed: only generic writes need ordering before the TMA write.
-            if (valid < 16)
-                rt::fence_proxy_async_smem();
-            issue(i + kStages, s);
-        }
+    const uint32_t b = it.b, h = it.h, n_g = it.n_g, Hq = a.num_q_heads;
+    const int chunk = it.chunk, n_chunks = it.n_chunks;
+    const size_t bh = (size_t)b * a.num_kv_heads + h;
+    if (it.kind == kSeqZero) {
+        for (int i = lane; i < G * 128; i += 32)
+            a.out[((size_t)b * Hq + (size_t)h * G) * 128 + i] = 0.0f;
+        return;
     }
+    if (it.kind != kSeqWork)
+        return;
 #pragma unroll
     for (int off = 4; off < 32; off <<= 1) {
         l0 += __shfl_xor_sync(0xffffffffu, l0, off);
@@ -477,7 +435,7 @@ __device__ __forceinline__ bool process_item(const CUtensorMap &kv_map, const At
                 d1[16 * dd + 8] = o[dd][3] * i1;
             }
         }
-        return true;
+        return;
     }
 
     // ---- split-K: write this chunk's partial; the last part to arrive merges ----
@@ -510,12 +468,235 @@ __device__ __forceinline__ bool process_item(const CUtensorMap &kv_map, const At
         prev = atomicAdd(&a.counters[bh], 1);
     prev = __shfl_sync(0xffffffffu, prev, 0);
     if (prev != n_chunks - 1)
-        return true;
+        return;
     __threadfence();
     merge_parts<G>(a, bh, b, h, 0u, (uint32_t)n_chunks);
     if (lane == 0)
         a.counters[bh] = 0;
-    return true;
+    return;
+}
+
+// A warp's items, one after another, with the next item prefetched.  Its
+// number is claimed from the global dispenser when the current item starts
+// (one item ahead, so warps hold no more work than they can start); its
+// setup loads (length, group coverage, page ids) and query rows follow the
+// current item's first page, so they wait behind the pages in flight, and
+// its first pages go into ring stages as the current item frees them: an
+// item's first page is usually resident when it starts.  Returns when the
+// dispenser is empty or a pipeline wait expired (flagged).
+template <int G>
+__device__ __forceinline__ void run_seq_items(const CUtensorMap &kv_map, const AttnArgs &a,
+                                              const SeqPlan &pl, uint32_t stage0,
+                                              uint8_t *base_ptr, uint32_t base_u32,
+                                              uint64_t (&bars)[kStages], uint64_t policy,
+                                              uint32_t *qs)
+{
+    const int lane = threadIdx.x & 31;
+    const int r = lane >> 2, q4 = lane & 3;
+    const int hd0 = 2 * q4, hd1 = 2 * q4 + 1;
+    // ldmatrix row addresses (swizzled 16-byte chunk = chunk ^ row%8): lane
+    // l points at token 8*((l/8)>>1) + l%8 and the (l/8)&1 half of a 16-dim
+    // block, so the four 8x8 matrices are (tokens lo|hi) x (dims lo|hi).
+    const int mi = lane >> 3, rr = lane & 7;
+    const uint32_t t_row = (uint32_t)((((mi >> 1) << 3) + rr) * 128);
+    uint32_t phases = 0, issued = 0, used = 0;  // ring: per-stage parity, pages issued / consumed
+    unsigned long long grab = 0;
+    if (lane == 0)
+        grab = atomicAdd(a.work_next, 1ull);
+    uint64_t id = __shfl_sync(0xffffffffu, grab, 0);
+    SeqItem cur = seq_setup<G>(a, pl, id);
+    // An empty item (nothing to write) costs only its setup: when one is
+    // found, the number of the item after it is claimed at once, so the
+    // claim's round trip overlaps the work still ahead.  A real item is
+    // still claimed only when its predecessor starts.
+    bool claimed = false;
+    if (cur.kind == kSeqNone && id < pl.n_items) {
+        if (lane == 0)
+            grab = atomicAdd(a.work_next, 1ull);
+        claimed = true;
+    }
+    int cur_iss = 0;
+    // (the ring is idle: order the mbarrier set-up before the first TMA writes)
+    rt::fence_proxy_async_smem();
+    for (; cur_iss < cur.n_mine && cur_iss < kStages; cur_iss++)
+        seq_issue(kv_map, a, cur, cur_iss, issued++, stage0, bars, policy);
+    if (cur.n_mine > 0)
+        seq_copy_q<G>(a, cur, qs);
+    __syncwarp();
+    while (id < pl.n_items) {
+        if (lane == 0 && !claimed)
+            grab = atomicAdd(a.work_next, 1ull);  // the next item, in flight meanwhile
+        claimed = false;
+        // Q as the B operand (col-major 16 dims x 8 heads): lane holds head
+        // r, dims 16j + 2q4 (+1) and 16j + 8 + 2q4 (+1); heads >= G are zero.
+        uint32_t qb[8][2];
+        {
+            const uint32_t *qrow = qs + (r < G ? r : 0) * kQRowWords;
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                qb[j][0] = r < G ? qrow[8 * j + q4] : 0u;
+                qb[j][1] = r < G ? qrow[8 * j + 4 + q4] : 0u;
+            }
+        }
+        __syncwarp();
+        uint64_t id_n = pl.n_items;
+        SeqItem nxt{};
+        bool have_nxt = false;
+        int nxt_iss = 0;
+        // the next item's setup and query rows (qs is free: this item's
+        // fragment is in registers)
+        auto setup_next = [&]() {
+            id_n = __shfl_sync(0xffffffffu, grab, 0);
+            nxt = seq_setup<G>(a, pl, id_n);
+            if (nxt.n_mine > 0)
+                seq_copy_q<G>(a, nxt, qs);
+            if (nxt.kind == kSeqNone && id_n < pl.n_items) {
+                if (lane == 0)
+                    grab = atomicAdd(a.work_next, 1ull);
+                claimed = true;
+            }
+            have_nxt = true;
+        };
+        // Online-softmax state: lane owns heads 2q4, 2q4 + 1 and dims 16dd + r,
+        // 16dd + r + 8 of the O^T tiles.
+        float o[8][4];
+#pragma unroll
+        for (int n = 0; n < 8; n++)
+            o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+        float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+        for (int i = 0; i < cur.n_mine; i++) {
+            const int s = (int)(used % (uint32_t)kStages);
+            const bool ok = rt::mbar_wait_bounded(rt::smem_u32(&bars[s]), (phases >> s) & 1u,
+                                                  kWaitLimitNs);
+            if (!__all_sync(0xffffffffu, ok)) {
+                if (lane == 0)
+                    flag_error(a.error, kErrTimeout);
+                // give the copies still in flight a bounded chance to land
+                // before the shared memory is released
+                for (uint32_t k = used; k < issued; k++) {
+                    const uint32_t s2 = k % (uint32_t)kStages;
+                    (void)rt::mbar_wait_bounded(rt::smem_u32(&bars[s2]), (phases >> s2) & 1u,
+                                                kWaitLimitNs / 4);
+                    phases ^= 1u << s2;
+                }
+                return;
+            }
+            phases ^= 1u << s;
+            used++;
+        const uint32_t st = stage0 + (uint32_t)(s * kStageBytes);
+        const int valid = min(16, cur.L - (cur.p_begin + i) * 16);
+        if (valid < 16) {
+            // Tail page: zero the V rows past the sequence end so that
+            // P = 0 never meets non-finite stale data.
+            uint8_t *vbase = base_ptr + (st - base_u32) + 4096;
+            for (int idx = lane; idx < (16 - valid) * 2 * 8; idx += 32) {
+                const int row = valid + idx / 16, halfc = idx % 16;
+                *reinterpret_cast<uint4 *>(vbase + (halfc >> 3) * 2048 + row * 128 +
+                                           (halfc & 7) * 16) = make_uint4(0, 0, 0, 0);
+            }
+            __syncwarp();
+        }
+
+        // S^T = K Q^T: 16 tokens x 8 heads, two accumulators (even / odd
+        // 16-dim steps) to halve the dependent mma chain.
+        float se[4] = {0.f, 0.f, 0.f, 0.f}, so[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const int c = ((j & 3) << 1) + (mi & 1);
+            const uint32_t addr = st + (uint32_t)((j >> 2) * 2048) + t_row + (uint32_t)((c ^ rr) << 4);
+            uint32_t k0, k1, k2, k3;
+            rt::ldsm_x4(addr, k0, k1, k2, k3);
+            const uint32_t ka[4] = {k0, k2, k1, k3};
+            if (j & 1)
+                rt::mma_bf16_16816(so, ka, qb[j][0], qb[j][1]);
+            else
+                rt::mma_bf16_16816(se, ka, qb[j][0], qb[j][1]);
+        }
+        // lane: tokens r (x0: head hd0, x1: head hd1) and r + 8 (x2, x3)
+        float x0 = (se[0] + so[0]) * a.scale_log2, x1 = (se[1] + so[1]) * a.scale_log2;
+        float x2 = (se[2] + so[2]) * a.scale_log2, x3 = (se[3] + so[3]) * a.scale_log2;
+        if (valid < 16) {
+            if (r >= valid) x0 = x1 = -INFINITY;
+            if (r + 8 >= valid) x2 = x3 = -INFINITY;
+        }
+        // max over the 16 tokens of each head: the 8 lanes of a column
+        float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+        }
+        const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
+        const float c0 = rt::fast_exp2(m0 - n0), c1 = rt::fast_exp2(m1 - n1);
+        const float p0 = rt::fast_exp2(x0 - n0), p1 = rt::fast_exp2(x1 - n1);
+        const float p2 = rt::fast_exp2(x2 - n0), p3 = rt::fast_exp2(x3 - n1);
+        l0 = l0 * c0 + (p0 + p2);
+        l1 = l1 * c1 + (p1 + p3);
+        m0 = n0;
+        m1 = n1;
+#pragma unroll
+        for (int dd = 0; dd < 8; dd++) {
+            o[dd][0] *= c0;
+            o[dd][2] *= c0;
+            o[dd][1] *= c1;
+            o[dd][3] *= c1;
+        }
+        // P^T as the B operand: transpose the two 8x8 (token x head) blocks;
+        // P in two bf16 terms (hi + lo) keeps ~16 mantissa bits.
+        uint32_t h01, l01, h23, l23;
+        rt::split_bf16x2(p0, p1, h01, l01);
+        rt::split_bf16x2(p2, p3, h23, l23);
+        const uint32_t bh0 = rt::movmatrix_trans(h01), bh1 = rt::movmatrix_trans(h23);
+        const uint32_t bl0 = rt::movmatrix_trans(l01), bl1 = rt::movmatrix_trans(l23);
+
+        // O^T += V^T P^T: 8 tiles of 16 dims; ldmatrix.trans of the V tile
+        // gives the (dims x tokens) A fragments directly.
+#pragma unroll
+        for (int dd = 0; dd < 8; dd++) {
+            const int c = ((dd & 3) << 1) + (mi & 1);
+            const uint32_t addr =
+                st + 4096u + (uint32_t)((dd >> 2) * 2048) + t_row + (uint32_t)((c ^ rr) << 4);
+            uint32_t v[4];
+            rt::ldsm_x4_trans(addr, v[0], v[1], v[2], v[3]);
+            rt::mma_bf16_16816(o[dd], v, bh0, bh1);
+            rt::mma_bf16_16816(o[dd], v, bl0, bl1);
+        }
+        __syncwarp();
+            // Refill the stage: this item's next page, else the next item's.
+            // After the first page the next item is set up - behind the
+            // refill when this item still has pages to issue, so that its
+            // loads wait with the ring full.
+            const bool more = cur_iss < cur.n_mine;
+            if (!have_nxt && !more)
+                setup_next();
+            if (more || nxt_iss < nxt.n_mine) {
+                // The stage's shared memory was only read (ldmatrix, consumed
+                // by the mma above) unless this was a tail page whose V rows
+                // were zeroed: only generic writes need ordering before the
+                // TMA write.
+                if (valid < 16)
+                    rt::fence_proxy_async_smem();
+                if (more)
+                    seq_issue(kv_map, a, cur, cur_iss++, issued++, stage0, bars, policy);
+                else
+                    seq_issue(kv_map, a, nxt, nxt_iss++, issued++, stage0, bars, policy);
+            }
+            if (!have_nxt)
+                setup_next();
+        }
+        if (!have_nxt)
+            setup_next();
+        seq_finalize<G>(a, cur, o, m0, m1, l0, l1);
+        id = id_n;
+        cur = nxt;
+        cur_iss = nxt_iss;
+        // top the ring up with the new item's first pages (stages freed by
+        // tail pages may hold generic writes)
+        rt::fence_proxy_async_smem();
+        for (; cur_iss < cur.n_mine && issued - used < (uint32_t)kStages; cur_iss++)
+            seq_issue(kv_map, a, cur, cur_iss, issued++, stage0, bars, policy);
+        __syncwarp();
+    }
 }
 
 // One (group, row block, KV head, prefix chunk) item, processed by the whole
@@ -713,7 +894,7 @@ __device__ __forceinline__ bool process_group_item(const CUtensorMap &kv_map, co
                 o[n][2] *= cB;
                 o[n][3] *= cB;
             }
-            uint32_t pf[4], pl[4];  // P = hi + lo in bf16 (see process_item)
+            uint32_t pf[4], pl[4];  // P = hi + lo in bf16 (as in the sequence items)
             rt::split_bf16x2(pa0, pa1, pf[0], pl[0]);
             rt::split_bf16x2(pb0, pb1, pf[1], pl[1]);
             rt::split_bf16x2(pa2, pa3, pf[2], pl[2]);
@@ -872,18 +1053,11 @@ paged_gqa_decode_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnAr
     // may be scheduled once every CTA of this grid has started.
     rt::grid_dep_launch();
     const uint64_t policy = a.evict_first ? rt::l2_policy_evict_first() : rt::l2_policy_evict_normal();
-    uint32_t phases = 0;
-    unsigned long long grab = 0;
-    if (lane == 0)
-        grab = atomicAdd(a.work_next, 1ull);
-    uint64_t item = __shfl_sync(0xffffffffu, grab, 0);
-    while (item < a.n_items) {
-        if (lane == 0)
-            grab = atomicAdd(a.work_next, 1ull);  // next item, in flight meanwhile
-        if (!process_item<G>(kv_map, a, item, stage0, base_ptr, base_u32, bars[warp], phases, policy))
-            break;
-        item = __shfl_sync(0xffffffffu, grab, 0);
-    }
+    // this warp's query-row buffer, after the CTA's stage rings
+    uint32_t *qs = reinterpret_cast<uint32_t *>(base_ptr + kWarps * kStages * kStageBytes) +
+                   warp * G * kQRowWords;
+    const SeqPlan pl = seq_plan(a);
+    run_seq_items<G>(kv_map, a, pl, stage0, base_ptr, base_u32, bars[warp], policy, qs);
     if (lane == 0) {
         __threadfence();
         const unsigned int total = gridDim.x * kWarps;
@@ -1034,7 +1208,7 @@ int prepare_g()
     if (dev < 64 && done[dev])
         return RT_OK;
     e = cudaFuncSetAttribute(paged_gqa_decode_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kSmemBytes);
+                             seq_smem_bytes<G>());
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(paged_gqa_group_kernel<G>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, kGroupSmemBytes);
@@ -1062,7 +1236,7 @@ int launch_g(const CUtensorMap &map, const AttnArgs &args, dim3 grid, cudaStream
     if (rc != RT_OK)
         return rc;
     if (!args.groups) {
-        paged_gqa_decode_kernel<G><<<grid, kWarps * 32, kSmemBytes, s>>>(map, args);
+        paged_gqa_decode_kernel<G><<<grid, kWarps * 32, seq_smem_bytes<G>(), s>>>(map, args);
         cudaError_t e = cudaGetLastError();
         return e == cudaSuccess ? RT_OK : rt::cuda_fail(e, "attention: launch");
     }
@@ -1088,7 +1262,7 @@ int launch_g(const CUtensorMap &map, const AttnArgs &args, dim3 grid, cudaStream
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = dim3(kWarps * 32);
-    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.dynamicSmemBytes = seq_smem_bytes<G>();
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -1147,7 +1321,7 @@ int launch_attention(const rt_attn_params_t *p, const rt_attn_group_params_t *gp
                      const void *kv_arena, const int32_t *page_table, const int32_t *seq_lens,
                      const rt_attn_group_t *groups, const uint32_t *n_groups,
                      const uint32_t *skip_pages, float *out, void *workspace,
-                     size_t workspace_bytes, void *stream)
+                     size_t workspace_bytes, void *stream, const uint32_t *dyn_chunks = nullptr)
 {
     Plan pl;
     int rc = make_plan(p, &pl, gp);
@@ -1215,6 +1389,7 @@ int launch_attention(const rt_attn_params_t *p, const rt_attn_group_params_t *gp
     args.gchunk_pages = gp ? pl.gchunk_pages : 1u;
     args.max_gchunks = pl.max_gchunks;
     args.slots = pl.slots;
+    args.dyn_chunks = dyn_chunks;
     // Persistent grid: kCtasPerSm CTAs per SM (the shared-memory limit), never
     // more CTAs than there are items to hand out.
     uint64_t ctas = (args.n_items + kWarps - 1) / kWarps;
@@ -1263,6 +1438,29 @@ extern "C" int rt_paged_decode_attention_grouped(
     }
     return launch_attention(p, gp, q, kv_arena, page_table, seq_lens, groups, n_groups,
                             skip_pages, out, workspace, workspace_bytes, stream);
+}
+
+int rt::attn_launch(const rt_attn_params_t *p, const rt_attn_group_params_t *gp, const void *q,
+                    const void *kv_arena, const int32_t *page_table, const int32_t *seq_lens,
+                    const rt_attn_group_t *groups, const uint32_t *n_groups,
+                    const uint32_t *skip_pages, float *out, void *workspace,
+                    size_t workspace_bytes, const uint32_t *dyn_chunks, cudaStream_t stream)
+{
+    return launch_attention(p, gp, q, kv_arena, page_table, seq_lens, groups, n_groups,
+                            skip_pages, out, workspace, workspace_bytes, stream, dyn_chunks);
+}
+
+int rt::attn_item_shape(const rt_attn_params_t *p, const rt_attn_group_params_t *gp,
+                        uint32_t *chunk_pages, uint32_t *gchunk_pages, uint32_t *max_gchunks)
+{
+    Plan pl;
+    const int rc = make_plan(p, &pl, gp);
+    if (rc != RT_OK)
+        return rc;
+    *chunk_pages = pl.chunk_pages;
+    *gchunk_pages = gp ? pl.gchunk_pages : 1u;
+    *max_gchunks = pl.max_gchunks;
+    return RT_OK;
 }
 
 extern "C" int rt_attn_workspace_error(void *workspace, void *stream, int32_t *code)

@@ -75,6 +75,8 @@ struct SlotExt {
     uint64_t seed;
     uint32_t prefix;  // shared-prefix id + 1, 0 = none
     uint32_t shared;  // full prefix pages at the head of the page table (shared, read-only)
+    uint32_t skip;    // of those, the pages its attention group covers (0 outside a group)
+    uint32_t pad_;
 };
 
 // Device trace ring (rt_trace_*): append counter, capacity (power of two),
@@ -123,6 +125,10 @@ struct Dev {
     float *logits;        // [max_slots][vocab]
     float *cmax;          // [max_slots][cstride] 16-column maxima of the synthetic logits
     uint32_t cstride;
+    // attention items: this pass's largest per-slot chunk count (written by
+    // the schedule kernel) and the plan values it is computed from
+    uint32_t *attn_chunks;
+    uint32_t attn_cp, attn_gcp, attn_mg;
     uint32_t *pf_len, *pf_np, *pf_off;
     int32_t *pf_pages;
     // shared-prefix attention groups, rebuilt by every schedule pass
@@ -569,8 +575,10 @@ __device__ void build_groups(const Dev &d, SchedShared &sh, uint32_t key, uint32
             d.groups[gid].shared_pages = shared;
         }
     }
-    if (s < d.max_slots)
+    if (s < d.max_slots) {
         d.skip[s] = ok ? shared : 0u;
+        sh.ext[s].skip = ok ? shared : 0u;
+    }
     __syncthreads();
     if (s == 0)
         *d.n_groups = min(sh.n_fin, d.max_groups);
@@ -985,6 +993,7 @@ __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
 
     // 4. this pass's decode: every slot still active generates one token
     uint32_t act = 0;
+    int32_t my_len = 0;  // the slot's attention length this pass
     if (s < d.max_slots) {
         GpuRolloutSlot &rs = sh.slot[s];
         act = rs.active && !fin;
@@ -996,7 +1005,8 @@ __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
                 atomicCAS(&ctl->error, 0, RT_EDEVICE);
             }
             d.enable[s] = act;
-            d.seq_lens[s] = act ? (int32_t)(e.pos + 1u) : 0;
+            my_len = act ? (int32_t)(e.pos + 1u) : 0;
+            d.seq_lens[s] = my_len;
             if (act) {
                 e.decoding = 1u;
                 rt_sample_row_t r;
@@ -1022,6 +1032,27 @@ __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
         if (s == 0) {
             ctl->groups_ok = 1u;
             ctl->groups_act = n_act;
+        }
+    }
+    if (full && d.attn_chunks) {
+        // this pass's largest chunk count over the slots, for the attention
+        // launch (its items then stop there, at least chunk 0 of every slot)
+        uint32_t nch = 0;
+        if (s < d.max_slots && my_len > 0) {
+            const uint32_t skip = d.max_groups ? sh.ext[s].skip : 0u;
+            const rt::AttnSeqShape shp = rt::attn_seq_shape(my_len, skip, d.maxp * 16u, d.maxp,
+                                                            d.attn_gcp, d.attn_mg, d.attn_cp);
+            nch = (uint32_t)shp.n_chunks;
+        }
+        nch = __reduce_max_sync(0xffffffffu, nch);
+        if ((s & 31u) == 0u)
+            sh.wcount[s >> 5] = nch;
+        __syncthreads();
+        if (s == 0) {
+            uint32_t m = 1u;
+            for (uint32_t w = 0; w < kSched / 32u; w++)
+                m = max(m, sh.wcount[w]);
+            *d.attn_chunks = m;
         }
     }
 
@@ -1426,11 +1457,12 @@ int launch_decode_model(rt_rollout *e, cudaStream_t st, cudaEvent_t *ev)
     if (ev)
         cudaEventRecord(ev[1], st);
     rc = d.max_groups
-             ? rt_paged_decode_attention_grouped(&e->ap, &e->gp, d.q, d.arena, d.page_table,
-                                                 d.seq_lens, d.groups, d.n_groups, d.skip,
-                                                 d.attn_out, e->attn_ws, e->attn_ws_bytes, st)
-             : rt_paged_decode_attention(&e->ap, d.q, d.arena, d.page_table, d.seq_lens,
-                                         d.attn_out, e->attn_ws, e->attn_ws_bytes, st);
+             ? rt::attn_launch(&e->ap, &e->gp, d.q, d.arena, d.page_table, d.seq_lens, d.groups,
+                               d.n_groups, d.skip, d.attn_out, e->attn_ws, e->attn_ws_bytes,
+                               d.attn_chunks, st)
+             : rt::attn_launch(&e->ap, nullptr, d.q, d.arena, d.page_table, d.seq_lens, nullptr,
+                               nullptr, nullptr, d.attn_out, e->attn_ws, e->attn_ws_bytes,
+                               d.attn_chunks, st);
     if (rc != RT_OK)
         return rc;
     if (ev)
@@ -1471,11 +1503,12 @@ int launch_decode(rt_rollout *e, cudaStream_t st, cudaEvent_t *ev)
     if (ev)
         cudaEventRecord(ev[1], st);
     int rc = d.max_groups
-                 ? rt_paged_decode_attention_grouped(&e->ap, &e->gp, d.q, d.arena, d.page_table,
-                                                     d.seq_lens, d.groups, d.n_groups, d.skip,
-                                                     d.attn_out, e->attn_ws, e->attn_ws_bytes, st)
-                 : rt_paged_decode_attention(&e->ap, d.q, d.arena, d.page_table, d.seq_lens,
-                                             d.attn_out, e->attn_ws, e->attn_ws_bytes, st);
+                 ? rt::attn_launch(&e->ap, &e->gp, d.q, d.arena, d.page_table, d.seq_lens,
+                                   d.groups, d.n_groups, d.skip, d.attn_out, e->attn_ws,
+                                   e->attn_ws_bytes, d.attn_chunks, st)
+                 : rt::attn_launch(&e->ap, nullptr, d.q, d.arena, d.page_table, d.seq_lens,
+                                   nullptr, nullptr, nullptr, d.attn_out, e->attn_ws,
+                                   e->attn_ws_bytes, d.attn_chunks, st);
     if (rc != RT_OK)
         return rc;
     if (ev)
@@ -1568,7 +1601,7 @@ void engine_free(rt_rollout *e)
         cudaStreamDestroy(e->cap);
     void *bufs[] = {e->d.io, e->d.ctl, e->d.ext, e->d.page_table, e->d.priv, e->d.seq_lens,
                     e->d.enable, e->d.srows, e->d.tokens, e->d.q, e->d.attn_out, e->d.logits,
-                    e->d.cmax, e->d.pf_len, e->d.pf_np, e->d.pf_off, e->d.pf_pages, e->d.groups,
+                    e->d.cmax, e->d.attn_chunks, e->d.pf_len, e->d.pf_np, e->d.pf_off, e->d.pf_pages, e->d.groups,
                     e->d.n_groups, e->d.skip, e->attn_ws, e->d.hin, e->d.hout, e->d.qkv,
                     e->d.emb_tok, e->d.gemm_err, e->d.gemm_ws, e->pre_x, e->pre_kv};
     for (void *p : bufs)
@@ -1676,6 +1709,7 @@ extern "C" int rt_rollout_create(const rt_rollout_config_t *cfg, KVArena *arena,
             ok(dalloc(&d.n_groups, 1));
             ok(dalloc(&d.skip, S));
         }
+        ok(dalloc(&d.attn_chunks, 1));
     }
     if (err != cudaSuccess) {
         engine_free(e);
@@ -1731,7 +1765,9 @@ extern "C" int rt_rollout_create(const rt_rollout_config_t *cfg, KVArena *arena,
         e->gp.reserved = 0u;
         e->attn_ws_bytes = d.max_groups ? rt_attn_grouped_workspace_bytes(&e->ap, &e->gp)
                                         : rt_attn_workspace_bytes(&e->ap);
-        if (e->attn_ws_bytes == 0) {
+        if (e->attn_ws_bytes == 0 ||
+            rt::attn_item_shape(&e->ap, d.max_groups ? &e->gp : nullptr, &d.attn_cp, &d.attn_gcp,
+                                &d.attn_mg) != RT_OK) {
             engine_free(e);
             return RT_EINVAL;
         }

@@ -284,6 +284,38 @@ __device__ __forceinline__ float fast_exp2(float x)
     return y;
 }
 
+// How paged decode attention splits a sequence into items: its own pages
+// are those past the group-covered prefix (skip), in chunks of chunk_pages;
+// chunk 0 holds the remainder and every other chunk is full.  A fully
+// covered sequence still has chunk 0, which folds the group's partials into
+// the output.  An invalid length gives no pages and an invalid skip counts
+// as 0 (the attention kernel flags both).  The rollout loop's schedule
+// kernel evaluates the same function to publish each pass's largest chunk
+// count.
+struct AttnSeqShape {
+    int n_pages, skip, n_chunks;
+    uint32_t n_g;
+    bool bad_len, bad_skip;
+};
+__host__ __device__ __forceinline__ AttnSeqShape attn_seq_shape(int L, uint32_t skip_raw,
+                                                                uint32_t max_seq_len,
+                                                                uint32_t max_pages,
+                                                                uint32_t gchunk_pages,
+                                                                uint32_t max_gchunks,
+                                                                uint32_t chunk_pages)
+{
+    AttnSeqShape sh;
+    sh.bad_len = L < 0 || (uint32_t)L > max_seq_len || (uint32_t)L > max_pages * 16u;
+    sh.n_pages = sh.bad_len ? 0 : (L + 15) >> 4;
+    sh.bad_skip = skip_raw > (uint32_t)sh.n_pages || skip_raw > max_gchunks * gchunk_pages;
+    sh.skip = sh.bad_skip ? 0 : (int)skip_raw;
+    const int cp = (int)chunk_pages;
+    sh.n_g = (uint32_t)((sh.skip + (int)gchunk_pages - 1) / (int)gchunk_pages);
+    const int own = (sh.n_pages - sh.skip + cp - 1) / cp;
+    sh.n_chunks = sh.n_pages ? (own > 0 ? own : (sh.n_g ? 1 : 0)) : 0;
+    return sh;
+}
+
 // Maximum that is NaN when either operand is NaN (the chunk maxima a logits
 // producer hands to the sampler flag NaN this way).
 __device__ __forceinline__ float nan_max(float x, float y)

@@ -116,3 +116,20 @@ def test_c2_full_config(pkg, orc, cuda):
     assert attn.error_code() == 0
     err = check(orc, *case[:4], 32, 8, got)
     assert err < 1e-3
+
+
+@pytest.mark.parametrize("B", [512, 600])
+def test_many_sequences_both_item_numberings(pkg, orc, cuda, B):
+    """Up to 512 sequences the kernel builds a per-CTA item table (no empty
+    items); beyond it, items are numbered statically (chunk, sequence, head)
+    with empty items past each sequence's end.  Both must match the oracle,
+    with zero-length sequences and multi-chunk ones mixed in."""
+    rng = np.random.default_rng(B)
+    lens = rng.integers(0, 200, size=B).astype(np.int32)
+    lens[::7] = 0
+    lens[3::50] = 700          # several chunks at chunk_pages 8
+    case = make_case(pkg, cuda, lens, 8, 2, seed=B)
+    got, attn = run(pkg, cuda, *case[:4], 8, 2, case[4], case[5], chunk_pages=8)
+    assert attn.error_code() == 0
+    assert np.all(got[lens == 0] == 0.0)
+    check(orc, *case[:4], 8, 2, got)
