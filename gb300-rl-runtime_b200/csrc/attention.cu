@@ -204,25 +204,43 @@ struct SeqItem {
 };
 enum : uint32_t { kSeqNone = 0, kSeqZero = 1, kSeqWork = 2 };
 
-// The launch's items: (chunk from the highest index down, sequence, KV
-// head), so the full chunks go first and chunk 0 - the remainders, folds and
-// zero outputs, the short items - last, which keeps the tail short.  The
-// chunk count is the plan's (from max_seq_len) or, when the caller publishes
-// this launch's largest chunk count on the device (the rollout loop's
-// schedule kernel does), that count: chunks past a sequence's end are empty
-// items, and the published count leaves none when every sequence has the
-// same number of chunks.
+// The launch's items, long ones first and the short ones - chunk 0: the
+// remainders, folds and zero outputs - last, which keeps the tail short.
+// By default they are (chunk from the highest index down, sequence, KV head)
+// up to the plan's chunk count (from max_seq_len); chunks past a sequence's
+// end are empty items.  When the caller publishes this launch's items on the
+// device (the rollout loop's schedule kernel does: dyn_chunks[0] = the
+// largest chunk count, [1] = all full chunks, i.e. chunks >= 1, [2 + b] =
+// the full chunks of the sequences before b), there are no empty items:
+// with one chunk per sequence the count alone says so, otherwise each CTA
+// copies the prefix table to shared memory and hands out every full chunk,
+// sequence by sequence (a binary search finds its sequence), then chunk 0
+// of every sequence.
+constexpr uint32_t kPlanSeqs = 512;
 struct SeqPlan {
     uint32_t max_chunks;
     uint64_t n_items;
+    const uint32_t *pre;  // shared-memory prefix table, or nullptr
+    uint64_t n_full;      // full chunks (units of num_kv_heads items) in table order
 };
-__device__ __forceinline__ SeqPlan seq_plan(const AttnArgs &a)
+__device__ __forceinline__ SeqPlan seq_plan(const AttnArgs &a, uint32_t *s_pre)
 {
     SeqPlan pl;
     pl.max_chunks = a.max_chunks;
+    pl.pre = nullptr;
+    pl.n_full = 0;
     if (a.dyn_chunks) {
-        const uint32_t c = *a.dyn_chunks;
+        const uint32_t c = a.dyn_chunks[0];
         pl.max_chunks = c < 1u ? 1u : (c < a.max_chunks ? c : a.max_chunks);
+        if (pl.max_chunks > 1u && a.num_seqs <= kPlanSeqs) {
+            for (uint32_t b = threadIdx.x; b < a.num_seqs; b += blockDim.x)
+                s_pre[b] = a.dyn_chunks[2u + b];
+            pl.n_full = a.dyn_chunks[1];
+            pl.pre = s_pre;
+            __syncthreads();
+            pl.n_items = (pl.n_full + a.num_seqs) * a.num_kv_heads;
+            return pl;
+        }
     }
     pl.n_items = (uint64_t)a.num_seqs * a.num_kv_heads * pl.max_chunks;
     return pl;
@@ -247,13 +265,40 @@ __device__ __forceinline__ SeqItem seq_setup(const AttnArgs &a, const SeqPlan &p
     const uint32_t B = a.num_seqs, Hkv = a.num_kv_heads;
     it.h = (uint32_t)(item % Hkv);
     const uint64_t unit = item / Hkv;
-    it.b = (uint32_t)(unit % B);
-    it.chunk = (int)pl.max_chunks - 1 - (int)(unit / B);
+    int from_top = -1;  // table order: a full chunk's rank below its sequence's top chunk
+    if (pl.pre) {
+        if (unit < pl.n_full) {
+            uint32_t lo = 0, hi = B;  // the last b with pre[b] <= unit
+            while (hi - lo > 1u) {
+                const uint32_t mid = (lo + hi) >> 1;
+                if ((uint64_t)pl.pre[mid] <= unit)
+                    lo = mid;
+                else
+                    hi = mid;
+            }
+            it.b = lo;
+            from_top = (int)(unit - pl.pre[lo]);
+        } else {
+            it.b = (uint32_t)(unit - pl.n_full);
+            it.chunk = 0;
+        }
+    } else {
+        it.b = (uint32_t)(unit % B);
+        it.chunk = (int)pl.max_chunks - 1 - (int)(unit / B);
+    }
     const int L = a.seq_lens[it.b];
     const uint32_t skip_raw = a.skip_pages ? a.skip_pages[it.b] : 0u;
     it.L = L;
     const rt::AttnSeqShape sh = rt::attn_seq_shape(L, skip_raw, a.max_seq_len, a.max_pages,
                                                    a.gchunk_pages, a.max_gchunks, a.chunk_pages);
+    if (from_top >= 0) {
+        it.chunk = sh.n_chunks - 1 - from_top;
+        if (it.chunk < 1) {  // the table disagrees with the lengths
+            if (lane == 0)
+                flag_error(a.error, kErrSeqLen);
+            return it;
+        }
+    }
     if (sh.bad_len) {
         if (lane == 0 && it.chunk == 0)
             flag_error(a.error, kErrSeqLen);
@@ -1056,7 +1101,8 @@ paged_gqa_decode_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnAr
     // this warp's query-row buffer, after the CTA's stage rings
     uint32_t *qs = reinterpret_cast<uint32_t *>(base_ptr + kWarps * kStages * kStageBytes) +
                    warp * G * kQRowWords;
-    const SeqPlan pl = seq_plan(a);
+    __shared__ uint32_t s_pre[kPlanSeqs];
+    const SeqPlan pl = seq_plan(a, s_pre);
     run_seq_items<G>(kv_map, a, pl, stage0, base_ptr, base_u32, bars[warp], policy, qs);
     if (lane == 0) {
         __threadfence();

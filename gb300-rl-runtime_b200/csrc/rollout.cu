@@ -125,8 +125,9 @@ struct Dev {
     float *logits;        // [max_slots][vocab]
     float *cmax;          // [max_slots][cstride] 16-column maxima of the synthetic logits
     uint32_t cstride;
-    // attention items: this pass's largest per-slot chunk count (written by
-    // the schedule kernel) and the plan values it is computed from
+    // attention items, written by the schedule kernel: [0] this pass's
+    // largest per-slot chunk count, [1] the full chunks of all slots, [2 + s]
+    // the full chunks of the slots before s; and the plan values they come from
     uint32_t *attn_chunks;
     uint32_t attn_cp, attn_gcp, attn_mg;
     uint32_t *pf_len, *pf_np, *pf_off;
@@ -1035,8 +1036,10 @@ __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
         }
     }
     if (full && d.attn_chunks) {
-        // this pass's largest chunk count over the slots, for the attention
-        // launch (its items then stop there, at least chunk 0 of every slot)
+        // This pass's attention items (rt::attn_seq_shape of every slot), for
+        // the attention launch: the largest chunk count (at least 1: chunk 0
+        // of every slot) and the slots' full chunks (all but chunk 0) as an
+        // exclusive prefix over slots, so that it hands out no empty items.
         uint32_t nch = 0;
         if (s < d.max_slots && my_len > 0) {
             const uint32_t skip = d.max_groups ? sh.ext[s].skip : 0u;
@@ -1044,15 +1047,36 @@ __device__ bool schedule_pass(const Dev &d, SchedShared &sh)
                                                             d.attn_gcp, d.attn_mg, d.attn_cp);
             nch = (uint32_t)shp.n_chunks;
         }
-        nch = __reduce_max_sync(0xffffffffu, nch);
-        if ((s & 31u) == 0u)
-            sh.wcount[s >> 5] = nch;
+        const uint32_t lane = s & 31u, warp = s >> 5;
+        const uint32_t fulls = nch > 1u ? nch - 1u : 0u;
+        uint32_t incl = fulls;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= (uint32_t)o)
+                incl += y;
+        }
+        const uint32_t wmax = __reduce_max_sync(0xffffffffu, nch);
+        if (lane == 31u)
+            sh.wcount[warp] = incl;
         __syncthreads();
+        uint32_t before = 0, total = 0;
+        for (uint32_t w = 0; w < kSched / 32u; w++) {
+            before += w < warp ? sh.wcount[w] : 0u;
+            total += sh.wcount[w];
+        }
+        __syncthreads();
+        if (lane == 0u)
+            sh.wcount[warp] = wmax;
+        __syncthreads();
+        uint32_t m = 1u;
+        for (uint32_t w = 0; w < kSched / 32u; w++)
+            m = max(m, sh.wcount[w]);
+        if (s < d.max_slots)
+            d.attn_chunks[2u + s] = before + incl - fulls;
         if (s == 0) {
-            uint32_t m = 1u;
-            for (uint32_t w = 0; w < kSched / 32u; w++)
-                m = max(m, sh.wcount[w]);
-            *d.attn_chunks = m;
+            d.attn_chunks[0] = m;
+            d.attn_chunks[1] = total;
         }
     }
 
@@ -1709,7 +1733,7 @@ extern "C" int rt_rollout_create(const rt_rollout_config_t *cfg, KVArena *arena,
             ok(dalloc(&d.n_groups, 1));
             ok(dalloc(&d.skip, S));
         }
-        ok(dalloc(&d.attn_chunks, 1));
+        ok(dalloc(&d.attn_chunks, 2u + S));
     }
     if (err != cudaSuccess) {
         engine_free(e);
@@ -1757,7 +1781,14 @@ extern "C" int rt_rollout_create(const rt_rollout_config_t *cfg, KVArena *arena,
         e->ap.max_seq_len = d.maxp * 16u;
         e->ap.arena_pages = arena_pages;
         e->ap.scale = 0.08838834764831845f;  // 1/sqrt(128)
-        e->ap.chunk_pages = cfg->chunk_pages;
+        // Auto: with contexts beyond 64 pages, 16-page items.  A slot whose
+        // GRPO group has no other active member attends its whole context
+        // alone, and short items keep such slots off the pass's tail; the
+        // schedule kernel's item table means the extra chunks of the other
+        // slots cost nothing (configuration 4: 1.33 against 1.26 M tokens/s
+        // with the plan's 48-page items).  Shorter contexts take the plan's
+        // own rule.
+        e->ap.chunk_pages = cfg->chunk_pages ? cfg->chunk_pages : (d.maxp > 64u ? 16u : 0u);
         e->ap.kv_evict_first = 0u;  // group members re-read shared prefix pages
         e->gp.max_groups = d.max_groups;
         e->gp.max_shared_pages = d.maxp;

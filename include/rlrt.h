@@ -304,7 +304,9 @@ typedef struct {
     uint32_t max_prefix_pages;  /* total pages over all registered prefixes */
     uint64_t max_passes;        /* stop with RT_ETIMEOUT after this many passes */
     uint32_t idle_timeout_ms;   /* ring source: stop with RT_ETIMEOUT when idle this long */
-    uint32_t chunk_pages;       /* attention split-K chunk (0 = auto) */
+    uint32_t chunk_pages;       /* attention split-K chunk (0 = auto: 16 pages when
+                                   max_context exceeds 64 pages, else the attention
+                                   plan's rule) */
     uint32_t prefix_attention;  /* RT_PREFIX_ATTN_*: how slots sharing a prefix attend */
 } rt_rollout_config_t;
 
