@@ -1378,12 +1378,18 @@ def config1_cpu_path(reps=5):
         return {"unavailable": f"reference build absent: {e}"}
     mine = orc.Harness("mine")
     descs = mine.gen_c1(10000, seed=0, max_tokens=2048)
-    r = [ref.run_c1(descs, depth_cap=1024) for _ in range(reps)]
-    m = [mine.run_c1(descs, depth_cap=1024) for _ in range(reps)]
+    # the two implementations alternate, so that drift of the host's clocks
+    # during the measurement falls on both alike; medians over the runs
+    r, m = [], []
+    for _ in range(reps):
+        r.append(ref.run_c1(descs, depth_cap=1024))
+        m.append(mine.run_c1(descs, depth_cap=1024))
     rs, ms = statistics.median(x[3] for x in r), statistics.median(x[3] for x in m)
     d, _, _ = _decode_ring_inputs(0)
-    rb = [ref.run_decode_batch(d, 32) for _ in range(4 * reps)]
-    mb = [mine.run_decode_batch(d, 32) for _ in range(4 * reps)]
+    rb, mb = [], []
+    for _ in range(8 * reps):
+        rb.append(ref.run_decode_batch(d, 32))
+        mb.append(mine.run_decode_batch(d, 32))
     rbs, mbs = statistics.median(x[1] for x in rb), statistics.median(x[1] for x in mb)
     return {"workload": "BASELINE config 1: 10,000 hw_desc_t, seed 0, depth 1,024",
             "kind": "reference", "cores": 2,
@@ -1391,13 +1397,13 @@ def config1_cpu_path(reps=5):
             "mine_descs_per_s": len(descs) / ms, "mine_tokens_per_s": m[0][1] / ms,
             "completion_stream_equal": bool(np.array_equal(r[0][0].view(np.uint8),
                                                            m[0][0].view(np.uint8))),
-            "reps": reps,
+            "reps": reps, "order": "alternating",
             "decode_batch": {
                 "workload": "10,000 src/main.c step descriptors, decode_batch_submit windows of 32, "
                             "CommandRing 4,096 slots, consumer thread",
                 "reference_descs_per_s": len(d) / rbs, "mine_descs_per_s": len(d) / mbs,
                 "command_ring_stream_equal": bool(rb[0][0].tobytes() == mb[0][0].tobytes()),
-                "reps": 4 * reps}}
+                "reps": 8 * reps, "order": "alternating"}}
 
 
 def roofline_block(wl, achieved_gbs, ms, peaks, src, traffic, traffic_commit=None):
