@@ -267,6 +267,8 @@ _SIGS = {
     "rt_gemm_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(rt_gemm_params_t)]),
     "rt_gemm_bf16": (ctypes.c_int, [ctypes.POINTER(rt_gemm_params_t), _P, _P, _P, _P,
                                     ctypes.c_size_t, _P, _P]),
+    "rt_gemm_bf16_chunk_max": (ctypes.c_int, [ctypes.POINTER(rt_gemm_params_t), _P, _P, _P, _P,
+                                              ctypes.c_size_t, _P, _P, ctypes.c_uint32, _P]),
     "ring_create": (_P, []), "ring_destroy": (None, [_P]),
     "comp_ring_create": (_P, []), "comp_ring_destroy": (None, [_P]),
     "req_ring_create": (_P, []), "req_ring_destroy": (None, [_P]),

@@ -100,8 +100,14 @@ struct AttnArgs {
 // kernel (a programmatic dependent) overlaps it, and 3 CTAs per SM, whose
 // idle CTAs exit at once and free their SMs, gave the shorter pass
 // (attention 60.3 against 64.0 us per pass, same box).
-constexpr int kGroupStages = kWarps * kStages;  // the CTA's whole ring, shared by its warps
-constexpr int kGroupCtasPerSm = kCtasPerSm;
+#ifndef RT_ATTN_GROUP_STAGES
+#define RT_ATTN_GROUP_STAGES (kWarps * kStages)
+#endif
+#ifndef RT_ATTN_GROUP_CTAS_PER_SM
+#define RT_ATTN_GROUP_CTAS_PER_SM kCtasPerSm
+#endif
+constexpr int kGroupStages = RT_ATTN_GROUP_STAGES;  // the CTA's whole ring, shared by its warps
+constexpr int kGroupCtasPerSm = RT_ATTN_GROUP_CTAS_PER_SM;
 constexpr int kGroupSmemBytes = kGroupStages * kStageBytes + 1024;
 constexpr uint32_t kMaxGroupMembers = 16;
 

@@ -76,7 +76,48 @@ struct GemmArgs {
     uint32_t accumulate;  // 1: add into C (K-splits always add)
     uint32_t vec_ok;      // the output rows allow 16-byte stores
     int32_t *error;
+    float *cmax;          // each row's 16-column maxima (written with the final C), or nullptr
+    uint32_t cstride;
 };
+
+// The 16-column maxima of the 32 columns n .. n+31 of row m that a thread
+// holds (n a multiple of 16): NaN if a column is NaN, columns past N left out.
+__device__ __forceinline__ void store_chunk_max(const GemmArgs &g, uint32_t m, uint32_t n,
+                                                const uint32_t (&r)[32])
+{
+    if (m >= g.M)
+        return;
+    if (n + 32u <= g.N) {
+        // a full slab: two 16-wide trees, no column checks
+        float t[16];
+#pragma unroll
+        for (uint32_t half = 0; half < 2u; half++) {
+#pragma unroll
+            for (uint32_t j = 0; j < 8u; j++)
+                t[j] = rt::nan_max(__uint_as_float(r[16u * half + 2u * j]),
+                                   __uint_as_float(r[16u * half + 2u * j + 1u]));
+#pragma unroll
+            for (uint32_t w = 4u; w >= 1u; w >>= 1)
+#pragma unroll
+                for (uint32_t j = 0; j < w; j++)
+                    t[j] = rt::nan_max(t[2u * j], t[2u * j + 1u]);
+            g.cmax[(size_t)m * g.cstride + n / 16u + half] = t[0];
+        }
+        return;
+    }
+#pragma unroll
+    for (uint32_t half = 0; half < 2u; half++) {
+        const uint32_t n0 = n + 16u * half;
+        if (n0 >= g.N)
+            break;
+        float mx = -INFINITY;
+#pragma unroll
+        for (uint32_t j = 0; j < 16u; j++)
+            if (n0 + j < g.N)
+                mx = rt::nan_max(mx, __uint_as_float(r[16u * half + j]));
+        g.cmax[(size_t)m * g.cstride + n0 / 16u] = mx;
+    }
+}
 
 struct Shared {
     uint64_t full[kStages], empty[kStages];
@@ -313,6 +354,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         // the buffer is reused by the next slab
                         asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
                     }
+                    // the chunk maxima from registers while the store drains
+                    if (g.cmax)
+                        store_chunk_max(g, m, n0 + c, r);
                     epilogue_sync();
                 }
             } else
@@ -321,6 +365,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint32_t r[32];
                 rt::tmem_ld32(tmem + half * kAccCols + ((quarter * 32u) << 16) + c, r);
                 rt::tmem_ld_wait();
+                if (g.cmax)
+                    store_chunk_max(g, m, n0 + c, r);
                 if (m < g.M) {
                     const uint32_t n = n0 + c;
                     if (n + 32u <= g.N && g.vec_ok) {
@@ -458,8 +504,9 @@ extern "C" size_t rt_gemm_workspace_bytes(const rt_gemm_params_t *p)
     return splits > 1u ? (size_t)splits * m_pad * p->N * sizeof(float) : 0u;
 }
 
-extern "C" int rt_gemm_bf16(const rt_gemm_params_t *p, const void *A, const void *B, float *C,
-                            void *workspace, size_t workspace_bytes, int32_t *error, void *stream)
+static int gemm_launch(const rt_gemm_params_t *p, const void *A, const void *B, float *C,
+                       void *workspace, size_t workspace_bytes, int32_t *error, float *cmax,
+                       uint32_t cmax_stride, void *stream)
 {
     if (!p || !A || !B || !C || !error) {
         rt::set_error("gemm_bf16: null argument");
@@ -505,6 +552,11 @@ extern "C" int rt_gemm_bf16(const rt_gemm_params_t *p, const void *A, const void
     g.units = g.m_tiles * g.n_tiles * g.splits;
     g.accumulate = p->flags & RT_GEMM_ACCUMULATE;
     g.error = error;
+    // chunk maxima: from the epilogue when it writes the final C, else by a
+    // pass over C afterwards
+    const bool cmax_fused = cmax && g.splits == 1u && !g.accumulate;
+    g.cmax = cmax_fused ? cmax : nullptr;
+    g.cstride = cmax_stride;
     g.vec_ok = g.splits > 1u ? (p->N % 4u) == 0u
                              : ((uintptr_t)C % 16u) == 0u && (p->ldc % 4u) == 0u;
     // TMA stores need 16-byte aligned rows; otherwise plain stores
@@ -541,5 +593,28 @@ extern "C" int rt_gemm_bf16(const rt_gemm_params_t *p, const void *A, const void
         if (err != cudaSuccess)
             return rt::cuda_fail(err, "gemm_bf16: split reduction launch");
     }
+    if (cmax && !cmax_fused)
+        return rt_logits_chunk_max(C, p->M, p->N, p->ldc, cmax, cmax_stride, stream);
     return RT_OK;
+}
+
+extern "C" int rt_gemm_bf16(const rt_gemm_params_t *p, const void *A, const void *B, float *C,
+                            void *workspace, size_t workspace_bytes, int32_t *error, void *stream)
+{
+    return gemm_launch(p, A, B, C, workspace, workspace_bytes, error, nullptr, 0u, stream);
+}
+
+extern "C" int rt_gemm_bf16_chunk_max(const rt_gemm_params_t *p, const void *A, const void *B,
+                                      float *C, void *workspace, size_t workspace_bytes,
+                                      int32_t *error, float *chunk_max, uint32_t cmax_stride,
+                                      void *stream)
+{
+    if (!chunk_max || ((uintptr_t)chunk_max & 3u) || !p ||
+        cmax_stride < rt_chunk_max_stride(p->N)) {
+        rt::set_error("gemm_bf16_chunk_max: chunk_max must be 4-byte aligned with a stride "
+                      ">= rt_chunk_max_stride(N)");
+        return RT_EINVAL;
+    }
+    return gemm_launch(p, A, B, C, workspace, workspace_bytes, error, chunk_max, cmax_stride,
+                       stream);
 }

@@ -1495,7 +1495,9 @@ int launch_decode_model(rt_rollout *e, cudaStream_t st, cudaEvent_t *ev)
     if (err != cudaSuccess)
         return rt::cuda_fail(err, "rollout: hidden launch");
     rt_gemm_params_t gl = {d.max_slots, d.vocab, d.dm, d.dm, d.dm, d.vocab, d.split_lm, 0u};
-    rc = rt_gemm_bf16(&gl, d.hout, d.w_lm, d.logits, d.gemm_ws, d.gemm_ws_bytes, d.gemm_err, st);
+    // the LM head's epilogue also writes each row's 16-column maxima for the sampler
+    rc = rt_gemm_bf16_chunk_max(&gl, d.hout, d.w_lm, d.logits, d.gemm_ws, d.gemm_ws_bytes,
+                                d.gemm_err, d.cmax, d.cstride, st);
     if (rc != RT_OK)
         return rc;
     if (ev)
@@ -1506,7 +1508,7 @@ int launch_decode_model(rt_rollout *e, cudaStream_t st, cudaEvent_t *ev)
     sp.row_stride = d.vocab;
     sp.fused_cum = 1u;
     sp.row_enable = d.enable;
-    rc = rt::sample_rows_launch(&sp, d.logits, d.srows, d.tokens, st, true);
+    rc = rt::sample_rows_launch(&sp, d.logits, d.srows, d.tokens, st, true, d.cmax, d.cstride);
     if (ev)
         cudaEventRecord(ev[4], st);
     return rc;

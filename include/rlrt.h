@@ -622,6 +622,16 @@ size_t rt_gemm_workspace_bytes(const rt_gemm_params_t *p);  /* 0 without K-split
 int rt_gemm_bf16(const rt_gemm_params_t *p, const void *A, const void *B, float *C,
                  void *workspace, size_t workspace_bytes, int32_t *error, void *stream);
 
+/* rt_gemm_bf16 that also writes C's 16-column maxima in the layout of
+ * rt_logits_chunk_max (chunk_max fp32 [M][cmax_stride], cmax_stride >=
+ * rt_chunk_max_stride(N)), for rt_sample_rows_cmax on an LM head's logits.
+ * Without K-splits or accumulation the epilogue writes them from the
+ * accumulators it already holds; otherwise they are computed from C
+ * afterwards. */
+int rt_gemm_bf16_chunk_max(const rt_gemm_params_t *p, const void *A, const void *B, float *C,
+                           void *workspace, size_t workspace_bytes, int32_t *error,
+                           float *chunk_max, uint32_t cmax_stride, void *stream);
+
 /* ------------------------------------------------------------------------
  * Rewards and group-normalised advantages (new; the reference has only the
  * mock scorer, cu/reward.cu:4-15, never launched).

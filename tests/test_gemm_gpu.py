@@ -102,3 +102,69 @@ def test_gemm_split_k_is_deterministic(pkg, cuda):
     for _ in range(3):
         assert torch.equal(gemm(pkg, A, B, split_k=14), first)
     check(first, A, B)
+
+
+def gemm_cmax(pkg, A, B, split_k=0, accumulate=False, ldc=None, base=None):
+    """rt_gemm_bf16_chunk_max; returns (C, chunk maxima)."""
+    M, K = A.shape
+    N = B.shape[0]
+    C = torch.full((M, ldc or N), float("nan"), dtype=torch.float32, device=A.device)
+    if base is not None:
+        C[:, :N] = base
+    cs = pkg.chunk_max_stride(N)
+    cm = torch.full((M, cs), -7.0, dtype=torch.float32, device=A.device)
+    p = pkg.rt_gemm_params_t(M, N, K, A.stride(0), B.stride(0), C.stride(0), split_k,
+                             1 if accumulate else 0)
+    err = torch.zeros(1, dtype=torch.int32, device=A.device)
+    wsb = pkg.lib().rt_gemm_workspace_bytes(ctypes.byref(p))
+    ws = torch.full((max(wsb, 4) // 4,), float("nan"), device=A.device) if wsb else None
+    pkg.check(pkg.lib().rt_gemm_bf16_chunk_max(ctypes.byref(p), pkg._ptr(A), pkg._ptr(B),
+                                               pkg._ptr(C), pkg._ptr(ws), wsb, pkg._ptr(err),
+                                               pkg._ptr(cm), cs, pkg._stream_ptr(None)),
+              "rt_gemm_bf16_chunk_max")
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    return C, cm
+
+
+def chunk_max_of(C, N):
+    x = C[:, :N].double().cpu().numpy()
+    M = x.shape[0]
+    nch = (N + 15) // 16
+    pad = np.full((M, nch * 16), -np.inf)
+    pad[:, :N] = x
+    c = pad.reshape(M, nch, 16)
+    m = c.max(axis=2)
+    m[np.isnan(c).any(axis=2)] = np.nan
+    return m
+
+
+@pytest.mark.parametrize("M,N,K,split,acc,ldc", [
+    (256, 32000 // 8, 256, 0, False, None),   # epilogue path, TMA stores
+    (130, 300, 128, 0, False, 301),           # epilogue path, plain stores, N % 16 != 0
+    (64, 1000, 512, 4, False, None),          # K-splits: maxima from C afterwards
+    (64, 448, 128, 0, True, None),            # accumulate: maxima from C afterwards
+])
+def test_gemm_chunk_max(pkg, cuda, M, N, K, split, acc, ldc):
+    """The LM head's maxima for the sampler equal the maxima of the C it
+    wrote, whichever path produced them."""
+    A, B = rand((M, K), 1, cuda), rand((N, K), 2, cuda)
+    base = rand((M, N), 3, cuda).float() if acc else None
+    C, cm = gemm_cmax(pkg, A, B, split_k=split, accumulate=acc, ldc=ldc, base=base)
+    check(C[:, :N], A, B, base)
+    want = chunk_max_of(C, N)
+    got = cm[:, : want.shape[1]].double().cpu().numpy()
+    assert np.array_equal(got, want)
+
+
+def test_gemm_chunk_max_propagates_nan(pkg, cuda):
+    M, N, K = 32, 224, 64
+    A, B = rand((M, K), 4, cuda), rand((N, K), 5, cuda)
+    A[3, 7] = float("nan")                    # row 3 of C is all NaN
+    B[40, 0] = float("inf")                   # column 40 is +-inf or NaN
+    C, cm = gemm_cmax(pkg, A, B)
+    want = chunk_max_of(C, N)
+    got = cm[:, : want.shape[1]].double().cpu().numpy()
+    assert np.array_equal(np.isnan(got), np.isnan(want))
+    assert np.array_equal(got[~np.isnan(got)], want[~np.isnan(want)])
+    assert np.isnan(got[3]).all()
