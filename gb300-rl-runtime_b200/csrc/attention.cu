@@ -1041,12 +1041,20 @@ paged_gqa_group_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnArg
     const uint32_t n_live = min(*a.n_groups, a.max_groups);
     const uint64_t n_gi = (uint64_t)n_live * RB * a.num_kv_heads * a.max_gchunks;
     uint32_t gphases = 0;
+    // The first item is the CTA's own index (no dispenser round trip before
+    // its first page); further items come from the dispenser, counted from
+    // gridDim.x.
+    bool first = true;
     while (n_gi) {
-        if (threadIdx.x == 0)
-            s_gitem = atomicAdd(a.group_next, 1ull);
-        __syncthreads();
-        const uint64_t gi = s_gitem;
-        __syncthreads();
+        uint64_t gi = blockIdx.x;
+        if (!first) {
+            if (threadIdx.x == 0)
+                s_gitem = gridDim.x + atomicAdd(a.group_next, 1ull);
+            __syncthreads();
+            gi = s_gitem;
+            __syncthreads();
+        }
+        first = false;
         if (gi >= n_gi)
             break;
         // A false return means a wait expired (flagged): stop taking items,
