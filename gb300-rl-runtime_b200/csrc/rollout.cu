@@ -40,7 +40,10 @@ namespace {
 
 constexpr int kSched = 256;  // schedule CTA: one thread per slot (GPU_MAX_ROLLOUTS)
 constexpr uint64_t kDonePushLimitNs = 10000000000ull;  // 10 s bounded wait on a full done ring
-constexpr int kPassesPerIteration = 4;  // passes captured in one graph-loop body
+#ifndef RT_PASSES_PER_ITERATION
+#define RT_PASSES_PER_ITERATION 16
+#endif
+constexpr int kPassesPerIteration = RT_PASSES_PER_ITERATION;  // passes captured in one graph-loop body
 
 struct RtIo {
     RequestRing *ring;
