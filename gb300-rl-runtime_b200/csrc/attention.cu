@@ -825,7 +825,10 @@ __device__ __forceinline__ bool process_group_item(const CUtensorMap &kv_map, co
     };
     // When the chunk is longer than the ring, stages are refilled while the
     // item runs, by whichever warp finishes a stage last (below), so the page
-    // ids go to shared memory where every warp can read them.
+    // ids go to shared memory where every warp can read them.  No barrier
+    // follows: the other warps load their query rows meanwhile, and a refill
+    // reads s_pg only after warp 0 has counted itself done with that stage
+    // (its writes here come first in its program order).
     const bool refill = np > kGroupStages;
     if (warp == 0) {
         if (refill) {
@@ -838,8 +841,6 @@ __device__ __forceinline__ bool process_group_item(const CUtensorMap &kv_map, co
                 issue_page(i, pg);
         }
     }
-    if (refill)
-        __syncthreads();  // s_pg is complete
 
     // A member takes part when the group covers exactly its skipped pages.
     auto member_ok = [&](int m) -> bool {
@@ -971,6 +972,7 @@ __device__ __forceinline__ bool process_group_item(const CUtensorMap &kv_map, co
             if (lane == 0) {
                 __threadfence_block();
                 if (atomicAdd(&s_cnt[s], 1u) == (uint32_t)kWarps - 1u) {
+                    __threadfence_block();  // every warp's count, warp 0's s_pg, then the read
                     s_cnt[s] = 0u;
                     if (i + kGroupStages < np)
                         issue_page(i + kGroupStages, s_pg[i + kGroupStages]);
