@@ -281,3 +281,51 @@ def test_loop_attention_matches_oracle(pkg, orc, cuda, mode):
     if mode == "grouped":
         assert checked[0] == 2 + 1 + 1  # 20 -> 16 + 4; 17 -> 16 + a lone (ungrouped) one; 3
     eng.close()
+
+
+@pytest.mark.parametrize("vocab", [2048, 2001])
+def test_loop_logits_equal_synth(pkg, orc, cuda, vocab):
+    """Pass by pass (host-stepped), every decoded slot's logits row is, bit for
+    bit, rt_logits_synth's row for that slot's (seed, request low 32, token
+    index), so the token replays above sample the loop's own logits.  Vocab
+    2001 leaves rows unaligned and a partial last group; seeds above 2^32
+    reach both key words."""
+    S = 64
+    cfg = full_cfg(max_slots=S, vocab=vocab)
+    arena = pkg.DeviceArena(1024)
+    eng = pkg.RolloutEngine(cfg, arena)
+    setup_prefixes(pkg, arena, eng, [40, 64])
+    n = 48
+    pfx = np.array([1] * 16 + [2] * 16 + [0] * 16)
+    reqs = make_requests(orc, n, np.random.default_rng(8).integers(4, 25, size=n),
+                         seed=0x9E3779B97F4A7C15, prefix_plus_one=pfx)
+    reqs["rng_seed"] = np.random.default_rng(9).integers(0, 2 ** 63, size=n, dtype=np.int64)
+    req_d = torch.from_numpy(reqs.view(np.uint8).copy()).to(cuda)
+    state = torch.zeros(STATE_BYTES, dtype=torch.uint8, device=cuda)
+    row_dt = np.dtype([("temperature", "<f4"), ("top_k", "<u4"), ("top_p", "<f4"),
+                       ("rollout_id", "<u4"), ("step", "<u8"), ("seed", "<u8")])
+    assert row_dt.itemsize == pkg.SAMPLE_ROW_BYTES
+    checked = []
+
+    def hook(p):
+        if p in (0, 1, 5, 11):
+            b = eng.buffers()
+            en = _dev(b.enable, (S,), "<u4", cuda).cpu().numpy()
+            rows = _dev(b.sample_rows, (S * row_dt.itemsize,), "|u1", cuda).cpu().numpy()
+            rows = rows.view(row_dt)
+            lg = _dev(b.logits, (S * vocab,), "<i4", cuda).clone().view(S, vocab)
+            ref = torch.empty(vocab, dtype=torch.float32, device=cuda)
+            live = np.flatnonzero(en)
+            assert len(live)
+            for s in live:
+                r = rows[s]
+                pkg.logits_synth(ref, vocab, int(r["seed"]), int(r["rollout_id"]), int(r["step"]),
+                                 2.0)
+                diff = torch.nonzero(lg[s] != ref.view(torch.int32))
+                assert diff.numel() == 0, f"pass {p} slot {s}: {diff.numel()} logits differ"
+            checked.append(len(live))
+        return p >= 11
+
+    eng.step(hook, requests=req_d, n_requests=n, state=state)
+    assert len(checked) == 4 and min(checked) > 0
+    eng.close()
