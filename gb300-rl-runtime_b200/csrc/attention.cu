@@ -793,6 +793,40 @@ __device__ __forceinline__ bool process_group_item(const CUtensorMap &kv_map, co
     }
     const int np = min(P, p0 + cpg) - p0;
 
+    // Every load of the prologue is one round trip behind the record: this
+    // warp's query rows (from the record's member indices, clamped into
+    // range and zeroed below if the member fails its checks), the members'
+    // lengths and skips, and the chunk's page ids all go out together,
+    // before the TMA issue (an asm statement the compiler does not move
+    // loads across).
+    // Rows of this warp: row r -> member (rb*kWarps + warp)*MPW + r/G, head r%G.
+    const int wm0 = (rb * kWarps + warp) * MPW;
+    const int rA = lane >> 2, rB = rA + 8, q4 = lane & 3;
+    const int mA = wm0 + rA / G, mB = wm0 + rB / G;
+    uint32_t bA = mA < (int)n_mem ? grp.members[mA] : a.num_seqs;
+    uint32_t bB = mB < (int)n_mem ? grp.members[mB] : a.num_seqs;
+    const bool inA = bA < a.num_seqs, inB = bB < a.num_seqs;
+    if (!inA)
+        bA = 0u;
+    if (!inB)
+        bB = 0u;
+    const int LA = a.seq_lens[bA], LB = a.seq_lens[bB];
+    const uint32_t kA = a.skip_pages[bA], kB = a.skip_pages[bB];
+    uint32_t qf[8][4];
+    {
+        const uint32_t *qa = reinterpret_cast<const uint32_t *>(
+            a.q + ((size_t)bA * Hq + (size_t)h * G + rA % G) * 128);
+        const uint32_t *qb = reinterpret_cast<const uint32_t *>(
+            a.q + ((size_t)bB * Hq + (size_t)h * G + rB % G) * 128);
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            qf[j][0] = qa[8 * j + q4];
+            qf[j][1] = qb[8 * j + q4];
+            qf[j][2] = qa[8 * j + 4 + q4];
+            qf[j][3] = qb[8 * j + 4 + q4];
+        }
+    }
+
     // Page ids (warp 0): lane i holds pages i and 32 + i of this chunk.
     int pg_lo = 0, pg_hi = 0;
     if (warp == 0) {
@@ -824,17 +858,20 @@ __device__ __forceinline__ bool process_group_item(const CUtensorMap &kv_map, co
         rt::tma_load_2d(dst + 6144u, &kv_map, 64, row_k + 16, bar, policy);
     };
     // When the chunk is longer than the ring, stages are refilled while the
-    // item runs, by whichever warp finishes a stage last (below), so the page
-    // ids go to shared memory where every warp can read them.  No barrier
-    // follows: the other warps load their query rows meanwhile, and a refill
-    // reads s_pg only after warp 0 has counted itself done with that stage
-    // (its writes here come first in its program order).
+    // item runs, by whichever warp finishes a stage last (below), so warp 0
+    // puts the page ids in shared memory where every warp can read them.  No
+    // barrier follows: a refill reads s_pg only after warp 0 has counted
+    // itself done with that stage (its writes here come first in its program
+    // order).
     const bool refill = np > kGroupStages;
+    if (warp == 0 && refill) {
+        s_pg[lane] = pg_lo;
+        s_pg[lane + 32] = pg_hi;
+    }
+    // The ring's first pages, from warp 0.  (Spreading their issue over the
+    // four warps started the pages sooner but lengthened the loop's pass by
+    // 0.7%: the sequence kernel runs beside this one.)
     if (warp == 0) {
-        if (refill) {
-            s_pg[lane] = pg_lo;
-            s_pg[lane + 32] = pg_hi;
-        }
         for (int i = 0; i < np && i < kGroupStages; i++) {
             const int pg = __shfl_sync(0xffffffffu, i < 32 ? pg_lo : pg_hi, i & 31);
             if (lane == 0)
@@ -843,42 +880,29 @@ __device__ __forceinline__ bool process_group_item(const CUtensorMap &kv_map, co
     }
 
     // A member takes part when the group covers exactly its skipped pages.
+    auto covers = [&](int L, uint32_t skip) -> bool {
+        if (L < 0 || (uint32_t)L > a.max_seq_len || (uint32_t)L > a.max_pages * 16u)
+            return false;
+        return skip == (uint32_t)P && P <= ((L + 15) >> 4);
+    };
     auto member_ok = [&](int m) -> bool {
         if (m >= (int)n_mem)
             return false;
         const uint32_t b = grp.members[m];
-        if (b >= a.num_seqs)
-            return false;
-        const int L = a.seq_lens[b];
-        if (L < 0 || (uint32_t)L > a.max_seq_len || (uint32_t)L > a.max_pages * 16u)
-            return false;
-        return a.skip_pages[b] == (uint32_t)P && P <= ((L + 15) >> 4);
+        return b < a.num_seqs && covers(a.seq_lens[b], a.skip_pages[b]);
     };
-
-    // Rows of this warp: row r -> member (rb*kWarps + warp)*MPW + r/G, head r%G.
-    const int wm0 = (rb * kWarps + warp) * MPW;
-    const int rA = lane >> 2, rB = rA + 8, q4 = lane & 3;
-    const int mA = wm0 + rA / G, mB = wm0 + rB / G;
-    const bool vA = member_ok(mA), vB = member_ok(mB);
+    const bool vA = inA && covers(LA, kA), vB = inB && covers(LB, kB);
     if (lane == 0 && chunk == 0 && h == 0)
         for (int m = wm0; m < wm0 + MPW && m < (int)n_mem; m++)
             if (!member_ok(m))
                 flag_error(a.error, kErrGroup);
     const bool active = __any_sync(0xffffffffu, vA || vB);
-    const uint32_t bA = vA ? grp.members[mA] : 0u, bB = vB ? grp.members[mB] : 0u;
-    uint32_t qf[8][4];
-    {
-        const uint32_t *qa = reinterpret_cast<const uint32_t *>(
-            a.q + ((size_t)bA * Hq + (size_t)h * G + rA % G) * 128);
-        const uint32_t *qb = reinterpret_cast<const uint32_t *>(
-            a.q + ((size_t)bB * Hq + (size_t)h * G + rB % G) * 128);
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-            qf[j][0] = vA ? qa[8 * j + q4] : 0u;
-            qf[j][1] = vB ? qb[8 * j + q4] : 0u;
-            qf[j][2] = vA ? qa[8 * j + 4 + q4] : 0u;
-            qf[j][3] = vB ? qb[8 * j + 4 + q4] : 0u;
-        }
+    for (int j = 0; j < 8; j++) {
+        if (!vA)
+            qf[j][0] = qf[j][2] = 0u;
+        if (!vB)
+            qf[j][1] = qf[j][3] = 0u;
     }
 
     float o[16][4];
