@@ -25,6 +25,7 @@
 // rt_launch_rollout_worker runs that pass in a persistent single-CTA kernel.
 #include <algorithm>
 #include <cstddef>
+#include <cublas_v2.h>
 #include <cstdint>
 #include <cstring>
 #include <mutex>
@@ -149,7 +150,7 @@ struct Dev {
     uint32_t dm, qkv_n;
     float *gemm_ws;             // K-split partials of the projections
     uint64_t gemm_ws_bytes;
-    uint32_t split_qkv, split_lm;
+    uint32_t split_lm;
     TraceRing *trace;           // device trace ring, or NULL
 };
 
@@ -1448,6 +1449,10 @@ struct rt_rollout {
     // model prefill scratch: embeddings and K/V projections of a token chunk
     __nv_bfloat16 *pre_x;
     float *pre_kv;
+    // model decode: the QKV projection through cuBLAS, with its own workspace
+    // (set once, so that calls inside stream capture allocate nothing)
+    cublasHandle_t blas;
+    void *blas_ws;
 };
 
 namespace {
@@ -1466,6 +1471,28 @@ uint32_t gemm_splits(uint32_t M, uint32_t N, uint32_t K)
     return std::max(1u, std::min(by_sm, K / 256u));
 }
 
+// qkv fp32 [slots][qkv_n] = hin bf16 [slots][dm] x w_qkv bf16 [qkv_n][dm]^T.
+// A plain GEMM of a narrow shape (N = 6,144): cuBLAS takes it in ~15 us
+// where the tcgen05 kernel of gemm.cu, built for the LM head's wide N, needs
+// K-splits and a reduction (~27 us).  Row-major C = A B^T is the
+// column-major C^T = B A^T that cuBLAS computes.
+int qkv_projection(rt_rollout *e, cudaStream_t st)
+{
+    const Dev &d = e->d;
+    const float one = 1.0f, zero = 0.0f;
+    cublasStatus_t bs = cublasSetStream(e->blas, st);
+    if (bs == CUBLAS_STATUS_SUCCESS)
+        bs = cublasGemmEx(e->blas, CUBLAS_OP_T, CUBLAS_OP_N, (int)d.qkv_n, (int)d.max_slots,
+                          (int)d.dm, &one, d.w_qkv, CUDA_R_16BF, (int)d.dm, d.hin, CUDA_R_16BF,
+                          (int)d.dm, &zero, d.qkv, CUDA_R_32F, (int)d.qkv_n, CUBLAS_COMPUTE_32F,
+                          CUBLAS_GEMM_DEFAULT);
+    if (bs != CUBLAS_STATUS_SUCCESS) {
+        rt::set_error("rollout: QKV projection (cuBLAS status %d)", (int)bs);
+        return RT_ECUDA;
+    }
+    return RT_OK;
+}
+
 int launch_decode_model(rt_rollout *e, cudaStream_t st, cudaEvent_t *ev)
 {
     const Dev &d = e->d;
@@ -1474,8 +1501,7 @@ int launch_decode_model(rt_rollout *e, cudaStream_t st, cudaEvent_t *ev)
     cudaError_t err = launch_pdl(embed_kernel, dim3(d.max_slots), dim3(256), st, d);
     if (err != cudaSuccess)
         return rt::cuda_fail(err, "rollout: embed launch");
-    rt_gemm_params_t gq = {d.max_slots, d.qkv_n, d.dm, d.dm, d.dm, d.qkv_n, d.split_qkv, 0u};
-    int rc = rt_gemm_bf16(&gq, d.hin, d.w_qkv, d.qkv, d.gemm_ws, d.gemm_ws_bytes, d.gemm_err, st);
+    int rc = qkv_projection(e, st);
     if (rc != RT_OK)
         return rc;
     err = launch_pdl(model_prepare_kernel, dim3(d.max_slots), dim3(256), st, d);
@@ -1638,6 +1664,10 @@ void engine_free(rt_rollout *e)
             cudaFree(p);
     if (e->io_stage)
         cudaFreeHost(e->io_stage);
+    if (e->blas)
+        cublasDestroy(e->blas);
+    if (e->blas_ws)
+        cudaFree(e->blas_ws);
     if (e->arena && e->priv_blocks)
         for (uint32_t i = 0; i < e->n_priv; i++)
             arena_release(e->arena, e->priv_blocks[i]);
@@ -1867,12 +1897,10 @@ extern "C" int rt_rollout_set_model(rt_rollout_t *e, const rt_model_weights_t *w
         if (err != cudaSuccess)
             return rt::cuda_fail(err, "rollout_set_model: buffers");
     }
-    // K-splits that fill the GPU, and their shared partial-sum workspace
-    d.split_qkv = gemm_splits(S, d.qkv_n, d.dm);
+    // K-splits of the LM head that fill the GPU, and their partial-sum workspace
     d.split_lm = gemm_splits(S, d.vocab, d.dm);
-    rt_gemm_params_t gq = {S, d.qkv_n, d.dm, d.dm, d.dm, d.qkv_n, d.split_qkv, 0u};
     rt_gemm_params_t gl = {S, d.vocab, d.dm, d.dm, d.dm, d.vocab, d.split_lm, 0u};
-    const uint64_t need = std::max(rt_gemm_workspace_bytes(&gq), rt_gemm_workspace_bytes(&gl));
+    const uint64_t need = rt_gemm_workspace_bytes(&gl);
     if (need > d.gemm_ws_bytes) {
         if (d.gemm_ws)
             cudaFree(d.gemm_ws);
@@ -1892,6 +1920,29 @@ extern "C" int rt_rollout_set_model(rt_rollout_t *e, const rt_model_weights_t *w
     d.w_embed = static_cast<const __nv_bfloat16 *>(w->embed);
     d.w_qkv = static_cast<const __nv_bfloat16 *>(w->w_qkv);
     d.w_lm = static_cast<const __nv_bfloat16 *>(w->w_lm);
+    if (!e->blas) {
+        // cuBLAS handle and workspace for the QKV projection, and one call
+        // outside capture (its first call loads its kernels)
+        constexpr size_t kBlasWs = 32u << 20;
+        if (cublasCreate(&e->blas) != CUBLAS_STATUS_SUCCESS) {
+            e->blas = nullptr;
+            rt::set_error("rollout_set_model: cublasCreate failed");
+            return RT_ECUDA;
+        }
+        if ((err = cudaMalloc(&e->blas_ws, kBlasWs)) != cudaSuccess)
+            return rt::cuda_fail(err, "rollout_set_model: cuBLAS workspace");
+        if (cublasSetWorkspace(e->blas, e->blas_ws, kBlasWs) != CUBLAS_STATUS_SUCCESS) {
+            rt::set_error("rollout_set_model: cublasSetWorkspace failed");
+            return RT_ECUDA;
+        }
+    }
+    {
+        const int qrc = qkv_projection(e, e->cap);
+        if (qrc != RT_OK)
+            return qrc;
+        if ((err = cudaStreamSynchronize(e->cap)) != cudaSuccess)
+            return rt::cuda_fail(err, "rollout_set_model: QKV projection");
+    }
     // kernel attributes before capture (the graph bakes the weight pointers in)
     int rc = rt::gemm_prepare();
     if (rc != RT_OK)
