@@ -410,14 +410,16 @@ int rt_rollout_buffers(rt_rollout_t *eng, rt_rollout_buffers_t *out);
  * d_model = num_q_heads * 128 elements, K contiguous; the engine keeps the
  * pointers).  Each pass then runs, for every decoding slot s:
  *   x_s      = embed[last token of s]            (token 0 before the first)
- *   [q|k|v]  = x_s . w_qkv^T                     (tensor-core GEMM, fp32)
+ *   [q|k|v]  = x_s . w_qkv^T                     (cuBLAS GEMM, fp32)
  *   q, and k / v written into the slot's page at its position (bf16)
  *   o_s      = paged GQA attention (as FULL)
  *   logits_s = bf16(o_s) . w_lm^T                (tensor-core GEMM, fp32)
  *   token    = fused sampling of logits_s (as FULL).
  * embed [vocab][d_model]; w_qkv [(num_q_heads + 2 num_kv_heads) * 128]
  * [d_model] (q rows, then k rows per kv head, then v rows per kv head);
- * w_lm [vocab][d_model].  Must be called before the first launch. */
+ * w_lm [vocab][d_model].  Must be called before the first launch.  The
+ * first call also creates the engine's cuBLAS handle and its 32 MiB
+ * workspace (the QKV product). */
 typedef struct {
     const void *embed;
     const void *w_qkv;
