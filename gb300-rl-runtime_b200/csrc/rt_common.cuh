@@ -113,6 +113,13 @@ __device__ __forceinline__ uint64_t l2_policy_evict_first()
     return p;
 }
 
+__device__ __forceinline__ uint64_t l2_policy_evict_last()
+{
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
 __device__ __forceinline__ uint64_t l2_policy_evict_normal()
 {
     uint64_t p;
